@@ -1,0 +1,77 @@
+"""ctypes binding of the llmyb C ABI (``include/llmyb.h``).
+
+The shared library is built in-tree (``hybrid_llm_b200/lib/libllmyb.so``).
+There is no fallback: if the library is missing or a symbol is absent, every
+call raises, so a GPU run can never silently take a CPU or eager path.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import threading
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "lib" / "libllmyb.so"
+
+LLMYB_OK = 0
+LLMYB_EINVAL = 1
+LLMYB_EUNSUPPORTED = 1001
+LLMYB_ETIMEOUT = 1002
+
+_ERRORS = {
+    LLMYB_EINVAL: "invalid argument",
+    LLMYB_EUNSUPPORTED: "shape not supported by this kernel",
+    LLMYB_ETIMEOUT: "device-side wait timed out",
+}
+
+P = C.c_void_p
+I32 = C.c_int32
+I64 = C.c_int64
+F32 = C.c_float
+U64 = C.c_uint64
+
+# name -> (restype, argtypes).  Kept in the same order as include/llmyb.h.
+SIGNATURES: dict[str, tuple[object, list[object]]] = {
+    # router / dispatch plan
+    "llmyb_router_topk": (I32, [P, P, I32, I32, I32, P, P, P]),
+    "llmyb_moe_plan_scratch_bytes": (I64, [I32, I32]),
+    "llmyb_moe_plan": (I32, [P, P, I32, I32, I32, I32, P, P, P, P, P, P, P, P, P, P]),
+    "llmyb_route": (I32, [P, P, I32, I32, I32, I32, P, P, P, P, P, P, P, P, P, P, P]),
+    # MoE expert FFN
+    "llmyb_moe_pack_w13": (I32, [P, P, I32, I32, I32, P, P]),
+    "llmyb_moe_grouped_scratch_bytes": (I64, [I32, I32, I32, I32]),
+    "llmyb_moe_grouped_swiglu": (I32, [P, I32, I32, I32, P, P, P, P, P, I32, P, P, I32, P, P, P, P]),
+}
+
+_lock = threading.Lock()
+_lib: C.CDLL | None = None
+
+
+def lib() -> C.CDLL:
+    """Load the native library once; raise if it is absent."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not LIB_PATH.exists():
+                raise RuntimeError(
+                    f"llmyb native library not found at {LIB_PATH}; "
+                    "build it with `python -m hybrid_llm_b200.build`")
+            handle = C.CDLL(str(LIB_PATH))
+            for name, (res, args) in SIGNATURES.items():
+                fn = getattr(handle, name)  # AttributeError if the export is missing
+                fn.restype = res
+                fn.argtypes = args
+            _lib = handle
+    return _lib
+
+
+def check(status: int, what: str) -> None:
+    if status != LLMYB_OK:
+        msg = _ERRORS.get(status, f"CUDA error {status}")
+        raise RuntimeError(f"{what} failed: {msg} (status {status})")
+
+
+def call(name: str, *args) -> None:
+    """Call an int32-status entry point and raise on a non-zero status."""
+    check(getattr(lib(), name)(*args), name)

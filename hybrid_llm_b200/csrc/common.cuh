@@ -1,0 +1,78 @@
+// Shared helpers for the llmyb sm_100a kernels: status codes, bf16 helpers,
+// bounded device-side waits and warp reductions.
+//
+// Every exported entry point returns an int32 status: 0 on success, a
+// cudaError_t value for CUDA failures (cudaErrorInvalidValue for bad
+// arguments, as the reference engine does in llmy_cuda/src/llmy.cpp:216-218),
+// or one of the LLMYB_E* codes below.  Kernels never allocate memory; every
+// buffer, including scratch, is owned by the caller.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#define LLMYB_OK 0
+#define LLMYB_EINVAL 1            /* == cudaErrorInvalidValue */
+#define LLMYB_EUNSUPPORTED 1001   /* shape outside what the kernel implements */
+#define LLMYB_ETIMEOUT 1002       /* a device-side wait ran out (see dev_status) */
+
+#define LLMYB_API extern "C" __attribute__((visibility("default")))
+
+namespace llmyb {
+
+__host__ __device__ inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+inline int32_t launch_status() {
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? LLMYB_OK : static_cast<int32_t>(e);
+}
+
+__device__ __forceinline__ float bf2f(__nv_bfloat16 v) { return __bfloat162float(v); }
+__device__ __forceinline__ __nv_bfloat16 f2bf(float v) { return __float2bfloat16_rn(v); }
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 p = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&p);
+}
+
+__device__ __forceinline__ float2 unpack_bf16x2(uint32_t v) {
+  __nv_bfloat162 p = *reinterpret_cast<__nv_bfloat162*>(&v);
+  return __bfloat1622float2(p);
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// silu(g) * u evaluated in fp32.  The reference applies
+// torch.nn.functional.silu(gate) * up (model/layers/moe.py:75).
+__device__ __forceinline__ float silu_mul(float g, float u) {
+  return g / (1.0f + expf(-g)) * u;
+}
+
+__device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + expf(-x)); }
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Upper bound for any spin-wait inside a kernel.  A legitimate wait in these
+// kernels lasts microseconds; one second means a peer role has stopped.
+constexpr uint64_t kWaitLimitNs = 1000000000ull;
+
+__device__ __forceinline__ void report_status(int32_t* dev_status, int32_t code) {
+  if (dev_status != nullptr) atomicCAS(dev_status, 0, code);
+}
+
+}  // namespace llmyb

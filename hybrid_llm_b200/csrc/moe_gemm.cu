@@ -1,0 +1,437 @@
+// Grouped SwiGLU expert FFN on 5th-generation tensor cores (tcgen05 + TMEM,
+// operands staged by TMA).
+//
+// Reference: model/layers/moe.py:29-82 (_moe_dispatch_fused) and
+// runpod/kernels/triton_swiglu_moe.py:160-218.  The reference scatters routed
+// rows into a capacity-padded [E, cap, D] buffer after a host sync on
+// counts.max(), runs two cuBLAS bmm calls with a separate SwiGLU pass, then
+// gathers and index_adds.  Here the routed rows are kept expert-contiguous
+// (no padding, no host sync) and a persistent kernel walks the
+// (expert, 128-row tile, N tile) schedule produced by the router plan:
+//
+//   gather : x_perm[pos]  = x[perm_token[pos]]                    (HBM copy)
+//   GEMM1  : h_perm[pos]  = silu(x_perm W_gate^T) * (x_perm W_up^T)  (epilogue)
+//   GEMM2  : y_perm[pos]  = perm_prob[pos] * (h_perm W_down^T)       (epilogue)
+//   combine: out[t]       = sum_s y_perm[route_pos[t, s]]          (fp32 sum)
+//
+// GEMM kernel structure (one CTA per SM, 256 threads):
+//   warp 0     TMA producer: A tile 128x64 and B tile 256x64 per stage,
+//              4-stage ring of 48 KB stages, 128-byte swizzle.
+//   warp 1     MMA issuer: 4 x tcgen05.mma (128x256x16, bf16 -> fp32) per
+//              stage into a TMEM accumulator; two accumulators of 256 columns
+//              so the epilogue of tile i overlaps the main loop of tile i+1.
+//   warp 2     TMEM allocation owner.
+//   warps 4-7  epilogue: tcgen05.ld 32 lanes x 32 columns, fused SwiGLU or
+//              probability scale, bf16 stores.
+// For GEMM1 the weight rows are pre-interleaved (llmyb_moe_pack_w13) so that
+// every 256-wide N tile holds 128 gate rows followed by the matching 128 up
+// rows, which keeps silu(gate) * up inside one accumulator.
+#include "common.cuh"
+#include "sm100.cuh"
+#include "tma_host.h"
+
+#include <algorithm>
+
+namespace llmyb {
+namespace {
+
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
+constexpr int A_STAGE_BYTES = BM * BK * 2;  // 16 KB
+constexpr int B_STAGE_BYTES = BN * BK * 2;  // 32 KB
+constexpr int STAGE_BYTES = A_STAGE_BYTES + B_STAGE_BYTES;
+constexpr int TMEM_COLS = 512;              // 2 accumulators x 256 fp32 columns
+constexpr int GEMM_SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+
+enum Epilogue { kSwiGLU = 0, kScale = 1 };
+
+struct TileInfo {
+  int expert, row0, rows_valid, n_tile;
+};
+
+// tile index -> (expert, first row, valid rows, n tile).  Experts without
+// rows own no tiles; tile_offsets is non-decreasing with E+1 entries.
+__device__ __forceinline__ TileInfo map_tile(int tile, int n_tiles, const int* tile_offsets,
+                                             const int* expert_offsets, int E) {
+  TileInfo ti;
+  const int m_global = tile / n_tiles;
+  ti.n_tile = tile - m_global * n_tiles;
+  int lo = 0, hi = E - 1;  // last e with tile_offsets[e] <= m_global
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (__ldg(tile_offsets + mid) <= m_global) lo = mid; else hi = mid - 1;
+  }
+  ti.expert = lo;
+  const int m_local = m_global - __ldg(tile_offsets + lo);
+  const int e_begin = __ldg(expert_offsets + lo), e_end = __ldg(expert_offsets + lo + 1);
+  ti.row0 = e_begin + m_local * BM;
+  ti.rows_valid = min(BM, e_end - ti.row0);
+  return ti;
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(256, 1) moe_gemm_kernel(
+    const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+    const int* __restrict__ expert_offsets, const int* __restrict__ tile_offsets, int E, int K,
+    int n_weight_rows, __nv_bfloat16* __restrict__ out, int out_ld,
+    const float* __restrict__ row_scale, int32_t* dev_status) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tmem_full = empty + STAGES;
+  uint64_t* tmem_empty = tmem_full + 2;
+  uint64_t* mma_done = tmem_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_tiles = n_weight_rows / BN;
+  const int total_tiles = __ldg(tile_offsets + E) * n_tiles;
+  const int kblocks = K / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      sm100::mbar_init(&full[s], 1);
+      sm100::mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      sm100::mbar_init(&tmem_full[a], 1);
+      sm100::mbar_init(&tmem_empty[a], 128);
+    }
+    sm100::mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    sm100::fence_mbar_init();
+    sm100::tma_prefetch_desc(&map_a);
+    sm100::tma_prefetch_desc(&map_b);
+  }
+  if (warp == 2) sm100::tmem_alloc(tmem_slot, TMEM_COLS);
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------- producer
+    // The whole warp walks the schedule; lane 0 issues, waits are warp-uniform.
+    int stage = 0;
+    uint32_t phase = 0;
+    uint32_t issued[STAGES] = {0, 0, 0, 0};
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
+      const TileInfo ti = map_tile(tile, n_tiles, tile_offsets, expert_offsets, E);
+      const int brow = ti.expert * n_weight_rows + ti.n_tile * BN;
+      for (int kb = 0; kb < kblocks; ++kb) {
+        if (!sm100::mbar_wait_warp(&empty[stage], phase ^ 1u, dev_status, abort_flag)) {
+          ok = false;
+          break;
+        }
+        if (lane == 0) {
+          uint8_t* sa = smem + stage * STAGE_BYTES;
+          uint8_t* sb = sa + A_STAGE_BYTES;
+          sm100::mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
+          sm100::tma_load_2d(&map_a, &full[stage], sa, kb * BK, ti.row0);
+          sm100::tma_load_2d(&map_b, &full[stage], sb, kb * BK, brow);
+        }
+        issued[stage]++;
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+    // make sure no TMA write into shared memory is still in flight
+    for (int s = 0; s < STAGES; ++s)
+      if (issued[s] > 0) sm100::mbar_wait_warp(&full[s], (issued[s] - 1u) & 1u, dev_status, nullptr);
+  } else if (warp == 1) {
+    // ------------------------------------------------------- MMA issuer
+    constexpr uint32_t idesc = sm100::make_idesc_bf16_f32(BM, BN);
+    int stage = 0;
+    uint32_t phase = 0;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
+      if (!sm100::mbar_wait_warp(&tmem_empty[acc], acc_phase ^ 1u, dev_status, abort_flag)) break;
+      sm100::tc_fence_after();
+      const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+      for (int kb = 0; kb < kblocks; ++kb) {
+        if (!sm100::mbar_wait_warp(&full[stage], phase, dev_status, abort_flag)) {
+          ok = false;
+          break;
+        }
+        sm100::tc_fence_after();
+        if (lane == 0) {
+          const uint32_t sa = sm100::smem_u32(smem + stage * STAGE_BYTES);
+          const uint64_t adesc = sm100::make_sw128_kmajor_desc(sa);
+          const uint64_t bdesc = sm100::make_sw128_kmajor_desc(sa + A_STAGE_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            // advance 16 bf16 (32 bytes) along K inside the swizzle atom
+            sm100::umma_bf16_ss(d_tmem, adesc + 2u * kk, bdesc + 2u * kk, idesc,
+                                (kb | kk) != 0 ? 1u : 0u);
+          }
+          sm100::umma_commit(&empty[stage]);
+        }
+        __syncwarp();
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (!ok) break;
+      if (lane == 0) sm100::umma_commit(&tmem_full[acc]);
+      __syncwarp();
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+    // wait for every MMA issued by lane 0 before TMEM/shared memory go away
+    if (lane == 0) sm100::umma_commit(mma_done);
+    __syncwarp();
+    sm100::mbar_wait_warp(mma_done, 0, dev_status, nullptr);
+  } else if (warp >= 4) {
+    // --------------------------------------------------------- epilogue
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int r = q * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x) {
+      const TileInfo ti = map_tile(tile, n_tiles, tile_offsets, expert_offsets, E);
+      if (!sm100::mbar_wait_warp(&tmem_full[acc], acc_phase, dev_status, abort_flag)) break;
+      sm100::tc_fence_after();
+      const uint32_t t_row = tmem_base + static_cast<uint32_t>(acc * BN) +
+                             (static_cast<uint32_t>(q * 32) << 16);
+      const bool valid = r < ti.rows_valid;
+      const int64_t row = static_cast<int64_t>(ti.row0) + r;
+      if (EPI == kSwiGLU) {
+        __nv_bfloat16* dst = out + row * out_ld + ti.n_tile * (BN / 2);
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN / 2; c0 += 32) {
+          uint32_t g[32], u[32];
+          sm100::tmem_ld_32x32b_x32(t_row + c0, g);
+          sm100::tmem_ld_32x32b_x32(t_row + BN / 2 + c0, u);
+          sm100::tmem_ld_wait();
+          if (valid) {
+            uint4 pk[4];
+            uint32_t* pw = reinterpret_cast<uint32_t*>(pk);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const float h0 = silu_mul(__uint_as_float(g[2 * j]), __uint_as_float(u[2 * j]));
+              const float h1 =
+                  silu_mul(__uint_as_float(g[2 * j + 1]), __uint_as_float(u[2 * j + 1]));
+              pw[j] = pack_bf16x2(h0, h1);
+            }
+            uint4* d4 = reinterpret_cast<uint4*>(dst + c0);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) d4[j] = pk[j];
+          }
+        }
+      } else {
+        const float scale = valid ? __ldg(row_scale + row) : 0.0f;
+        __nv_bfloat16* dst = out + row * out_ld + ti.n_tile * BN;
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += 32) {
+          uint32_t a[32];
+          sm100::tmem_ld_32x32b_x32(t_row + c0, a);
+          sm100::tmem_ld_wait();
+          if (valid) {
+            uint4 pk[4];
+            uint32_t* pw = reinterpret_cast<uint32_t*>(pk);
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+              pw[j] = pack_bf16x2(__uint_as_float(a[2 * j]) * scale,
+                                  __uint_as_float(a[2 * j + 1]) * scale);
+            uint4* d4 = reinterpret_cast<uint4*>(dst + c0);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) d4[j] = pk[j];
+          }
+        }
+      }
+      sm100::tc_fence_before();
+      sm100::mbar_arrive(&tmem_empty[acc]);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    sm100::tc_fence_after();
+    sm100::tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+// x_perm[pos, :] = x[perm_token[pos], :]   (16-byte vectors)
+__global__ void gather_rows_kernel(const __nv_bfloat16* __restrict__ x,
+                                   const int* __restrict__ perm_token, int64_t rows, int D,
+                                   __nv_bfloat16* __restrict__ x_perm) {
+  const int vec = D / 8;
+  const int64_t total = rows * vec;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t pos = i / vec;
+    const int c = static_cast<int>(i - pos * vec);
+    const int t = __ldg(perm_token + pos);
+    reinterpret_cast<uint4*>(x_perm + pos * D)[c] =
+        __ldg(reinterpret_cast<const uint4*>(x + static_cast<int64_t>(t) * D) + c);
+  }
+}
+
+// out[t, :] = sum_s y_perm[route_pos[t*k + s], :], fp32 accumulation.
+__global__ void combine_rows_kernel(const __nv_bfloat16* __restrict__ y_perm,
+                                    const int* __restrict__ route_pos, int64_t N, int k, int D,
+                                    __nv_bfloat16* __restrict__ out) {
+  const int vec = D / 8;
+  const int64_t total = N * vec;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t t = i / vec;
+    const int c = static_cast<int>(i - t * vec);
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int s = 0; s < k; ++s) {
+      const int pos = __ldg(route_pos + t * k + s);
+      const uint4 v = __ldg(reinterpret_cast<const uint4*>(y_perm + static_cast<int64_t>(pos) * D) + c);
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = unpack_bf16x2(w[j]);
+        acc[2 * j] += f.x;
+        acc[2 * j + 1] += f.y;
+      }
+    }
+    uint4 o;
+    o.x = pack_bf16x2(acc[0], acc[1]);
+    o.y = pack_bf16x2(acc[2], acc[3]);
+    o.z = pack_bf16x2(acc[4], acc[5]);
+    o.w = pack_bf16x2(acc[6], acc[7]);
+    reinterpret_cast<uint4*>(out + t * D)[c] = o;
+  }
+}
+
+// w13[e, 256*j + r] = r < 128 ? w_gate[e, 128*j + r] : w_up[e, 128*j + r - 128]
+__global__ void pack_w13_kernel(const __nv_bfloat16* __restrict__ w_gate,
+                                const __nv_bfloat16* __restrict__ w_up, int E, int F, int D,
+                                __nv_bfloat16* __restrict__ w13) {
+  const int vec = D / 8;
+  const int64_t total = static_cast<int64_t>(E) * 2 * F * vec;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t row = i / vec;  // row of w13 (0 .. E*2F)
+    const int c = static_cast<int>(i - row * vec);
+    const int e = static_cast<int>(row / (2 * F));
+    const int rr = static_cast<int>(row - static_cast<int64_t>(e) * 2 * F);
+    const int j = rr / BN, r = rr % BN;
+    const __nv_bfloat16* src = r < BN / 2 ? w_gate : w_up;
+    const int64_t srow = static_cast<int64_t>(e) * F + j * (BN / 2) + (r % (BN / 2));
+    reinterpret_cast<uint4*>(w13 + row * D)[c] =
+        __ldg(reinterpret_cast<const uint4*>(src + srow * D) + c);
+  }
+}
+
+int grid_for(int64_t work, int threads) {
+  const int64_t blocks = ceil_div(work, threads);
+  return static_cast<int>(blocks < 8 * 148 ? (blocks > 0 ? blocks : 1) : 8 * 148);
+}
+
+bool gemm_attr_set = false;
+
+int32_t ensure_gemm_attrs() {
+  if (gemm_attr_set) return LLMYB_OK;
+  cudaError_t e1 = cudaFuncSetAttribute(moe_gemm_kernel<kSwiGLU>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, GEMM_SMEM);
+  cudaError_t e2 = cudaFuncSetAttribute(moe_gemm_kernel<kScale>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, GEMM_SMEM);
+  if (e1 != cudaSuccess) return e1;
+  if (e2 != cudaSuccess) return e2;
+  gemm_attr_set = true;
+  return LLMYB_OK;
+}
+
+}  // namespace
+}  // namespace llmyb
+
+using namespace llmyb;
+
+LLMYB_API int32_t llmyb_moe_pack_w13(const __nv_bfloat16* w_gate, const __nv_bfloat16* w_up,
+                                     int32_t n_experts, int32_t ffn, int32_t d_model,
+                                     __nv_bfloat16* w13, void* stream) {
+  if (!w_gate || !w_up || !w13 || n_experts <= 0 || ffn <= 0 || d_model <= 0) return LLMYB_EINVAL;
+  if (ffn % (BN / 2) != 0 || d_model % BK != 0) return LLMYB_EUNSUPPORTED;
+  const int64_t work = static_cast<int64_t>(n_experts) * 2 * ffn * (d_model / 8);
+  pack_w13_kernel<<<grid_for(work, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      w_gate, w_up, n_experts, ffn, d_model, w13);
+  return launch_status();
+}
+
+// Bytes of caller-provided scratch for llmyb_moe_grouped_swiglu:
+// x_perm [N*k, D] + h_perm [N*k, F] + y_perm [N*k, D], bf16, 256-byte aligned.
+LLMYB_API int64_t llmyb_moe_grouped_scratch_bytes(int32_t n_tokens, int32_t top_k,
+                                                  int32_t d_model, int32_t ffn) {
+  if (n_tokens < 0 || top_k <= 0 || d_model <= 0 || ffn <= 0) return -1;
+  const int64_t rows = static_cast<int64_t>(n_tokens) * top_k;
+  auto al = [](int64_t b) { return (b + 255) / 256 * 256; };
+  return al(rows * d_model * 2) + al(rows * ffn * 2) + al(rows * d_model * 2);
+}
+
+// Routed SwiGLU experts for a dispatch plan produced by llmyb_route /
+// llmyb_moe_plan.  w13 is the [E, 2F, D] interleaved gate/up stack from
+// llmyb_moe_pack_w13 and w2 the [E, D, F] down stack (moe.py:119-125 layout).
+LLMYB_API int32_t llmyb_moe_grouped_swiglu(
+    const __nv_bfloat16* x, int32_t n_tokens, int32_t d_model, int32_t top_k,
+    const int32_t* perm_token, const float* perm_prob, const int32_t* route_pos,
+    const int32_t* expert_offsets, const int32_t* tile_offsets, int32_t n_experts,
+    const __nv_bfloat16* w13, const __nv_bfloat16* w2, int32_t ffn, void* scratch,
+    __nv_bfloat16* out, int32_t* dev_status, void* stream) {
+  if (n_tokens < 0 || d_model <= 0 || top_k <= 0 || n_experts <= 0 || ffn <= 0)
+    return LLMYB_EINVAL;
+  if (n_tokens == 0) return LLMYB_OK;
+  if (!x || !perm_token || !perm_prob || !route_pos || !expert_offsets || !tile_offsets || !w13 ||
+      !w2 || !scratch || !out || !dev_status)
+    return LLMYB_EINVAL;
+  if (d_model % BN != 0 || ffn % (BN / 2) != 0 || ffn % BK != 0 || d_model % BK != 0)
+    return LLMYB_EUNSUPPORTED;
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out) |
+       reinterpret_cast<uintptr_t>(scratch)) & 15u)
+    return LLMYB_EINVAL;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int32_t st = ensure_gemm_attrs();
+  if (st) return st;
+
+  const int64_t rows = static_cast<int64_t>(n_tokens) * top_k;
+  auto al = [](int64_t b) { return (b + 255) / 256 * 256; };
+  uint8_t* sp = static_cast<uint8_t*>(scratch);
+  __nv_bfloat16* x_perm = reinterpret_cast<__nv_bfloat16*>(sp);
+  __nv_bfloat16* h_perm = reinterpret_cast<__nv_bfloat16*>(sp + al(rows * d_model * 2));
+  __nv_bfloat16* y_perm =
+      reinterpret_cast<__nv_bfloat16*>(sp + al(rows * d_model * 2) + al(rows * ffn * 2));
+
+  gather_rows_kernel<<<grid_for(rows * (d_model / 8), 256), 256, 0, s>>>(x, perm_token, rows,
+                                                                         d_model, x_perm);
+
+  CUtensorMap ma1, mb1, ma2, mb2;
+  if (!make_bf16_2d_map(&ma1, x_perm, rows, d_model, d_model, BM, BK) ||
+      !make_bf16_2d_map(&mb1, w13, static_cast<uint64_t>(n_experts) * 2 * ffn, d_model, d_model,
+                        BN, BK) ||
+      !make_bf16_2d_map(&ma2, h_perm, rows, ffn, ffn, BM, BK) ||
+      !make_bf16_2d_map(&mb2, w2, static_cast<uint64_t>(n_experts) * d_model, ffn, ffn, BN, BK))
+    return LLMYB_EUNSUPPORTED;
+
+  // upper bound of the m-tile count without reading device memory
+  const int64_t m_tiles_max = ceil_div(rows, BM) + n_experts;
+  const int sms = num_sms();
+  const int grid1 = static_cast<int>(std::min<int64_t>(sms, m_tiles_max * (2 * ffn / BN)));
+  const int grid2 = static_cast<int>(std::min<int64_t>(sms, m_tiles_max * (d_model / BN)));
+  moe_gemm_kernel<kSwiGLU><<<grid1, 256, GEMM_SMEM, s>>>(ma1, mb1, expert_offsets, tile_offsets,
+                                                          n_experts, d_model, 2 * ffn, h_perm,
+                                                          ffn, nullptr, dev_status);
+  moe_gemm_kernel<kScale><<<grid2, 256, GEMM_SMEM, s>>>(ma2, mb2, expert_offsets, tile_offsets,
+                                                         n_experts, ffn, d_model, y_perm,
+                                                         d_model, perm_prob, dev_status);
+  combine_rows_kernel<<<grid_for(static_cast<int64_t>(n_tokens) * (d_model / 8), 256), 256, 0,
+                        s>>>(y_perm, route_pos, n_tokens, top_k, d_model, out);
+  return launch_status();
+}

@@ -1,0 +1,450 @@
+// Top-k router and MoE dispatch plan.
+//
+// Reference semantics (StillPillWill/Hybrid_LLM):
+//   * top-k + softmax over the selected logits:
+//       model/layers/context_router.py:72-74
+//       (top_values, top_indices = topk(route_logits.float(), k); softmax(top_values))
+//   * dispatch permutation: model/layers/moe.py:42-60 (flat route r = t*k + s,
+//     sort by expert, bincount, offsets = cumsum - counts).
+//
+// Ordering contract (bit-exact): top-k is ordered by (value desc, index asc);
+// the permutation is the STABLE sort of the flat route expert ids, i.e. routes
+// ordered by (expert, token, slot).  This equals
+// torch.sort(flat_experts, stable=True) and, because each token's k experts
+// are distinct, every permutation the reference's unstable sort may return
+// produces the same per-token sums.
+//
+// Work split: one warp per token for top-k (HBM-bound: N*E*4 bytes read);
+// the plan is a three-pass counting sort over 256-token chunks (histogram,
+// one-CTA scan, in-order scatter), with a single-CTA fused path for decode
+// batches (N <= 256) so that a decode step costs one launch.
+#include "common.cuh"
+
+namespace llmyb {
+namespace {
+
+constexpr int kChunk = 256;        // tokens per chunk in the multi-CTA plan
+constexpr int kMaxTopK = 32;       // one lane per selected slot
+constexpr int kMaxPerLane = 8;     // experts per lane -> E <= 256
+constexpr int kMaxExperts = 32 * kMaxPerLane;
+
+// Warp-cooperative top-k over one row of E logits.  Returns, in lane s < k,
+// the index and value of the s-th selected expert.
+__device__ __forceinline__ void warp_topk_row(const float* __restrict__ row,
+                                              const float* __restrict__ bias, int E, int k,
+                                              int lane, int& out_idx, float& out_val) {
+  float v[kMaxPerLane];
+#pragma unroll
+  for (int j = 0; j < kMaxPerLane; ++j) {
+    const int e = j * 32 + lane;
+    float x = -INFINITY;
+    if (e < E) {
+      x = row[e];
+      if (bias != nullptr) x += bias[e];
+    }
+    v[j] = x;
+  }
+  unsigned taken = 0u;  // bit j: slot j of this lane already selected
+  out_idx = -1;
+  out_val = -INFINITY;
+  for (int s = 0; s < k; ++s) {
+    // local best: value desc, index asc (index grows with j for a lane)
+    float best = -INFINITY;
+    int best_e = 0x7fffffff;  // sentinel: no candidate in this lane
+#pragma unroll
+    for (int j = 0; j < kMaxPerLane; ++j) {
+      const int e = j * 32 + lane;
+      // e grows with j, so the first candidate wins ties inside a lane
+      if (e < E && !((taken >> j) & 1u) && (best_e == 0x7fffffff || v[j] > best)) {
+        best = v[j];
+        best_e = e;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oe = __shfl_xor_sync(0xffffffffu, best_e, o);
+      if (ov > best || (ov == best && oe < best_e)) {
+        best = ov;
+        best_e = oe;
+      }
+    }
+    if (lane == s) {
+      out_idx = best_e;
+      out_val = best;
+    }
+    if ((best_e & 31) == lane) taken |= 1u << (best_e >> 5);
+  }
+}
+
+// softmax over the k selected values held in lanes 0..k-1 (value order:
+// lane 0 holds the maximum).  fp32, exp via expf.
+__device__ __forceinline__ float warp_topk_softmax(float val, int k, int lane) {
+  const float mx = __shfl_sync(0xffffffffu, val, 0);
+  const float ex = lane < k ? expf(val - mx) : 0.0f;
+  const float sum = warp_sum(ex);
+  return ex / sum;
+}
+
+__global__ void __launch_bounds__(256) router_topk_kernel(
+    const float* __restrict__ logits, const float* __restrict__ bias, int N, int E, int k,
+    int64_t* __restrict__ topk_idx, float* __restrict__ topk_prob, int* __restrict__ hist) {
+  __shared__ int s_hist[kMaxExperts];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (hist != nullptr) {
+    for (int e = threadIdx.x; e < E; e += blockDim.x) s_hist[e] = 0;
+    __syncthreads();
+  }
+  const int chunk0 = blockIdx.x * kChunk;
+  for (int t = chunk0 + warp; t < min(N, chunk0 + kChunk); t += 8) {
+    int idx;
+    float val;
+    warp_topk_row(logits + static_cast<int64_t>(t) * E, bias, E, k, lane, idx, val);
+    const float p = warp_topk_softmax(val, k, lane);
+    if (lane < k) {
+      topk_idx[static_cast<int64_t>(t) * k + lane] = idx;
+      topk_prob[static_cast<int64_t>(t) * k + lane] = p;
+      if (hist != nullptr) atomicAdd(&s_hist[idx], 1);
+    }
+  }
+  if (hist != nullptr) {
+    __syncthreads();
+    const int nchunks = gridDim.x;
+    for (int e = threadIdx.x; e < E; e += blockDim.x) hist[e * nchunks + blockIdx.x] = s_hist[e];
+  }
+}
+
+// Histogram only (top-k supplied by the caller, e.g. the reference router).
+__global__ void __launch_bounds__(256) plan_hist_kernel(const int64_t* __restrict__ topk_idx, int N,
+                                                        int E, int k, int* __restrict__ hist,
+                                                        int* __restrict__ bad) {
+  extern __shared__ int s_hist_dyn[];
+  for (int e = threadIdx.x; e < E; e += blockDim.x) s_hist_dyn[e] = 0;
+  __syncthreads();
+  const int64_t r0 = static_cast<int64_t>(blockIdx.x) * kChunk * k;
+  const int64_t r1 = min(static_cast<int64_t>(N) * k, r0 + static_cast<int64_t>(kChunk) * k);
+  for (int64_t r = r0 + threadIdx.x; r < r1; r += blockDim.x) {
+    const int64_t e = topk_idx[r];
+    if (e < 0 || e >= E) {
+      report_status(bad, LLMYB_EINVAL);
+      continue;
+    }
+    atomicAdd(&s_hist_dyn[e], 1);
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) hist[e * gridDim.x + blockIdx.x] = s_hist_dyn[e];
+}
+
+// Block-wide exclusive scan of one int per thread (blockDim.x == 1024).
+__device__ int block_exclusive_scan(int v, int* s_warp, int& total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) s_warp[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    int w = s_warp[lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += y;
+    }
+    s_warp[lane] = w;
+  }
+  __syncthreads();
+  total = s_warp[31];
+  const int excl = x - v + (warp > 0 ? s_warp[warp - 1] : 0);
+  __syncthreads();
+  return excl;
+}
+
+// One CTA of 1024 threads.  hist is [E][nchunks]; on exit it holds the global
+// base position of every (expert, chunk) pair.  Also writes counts, offsets
+// (E+1) and tile_offsets (E+1, tiles of tile_m rows per expert).
+__global__ void __launch_bounds__(1024) plan_scan_kernel(int* __restrict__ hist, int nchunks, int E,
+                                                         int tile_m, int* __restrict__ counts,
+                                                         int* __restrict__ offsets,
+                                                         int* __restrict__ tile_offsets) {
+  __shared__ int s_warp[32];
+  __shared__ int s_count[1024];
+  // groups of chunks per expert handled by one thread
+  int G = 1;
+  while (G * 2 * E <= 1024 && G * 2 <= nchunks) G *= 2;
+  const int per = static_cast<int>(ceil_div(nchunks, G));
+  // pass 1: per-(e,g) partial sums and in-group exclusive prefixes
+  __shared__ int s_part[1024];
+  for (int item = threadIdx.x; item < E * G; item += blockDim.x) {
+    const int e = item / G, g = item % G;
+    const int c0 = g * per, c1 = min(nchunks, c0 + per);
+    int run = 0;
+    int* h = hist + static_cast<int64_t>(e) * nchunks;
+    for (int c = c0; c < c1; ++c) {
+      const int x = h[c];
+      h[c] = run;
+      run += x;
+    }
+    s_part[item] = run;
+  }
+  __syncthreads();
+  // per-expert totals and group bases
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    int run = 0;
+    for (int g = 0; g < G; ++g) {
+      const int x = s_part[e * G + g];
+      s_part[e * G + g] = run;
+      run += x;
+    }
+    s_count[e] = run;
+  }
+  __syncthreads();
+  // exclusive scan over experts (E <= 1024)
+  const int c = threadIdx.x < E ? s_count[threadIdx.x] : 0;
+  int total = 0;
+  const int off = block_exclusive_scan(c, s_warp, total);
+  const int tiles = threadIdx.x < E ? static_cast<int>(ceil_div(c, tile_m)) : 0;
+  int total_tiles = 0;
+  const int toff = block_exclusive_scan(tiles, s_warp, total_tiles);
+  if (threadIdx.x < E) {
+    counts[threadIdx.x] = c;
+    offsets[threadIdx.x] = off;
+    tile_offsets[threadIdx.x] = toff;
+    s_count[threadIdx.x] = off;  // reuse as expert base
+  }
+  if (threadIdx.x == 0) {
+    offsets[E] = total;
+    tile_offsets[E] = total_tiles;
+  }
+  __syncthreads();
+  for (int item = threadIdx.x; item < E * G; item += blockDim.x) {
+    const int e = item / G, g = item % G;
+    const int c0 = g * per, c1 = min(nchunks, c0 + per);
+    const int base = s_count[e] + s_part[item];
+    int* h = hist + static_cast<int64_t>(e) * nchunks;
+    for (int cc = c0; cc < c1; ++cc) h[cc] += base;
+  }
+}
+
+// In-order scatter.  CTA = one 256-token chunk = 8 warps x 32 tokens; lane s
+// walks slot s of the warp's tokens in token order, so equal experts get
+// increasing positions in (token, slot) order.
+__global__ void __launch_bounds__(256) plan_scatter_kernel(
+    const int64_t* __restrict__ topk_idx, const float* __restrict__ topk_prob, int N, int E, int k,
+    const int* __restrict__ hist_base, int* __restrict__ perm_token, float* __restrict__ perm_prob,
+    int* __restrict__ route_pos, int64_t* __restrict__ sort_order) {
+  extern __shared__ int s_cnt[];  // [8][E]
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nchunks = gridDim.x;
+  int* my = s_cnt + warp * E;
+  for (int e = lane; e < E; e += 32) my[e] = 0;
+  __syncwarp();
+  const int t0 = blockIdx.x * kChunk + warp * 32;
+  const int tn = max(0, min(32, N - t0));
+  // phase 1: per-warp counts
+  for (int j = 0; j < tn; ++j) {
+    if (lane < k) {
+      const int64_t e = topk_idx[static_cast<int64_t>(t0 + j) * k + lane];
+      if (e >= 0 && e < E) my[e] += 1;  // a token's experts are distinct: no lane collision
+    }
+    __syncwarp();
+  }
+  __syncthreads();
+  // phase 2: turn counts into starting positions
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    int run = hist_base[e * nchunks + blockIdx.x];
+    for (int w = 0; w < 8; ++w) {
+      const int x = s_cnt[w * E + e];
+      s_cnt[w * E + e] = run;
+      run += x;
+    }
+  }
+  __syncthreads();
+  for (int j = 0; j < tn; ++j) {
+    if (lane < k) {
+      const int t = t0 + j;
+      const int64_t r = static_cast<int64_t>(t) * k + lane;
+      const int64_t e = topk_idx[r];
+      if (e < 0 || e >= E) continue;  // flagged by plan_hist_kernel
+      const int pos = my[e];
+      my[e] = pos + 1;
+      perm_token[pos] = t;
+      perm_prob[pos] = topk_prob[r];
+      route_pos[r] = pos;
+      if (sort_order != nullptr) sort_order[pos] = r;
+    }
+    __syncwarp();
+  }
+}
+
+// Fused single-CTA route for small batches (decode): top-k, softmax, counts,
+// offsets, tile offsets and the in-order permutation in one launch.
+__global__ void __launch_bounds__(1024) route_small_kernel(
+    const float* __restrict__ logits, const float* __restrict__ bias, int N, int E, int k,
+    int tile_m, int64_t* __restrict__ topk_idx, float* __restrict__ topk_prob,
+    int* __restrict__ counts, int* __restrict__ offsets, int* __restrict__ tile_offsets,
+    int* __restrict__ perm_token, float* __restrict__ perm_prob, int* __restrict__ route_pos,
+    int64_t* __restrict__ sort_order) {
+  __shared__ int s_idx[256 * kMaxTopK / 4];  // N*k <= 2048
+  __shared__ float s_prob[256 * kMaxTopK / 4];
+  __shared__ int s_cnt[kMaxExperts];
+  __shared__ int s_warp[32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int e = threadIdx.x; e < E; e += blockDim.x) s_cnt[e] = 0;
+  __syncthreads();
+  for (int t = warp; t < N; t += 32) {
+    int idx;
+    float val;
+    warp_topk_row(logits + static_cast<int64_t>(t) * E, bias, E, k, lane, idx, val);
+    const float p = warp_topk_softmax(val, k, lane);
+    if (lane < k) {
+      s_idx[t * k + lane] = idx;
+      s_prob[t * k + lane] = p;
+      topk_idx[static_cast<int64_t>(t) * k + lane] = idx;
+      topk_prob[static_cast<int64_t>(t) * k + lane] = p;
+      atomicAdd(&s_cnt[idx], 1);
+    }
+  }
+  __syncthreads();
+  const int c = threadIdx.x < E ? s_cnt[threadIdx.x] : 0;
+  int total = 0;
+  const int off = block_exclusive_scan(c, s_warp, total);
+  const int tiles = threadIdx.x < E ? static_cast<int>(ceil_div(c, tile_m)) : 0;
+  int total_tiles = 0;
+  const int toff = block_exclusive_scan(tiles, s_warp, total_tiles);
+  if (threadIdx.x < E) {
+    counts[threadIdx.x] = c;
+    offsets[threadIdx.x] = off;
+    tile_offsets[threadIdx.x] = toff;
+    s_cnt[threadIdx.x] = off;
+  }
+  if (threadIdx.x == 0) {
+    offsets[E] = total;
+    tile_offsets[E] = total_tiles;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    for (int t = 0; t < N; ++t) {
+      if (lane < k) {
+        const int r = t * k + lane;
+        const int e = s_idx[r];
+        const int pos = s_cnt[e];
+        s_cnt[e] = pos + 1;
+        perm_token[pos] = t;
+        perm_prob[pos] = s_prob[r];
+        route_pos[r] = pos;
+        if (sort_order != nullptr) sort_order[pos] = r;
+      }
+      __syncwarp();
+    }
+  }
+}
+
+int32_t check_route_args(int N, int E, int k, int tile_m) {
+  if (N < 0 || E <= 0 || k <= 0 || k > E || tile_m <= 0) return LLMYB_EINVAL;
+  if (k > kMaxTopK || E > kMaxExperts) return LLMYB_EUNSUPPORTED;
+  return LLMYB_OK;
+}
+
+}  // namespace
+}  // namespace llmyb
+
+using namespace llmyb;
+
+LLMYB_API int32_t llmyb_router_topk(const float* logits, const float* bias, int32_t n_tokens,
+                                    int32_t n_experts, int32_t top_k, int64_t* topk_idx,
+                                    float* topk_prob, void* stream) {
+  int32_t st = check_route_args(n_tokens, n_experts, top_k, 1);
+  if (st) return st;
+  if (n_tokens == 0) return LLMYB_OK;
+  if (!logits || !topk_idx || !topk_prob) return LLMYB_EINVAL;
+  const int nchunks = static_cast<int>(ceil_div(n_tokens, kChunk));
+  router_topk_kernel<<<nchunks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      logits, bias, n_tokens, n_experts, top_k, topk_idx, topk_prob, nullptr);
+  return launch_status();
+}
+
+LLMYB_API int64_t llmyb_moe_plan_scratch_bytes(int32_t n_tokens, int32_t n_experts) {
+  if (n_tokens < 0 || n_experts <= 0) return -1;
+  const int64_t nchunks = ceil_div(n_tokens, kChunk);
+  return (nchunks * n_experts + 1) * static_cast<int64_t>(sizeof(int));
+}
+
+namespace {
+int32_t plan_tail(const int64_t* topk_idx, const float* topk_prob, int N, int E, int k, int tile_m,
+                  int* counts, int* offsets, int* tile_offsets, int* perm_token, float* perm_prob,
+                  int* route_pos, int64_t* sort_order, int* hist, cudaStream_t s) {
+  const int nchunks = static_cast<int>(ceil_div(N, kChunk));
+  plan_scan_kernel<<<1, 1024, 0, s>>>(hist, nchunks, E, tile_m, counts, offsets, tile_offsets);
+  plan_scatter_kernel<<<nchunks, 256, 8 * E * sizeof(int), s>>>(
+      topk_idx, topk_prob, N, E, k, hist, perm_token, perm_prob, route_pos, sort_order);
+  return launch_status();
+}
+
+int32_t empty_plan(int E, int* counts, int* offsets, int* tile_offsets, cudaStream_t s) {
+  cudaError_t e1 = cudaMemsetAsync(counts, 0, sizeof(int) * E, s);
+  cudaError_t e2 = cudaMemsetAsync(offsets, 0, sizeof(int) * (E + 1), s);
+  cudaError_t e3 = cudaMemsetAsync(tile_offsets, 0, sizeof(int) * (E + 1), s);
+  if (e1 != cudaSuccess) return e1;
+  if (e2 != cudaSuccess) return e2;
+  return e3;
+}
+}  // namespace
+
+// Dispatch plan for top-k routes computed elsewhere (e.g. the reference's
+// torch.topk router): model/layers/moe.py:42-60.
+LLMYB_API int32_t llmyb_moe_plan(const int64_t* topk_idx, const float* topk_prob, int32_t n_tokens,
+                                 int32_t n_experts, int32_t top_k, int32_t tile_m,
+                                 int32_t* expert_counts, int32_t* expert_offsets,
+                                 int32_t* tile_offsets, int32_t* perm_token, float* perm_prob,
+                                 int32_t* route_pos, int64_t* sort_order, void* scratch,
+                                 int32_t* dev_status, void* stream) {
+  int32_t st = check_route_args(n_tokens, n_experts, top_k, tile_m);
+  if (st) return st;
+  if (!expert_counts || !expert_offsets || !tile_offsets || !dev_status) return LLMYB_EINVAL;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (n_tokens == 0) return empty_plan(n_experts, expert_counts, expert_offsets, tile_offsets, s);
+  if (!topk_idx || !topk_prob || !perm_token || !perm_prob || !route_pos || !scratch)
+    return LLMYB_EINVAL;
+  const int nchunks = static_cast<int>(ceil_div(n_tokens, kChunk));
+  int* hist = static_cast<int*>(scratch);
+  plan_hist_kernel<<<nchunks, 256, n_experts * sizeof(int), s>>>(topk_idx, n_tokens, n_experts,
+                                                                 top_k, hist, dev_status);
+  return plan_tail(topk_idx, topk_prob, n_tokens, n_experts, top_k, tile_m, expert_counts,
+                   expert_offsets, tile_offsets, perm_token, perm_prob, route_pos, sort_order,
+                   hist, s);
+}
+
+// Router top-k + softmax + dispatch plan from fp32 logits (plus an optional
+// per-expert bias added before selection).
+LLMYB_API int32_t llmyb_route(const float* logits, const float* bias, int32_t n_tokens,
+                              int32_t n_experts, int32_t top_k, int32_t tile_m, int64_t* topk_idx,
+                              float* topk_prob, int32_t* expert_counts, int32_t* expert_offsets,
+                              int32_t* tile_offsets, int32_t* perm_token, float* perm_prob,
+                              int32_t* route_pos, int64_t* sort_order, void* scratch,
+                              void* stream) {
+  int32_t st = check_route_args(n_tokens, n_experts, top_k, tile_m);
+  if (st) return st;
+  if (!expert_counts || !expert_offsets || !tile_offsets) return LLMYB_EINVAL;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (n_tokens == 0) return empty_plan(n_experts, expert_counts, expert_offsets, tile_offsets, s);
+  if (!logits || !topk_idx || !topk_prob || !perm_token || !perm_prob || !route_pos)
+    return LLMYB_EINVAL;
+  if (n_tokens <= 256 && n_tokens * top_k <= 256 * kMaxTopK / 4) {
+    route_small_kernel<<<1, 1024, 0, s>>>(logits, bias, n_tokens, n_experts, top_k, tile_m,
+                                          topk_idx, topk_prob, expert_counts, expert_offsets,
+                                          tile_offsets, perm_token, perm_prob, route_pos,
+                                          sort_order);
+    return launch_status();
+  }
+  if (!scratch) return LLMYB_EINVAL;
+  const int nchunks = static_cast<int>(ceil_div(n_tokens, kChunk));
+  int* hist = static_cast<int*>(scratch);
+  router_topk_kernel<<<nchunks, 256, 0, s>>>(logits, bias, n_tokens, n_experts, top_k, topk_idx,
+                                             topk_prob, hist);
+  return plan_tail(topk_idx, topk_prob, n_tokens, n_experts, top_k, tile_m, expert_counts,
+                   expert_offsets, tile_offsets, perm_token, perm_prob, route_pos, sort_order,
+                   hist, s);
+}

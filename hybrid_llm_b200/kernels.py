@@ -1,0 +1,173 @@
+"""Torch-tensor wrappers around the llmyb C ABI.
+
+Each wrapper validates dtypes/contiguity on the host, allocates outputs and
+scratch with torch's caching allocator (the kernels themselves never
+allocate) and launches on torch's current CUDA stream.  Nothing here has a
+CPU path: tensors must live on a CUDA device.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from . import _native
+
+TILE_M = 128  # rows per grouped-GEMM tile; the plan's tile_offsets use it
+
+_status: dict[int, torch.Tensor] = {}
+
+
+def _ptr(t: torch.Tensor | None):
+    return None if t is None else t.data_ptr()
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _require_cuda(*tensors: torch.Tensor | None) -> None:
+    for t in tensors:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError("llmyb kernels take CUDA tensors only (no CPU fallback)")
+
+
+def device_status(device: torch.device | None = None) -> torch.Tensor:
+    """Per-device int32 word the kernels set when a bounded wait gives up."""
+    idx = torch.cuda.current_device() if device is None else torch.device(device).index or 0
+    buf = _status.get(idx)
+    if buf is None:
+        buf = torch.zeros(1, dtype=torch.int32, device=f"cuda:{idx}")
+        _status[idx] = buf
+    return buf
+
+
+def check_device_status(device: torch.device | None = None) -> None:
+    """Synchronize and raise if any kernel recorded a device-side error."""
+    buf = device_status(device)
+    code = int(buf.item())
+    if code != 0:
+        buf.zero_()
+        _native.check(code, "device-side status")
+
+
+@dataclass
+class RoutePlan:
+    """Top-k routes and the expert-grouped dispatch order (all on device)."""
+
+    topk_idx: torch.Tensor      # [N, k] int64
+    topk_prob: torch.Tensor     # [N, k] fp32
+    counts: torch.Tensor        # [E] int32
+    offsets: torch.Tensor       # [E+1] int32, expert row ranges in permuted order
+    tile_offsets: torch.Tensor  # [E+1] int32, 128-row tiles per expert (prefix)
+    perm_token: torch.Tensor    # [N*k] int32, token of each permuted row
+    perm_prob: torch.Tensor     # [N*k] fp32, route probability of each permuted row
+    route_pos: torch.Tensor     # [N*k] int32, permuted row of route t*k+s
+    sort_order: torch.Tensor | None  # [N*k] int64, flat route id of each permuted row
+
+    @property
+    def n_experts(self) -> int:
+        return self.counts.numel()
+
+
+def _plan_buffers(n: int, e: int, k: int, device, with_sort_order: bool):
+    i32 = dict(dtype=torch.int32, device=device)
+    return dict(
+        counts=torch.empty(e, **i32), offsets=torch.empty(e + 1, **i32),
+        tile_offsets=torch.empty(e + 1, **i32), perm_token=torch.empty(n * k, **i32),
+        perm_prob=torch.empty(n * k, dtype=torch.float32, device=device),
+        route_pos=torch.empty(n * k, **i32),
+        sort_order=torch.empty(n * k, dtype=torch.int64, device=device) if with_sort_order else None,
+    )
+
+
+def _plan_scratch(n: int, e: int, device) -> torch.Tensor:
+    nbytes = int(_native.lib().llmyb_moe_plan_scratch_bytes(n, e))
+    return torch.empty(max(nbytes, 4), dtype=torch.uint8, device=device)
+
+
+def route(logits: torch.Tensor, k: int, bias: torch.Tensor | None = None, *,
+          with_sort_order: bool = False) -> RoutePlan:
+    """Top-k + softmax + dispatch plan from fp32 router logits [N, E]."""
+    _require_cuda(logits, bias)
+    if logits.dtype != torch.float32 or logits.dim() != 2:
+        raise ValueError("route expects fp32 logits of shape [N, E]")
+    logits = logits.contiguous()
+    n, e = logits.shape
+    if bias is not None:
+        bias = bias.to(torch.float32).contiguous()
+    dev = logits.device
+    idx = torch.empty(n, k, dtype=torch.int64, device=dev)
+    prob = torch.empty(n, k, dtype=torch.float32, device=dev)
+    b = _plan_buffers(n, e, k, dev, with_sort_order)
+    scratch = _plan_scratch(n, e, dev)
+    _native.call("llmyb_route", _ptr(logits), _ptr(bias), n, e, k, TILE_M, _ptr(idx), _ptr(prob),
+                 _ptr(b["counts"]), _ptr(b["offsets"]), _ptr(b["tile_offsets"]),
+                 _ptr(b["perm_token"]), _ptr(b["perm_prob"]), _ptr(b["route_pos"]),
+                 _ptr(b["sort_order"]), _ptr(scratch), _stream())
+    return RoutePlan(idx, prob, **b)
+
+
+def router_topk(logits: torch.Tensor, k: int, bias: torch.Tensor | None = None):
+    """(indices int64, probabilities fp32) — context_router.py:73-74 semantics."""
+    _require_cuda(logits, bias)
+    logits = logits.to(torch.float32).contiguous()
+    n, e = logits.shape
+    idx = torch.empty(n, k, dtype=torch.int64, device=logits.device)
+    prob = torch.empty(n, k, dtype=torch.float32, device=logits.device)
+    _native.call("llmyb_router_topk", _ptr(logits), _ptr(bias), n, e, k, _ptr(idx), _ptr(prob),
+                 _stream())
+    return idx, prob
+
+
+def moe_plan(topk_idx: torch.Tensor, topk_prob: torch.Tensor, n_experts: int, *,
+             with_sort_order: bool = False) -> RoutePlan:
+    """Dispatch plan for externally computed top-k routes (moe.py:42-60)."""
+    _require_cuda(topk_idx, topk_prob)
+    idx = topk_idx.to(torch.int64).contiguous()
+    prob = topk_prob.to(torch.float32).contiguous()
+    n, k = idx.shape
+    dev = idx.device
+    b = _plan_buffers(n, n_experts, k, dev, with_sort_order)
+    scratch = _plan_scratch(n, n_experts, dev)
+    _native.call("llmyb_moe_plan", _ptr(idx), _ptr(prob), n, n_experts, k, TILE_M,
+                 _ptr(b["counts"]), _ptr(b["offsets"]), _ptr(b["tile_offsets"]),
+                 _ptr(b["perm_token"]), _ptr(b["perm_prob"]), _ptr(b["route_pos"]),
+                 _ptr(b["sort_order"]), _ptr(scratch), _ptr(device_status(dev)), _stream())
+    return RoutePlan(idx, prob, **b)
+
+
+def pack_w13(w_gate: torch.Tensor, w_up: torch.Tensor) -> torch.Tensor:
+    """Interleave [E,F,D] gate/up stacks into the [E,2F,D] GEMM1 operand."""
+    _require_cuda(w_gate, w_up)
+    w_gate = w_gate.to(torch.bfloat16).contiguous()
+    w_up = w_up.to(torch.bfloat16).contiguous()
+    e, f, d = w_gate.shape
+    out = torch.empty(e, 2 * f, d, dtype=torch.bfloat16, device=w_gate.device)
+    _native.call("llmyb_moe_pack_w13", _ptr(w_gate), _ptr(w_up), e, f, d, _ptr(out), _stream())
+    return out
+
+
+def moe_grouped(x: torch.Tensor, plan: RoutePlan, w13: torch.Tensor, w2: torch.Tensor,
+                out: torch.Tensor | None = None, scratch: torch.Tensor | None = None) -> torch.Tensor:
+    """Routed SwiGLU experts: out[t] = sum_s p_ts * down(silu(gate x_t) * up x_t)."""
+    _require_cuda(x, w13, w2)
+    if x.dtype != torch.bfloat16:
+        raise ValueError("moe_grouped computes in bf16")
+    x = x.contiguous()
+    n, d = x.shape
+    k = plan.topk_idx.shape[1]
+    e, f2, d2 = w13.shape
+    f = f2 // 2
+    if d2 != d or tuple(w2.shape) != (e, d, f):
+        raise ValueError("expert weight shapes do not match the activations")
+    if out is None:
+        out = torch.empty(n, d, dtype=torch.bfloat16, device=x.device)
+    need = int(_native.lib().llmyb_moe_grouped_scratch_bytes(n, k, d, f))
+    if scratch is None or scratch.numel() < need:
+        scratch = torch.empty(max(need, 16), dtype=torch.uint8, device=x.device)
+    _native.call("llmyb_moe_grouped_swiglu", _ptr(x), n, d, k, _ptr(plan.perm_token),
+                 _ptr(plan.perm_prob), _ptr(plan.route_pos), _ptr(plan.offsets),
+                 _ptr(plan.tile_offsets), e, _ptr(w13), _ptr(w2), f, _ptr(scratch), _ptr(out),
+                 _ptr(device_status(x.device)), _stream())
+    return out

@@ -1,0 +1,127 @@
+"""Generate the golden fixtures by running the reference's own PyTorch code.
+
+Run in a container that has the reference checkout (default
+``/root/reference``; override with ``LLMY_REFERENCE``)::
+
+    python tests/golden/make_golden.py [section ...]
+
+Each section seeds its inputs with numpy, runs the reference modules on CPU
+(fp32, Triton off) and writes ``tests/golden/<section>.npz``.  The fixtures
+are small; the tests compare the numpy oracle against them on CPU and the CUDA
+kernels against the oracle on a GPU.  Nothing at run time reads the reference.
+"""
+from __future__ import annotations
+
+import importlib.util
+import os
+import sys
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+REF = Path(os.environ.get("LLMY_REFERENCE", "/root/reference"))
+sys.path.insert(0, str(HERE.parents[1]))  # repo root, for the weight generator
+
+os.environ.setdefault("LLMY_DISABLE_TRITON", "1")
+
+import torch  # noqa: E402
+
+sys.path.insert(0, str(HERE))
+import inputs  # noqa: E402
+
+torch.set_num_threads(max(1, os.cpu_count() or 1))
+
+
+def _ref_import():
+    if str(REF) not in sys.path:
+        sys.path.insert(0, str(REF))
+    import model.layers.gated_deltanet as gdn_mod  # noqa: F401
+    import model.layers.moe as moe_mod
+    gdn_mod._triton_gdn_available = False
+    moe_mod._triton_available = False
+    return gdn_mod, moe_mod
+
+
+def _standalone():
+    """Import sample_standalone.py as a module (it must be in sys.modules first)."""
+    name = "llmy_sample_standalone"
+    if name in sys.modules:
+        return sys.modules[name]
+    spec = importlib.util.spec_from_file_location(name, REF / "sample_standalone.py")
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[name] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def save(name: str, **arrays) -> None:
+    path = HERE / f"{name}.npz"
+    np.savez_compressed(path, **{k: np.asarray(v) for k, v in arrays.items()})
+    print(f"wrote {path.relative_to(HERE.parents[1])} ({path.stat().st_size} bytes)")
+
+
+def t(x) -> torch.Tensor:
+    return torch.from_numpy(np.ascontiguousarray(x))
+
+
+# ----------------------------------------------------------------- sections
+def sec_router() -> None:
+    """ContextAwareRouter.forward (context_router.py:59-86), context off."""
+    _ref_import()
+    from model.layers.context_router import ContextAwareRouter
+
+    out = {}
+    for tag in inputs.ROUTER_CASES:
+        c = inputs.router_case(tag)
+        n, d = c["hidden"].shape[1:]
+        e, k = c["weight"].shape[0], c["k"]
+        router = ContextAwareRouter(d, e, k, context_aware=False)
+        with torch.no_grad():
+            router.logits.weight.copy_(t(c["weight"]))
+        captured = {}
+        router.logits.register_forward_hook(lambda m, i, o: captured.setdefault("logits", o.detach()))
+        with torch.no_grad():
+            idx, prob, _ = router(t(c["hidden"]), return_stats=False)
+        flat = idx.reshape(-1)
+        _, stable = torch.sort(flat, stable=True)
+        _, unstable = torch.sort(flat)
+        out.update({
+            f"{tag}_checksum": inputs.checksum(c["hidden"], c["weight"]),
+            f"{tag}_logits": captured["logits"].reshape(n, e).numpy(),
+            f"{tag}_idx": idx.reshape(n, k).numpy(), f"{tag}_prob": prob.reshape(n, k).numpy(),
+            f"{tag}_stable_order": stable.numpy(), f"{tag}_unstable_order": unstable.numpy(),
+            f"{tag}_counts": torch.bincount(flat, minlength=e).numpy(),
+        })
+    save("router", **out)
+
+
+def sec_moe() -> None:
+    """_moe_dispatch_fused (moe.py:29-82) with torch.topk routes, fp32."""
+    _, moe_mod = _ref_import()
+    out = {}
+    for tag in inputs.MOE_CASES:
+        c = inputs.moe_case(tag)
+        vals, idx = torch.topk(t(c["logits"]), c["k"], dim=-1)
+        prob = vals.softmax(-1)
+        with torch.no_grad():
+            y = moe_mod._moe_dispatch_fused(t(c["flat"]), idx, prob, t(c["w_gate"]),
+                                            t(c["w_up"]), t(c["w_down"]))
+        out.update({f"{tag}_checksum": inputs.checksum(*(c[k] for k in ("flat", "logits", "w_gate", "w_up", "w_down"))),
+                    f"{tag}_idx": idx.numpy(), f"{tag}_prob": prob.numpy(), f"{tag}_out": y.numpy()})
+    save("moe", **out)
+
+
+SECTIONS = {"router": sec_router, "moe": sec_moe}
+
+
+def main(argv: list[str]) -> None:
+    if not REF.exists():
+        raise SystemExit(f"reference checkout not found at {REF}")
+    names = argv or list(SECTIONS)
+    for name in names:
+        SECTIONS[name]()
+
+
+if __name__ == "__main__":
+    main(sys.argv[1:])

@@ -1,0 +1,91 @@
+"""GPU: tcgen05 grouped SwiGLU experts vs the fp64 oracle and a torch fp32 reference."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import routing
+
+pytestmark = pytest.mark.gpu
+
+# bf16 tolerance for the routed output: the kernel rounds the SwiGLU
+# activation and every routed row to bf16 and sums the k rows in fp32.
+MAX_REL = 2e-2   # max |out - ref| / max |ref|
+MEAN_REL = 5e-3  # mean |out - ref| / mean |ref|
+
+
+def _case(n, d, e, k, f, seed, zipf=False):
+    rng = np.random.default_rng(seed)
+    bf = lambda a: torch.from_numpy(a.astype(np.float32)).to(torch.bfloat16)
+    x = bf(rng.normal(0, 1, (n, d)))
+    logits = rng.normal(0, 0.64, (n, e)).astype(np.float32)
+    bias = routing.zipf_expert_bias(e) if zipf else None
+    wg = bf(rng.normal(0, 0.02, (e, f, d)))
+    wu = bf(rng.normal(0, 0.02, (e, f, d)))
+    wd = bf(rng.normal(0, 0.02, (e, d, f)))
+    return x, logits, bias, wg, wu, wd
+
+
+def _run(x, logits, bias, wg, wu, wd, k):
+    from hybrid_llm_b200 import kernels
+    dev = "cuda"
+    plan = kernels.route(torch.from_numpy(logits).to(dev), k,
+                         None if bias is None else torch.from_numpy(bias).to(dev))
+    w13 = kernels.pack_w13(wg.to(dev), wu.to(dev))
+    out = kernels.moe_grouped(x.to(dev), plan, w13, wd.to(dev))
+    torch.cuda.synchronize()
+    kernels.check_device_status()
+    return out, plan
+
+
+def _errors(out, ref):
+    out = out.float().cpu().numpy().astype(np.float64)
+    ref = np.asarray(ref, dtype=np.float64)
+    err = np.abs(out - ref)
+    return err.max() / np.abs(ref).max(), err.mean() / np.abs(ref).mean()
+
+
+@pytest.mark.parametrize("n,d,e,k,f", [(300, 256, 8, 2, 128), (1, 768, 16, 2, 1024),
+                                       (5, 512, 8, 2, 1024), (700, 256, 4, 4, 256),
+                                       (129, 1024, 32, 4, 512)])
+def test_moe_matches_oracle(cuda, n, d, e, k, f):
+    x, logits, bias, wg, wu, wd = _case(n, d, e, k, f, seed=n + d)
+    out, plan = _run(x, logits, bias, wg, wu, wd, k)
+    idx, prob = routing.router_topk(logits, k, bias)
+    ref = routing.moe_forward(x.float().numpy(), idx, prob, wg.float().numpy(),
+                              wu.float().numpy(), wd.float().numpy())
+    mx, mean = _errors(out, ref)
+    assert mx < MAX_REL and mean < MEAN_REL, (mx, mean)
+
+
+def _torch_reference(x, plan, wg, wu, wd):
+    """fp32 torch restatement of moe.py:72-81 on the GPU (per-expert matmuls)."""
+    xf = x.float()
+    out = torch.zeros_like(xf)
+    idx, prob = plan.topk_idx, plan.topk_prob
+    for e in range(wg.shape[0]):
+        tok, slot = torch.nonzero(idx == e, as_tuple=True)
+        if tok.numel() == 0:
+            continue
+        h = torch.nn.functional.silu(xf[tok] @ wg[e].float().T) * (xf[tok] @ wu[e].float().T)
+        out.index_add_(0, tok, (h @ wd[e].float().T) * prob[tok, slot, None])
+    return out
+
+
+def test_moe_isolated_layer_full_size(cuda):
+    """16384 tokens x 1024, 32 experts top-4, F=512, Zipf-skewed routing."""
+    x, logits, bias, wg, wu, wd = _case(16384, 1024, 32, 4, 512, seed=3, zipf=True)
+    dev = "cuda"
+    out, plan = _run(x, logits, bias, wg, wu, wd, 4)
+    ref = _torch_reference(x.to(dev), plan, wg.to(dev), wu.to(dev), wd.to(dev))
+    err = (out.float() - ref).abs()
+    assert float(err.max() / ref.abs().max()) < MAX_REL
+    assert float(err.mean() / ref.abs().mean()) < MEAN_REL
+    counts = plan.counts.cpu()
+    assert int(counts.sum()) == 16384 * 4 and int(counts.max()) > 4 * int(counts.min() + 1)
+
+
+def test_moe_repeated_calls_identical(cuda):
+    x, logits, bias, wg, wu, wd = _case(513, 512, 8, 2, 256, seed=9)
+    a, _ = _run(x, logits, bias, wg, wu, wd, 2)
+    b, _ = _run(x, logits, bias, wg, wu, wd, 2)
+    assert torch.equal(a, b)
