@@ -40,6 +40,14 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "llmyb_moe_pack_w13": (I32, [P, P, I32, I32, I32, P, P]),
     "llmyb_moe_grouped_scratch_bytes": (I64, [I32, I32, I32, I32]),
     "llmyb_moe_grouped_swiglu": (I32, [P, I32, I32, I32, P, P, P, P, P, I32, P, P, I32, P, P, P, P]),
+    # gated delta rule
+    "llmyb_gdn_activate": (I32, [P, I64, I32, I32, I32, I32, P, P]),
+    "llmyb_gdn_step": (I32, [P, I64, P, I64, P, I64, P, I64, P, I64, P, P, P, I32, I32, I32, I32,
+                             P, P, I64, P]),
+    "llmyb_gdn_prefill_scratch_bytes": (I64, [I32, I32, I32, I32, I32]),
+    "llmyb_gdn_prefill": (I32, [P, I64, P, I64, P, I64, P, I64, P, I64, P, P, P, I32, I32, I32,
+                                I32, I32, P, P, I64, P, P]),
+    "llmyb_gdn_conv_gate": (I32, [P, P, P, P, P, I32, I32, I32, P, P, I32, P]),
 }
 
 _lock = threading.Lock()

@@ -1,0 +1,853 @@
+// Gated DeltaNet recurrence: decode step and chunked prefill scan.
+//
+// Reference: model/layers/gated_deltanet.py:140-149 (step), :128-132 (q/k
+// L2 norm, sigmoid beta/gate, per-head decay = sigmoid(decay_logit)), the
+// Triton serial scan/step (sample_standalone.py:435-531) and the native
+// gdn_step kernel (llmy_cuda/src/kernels/gdn.cu:22-87).
+//
+//   S_t = a_t S_{t-1} + k_t w_t^T,   w_t = beta_t (v_t - S_{t-1}^T k_t)
+//   o_t = (S_t^T q_t) * gate_t                       (S_t: the updated state)
+//   S is zeroed before token t when reset_t is set.
+//
+// Decode (llmyb_gdn_step): one CTA per (row, head, 32 value columns); four
+// warps split the key dimension, lane = value column; the fp32 state streams
+// through registers once (read + write = 8*K*V bytes per head).  HBM-bound.
+//
+// Prefill (llmyb_gdn_chunk_prep + llmyb_gdn_chunk_scan), chunk C = 64:
+// inside a chunk with Gamma_t = prod_{j<=t} a_j (segment-masked at resets)
+//   S_t = Gamma_t S_0 + sum_{i<=t} (Gamma_t/Gamma_i) k_i w_i^T
+//   (I + A) W = diag(beta) V - diag(beta Gamma_{t-1}) K S_0,
+//       A[t,i] = beta_t (Gamma_{t-1}/Gamma_i) k_t.k_i  (i < t)
+//   O   = diag(Gamma) Q S_0 + (M o Q K^T) W,   M[t,i] = Gamma_t/Gamma_i (i <= t)
+//   S_C = Gamma_C S_0 + K^T diag(Gamma_C/Gamma_i) W
+// The prep kernel (fully parallel over chunks) forms T = (I + A)^-1 by blocked
+// forward substitution and writes U = T diag(beta) V, Kw = T diag(beta
+// Gamma_{t-1}) K and Aqk = M o QK^T; the scan kernel (one CTA per row, head
+// and value slice) walks the chunks: W = U - Kw S, O = qs*QS + Aqk W,
+// S <- sd*S + K^T diag(ks) W, with the fp32 state kept in mma accumulators
+// and fed to the tensor cores as a bf16 hi/lo pair.
+#include "common.cuh"
+#include "mma.cuh"
+
+#include <algorithm>
+
+namespace llmyb {
+namespace {
+
+constexpr int kC = 64;  // chunk length
+
+// ------------------------------------------------------------- activation
+// In place on the fused projection [N, width] = [q | k | v | gate | beta]:
+// q, k <- x * rsqrt(max(sum x^2, 1e-12)) per head; gate <- sigmoid(gate);
+// beta <- sigmoid(beta + bias).  One warp per (token, head).
+__global__ void gdn_activate_kernel(__nv_bfloat16* __restrict__ proj, int64_t N, int width, int H,
+                                    int KD, int VD, const float* __restrict__ beta_bias) {
+  const int lane = threadIdx.x & 31;
+  const int64_t wid = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
+  if (wid >= N * H) return;
+  const int64_t tok = wid / H;
+  const int h = static_cast<int>(wid - tok * H);
+  __nv_bfloat16* row = proj + tok * width;
+  for (int part = 0; part < 2; ++part) {
+    __nv_bfloat16* x = row + part * H * KD + h * KD;
+    float ss = 0.f;
+    for (int i = lane; i < KD; i += 32) {
+      const float v = bf2f(x[i]);
+      ss += v * v;
+    }
+    ss = warp_sum(ss);
+    const float sc = rsqrtf(fmaxf(ss, 1e-12f));
+    for (int i = lane; i < KD; i += 32) x[i] = f2bf(bf2f(x[i]) * sc);
+  }
+  __nv_bfloat16* g = row + 2 * H * KD + H * VD + h * VD;
+  for (int i = lane; i < VD; i += 32) g[i] = f2bf(sigmoidf_(bf2f(g[i])));
+  if (lane == 0) {
+    __nv_bfloat16* b = row + 2 * H * KD + 2 * H * VD + h;
+    *b = f2bf(sigmoidf_(bf2f(*b) + (beta_bias ? beta_bias[h] : 0.f)));
+  }
+}
+
+// --------------------------------------------------------------- decode
+struct GdnIO {
+  const __nv_bfloat16 *q, *k, *v, *gate, *beta;  // token-major with strides below
+  int64_t sq, sk, sv, sg, sb;                    // elements between consecutive tokens
+  const float* decay_logit;                      // [H] (alpha = sigmoid), or null
+  const float* log_alpha;                        // [B*T, H] per-token log decay, or null
+  const uint8_t* reset;                          // [B*T] or null
+};
+
+__device__ __forceinline__ float alpha_of(const GdnIO& io, int64_t tok, int h, int H) {
+  if (io.log_alpha != nullptr) return expf(io.log_alpha[tok * H + h]);
+  return sigmoidf_(io.decay_logit[h]);
+}
+
+template <int KD>
+__global__ void __launch_bounds__(128) gdn_step_kernel(GdnIO io, int H, int VD,
+                                                       float* __restrict__ state,
+                                                       __nv_bfloat16* __restrict__ out,
+                                                       int64_t so) {
+  constexpr int RPW = KD / 4;  // state rows per warp
+  __shared__ float s_q[KD], s_k[KD];
+  __shared__ float s_red[4][32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nvc = VD / 32;
+  const int b = blockIdx.x / (H * nvc);
+  const int h = (blockIdx.x / nvc) % H;
+  const int v0 = (blockIdx.x % nvc) * 32;
+  const int64_t tok = b;  // one token per row
+  for (int i = threadIdx.x; i < KD; i += 128) {
+    s_q[i] = bf2f(io.q[tok * io.sq + h * KD + i]);
+    s_k[i] = bf2f(io.k[tok * io.sk + h * KD + i]);
+  }
+  __syncthreads();
+  const bool rst = io.reset != nullptr && io.reset[tok] != 0;
+  const float a = alpha_of(io, tok, h, H);
+  const float beta = bf2f(io.beta[tok * io.sb + h]);
+  float* S = state + ((static_cast<int64_t>(b) * H + h) * KD) * VD + v0 + lane;
+  float s[RPW];
+  float pred = 0.f;
+#pragma unroll
+  for (int r = 0; r < RPW; ++r) {
+    const int kr = warp * RPW + r;
+    s[r] = rst ? 0.f : S[static_cast<int64_t>(kr) * VD];
+    pred += s_k[kr] * s[r];
+  }
+  s_red[warp][lane] = pred;
+  __syncthreads();
+  pred = s_red[0][lane] + s_red[1][lane] + s_red[2][lane] + s_red[3][lane];
+  const float delta = bf2f(io.v[tok * io.sv + h * VD + v0 + lane]) - pred;
+  float o = 0.f;
+#pragma unroll
+  for (int r = 0; r < RPW; ++r) {
+    const int kr = warp * RPW + r;
+    const float ns = a * s[r] + beta * s_k[kr] * delta;
+    S[static_cast<int64_t>(kr) * VD] = ns;
+    o += s_q[kr] * ns;
+  }
+  __syncthreads();
+  s_red[warp][lane] = o;
+  __syncthreads();
+  if (warp == 0) {
+    o = s_red[0][lane] + s_red[1][lane] + s_red[2][lane] + s_red[3][lane];
+    // reference order: out.to(hidden dtype) * gate (gated_deltanet.py:149)
+    const float gt = bf2f(io.gate[tok * io.sg + h * VD + v0 + lane]);
+    out[tok * so + h * VD + v0 + lane] = f2bf(bf2f(f2bf(o)) * gt);
+  }
+}
+
+// ----------------------------------------------------------- chunk prep
+struct PrepOut {
+  __nv_bfloat16* U;   // [B*T, H, VD]
+  __nv_bfloat16* Kw;  // [B*T, H, KD]
+  __nv_bfloat16* Aqk; // [B, H, nC, C, C]
+  float* qscale;      // [B*T, H]
+  float* kscale;      // [B*T, H]
+  float* sdecay;      // [B, H, nC]
+};
+
+template <int KD, int VD>
+struct PrepSmem {
+  static constexpr int LK = KD + 8, LV = VD + 8, LT = kC + 8, LF = kC + 1;
+  __nv_bfloat16 K[kC * LK];
+  __nv_bfloat16 Q[kC * LK];
+  __nv_bfloat16 V[kC * LV];
+  __nv_bfloat16 T1[kC * LT];  // bf16(T diag(beta))
+  __nv_bfloat16 T2[kC * LT];  // bf16(T diag(beta Gamma_prev seg0))
+  float A[kC * LF];           // strictly lower (I + A) factor
+  float Tm[kC * LF];          // T = (I + A)^-1
+  float R[kC * LF];           // blocked substitution workspace
+  float g[kC], gprev[kC], beta[kC];
+  int seg[kC];
+  int n;
+};
+
+template <int KD, int VD>
+__global__ void __launch_bounds__(128) gdn_chunk_prep_kernel(GdnIO io, int B, int T, int H,
+                                                             PrepOut po) {
+  using SM = PrepSmem<KD, VD>;
+  extern __shared__ uint8_t smem_raw[];
+  SM& sm = *reinterpret_cast<SM*>(smem_raw);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nC = static_cast<int>(ceil_div(T, kC));
+  const int c = blockIdx.x % nC;
+  const int h = (blockIdx.x / nC) % H;
+  const int b = blockIdx.x / (nC * H);
+  const int t0 = c * kC;
+  const int n = min(kC, T - t0);
+  const int64_t tok0 = static_cast<int64_t>(b) * T + t0;
+
+  // ---- load K, Q, V (zero rows beyond n)
+  for (int i = tid; i < kC * (KD / 8); i += 128) {
+    const int r = i / (KD / 8), cc = (i % (KD / 8)) * 8;
+    uint4 kv = make_uint4(0, 0, 0, 0), qv = kv;
+    if (r < n) {
+      kv = *reinterpret_cast<const uint4*>(io.k + (tok0 + r) * io.sk + h * KD + cc);
+      qv = *reinterpret_cast<const uint4*>(io.q + (tok0 + r) * io.sq + h * KD + cc);
+    }
+    *reinterpret_cast<uint4*>(&sm.K[r * SM::LK + cc]) = kv;
+    *reinterpret_cast<uint4*>(&sm.Q[r * SM::LK + cc]) = qv;
+  }
+  for (int i = tid; i < kC * (VD / 8); i += 128) {
+    const int r = i / (VD / 8), cc = (i % (VD / 8)) * 8;
+    uint4 vv = make_uint4(0, 0, 0, 0);
+    if (r < n) vv = *reinterpret_cast<const uint4*>(io.v + (tok0 + r) * io.sv + h * VD + cc);
+    *reinterpret_cast<uint4*>(&sm.V[r * SM::LV + cc]) = vv;
+  }
+  if (tid == 0) {
+    float g = 0.f;
+    int seg = 0;
+    for (int t = 0; t < kC; ++t) {
+      float la = 0.f, bt = 0.f;
+      if (t < n) {
+        const int64_t tok = tok0 + t;
+        la = io.log_alpha != nullptr ? io.log_alpha[tok * H + h]
+                                     : logf(sigmoidf_(io.decay_logit[h]));
+        bt = bf2f(io.beta[tok * io.sb + h]);
+        if (io.reset != nullptr && io.reset[tok] != 0) seg += 1;
+      }
+      sm.gprev[t] = g;
+      g += la;
+      sm.g[t] = g;
+      sm.beta[t] = bt;
+      sm.seg[t] = seg;
+    }
+    sm.n = n;
+  }
+  __syncthreads();
+
+  // ---- KK^T and QK^T for rows 16*warp .. +15 (all 64 columns)
+  float kk[8][4], qk[8][4];
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) kk[j][e] = qk[j][e] = 0.f;
+#pragma unroll
+  for (int ks = 0; ks < KD; ks += 16) {
+    uint32_t ak[4], aq[4];
+    mma::load_a(ak, sm.K, SM::LK, warp * 16, ks);
+    mma::load_a(aq, sm.Q, SM::LK, warp * 16, ks);
+#pragma unroll
+    for (int nb = 0; nb < 8; nb += 2) {
+      uint32_t bb[4];
+      mma::load_b_nk(bb, sm.K, SM::LK, nb * 8, ks);
+      mma::mma_bf16(kk[nb], ak, bb[0], bb[1]);
+      mma::mma_bf16(kk[nb + 1], ak, bb[2], bb[3]);
+      mma::mma_bf16(qk[nb], aq, bb[0], bb[1]);
+      mma::mma_bf16(qk[nb + 1], aq, bb[2], bb[3]);
+    }
+  }
+  // ---- masks and scales; A to smem (fp32), Aqk to global (bf16)
+  __nv_bfloat16* aqk_out = po.Aqk + ((static_cast<int64_t>(b) * H + h) * nC + c) * kC * kC;
+  {
+    const int r0 = warp * 16 + (lane >> 2);
+#pragma unroll
+    for (int nb = 0; nb < 8; ++nb) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int t = r0 + (e >> 1) * 8;
+        const int i = nb * 8 + (lane & 3) * 2 + (e & 1);
+        const bool same = sm.seg[t] == sm.seg[i];
+        sm.A[t * SM::LF + i] =
+            (i < t && same) ? sm.beta[t] * expf(sm.gprev[t] - sm.g[i]) * kk[nb][e] : 0.f;
+        const float m = (i <= t && same && t < n) ? expf(sm.g[t] - sm.g[i]) * qk[nb][e] : 0.f;
+        aqk_out[t * kC + i] = f2bf(m);
+      }
+    }
+  }
+  __syncthreads();
+
+  // ---- T = (I + A)^-1, blocked: 16x16 diagonal blocks by forward
+  // substitution (one thread per column), then off-diagonal blocks
+  // T_ij = -T_ii * sum_{k=j}^{i-1} A_ik T_kj, block row by block row.
+  if (tid < 64) {
+    const int blk = tid >> 4, j = tid & 15, base = blk * 16;
+    for (int t = 0; t < 16; ++t) {
+      float acc = (t == j) ? 1.f : 0.f;
+      for (int i = 0; i < t; ++i)
+        acc -= sm.A[(base + t) * SM::LF + base + i] * sm.Tm[(base + i) * SM::LF + base + j];
+      sm.Tm[(base + t) * SM::LF + base + j] = acc;
+    }
+  }
+  // zero the strictly upper blocks
+  for (int i = tid; i < kC * kC; i += 128) {
+    const int r = i / kC, cc = i % kC;
+    if ((cc >> 4) > (r >> 4)) sm.Tm[r * SM::LF + cc] = 0.f;
+  }
+  __syncthreads();
+  for (int bi = 1; bi < 4; ++bi) {
+    // R_ij = sum_{k=j}^{i-1} A_ik T_kj for all j < i  (rows of block bi, cols < 16*bi)
+    for (int idx = tid; idx < 16 * 16 * bi; idx += 128) {
+      const int r = bi * 16 + idx / (16 * bi);
+      const int cc = idx % (16 * bi);
+      float acc = 0.f;
+      for (int kq = (cc >> 4) * 16; kq < bi * 16; ++kq)
+        acc += sm.A[r * SM::LF + kq] * sm.Tm[kq * SM::LF + cc];
+      sm.R[r * SM::LF + cc] = acc;
+    }
+    __syncthreads();
+    for (int idx = tid; idx < 16 * 16 * bi; idx += 128) {
+      const int r = bi * 16 + idx / (16 * bi);
+      const int cc = idx % (16 * bi);
+      float acc = 0.f;
+      for (int kq = bi * 16; kq <= r; ++kq) acc += sm.Tm[r * SM::LF + kq] * sm.R[kq * SM::LF + cc];
+      sm.Tm[r * SM::LF + cc] = -acc;
+    }
+    __syncthreads();
+  }
+
+  // ---- scaled bf16 copies of T; per-token scales
+  for (int i = tid; i < kC * kC; i += 128) {
+    const int r = i / kC, cc = i % kC;
+    const float tv = sm.Tm[r * SM::LF + cc];
+    sm.T1[r * SM::LT + cc] = f2bf(tv * sm.beta[cc]);
+    const float s2 = sm.seg[cc] == 0 ? sm.beta[cc] * expf(sm.gprev[cc]) : 0.f;
+    sm.T2[r * SM::LT + cc] = f2bf(tv * s2);
+  }
+  if (tid < kC) {
+    const int t = tid;
+    const int last = n - 1;
+    if (t < n) {
+      po.qscale[(tok0 + t) * H + h] = sm.seg[t] == 0 ? expf(sm.g[t]) : 0.f;
+      po.kscale[(tok0 + t) * H + h] = sm.seg[t] == sm.seg[last] ? expf(sm.g[last] - sm.g[t]) : 0.f;
+    }
+    if (t == 0)
+      po.sdecay[(static_cast<int64_t>(b) * H + h) * nC + c] =
+          sm.seg[last] == 0 ? expf(sm.g[last]) : 0.f;
+  }
+  __syncthreads();
+
+  // ---- U = T1 V  (64 x VD), Kw = T2 K (64 x KD): rows 16*warp..
+  {
+    uint32_t a1[4][4], a2[4][4];
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) {
+      mma::load_a(a1[ks], sm.T1, SM::LT, warp * 16, ks * 16);
+      mma::load_a(a2[ks], sm.T2, SM::LT, warp * 16, ks * 16);
+    }
+    const int r = warp * 16 + (lane >> 2);
+#pragma unroll
+    for (int nb = 0; nb < VD / 8; nb += 2) {
+      float acc0[4] = {0, 0, 0, 0}, acc1[4] = {0, 0, 0, 0};
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks) {
+        uint32_t bb[4];
+        mma::load_b_kn(bb, sm.V, SM::LV, ks * 16, nb * 8);
+        mma::mma_bf16(acc0, a1[ks], bb[0], bb[1]);
+        mma::mma_bf16(acc1, a1[ks], bb[2], bb[3]);
+      }
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        const int t = r + half * 8;
+        if (t < n) {
+          const int col = nb * 8 + (lane & 3) * 2;
+          __nv_bfloat16* dst = po.U + ((tok0 + t) * H + h) * VD + col;
+          *reinterpret_cast<uint32_t*>(dst) = pack_bf16x2(acc0[half * 2], acc0[half * 2 + 1]);
+          *reinterpret_cast<uint32_t*>(dst + 8) = pack_bf16x2(acc1[half * 2], acc1[half * 2 + 1]);
+        }
+      }
+    }
+#pragma unroll
+    for (int nb = 0; nb < KD / 8; nb += 2) {
+      float acc0[4] = {0, 0, 0, 0}, acc1[4] = {0, 0, 0, 0};
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks) {
+        uint32_t bb[4];
+        mma::load_b_kn(bb, sm.K, SM::LK, ks * 16, nb * 8);
+        mma::mma_bf16(acc0, a2[ks], bb[0], bb[1]);
+        mma::mma_bf16(acc1, a2[ks], bb[2], bb[3]);
+      }
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        const int t = r + half * 8;
+        if (t < n) {
+          const int col = nb * 8 + (lane & 3) * 2;
+          __nv_bfloat16* dst = po.Kw + ((tok0 + t) * H + h) * KD + col;
+          *reinterpret_cast<uint32_t*>(dst) = pack_bf16x2(acc0[half * 2], acc0[half * 2 + 1]);
+          *reinterpret_cast<uint32_t*>(dst + 8) = pack_bf16x2(acc1[half * 2], acc1[half * 2 + 1]);
+        }
+      }
+    }
+  }
+}
+
+// ----------------------------------------------------------- chunk scan
+template <int KD, int VC>
+struct ScanSmem {
+  static constexpr int LK = KD + 8, LVC = VC + 8, LT = kC + 8;
+  __nv_bfloat16 Kw[kC * LK];
+  __nv_bfloat16 Q[kC * LK];
+  __nv_bfloat16 K[kC * LK];
+  __nv_bfloat16 Aqk[kC * LT];
+  __nv_bfloat16 Sh[KD * LVC], Sl[KD * LVC];   // state hi/lo
+  __nv_bfloat16 Wh[kC * LVC], Wl[kC * LVC];   // W hi/lo
+  __nv_bfloat16 Xh[kC * LVC], Xl[kC * LVC];   // diag(kscale) W hi/lo
+  float U[kC * VC];
+  float gate[kC * VC];
+  float qs[kC], ks[kC];
+  float sd;
+};
+
+__device__ __forceinline__ void split_store(__nv_bfloat16* hi, __nv_bfloat16* lo, int idx, float x0,
+                                            float x1) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
+  const float2 hf = __bfloat1622float2(h);
+  *reinterpret_cast<__nv_bfloat162*>(hi + idx) = h;
+  *reinterpret_cast<__nv_bfloat162*>(lo + idx) = __floats2bfloat162_rn(x0 - hf.x, x1 - hf.y);
+}
+
+template <int KD, int VD, int VC>
+__global__ void __launch_bounds__(128) gdn_chunk_scan_kernel(GdnIO io, int B, int T, int H,
+                                                             PrepOut po, float* __restrict__ state,
+                                                             __nv_bfloat16* __restrict__ out,
+                                                             int64_t so) {
+  using SM = ScanSmem<KD, VC>;
+  constexpr int NB = VC / 8;        // n-blocks of the value slice
+  constexpr int MT = KD / 64;       // 16-row state tiles per warp (KD/4 rows per warp)
+  extern __shared__ uint8_t smem_raw[];
+  SM& sm = *reinterpret_cast<SM*>(smem_raw);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nvs = VD / VC;
+  const int vs = blockIdx.x % nvs;
+  const int h = (blockIdx.x / nvs) % H;
+  const int b = blockIdx.x / (nvs * H);
+  const int v0 = vs * VC;
+  const int nC = static_cast<int>(ceil_div(T, kC));
+  const int r_lo = lane >> 2, cq = (lane & 3) * 2;
+
+  // ---- state rows [warp*KD/4, +KD/4) x VC columns in accumulator layout
+  float* Sg = state + (static_cast<int64_t>(b) * H + h) * KD * VD + v0;
+  float sacc[MT][NB][4];
+#pragma unroll
+  for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+    for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int kr = warp * (KD / 4) + mt * 16 + r_lo + (e >> 1) * 8;
+        const int vc = nb * 8 + cq + (e & 1);
+        sacc[mt][nb][e] = Sg[static_cast<int64_t>(kr) * VD + vc];
+      }
+
+  for (int c = 0; c < nC; ++c) {
+    const int t0 = c * kC;
+    const int n = min(kC, T - t0);
+    const int64_t tok0 = static_cast<int64_t>(b) * T + t0;
+    // ---- publish S (hi/lo) and load the chunk operands
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+      for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          const int kr = warp * (KD / 4) + mt * 16 + r_lo + half * 8;
+          split_store(sm.Sh, sm.Sl, kr * SM::LVC + nb * 8 + cq, sacc[mt][nb][half * 2],
+                      sacc[mt][nb][half * 2 + 1]);
+        }
+    for (int i = tid; i < kC * (KD / 8); i += 128) {
+      const int r = i / (KD / 8), cc = (i % (KD / 8)) * 8;
+      uint4 a = make_uint4(0, 0, 0, 0), qv = a, kv = a;
+      if (r < n) {
+        const int64_t tok = tok0 + r;
+        a = *reinterpret_cast<const uint4*>(po.Kw + (tok * H + h) * KD + cc);
+        qv = *reinterpret_cast<const uint4*>(io.q + tok * io.sq + h * KD + cc);
+        kv = *reinterpret_cast<const uint4*>(io.k + tok * io.sk + h * KD + cc);
+      }
+      *reinterpret_cast<uint4*>(&sm.Kw[r * SM::LK + cc]) = a;
+      *reinterpret_cast<uint4*>(&sm.Q[r * SM::LK + cc]) = qv;
+      *reinterpret_cast<uint4*>(&sm.K[r * SM::LK + cc]) = kv;
+    }
+    const __nv_bfloat16* aq = po.Aqk + ((static_cast<int64_t>(b) * H + h) * nC + c) * kC * kC;
+    for (int i = tid; i < kC * (kC / 8); i += 128) {
+      const int r = i / (kC / 8), cc = (i % (kC / 8)) * 8;
+      *reinterpret_cast<uint4*>(&sm.Aqk[r * SM::LT + cc]) =
+          *reinterpret_cast<const uint4*>(aq + r * kC + cc);
+    }
+    for (int i = tid; i < kC * VC; i += 128) {
+      const int r = i / VC, cc = i % VC;
+      float u = 0.f, g = 0.f;
+      if (r < n) {
+        const int64_t tok = tok0 + r;
+        u = bf2f(po.U[(tok * H + h) * VD + v0 + cc]);
+        g = bf2f(io.gate[tok * io.sg + h * VD + v0 + cc]);
+      }
+      sm.U[i] = u;
+      sm.gate[i] = g;
+    }
+    if (tid < kC) {
+      const int64_t tok = tok0 + tid;
+      sm.qs[tid] = tid < n ? po.qscale[tok * H + h] : 0.f;
+      sm.ks[tid] = tid < n ? po.kscale[tok * H + h] : 0.f;
+    }
+    if (tid == 0) sm.sd = po.sdecay[(static_cast<int64_t>(b) * H + h) * nC + c];
+    __syncthreads();
+
+    // ---- W = U - Kw S and QS for rows 16*warp..
+    float w[NB][4], qsacc[NB][4];
+#pragma unroll
+    for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) w[nb][e] = qsacc[nb][e] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < KD; kk += 16) {
+      uint32_t akw[4], aqq[4];
+      mma::load_a(akw, sm.Kw, SM::LK, warp * 16, kk);
+      mma::load_a(aqq, sm.Q, SM::LK, warp * 16, kk);
+#pragma unroll
+      for (int nb = 0; nb < NB; nb += 2) {
+        uint32_t bh[4], bl[4];
+        mma::load_b_kn(bh, sm.Sh, SM::LVC, kk, nb * 8);
+        mma::load_b_kn(bl, sm.Sl, SM::LVC, kk, nb * 8);
+        mma::mma_bf16(w[nb], akw, bh[0], bh[1]);
+        mma::mma_bf16(w[nb + 1], akw, bh[2], bh[3]);
+        mma::mma_bf16(w[nb], akw, bl[0], bl[1]);
+        mma::mma_bf16(w[nb + 1], akw, bl[2], bl[3]);
+        mma::mma_bf16(qsacc[nb], aqq, bh[0], bh[1]);
+        mma::mma_bf16(qsacc[nb + 1], aqq, bh[2], bh[3]);
+        mma::mma_bf16(qsacc[nb], aqq, bl[0], bl[1]);
+        mma::mma_bf16(qsacc[nb + 1], aqq, bl[2], bl[3]);
+      }
+    }
+#pragma unroll
+    for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        const int t = warp * 16 + r_lo + half * 8;
+        const int col = nb * 8 + cq;
+        const float w0 = sm.U[t * VC + col] - w[nb][half * 2];
+        const float w1 = sm.U[t * VC + col + 1] - w[nb][half * 2 + 1];
+        w[nb][half * 2] = w0;
+        w[nb][half * 2 + 1] = w1;
+        split_store(sm.Wh, sm.Wl, t * SM::LVC + col, w0, w1);
+        split_store(sm.Xh, sm.Xl, t * SM::LVC + col, w0 * sm.ks[t], w1 * sm.ks[t]);
+      }
+    __syncthreads();
+
+    // ---- O = qs * QS + Aqk W ; out = O * gate
+    float o[NB][4];
+#pragma unroll
+    for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) o[nb][e] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < kC; kk += 16) {
+      uint32_t aa[4];
+      mma::load_a(aa, sm.Aqk, SM::LT, warp * 16, kk);
+#pragma unroll
+      for (int nb = 0; nb < NB; nb += 2) {
+        uint32_t bh[4], bl[4];
+        mma::load_b_kn(bh, sm.Wh, SM::LVC, kk, nb * 8);
+        mma::load_b_kn(bl, sm.Wl, SM::LVC, kk, nb * 8);
+        mma::mma_bf16(o[nb], aa, bh[0], bh[1]);
+        mma::mma_bf16(o[nb + 1], aa, bh[2], bh[3]);
+        mma::mma_bf16(o[nb], aa, bl[0], bl[1]);
+        mma::mma_bf16(o[nb + 1], aa, bl[2], bl[3]);
+      }
+    }
+#pragma unroll
+    for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        const int t = warp * 16 + r_lo + half * 8;
+        if (t < n) {
+          const int col = nb * 8 + cq;
+          const float o0 = sm.qs[t] * qsacc[nb][half * 2] + o[nb][half * 2];
+          const float o1 = sm.qs[t] * qsacc[nb][half * 2 + 1] + o[nb][half * 2 + 1];
+          // reference order: out.to(hidden dtype) * gate
+          const float r0 = bf2f(f2bf(o0)) * sm.gate[t * VC + col];
+          const float r1 = bf2f(f2bf(o1)) * sm.gate[t * VC + col + 1];
+          *reinterpret_cast<uint32_t*>(out + (tok0 + t) * so + h * VD + v0 + col) =
+              pack_bf16x2(r0, r1);
+        }
+      }
+
+    // ---- S <- sd * S + K^T diag(ks) W   (rows warp*KD/4 ..)
+    const float sd = sm.sd;
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+      for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) sacc[mt][nb][e] *= sd;
+#pragma unroll
+    for (int kk = 0; kk < kC; kk += 16) {
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt) {
+        uint32_t ak[4];
+        mma::load_a_t(ak, sm.K, SM::LK, warp * (KD / 4) + mt * 16, kk);
+#pragma unroll
+        for (int nb = 0; nb < NB; nb += 2) {
+          uint32_t bh[4], bl[4];
+          mma::load_b_kn(bh, sm.Xh, SM::LVC, kk, nb * 8);
+          mma::load_b_kn(bl, sm.Xl, SM::LVC, kk, nb * 8);
+          mma::mma_bf16(sacc[mt][nb], ak, bh[0], bh[1]);
+          mma::mma_bf16(sacc[mt][nb + 1], ak, bh[2], bh[3]);
+          mma::mma_bf16(sacc[mt][nb], ak, bl[0], bl[1]);
+          mma::mma_bf16(sacc[mt][nb + 1], ak, bl[2], bl[3]);
+        }
+      }
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+    for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int kr = warp * (KD / 4) + mt * 16 + r_lo + (e >> 1) * 8;
+        const int vc = nb * 8 + cq + (e & 1);
+        Sg[static_cast<int64_t>(kr) * VD + vc] = sacc[mt][nb][e];
+      }
+}
+
+// ------------------------------------------------------------ conv gate
+// Decode/prefill epilogue of the GDN mixer (gated_deltanet.py:254-276):
+//   y[t] = out_proj(o)[t] * sigmoid(sum_j w[:, j] * x[t - 3 + j])
+// x = block input (normed hidden) [B, T, D]; history [B, 3, D] holds the
+// previous three inputs (decode) or is null (prefill: zero left padding).
+// Taps that cross a reset (same-segment rule of :56-78) are dropped.  With
+// `residual` non-null the result is added into it (streams += mixed).
+// When `history` is given and `roll_history` is set, the history is advanced
+// by the last T inputs (model/model.py:283-289).
+__global__ void gdn_conv_gate_kernel(const __nv_bfloat16* __restrict__ x,
+                                     const __nv_bfloat16* __restrict__ y_proj,
+                                     const float* __restrict__ conv_w, __nv_bfloat16* history,
+                                     const uint8_t* __restrict__ reset, int B, int T, int D,
+                                     __nv_bfloat16* __restrict__ out,
+                                     __nv_bfloat16* __restrict__ residual) {
+  const int64_t total = static_cast<int64_t>(B) * T * D;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int d = static_cast<int>(i % D);
+    const int64_t bt = i / D;
+    const int t = static_cast<int>(bt % T);
+    const int b = static_cast<int>(bt / T);
+    float acc = 0.f;
+    // segment of t: taps from before the latest reset at or before t are dropped
+    int seg_start = 0;
+    if (reset != nullptr) {
+      for (int j = 0; j <= min(t, 3); ++j)
+        if (reset[static_cast<int64_t>(b) * T + (t - j)]) {
+          seg_start = t - j;
+          break;
+        }
+    }
+    const bool hist_ok = history != nullptr &&
+                         !(reset != nullptr && seg_start == 0 &&
+                           reset[static_cast<int64_t>(b) * T] != 0);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int tt = t - 3 + j;
+      float xv = 0.f;
+      if (tt >= 0) {
+        if (tt >= seg_start) xv = bf2f(x[(static_cast<int64_t>(b) * T + tt) * D + d]);
+      } else if (hist_ok && seg_start == 0) {
+        xv = bf2f(history[(static_cast<int64_t>(b) * 3 + (3 + tt)) * D + d]);
+      }
+      acc += conv_w[d * 4 + j] * xv;
+    }
+    const float yv = bf2f(y_proj[i]) * sigmoidf_(acc);
+    if (residual != nullptr) {
+      residual[i] = f2bf(bf2f(residual[i]) + bf2f(f2bf(yv)));
+    } else {
+      out[i] = f2bf(yv);
+    }
+  }
+}
+
+// history[b] <- the last three block inputs of row b (older slots shift in
+// from the previous history when T < 3).  One CTA per row; all reads land in
+// shared memory before any write.
+__global__ void gdn_conv_roll_kernel(const __nv_bfloat16* __restrict__ x,
+                                     __nv_bfloat16* __restrict__ history, int T, int D) {
+  extern __shared__ __nv_bfloat16 s_roll[];  // [3, D]
+  const int b = blockIdx.x;
+  for (int i = threadIdx.x; i < 3 * D; i += blockDim.x) {
+    const int j = i / D, d = i - j * D;
+    const int src = T - 3 + j;
+    s_roll[i] = src >= 0 ? x[(static_cast<int64_t>(b) * T + src) * D + d]
+                         : history[(static_cast<int64_t>(b) * 3 + (3 + src)) * D + d];
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < 3 * D; i += blockDim.x)
+    history[static_cast<int64_t>(b) * 3 * D + i] = s_roll[i];
+}
+
+template <typename K>
+int32_t set_smem(K kernel, int bytes) {
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  return e == cudaSuccess ? LLMYB_OK : static_cast<int32_t>(e);
+}
+
+int32_t check_io(const GdnIO& io, int KD, int VD) {
+  if (!io.q || !io.k || !io.v || !io.gate || !io.beta) return LLMYB_EINVAL;
+  if (!io.decay_logit && !io.log_alpha) return LLMYB_EINVAL;
+  if (!((KD == 64 || KD == 128) && (VD == 64 || VD == 128))) return LLMYB_EUNSUPPORTED;
+  return LLMYB_OK;
+}
+
+GdnIO make_io(const void* q, int64_t sq, const void* k, int64_t sk, const void* v, int64_t sv,
+              const void* gate, int64_t sg, const void* beta, int64_t sb,
+              const float* decay_logit, const float* log_alpha, const uint8_t* reset) {
+  GdnIO io;
+  io.q = static_cast<const __nv_bfloat16*>(q);
+  io.k = static_cast<const __nv_bfloat16*>(k);
+  io.v = static_cast<const __nv_bfloat16*>(v);
+  io.gate = static_cast<const __nv_bfloat16*>(gate);
+  io.beta = static_cast<const __nv_bfloat16*>(beta);
+  io.sq = sq; io.sk = sk; io.sv = sv; io.sg = sg; io.sb = sb;
+  io.decay_logit = decay_logit;
+  io.log_alpha = log_alpha;
+  io.reset = reset;
+  return io;
+}
+
+struct ScratchLayout {
+  int64_t u, kw, aqk, qs, ks, sd, total;
+};
+
+ScratchLayout scratch_layout(int B, int T, int H, int KD, int VD) {
+  auto al = [](int64_t x) { return (x + 255) / 256 * 256; };
+  const int64_t nC = ceil_div(T, kC);
+  const int64_t bt = static_cast<int64_t>(B) * T;
+  ScratchLayout s;
+  s.u = 0;
+  s.kw = s.u + al(bt * H * VD * 2);
+  s.aqk = s.kw + al(bt * H * KD * 2);
+  s.qs = s.aqk + al(static_cast<int64_t>(B) * H * nC * kC * kC * 2);
+  s.ks = s.qs + al(bt * H * 4);
+  s.sd = s.ks + al(bt * H * 4);
+  s.total = s.sd + al(static_cast<int64_t>(B) * H * nC * 4);
+  return s;
+}
+
+template <int KD, int VD>
+int32_t launch_prefill(const GdnIO& io, int B, int T, int H, void* scratch, float* state,
+                       __nv_bfloat16* out, int64_t so, cudaStream_t s) {
+  const ScratchLayout L = scratch_layout(B, T, H, KD, VD);
+  uint8_t* base = static_cast<uint8_t*>(scratch);
+  PrepOut po;
+  po.U = reinterpret_cast<__nv_bfloat16*>(base + L.u);
+  po.Kw = reinterpret_cast<__nv_bfloat16*>(base + L.kw);
+  po.Aqk = reinterpret_cast<__nv_bfloat16*>(base + L.aqk);
+  po.qscale = reinterpret_cast<float*>(base + L.qs);
+  po.kscale = reinterpret_cast<float*>(base + L.ks);
+  po.sdecay = reinterpret_cast<float*>(base + L.sd);
+  const int nC = static_cast<int>(ceil_div(T, kC));
+  constexpr int kPrepSmem = sizeof(PrepSmem<KD, VD>);
+  constexpr int VC = 32;
+  constexpr int kScanSmem = sizeof(ScanSmem<KD, VC>);
+  static bool attrs = false;
+  if (!attrs) {
+    int32_t st = set_smem(gdn_chunk_prep_kernel<KD, VD>, kPrepSmem);
+    if (st) return st;
+    st = set_smem(gdn_chunk_scan_kernel<KD, VD, VC>, kScanSmem);
+    if (st) return st;
+    attrs = true;
+  }
+  gdn_chunk_prep_kernel<KD, VD><<<B * H * nC, 128, kPrepSmem, s>>>(io, B, T, H, po);
+  gdn_chunk_scan_kernel<KD, VD, VC><<<B * H * (VD / VC), 128, kScanSmem, s>>>(io, B, T, H, po,
+                                                                             state, out, so);
+  return launch_status();
+}
+
+}  // namespace
+}  // namespace llmyb
+
+using namespace llmyb;
+
+LLMYB_API int32_t llmyb_gdn_activate(void* proj, int64_t n_tokens, int32_t width, int32_t heads,
+                                     int32_t key_dim, int32_t value_dim, const float* beta_bias,
+                                     void* stream) {
+  if (!proj || n_tokens < 0 || heads <= 0 || key_dim <= 0 || value_dim <= 0) return LLMYB_EINVAL;
+  if (width < 2 * heads * (key_dim + value_dim) + heads) return LLMYB_EINVAL;
+  if (n_tokens == 0) return LLMYB_OK;
+  const int64_t warps = n_tokens * heads;
+  gdn_activate_kernel<<<static_cast<int>(ceil_div(warps * 32, 256)), 256, 0,
+                        static_cast<cudaStream_t>(stream)>>>(
+      static_cast<__nv_bfloat16*>(proj), n_tokens, width, heads, key_dim, value_dim, beta_bias);
+  return launch_status();
+}
+
+// One decode token per row: state [B,H,K,V] fp32 updated in place.
+LLMYB_API int32_t llmyb_gdn_step(const void* q, int64_t q_stride, const void* k, int64_t k_stride,
+                                 const void* v, int64_t v_stride, const void* gate,
+                                 int64_t gate_stride, const void* beta, int64_t beta_stride,
+                                 const float* decay_logit, const float* log_alpha,
+                                 const uint8_t* reset, int32_t batch, int32_t heads,
+                                 int32_t key_dim, int32_t value_dim, float* state, void* out,
+                                 int64_t out_stride, void* stream) {
+  const GdnIO io = make_io(q, q_stride, k, k_stride, v, v_stride, gate, gate_stride, beta,
+                           beta_stride, decay_logit, log_alpha, reset);
+  int32_t st = check_io(io, key_dim, value_dim);
+  if (st) return st;
+  if (!state || !out || batch < 0 || heads <= 0) return LLMYB_EINVAL;
+  if (batch == 0) return LLMYB_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int grid = batch * heads * (value_dim / 32);
+  auto* o = static_cast<__nv_bfloat16*>(out);
+  if (key_dim == 64)
+    gdn_step_kernel<64><<<grid, 128, 0, s>>>(io, heads, value_dim, state, o, out_stride);
+  else
+    gdn_step_kernel<128><<<grid, 128, 0, s>>>(io, heads, value_dim, state, o, out_stride);
+  return launch_status();
+}
+
+LLMYB_API int64_t llmyb_gdn_prefill_scratch_bytes(int32_t batch, int32_t seq, int32_t heads,
+                                                  int32_t key_dim, int32_t value_dim) {
+  if (batch < 0 || seq < 0 || heads <= 0 || key_dim <= 0 || value_dim <= 0) return -1;
+  return scratch_layout(batch, seq, heads, key_dim, value_dim).total;
+}
+
+// Chunked scan over [B, T] tokens (token index b*T + t): state [B,H,K,V] fp32
+// is read as the initial state and overwritten with the final state.
+LLMYB_API int32_t llmyb_gdn_prefill(const void* q, int64_t q_stride, const void* k,
+                                    int64_t k_stride, const void* v, int64_t v_stride,
+                                    const void* gate, int64_t gate_stride, const void* beta,
+                                    int64_t beta_stride, const float* decay_logit,
+                                    const float* log_alpha, const uint8_t* reset, int32_t batch,
+                                    int32_t seq, int32_t heads, int32_t key_dim,
+                                    int32_t value_dim, float* state, void* out,
+                                    int64_t out_stride, void* scratch, void* stream) {
+  const GdnIO io = make_io(q, q_stride, k, k_stride, v, v_stride, gate, gate_stride, beta,
+                           beta_stride, decay_logit, log_alpha, reset);
+  int32_t st = check_io(io, key_dim, value_dim);
+  if (st) return st;
+  if (!state || !out || !scratch || batch < 0 || seq < 0 || heads <= 0) return LLMYB_EINVAL;
+  if (batch == 0 || seq == 0) return LLMYB_OK;
+  if ((q_stride | k_stride | v_stride) % 8 != 0) return LLMYB_EUNSUPPORTED;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  auto* o = static_cast<__nv_bfloat16*>(out);
+  if (key_dim == 64 && value_dim == 64)
+    return launch_prefill<64, 64>(io, batch, seq, heads, scratch, state, o, out_stride, s);
+  if (key_dim == 128 && value_dim == 128)
+    return launch_prefill<128, 128>(io, batch, seq, heads, scratch, state, o, out_stride, s);
+  if (key_dim == 64 && value_dim == 128)
+    return launch_prefill<64, 128>(io, batch, seq, heads, scratch, state, o, out_stride, s);
+  return launch_prefill<128, 64>(io, batch, seq, heads, scratch, state, o, out_stride, s);
+}
+
+// Conv gate + (optional) residual add + (optional) history roll; see
+// gdn_conv_gate_kernel.  x, y_proj, out, residual: [B*T, D] bf16; conv_w
+// [D, 4] fp32; history [B, 3, D] bf16 or null.
+LLMYB_API int32_t llmyb_gdn_conv_gate(const void* x, const void* y_proj, const float* conv_w,
+                                      void* history, const uint8_t* reset, int32_t batch,
+                                      int32_t seq, int32_t d_model, void* out, void* residual,
+                                      int32_t roll_history, void* stream) {
+  if (!x || !y_proj || !conv_w || batch < 0 || seq < 0 || d_model <= 0) return LLMYB_EINVAL;
+  if (!out && !residual) return LLMYB_EINVAL;
+  if (roll_history && !history) return LLMYB_EINVAL;
+  if (batch == 0 || seq == 0) return LLMYB_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t total = static_cast<int64_t>(batch) * seq * d_model;
+  const int grid = static_cast<int>(std::min<int64_t>(ceil_div(total, 256), 148 * 16));
+  gdn_conv_gate_kernel<<<grid, 256, 0, s>>>(
+      static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(y_proj), conv_w,
+      static_cast<__nv_bfloat16*>(history), reset, batch, seq, d_model,
+      static_cast<__nv_bfloat16*>(out), static_cast<__nv_bfloat16*>(residual));
+  if (roll_history) {
+    gdn_conv_roll_kernel<<<batch, 256, 3 * d_model * sizeof(__nv_bfloat16), s>>>(
+        static_cast<const __nv_bfloat16*>(x), static_cast<__nv_bfloat16*>(history), seq, d_model);
+  }
+  return launch_status();
+}

@@ -88,29 +88,17 @@ __device__ __forceinline__ float warp_topk_softmax(float val, int k, int lane) {
 
 __global__ void __launch_bounds__(256) router_topk_kernel(
     const float* __restrict__ logits, const float* __restrict__ bias, int N, int E, int k,
-    int64_t* __restrict__ topk_idx, float* __restrict__ topk_prob, int* __restrict__ hist) {
-  __shared__ int s_hist[kMaxExperts];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  if (hist != nullptr) {
-    for (int e = threadIdx.x; e < E; e += blockDim.x) s_hist[e] = 0;
-    __syncthreads();
-  }
-  const int chunk0 = blockIdx.x * kChunk;
-  for (int t = chunk0 + warp; t < min(N, chunk0 + kChunk); t += 8) {
-    int idx;
-    float val;
-    warp_topk_row(logits + static_cast<int64_t>(t) * E, bias, E, k, lane, idx, val);
-    const float p = warp_topk_softmax(val, k, lane);
-    if (lane < k) {
-      topk_idx[static_cast<int64_t>(t) * k + lane] = idx;
-      topk_prob[static_cast<int64_t>(t) * k + lane] = p;
-      if (hist != nullptr) atomicAdd(&s_hist[idx], 1);
-    }
-  }
-  if (hist != nullptr) {
-    __syncthreads();
-    const int nchunks = gridDim.x;
-    for (int e = threadIdx.x; e < E; e += blockDim.x) hist[e * nchunks + blockIdx.x] = s_hist[e];
+    int64_t* __restrict__ topk_idx, float* __restrict__ topk_prob) {
+  const int lane = threadIdx.x & 31;
+  const int t = blockIdx.x * 8 + (threadIdx.x >> 5);  // one token per warp
+  if (t >= N) return;
+  int idx;
+  float val;
+  warp_topk_row(logits + static_cast<int64_t>(t) * E, bias, E, k, lane, idx, val);
+  const float p = warp_topk_softmax(val, k, lane);
+  if (lane < k) {
+    topk_idx[static_cast<int64_t>(t) * k + lane] = idx;
+    topk_prob[static_cast<int64_t>(t) * k + lane] = p;
   }
 }
 
@@ -243,12 +231,18 @@ __global__ void __launch_bounds__(256) plan_scatter_kernel(
   __syncwarp();
   const int t0 = blockIdx.x * kChunk + warp * 32;
   const int tn = max(0, min(32, N - t0));
-  // phase 1: per-warp counts
-  for (int j = 0; j < tn; ++j) {
-    if (lane < k) {
-      const int64_t e = topk_idx[static_cast<int64_t>(t0 + j) * k + lane];
-      if (e >= 0 && e < E) my[e] += 1;  // a token's experts are distinct: no lane collision
-    }
+  // lane s holds slot s of the warp's 32 tokens (loads issued together)
+  int ev[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    int64_t e = -1;
+    if (j < tn && lane < k) e = topk_idx[static_cast<int64_t>(t0 + j) * k + lane];
+    ev[j] = (e >= 0 && e < E) ? static_cast<int>(e) : -1;  // -1: absent or flagged
+  }
+  // phase 1: per-warp counts (a token's experts are distinct: no lane collision)
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    if (ev[j] >= 0) my[ev[j]] += 1;
     __syncwarp();
   }
   __syncthreads();
@@ -262,14 +256,13 @@ __global__ void __launch_bounds__(256) plan_scatter_kernel(
     }
   }
   __syncthreads();
-  for (int j = 0; j < tn; ++j) {
-    if (lane < k) {
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    if (ev[j] >= 0) {
       const int t = t0 + j;
       const int64_t r = static_cast<int64_t>(t) * k + lane;
-      const int64_t e = topk_idx[r];
-      if (e < 0 || e >= E) continue;  // flagged by plan_hist_kernel
-      const int pos = my[e];
-      my[e] = pos + 1;
+      const int pos = my[ev[j]];
+      my[ev[j]] = pos + 1;
       perm_token[pos] = t;
       perm_prob[pos] = topk_prob[r];
       route_pos[r] = pos;
@@ -360,9 +353,9 @@ LLMYB_API int32_t llmyb_router_topk(const float* logits, const float* bias, int3
   if (st) return st;
   if (n_tokens == 0) return LLMYB_OK;
   if (!logits || !topk_idx || !topk_prob) return LLMYB_EINVAL;
-  const int nchunks = static_cast<int>(ceil_div(n_tokens, kChunk));
-  router_topk_kernel<<<nchunks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      logits, bias, n_tokens, n_experts, top_k, topk_idx, topk_prob, nullptr);
+  router_topk_kernel<<<static_cast<int>(ceil_div(n_tokens, 8)), 256, 0,
+                       static_cast<cudaStream_t>(stream)>>>(logits, bias, n_tokens, n_experts,
+                                                            top_k, topk_idx, topk_prob);
   return launch_status();
 }
 
@@ -442,8 +435,10 @@ LLMYB_API int32_t llmyb_route(const float* logits, const float* bias, int32_t n_
   if (!scratch) return LLMYB_EINVAL;
   const int nchunks = static_cast<int>(ceil_div(n_tokens, kChunk));
   int* hist = static_cast<int*>(scratch);
-  router_topk_kernel<<<nchunks, 256, 0, s>>>(logits, bias, n_tokens, n_experts, top_k, topk_idx,
-                                             topk_prob, hist);
+  router_topk_kernel<<<static_cast<int>(ceil_div(n_tokens, 8)), 256, 0, s>>>(
+      logits, bias, n_tokens, n_experts, top_k, topk_idx, topk_prob);
+  plan_hist_kernel<<<nchunks, 256, n_experts * sizeof(int), s>>>(topk_idx, n_tokens, n_experts,
+                                                                 top_k, hist, nullptr);
   return plan_tail(topk_idx, topk_prob, n_tokens, n_experts, top_k, tile_m, expert_counts,
                    expert_offsets, tile_offsets, perm_token, perm_prob, route_pos, sort_order,
                    hist, s);

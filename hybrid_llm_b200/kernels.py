@@ -171,3 +171,98 @@ def moe_grouped(x: torch.Tensor, plan: RoutePlan, w13: torch.Tensor, w2: torch.T
                  _ptr(plan.tile_offsets), e, _ptr(w13), _ptr(w2), f, _ptr(scratch), _ptr(out),
                  _ptr(device_status(x.device)), _stream())
     return out
+
+
+# ------------------------------------------------------------------- GDN
+def _heads_view(t: torch.Tensor, name: str) -> tuple[int, int]:
+    """(data pointer, elements between consecutive tokens) of a [..., H, D] view
+    whose last two dims are packed and whose tokens are evenly strided."""
+    if t.dtype != torch.bfloat16:
+        raise ValueError(f"{name} must be bf16")
+    if t.stride(-1) != 1 or t.stride(-2) != t.shape[-1]:
+        raise ValueError(f"{name}: last two dims must be contiguous")
+    tok = t.stride(-3)
+    if t.dim() == 4 and t.stride(0) != t.shape[1] * tok:
+        raise ValueError(f"{name}: tokens must be evenly strided")
+    return t.data_ptr(), tok
+
+
+def _beta_view(beta: torch.Tensor) -> tuple[int, int]:
+    """beta [..., tokens, H] (bf16, heads contiguous) -> (pointer, token stride)."""
+    if beta.dtype != torch.bfloat16:
+        raise ValueError("beta must be bf16")
+    if beta.stride(-1) != 1:
+        raise ValueError("beta heads must be contiguous")
+    return beta.data_ptr(), beta.stride(-2)
+
+
+def gdn_activate(proj: torch.Tensor, heads: int, key_dim: int, value_dim: int,
+                 beta_bias: torch.Tensor | None) -> None:
+    """In place on the fused [N, 2HK+2HV+H] projection: L2-normalise q,k per head,
+    sigmoid(gate), sigmoid(beta + bias)  (gated_deltanet.py:128-131)."""
+    _require_cuda(proj)
+    n = proj.numel() // proj.shape[-1]
+    _native.call("llmyb_gdn_activate", _ptr(proj), n, proj.shape[-1], heads, key_dim, value_dim,
+                 _ptr(beta_bias), _stream())
+
+
+def gdn_step(q, k, v, gate, beta, state, *, decay_logit=None, log_alpha=None, reset=None,
+             out=None):
+    """One decode token per row.  q,k [B,H,K]; v,gate [B,H,V]; beta [B,H] (all bf16,
+    already activated); state [B,H,K,V] fp32 updated in place; returns out [B,H,V] bf16."""
+    _require_cuda(q, k, v, gate, beta, state)
+    bsz, h, kd = q.shape
+    vd = v.shape[-1]
+    qp, qs = _heads_view(q, "q")
+    kp, ks = _heads_view(k, "k")
+    vp, vs = _heads_view(v, "v")
+    gp, gs = _heads_view(gate, "gate")
+    bp, bs = _beta_view(beta)
+    if out is None:
+        out = torch.empty(bsz, h, vd, dtype=torch.bfloat16, device=q.device)
+    if state.dtype != torch.float32 or not state.is_contiguous():
+        raise ValueError("state must be contiguous fp32")
+    r = None if reset is None else reset.to(torch.uint8).contiguous()
+    _native.call("llmyb_gdn_step", qp, qs, kp, ks, vp, vs, gp, gs, bp, bs, _ptr(decay_logit),
+                 _ptr(log_alpha), _ptr(r), bsz, h, kd, vd, _ptr(state), _ptr(out),
+                 out.stride(-3), _stream())
+    return out
+
+
+def gdn_prefill(q, k, v, gate, beta, state, *, decay_logit=None, log_alpha=None, reset=None,
+                out=None, scratch=None):
+    """Chunked scan over [B,T] tokens.  q,k [B,T,H,K]; v,gate [B,T,H,V]; beta [B,T,H]
+    (bf16, activated); state [B,H,K,V] fp32 in/out; returns out [B,T,H,V] bf16."""
+    _require_cuda(q, k, v, gate, beta, state)
+    bsz, t, h, kd = q.shape
+    vd = v.shape[-1]
+    qp, qs = _heads_view(q, "q")
+    kp, ks = _heads_view(k, "k")
+    vp, vs = _heads_view(v, "v")
+    gp, gs = _heads_view(gate, "gate")
+    bp, bs = _beta_view(beta)
+    if out is None:
+        out = torch.empty(bsz, t, h, vd, dtype=torch.bfloat16, device=q.device)
+    need = int(_native.lib().llmyb_gdn_prefill_scratch_bytes(bsz, t, h, kd, vd))
+    if scratch is None or scratch.numel() < need:
+        scratch = torch.empty(max(need, 16), dtype=torch.uint8, device=q.device)
+    r = None if reset is None else reset.to(torch.uint8).contiguous()
+    la = None if log_alpha is None else log_alpha.to(torch.float32).contiguous()
+    _native.call("llmyb_gdn_prefill", qp, qs, kp, ks, vp, vs, gp, gs, bp, bs, _ptr(decay_logit),
+                 _ptr(la), _ptr(r), bsz, t, h, kd, vd, _ptr(state), _ptr(out), out.stride(-3),
+                 _ptr(scratch), _stream())
+    return out
+
+
+def gdn_conv_gate(x, y_proj, conv_w, *, history=None, reset=None, out=None, residual=None,
+                  roll_history=False):
+    """y = y_proj * sigmoid(causal_conv4(x)); into `out` or added into `residual`."""
+    _require_cuda(x, y_proj, conv_w)
+    bsz, t, d = x.shape
+    w = conv_w.reshape(d, -1).to(torch.float32).contiguous()
+    if out is None and residual is None:
+        out = torch.empty_like(y_proj)
+    r = None if reset is None else reset.to(torch.uint8).contiguous()
+    _native.call("llmyb_gdn_conv_gate", _ptr(x), _ptr(y_proj), _ptr(w), _ptr(history), _ptr(r),
+                 bsz, t, d, _ptr(out), _ptr(residual), int(roll_history), _stream())
+    return residual if residual is not None else out

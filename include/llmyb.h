@@ -88,6 +88,56 @@ int32_t llmyb_moe_grouped_swiglu(const void* x, int32_t n_tokens, int32_t d_mode
                                  const void* w2, int32_t ffn, void* scratch, void* out,
                                  int32_t* dev_status, void* stream);
 
+/* ------------------------------------------------------ gated delta rule
+ * Replaces GatedDeltaNet's recurrence (model/layers/gated_deltanet.py:140-149
+ * and the seams _triton_gdn_scan/_triton_gdn_step at :179-235), the Triton
+ * kernels (sample_standalone.py:435-531) and the native gdn_step /
+ * gdn_conv_gate kernels (llmy_cuda/src/kernels/gdn.cu:22-145).
+ * Token-major bf16 inputs are given as (pointer, stride): element (token, h, i)
+ * lives at ptr[token*stride + h*dim + i], so q/k/v/gate/beta may be views into
+ * one fused projection.  alpha = sigmoid(decay_logit[h]) (reference), or
+ * exp(log_alpha[token, h]) when log_alpha is non-null.  K, V in {64, 128}. */
+
+/* In place on proj [N, width] = [q (H*K) | k (H*K) | v (H*V) | gate (H*V) | beta (H)]:
+ * q,k L2-normalised per head, gate = sigmoid(gate), beta = sigmoid(beta + bias). */
+int32_t llmyb_gdn_activate(void* proj, int64_t n_tokens, int32_t width, int32_t heads,
+                           int32_t key_dim, int32_t value_dim, const float* beta_bias,
+                           void* stream);
+
+/* One token per row (decode): state [B,H,K,V] fp32 updated in place;
+ * out (row stride out_stride) = ((S^T q) rounded to bf16) * gate. */
+int32_t llmyb_gdn_step(const void* q, int64_t q_stride, const void* k, int64_t k_stride,
+                       const void* v, int64_t v_stride, const void* gate, int64_t gate_stride,
+                       const void* beta, int64_t beta_stride, const float* decay_logit,
+                       const float* log_alpha, const uint8_t* reset, int32_t batch,
+                       int32_t heads, int32_t key_dim, int32_t value_dim, float* state,
+                       void* out, int64_t out_stride, void* stream);
+
+/* Scratch bytes needed by llmyb_gdn_prefill. */
+int64_t llmyb_gdn_prefill_scratch_bytes(int32_t batch, int32_t seq, int32_t heads,
+                                        int32_t key_dim, int32_t value_dim);
+
+/* Chunked (C = 64) scan over [B, T] tokens with resets: state [B,H,K,V] fp32
+ * holds the initial state on entry and the final state on exit. */
+int32_t llmyb_gdn_prefill(const void* q, int64_t q_stride, const void* k, int64_t k_stride,
+                          const void* v, int64_t v_stride, const void* gate, int64_t gate_stride,
+                          const void* beta, int64_t beta_stride, const float* decay_logit,
+                          const float* log_alpha, const uint8_t* reset, int32_t batch,
+                          int32_t seq, int32_t heads, int32_t key_dim, int32_t value_dim,
+                          float* state, void* out, int64_t out_stride, void* scratch,
+                          void* stream);
+
+/* GDN epilogue (gated_deltanet.py:254-276): y = y_proj * sigmoid(conv4(x)),
+ * depthwise causal conv over the block input x [B,T,D] with weight [D,4]
+ * fp32; history [B,3,D] (decode) or null (prefill, zero left padding).  The
+ * result goes to `out`, or is added into `residual` when that is non-null;
+ * roll_history advances the history by the last inputs
+ * (model/model.py:283-289). */
+int32_t llmyb_gdn_conv_gate(const void* x, const void* y_proj, const float* conv_w,
+                            void* history, const uint8_t* reset, int32_t batch, int32_t seq,
+                            int32_t d_model, void* out, void* residual, int32_t roll_history,
+                            void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -48,3 +48,23 @@ def moe_case(tag: str):
         w_down=rng.normal(0, 0.05, (e, d, f)).astype(np.float32),
         k=k,
     )
+
+
+GDN_CASES = {"a": (2, 40, 64, 2, 64, 64), "b": (1, 130, 128, 2, 64, 64)}
+
+
+def gdn_case(tag: str):
+    """GatedDeltaNet weights (reference parameter names), input, state and resets."""
+    b, t, d, h, kd, vd = GDN_CASES[tag]
+    rng = np.random.default_rng(3000 + ord(tag))
+    w = lambda *s: rng.normal(0, 0.1, s).astype(np.float32)
+    p = dict(q_proj=w(h * kd, d), k_proj=w(h * kd, d), v_proj=w(h * vd, d), beta_proj=w(h, d),
+             beta_bias=w(h), gate_proj=w(h * vd, d), out_proj=w(d, h * vd), conv=w(d, 1, 4),
+             decay_logit=rng.uniform(0.5, 3.0, h).astype(np.float32))
+    hidden = rng.normal(0, 1, (b, t, d)).astype(np.float32)
+    state = rng.normal(0, 0.3, (b, h, kd, vd)).astype(np.float32)
+    reset = np.zeros((b, t), dtype=bool)
+    reset[0, t // 3] = True
+    steps = rng.normal(0, 1, (b, 3, d)).astype(np.float32)  # decode tokens after the prefix
+    return dict(p=p, hidden=hidden, state=state, reset=reset, steps=steps, heads=h, key_dim=kd,
+                value_dim=vd)

@@ -112,7 +112,43 @@ def sec_moe() -> None:
     save("moe", **out)
 
 
-SECTIONS = {"router": sec_router, "moe": sec_moe}
+def sec_gdn() -> None:
+    """GatedDeltaNet.forward (gated_deltanet.py:119-276): prefill with resets, then
+    three decode steps with the conv history the block keeps (model/model.py:283-289)."""
+    gdn_mod, _ = _ref_import()
+    out = {}
+    for tag in inputs.GDN_CASES:
+        c = inputs.gdn_case(tag)
+        p = c["p"]
+        d = c["hidden"].shape[-1]
+        m = gdn_mod.GatedDeltaNet(d, c["heads"], c["heads"], c["key_dim"], c["value_dim"], 4)
+        with torch.no_grad():
+            for name in ("q_proj", "k_proj", "v_proj", "beta_proj", "gate_proj", "out_proj"):
+                getattr(m, name).weight.copy_(t(p[name]))
+            m.beta_proj.bias.copy_(t(p["beta_bias"]))
+            m.conv.weight.copy_(t(p["conv"]))
+            m.decay_logit.copy_(t(p["decay_logit"]))
+        scan = []
+        m.out_proj.register_forward_pre_hook(lambda mod, a: scan.append(a[0].detach().clone()))
+        with torch.no_grad():
+            y, s_pre = m(t(c["hidden"]), t(c["state"]), t(c["reset"]), reference=True)
+            s = s_pre.clone()
+            hist = t(c["hidden"])[:, -3:].clone()
+            ys, ss = [], []
+            for i in range(c["steps"].shape[1]):
+                x1 = t(c["steps"][:, i:i + 1])
+                y1, s = m(x1, s.clone(), None, conv_history=hist)
+                hist = torch.cat([hist[:, 1:], x1], dim=1)
+                ys.append(y1.numpy())
+                ss.append(s.numpy())
+        out.update({f"{tag}_checksum": inputs.checksum(c["hidden"], c["state"], *p.values()),
+                    f"{tag}_out": y.numpy(), f"{tag}_prefill_state": s_pre.numpy(),
+                    f"{tag}_scan": scan[0].numpy(), f"{tag}_step_out": np.stack(ys, 1),
+                    f"{tag}_step_state": ss[-1]})
+    save("gdn", **out)
+
+
+SECTIONS = {"router": sec_router, "moe": sec_moe, "gdn": sec_gdn}
 
 
 def main(argv: list[str]) -> None:
