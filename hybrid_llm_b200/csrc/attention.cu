@@ -1,0 +1,680 @@
+// Banded (sliding-window) causal attention: prefill and decode.
+//
+// Reference semantics:
+//   * per-head banded attention (per-head V, or one V broadcast to all heads):
+//     fused_banded_local_attention / _banded_attn_fwd_kernel
+//     (sample_standalone.py:70-85, :253-322); key j is visible from query t
+//     iff j <= t and t - j < window.
+//   * CSA local branch (model/layers/csa.py:42-75, decode :172-206): per-head
+//     softmax over the window, probabilities AVERAGED over heads, applied to
+//     one shared value stream of width D:
+//         out[t] = sum_j (1/H sum_h P_h[t, j]) V[j].
+//
+// Prefill kernels (bf16 mma.sync, fp32 accumulate, 64-query x 64-key tiles,
+// K/V double-buffered with cp.async; key tiles outside the band are never
+// visited, only the two band-edge tiles are masked):
+//   banded_attn_kernel<D, STATS>  per-head flash attention (online softmax);
+//                                 STATS = true writes only the row max and
+//                                 sum-of-exp per head (first CSA pass).
+//   csa_pv_kernel<DH, BM, DC>     second CSA pass: for each key tile the
+//                                 head-averaged probabilities
+//                                 Pbar = sum_h exp2(s_h - m_h) / (H l_h)
+//                                 are formed in registers and multiplied with
+//                                 a DC-wide slice of the shared V.
+// Decode kernel (memory-bound on the K/V window):
+//   csa_decode_kernel             one 8-CTA cluster per row; every CTA scores
+//                                 one eighth of the window, the per-head
+//                                 max/sum and the partial outputs are
+//                                 combined through distributed shared memory.
+//                                 The current token's K/V are read from the
+//                                 projection and written into the ring cache.
+#include <cooperative_groups.h>
+
+#include "common.cuh"
+#include "mma.cuh"
+
+#include <algorithm>
+
+namespace cg = cooperative_groups;
+
+namespace llmyb {
+namespace {
+
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr int BMQ = 64, BNK = 64;
+
+// key block range [kb0, kb1] visited by the query tile starting at m0
+__device__ __forceinline__ void band_blocks(int m0, int T, int W, int& kb0, int& kb1) {
+  const int lo = max(0, m0 - W + 1);
+  const int hi = min(T - 1, m0 + BMQ - 1);
+  kb0 = lo / BNK;
+  kb1 = hi / BNK;
+}
+
+// Copy a [64 x width] bf16 tile (rows r0.. of a token-major tensor with the
+// given row stride) into shared memory with leading dimension ld.
+template <int WIDTH>
+__device__ __forceinline__ void load_tile_async(__nv_bfloat16* dst, int ld,
+                                                const __nv_bfloat16* src, int64_t stride, int r0,
+                                                int rmax, int tid, int nthreads) {
+  constexpr int VPR = WIDTH / 8;  // 16-byte vectors per row
+  for (int i = tid; i < 64 * VPR; i += nthreads) {
+    const int r = i / VPR, c = (i - r * VPR) * 8;
+    const int row = r0 + r;
+    const bool ok = row < rmax && row >= 0;
+    const __nv_bfloat16* s = src + static_cast<int64_t>(ok ? row : 0) * stride + c;
+    mma::cp_async16(dst + r * ld + c, s, ok);
+  }
+}
+
+// --------------------------------------------------------------- per head
+template <int D, bool STATS>
+struct BandSmem {
+  static constexpr int LD = D + 8;
+  __nv_bfloat16 Q[BMQ * LD];
+  __nv_bfloat16 K[2][BNK * LD];
+  __nv_bfloat16 V[STATS ? 1 : 2][STATS ? 8 : BNK * LD];
+};
+
+template <int D, bool STATS>
+__global__ void __launch_bounds__(128) banded_attn_kernel(
+    const __nv_bfloat16* __restrict__ q, int64_t sq, const __nv_bfloat16* __restrict__ k,
+    int64_t sk, const __nv_bfloat16* __restrict__ v, int64_t sv, int v_heads, int B, int T, int H,
+    int W, float scale_log2, __nv_bfloat16* __restrict__ out, int64_t so, float* __restrict__ m_out,
+    float* __restrict__ l_out) {
+  using SM = BandSmem<D, STATS>;
+  extern __shared__ uint8_t smem_raw[];
+  SM& sm = *reinterpret_cast<SM*>(smem_raw);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nqb = static_cast<int>(ceil_div(T, BMQ));
+  const int qb = blockIdx.x % nqb;
+  const int h = (blockIdx.x / nqb) % H;
+  const int b = blockIdx.x / (nqb * H);
+  const int m0 = qb * BMQ;
+  int kb0, kb1;
+  band_blocks(m0, T, W, kb0, kb1);
+  const int64_t rowb = static_cast<int64_t>(b) * T;
+  const __nv_bfloat16* qh = q + rowb * sq + h * D;
+  const __nv_bfloat16* kh = k + rowb * sk + h * D;
+  const __nv_bfloat16* vh = v + rowb * sv + (v_heads == 1 ? 0 : h * D);
+
+  load_tile_async<D>(sm.Q, SM::LD, qh, sq, m0, T, tid, 128);
+  load_tile_async<D>(sm.K[0], SM::LD, kh, sk, kb0 * BNK, T, tid, 128);
+  if (!STATS) load_tile_async<D>(sm.V[0], SM::LD, vh, sv, kb0 * BNK, T, tid, 128);
+  mma::cp_async_commit();
+
+  const int r_lo = lane >> 2, cq = (lane & 3) * 2;
+  const int t_r0 = m0 + warp * 16 + r_lo;  // query rows of this thread: t_r0, t_r0 + 8
+  float o[STATS ? 1 : D / 8][4];
+  if (!STATS) {
+#pragma unroll
+    for (int nb = 0; nb < (STATS ? 1 : D / 8); ++nb)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) o[nb][e] = 0.f;
+  }
+  float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.f, 0.f};
+  uint32_t qf[D / 16][4];
+
+  for (int kb = kb0; kb <= kb1; ++kb) {
+    const int st = (kb - kb0) & 1;
+    if (kb < kb1) {
+      load_tile_async<D>(sm.K[st ^ 1], SM::LD, kh, sk, (kb + 1) * BNK, T, tid, 128);
+      if (!STATS) load_tile_async<D>(sm.V[STATS ? 0 : (st ^ 1)], SM::LD, vh, sv, (kb + 1) * BNK,
+                                     T, tid, 128);
+      mma::cp_async_commit();
+      mma::cp_async_wait<1>();
+    } else {
+      mma::cp_async_wait<0>();
+    }
+    __syncthreads();
+    if (kb == kb0) {
+#pragma unroll
+      for (int kk = 0; kk < D / 16; ++kk) mma::load_a(qf[kk], sm.Q, SM::LD, warp * 16, kk * 16);
+    }
+    // S = Q K^T (16 x 64 per warp)
+    float s[8][4];
+#pragma unroll
+    for (int nb = 0; nb < 8; ++nb)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) s[nb][e] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk) {
+#pragma unroll
+      for (int nb = 0; nb < 8; nb += 2) {
+        uint32_t bb[4];
+        mma::load_b_nk(bb, sm.K[st], SM::LD, nb * 8, kk * 16);
+        mma::mma_bf16(s[nb], qf[kk], bb[0], bb[1]);
+        mma::mma_bf16(s[nb + 1], qf[kk], bb[2], bb[3]);
+      }
+    }
+    // scale, mask (only the band-edge tiles), online softmax in base 2
+    const int j0 = kb * BNK;
+    const bool edge = (j0 + BNK - 1 > m0) || (j0 < m0 + BMQ - W) || (j0 + BNK > T);
+    float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int nb = 0; nb < 8; ++nb)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float x = s[nb][e] * scale_log2;
+        if (edge) {
+          const int t = t_r0 + (e >> 1) * 8;
+          const int j = j0 + nb * 8 + cq + (e & 1);
+          if (j > t || t - j >= W || j >= T) x = -INFINITY;
+        }
+        s[nb][e] = x;
+        mx[e >> 1] = fmaxf(mx[e >> 1], x);
+      }
+    float corr[2];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      mx[i] = fmaxf(mx[i], __shfl_xor_sync(0xffffffffu, mx[i], 1));
+      mx[i] = fmaxf(mx[i], __shfl_xor_sync(0xffffffffu, mx[i], 2));
+      const float mnew = fmaxf(mrow[i], mx[i]);
+      const float mref = mnew == -INFINITY ? 0.f : mnew;
+      corr[i] = exp2f(mrow[i] - mref);
+      mrow[i] = mnew;
+      mx[i] = mref;
+    }
+    float rs[2] = {0.f, 0.f};
+#pragma unroll
+    for (int nb = 0; nb < 8; ++nb)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float p = exp2f(s[nb][e] - mx[e >> 1]);
+        s[nb][e] = p;
+        rs[e >> 1] += p;
+      }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) lrow[i] = lrow[i] * corr[i] + rs[i];
+    if (!STATS) {
+#pragma unroll
+      for (int nb = 0; nb < (STATS ? 1 : D / 8); ++nb) {
+        o[nb][0] *= corr[0];
+        o[nb][1] *= corr[0];
+        o[nb][2] *= corr[1];
+        o[nb][3] *= corr[1];
+      }
+      // O += P V
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks) {
+        uint32_t a[4];
+        a[0] = pack_bf16x2(s[2 * ks][0], s[2 * ks][1]);
+        a[1] = pack_bf16x2(s[2 * ks][2], s[2 * ks][3]);
+        a[2] = pack_bf16x2(s[2 * ks + 1][0], s[2 * ks + 1][1]);
+        a[3] = pack_bf16x2(s[2 * ks + 1][2], s[2 * ks + 1][3]);
+#pragma unroll
+        for (int nb = 0; nb < (STATS ? 2 : D / 8); nb += 2) {
+          uint32_t bb[4];
+          mma::load_b_kn(bb, sm.V[STATS ? 0 : st], SM::LD, ks * 16, nb * 8);
+          mma::mma_bf16(o[nb], a, bb[0], bb[1]);
+          mma::mma_bf16(o[nb + 1], a, bb[2], bb[3]);
+        }
+      }
+    }
+    __syncthreads();
+  }
+  // finalize
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    lrow[i] += __shfl_xor_sync(0xffffffffu, lrow[i], 1);
+    lrow[i] += __shfl_xor_sync(0xffffffffu, lrow[i], 2);
+  }
+  if (STATS) {
+    if ((lane & 3) == 0) {
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const int t = t_r0 + i * 8;
+        if (t < T) {
+          m_out[(rowb + t) * H + h] = mrow[i];
+          l_out[(rowb + t) * H + h] = lrow[i];
+        }
+      }
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int t = t_r0 + i * 8;
+      if (t >= T) continue;
+      const float inv = 1.f / lrow[i];
+      __nv_bfloat16* dst = out + (rowb + t) * so + h * D;
+#pragma unroll
+      for (int nb = 0; nb < (STATS ? 1 : D / 8); ++nb)
+        *reinterpret_cast<uint32_t*>(dst + nb * 8 + cq) =
+            pack_bf16x2(o[nb][2 * i] * inv, o[nb][2 * i + 1] * inv);
+    }
+  }
+}
+
+// ------------------------------------------------------- CSA second pass
+template <int DH, int BM, int DC>
+struct CsaSmem {
+  static constexpr int LK = DH + 8, LV = DC + 8;
+  __nv_bfloat16 K[2][BNK * LK];
+  __nv_bfloat16 V[2][BNK * LV];
+  // followed by Q [BM][H*DH + 8] and stats [BM][H] (m, 1/(H l)) in dynamic memory
+};
+
+template <int DH, int BM, int DC>
+__global__ void __launch_bounds__(BM * 2) csa_pv_kernel(
+    const __nv_bfloat16* __restrict__ q, int64_t sq, const __nv_bfloat16* __restrict__ k,
+    int64_t sk, const __nv_bfloat16* __restrict__ v, int64_t sv, int B, int T, int H, int D, int W,
+    float scale_log2, const float* __restrict__ m_in, const float* __restrict__ l_in,
+    __nv_bfloat16* __restrict__ out, int64_t so) {
+  using SM = CsaSmem<DH, BM, DC>;
+  constexpr int NT = BM * 2;  // threads (BM/16 warps)
+  extern __shared__ uint8_t smem_raw[];
+  SM& sm = *reinterpret_cast<SM*>(smem_raw);
+  const int LQ = H * DH + 8;
+  __nv_bfloat16* sQ = reinterpret_cast<__nv_bfloat16*>(smem_raw + sizeof(SM));
+  float* sM = reinterpret_cast<float*>(sQ + BM * LQ);  // [BM][H]
+  float* sL = sM + BM * H;                             // [BM][H], holds 1/(H l)
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nqb = static_cast<int>(ceil_div(T, BM));
+  const int ndc = D / DC;
+  const int dc = blockIdx.x % ndc;
+  const int qb = (blockIdx.x / ndc) % nqb;
+  const int b = blockIdx.x / (ndc * nqb);
+  const int m0 = qb * BM;
+  const int lo = max(0, m0 - W + 1), hi = min(T - 1, m0 + BM - 1);
+  const int kb0 = lo / BNK, kb1 = hi / BNK;
+  const int64_t rowb = static_cast<int64_t>(b) * T;
+
+  // Q tile for all heads and the per-row stats
+  {
+    const int vpr = (H * DH) / 8;
+    for (int i = tid; i < BM * vpr; i += NT) {
+      const int r = i / vpr, c = (i - r * vpr) * 8;
+      const int row = m0 + r;
+      const bool ok = row < T;
+      mma::cp_async16(sQ + r * LQ + c, q + (rowb + (ok ? row : 0)) * sq + c, ok);
+    }
+    for (int i = tid; i < BM * H; i += NT) {
+      const int r = i / H, hh = i - r * H;
+      const int row = m0 + r;
+      float mm = 0.f, il = 0.f;
+      if (row < T) {
+        mm = m_in[(rowb + row) * H + hh];
+        il = 1.f / (static_cast<float>(H) * l_in[(rowb + row) * H + hh]);
+      }
+      sM[i] = mm;
+      sL[i] = il;
+    }
+  }
+  const int steps = (kb1 - kb0 + 1) * H;
+  // step i = (kb, h): K tile of head h; the V tile is loaded with h == 0
+  auto issue = [&](int i) {
+    const int kb = kb0 + i / H, hh = i % H, st = i & 1;
+    load_tile_async<DH>(sm.K[st], SM::LK, k + rowb * sk + hh * DH, sk, kb * BNK, T, tid, NT);
+    if (hh == 0)
+      load_tile_async<DC>(sm.V[(i / H) & 1], SM::LV, v + rowb * sv + dc * DC, sv, kb * BNK, T,
+                          tid, NT);
+  };
+  issue(0);
+  mma::cp_async_commit();
+
+  const int r_lo = lane >> 2, cq = (lane & 3) * 2;
+  const int t_r0 = m0 + warp * 16 + r_lo;
+  float o[DC / 8][4];
+#pragma unroll
+  for (int nb = 0; nb < DC / 8; ++nb)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) o[nb][e] = 0.f;
+  float pbar[8][4];
+
+  for (int i = 0; i < steps; ++i) {
+    const int kb = kb0 + i / H, hh = i % H, st = i & 1;
+    if (i + 1 < steps) {
+      issue(i + 1);
+      mma::cp_async_commit();
+      mma::cp_async_wait<1>();
+    } else {
+      mma::cp_async_wait<0>();
+    }
+    __syncthreads();
+    if (hh == 0) {
+#pragma unroll
+      for (int nb = 0; nb < 8; ++nb)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) pbar[nb][e] = 0.f;
+    }
+    float s[8][4];
+#pragma unroll
+    for (int nb = 0; nb < 8; ++nb)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) s[nb][e] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < DH / 16; ++kk) {
+      uint32_t a[4];
+      mma::load_a(a, sQ, LQ, warp * 16, hh * DH + kk * 16);
+#pragma unroll
+      for (int nb = 0; nb < 8; nb += 2) {
+        uint32_t bb[4];
+        mma::load_b_nk(bb, sm.K[st], SM::LK, nb * 8, kk * 16);
+        mma::mma_bf16(s[nb], a, bb[0], bb[1]);
+        mma::mma_bf16(s[nb + 1], a, bb[2], bb[3]);
+      }
+    }
+    const int j0 = kb * BNK;
+    const float mm0 = sM[(warp * 16 + r_lo) * H + hh], mm1 = sM[(warp * 16 + r_lo + 8) * H + hh];
+    const float il0 = sL[(warp * 16 + r_lo) * H + hh], il1 = sL[(warp * 16 + r_lo + 8) * H + hh];
+#pragma unroll
+    for (int nb = 0; nb < 8; ++nb)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int t = t_r0 + (e >> 1) * 8;
+        const int j = j0 + nb * 8 + cq + (e & 1);
+        const bool ok = j <= t && t - j < W && t < T;
+        const float p = ok ? exp2f(s[nb][e] * scale_log2 - ((e >> 1) ? mm1 : mm0)) *
+                                 ((e >> 1) ? il1 : il0)
+                           : 0.f;
+        pbar[nb][e] += p;
+      }
+    if (hh == H - 1) {
+      const int vst = (i / H) & 1;
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks) {
+        uint32_t a[4];
+        a[0] = pack_bf16x2(pbar[2 * ks][0], pbar[2 * ks][1]);
+        a[1] = pack_bf16x2(pbar[2 * ks][2], pbar[2 * ks][3]);
+        a[2] = pack_bf16x2(pbar[2 * ks + 1][0], pbar[2 * ks + 1][1]);
+        a[3] = pack_bf16x2(pbar[2 * ks + 1][2], pbar[2 * ks + 1][3]);
+#pragma unroll
+        for (int nb = 0; nb < DC / 8; nb += 2) {
+          uint32_t bb[4];
+          mma::load_b_kn(bb, sm.V[vst], SM::LV, ks * 16, nb * 8);
+          mma::mma_bf16(o[nb], a, bb[0], bb[1]);
+          mma::mma_bf16(o[nb + 1], a, bb[2], bb[3]);
+        }
+      }
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int t = t_r0 + i * 8;
+    if (t >= T) continue;
+    __nv_bfloat16* dst = out + (rowb + t) * so + dc * DC;
+#pragma unroll
+    for (int nb = 0; nb < DC / 8; ++nb)
+      *reinterpret_cast<uint32_t*>(dst + nb * 8 + cq) = pack_bf16x2(o[nb][2 * i], o[nb][2 * i + 1]);
+  }
+}
+
+// ------------------------------------------------------------- decode
+constexpr int kClusterCtas = 8;
+
+// scores of this CTA's keys live in dynamic shared memory: [H][keys_per_cta]
+__global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(256)
+    csa_decode_kernel(const __nv_bfloat16* __restrict__ q, int64_t sq,
+                      const __nv_bfloat16* __restrict__ knew, int64_t skn,
+                      const __nv_bfloat16* __restrict__ vnew, int64_t svn,
+                      __nv_bfloat16* __restrict__ kcache, __nv_bfloat16* __restrict__ vcache,
+                      const int* __restrict__ positions, int H, int DH, int D, int Wc,
+                      float scale_log2, __nv_bfloat16* __restrict__ out, int64_t so) {
+  extern __shared__ float dsm[];
+  cg::cluster_group cluster = cg::this_cluster();
+  const int crank = static_cast<int>(cluster.block_rank());
+  const int b = blockIdx.x / kClusterCtas;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int kpc = (Wc + kClusterCtas - 1) / kClusterCtas;  // keys per CTA
+  const int HD = H * DH;
+  float* s_q = dsm;                 // [H*DH]
+  float* s_sc = s_q + HD;           // [H][kpc] scores (log2 units)
+  float* s_m = s_sc + H * kpc;      // [H] local max
+  float* s_l = s_m + H;             // [H] local sum
+  float* s_M = s_l + H;             // [H] cluster-wide max
+  float* s_L = s_M + H;             // [H] cluster-wide sum
+  float* s_p = s_L + H;             // [kpc] head-averaged probabilities
+  float* s_o = s_p + kpc;           // [D] partial output
+
+  const int pos = positions[b];
+  const int n_valid = min(pos + 1, Wc);
+  const int cur_slot = pos % Wc;
+  const int j_begin = crank * kpc;
+  const int j_end = min(Wc, j_begin + kpc);
+  const int64_t cache_row = static_cast<int64_t>(b) * Wc;
+
+  for (int i = tid; i < HD; i += 256) s_q[i] = bf2f(q[b * sq + i]);
+  __syncthreads();
+  // ---- scores
+  for (int j = j_begin + warp; j < j_end; j += 8) {
+    const bool valid = j < n_valid;
+    const __nv_bfloat16* kr = (j == cur_slot) ? knew + b * skn : kcache + (cache_row + j) * HD;
+    for (int hh = 0; hh < H; ++hh) {
+      float acc = 0.f;
+      if (valid)
+        for (int d = lane; d < DH; d += 32) acc += s_q[hh * DH + d] * bf2f(kr[hh * DH + d]);
+      acc = warp_sum(acc);
+      if (lane == 0) s_sc[hh * kpc + (j - j_begin)] = valid ? acc * scale_log2 : -INFINITY;
+    }
+    if (j == cur_slot) {  // append the current token to the ring
+      for (int d = lane; d < HD; d += 32) kcache[(cache_row + j) * HD + d] = knew[b * skn + d];
+      for (int d = lane; d < D; d += 32) vcache[(cache_row + j) * D + d] = vnew[b * svn + d];
+    }
+  }
+  __syncthreads();
+  const int nk = max(0, j_end - j_begin);
+  for (int hh = warp; hh < H; hh += 8) {
+    float mx = -INFINITY;
+    for (int j = lane; j < nk; j += 32) mx = fmaxf(mx, s_sc[hh * kpc + j]);
+    mx = warp_max(mx);
+    float sum = 0.f;
+    if (mx != -INFINITY)
+      for (int j = lane; j < nk; j += 32) sum += exp2f(s_sc[hh * kpc + j] - mx);
+    sum = warp_sum(sum);
+    if (lane == 0) {
+      s_m[hh] = mx;
+      s_l[hh] = sum;
+    }
+  }
+  cluster.sync();
+  // ---- global per-head max/sum from every CTA of the cluster
+  for (int hh = warp; hh < H; hh += 8) {
+    float mloc = -INFINITY, lloc = 0.f;
+    if (lane < kClusterCtas) {
+      mloc = *cluster.map_shared_rank(&s_m[hh], lane);
+      lloc = *cluster.map_shared_rank(&s_l[hh], lane);
+    }
+    const float M = warp_max(mloc);
+    const float L = warp_sum(mloc == -INFINITY ? 0.f : lloc * exp2f(mloc - M));
+    if (lane == 0) {
+      s_M[hh] = M;
+      s_L[hh] = L;
+    }
+  }
+  __syncthreads();
+  // ---- head-averaged probabilities of this CTA's keys
+  for (int j = tid; j < nk; j += 256) {
+    float p = 0.f;
+    for (int hh = 0; hh < H; ++hh) {
+      const float x = s_sc[hh * kpc + j];
+      if (x != -INFINITY) p += exp2f(x - s_M[hh]) / s_L[hh];
+    }
+    s_p[j] = p / static_cast<float>(H);
+  }
+  __syncthreads();
+  // ---- partial output over this CTA's keys
+  for (int d0 = tid * 2; d0 < D; d0 += 512) {
+    float a0 = 0.f, a1 = 0.f;
+    for (int j = 0; j < nk; ++j) {
+      const float p = s_p[j];
+      if (p == 0.f) continue;
+      const int jj = j_begin + j;
+      const __nv_bfloat16* vr = (jj == cur_slot) ? vnew + b * svn : vcache + (cache_row + jj) * D;
+      const float2 vv = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(vr + d0));
+      a0 += p * vv.x;
+      a1 += p * vv.y;
+    }
+    s_o[d0] = a0;
+    s_o[d0 + 1] = a1;
+  }
+  cluster.sync();
+  // ---- reduce this CTA's column slice over the cluster
+  const int cols = D / kClusterCtas;
+  for (int d = crank * cols + tid; d < (crank + 1) * cols; d += 256) {
+    float acc = 0.f;
+    for (int r = 0; r < kClusterCtas; ++r) acc += *cluster.map_shared_rank(&s_o[d], r);
+    out[b * so + d] = f2bf(acc);
+  }
+  cluster.sync();  // keep shared memory alive until every peer finished reading
+}
+
+template <typename K>
+int32_t set_smem(K kernel, int bytes) {
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  return e == cudaSuccess ? LLMYB_OK : static_cast<int32_t>(e);
+}
+
+template <int D, bool STATS>
+int32_t launch_band(const __nv_bfloat16* q, int64_t sq, const __nv_bfloat16* k, int64_t sk,
+                    const __nv_bfloat16* v, int64_t sv, int v_heads, int B, int T, int H, int W,
+                    float scale, __nv_bfloat16* out, int64_t so, float* m_out, float* l_out,
+                    cudaStream_t s) {
+  constexpr int bytes = sizeof(BandSmem<D, STATS>);
+  static bool attr = false;
+  if (!attr) {
+    int32_t st = set_smem(banded_attn_kernel<D, STATS>, bytes);
+    if (st) return st;
+    attr = true;
+  }
+  const int grid = B * H * static_cast<int>(ceil_div(T, BMQ));
+  banded_attn_kernel<D, STATS><<<grid, 128, bytes, s>>>(q, sq, k, sk, v, sv, v_heads, B, T, H, W,
+                                                        scale * kLog2e, out, so, m_out, l_out);
+  return launch_status();
+}
+
+bool aligned16(const void* p, int64_t stride) {
+  return (reinterpret_cast<uintptr_t>(p) & 15u) == 0 && stride % 8 == 0;
+}
+
+}  // namespace
+}  // namespace llmyb
+
+using namespace llmyb;
+
+// Per-head banded attention: q,k [B*T, H*D] (token stride sq/sk), v with
+// v_heads in {1, H} heads of width D, out [B*T, H*D] (stride so).
+LLMYB_API int32_t llmyb_banded_attention(const void* q, int64_t q_stride, const void* k,
+                                         int64_t k_stride, const void* v, int64_t v_stride,
+                                         int32_t v_heads, int32_t batch, int32_t seq,
+                                         int32_t heads, int32_t head_dim, int32_t window,
+                                         float scale, void* out, int64_t out_stride,
+                                         void* stream) {
+  if (!q || !k || !v || !out || batch < 0 || seq < 0 || heads <= 0 || window <= 0)
+    return LLMYB_EINVAL;
+  if (v_heads != 1 && v_heads != heads) return LLMYB_EINVAL;
+  if (batch == 0 || seq == 0) return LLMYB_OK;
+  if (!aligned16(q, q_stride) || !aligned16(k, k_stride) || !aligned16(v, v_stride) ||
+      !aligned16(out, out_stride))
+    return LLMYB_EUNSUPPORTED;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  auto Q = static_cast<const __nv_bfloat16*>(q);
+  auto K = static_cast<const __nv_bfloat16*>(k);
+  auto V = static_cast<const __nv_bfloat16*>(v);
+  auto O = static_cast<__nv_bfloat16*>(out);
+  switch (head_dim) {
+    case 64:
+      return launch_band<64, false>(Q, q_stride, K, k_stride, V, v_stride, v_heads, batch, seq,
+                                    heads, window, scale, O, out_stride, nullptr, nullptr, s);
+    case 128:
+      return launch_band<128, false>(Q, q_stride, K, k_stride, V, v_stride, v_heads, batch, seq,
+                                     heads, window, scale, O, out_stride, nullptr, nullptr, s);
+    default:
+      return LLMYB_EUNSUPPORTED;
+  }
+}
+
+LLMYB_API int64_t llmyb_csa_prefill_scratch_bytes(int32_t batch, int32_t seq, int32_t heads) {
+  if (batch < 0 || seq < 0 || heads <= 0) return -1;
+  return static_cast<int64_t>(batch) * seq * heads * 2 * sizeof(float);
+}
+
+// CSA local branch, prefill: q,k [B*T, H*DH] (strides), v [B*T, D] shared
+// value stream (stride sv); out [B*T, D].  scratch holds the per-head row
+// statistics (llmyb_csa_prefill_scratch_bytes).
+LLMYB_API int32_t llmyb_csa_local_prefill(const void* q, int64_t q_stride, const void* k,
+                                          int64_t k_stride, const void* v, int64_t v_stride,
+                                          int32_t batch, int32_t seq, int32_t heads,
+                                          int32_t head_dim, int32_t d_model, int32_t window,
+                                          void* out, int64_t out_stride, void* scratch,
+                                          void* stream) {
+  if (!q || !k || !v || !out || !scratch || batch < 0 || seq < 0 || heads <= 0 || window <= 0)
+    return LLMYB_EINVAL;
+  if (batch == 0 || seq == 0) return LLMYB_OK;
+  if (!aligned16(q, q_stride) || !aligned16(k, k_stride) || !aligned16(v, v_stride) ||
+      !aligned16(out, out_stride) || d_model % 64 != 0)
+    return LLMYB_EUNSUPPORTED;
+  // csa.py:42: the window never exceeds the sequence
+  const int w = std::max(1, std::min<int>(window, seq));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  auto Q = static_cast<const __nv_bfloat16*>(q);
+  auto K = static_cast<const __nv_bfloat16*>(k);
+  auto V = static_cast<const __nv_bfloat16*>(v);
+  auto O = static_cast<__nv_bfloat16*>(out);
+  float* m = static_cast<float*>(scratch);
+  float* l = m + static_cast<int64_t>(batch) * seq * heads;
+  const float scale = 1.0f / sqrtf(static_cast<float>(head_dim));
+  int32_t st;
+  if (head_dim == 64)
+    st = launch_band<64, true>(Q, q_stride, K, k_stride, V, v_stride, 1, batch, seq, heads, w,
+                               scale, nullptr, 0, m, l, s);
+  else if (head_dim == 128)
+    st = launch_band<128, true>(Q, q_stride, K, k_stride, V, v_stride, 1, batch, seq, heads, w,
+                                scale, nullptr, 0, m, l, s);
+  else
+    return LLMYB_EUNSUPPORTED;
+  if (st) return st;
+  const int hd = heads * head_dim;
+  constexpr int DC = 64;
+  auto run = [&](auto kern, int BM, int base_bytes, int dh) -> int32_t {
+    const int bytes = base_bytes + BM * (hd + 8) * 2 + BM * heads * 2 * 4;
+    if (bytes > 227 * 1024) return LLMYB_EUNSUPPORTED;
+    int32_t e = set_smem(kern, bytes);
+    if (e) return e;
+    const int grid = batch * static_cast<int>(ceil_div(seq, BM)) * (d_model / DC);
+    kern<<<grid, BM * 2, bytes, s>>>(Q, q_stride, K, k_stride, V, v_stride, batch, seq, heads,
+                                     d_model, w, scale * kLog2e, m, l, O, out_stride);
+    (void)dh;
+    return launch_status();
+  };
+  if (head_dim == 64) {
+    if (hd <= 1024) return run(csa_pv_kernel<64, 64, DC>, 64, sizeof(CsaSmem<64, 64, DC>), 64);
+    return run(csa_pv_kernel<64, 32, DC>, 32, sizeof(CsaSmem<64, 32, DC>), 64);
+  }
+  if (hd <= 1024) return run(csa_pv_kernel<128, 64, DC>, 64, sizeof(CsaSmem<128, 64, DC>), 128);
+  return run(csa_pv_kernel<128, 32, DC>, 32, sizeof(CsaSmem<128, 32, DC>), 128);
+}
+
+// CSA local branch, decode: one new token per row.  q/knew [B, H*DH],
+// vnew [B, D] (row strides); the ring caches kcache [B, Wc, H*DH] and
+// vcache [B, Wc, D] hold token p at slot p % Wc; positions[b] is the new
+// token's position (its K/V are written to slot positions[b] % Wc).  The
+// window is the last min(positions[b] + 1, Wc) tokens (csa.py:185-187).
+LLMYB_API int32_t llmyb_csa_local_decode(const void* q, int64_t q_stride, const void* knew,
+                                         int64_t knew_stride, const void* vnew,
+                                         int64_t vnew_stride, void* kcache, void* vcache,
+                                         const int32_t* positions, int32_t batch, int32_t heads,
+                                         int32_t head_dim, int32_t d_model, int32_t window,
+                                         void* out, int64_t out_stride, void* stream) {
+  if (!q || !knew || !vnew || !kcache || !vcache || !positions || !out || batch < 0 ||
+      heads <= 0 || head_dim <= 0 || window <= 0)
+    return LLMYB_EINVAL;
+  if (batch == 0) return LLMYB_OK;
+  if (d_model % (2 * kClusterCtas) != 0) return LLMYB_EUNSUPPORTED;
+  const int kpc = (window + kClusterCtas - 1) / kClusterCtas;
+  const int bytes = (heads * head_dim + heads * kpc + 4 * heads + kpc + d_model) * 4;
+  if (bytes > 227 * 1024) return LLMYB_EUNSUPPORTED;
+  static int attr_bytes = 0;
+  if (bytes > attr_bytes) {
+    int32_t st = set_smem(csa_decode_kernel, bytes);
+    if (st) return st;
+    attr_bytes = bytes;
+  }
+  csa_decode_kernel<<<batch * kClusterCtas, 256, bytes, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(q), q_stride, static_cast<const __nv_bfloat16*>(knew),
+      knew_stride, static_cast<const __nv_bfloat16*>(vnew), vnew_stride,
+      static_cast<__nv_bfloat16*>(kcache), static_cast<__nv_bfloat16*>(vcache), positions, heads,
+      head_dim, d_model, window, kLog2e / sqrtf(static_cast<float>(head_dim)),
+      static_cast<__nv_bfloat16*>(out), out_stride);
+  return launch_status();
+}

@@ -816,6 +816,9 @@ LLMYB_API int32_t llmyb_gdn_prefill(const void* q, int64_t q_stride, const void*
   if (!state || !out || !scratch || batch < 0 || seq < 0 || heads <= 0) return LLMYB_EINVAL;
   if (batch == 0 || seq == 0) return LLMYB_OK;
   if ((q_stride | k_stride | v_stride) % 8 != 0) return LLMYB_EUNSUPPORTED;
+  if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) |
+       reinterpret_cast<uintptr_t>(v) | reinterpret_cast<uintptr_t>(scratch)) & 15u)
+    return LLMYB_EUNSUPPORTED;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   auto* o = static_cast<__nv_bfloat16*>(out);
   if (key_dim == 64 && value_dim == 64)

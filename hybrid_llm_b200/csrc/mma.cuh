@@ -82,5 +82,17 @@ __device__ __forceinline__ void load_b_kn(uint32_t (&b)[4], const __nv_bfloat16*
   ldsm_x4_t(b, base + k * ld + n);
 }
 
+// 16-byte asynchronous global -> shared copy; src_bytes = 0 zero-fills.
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_addr(dst)), "l"(src),
+               "r"(valid ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 }  // namespace mma
 }  // namespace llmyb

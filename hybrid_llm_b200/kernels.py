@@ -266,3 +266,70 @@ def gdn_conv_gate(x, y_proj, conv_w, *, history=None, reset=None, out=None, resi
     _native.call("llmyb_gdn_conv_gate", _ptr(x), _ptr(y_proj), _ptr(w), _ptr(history), _ptr(r),
                  bsz, t, d, _ptr(out), _ptr(residual), int(roll_history), _stream())
     return residual if residual is not None else out
+
+
+# ------------------------------------------------------ banded attention
+def _tokens(t: torch.Tensor, name: str) -> tuple[int, int]:
+    """(pointer, token stride) of a bf16 [B, T, ...] tensor whose per-token
+    block is packed and whose tokens are evenly strided."""
+    if t.dtype != torch.bfloat16:
+        raise ValueError(f"{name} must be bf16")
+    inner = 1
+    for dim in range(t.dim() - 1, 1, -1):
+        if t.stride(dim) != inner:
+            raise ValueError(f"{name}: per-token block must be contiguous")
+        inner *= t.shape[dim]
+    if t.stride(0) != t.shape[1] * t.stride(1):
+        raise ValueError(f"{name}: tokens must be evenly strided")
+    return t.data_ptr(), t.stride(1)
+
+
+def banded_attention(q, k, v, window: int, scale: float | None = None, out=None):
+    """Per-head causal sliding-window attention (sample_standalone.py:70-85):
+    q,k [B,T,H,D]; v [B,T,H or 1,D] -> [B,T,H,D] bf16."""
+    _require_cuda(q, k, v)
+    bsz, t, h, d = q.shape
+    qp, qs = _tokens(q, "q")
+    kp, ks = _tokens(k, "k")
+    vp, vs = _tokens(v, "v")
+    if out is None:
+        out = torch.empty(bsz, t, h, d, dtype=torch.bfloat16, device=q.device)
+    scale = d ** -0.5 if scale is None else float(scale)
+    _native.call("llmyb_banded_attention", qp, qs, kp, ks, vp, vs, v.shape[2], bsz, t, h, d,
+                 int(window), scale, _ptr(out), out.stride(1), _stream())
+    return out
+
+
+def csa_local_prefill(q, k, v, window: int, out=None):
+    """CSA local branch (csa.py:42-75): q,k [B,T,H,Dh]; v [B,T,D] -> [B,T,D]."""
+    _require_cuda(q, k, v)
+    bsz, t, h, dh = q.shape
+    dm = v.shape[-1]
+    qp, qs = _tokens(q, "q")
+    kp, ks = _tokens(k, "k")
+    vp, vs = _tokens(v, "v")
+    if out is None:
+        out = torch.empty(bsz, t, dm, dtype=torch.bfloat16, device=q.device)
+    need = int(_native.lib().llmyb_csa_prefill_scratch_bytes(bsz, t, h))
+    scratch = torch.empty(max(need, 16), dtype=torch.uint8, device=q.device)
+    _native.call("llmyb_csa_local_prefill", qp, qs, kp, ks, vp, vs, bsz, t, h, dh, dm, int(window),
+                 _ptr(out), out.stride(1), _ptr(scratch), _stream())
+    return out
+
+
+def csa_local_decode(q, knew, vnew, kcache, vcache, positions, heads: int, out=None):
+    """CSA decode (csa.py:172-206) over a ring K/V cache: q,knew [B,H*Dh]; vnew [B,D];
+    kcache [B,W,H*Dh]; vcache [B,W,D]; positions [B] int32 = position of the new
+    token, whose K/V are written to slot position % W.  Returns [B,D] bf16."""
+    _require_cuda(q, knew, vnew, kcache, vcache, positions)
+    bsz, hd = q.shape
+    dm = vnew.shape[-1]
+    w = kcache.shape[1]
+    if positions.dtype != torch.int32:
+        raise ValueError("positions must be int32")
+    if out is None:
+        out = torch.empty(bsz, dm, dtype=torch.bfloat16, device=q.device)
+    _native.call("llmyb_csa_local_decode", _ptr(q), q.stride(0), _ptr(knew), knew.stride(0),
+                 _ptr(vnew), vnew.stride(0), _ptr(kcache), _ptr(vcache), _ptr(positions), bsz,
+                 heads, hd // heads, dm, w, _ptr(out), out.stride(0), _stream())
+    return out

@@ -138,6 +138,43 @@ int32_t llmyb_gdn_conv_gate(const void* x, const void* y_proj, const float* conv
                             int32_t d_model, void* out, void* residual, int32_t roll_history,
                             void* stream);
 
+/* ------------------------------------------------------ banded attention
+ * Replaces fused_banded_local_attention / triton_banded_local_attention
+ * (sample_standalone.py:70-85, :253-409), the CSA local branch
+ * (model/layers/csa.py:39-75, decode :172-206) and the native
+ * banded_attn_kernel / local_attn_decode_kernel
+ * (llmy_cuda/src/kernels/attn.cu:17-229).  Key j is visible from query t iff
+ * j <= t and t - j < window.  Token-major bf16 tensors with token strides. */
+
+/* Per-head attention: q,k [B*T, H*D], v with v_heads in {1, H} heads of
+ * width D, out [B*T, H*D]; D in {64, 128}; scale multiplies q.k. */
+int32_t llmyb_banded_attention(const void* q, int64_t q_stride, const void* k, int64_t k_stride,
+                               const void* v, int64_t v_stride, int32_t v_heads, int32_t batch,
+                               int32_t seq, int32_t heads, int32_t head_dim, int32_t window,
+                               float scale, void* out, int64_t out_stride, void* stream);
+
+/* Scratch bytes needed by llmyb_csa_local_prefill (per-head row max / sum). */
+int64_t llmyb_csa_prefill_scratch_bytes(int32_t batch, int32_t seq, int32_t heads);
+
+/* CSA local branch, prefill: head-averaged probabilities times the shared
+ * value stream v [B*T, D]; out [B*T, D].  Window = min(window, T) as
+ * csa.py:42 does.  Head dim in {64, 128}, D % 64 == 0. */
+int32_t llmyb_csa_local_prefill(const void* q, int64_t q_stride, const void* k, int64_t k_stride,
+                                const void* v, int64_t v_stride, int32_t batch, int32_t seq,
+                                int32_t heads, int32_t head_dim, int32_t d_model, int32_t window,
+                                void* out, int64_t out_stride, void* scratch, void* stream);
+
+/* CSA local branch, decode: q/knew [B, H*DH], vnew [B, D]; ring caches
+ * kcache [B, window, H*DH], vcache [B, window, D] hold token p at slot
+ * p % window; positions[b] is the new token's position.  Writes the new K/V
+ * into the ring and attends over the last min(positions[b]+1, window)
+ * tokens. */
+int32_t llmyb_csa_local_decode(const void* q, int64_t q_stride, const void* knew,
+                               int64_t knew_stride, const void* vnew, int64_t vnew_stride,
+                               void* kcache, void* vcache, const int32_t* positions,
+                               int32_t batch, int32_t heads, int32_t head_dim, int32_t d_model,
+                               int32_t window, void* out, int64_t out_stride, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -68,3 +68,30 @@ def gdn_case(tag: str):
     steps = rng.normal(0, 1, (b, 3, d)).astype(np.float32)  # decode tokens after the prefix
     return dict(p=p, hidden=hidden, state=state, reset=reset, steps=steps, heads=h, key_dim=kd,
                 value_dim=vd)
+
+
+CSA_CASES = {"a": (1, 100, 64, 4, 16, 32), "b": (2, 70, 96, 3, 32, 128)}
+
+
+def csa_case(tag: str):
+    """CSA weights (reference parameter names), input and decode tokens."""
+    b, t, d, h, dh, w = CSA_CASES[tag]
+    rng = np.random.default_rng(4000 + ord(tag))
+    m = lambda *s: rng.normal(0, 0.15, s).astype(np.float32)
+    p = dict(query=m(h * dh, d), key=m(h * dh, d), value=m(d, d), local_out=m(d, d),
+             remote_out=m(d, d), out=m(d, d))
+    hidden = rng.normal(0, 1, (b, t, d)).astype(np.float32)
+    steps = rng.normal(0, 1, (b, 3, d)).astype(np.float32)
+    return dict(p=p, hidden=hidden, steps=steps, heads=h, head_dim=dh, window=w)
+
+
+BAND_CASES = {"a": (2, 90, 3, 16, 16, 24, 3), "b": (1, 64, 2, 32, 32, 64, 1)}
+
+
+def band_case(tag: str):
+    """q,k [B,T,H,D], v [B,T,Hv,Dv] for the per-head banded SDPA."""
+    b, t, h, d, dv, w, hv = BAND_CASES[tag]
+    rng = np.random.default_rng(5000 + ord(tag))
+    return dict(q=rng.normal(size=(b, t, h, d)).astype(np.float32),
+                k=rng.normal(size=(b, t, h, d)).astype(np.float32),
+                v=rng.normal(size=(b, t, hv, dv)).astype(np.float32), window=w)

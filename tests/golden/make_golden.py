@@ -148,7 +148,54 @@ def sec_gdn() -> None:
     save("gdn", **out)
 
 
-SECTIONS = {"router": sec_router, "moe": sec_moe, "gdn": sec_gdn}
+def sec_csa() -> None:
+    """CompressedSelectiveAttention (csa.py:35-259) with the remote branch
+    disabled (temporal_compression=10**9): prefill, then decode steps that
+    keep the normed-hidden local history as PhysicalBlock does
+    (model/model.py:340-357)."""
+    _ref_import()
+    from model.layers.csa import CompressedSelectiveAttention
+
+    out = {}
+    for tag in inputs.CSA_CASES:
+        c = inputs.csa_case(tag)
+        d = c["hidden"].shape[-1]
+        m = CompressedSelectiveAttention(d, compression=10**9, local_window=c["window"],
+                                         index_heads=c["heads"], index_head_dim=c["head_dim"],
+                                         top_k=4)
+        with torch.no_grad():
+            for name, w in c["p"].items():
+                getattr(m, name).weight.copy_(t(w))
+            y, _, _ = m(t(c["hidden"]), return_stats=False)
+            hist = t(c["hidden"])[:, -(c["window"] - 1):].clone()
+            ys = []
+            for i in range(c["steps"].shape[1]):
+                x1 = t(c["steps"][:, i:i + 1])
+                valid = torch.ones(hist.shape[:2], dtype=torch.bool)
+                y1, _, _ = m.forward_step(x1, local_history=hist, local_history_valid=valid,
+                                          position=torch.full((x1.shape[0],), c["hidden"].shape[1] + i))
+                hist = torch.cat([hist, x1], dim=1)[:, -(c["window"] - 1):]
+                ys.append(y1.numpy())
+        out.update({f"{tag}_checksum": inputs.checksum(c["hidden"], *c["p"].values()),
+                    f"{tag}_out": y.numpy(), f"{tag}_step_out": np.stack(ys, 1)})
+    save("csa", **out)
+
+
+def sec_band() -> None:
+    """fused_banded_local_attention (sample_standalone.py:70-85), per-head V."""
+    sa = _standalone()
+    out = {}
+    for tag in inputs.BAND_CASES:
+        c = inputs.band_case(tag)
+        with torch.no_grad():
+            y = sa.fused_banded_local_attention(t(c["q"]), t(c["k"]), t(c["v"]),
+                                                window_size=c["window"])
+        out.update({f"{tag}_checksum": inputs.checksum(c["q"], c["k"], c["v"]),
+                    f"{tag}_out": y.numpy()})
+    save("band", **out)
+
+
+SECTIONS = {"router": sec_router, "moe": sec_moe, "gdn": sec_gdn, "csa": sec_csa, "band": sec_band}
 
 
 def main(argv: list[str]) -> None:

@@ -110,6 +110,8 @@ def test_gdn_scan_on_reference_layer_inputs(cuda, tag):
     h, kd, vd = c["heads"], c["key_dim"], c["value_dim"]
     proj = np.concatenate([x @ p["q_proj"].T, x @ p["k_proj"].T, x @ p["v_proj"].T,
                            x @ p["gate_proj"].T, x @ p["beta_proj"].T], axis=-1)
+    pad = (-proj.shape[-1]) % 8  # the fused projection is padded to 16-byte rows
+    proj = np.concatenate([proj, np.zeros(proj.shape[:-1] + (pad,))], axis=-1)
     pr = _bf(proj.reshape(b * t, -1)).cuda()
     kernels.gdn_activate(pr, h, kd, vd, torch.from_numpy(p["beta_bias"]).cuda())
     pr = pr.view(b, t, -1)
@@ -118,7 +120,7 @@ def test_gdn_scan_on_reference_layer_inputs(cuda, tag):
     k = pr[..., hk:2 * hk].unflatten(-1, (h, kd))
     v = pr[..., 2 * hk:2 * hk + hv].unflatten(-1, (h, vd))
     gate = pr[..., 2 * hk + hv:2 * hk + 2 * hv].unflatten(-1, (h, vd))
-    beta = pr[..., 2 * hk + 2 * hv:]
+    beta = pr[..., 2 * hk + 2 * hv:2 * hk + 2 * hv + h]
     st = torch.from_numpy(c["state"]).cuda()
     out = kernels.gdn_prefill(q, k, v, gate, beta, st,
                               decay_logit=torch.from_numpy(p["decay_logit"]).cuda(),
