@@ -1,0 +1,105 @@
+"""Model configuration of the looped hybrid stack served by this package.
+
+Mirrors the parts of the reference V6Config (model/config.py:107-191) that the
+B200 path implements: a recurrent core of ``gdn_moe`` / ``csa_moe`` blocks run
+``num_loops`` times, mHC disabled (one residual stream), plain top-k softmax
+router (no context path), no shared experts, CSA with its remote compressed
+branch disabled (temporal_compression beyond any sequence), no stem/tail
+blocks.  ``from_v6`` converts a reference config (dataclass or mapping) and
+rejects anything outside that subset instead of silently changing the model.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+from typing import Any
+
+
+@dataclass(frozen=True)
+class HybridConfig:
+    vocab_size: int
+    d_model: int
+    recurrent_layout: tuple[str, ...]
+    num_loops: int
+    gdn_heads: int
+    gdn_key_dim: int
+    gdn_value_dim: int
+    csa_heads: int
+    csa_head_dim: int
+    csa_window: int
+    moe_experts: int
+    moe_top_k: int
+    moe_hidden: int
+    conv_kernel: int = 4
+    rms_eps: float = 1e-6
+    name: str = field(default="custom", compare=False)
+
+    def __post_init__(self) -> None:
+        for kind in self.recurrent_layout:
+            if kind not in ("gdn_moe", "csa_moe"):
+                raise ValueError(f"unsupported block kind {kind!r} (gdn_moe or csa_moe)")
+        if self.num_loops < 1:
+            raise ValueError("num_loops must be positive")
+        if self.moe_top_k > self.moe_experts:
+            raise ValueError("moe_top_k cannot exceed moe_experts")
+        if self.conv_kernel != 4:
+            raise ValueError("the GDN conv gate kernel implements kernel size 4")
+
+    @property
+    def n_blocks(self) -> int:
+        return len(self.recurrent_layout)
+
+    def block_kind(self, j: int) -> str:
+        return self.recurrent_layout[j].split("_")[0]
+
+    @classmethod
+    def from_v6(cls, cfg: Any) -> "HybridConfig":
+        """Convert a reference V6Config (or the mapping its checkpoints embed)."""
+        get = (lambda o, k: o[k]) if isinstance(cfg, dict) else getattr
+        sub = lambda name: get(cfg, name)
+        sget = lambda o, k: o[k] if isinstance(o, dict) else getattr(o, k)
+        if sget(sub("mhc"), "enabled") and sget(sub("mhc"), "streams") != 1:
+            raise ValueError("multi-stream hyper-connections are not implemented (mhc.enabled)")
+        if sget(sub("router"), "context_aware"):
+            raise ValueError("the context-aware router path is not implemented")
+        if sget(sub("moe"), "shared_experts") != 0:
+            raise ValueError("shared experts are not implemented")
+        if sub("stem_blocks") or sub("tail_blocks"):
+            raise ValueError("stem/tail dense blocks are not implemented")
+        if sget(sub("loop_attnres"), "enabled") or sget(sub("adaptive_loops"), "enabled"):
+            raise ValueError("loop memory and adaptive halting are not implemented")
+        csa = sub("csa")
+        return cls(
+            vocab_size=sub("vocab_size"), d_model=sub("d_model"),
+            recurrent_layout=tuple(sub("recurrent_layout")), num_loops=sub("num_loops"),
+            gdn_heads=sget(sub("gdn"), "qk_heads"), gdn_key_dim=sget(sub("gdn"), "qk_head_dim"),
+            gdn_value_dim=sget(sub("gdn"), "value_head_dim"),
+            csa_heads=sget(csa, "index_heads"), csa_head_dim=sget(csa, "index_head_dim"),
+            csa_window=sget(csa, "local_window"),
+            moe_experts=sget(sub("moe"), "routed_experts"), moe_top_k=sget(sub("moe"), "routed_top_k"),
+            moe_hidden=sget(sub("moe"), "expert_hidden"),
+            conv_kernel=sget(sub("gdn"), "conv_kernel"),
+        )
+
+
+def single_block_config() -> HybridConfig:
+    """The single looped hybrid block workload (csa_moe + gdn_moe, d=512, 2 loops)."""
+    return HybridConfig(vocab_size=32000, d_model=512, recurrent_layout=("csa_moe", "gdn_moe"),
+                        num_loops=2, gdn_heads=8, gdn_key_dim=64, gdn_value_dim=64, csa_heads=8,
+                        csa_head_dim=64, csa_window=128, moe_experts=8, moe_top_k=2,
+                        moe_hidden=1024, name="single-block")
+
+
+def small_llmy_config() -> HybridConfig:
+    """Full small LLMY model: vocab 32000, d 768, 12 alternating blocks, 16 experts top-2."""
+    return HybridConfig(vocab_size=32000, d_model=768, recurrent_layout=("csa_moe", "gdn_moe") * 6,
+                        num_loops=2, gdn_heads=12, gdn_key_dim=64, gdn_value_dim=64, csa_heads=12,
+                        csa_head_dim=64, csa_window=512, moe_experts=16, moe_top_k=2,
+                        moe_hidden=1024, name="small-llmy")
+
+
+def large_ep_config() -> HybridConfig:
+    """Expert-parallel large model: d 2048, 24 blocks, 64 experts top-8, 3 loops, vocab 64000."""
+    return HybridConfig(vocab_size=64000, d_model=2048, recurrent_layout=("csa_moe", "gdn_moe") * 12,
+                        num_loops=3, gdn_heads=16, gdn_key_dim=128, gdn_value_dim=128, csa_heads=16,
+                        csa_head_dim=128, csa_window=2048, moe_experts=64, moe_top_k=8,
+                        moe_hidden=1024, name="large-ep")

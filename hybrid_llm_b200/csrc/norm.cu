@@ -1,0 +1,123 @@
+// Residual stream helpers: token embedding into the fp32 residual stream and
+// the fused "residual add + RMSNorm" that sits between every pair of
+// sub-layers of PhysicalBlock.
+//
+// Reference: model/layers/norms.py:13-16 (RMSNorm: variance of the fp32
+// value, x * rsqrt(var + eps) * weight), model/model.py:119-126 (with mHC
+// off: read = mean over the single stream, write = streams + update) and
+// :442-444 (embedding + stream_seed).  Under bf16 autocast the residual
+// stream stays fp32 while sub-layer outputs are bf16; the same split is
+// used here: streams fp32, normalised activations bf16 (fp32 on request).
+#include "common.cuh"
+
+namespace llmyb {
+namespace {
+
+// streams[n] = float(table[ids[n]]) + seed      (one CTA per token)
+__global__ void embed_kernel(const int64_t* __restrict__ ids, const __nv_bfloat16* __restrict__ table,
+                             const float* __restrict__ seed, int D, int64_t vocab,
+                             float* __restrict__ streams, int32_t* status) {
+  const int64_t n = blockIdx.x;
+  int64_t id = ids[n];
+  if (id < 0 || id >= vocab) {
+    if (threadIdx.x == 0) report_status(status, LLMYB_EINVAL);
+    id = 0;
+  }
+  const __nv_bfloat16* row = table + id * D;
+  for (int d = threadIdx.x; d < D; d += blockDim.x)
+    streams[n * D + d] = bf2f(row[d]) + (seed ? seed[d] : 0.f);
+}
+
+// streams += delta (optional); y = streams * rsqrt(mean(streams^2) + eps) * w
+// (normalize = 0: y = streams, the plain residual value)
+__global__ void __launch_bounds__(256) add_rmsnorm_kernel(
+    float* __restrict__ streams, const __nv_bfloat16* __restrict__ delta, int D,
+    const float* __restrict__ weight, float eps, int normalize,
+    __nv_bfloat16* __restrict__ out_bf16, float* __restrict__ out_f32) {
+  __shared__ float red[8];
+  const int64_t n = blockIdx.x;
+  float* x = streams + n * D;
+  float ss = 0.f;
+  for (int d = threadIdx.x; d < D; d += 256) {
+    float v = x[d];
+    if (delta != nullptr) {
+      v += bf2f(delta[n * D + d]);
+      x[d] = v;
+    }
+    ss += v * v;
+  }
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) tot += red[i];
+  const float r = normalize ? rsqrtf(tot / static_cast<float>(D) + eps) : 1.f;
+  for (int d = threadIdx.x; d < D; d += 256) {
+    const float y = normalize ? x[d] * r * (weight ? weight[d] : 1.f) : x[d];
+    if (out_bf16) out_bf16[n * D + d] = f2bf(y);
+    if (out_f32) out_f32[n * D + d] = y;
+  }
+}
+
+// RMSNorm of a bf16 input (used on the collapsed stream before the LM head)
+__global__ void __launch_bounds__(256) rmsnorm_bf16_kernel(const __nv_bfloat16* __restrict__ x, int D,
+                                                           const float* __restrict__ weight,
+                                                           float eps,
+                                                           __nv_bfloat16* __restrict__ out) {
+  __shared__ float red[8];
+  const int64_t n = blockIdx.x;
+  float ss = 0.f;
+  for (int d = threadIdx.x; d < D; d += 256) {
+    const float v = bf2f(x[n * D + d]);
+    ss += v * v;
+  }
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) tot += red[i];
+  const float r = rsqrtf(tot / static_cast<float>(D) + eps);
+  for (int d = threadIdx.x; d < D; d += 256)
+    out[n * D + d] = f2bf(bf2f(x[n * D + d]) * r * (weight ? weight[d] : 1.f));
+}
+
+}  // namespace
+}  // namespace llmyb
+
+using namespace llmyb;
+
+LLMYB_API int32_t llmyb_embed(const int64_t* ids, int64_t n_tokens, const void* table,
+                              int64_t vocab, int32_t d_model, const float* stream_seed,
+                              float* streams, int32_t* dev_status, void* stream) {
+  if (!ids || !table || !streams || n_tokens < 0 || d_model <= 0 || vocab <= 0) return LLMYB_EINVAL;
+  if (n_tokens == 0) return LLMYB_OK;
+  embed_kernel<<<static_cast<unsigned>(n_tokens), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      ids, static_cast<const __nv_bfloat16*>(table), stream_seed, d_model, vocab, streams,
+      dev_status);
+  return launch_status();
+}
+
+LLMYB_API int32_t llmyb_add_rmsnorm(float* streams, const void* delta, int64_t n_tokens,
+                                    int32_t d_model, const float* weight, float eps,
+                                    int32_t normalize, void* out_bf16, float* out_f32,
+                                    void* stream) {
+  if (!streams || n_tokens < 0 || d_model <= 0) return LLMYB_EINVAL;
+  if (n_tokens == 0) return LLMYB_OK;
+  add_rmsnorm_kernel<<<static_cast<unsigned>(n_tokens), 256, 0,
+                       static_cast<cudaStream_t>(stream)>>>(
+      streams, static_cast<const __nv_bfloat16*>(delta), d_model, weight, eps, normalize,
+      static_cast<__nv_bfloat16*>(out_bf16), out_f32);
+  return launch_status();
+}
+
+LLMYB_API int32_t llmyb_rmsnorm_bf16(const void* x, int64_t n_tokens, int32_t d_model,
+                                     const float* weight, float eps, void* out, void* stream) {
+  if (!x || !out || n_tokens < 0 || d_model <= 0) return LLMYB_EINVAL;
+  if (n_tokens == 0) return LLMYB_OK;
+  rmsnorm_bf16_kernel<<<static_cast<unsigned>(n_tokens), 256, 0,
+                        static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(x), d_model, weight, eps, static_cast<__nv_bfloat16*>(out));
+  return launch_status();
+}

@@ -333,3 +333,79 @@ def csa_local_decode(q, knew, vnew, kcache, vcache, positions, heads: int, out=N
                  _ptr(vnew), vnew.stride(0), _ptr(kcache), _ptr(vcache), _ptr(positions), bsz,
                  heads, hd // heads, dm, w, _ptr(out), out.stride(0), _stream())
     return out
+
+
+# ------------------------------------------------------------- sampling
+def seen_bitmask(generated: list[list[int]], vocab: int, device) -> torch.Tensor:
+    """[B, ceil(V/32)] int32 bitmask of the ids in each row's generated list."""
+    words = (vocab + 31) // 32
+    mask = torch.zeros(len(generated), words * 32, dtype=torch.bool)
+    for r, ids in enumerate(generated):
+        if ids:
+            mask[r, torch.tensor(sorted(set(int(i) for i in ids)), dtype=torch.long)] = True
+    bits = (mask.view(len(generated), words, 32).to(torch.int64)
+            << torch.arange(32, dtype=torch.int64)).sum(-1)
+    return bits.to(torch.uint32).view(torch.int32).to(device)
+
+
+def sample(logits: torch.Tensor, *, temperature: float, top_k: int, top_p: float,
+           repetition_penalty: float = 1.0, seen: torch.Tensor | None = None,
+           blocked: torch.Tensor | None = None, uniforms: torch.Tensor | None = None,
+           update_seen: bool = False, out: torch.Tensor | None = None,
+           logprob: torch.Tensor | None = None):
+    """Device sampler (sample_standalone.py:5383-5423 semantics, inverse-CDF draw at
+    `uniforms`).  Returns (tokens [B] int64, raw log-prob of each token [B] fp32)."""
+    _require_cuda(logits, seen, blocked, uniforms)
+    if logits.dtype != torch.float32 or logits.stride(-1) != 1:
+        raise ValueError("logits must be fp32 with a contiguous vocabulary dim")
+    bsz, vocab = logits.shape
+    if uniforms is None and temperature > 1e-4:
+        uniforms = torch.rand(bsz, device=logits.device)
+    if out is None:
+        out = torch.empty(bsz, dtype=torch.int64, device=logits.device)
+    if logprob is None:
+        logprob = torch.empty(bsz, dtype=torch.float32, device=logits.device)
+    nb = 0 if blocked is None else blocked.numel()
+    _native.call("llmyb_sample", _ptr(logits), logits.stride(0), bsz, vocab, _ptr(seen),
+                 0 if seen is None else seen.stride(0), float(repetition_penalty), _ptr(blocked),
+                 nb, float(temperature), int(top_k), float(top_p), _ptr(uniforms), _ptr(out),
+                 _ptr(logprob), int(update_seen), _ptr(device_status(logits.device)), _stream())
+    return out, logprob
+
+
+# ------------------------------------------------------- residual stream
+def embed(ids: torch.Tensor, table: torch.Tensor, stream_seed: torch.Tensor | None,
+          out: torch.Tensor | None = None) -> torch.Tensor:
+    """fp32 residual stream = table[ids] + stream_seed (model/model.py:442-444)."""
+    _require_cuda(ids, table, stream_seed)
+    ids = ids.to(torch.int64)
+    n = ids.numel()
+    d = table.shape[1]
+    if out is None:
+        out = torch.empty(*ids.shape, d, dtype=torch.float32, device=ids.device)
+    _native.call("llmyb_embed", _ptr(ids), n, _ptr(table), table.shape[0], d, _ptr(stream_seed),
+                 _ptr(out), _ptr(device_status(ids.device)), _stream())
+    return out
+
+
+def add_rmsnorm(streams: torch.Tensor, delta: torch.Tensor | None, weight: torch.Tensor | None,
+                eps: float, *, out_bf16: torch.Tensor | None = None,
+                out_f32: torch.Tensor | None = None, normalize: bool = True) -> None:
+    """streams (fp32) += delta (bf16, optional); write RMSNorm(streams) * weight
+    (norms.py:13-16) as bf16 and/or fp32."""
+    _require_cuda(streams, delta, weight)
+    d = streams.shape[-1]
+    n = streams.numel() // d
+    _native.call("llmyb_add_rmsnorm", _ptr(streams), _ptr(delta), n, d, _ptr(weight), float(eps),
+                 int(normalize), _ptr(out_bf16), _ptr(out_f32), _stream())
+
+
+def rmsnorm_bf16(x: torch.Tensor, weight: torch.Tensor | None, eps: float,
+                 out: torch.Tensor | None = None) -> torch.Tensor:
+    _require_cuda(x, weight)
+    d = x.shape[-1]
+    if out is None:
+        out = torch.empty_like(x)
+    _native.call("llmyb_rmsnorm_bf16", _ptr(x), x.numel() // d, d, _ptr(weight), float(eps),
+                 _ptr(out), _stream())
+    return out

@@ -1,0 +1,298 @@
+"""Looped hybrid LLMY stack on the llmyb kernels: prefill forward and decode step.
+
+Host-side mirror of LoopedHybridMoEForCausalLM.forward / decode_step
+(model/model.py:530-707, :787-915) and PhysicalBlock.forward / forward_step
+(:162-376) for the configuration subset in ``config.HybridConfig``:
+
+    streams = embed(ids) + stream_seed                        (fp32 residual)
+    for loop in range(num_loops):            state namespace "loop{i}.core.{j}"
+        for block j:
+            x = RMSNorm_mixer(streams)                           (bf16)
+            streams += GDN(x)  |  CSA_local(x)
+            m = RMSNorm_ffn(streams)
+            streams += MoE(m)         router: top-k(softmax) over W_r RMSNorm(m)
+    logits = embed^T RMSNorm_final(collapse(streams))        (tied LM head)
+
+Every hot operation is an llmyb kernel (router + dispatch plan, grouped
+SwiGLU experts, GDN scan/step + conv gate, banded/CSA attention, fused
+residual-add RMSNorm, embedding, sampling); the dense projections are plain
+cuBLAS GEMMs through torch.  There is no CPU path: every tensor lives on the
+GPU and the kernels raise if the native library is missing.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+import torch.nn.functional as F
+
+from . import kernels
+from .config import HybridConfig
+from .state import RecurrentState, state_key
+from .weights import Block, CsaBlock, GdnBlock, ModelWeights
+
+
+@dataclass
+class HybridOutput:
+    """Subset of LoopedHybridOutput (model/model.py:67-73) the inference path fills."""
+
+    logits: torch.Tensor
+    state: RecurrentState
+
+
+class LoopedHybridModel:
+    def __init__(self, weights: ModelWeights):
+        self.w = weights
+        self.cfg: HybridConfig = weights.cfg
+        self.device = weights.embed.device
+
+    # ------------------------------------------------------------- helpers
+    def _gdn_views(self, proj: torch.Tensor, lead: tuple[int, ...]):
+        c = self.cfg
+        h, kd, vd = c.gdn_heads, c.gdn_key_dim, c.gdn_value_dim
+        hk, hv = h * kd, h * vd
+        q = proj[..., :hk].unflatten(-1, (h, kd))
+        k = proj[..., hk:2 * hk].unflatten(-1, (h, kd))
+        v = proj[..., 2 * hk:2 * hk + hv].unflatten(-1, (h, vd))
+        gate = proj[..., 2 * hk + hv:2 * hk + 2 * hv].unflatten(-1, (h, vd))
+        beta = proj[..., 2 * hk + 2 * hv:2 * hk + 2 * hv + h]
+        return q, k, v, gate, beta
+
+    def _moe(self, blk: Block, m_bf: torch.Tensor, m_f32: torch.Tensor) -> torch.Tensor:
+        """SparseMoE.forward without shared experts (moe.py:172-204)."""
+        c = self.cfg
+        r_in = torch.empty_like(m_f32)
+        # ContextAwareRouter: local = RMSNorm(hidden); logits = W local (context_router.py:62-72)
+        kernels.add_rmsnorm(m_f32, None, blk.moe.router_norm, c.rms_eps, out_f32=r_in)
+        logits = torch.mm(r_in, blk.moe.router.t())
+        plan = kernels.route(logits, c.moe_top_k)
+        return kernels.moe_grouped(m_bf, plan, blk.moe.w13, blk.moe.w2)
+
+    def _head(self, streams: torch.Tensor) -> torch.Tensor:
+        """mhc_collapse -> final_norm -> tied LM head (model/model.py:699-707)."""
+        c = self.cfg
+        sb = torch.empty(streams.shape, dtype=torch.bfloat16, device=streams.device)
+        kernels.add_rmsnorm(streams, None, None, c.rms_eps, out_bf16=sb, normalize=False)
+        collapsed = torch.mm(sb, self.w.collapse.t())
+        h = kernels.rmsnorm_bf16(collapsed, self.w.final_norm, c.rms_eps)
+        return torch.mm(h, self.w.embed.t())
+
+    # ------------------------------------------------------------- prefill
+    @torch.no_grad()
+    def forward(self, input_ids: torch.Tensor, *, state: RecurrentState | None = None,
+                reset_mask: torch.Tensor | None = None, last_logits_only: bool = False,
+                num_loops: int | None = None) -> HybridOutput:
+        """Sequence forward (LoopedHybridMoEForCausalLM.forward, inference subset)."""
+        c = self.cfg
+        if input_ids.dim() != 2:
+            raise ValueError("input_ids must have shape [batch, time]")
+        bsz, t = input_ids.shape
+        loops = c.num_loops if num_loops is None else int(num_loops)
+        if state is None:
+            state = RecurrentState(c, bsz, self.device)
+        ids = input_ids.to(self.device)
+        reset = None if reset_mask is None else reset_mask.to(self.device, torch.bool)
+        if reset is not None and bool(reset[:, 0].any()):
+            state.reset_rows(reset[:, 0])
+        streams = kernels.embed(ids.reshape(-1), self.w.embed, self.w.stream_seed)  # [N, D] fp32
+        self._run_core(streams, state, bsz, t, reset, loops)
+        state.positions.fill_(t)
+        d = c.d_model
+        hs = streams.view(bsz, t, d)
+        if last_logits_only:
+            hs = hs[:, -1:].contiguous()
+        logits = self._head(hs.reshape(-1, d)).view(bsz, -1, c.vocab_size)
+        return HybridOutput(logits, state)
+
+    @torch.no_grad()
+    def run_stack(self, hidden: torch.Tensor, *, state: RecurrentState | None = None,
+                  num_loops: int | None = None) -> torch.Tensor:
+        """The looped recurrent core on hidden states [B,T,D] (the single-block
+        workload; model/model.py:618-687 without embedding and head).  Returns
+        the fp32 residual stream after the last loop."""
+        c = self.cfg
+        bsz, t, d = hidden.shape
+        if state is None:
+            state = RecurrentState(c, bsz, self.device)
+        streams = hidden.to(self.device, torch.float32).reshape(bsz * t, d).clone()
+        self._run_core(streams, state, bsz, t, None, c.num_loops if num_loops is None else num_loops)
+        state.positions.fill_(t)
+        return streams.view(bsz, t, d)
+
+    def _run_core(self, streams, state, bsz, t, reset, loops) -> None:
+        c = self.cfg
+        n, d = bsz * t, c.d_model
+        normed = torch.empty(n, d, dtype=torch.bfloat16, device=self.device)
+        m_bf = torch.empty_like(normed)
+        m_f32 = torch.empty_like(streams)
+        pending = None  # bf16 update not yet added to the residual stream
+        for i in range(loops):
+            for j, blk in enumerate(self.w.blocks):
+                key = state_key(i, j)
+                kernels.add_rmsnorm(streams, pending, blk.mixer_norm, c.rms_eps, out_bf16=normed)
+                if isinstance(blk.mixer, GdnBlock):
+                    mixed = self._gdn_prefill(blk.mixer, normed, state, key, bsz, t, reset)
+                else:
+                    mixed = self._csa_prefill(blk.mixer, normed, state, key, bsz, t)
+                kernels.add_rmsnorm(streams, mixed, blk.ffn_norm, c.rms_eps, out_bf16=m_bf,
+                                    out_f32=m_f32)
+                pending = self._moe(blk, m_bf, m_f32)
+        kernels.add_rmsnorm(streams, pending, None, c.rms_eps, normalize=False)
+
+    def _gdn_prefill(self, g: GdnBlock, normed, state: RecurrentState, key: str, bsz: int, t: int,
+                     reset) -> torch.Tensor:
+        """GatedDeltaNet.forward (gated_deltanet.py:119-276) + the block's state carry."""
+        c = self.cfg
+        proj = torch.mm(normed, g.w_in.t())
+        kernels.gdn_activate(proj, c.gdn_heads, c.gdn_key_dim, c.gdn_value_dim, g.beta_bias)
+        q, k, v, gate, beta = self._gdn_views(proj.view(bsz, t, -1), (bsz, t))
+        o = kernels.gdn_prefill(q, k, v, gate, beta, state.gdn_states[key],
+                                decay_logit=g.decay_logit, reset=reset)
+        y = torch.mm(o.view(bsz * t, -1), g.w_out.t())
+        x3 = normed.view(bsz, t, -1)
+        mixed = kernels.gdn_conv_gate(x3, y.view(bsz, t, -1), g.conv, reset=reset)
+        # conv history for decode: the last three inputs (model/model.py:180-182)
+        hist = state.gdn_conv_histories[key]
+        keep = min(t, hist.shape[1])
+        hist.zero_()
+        hist[:, hist.shape[1] - keep:] = x3[:, t - keep:]
+        return mixed.view(bsz * t, -1)
+
+    def _csa_prefill(self, a: CsaBlock, normed, state: RecurrentState, key: str, bsz: int,
+                     t: int) -> torch.Tensor:
+        """CSA local branch (csa.py:35-75) with the remote branch disabled."""
+        c = self.cfg
+        hd = c.csa_heads * c.csa_head_dim
+        proj = torch.mm(normed, a.w_in.t()).view(bsz, t, -1)
+        q = proj[..., :hd].unflatten(-1, (c.csa_heads, c.csa_head_dim))
+        k = proj[..., hd:2 * hd].unflatten(-1, (c.csa_heads, c.csa_head_dim))
+        v = proj[..., 2 * hd:]
+        local = kernels.csa_local_prefill(q, k, v, c.csa_window)
+        mixed = torch.mm(torch.mm(local.view(bsz * t, -1), a.local_out.t()), a.out.t())
+        # ring caches for decode: token p at slot p % W (last min(T, W) tokens)
+        w = c.csa_window
+        lo = max(0, t - w)
+        src = torch.arange(lo, t, device=self.device)
+        slots = src % w
+        state.local_k[key][:, slots] = proj[:, lo:t, hd:2 * hd]
+        state.local_v[key][:, slots] = proj[:, lo:t, 2 * hd:]
+        return mixed
+
+    # -------------------------------------------------------------- decode
+    @torch.no_grad()
+    def decode_step(self, input_ids: torch.Tensor, state: RecurrentState,
+                    num_loops: int | None = None) -> torch.Tensor:
+        """One token per row (LoopedHybridMoEForCausalLM.decode_step, model/model.py:787-915).
+
+        input_ids [B] or [B, 1] on the device.  Updates `state` in place
+        (GDN states, conv histories, ring caches, positions) and returns the
+        logits [B, V] (bf16).  Allocation-stable, so it can be captured in a
+        CUDA graph after one warm-up call.
+        """
+        c = self.cfg
+        ids = input_ids.reshape(-1)
+        bsz = ids.shape[0]
+        loops = c.num_loops if num_loops is None else int(num_loops)
+        d = c.d_model
+        streams = kernels.embed(ids, self.w.embed, self.w.stream_seed)
+        normed = torch.empty(bsz, d, dtype=torch.bfloat16, device=self.device)
+        m_bf = torch.empty_like(normed)
+        m_f32 = torch.empty_like(streams)
+        pending = None
+        for i in range(loops):
+            for j, blk in enumerate(self.w.blocks):
+                key = state_key(i, j)
+                kernels.add_rmsnorm(streams, pending, blk.mixer_norm, c.rms_eps, out_bf16=normed)
+                if isinstance(blk.mixer, GdnBlock):
+                    mixed = self._gdn_step(blk.mixer, normed, state, key, bsz)
+                else:
+                    mixed = self._csa_step(blk.mixer, normed, state, key, bsz)
+                kernels.add_rmsnorm(streams, mixed, blk.ffn_norm, c.rms_eps, out_bf16=m_bf,
+                                    out_f32=m_f32)
+                pending = self._moe(blk, m_bf, m_f32)
+        kernels.add_rmsnorm(streams, pending, None, c.rms_eps, normalize=False)
+        logits = self._head(streams)
+        state.positions.add_(1)
+        return logits
+
+    def _gdn_step(self, g: GdnBlock, normed, state: RecurrentState, key: str, bsz: int):
+        c = self.cfg
+        proj = torch.mm(normed, g.w_in.t())
+        kernels.gdn_activate(proj, c.gdn_heads, c.gdn_key_dim, c.gdn_value_dim, g.beta_bias)
+        q, k, v, gate, beta = self._gdn_views(proj, (bsz,))
+        o = kernels.gdn_step(q, k, v, gate, beta, state.gdn_states[key], decay_logit=g.decay_logit)
+        y = torch.mm(o.view(bsz, -1), g.w_out.t())
+        return kernels.gdn_conv_gate(normed.view(bsz, 1, -1), y.view(bsz, 1, -1), g.conv,
+                                     history=state.gdn_conv_histories[key],
+                                     roll_history=True).view(bsz, -1)
+
+    def _csa_step(self, a: CsaBlock, normed, state: RecurrentState, key: str, bsz: int):
+        c = self.cfg
+        hd = c.csa_heads * c.csa_head_dim
+        proj = torch.mm(normed, a.w_in.t())
+        local = kernels.csa_local_decode(proj[:, :hd], proj[:, hd:2 * hd], proj[:, 2 * hd:],
+                                         state.local_k[key], state.local_v[key], state.positions,
+                                         c.csa_heads)
+        return torch.mm(torch.mm(local, a.local_out.t()), a.out.t())
+
+
+class GreedyDecoder:
+    """Decode loop with the whole step (model + sampler) captured in one CUDA graph.
+
+    The sampled token feeds the next step's embedding on the device; `step()`
+    replays the graph once per token (the role of _CudaGraphDecoder,
+    sample_standalone.py:4562-4794).
+    """
+
+    def __init__(self, model: LoopedHybridModel, state: RecurrentState, *, use_graph: bool = True,
+                 temperature: float = 0.0, top_k: int = 0, top_p: float = 1.0,
+                 repetition_penalty: float = 1.0):
+        self.model, self.state = model, state
+        self.bsz = state.batch
+        dev = model.device
+        self.tokens = torch.zeros(self.bsz, dtype=torch.int64, device=dev)
+        self.uniforms = torch.zeros(self.bsz, dtype=torch.float32, device=dev)
+        v = model.cfg.vocab_size
+        self.seen = torch.zeros(self.bsz, (v + 31) // 32, dtype=torch.int32, device=dev)
+        self.sampling = dict(temperature=temperature, top_k=top_k, top_p=top_p,
+                             repetition_penalty=repetition_penalty)
+        self.graph = None
+        self.use_graph = use_graph
+        self.logprob = None
+
+    def _body(self):
+        logits = self.model.decode_step(self.tokens, self.state).float()
+        tok, lp = kernels.sample(logits, seen=self.seen, uniforms=self.uniforms, update_seen=True,
+                                 out=self.tokens, **self.sampling)
+        self.logprob = lp
+        return logits
+
+    def prime(self, first_tokens: torch.Tensor) -> None:
+        self.tokens.copy_(first_tokens.reshape(-1))
+
+    def capture(self) -> None:
+        """Warm up once (eager) on a copy of the state, then capture the step."""
+        saved = self.state.state_dict()
+        tok0 = self.tokens.clone()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            self._body()
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        self.state.load_state_dict(saved)
+        self.tokens.copy_(tok0)
+        self.seen.zero_()
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self._body()
+        torch.cuda.synchronize()
+
+    def step(self) -> torch.Tensor:
+        if self.use_graph:
+            if self.graph is None:
+                self.capture()
+            self.graph.replay()
+        else:
+            self._body()
+        return self.tokens

@@ -1,0 +1,81 @@
+"""Device-resident recurrent state carried between tokens and loop passes.
+
+Mirrors RecurrentState (model/recurrent_state.py:76-98): per loop pass and
+block, keyed ``"loop{i}.core.{j}"`` exactly as PhysicalBlock builds its state
+keys (model/model.py:168-171) —
+  * ``gdn_states[key]``         [B, H, K, V] fp32 delta-rule state
+  * ``gdn_conv_histories[key]`` [B, 3, D] bf16, last three GDN block inputs
+  * ``local_k[key]`` / ``local_v[key]``  ring caches [B, W, H*Dh] / [B, W, D]
+    of the CSA window (token p at slot p % W).  The reference keeps the
+    normed hidden rows and re-projects K/V every step (csa.py:176-178); the
+    cache holds the same projections computed once.
+  * ``positions`` [B] int32, position of the next token of each row.
+All buffers are allocated once for a batch size so that a captured decode
+graph can update them in place.
+"""
+from __future__ import annotations
+
+import torch
+
+from .config import HybridConfig
+
+
+def state_key(loop: int, block: int) -> str:
+    return f"loop{loop}.core.{block}"
+
+
+class RecurrentState:
+    def __init__(self, cfg: HybridConfig, batch: int, device: torch.device | str = "cuda"):
+        self.cfg = cfg
+        self.batch = int(batch)
+        self.device = torch.device(device)
+        d = cfg.d_model
+        self.gdn_states: dict[str, torch.Tensor] = {}
+        self.gdn_conv_histories: dict[str, torch.Tensor] = {}
+        self.local_k: dict[str, torch.Tensor] = {}
+        self.local_v: dict[str, torch.Tensor] = {}
+        for i in range(cfg.num_loops):
+            for j in range(cfg.n_blocks):
+                key = state_key(i, j)
+                if cfg.block_kind(j) == "gdn":
+                    self.gdn_states[key] = torch.zeros(
+                        batch, cfg.gdn_heads, cfg.gdn_key_dim, cfg.gdn_value_dim,
+                        dtype=torch.float32, device=self.device)
+                    self.gdn_conv_histories[key] = torch.zeros(
+                        batch, cfg.conv_kernel - 1, d, dtype=torch.bfloat16, device=self.device)
+                else:
+                    self.local_k[key] = torch.zeros(
+                        batch, cfg.csa_window, cfg.csa_heads * cfg.csa_head_dim,
+                        dtype=torch.bfloat16, device=self.device)
+                    self.local_v[key] = torch.zeros(batch, cfg.csa_window, d,
+                                                    dtype=torch.bfloat16, device=self.device)
+        self.positions = torch.zeros(batch, dtype=torch.int32, device=self.device)
+
+    def reset_rows(self, rows: torch.Tensor) -> None:
+        """Clear the state of the selected rows (recurrent_state.py:218-244)."""
+        mask = rows.to(device=self.device, dtype=torch.bool)
+        for t in (*self.gdn_states.values(), *self.gdn_conv_histories.values()):
+            t[mask] = 0
+        self.positions[mask] = 0
+
+    def nbytes(self) -> int:
+        tensors = (*self.gdn_states.values(), *self.gdn_conv_histories.values(),
+                   *self.local_k.values(), *self.local_v.values(), self.positions)
+        return sum(t.numel() * t.element_size() for t in tensors)
+
+    def state_dict(self) -> dict[str, torch.Tensor]:
+        out: dict[str, torch.Tensor] = {"positions": self.positions.clone()}
+        for name, table in (("gdn_states", self.gdn_states),
+                            ("gdn_conv_histories", self.gdn_conv_histories),
+                            ("local_k", self.local_k), ("local_v", self.local_v)):
+            for key, t in table.items():
+                out[f"{name}.{key}"] = t.clone()
+        return out
+
+    def load_state_dict(self, sd: dict[str, torch.Tensor]) -> None:
+        self.positions.copy_(sd["positions"])
+        for name, table in (("gdn_states", self.gdn_states),
+                            ("gdn_conv_histories", self.gdn_conv_histories),
+                            ("local_k", self.local_k), ("local_v", self.local_v)):
+            for key, t in table.items():
+                t.copy_(sd[f"{name}.{key}"])

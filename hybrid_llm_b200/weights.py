@@ -1,0 +1,204 @@
+"""Weights of the looped hybrid stack in the kernels' device layout.
+
+Parameter names follow the reference state dict (model/model.py:383-423 and
+the layer modules), so a reference checkpoint's tensors load directly:
+  embed_tokens.weight [V,D]; stream_seed [1,D]; mhc_collapse.weight [D,D];
+  final_norm.weight [D]; recurrent_core.{j}.mixer_norm.weight / ffn_norm.weight;
+  GDN  recurrent_core.{j}.mixer.{q,k,v,gate,out}_proj.weight, beta_proj.{weight,bias},
+       conv.weight [D,1,4], decay_logit [H]          (gated_deltanet.py:105-113)
+  CSA  recurrent_core.{j}.mixer.{query,key,value,local_out,out}.weight  (csa.py:23-28)
+  MoE  recurrent_core.{j}.moe.router.norm.weight, moe.router.logits.weight [E,D],
+       moe.experts.{e}.{gate,up,down}_proj.weight   (moe.py:104-110, expert.py)
+Device layout: the GDN q/k/v/gate/beta projections are fused into one
+[P, D] matrix (P padded to a multiple of 8 for 16-byte rows), the CSA
+query/key/value into one [2*H*Dh + D, D] matrix, and the experts into the
+interleaved gate/up stack w13 [E, 2F, D] plus w2 [E, D, F] (bf16).
+
+``synthetic_state_dict`` draws the random-init weights of the benchmark
+workloads: every tensor with two or more dimensions ~ N(0, 0.02), norm
+weights 1, beta bias 0, decay_logit 2 (the reference's own 1-D inits), each
+tensor from its own generator seeded by (seed, name) so that any subset can
+be regenerated identically on any machine (CPU generation) or quickly on the
+GPU (CUDA generation).
+"""
+from __future__ import annotations
+
+import zlib
+from dataclasses import dataclass
+from typing import Callable, Mapping
+
+import torch
+
+from . import kernels
+from .config import HybridConfig
+
+
+def parameter_shapes(cfg: HybridConfig) -> dict[str, tuple[int, ...]]:
+    """Every reference parameter name the B200 path reads, with its shape."""
+    d, e, f = cfg.d_model, cfg.moe_experts, cfg.moe_hidden
+    shapes: dict[str, tuple[int, ...]] = {
+        "embed_tokens.weight": (cfg.vocab_size, d), "stream_seed": (1, d),
+        "mhc_collapse.weight": (d, d), "final_norm.weight": (d,),
+    }
+    for j in range(cfg.n_blocks):
+        p = f"recurrent_core.{j}."
+        shapes[p + "mixer_norm.weight"] = (d,)
+        shapes[p + "ffn_norm.weight"] = (d,)
+        if cfg.block_kind(j) == "gdn":
+            h, kd, vd = cfg.gdn_heads, cfg.gdn_key_dim, cfg.gdn_value_dim
+            shapes.update({
+                p + "mixer.q_proj.weight": (h * kd, d), p + "mixer.k_proj.weight": (h * kd, d),
+                p + "mixer.v_proj.weight": (h * vd, d), p + "mixer.beta_proj.weight": (h, d),
+                p + "mixer.beta_proj.bias": (h,), p + "mixer.gate_proj.weight": (h * vd, d),
+                p + "mixer.out_proj.weight": (d, h * vd), p + "mixer.conv.weight": (d, 1, cfg.conv_kernel),
+                p + "mixer.decay_logit": (h,),
+            })
+        else:
+            w = cfg.csa_heads * cfg.csa_head_dim
+            shapes.update({
+                p + "mixer.query.weight": (w, d), p + "mixer.key.weight": (w, d),
+                p + "mixer.value.weight": (d, d), p + "mixer.local_out.weight": (d, d),
+                p + "mixer.out.weight": (d, d),
+            })
+        shapes[p + "moe.router.norm.weight"] = (d,)
+        shapes[p + "moe.router.logits.weight"] = (e, d)
+        for x in range(e):
+            q = f"{p}moe.experts.{x}."
+            shapes[q + "gate_proj.weight"] = (f, d)
+            shapes[q + "up_proj.weight"] = (f, d)
+            shapes[q + "down_proj.weight"] = (d, f)
+    return shapes
+
+
+class LazyStateDict(Mapping):
+    """Read-only mapping name -> tensor that materialises tensors on access."""
+
+    def __init__(self, shapes: dict[str, tuple[int, ...]], make: Callable[[str, tuple], torch.Tensor]):
+        self._shapes = shapes
+        self._make = make
+
+    def __getitem__(self, name: str) -> torch.Tensor:
+        return self._make(name, self._shapes[name])
+
+    def __iter__(self):
+        return iter(self._shapes)
+
+    def __len__(self) -> int:
+        return len(self._shapes)
+
+
+def synthetic_state_dict(cfg: HybridConfig, seed: int = 0, device: str | torch.device = "cpu",
+                         std: float = 0.02) -> LazyStateDict:
+    device = torch.device(device)
+
+    def make(name: str, shape: tuple) -> torch.Tensor:
+        if len(shape) >= 2:
+            gen = torch.Generator(device=device)
+            gen.manual_seed((seed * 1_000_003 + zlib.crc32(name.encode())) % (2 ** 62))
+            return torch.randn(shape, generator=gen, device=device, dtype=torch.float32) * std
+        if name.endswith("beta_proj.bias"):
+            return torch.zeros(shape, device=device)
+        if name.endswith("decay_logit"):
+            return torch.full(shape, 2.0, device=device)
+        return torch.ones(shape, device=device)  # norm weights
+
+    return LazyStateDict(parameter_shapes(cfg), make)
+
+
+@dataclass
+class GdnBlock:
+    w_in: torch.Tensor       # [P, D] bf16: q | k | v | gate | beta | zero pad
+    beta_bias: torch.Tensor  # [H] fp32
+    decay_logit: torch.Tensor  # [H] fp32
+    w_out: torch.Tensor      # [D, H*V] bf16
+    conv: torch.Tensor       # [D, 4] fp32
+
+
+@dataclass
+class CsaBlock:
+    w_in: torch.Tensor       # [2*H*Dh + D, D] bf16: query | key | value
+    local_out: torch.Tensor  # [D, D] bf16
+    out: torch.Tensor        # [D, D] bf16
+
+
+@dataclass
+class MoeBlock:
+    router_norm: torch.Tensor  # [D] fp32
+    router: torch.Tensor       # [E, D] fp32
+    w13: torch.Tensor          # [E, 2F, D] bf16 (interleaved gate/up)
+    w2: torch.Tensor           # [E, D, F] bf16
+
+
+@dataclass
+class Block:
+    kind: str
+    mixer_norm: torch.Tensor
+    ffn_norm: torch.Tensor
+    mixer: GdnBlock | CsaBlock
+    moe: MoeBlock
+
+
+@dataclass
+class ModelWeights:
+    cfg: HybridConfig
+    embed: torch.Tensor       # [V, D] bf16 (tied LM head)
+    stream_seed: torch.Tensor  # [D] fp32
+    collapse: torch.Tensor    # [D, D] bf16
+    final_norm: torch.Tensor  # [D] fp32
+    blocks: list[Block]
+
+    @classmethod
+    def from_state_dict(cls, cfg: HybridConfig, sd: Mapping[str, torch.Tensor],
+                        device: str | torch.device = "cuda") -> "ModelWeights":
+        dev = torch.device(device)
+        bf = lambda n: sd[n].to(device=dev, dtype=torch.bfloat16).contiguous()
+        f32 = lambda n: sd[n].to(device=dev, dtype=torch.float32).contiguous()
+        blocks = []
+        for j in range(cfg.n_blocks):
+            p = f"recurrent_core.{j}."
+            if cfg.block_kind(j) == "gdn":
+                parts = [sd[p + f"mixer.{n}.weight"].to(dev, torch.bfloat16)
+                         for n in ("q_proj", "k_proj", "v_proj", "gate_proj", "beta_proj")]
+                rows = sum(x.shape[0] for x in parts)
+                pad = (-rows) % 8
+                if pad:
+                    parts.append(torch.zeros(pad, cfg.d_model, dtype=torch.bfloat16, device=dev))
+                mixer = GdnBlock(
+                    w_in=torch.cat(parts).contiguous(), beta_bias=f32(p + "mixer.beta_proj.bias"),
+                    decay_logit=f32(p + "mixer.decay_logit"), w_out=bf(p + "mixer.out_proj.weight"),
+                    conv=f32(p + "mixer.conv.weight").reshape(cfg.d_model, -1).contiguous())
+            else:
+                mixer = CsaBlock(
+                    w_in=torch.cat([bf(p + "mixer.query.weight"), bf(p + "mixer.key.weight"),
+                                    bf(p + "mixer.value.weight")]).contiguous(),
+                    local_out=bf(p + "mixer.local_out.weight"), out=bf(p + "mixer.out.weight"))
+            e = cfg.moe_experts
+            gate = torch.stack([sd[f"{p}moe.experts.{x}.gate_proj.weight"].to(dev, torch.bfloat16)
+                                for x in range(e)])
+            up = torch.stack([sd[f"{p}moe.experts.{x}.up_proj.weight"].to(dev, torch.bfloat16)
+                              for x in range(e)])
+            w13 = kernels.pack_w13(gate, up)
+            del gate, up
+            w2 = torch.stack([sd[f"{p}moe.experts.{x}.down_proj.weight"].to(dev, torch.bfloat16)
+                              for x in range(e)]).contiguous()
+            moe = MoeBlock(router_norm=f32(p + "moe.router.norm.weight"),
+                           router=f32(p + "moe.router.logits.weight"), w13=w13, w2=w2)
+            blocks.append(Block(cfg.block_kind(j), f32(p + "mixer_norm.weight"),
+                                f32(p + "ffn_norm.weight"), mixer, moe))
+        return cls(cfg=cfg, embed=bf("embed_tokens.weight"),
+                   stream_seed=f32("stream_seed").reshape(-1).contiguous(),
+                   collapse=bf("mhc_collapse.weight"), final_norm=f32("final_norm.weight"),
+                   blocks=blocks)
+
+    def nbytes(self) -> int:
+        total = 0
+        for t in self._tensors():
+            total += t.numel() * t.element_size()
+        return total
+
+    def _tensors(self):
+        yield from (self.embed, self.stream_seed, self.collapse, self.final_norm)
+        for b in self.blocks:
+            yield from (b.mixer_norm, b.ffn_norm)
+            yield from vars(b.mixer).values()
+            yield from vars(b.moe).values()

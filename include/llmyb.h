@@ -175,6 +175,46 @@ int32_t llmyb_csa_local_decode(const void* q, int64_t q_stride, const void* knew
                                int32_t batch, int32_t heads, int32_t head_dim, int32_t d_model,
                                int32_t window, void* out, int64_t out_stride, void* stream);
 
+/* --------------------------------------------------------- residual stream
+ * PhysicalBlock's residual glue with mHC disabled (model/model.py:119-126,
+ * :442-444) and RMSNorm (model/layers/norms.py:13-16).  The residual stream
+ * is fp32 (as under the reference's bf16 autocast); sub-layer outputs bf16. */
+
+/* streams[n] = float(table[ids[n]]) + stream_seed (nullable); out-of-range
+ * ids set dev_status to LLMYB_EINVAL and read row 0. */
+int32_t llmyb_embed(const int64_t* ids, int64_t n_tokens, const void* table, int64_t vocab,
+                    int32_t d_model, const float* stream_seed, float* streams,
+                    int32_t* dev_status, void* stream);
+
+/* streams (fp32) += delta (bf16, nullable), then
+ * y = streams * rsqrt(mean(streams^2) + eps) * weight (normalize != 0) or
+ * y = streams (normalize == 0), written to out_bf16 and/or out_f32. */
+int32_t llmyb_add_rmsnorm(float* streams, const void* delta, int64_t n_tokens, int32_t d_model,
+                          const float* weight, float eps, int32_t normalize, void* out_bf16,
+                          float* out_f32, void* stream);
+
+/* RMSNorm of a bf16 tensor [N, D] (final_norm before the tied LM head). */
+int32_t llmyb_rmsnorm_bf16(const void* x, int64_t n_tokens, int32_t d_model, const float* weight,
+                           float eps, void* out, void* stream);
+
+/* ---------------------------------------------------------------- sampling
+ * Replaces _sample_next_token / the sampling block of sample()
+ * (sample_standalone.py:5383-5423, :5596-5636), the native sampler
+ * (llmy_cuda/src/kernels/sample.cu:116-234) and llmy_sample
+ * (llmy_cuda/include/llmy.h:64-68).  logits [B,V] fp32 (row stride ld);
+ * seen [B, ceil(V/32)] bitmask of generated ids (repetition penalty) or null;
+ * blocked ids forced to -inf or null; temperature <= 1e-4 is greedy; top_k 0
+ * disables top-k (else <= 1024); 0 < top_p < 1 enables nucleus filtering;
+ * uniforms [B] in [0,1) drive an inverse-CDF draw.  Writes token ids [B]
+ * int64 and raw log-softmax of each token [B] (nullable); update_seen adds
+ * the token to `seen`.  dev_status gets LLMYB_EUNSUPPORTED when a top-p-only
+ * nucleus would extend beyond the 1024 best tokens. */
+int32_t llmyb_sample(const float* logits, int64_t ld, int32_t batch, int32_t vocab,
+                     uint32_t* seen, int64_t seen_ld, float repetition_penalty,
+                     const int32_t* blocked, int32_t n_blocked, float temperature, int32_t top_k,
+                     float top_p, const float* uniforms, int64_t* out_tokens, float* out_logprob,
+                     int32_t update_seen, int32_t* dev_status, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

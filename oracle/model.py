@@ -1,0 +1,139 @@
+"""Looped hybrid stack forward / decode (numpy oracle, float64).
+
+Restates LoopedHybridMoEForCausalLM.forward and decode_step
+(model/model.py:530-707, :787-915) and PhysicalBlock.forward / forward_step
+(:162-376) for the configuration subset the B200 path serves (mHC off,
+plain router, no shared experts, CSA remote branch off, no stem/tail), over a
+state dict with the reference's parameter names.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+from . import attention, gdn, routing
+
+
+def rmsnorm(x, w, eps=1e-6):
+    """norms.py:13-16."""
+    x = np.asarray(x, dtype=np.float64)
+    r = 1.0 / np.sqrt((x * x).mean(-1, keepdims=True) + eps)
+    return x * r * (1.0 if w is None else np.asarray(w, dtype=np.float64))
+
+
+class OracleModel:
+    def __init__(self, cfg, sd):
+        """cfg: hybrid_llm_b200.config.HybridConfig-like; sd: name -> array-like."""
+        self.cfg = cfg
+        self.p = {k: np.asarray(v.detach().cpu().numpy() if hasattr(v, "detach") else v,
+                                dtype=np.float64) for k, v in sd.items()}
+
+    def _gdn_params(self, j):
+        p = f"recurrent_core.{j}.mixer."
+        g = lambda n: self.p[p + n]
+        return dict(q_proj=g("q_proj.weight"), k_proj=g("k_proj.weight"), v_proj=g("v_proj.weight"),
+                    beta_proj=g("beta_proj.weight"), beta_bias=g("beta_proj.bias"),
+                    gate_proj=g("gate_proj.weight"), out_proj=g("out_proj.weight"),
+                    conv=g("conv.weight"), decay_logit=g("decay_logit"))
+
+    def _csa_params(self, j):
+        p = f"recurrent_core.{j}.mixer."
+        return {n: self.p[p + n + ".weight"] for n in ("query", "key", "value", "local_out", "out")}
+
+    def _moe(self, j, m):
+        """SparseMoE.forward (moe.py:172-199) without shared experts."""
+        c, p = self.cfg, f"recurrent_core.{j}.moe."
+        lead = m.shape[:-1]
+        flat = m.reshape(-1, m.shape[-1])
+        r = rmsnorm(flat, self.p[p + "router.norm.weight"], c.rms_eps)
+        logits = r @ self.p[p + "router.logits.weight"].T
+        idx, prob = routing.router_topk(logits.astype(np.float32), c.moe_top_k)
+        e = c.moe_experts
+        wg = np.stack([self.p[f"{p}experts.{x}.gate_proj.weight"] for x in range(e)])
+        wu = np.stack([self.p[f"{p}experts.{x}.up_proj.weight"] for x in range(e)])
+        wd = np.stack([self.p[f"{p}experts.{x}.down_proj.weight"] for x in range(e)])
+        return routing.moe_forward(flat, idx, prob, wg, wu, wd).reshape(*lead, -1), logits
+
+    def new_state(self, batch):
+        c = self.cfg
+        st = {"gdn": {}, "conv": {}, "hist": {}, "pos": np.zeros(batch, dtype=np.int64)}
+        for i in range(c.num_loops):
+            for j in range(c.n_blocks):
+                if c.block_kind(j) == "gdn":
+                    st["gdn"][(i, j)] = np.zeros((batch, c.gdn_heads, c.gdn_key_dim, c.gdn_value_dim))
+        return st
+
+    def run_stack(self, streams, state, loops=None, router_logits=None):
+        """Recurrent core over streams [B,T,D] (model/model.py:618-687)."""
+        c = self.cfg
+        loops = c.num_loops if loops is None else loops
+        x = np.asarray(streams, dtype=np.float64)
+        t = x.shape[1]
+        for i in range(loops):
+            for j in range(c.n_blocks):
+                pre = f"recurrent_core.{j}."
+                normed = rmsnorm(x, self.p[pre + "mixer_norm.weight"], c.rms_eps)
+                if c.block_kind(j) == "gdn":
+                    mixed, s = gdn.gdn_layer(normed, self._gdn_params(j), state["gdn"][(i, j)])
+                    state["gdn"][(i, j)] = s
+                    state["conv"][(i, j)] = normed[:, -(c.conv_kernel - 1):]
+                else:
+                    mixed = attention.csa_layer(normed, self._csa_params(j), c.csa_heads, c.csa_window)
+                    state["hist"][(i, j)] = normed[:, -(c.csa_window - 1):]
+                x = x + mixed
+                m = rmsnorm(x, self.p[pre + "ffn_norm.weight"], c.rms_eps)
+                y, lg = self._moe(j, m)
+                if router_logits is not None:
+                    router_logits.append(lg)
+                x = x + y
+        state["pos"][:] = t
+        return x
+
+    def head(self, x):
+        c = self.cfg
+        col = np.asarray(x) @ self.p["mhc_collapse.weight"].T
+        h = rmsnorm(col, self.p["final_norm.weight"], c.rms_eps)
+        return h @ self.p["embed_tokens.weight"].T
+
+    def embed(self, ids):
+        return self.p["embed_tokens.weight"][np.asarray(ids)] + self.p["stream_seed"].reshape(-1)
+
+    def forward(self, ids, state=None):
+        ids = np.asarray(ids)
+        state = self.new_state(ids.shape[0]) if state is None else state
+        x = self.run_stack(self.embed(ids), state)
+        return self.head(x), state
+
+    def decode_step(self, ids, state):
+        """model/model.py:787-915 with PhysicalBlock.forward_step (:266-376)."""
+        c = self.cfg
+        ids = np.asarray(ids).reshape(-1)
+        x = self.embed(ids)[:, None, :]
+        for i in range(c.num_loops):
+            for j in range(c.n_blocks):
+                pre = f"recurrent_core.{j}."
+                normed = rmsnorm(x, self.p[pre + "mixer_norm.weight"], c.rms_eps)
+                if c.block_kind(j) == "gdn":
+                    hist = state["conv"][(i, j)]
+                    if hist.shape[1] < c.conv_kernel - 1:
+                        pad = np.zeros((hist.shape[0], c.conv_kernel - 1 - hist.shape[1], hist.shape[2]))
+                        hist = np.concatenate([pad, hist], axis=1)
+                    mixed, s = gdn.gdn_layer(normed, self._gdn_params(j), state["gdn"][(i, j)],
+                                             conv_history=hist)
+                    state["gdn"][(i, j)] = s
+                    state["conv"][(i, j)] = np.concatenate([hist, normed], axis=1)[:, 1:]
+                else:
+                    a = self._csa_params(j)
+                    win = np.concatenate([state["hist"][(i, j)], normed], axis=1)[:, -c.csa_window:]
+                    b_, L, _ = win.shape
+                    q = (normed[:, 0] @ a["query"].T).reshape(b_, c.csa_heads, -1)
+                    k = (win @ a["key"].T).reshape(b_, L, c.csa_heads, -1)
+                    v = win @ a["value"].T
+                    local = attention.csa_local_step(q, k, v)
+                    mixed = ((local @ a["local_out"].T) @ a["out"].T)[:, None, :]
+                    state["hist"][(i, j)] = win[:, -(c.csa_window - 1):]
+                x = x + mixed
+                m = rmsnorm(x, self.p[pre + "ffn_norm.weight"], c.rms_eps)
+                y, _ = self._moe(j, m)
+                x = x + y
+        state["pos"] += 1
+        return self.head(x[:, 0]), state

@@ -95,3 +95,63 @@ def band_case(tag: str):
     return dict(q=rng.normal(size=(b, t, h, d)).astype(np.float32),
                 k=rng.normal(size=(b, t, h, d)).astype(np.float32),
                 v=rng.normal(size=(b, t, hv, dv)).astype(np.float32), window=w)
+
+
+SAMPLE_CASES = {
+    "greedy": dict(temp=0.0, top_k=50, top_p=0.9, rep=1.1),
+    "topk": dict(temp=0.7, top_k=50, top_p=1.0, rep=1.0),
+    "topk_topp": dict(temp=0.7, top_k=50, top_p=0.9, rep=1.1),
+    "topp_only": dict(temp=1.3, top_k=0, top_p=0.8, rep=1.2),
+    "temp_only": dict(temp=0.9, top_k=0, top_p=1.0, rep=1.0),
+    "topk_big": dict(temp=1.0, top_k=700, top_p=0.95, rep=1.05),
+}
+
+
+def sample_case(tag: str):
+    """logits [4, 1000] (a few sharp rows), generated ids per row, uniforms."""
+    rng = np.random.default_rng(6000 + sum(map(ord, tag)))
+    logits = rng.normal(0, 2.0, (4, 1000)).astype(np.float32)
+    logits[1] *= 4.0
+    generated = [rng.integers(0, 1000, size=n).tolist() for n in (0, 5, 40, 200)]
+    # the rows with many repeats get penalised ids among their top logits
+    generated[2] += np.argsort(-logits[2])[:3].tolist()
+    uniforms = rng.uniform(0, 1, 4).astype(np.float32)
+    return dict(logits=logits, generated=generated, uniforms=uniforms, **SAMPLE_CASES[tag])
+
+
+def mini_config():
+    """A small looped hybrid model inside every kernel's supported shapes."""
+    from hybrid_llm_b200.config import HybridConfig
+    return HybridConfig(vocab_size=1000, d_model=256, recurrent_layout=("csa_moe", "gdn_moe"),
+                        num_loops=2, gdn_heads=2, gdn_key_dim=64, gdn_value_dim=64, csa_heads=4,
+                        csa_head_dim=64, csa_window=32, moe_experts=8, moe_top_k=2, moe_hidden=128,
+                        name="mini")
+
+
+def mini_prompt():
+    rng = np.random.default_rng(7000)
+    return rng.integers(0, 1000, size=(2, 50)).astype(np.int64)
+
+
+def block_hidden():
+    """Single-block workload input: hidden [1, 256, 512] ~ N(0, 1)."""
+    return np.random.default_rng(1).normal(0, 1, (1, 256, 512)).astype(np.float32)
+
+
+def v6_mapping(cfg) -> dict:
+    """Reference V6Config fields for a HybridConfig (mHC, context router, shared
+    experts, loop memory, halting and the CSA remote branch switched off)."""
+    return dict(
+        vocab_size=cfg.vocab_size, d_model=cfg.d_model, physical_blocks=cfg.n_blocks,
+        stem_blocks=0, recurrent_blocks=cfg.n_blocks, tail_blocks=0, num_loops=cfg.num_loops,
+        recurrent_layout=list(cfg.recurrent_layout),
+        mhc=dict(enabled=False, streams=1),
+        gdn=dict(qk_heads=cfg.gdn_heads, value_heads=cfg.gdn_heads, qk_head_dim=cfg.gdn_key_dim,
+                 value_head_dim=cfg.gdn_value_dim, conv_kernel=cfg.conv_kernel),
+        moe=dict(routed_experts=cfg.moe_experts, shared_experts=0, routed_top_k=cfg.moe_top_k,
+                 expert_hidden=cfg.moe_hidden),
+        router=dict(context_aware=False),
+        csa=dict(temporal_compression=10 ** 9, local_window=cfg.csa_window,
+                 index_heads=cfg.csa_heads, index_head_dim=cfg.csa_head_dim, index_top_k=4),
+        loop_attnres=dict(enabled=False), adaptive_loops=dict(enabled=False),
+    )

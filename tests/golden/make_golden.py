@@ -195,7 +195,115 @@ def sec_band() -> None:
     save("band", **out)
 
 
-SECTIONS = {"router": sec_router, "moe": sec_moe, "gdn": sec_gdn, "csa": sec_csa, "band": sec_band}
+def sec_sample() -> None:
+    """_sample_next_token (sample_standalone.py:5383-5423), one row at a time, with
+    torch.multinomial replaced by the deterministic inverse CDF on a given uniform."""
+    sa = _standalone()
+    out = {}
+    real_multinomial = torch.multinomial
+    for tag in inputs.SAMPLE_CASES:
+        c = inputs.sample_case(tag)
+        toks, lps, kept = [], [], []
+        for r in range(c["logits"].shape[0]):
+            u = float(c["uniforms"][r])
+            seen_probs = []
+
+            def fake_multinomial(probs, n, *a, **k):
+                pr = probs.double()
+                cum = torch.cumsum(pr, dim=-1)
+                hit = torch.nonzero(u < cum[0])
+                idx = int(hit[0, 0]) if hit.numel() else int(torch.nonzero(pr[0] > 0)[-1, 0])
+                seen_probs.append(probs[0].clone())
+                return torch.tensor([[idx]])
+
+            torch.multinomial = fake_multinomial
+            try:
+                tok, lp = sa._sample_next_token(t(c["logits"][r:r + 1]), c["generated"][r],
+                                                temp=c["temp"], top_k=c["top_k"], top_p=c["top_p"],
+                                                rep=c["rep"])
+            finally:
+                torch.multinomial = real_multinomial
+            toks.append(int(tok))
+            lps.append(float(lp))
+            kept.append(float(seen_probs[0].max()) if seen_probs else 1.0)
+        out.update({f"{tag}_checksum": inputs.checksum(c["logits"], c["uniforms"]),
+                    f"{tag}_tokens": np.array(toks), f"{tag}_logprob": np.array(lps),
+                    f"{tag}_max_prob": np.array(kept)})
+    save("sample", **out)
+
+
+def _reference_model(cfg, standalone: bool = False):
+    """The reference model with the synthetic weights.  standalone=True builds
+    the copy in sample_standalone.py, whose decode_step carries the loop
+    output (model/model.py:846-905 leaves `streams` unchanged when every row
+    is active, so its decode logits skip the recurrent core)."""
+    from hybrid_llm_b200.weights import synthetic_state_dict
+
+    if standalone:
+        sa = _standalone()
+        V6Config, LoopedHybridMoEForCausalLM = sa.V6Config, sa.LoopedHybridMoEForCausalLM
+    else:
+        _ref_import()
+        from model.config import V6Config
+        from model.model import LoopedHybridMoEForCausalLM
+
+    model = LoopedHybridMoEForCausalLM(V6Config.from_mapping(inputs.v6_mapping(cfg))).eval()
+    sd = synthetic_state_dict(cfg, seed=0)
+    own = dict(model.named_parameters())
+    with torch.no_grad():
+        for name in sd:
+            own[name].copy_(sd[name].reshape(own[name].shape))
+    return model
+
+
+def sec_model() -> None:
+    """LoopedHybridMoEForCausalLM.forward + 6 greedy decode_step calls on the mini
+    config, and the single looped block on hidden states [1, 256, 512]."""
+    from hybrid_llm_b200.config import single_block_config
+
+    _ref_import()
+    from model.recurrent_state import RecurrentState
+
+    cfg = inputs.mini_config()
+    model = _reference_model(cfg, standalone=True)
+    ids = torch.from_numpy(inputs.mini_prompt())
+    with torch.no_grad():
+        out = model(ids, collect_diagnostics=False)
+        state = out.state
+        logits = out.logits[:, -1]
+        toks, step_logits = [], []
+        for _ in range(6):
+            nxt = logits.argmax(-1, keepdim=True)
+            toks.append(nxt[:, 0].numpy())
+            o = model.decode_step(nxt, state=state)
+            logits = o.logits[:, -1]
+            step_logits.append(logits.numpy())
+    res = {"mini_prefill_last": out.logits[:, -1].numpy(), "mini_tokens": np.stack(toks, 1),
+           "mini_step_logits": np.stack(step_logits, 1)}
+    # model/model.py's decode_step on the same inputs (loop output dropped)
+    pkg = _reference_model(cfg)
+    with torch.no_grad():
+        o1 = pkg(ids, collect_diagnostics=False)
+        o2 = pkg.decode_step(o1.logits[:, -1].argmax(-1, keepdim=True), state=o1.state)
+    res["mini_pkg_prefill_last"] = o1.logits[:, -1].numpy()
+    res["mini_pkg_step0_logits"] = o2.logits[:, -1].numpy()
+
+    bcfg = single_block_config()
+    bmodel = _reference_model(bcfg)
+    x = torch.from_numpy(inputs.block_hidden())
+    with torch.no_grad():
+        st = RecurrentState()
+        streams = x.unsqueeze(-2)
+        for i in range(bcfg.num_loops):
+            streams, _ = bmodel._run_stack(bmodel.recurrent_core, streams, st, segment_ids=None,
+                                           reset_mask=None, diagnostics={},
+                                           collect_diagnostics=False, state_namespace=f"loop{i}")
+    res["block_out_rows"] = streams[0, ::4, 0].numpy()
+    res["block_checksum"] = inputs.checksum(inputs.block_hidden())
+    save("model", **res)
+
+
+SECTIONS = {"model": sec_model, "sample": sec_sample, "router": sec_router, "moe": sec_moe, "gdn": sec_gdn, "csa": sec_csa, "band": sec_band}
 
 
 def main(argv: list[str]) -> None:
