@@ -623,25 +623,27 @@ __global__ void gdn_conv_gate_kernel(const __nv_bfloat16* __restrict__ x,
     const int t = static_cast<int>(bt % T);
     const int b = static_cast<int>(bt / T);
     float acc = 0.f;
-    // segment of t: taps from before the latest reset at or before t are dropped
+    // Prefill (no history): taps from before the latest reset at or before t
+    // are dropped (same-segment rule).  With a history (the decode path,
+    // gated_deltanet.py:257-268) there is no in-sequence masking: the history
+    // is zeroed when the row's first token carries a reset.
     int seg_start = 0;
-    if (reset != nullptr) {
+    if (reset != nullptr && history == nullptr) {
       for (int j = 0; j <= min(t, 3); ++j)
         if (reset[static_cast<int64_t>(b) * T + (t - j)]) {
           seg_start = t - j;
           break;
         }
     }
-    const bool hist_ok = history != nullptr &&
-                         !(reset != nullptr && seg_start == 0 &&
-                           reset[static_cast<int64_t>(b) * T] != 0);
+    const bool hist_ok =
+        history != nullptr && !(reset != nullptr && reset[static_cast<int64_t>(b) * T] != 0);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const int tt = t - 3 + j;
       float xv = 0.f;
       if (tt >= 0) {
         if (tt >= seg_start) xv = bf2f(x[(static_cast<int64_t>(b) * T + tt) * D + d]);
-      } else if (hist_ok && seg_start == 0) {
+      } else if (hist_ok) {
         xv = bf2f(history[(static_cast<int64_t>(b) * 3 + (3 + tt)) * D + d]);
       }
       acc += conv_w[d * 4 + j] * xv;

@@ -32,6 +32,19 @@ def _require_cuda(*tensors: torch.Tensor | None) -> None:
             raise RuntimeError("llmyb kernels take CUDA tensors only (no CPU fallback)")
 
 
+def _inplace(t: torch.Tensor, name: str) -> torch.Tensor:
+    """Tensors a kernel writes in place must already be dense."""
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous (it is updated in place)")
+    return t
+
+
+def _rows(t: torch.Tensor, name: str) -> None:
+    """[rows, cols] views read with a row stride need a unit column stride."""
+    if t.stride(-1) != 1:
+        raise ValueError(f"{name}: the last dimension must be contiguous")
+
+
 def device_status(device: torch.device | None = None) -> torch.Tensor:
     """Per-device int32 word the kernels set when a bounded wait gives up."""
     idx = torch.cuda.current_device() if device is None else torch.device(device).index or 0
@@ -201,6 +214,8 @@ def gdn_activate(proj: torch.Tensor, heads: int, key_dim: int, value_dim: int,
     """In place on the fused [N, 2HK+2HV+H] projection: L2-normalise q,k per head,
     sigmoid(gate), sigmoid(beta + bias)  (gated_deltanet.py:128-131)."""
     _require_cuda(proj)
+    _inplace(proj, "proj")
+    beta_bias = None if beta_bias is None else beta_bias.to(torch.float32).contiguous()
     n = proj.numel() // proj.shape[-1]
     _native.call("llmyb_gdn_activate", _ptr(proj), n, proj.shape[-1], heads, key_dim, value_dim,
                  _ptr(beta_bias), _stream())
@@ -223,6 +238,9 @@ def gdn_step(q, k, v, gate, beta, state, *, decay_logit=None, log_alpha=None, re
     if state.dtype != torch.float32 or not state.is_contiguous():
         raise ValueError("state must be contiguous fp32")
     r = None if reset is None else reset.to(torch.uint8).contiguous()
+    _inplace(state, "state")
+    decay_logit = None if decay_logit is None else decay_logit.to(torch.float32).contiguous()
+    log_alpha = None if log_alpha is None else log_alpha.to(torch.float32).contiguous()
     _native.call("llmyb_gdn_step", qp, qs, kp, ks, vp, vs, gp, gs, bp, bs, _ptr(decay_logit),
                  _ptr(log_alpha), _ptr(r), bsz, h, kd, vd, _ptr(state), _ptr(out),
                  out.stride(-3), _stream())
@@ -248,6 +266,8 @@ def gdn_prefill(q, k, v, gate, beta, state, *, decay_logit=None, log_alpha=None,
         scratch = torch.empty(max(need, 16), dtype=torch.uint8, device=q.device)
     r = None if reset is None else reset.to(torch.uint8).contiguous()
     la = None if log_alpha is None else log_alpha.to(torch.float32).contiguous()
+    _inplace(state, "state")
+    decay_logit = None if decay_logit is None else decay_logit.to(torch.float32).contiguous()
     _native.call("llmyb_gdn_prefill", qp, qs, kp, ks, vp, vs, gp, gs, bp, bs, _ptr(decay_logit),
                  _ptr(la), _ptr(r), bsz, t, h, kd, vd, _ptr(state), _ptr(out), out.stride(-3),
                  _ptr(scratch), _stream())
@@ -258,6 +278,11 @@ def gdn_conv_gate(x, y_proj, conv_w, *, history=None, reset=None, out=None, resi
                   roll_history=False):
     """y = y_proj * sigmoid(causal_conv4(x)); into `out` or added into `residual`."""
     _require_cuda(x, y_proj, conv_w)
+    x, y_proj = x.contiguous(), y_proj.contiguous()
+    if history is not None:
+        _inplace(history, "history")
+    if residual is not None:
+        _inplace(residual, "residual")
     bsz, t, d = x.shape
     w = conv_w.reshape(d, -1).to(torch.float32).contiguous()
     if out is None and residual is None:
@@ -322,6 +347,11 @@ def csa_local_decode(q, knew, vnew, kcache, vcache, positions, heads: int, out=N
     kcache [B,W,H*Dh]; vcache [B,W,D]; positions [B] int32 = position of the new
     token, whose K/V are written to slot position % W.  Returns [B,D] bf16."""
     _require_cuda(q, knew, vnew, kcache, vcache, positions)
+    for t_, nm in ((q, "q"), (knew, "knew"), (vnew, "vnew")):
+        _rows(t_, nm)
+    _inplace(kcache, "kcache")
+    _inplace(vcache, "vcache")
+    positions = positions.contiguous()
     bsz, hd = q.shape
     dm = vnew.shape[-1]
     w = kcache.shape[1]
@@ -358,6 +388,12 @@ def sample(logits: torch.Tensor, *, temperature: float, top_k: int, top_p: float
     _require_cuda(logits, seen, blocked, uniforms)
     if logits.dtype != torch.float32 or logits.stride(-1) != 1:
         raise ValueError("logits must be fp32 with a contiguous vocabulary dim")
+    if seen is not None:
+        _inplace(seen, "seen")
+    if blocked is not None:
+        blocked = blocked.to(torch.int32).contiguous()
+    if uniforms is not None:
+        uniforms = uniforms.to(torch.float32).contiguous()
     bsz, vocab = logits.shape
     if uniforms is None and temperature > 1e-4:
         uniforms = torch.rand(bsz, device=logits.device)
@@ -378,7 +414,8 @@ def embed(ids: torch.Tensor, table: torch.Tensor, stream_seed: torch.Tensor | No
           out: torch.Tensor | None = None) -> torch.Tensor:
     """fp32 residual stream = table[ids] + stream_seed (model/model.py:442-444)."""
     _require_cuda(ids, table, stream_seed)
-    ids = ids.to(torch.int64)
+    ids = ids.to(torch.int64).contiguous()
+    table = table.contiguous()
     n = ids.numel()
     d = table.shape[1]
     if out is None:
@@ -394,6 +431,11 @@ def add_rmsnorm(streams: torch.Tensor, delta: torch.Tensor | None, weight: torch
     """streams (fp32) += delta (bf16, optional); write RMSNorm(streams) * weight
     (norms.py:13-16) as bf16 and/or fp32."""
     _require_cuda(streams, delta, weight)
+    _inplace(streams, "streams")
+    delta = None if delta is None else delta.contiguous()
+    for o, nm in ((out_bf16, "out_bf16"), (out_f32, "out_f32")):
+        if o is not None:
+            _inplace(o, nm)
     d = streams.shape[-1]
     n = streams.numel() // d
     _native.call("llmyb_add_rmsnorm", _ptr(streams), _ptr(delta), n, d, _ptr(weight), float(eps),
@@ -403,9 +445,11 @@ def add_rmsnorm(streams: torch.Tensor, delta: torch.Tensor | None, weight: torch
 def rmsnorm_bf16(x: torch.Tensor, weight: torch.Tensor | None, eps: float,
                  out: torch.Tensor | None = None) -> torch.Tensor:
     _require_cuda(x, weight)
+    x = x.contiguous()
     d = x.shape[-1]
     if out is None:
         out = torch.empty_like(x)
+    _inplace(out, "out")
     _native.call("llmyb_rmsnorm_bf16", _ptr(x), x.numel() // d, d, _ptr(weight), float(eps),
                  _ptr(out), _stream())
     return out
