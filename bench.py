@@ -1,0 +1,452 @@
+"""Benchmark of the B200-native looped hybrid LLMY stack (one JSON line on rank 0).
+
+Headline workload (N=1): the full small LLMY model (vocab 32000, d_model 768,
+12 alternating CSA/GDN blocks with a 16-expert top-2 MoE in each, 2 loops),
+bf16, random-init N(0, 0.02) weights, a 512-token prompt of uniform ids,
+then greedy decode at batch 1.  One step = one decoded token: the whole
+decode step (embedding -> 2 x 12 blocks -> LM head -> sampler) is one CUDA
+graph replay, the sampled token feeding the next step on the device.
+
+  value   decode tokens/s with everything resident on the device
+  e2e     the same through the public decode API with a pinned-host token
+          round trip every step (H2D of the input id, D2H of the sampled id
+          and its log-probability)
+  secondary  isolated-MoE-layer TFLOPS (16384 tokens x 1024, 32 experts top-4,
+          Zipf-skewed routing), long-context prefill (banded attention and the
+          GDN chunked scan at B=8, T=8192), small-model prefill tokens/s
+  cpu_baseline  the CPU port of the reference algorithm (oracle/) timed on
+          this host on a bounded sample of the same decode workload
+
+Under torchrun (N > 1) every rank decodes its own replica (the decode path
+has no cross-GPU exchange: "replicas only"), the time is the max over ranks
+and value is the sum of all ranks' tokens / that time.
+
+``--impl reference`` times the CPU port of the reference's decode path on the
+host cores (rank 0 only), with the same metric and workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "decode tok/s (B=1, B=64), prefill tok/s, MoE TFLOPS at 1/2/4/8 B200"
+WORKLOAD = "small-llmy greedy decode B=1 (vocab 32000, d768, 12 blocks csa/gdn+moe16top2, 2 loops, prompt 512)"
+
+
+def peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained", d["bf16_tflops"]),
+                "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+            "source": "fallback"}
+
+
+# ----------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi clock/throttle samples during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        import statistics
+        rows = []
+        if self.path and os.path.exists(self.path):
+            for line in open(self.path):
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) >= 9 and parts[1].replace(".", "").isdigit():
+                    rows.append(parts)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        sm = [float(r[1]) for r in rows]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            for name, val in zip(names, r[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": float(rows[0][2]),
+                "reasons": sorted(reasons), "samples": len(rows)}
+
+
+# ------------------------------------------------------------ CPU baseline
+def cpu_decode_baseline(steps: int, warmup: int, prompt_len: int = 16) -> dict:
+    """Time the CPU port of the reference decode path (oracle/) on this host.
+
+    Same model shape as the GPU workload, fp32 numpy, batch 1.  The prompt is
+    shortened to bound the (untimed) prefill; per-token decode work differs
+    only in the CSA window length (negligible next to the dense and expert
+    GEMVs).  Weights are N(0, 0.02) from numpy's generator (values do not
+    affect the timing).
+    """
+    import numpy as np
+    import torch
+
+    from hybrid_llm_b200.config import small_llmy_config
+    from hybrid_llm_b200.weights import parameter_shapes
+    from oracle.model import OracleModel
+
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    cfg = small_llmy_config()
+    rng = np.random.default_rng(0)
+    sd = {}
+    for name, shape in parameter_shapes(cfg).items():
+        if len(shape) >= 2:
+            sd[name] = rng.standard_normal(shape, dtype=np.float32) * np.float32(0.02)
+        elif name.endswith("decay_logit"):
+            sd[name] = np.full(shape, 2.0, np.float32)
+        elif name.endswith("beta_proj.bias"):
+            sd[name] = np.zeros(shape, np.float32)
+        else:
+            sd[name] = np.ones(shape, np.float32)
+    m = OracleModel(cfg, sd, dtype=np.float32)
+    ids = rng.integers(0, cfg.vocab_size, (1, prompt_len))
+    logits, st = m.forward(ids)
+    tok = logits[:, -1].argmax(-1)
+    for _ in range(warmup):
+        logits, st = m.decode_step(tok, st)
+        tok = logits.argmax(-1)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        logits, st = m.decode_step(tok, st)
+        tok = logits.argmax(-1)
+    dt = time.perf_counter() - t0
+    return {"value": steps / dt, "unit": "tok/s", "cores": cores, "kind": "port",
+            "sample": f"{steps} greedy decode tokens at B=1 after a {prompt_len}-token prompt, "
+                      f"fp32 numpy port of the reference decode path, {cores} host threads"}
+
+
+# -------------------------------------------------------------- reference
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    steps = max(1, min(args.steps, 5))
+    res = cpu_decode_baseline(steps=steps, warmup=1)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": res["value"], "unit": "tok/s",
+        "n_gpus": args.gpus, "steps": steps, "warmup": 1, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
+        "config": {"workload": WORKLOAD + " [CPU port, prompt 16]"},
+        "cpu_baseline": res,
+        "e2e": {"value": res["value"], "unit": "tok/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------- our path
+def _events():
+    import torch
+    return torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+
+def secondary_moe(p: dict) -> dict:
+    """Isolated MoE layer: 16384 x 1024 bf16, 32 experts top-4, F=512, Zipf bias."""
+    import numpy as np
+    import torch
+
+    from hybrid_llm_b200 import kernels
+    from oracle.routing import zipf_expert_bias
+
+    n, d, e, k, f = 16384, 1024, 32, 4, 512
+    g = torch.Generator(device="cuda").manual_seed(0)
+    x = torch.randn(n, d, device="cuda", generator=g).bfloat16()
+    wr = torch.randn(e, d, device="cuda", generator=g) * 0.02
+    bias = torch.from_numpy(zipf_expert_bias(e)).cuda()
+    wg = (torch.randn(e, f, d, device="cuda", generator=g) * 0.02).bfloat16()
+    wu = (torch.randn(e, f, d, device="cuda", generator=g) * 0.02).bfloat16()
+    wd = (torch.randn(e, d, f, device="cuda", generator=g) * 0.02).bfloat16()
+    w13 = kernels.pack_w13(wg, wu)
+    out = torch.empty(n, d, device="cuda", dtype=torch.bfloat16)
+    scratch = torch.empty(int(kernels._native.lib().llmyb_moe_grouped_scratch_bytes(n, k, d, f)),
+                          dtype=torch.uint8, device="cuda")
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+
+    def layer():
+        logits = torch.mm(x.float(), wr.t())
+        plan = kernels.route(logits, k, bias)
+        kernels.moe_grouped(x, plan, w13, wd, out=out, scratch=scratch)
+        return plan
+
+    for _ in range(3):
+        plan = layer()
+    times = []
+    for _ in range(10):
+        flush.zero_()
+        a, b = _events()
+        a.record()
+        layer()
+        b.record()
+        torch.cuda.synchronize()
+        times.append(a.elapsed_time(b))
+    t = float(np.median(times)) * 1e-3
+    flops = 2.0 * n * k * 3 * f * d
+    counts = plan.counts.cpu().tolist()
+    return {"workload": "isolated MoE layer 16384x1024, 32 experts top-4, F=512, Zipf(1.1) bias",
+            "ms": t * 1e3, "tflops": flops / t / 1e12,
+            "frac_of_bf16_peak": flops / t / 1e12 / p["bf16_tflops"],
+            "includes": "router logits GEMM + top-k/plan + gather + 2 grouped GEMMs + combine",
+            "expert_load": counts}
+
+
+def secondary_prefill(p: dict) -> dict:
+    """Long-context prefill kernels: banded attention and the GDN chunked scan."""
+    import numpy as np
+    import torch
+
+    from hybrid_llm_b200 import kernels
+
+    b, t, h, d, w = 8, 8192, 16, 128, 1024
+    g = torch.Generator(device="cuda").manual_seed(1)
+    q, k, v = (torch.randn(b, t, h, d, device="cuda", generator=g).bfloat16() for _ in range(3))
+    out = torch.empty_like(q)
+    for _ in range(3):
+        kernels.banded_attention(q, k, v, w, out=out)
+    times = []
+    for _ in range(5):
+        a, e_ = _events()
+        a.record()
+        kernels.banded_attention(q, k, v, w, out=out)
+        e_.record()
+        torch.cuda.synchronize()
+        times.append(a.elapsed_time(e_))
+    ta = float(np.median(times)) * 1e-3
+    pairs = w * (w + 1) / 2 + (t - w) * w
+    attn_flops = 4.0 * d * pairs * b * h
+    del out
+    qn = torch.nn.functional.normalize(q.float(), dim=-1).bfloat16()
+    kn = torch.nn.functional.normalize(k.float(), dim=-1).bfloat16()
+    del q, k
+    beta = torch.rand(b, t, h, device="cuda", generator=g).bfloat16()
+    gate = torch.rand(b, t, h, d, device="cuda", generator=g).bfloat16()
+    la = -0.1 * torch.rand(b, t, h, device="cuda", generator=g)
+    st = torch.zeros(b, h, d, d, device="cuda")
+    o = torch.empty_like(v)
+    need = int(kernels._native.lib().llmyb_gdn_prefill_scratch_bytes(b, t, h, d, d))
+    scratch = torch.empty(need, dtype=torch.uint8, device="cuda")
+    for _ in range(2):
+        st.zero_()
+        kernels.gdn_prefill(qn, kn, v, gate, beta, st, log_alpha=la, out=o, scratch=scratch)
+    times = []
+    for _ in range(5):
+        st.zero_()
+        a, e_ = _events()
+        a.record()
+        kernels.gdn_prefill(qn, kn, v, gate, beta, st, log_alpha=la, out=o, scratch=scratch)
+        e_.record()
+        torch.cuda.synchronize()
+        times.append(a.elapsed_time(e_))
+    tg = float(np.median(times)) * 1e-3
+    gdn_bytes = b * t * h * (4 * d * 2 + 2 + 4) + 2 * b * h * d * d * 4
+    return {"workload": "B=8 T=8192 H=16 Dh=128: banded attention W=1024; GDN chunk-64 scan K=V=128",
+            "banded_attention_ms": ta * 1e3, "banded_attention_tflops": attn_flops / ta / 1e12,
+            "banded_attention_frac_of_bf16_peak": attn_flops / ta / 1e12 / p["bf16_tflops"],
+            "gdn_scan_ms": tg * 1e3, "gdn_scan_gbs": gdn_bytes / tg / 1e9,
+            "gdn_scan_frac_of_hbm": gdn_bytes / tg / 1e9 / p["hbm_gbs"],
+            "prefill_tok_s": b * t / (ta + tg)}
+
+
+def run_ours(args) -> None:
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from hybrid_llm_b200 import kernels
+    from hybrid_llm_b200.config import small_llmy_config
+    from hybrid_llm_b200.model import GreedyDecoder, LoopedHybridModel
+    from hybrid_llm_b200.weights import ModelWeights, synthetic_state_dict
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    p = peaks()
+    cfg = small_llmy_config()
+    bsz, prompt_len = 1, 512
+    model = LoopedHybridModel(ModelWeights.from_state_dict(
+        cfg, synthetic_state_dict(cfg, seed=0, device="cuda"), "cuda"))
+    prompt = torch.from_numpy(np.random.default_rng(0).integers(0, cfg.vocab_size, (bsz, prompt_len))).cuda()
+
+    # prefill (timed separately: prompt tokens/s)
+    model.forward(prompt, last_logits_only=True)
+    torch.cuda.synchronize()
+    a, b = _events()
+    a.record()
+    out = model.forward(prompt, last_logits_only=True)
+    b.record()
+    torch.cuda.synchronize()
+    prefill_s = a.elapsed_time(b) * 1e-3
+
+    dec = GreedyDecoder(model, out.state, use_graph=True)
+    dec.prime(out.logits[:, -1].float().argmax(-1))
+    n0 = kernels.launch_count()
+    dec.capture()
+    launches_capture = kernels.launch_count() - n0
+    # capture() runs one eager warm-up step then captures one step
+    launches_per_step = launches_capture // 2
+    for _ in range(args.warmup):
+        dec.step()
+    torch.cuda.synchronize()
+
+    clocks = ClockSampler(local)
+    with clocks:
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        a, b = _events()
+        a.record()
+        for _ in range(args.steps):
+            dec.step()
+        b.record()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+    t_ms = a.elapsed_time(b)
+    if world > 1:
+        tt = torch.tensor([t_ms], device="cuda")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        t_ms = float(tt.item())
+    value = bsz * args.steps * world / (t_ms * 1e-3)
+
+    # e2e: public decode API with a pinned-host token round trip per step
+    host_in = torch.empty(bsz, dtype=torch.int64).pin_memory()
+    host_out = torch.empty(bsz, dtype=torch.int64).pin_memory()
+    host_lp = torch.empty(bsz, dtype=torch.float32).pin_memory()
+    host_in.copy_(dec.tokens.cpu())
+    torch.cuda.synchronize()
+    a, b = _events()
+    a.record()
+    for _ in range(args.steps):
+        dec.tokens.copy_(host_in, non_blocking=True)
+        tok = dec.step()
+        host_out.copy_(tok, non_blocking=True)
+        host_lp.copy_(dec.logprob, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        host_in.copy_(host_out)
+    b.record()
+    torch.cuda.synchronize()
+    e2e_ms = a.elapsed_time(b)
+    if world > 1:
+        tt = torch.tensor([e2e_ms], device="cuda")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        e2e_ms = float(tt.item())
+    e2e = {"value": bsz * args.steps * world / (e2e_ms * 1e-3), "unit": "tok/s",
+           "h2d_bytes_per_step": host_in.numel() * 8,
+           "d2h_bytes_per_step": host_out.numel() * 8 + host_lp.numel() * 4}
+
+    # roofline of the dominant kernel family: the decode step is HBM-bound on
+    # the weights it streams; measured per step over the timed region
+    touched = decode_bytes_per_step(model, cfg)
+    achieved = touched / (t_ms * 1e-3 / args.steps) / 1e9
+    roofline = {"bound": "hbm", "achieved": achieved, "peak": p["hbm_gbs"], "unit": "GB/s",
+                "frac": achieved / p["hbm_gbs"], "traffic": None,
+                "kernel": "whole decode step (one CUDA graph); algorithmic bytes = weights and "
+                          "state touched per token",
+                "algorithmic_bytes_per_step": touched, "peak_source": p["source"]}
+
+    line = {
+        "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": t_ms / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (uniform token ids, N(0,0.02) random-init weights)",
+        "config": {"workload": WORKLOAD, "batch": bsz, "prompt_len": prompt_len,
+                   "parallelism": f"replicas{world}" if world > 1 else "single",
+                   "l2": "no flush: >1 GB of weights, about 0.3 GB touched per step (> 126 MB L2)"},
+        "e2e": e2e, "gpu_launches": launches_per_step * args.steps, "roofline": roofline,
+        "clocks": clocks.summary(), "prefill_tok_s_c2": bsz * prompt_len / prefill_s,
+    }
+    if rank == 0 and world == 1 and not args.no_secondary:
+        del dec, out
+        torch.cuda.empty_cache()
+        line["secondary"] = {"moe_layer": secondary_moe(p), "long_prefill": secondary_prefill(p)}
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_decode_baseline(steps=3, warmup=1)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def decode_bytes_per_step(model, cfg) -> float:
+    """Algorithmic HBM bytes of one decode token at B=1: every dense weight once,
+    the routed experts (top-k of E per block and loop), the KV window and GDN
+    state of every block-loop, the tied LM head."""
+    d = cfg.d_model
+    dense = 0
+    for blk in model.w.blocks:
+        m = blk.mixer
+        dense += sum(t.numel() * t.element_size() for t in vars(m).values())
+        dense += blk.moe.router.numel() * 4
+    dense *= cfg.num_loops
+    expert = 3 * cfg.moe_hidden * d * 2 * cfg.moe_top_k * cfg.n_blocks * cfg.num_loops
+    n_csa = sum(1 for j in range(cfg.n_blocks) if cfg.block_kind(j) == "csa") * cfg.num_loops
+    n_gdn = cfg.n_blocks * cfg.num_loops - n_csa
+    kv = n_csa * cfg.csa_window * (cfg.csa_heads * cfg.csa_head_dim + d) * 2
+    gdn_state = n_gdn * cfg.gdn_heads * cfg.gdn_key_dim * cfg.gdn_value_dim * 4 * 2
+    head = cfg.vocab_size * d * 2 + d * d * 2
+    return float(dense + expert + kv + gdn_state + head)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-secondary", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -40,6 +40,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "llmyb_moe_pack_w13": (I32, [P, P, I32, I32, I32, P, P]),
     "llmyb_moe_grouped_scratch_bytes": (I64, [I32, I32, I32, I32]),
     "llmyb_moe_grouped_swiglu": (I32, [P, I32, I32, I32, P, P, P, P, P, I32, P, P, I32, P, P, P, P]),
+    "llmyb_moe_decode_scratch_bytes": (I64, [I32, I32, I32, I32]),
+    "llmyb_moe_decode_swiglu": (I32, [P, I32, I32, I32, P, P, P, P, I32, P, P, I32, P, P, P]),
     # gated delta rule
     "llmyb_gdn_activate": (I32, [P, I64, I32, I32, I32, I32, P, P]),
     "llmyb_gdn_step": (I32, [P, I64, P, I64, P, I64, P, I64, P, I64, P, P, P, I32, I32, I32, I32,
@@ -56,6 +58,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
                                       P, P]),
     "llmyb_csa_local_decode": (I32, [P, I64, P, I64, P, I64, P, P, P, I32, I32, I32, I32, I32, P,
                                      I64, P]),
+    # diagnostics
+    "llmyb_launch_count": (I64, []),
     # residual stream
     "llmyb_embed": (I32, [P, I64, P, I64, I32, P, P, P, P]),
     "llmyb_add_rmsnorm": (I32, [P, P, I64, I32, P, F32, I32, P, P, P]),

@@ -402,8 +402,12 @@ __global__ void __launch_bounds__(BM * 2) csa_pv_kernel(
 
 // ------------------------------------------------------------- decode
 constexpr int kClusterCtas = 8;
+constexpr int kMaxChunks = 8;  // 16-byte chunks of a K row per lane: H*DH <= 2048
 
-// scores of this CTA's keys live in dynamic shared memory: [H][keys_per_cta]
+// Scores and partial outputs are computed from 16-byte row loads with many
+// loads in flight per warp (the kernel is bound by the K/V window bytes).
+// Dynamic shared memory: q [H*DH] | scores [H][kpc] | m, l, M, L [H] |
+// p [kpc] | partial out [groups][D].
 __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(256)
     csa_decode_kernel(const __nv_bfloat16* __restrict__ q, int64_t sq,
                       const __nv_bfloat16* __restrict__ knew, int64_t skn,
@@ -418,42 +422,67 @@ __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(256)
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int kpc = (Wc + kClusterCtas - 1) / kClusterCtas;  // keys per CTA
   const int HD = H * DH;
-  float* s_q = dsm;                 // [H*DH]
-  float* s_sc = s_q + HD;           // [H][kpc] scores (log2 units)
-  float* s_m = s_sc + H * kpc;      // [H] local max
-  float* s_l = s_m + H;             // [H] local sum
-  float* s_M = s_l + H;             // [H] cluster-wide max
-  float* s_L = s_M + H;             // [H] cluster-wide sum
-  float* s_p = s_L + H;             // [kpc] head-averaged probabilities
-  float* s_o = s_p + kpc;           // [D] partial output
+  const int nch = HD / 8;            // 16-byte chunks per K row
+  const int seg = DH / 8;            // lanes per head within one pass (8 or 16)
+  const int vch = D / 8;             // 16-byte chunks per V row
+  const int groups = max(1, 256 / vch);
+  float* s_q = dsm;
+  float* s_sc = s_q + HD;
+  float* s_m = s_sc + H * kpc;
+  float* s_l = s_m + H;
+  float* s_M = s_l + H;
+  float* s_L = s_M + H;
+  float* s_p = s_L + H;
+  float* s_o = s_p + kpc;            // [groups][D]
 
   const int pos = positions[b];
   const int n_valid = min(pos + 1, Wc);
   const int cur_slot = pos % Wc;
   const int j_begin = crank * kpc;
   const int j_end = min(Wc, j_begin + kpc);
+  const int nk = max(0, min(j_end, n_valid) - j_begin);  // valid keys of this CTA
   const int64_t cache_row = static_cast<int64_t>(b) * Wc;
 
   for (int i = tid; i < HD; i += 256) s_q[i] = bf2f(q[b * sq + i]);
   __syncthreads();
-  // ---- scores
-  for (int j = j_begin + warp; j < j_end; j += 8) {
-    const bool valid = j < n_valid;
+  // ---- scores: one key per warp iteration, the whole K row in flight
+  for (int jl = warp; jl < nk; jl += 8) {
+    const int j = j_begin + jl;
     const __nv_bfloat16* kr = (j == cur_slot) ? knew + b * skn : kcache + (cache_row + j) * HD;
-    for (int hh = 0; hh < H; ++hh) {
+    uint4 kv[kMaxChunks];
+#pragma unroll
+    for (int i = 0; i < kMaxChunks; ++i) {
+      const int c = lane + 32 * i;
+      if (c < nch) kv[i] = __ldg(reinterpret_cast<const uint4*>(kr) + c);
+    }
+#pragma unroll
+    for (int i = 0; i < kMaxChunks; ++i) {
+      const int c = lane + 32 * i;
       float acc = 0.f;
-      if (valid)
-        for (int d = lane; d < DH; d += 32) acc += s_q[hh * DH + d] * bf2f(kr[hh * DH + d]);
-      acc = warp_sum(acc);
-      if (lane == 0) s_sc[hh * kpc + (j - j_begin)] = valid ? acc * scale_log2 : -INFINITY;
+      if (c < nch) {
+        const uint32_t w[4] = {kv[i].x, kv[i].y, kv[i].z, kv[i].w};
+        const float* qq = s_q + c * 8;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = unpack_bf16x2(w[e]);
+          acc += qq[2 * e] * f.x + qq[2 * e + 1] * f.y;
+        }
+      }
+      if (32 * i < nch) {
+        for (int o = 1; o < seg; o <<= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+        if (c < nch && (c % seg) == 0) s_sc[(c / seg) * kpc + jl] = acc * scale_log2;
+      }
     }
     if (j == cur_slot) {  // append the current token to the ring
-      for (int d = lane; d < HD; d += 32) kcache[(cache_row + j) * HD + d] = knew[b * skn + d];
-      for (int d = lane; d < D; d += 32) vcache[(cache_row + j) * D + d] = vnew[b * svn + d];
+      for (int c = lane; c < nch; c += 32)
+        reinterpret_cast<uint4*>(kcache + (cache_row + j) * HD)[c] =
+            reinterpret_cast<const uint4*>(knew + b * skn)[c];
+      for (int c = lane; c < vch; c += 32)
+        reinterpret_cast<uint4*>(vcache + (cache_row + j) * D)[c] =
+            reinterpret_cast<const uint4*>(vnew + b * svn)[c];
     }
   }
   __syncthreads();
-  const int nk = max(0, j_end - j_begin);
   for (int hh = warp; hh < H; hh += 8) {
     float mx = -INFINITY;
     for (int j = lane; j < nk; j += 32) mx = fmaxf(mx, s_sc[hh * kpc + j]);
@@ -468,7 +497,7 @@ __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(256)
     }
   }
   cluster.sync();
-  // ---- global per-head max/sum from every CTA of the cluster
+  // ---- cluster-wide per-head max / sum
   for (int hh = warp; hh < H; hh += 8) {
     float mloc = -INFINITY, lloc = 0.f;
     if (lane < kClusterCtas) {
@@ -486,27 +515,41 @@ __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(256)
   // ---- head-averaged probabilities of this CTA's keys
   for (int j = tid; j < nk; j += 256) {
     float p = 0.f;
-    for (int hh = 0; hh < H; ++hh) {
-      const float x = s_sc[hh * kpc + j];
-      if (x != -INFINITY) p += exp2f(x - s_M[hh]) / s_L[hh];
-    }
+    for (int hh = 0; hh < H; ++hh) p += exp2f(s_sc[hh * kpc + j] - s_M[hh]) / s_L[hh];
     s_p[j] = p / static_cast<float>(H);
   }
   __syncthreads();
-  // ---- partial output over this CTA's keys
-  for (int d0 = tid * 2; d0 < D; d0 += 512) {
-    float a0 = 0.f, a1 = 0.f;
-    for (int j = 0; j < nk; ++j) {
-      const float p = s_p[j];
-      if (p == 0.f) continue;
-      const int jj = j_begin + j;
-      const __nv_bfloat16* vr = (jj == cur_slot) ? vnew + b * svn : vcache + (cache_row + jj) * D;
-      const float2 vv = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(vr + d0));
-      a0 += p * vv.x;
-      a1 += p * vv.y;
+  // ---- partial output: thread = (key group, 16-byte column chunk)
+  {
+    const int g = tid / vch, c = tid - g * vch;
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    if (g < groups) {
+      int j = g;
+#pragma unroll 4
+      for (; j < nk; j += groups) {
+        const int jj = j_begin + j;
+        const __nv_bfloat16* vr =
+            (jj == cur_slot) ? vnew + b * svn : vcache + (cache_row + jj) * D;
+        const uint4 v4 = __ldg(reinterpret_cast<const uint4*>(vr) + c);
+        const float p = s_p[j];
+        const uint32_t w[4] = {v4.x, v4.y, v4.z, v4.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = unpack_bf16x2(w[e]);
+          acc[2 * e] += p * f.x;
+          acc[2 * e + 1] += p * f.y;
+        }
+      }
+      for (int e = 0; e < 8; ++e) s_o[g * D + c * 8 + e] = acc[e];
     }
-    s_o[d0] = a0;
-    s_o[d0 + 1] = a1;
+  }
+  __syncthreads();
+  if (groups > 1) {
+    for (int d = tid; d < D; d += 256) {
+      float acc = s_o[d];
+      for (int g = 1; g < groups; ++g) acc += s_o[g * D + d];
+      s_o[d] = acc;
+    }
   }
   cluster.sync();
   // ---- reduce this CTA's column slice over the cluster
@@ -540,6 +583,7 @@ int32_t launch_band(const __nv_bfloat16* q, int64_t sq, const __nv_bfloat16* k, 
   const int grid = B * H * static_cast<int>(ceil_div(T, BMQ));
   banded_attn_kernel<D, STATS><<<grid, 128, bytes, s>>>(q, sq, k, sk, v, sv, v_heads, B, T, H, W,
                                                         scale * kLog2e, out, so, m_out, l_out);
+  count_launch();
   return launch_status();
 }
 
@@ -634,6 +678,7 @@ LLMYB_API int32_t llmyb_csa_local_prefill(const void* q, int64_t q_stride, const
     const int grid = batch * static_cast<int>(ceil_div(seq, BM)) * (d_model / DC);
     kern<<<grid, BM * 2, bytes, s>>>(Q, q_stride, K, k_stride, V, v_stride, batch, seq, heads,
                                      d_model, w, scale * kLog2e, m, l, O, out_stride);
+    count_launch();
     (void)dh;
     return launch_status();
   };
@@ -660,9 +705,17 @@ LLMYB_API int32_t llmyb_csa_local_decode(const void* q, int64_t q_stride, const 
       heads <= 0 || head_dim <= 0 || window <= 0)
     return LLMYB_EINVAL;
   if (batch == 0) return LLMYB_OK;
-  if (d_model % (2 * kClusterCtas) != 0) return LLMYB_EUNSUPPORTED;
+  const int hd = heads * head_dim;
+  if (d_model % (8 * kClusterCtas) != 0 || head_dim % 8 != 0 || hd > 8 * 32 * kMaxChunks ||
+      d_model > 8 * 256 || !(head_dim == 64 || head_dim == 128))
+    return LLMYB_EUNSUPPORTED;
+  if (((reinterpret_cast<uintptr_t>(knew) | reinterpret_cast<uintptr_t>(vnew) |
+        reinterpret_cast<uintptr_t>(kcache) | reinterpret_cast<uintptr_t>(vcache)) & 15u) ||
+      knew_stride % 8 != 0 || vnew_stride % 8 != 0)
+    return LLMYB_EUNSUPPORTED;
   const int kpc = (window + kClusterCtas - 1) / kClusterCtas;
-  const int bytes = (heads * head_dim + heads * kpc + 4 * heads + kpc + d_model) * 4;
+  const int groups = std::max(1, 256 / (d_model / 8));
+  const int bytes = (hd + heads * kpc + 4 * heads + kpc + groups * d_model) * 4;
   if (bytes > 227 * 1024) return LLMYB_EUNSUPPORTED;
   static int attr_bytes = 0;
   if (bytes > attr_bytes) {
@@ -676,5 +729,6 @@ LLMYB_API int32_t llmyb_csa_local_decode(const void* q, int64_t q_stride, const 
       static_cast<__nv_bfloat16*>(kcache), static_cast<__nv_bfloat16*>(vcache), positions, heads,
       head_dim, d_model, window, kLog2e / sqrtf(static_cast<float>(head_dim)),
       static_cast<__nv_bfloat16*>(out), out_stride);
+  count_launch();
   return launch_status();
 }

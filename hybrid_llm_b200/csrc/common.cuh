@@ -23,6 +23,12 @@ namespace llmyb {
 
 __host__ __device__ inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
+// Host-side count of kernel launches issued by this library (diagnostics:
+// lets a caller state how many of its kernels a step or a captured graph
+// contains).  Incremented by every launch site through count_launch().
+int64_t& launch_counter();
+inline void count_launch(int n = 1) { launch_counter() += n; }
+
 inline int32_t launch_status() {
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? LLMYB_OK : static_cast<int32_t>(e);

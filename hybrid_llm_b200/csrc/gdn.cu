@@ -748,8 +748,10 @@ int32_t launch_prefill(const GdnIO& io, int B, int T, int H, void* scratch, floa
     attrs = true;
   }
   gdn_chunk_prep_kernel<KD, VD><<<B * H * nC, 128, kPrepSmem, s>>>(io, B, T, H, po);
+  count_launch();
   gdn_chunk_scan_kernel<KD, VD, VC><<<B * H * (VD / VC), 128, kScanSmem, s>>>(io, B, T, H, po,
                                                                              state, out, so);
+  count_launch();
   return launch_status();
 }
 
@@ -768,6 +770,7 @@ LLMYB_API int32_t llmyb_gdn_activate(void* proj, int64_t n_tokens, int32_t width
   gdn_activate_kernel<<<static_cast<int>(ceil_div(warps * 32, 256)), 256, 0,
                         static_cast<cudaStream_t>(stream)>>>(
       static_cast<__nv_bfloat16*>(proj), n_tokens, width, heads, key_dim, value_dim, beta_bias);
+  count_launch();
   return launch_status();
 }
 
@@ -792,6 +795,7 @@ LLMYB_API int32_t llmyb_gdn_step(const void* q, int64_t q_stride, const void* k,
     gdn_step_kernel<64><<<grid, 128, 0, s>>>(io, heads, value_dim, state, o, out_stride);
   else
     gdn_step_kernel<128><<<grid, 128, 0, s>>>(io, heads, value_dim, state, o, out_stride);
+  count_launch();
   return launch_status();
 }
 
@@ -850,9 +854,11 @@ LLMYB_API int32_t llmyb_gdn_conv_gate(const void* x, const void* y_proj, const f
       static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(y_proj), conv_w,
       static_cast<__nv_bfloat16*>(history), reset, batch, seq, d_model,
       static_cast<__nv_bfloat16*>(out), static_cast<__nv_bfloat16*>(residual));
+  count_launch();
   if (roll_history) {
     gdn_conv_roll_kernel<<<batch, 256, 3 * d_model * sizeof(__nv_bfloat16), s>>>(
         static_cast<const __nv_bfloat16*>(x), static_cast<__nv_bfloat16*>(history), seq, d_model);
+    count_launch();
   }
   return launch_status();
 }

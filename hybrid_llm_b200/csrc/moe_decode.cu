@@ -1,0 +1,245 @@
+// Routed SwiGLU experts for small token counts (decode): weight streaming.
+//
+// Same math as moe_gemm.cu (reference model/layers/moe.py:68-81), for the
+// regime where each expert sees a handful of rows (batch-1 decode: one row
+// for each of the top-k experts; batch-64 decode: ~N*k/E rows).  There the
+// cost is reading the routed experts' weights once, so the kernels stream
+// every weight row exactly once with 16-byte loads and keep the few token
+// rows in shared memory:
+//   up  : CTA = (expert, 8 features); warp = one feature; the gate and up
+//         rows of that feature are held in registers while the expert's rows
+//         (16 at a time, bf16 in shared memory) are dotted against them:
+//         h[pos, f] = silu(x.w_gate_f) * (x.w_up_f)
+//   down: CTA = (expert, 8 output columns); warp = one column of W2:
+//         y[pos, d] = p[pos] * (h[pos, :] . w2_d)
+//   combine (moe_gemm.cu): out[t] = sum_s y[route_pos[t, s]]
+// Experts without routed rows exit immediately, so an inactive expert costs
+// no weight traffic.  Grid size scales with E x features and needs no
+// device-to-host read of the routing result.
+#include "common.cuh"
+
+#include <algorithm>
+
+namespace llmyb {
+namespace {
+
+constexpr int kTok = 16;        // token rows staged per pass
+constexpr int kWarps = 8;       // features (up) or columns (down) per CTA
+constexpr int kMaxChunk = 8;    // 16-byte chunks per lane and row: D, F <= 2048
+
+__global__ void __launch_bounds__(256) moe_decode_up_kernel(
+    const __nv_bfloat16* __restrict__ x, const int* __restrict__ perm_token,
+    const int* __restrict__ expert_offsets, const __nv_bfloat16* __restrict__ w13, int D, int F,
+    __nv_bfloat16* __restrict__ h_perm) {
+  extern __shared__ __nv_bfloat16 s_x[];  // [kTok][D]
+  const int fblocks = F / kWarps;
+  const int e = blockIdx.x / fblocks;
+  const int r0 = __ldg(expert_offsets + e), r1 = __ldg(expert_offsets + e + 1);
+  if (r1 <= r0) return;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int f = (blockIdx.x - e * fblocks) * kWarps + warp;
+  const int nch = D / 8;
+  // interleaved stack: feature f of tile j = f/128 -> gate row 256j + f%128, up row +128
+  const int64_t grow = static_cast<int64_t>(e) * 2 * F + (f / 128) * 256 + (f % 128);
+  const uint4* wg = reinterpret_cast<const uint4*>(w13 + grow * D);
+  const uint4* wu = reinterpret_cast<const uint4*>(w13 + (grow + 128) * D);
+  uint4 g4[kMaxChunk], u4[kMaxChunk];
+#pragma unroll
+  for (int i = 0; i < kMaxChunk; ++i) {
+    const int c = lane + 32 * i;
+    if (c < nch) {
+      g4[i] = __ldg(wg + c);
+      u4[i] = __ldg(wu + c);
+    }
+  }
+  for (int base = r0; base < r1; base += kTok) {
+    const int nt = min(kTok, r1 - base);
+    __syncthreads();
+    for (int i = threadIdx.x; i < nt * nch; i += blockDim.x) {
+      const int t = i / nch, c = i - t * nch;
+      const int tok = __ldg(perm_token + base + t);
+      reinterpret_cast<uint4*>(s_x + t * D)[c] =
+          __ldg(reinterpret_cast<const uint4*>(x + static_cast<int64_t>(tok) * D) + c);
+    }
+    __syncthreads();
+    for (int t = 0; t < nt; ++t) {
+      float ga = 0.f, ua = 0.f;
+      const uint4* xr = reinterpret_cast<const uint4*>(s_x + t * D);
+#pragma unroll
+      for (int i = 0; i < kMaxChunk; ++i) {
+        const int c = lane + 32 * i;
+        if (c < nch) {
+          const uint4 xv = xr[c];
+          const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
+          const uint32_t gw[4] = {g4[i].x, g4[i].y, g4[i].z, g4[i].w};
+          const uint32_t uw[4] = {u4[i].x, u4[i].y, u4[i].z, u4[i].w};
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const float2 xf = unpack_bf16x2(xw[k]);
+            const float2 gf = unpack_bf16x2(gw[k]);
+            const float2 uf = unpack_bf16x2(uw[k]);
+            ga += xf.x * gf.x + xf.y * gf.y;
+            ua += xf.x * uf.x + xf.y * uf.y;
+          }
+        }
+      }
+      ga = warp_sum(ga);
+      ua = warp_sum(ua);
+      if (lane == 0) h_perm[static_cast<int64_t>(base + t) * F + f] = f2bf(silu_mul(ga, ua));
+    }
+  }
+}
+
+__global__ void __launch_bounds__(256) moe_decode_down_kernel(
+    const __nv_bfloat16* __restrict__ h_perm, const float* __restrict__ perm_prob,
+    const int* __restrict__ expert_offsets, const __nv_bfloat16* __restrict__ w2, int D, int F,
+    __nv_bfloat16* __restrict__ y_perm) {
+  extern __shared__ __nv_bfloat16 s_h[];  // [kTok][F]
+  const int dblocks = D / kWarps;
+  const int e = blockIdx.x / dblocks;
+  const int r0 = __ldg(expert_offsets + e), r1 = __ldg(expert_offsets + e + 1);
+  if (r1 <= r0) return;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int d = (blockIdx.x - e * dblocks) * kWarps + warp;
+  const int nch = F / 8;
+  const uint4* wr = reinterpret_cast<const uint4*>(w2 + (static_cast<int64_t>(e) * D + d) * F);
+  uint4 w4[kMaxChunk];
+#pragma unroll
+  for (int i = 0; i < kMaxChunk; ++i) {
+    const int c = lane + 32 * i;
+    if (c < nch) w4[i] = __ldg(wr + c);
+  }
+  for (int base = r0; base < r1; base += kTok) {
+    const int nt = min(kTok, r1 - base);
+    __syncthreads();
+    for (int i = threadIdx.x; i < nt * nch; i += blockDim.x) {
+      const int t = i / nch, c = i - t * nch;
+      reinterpret_cast<uint4*>(s_h + t * F)[c] =
+          __ldg(reinterpret_cast<const uint4*>(h_perm + static_cast<int64_t>(base + t) * F) + c);
+    }
+    __syncthreads();
+    for (int t = 0; t < nt; ++t) {
+      float acc = 0.f;
+      const uint4* hr = reinterpret_cast<const uint4*>(s_h + t * F);
+#pragma unroll
+      for (int i = 0; i < kMaxChunk; ++i) {
+        const int c = lane + 32 * i;
+        if (c < nch) {
+          const uint4 hv = hr[c];
+          const uint32_t hw[4] = {hv.x, hv.y, hv.z, hv.w};
+          const uint32_t ww[4] = {w4[i].x, w4[i].y, w4[i].z, w4[i].w};
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const float2 hf = unpack_bf16x2(hw[k]);
+            const float2 wf = unpack_bf16x2(ww[k]);
+            acc += hf.x * wf.x + hf.y * wf.y;
+          }
+        }
+      }
+      acc = warp_sum(acc);
+      if (lane == 0) {
+        const int pos = base + t;
+        y_perm[static_cast<int64_t>(pos) * D + d] = f2bf(acc * __ldg(perm_prob + pos));
+      }
+    }
+  }
+}
+
+// out[t] = sum_s y_perm[route_pos[t*k + s]]   (deterministic fp32 sum)
+__global__ void moe_decode_combine_kernel(const __nv_bfloat16* __restrict__ y_perm,
+                                          const int* __restrict__ route_pos, int N, int k, int D,
+                                          __nv_bfloat16* __restrict__ out) {
+  const int vec = D / 8;
+  const int64_t total = static_cast<int64_t>(N) * vec;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t t = i / vec;
+    const int c = static_cast<int>(i - t * vec);
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int s = 0; s < k; ++s) {
+      const int pos = __ldg(route_pos + t * k + s);
+      const uint4 v = __ldg(reinterpret_cast<const uint4*>(y_perm + static_cast<int64_t>(pos) * D) + c);
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = unpack_bf16x2(w[j]);
+        acc[2 * j] += f.x;
+        acc[2 * j + 1] += f.y;
+      }
+    }
+    uint4 o;
+    o.x = pack_bf16x2(acc[0], acc[1]);
+    o.y = pack_bf16x2(acc[2], acc[3]);
+    o.z = pack_bf16x2(acc[4], acc[5]);
+    o.w = pack_bf16x2(acc[6], acc[7]);
+    reinterpret_cast<uint4*>(out + t * D)[c] = o;
+  }
+}
+
+}  // namespace
+}  // namespace llmyb
+
+using namespace llmyb;
+
+LLMYB_API int64_t llmyb_moe_decode_scratch_bytes(int32_t n_tokens, int32_t top_k, int32_t d_model,
+                                                 int32_t ffn) {
+  if (n_tokens < 0 || top_k <= 0 || d_model <= 0 || ffn <= 0) return -1;
+  const int64_t rows = static_cast<int64_t>(n_tokens) * top_k;
+  auto al = [](int64_t b) { return (b + 255) / 256 * 256; };
+  return al(rows * ffn * 2) + al(rows * d_model * 2);
+}
+
+// Weight-streaming variant of llmyb_moe_grouped_swiglu for small token counts
+// (same inputs, same plan, w13 from llmyb_moe_pack_w13).  D, F multiples of
+// 128 and at most 2048.
+LLMYB_API int32_t llmyb_moe_decode_swiglu(const void* x, int32_t n_tokens, int32_t d_model,
+                                          int32_t top_k, const int32_t* perm_token,
+                                          const float* perm_prob, const int32_t* route_pos,
+                                          const int32_t* expert_offsets, int32_t n_experts,
+                                          const void* w13, const void* w2, int32_t ffn,
+                                          void* scratch, void* out, void* stream) {
+  if (n_tokens < 0 || d_model <= 0 || top_k <= 0 || n_experts <= 0 || ffn <= 0) return LLMYB_EINVAL;
+  if (n_tokens == 0) return LLMYB_OK;
+  if (!x || !perm_token || !perm_prob || !route_pos || !expert_offsets || !w13 || !w2 ||
+      !scratch || !out)
+    return LLMYB_EINVAL;
+  if (d_model % 128 != 0 || ffn % 128 != 0 || d_model > 8 * 32 * kMaxChunk ||
+      ffn > 8 * 32 * kMaxChunk)
+    return LLMYB_EUNSUPPORTED;
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out) |
+       reinterpret_cast<uintptr_t>(w13) | reinterpret_cast<uintptr_t>(w2) |
+       reinterpret_cast<uintptr_t>(scratch)) & 15u)
+    return LLMYB_EUNSUPPORTED;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t rows = static_cast<int64_t>(n_tokens) * top_k;
+  auto al = [](int64_t b) { return (b + 255) / 256 * 256; };
+  auto* h = static_cast<__nv_bfloat16*>(scratch);
+  auto* y = reinterpret_cast<__nv_bfloat16*>(static_cast<uint8_t*>(scratch) + al(rows * ffn * 2));
+  const int up_smem = kTok * d_model * 2, down_smem = kTok * ffn * 2;
+  static int up_attr = 0, down_attr = 0;
+  if (up_smem > 48 * 1024 && up_smem > up_attr) {
+    cudaError_t e = cudaFuncSetAttribute(moe_decode_up_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, up_smem);
+    if (e != cudaSuccess) return e;
+    up_attr = up_smem;
+  }
+  if (down_smem > 48 * 1024 && down_smem > down_attr) {
+    cudaError_t e = cudaFuncSetAttribute(moe_decode_down_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, down_smem);
+    if (e != cudaSuccess) return e;
+    down_attr = down_smem;
+  }
+  moe_decode_up_kernel<<<n_experts * (ffn / kWarps), 256, up_smem, s>>>(
+      static_cast<const __nv_bfloat16*>(x), perm_token, expert_offsets,
+      static_cast<const __nv_bfloat16*>(w13), d_model, ffn, h);
+  count_launch();
+  moe_decode_down_kernel<<<n_experts * (d_model / kWarps), 256, down_smem, s>>>(
+      h, perm_prob, expert_offsets, static_cast<const __nv_bfloat16*>(w2), d_model, ffn, y);
+  count_launch();
+  const int64_t work = static_cast<int64_t>(n_tokens) * (d_model / 8);
+  moe_decode_combine_kernel<<<static_cast<int>(std::min<int64_t>(ceil_div(work, 256), 1184)), 256,
+                              0, s>>>(y, route_pos, n_tokens, top_k, d_model,
+                                      static_cast<__nv_bfloat16*>(out));
+  count_launch();
+  return launch_status();
+}

@@ -364,6 +364,7 @@ LLMYB_API int32_t llmyb_moe_pack_w13(const __nv_bfloat16* w_gate, const __nv_bfl
   const int64_t work = static_cast<int64_t>(n_experts) * 2 * ffn * (d_model / 8);
   pack_w13_kernel<<<grid_for(work, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
       w_gate, w_up, n_experts, ffn, d_model, w13);
+  count_launch();
   return launch_status();
 }
 
@@ -411,6 +412,7 @@ LLMYB_API int32_t llmyb_moe_grouped_swiglu(
 
   gather_rows_kernel<<<grid_for(rows * (d_model / 8), 256), 256, 0, s>>>(x, perm_token, rows,
                                                                          d_model, x_perm);
+  count_launch();
 
   CUtensorMap ma1, mb1, ma2, mb2;
   if (!make_bf16_2d_map(&ma1, x_perm, rows, d_model, d_model, BM, BK) ||
@@ -428,10 +430,13 @@ LLMYB_API int32_t llmyb_moe_grouped_swiglu(
   moe_gemm_kernel<kSwiGLU><<<grid1, 256, GEMM_SMEM, s>>>(ma1, mb1, expert_offsets, tile_offsets,
                                                           n_experts, d_model, 2 * ffn, h_perm,
                                                           ffn, nullptr, dev_status);
+  count_launch();
   moe_gemm_kernel<kScale><<<grid2, 256, GEMM_SMEM, s>>>(ma2, mb2, expert_offsets, tile_offsets,
                                                          n_experts, ffn, d_model, y_perm,
                                                          d_model, perm_prob, dev_status);
+  count_launch();
   combine_rows_kernel<<<grid_for(static_cast<int64_t>(n_tokens) * (d_model / 8), 256), 256, 0,
                         s>>>(y_perm, route_pos, n_tokens, top_k, d_model, out);
+  count_launch();
   return launch_status();
 }

@@ -86,7 +86,17 @@ __global__ void __launch_bounds__(256) rmsnorm_bf16_kernel(const __nv_bfloat16* 
 }  // namespace
 }  // namespace llmyb
 
+namespace llmyb {
+int64_t& launch_counter() {
+  static int64_t n = 0;
+  return n;
+}
+}  // namespace llmyb
+
 using namespace llmyb;
+
+// Number of kernel launches this library has issued since it was loaded.
+LLMYB_API int64_t llmyb_launch_count(void) { return launch_counter(); }
 
 LLMYB_API int32_t llmyb_embed(const int64_t* ids, int64_t n_tokens, const void* table,
                               int64_t vocab, int32_t d_model, const float* stream_seed,
@@ -96,6 +106,7 @@ LLMYB_API int32_t llmyb_embed(const int64_t* ids, int64_t n_tokens, const void* 
   embed_kernel<<<static_cast<unsigned>(n_tokens), 256, 0, static_cast<cudaStream_t>(stream)>>>(
       ids, static_cast<const __nv_bfloat16*>(table), stream_seed, d_model, vocab, streams,
       dev_status);
+  count_launch();
   return launch_status();
 }
 
@@ -109,6 +120,7 @@ LLMYB_API int32_t llmyb_add_rmsnorm(float* streams, const void* delta, int64_t n
                        static_cast<cudaStream_t>(stream)>>>(
       streams, static_cast<const __nv_bfloat16*>(delta), d_model, weight, eps, normalize,
       static_cast<__nv_bfloat16*>(out_bf16), out_f32);
+  count_launch();
   return launch_status();
 }
 
@@ -119,5 +131,6 @@ LLMYB_API int32_t llmyb_rmsnorm_bf16(const void* x, int64_t n_tokens, int32_t d_
   rmsnorm_bf16_kernel<<<static_cast<unsigned>(n_tokens), 256, 0,
                         static_cast<cudaStream_t>(stream)>>>(
       static_cast<const __nv_bfloat16*>(x), d_model, weight, eps, static_cast<__nv_bfloat16*>(out));
+  count_launch();
   return launch_status();
 }

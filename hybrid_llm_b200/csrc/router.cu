@@ -356,6 +356,7 @@ LLMYB_API int32_t llmyb_router_topk(const float* logits, const float* bias, int3
   router_topk_kernel<<<static_cast<int>(ceil_div(n_tokens, 8)), 256, 0,
                        static_cast<cudaStream_t>(stream)>>>(logits, bias, n_tokens, n_experts,
                                                             top_k, topk_idx, topk_prob);
+  count_launch();
   return launch_status();
 }
 
@@ -371,8 +372,10 @@ int32_t plan_tail(const int64_t* topk_idx, const float* topk_prob, int N, int E,
                   int* route_pos, int64_t* sort_order, int* hist, cudaStream_t s) {
   const int nchunks = static_cast<int>(ceil_div(N, kChunk));
   plan_scan_kernel<<<1, 1024, 0, s>>>(hist, nchunks, E, tile_m, counts, offsets, tile_offsets);
+  count_launch();
   plan_scatter_kernel<<<nchunks, 256, 8 * E * sizeof(int), s>>>(
       topk_idx, topk_prob, N, E, k, hist, perm_token, perm_prob, route_pos, sort_order);
+  count_launch();
   return launch_status();
 }
 
@@ -405,6 +408,7 @@ LLMYB_API int32_t llmyb_moe_plan(const int64_t* topk_idx, const float* topk_prob
   int* hist = static_cast<int*>(scratch);
   plan_hist_kernel<<<nchunks, 256, n_experts * sizeof(int), s>>>(topk_idx, n_tokens, n_experts,
                                                                  top_k, hist, dev_status);
+  count_launch();
   return plan_tail(topk_idx, topk_prob, n_tokens, n_experts, top_k, tile_m, expert_counts,
                    expert_offsets, tile_offsets, perm_token, perm_prob, route_pos, sort_order,
                    hist, s);
@@ -430,6 +434,7 @@ LLMYB_API int32_t llmyb_route(const float* logits, const float* bias, int32_t n_
                                           topk_idx, topk_prob, expert_counts, expert_offsets,
                                           tile_offsets, perm_token, perm_prob, route_pos,
                                           sort_order);
+    count_launch();
     return launch_status();
   }
   if (!scratch) return LLMYB_EINVAL;
@@ -437,8 +442,10 @@ LLMYB_API int32_t llmyb_route(const float* logits, const float* bias, int32_t n_
   int* hist = static_cast<int*>(scratch);
   router_topk_kernel<<<static_cast<int>(ceil_div(n_tokens, 8)), 256, 0, s>>>(
       logits, bias, n_tokens, n_experts, top_k, topk_idx, topk_prob);
+  count_launch();
   plan_hist_kernel<<<nchunks, 256, n_experts * sizeof(int), s>>>(topk_idx, n_tokens, n_experts,
                                                                  top_k, hist, nullptr);
+  count_launch();
   return plan_tail(topk_idx, topk_prob, n_tokens, n_experts, top_k, tile_m, expert_counts,
                    expert_offsets, tile_offsets, perm_token, perm_prob, route_pos, sort_order,
                    hist, s);

@@ -392,5 +392,6 @@ LLMYB_API int32_t llmyb_sample(const float* logits, int64_t ld, int32_t batch, i
     if (e != cudaSuccess) return e;
   }
   sample_kernel<<<batch, kThreads, dyn, static_cast<cudaStream_t>(stream)>>>(a);
+  count_launch();
   return launch_status();
 }

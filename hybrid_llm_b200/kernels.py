@@ -64,6 +64,11 @@ def check_device_status(device: torch.device | None = None) -> None:
         _native.check(code, "device-side status")
 
 
+def launch_count() -> int:
+    """Kernel launches issued by the native library so far (host-side count)."""
+    return int(_native.lib().llmyb_launch_count())
+
+
 @dataclass
 class RoutePlan:
     """Top-k routes and the expert-grouped dispatch order (all on device)."""
@@ -162,8 +167,13 @@ def pack_w13(w_gate: torch.Tensor, w_up: torch.Tensor) -> torch.Tensor:
 
 
 def moe_grouped(x: torch.Tensor, plan: RoutePlan, w13: torch.Tensor, w2: torch.Tensor,
-                out: torch.Tensor | None = None, scratch: torch.Tensor | None = None) -> torch.Tensor:
-    """Routed SwiGLU experts: out[t] = sum_s p_ts * down(silu(gate x_t) * up x_t)."""
+                out: torch.Tensor | None = None, scratch: torch.Tensor | None = None,
+                path: str = "auto") -> torch.Tensor:
+    """Routed SwiGLU experts: out[t] = sum_s p_ts * down(silu(gate x_t) * up x_t).
+
+    path "grouped" = tcgen05 grouped GEMM over 128-row expert tiles,
+    "decode" = weight-streaming kernels for a few rows per expert, "auto"
+    picks "decode" when the average expert sees fewer than 32 rows."""
     _require_cuda(x, w13, w2)
     if x.dtype != torch.bfloat16:
         raise ValueError("moe_grouped computes in bf16")
@@ -176,13 +186,25 @@ def moe_grouped(x: torch.Tensor, plan: RoutePlan, w13: torch.Tensor, w2: torch.T
         raise ValueError("expert weight shapes do not match the activations")
     if out is None:
         out = torch.empty(n, d, dtype=torch.bfloat16, device=x.device)
-    need = int(_native.lib().llmyb_moe_grouped_scratch_bytes(n, k, d, f))
+    if path == "auto":
+        path = "decode" if (n * k < 32 * e and d <= 2048 and f <= 2048
+                            and d % 128 == 0 and f % 128 == 0) else "grouped"
+    lib = _native.lib()
+    if path == "decode":
+        need = int(lib.llmyb_moe_decode_scratch_bytes(n, k, d, f))
+    else:
+        need = int(lib.llmyb_moe_grouped_scratch_bytes(n, k, d, f))
     if scratch is None or scratch.numel() < need:
         scratch = torch.empty(max(need, 16), dtype=torch.uint8, device=x.device)
-    _native.call("llmyb_moe_grouped_swiglu", _ptr(x), n, d, k, _ptr(plan.perm_token),
-                 _ptr(plan.perm_prob), _ptr(plan.route_pos), _ptr(plan.offsets),
-                 _ptr(plan.tile_offsets), e, _ptr(w13), _ptr(w2), f, _ptr(scratch), _ptr(out),
-                 _ptr(device_status(x.device)), _stream())
+    if path == "decode":
+        _native.call("llmyb_moe_decode_swiglu", _ptr(x), n, d, k, _ptr(plan.perm_token),
+                     _ptr(plan.perm_prob), _ptr(plan.route_pos), _ptr(plan.offsets), e, _ptr(w13),
+                     _ptr(w2), f, _ptr(scratch), _ptr(out), _stream())
+    else:
+        _native.call("llmyb_moe_grouped_swiglu", _ptr(x), n, d, k, _ptr(plan.perm_token),
+                     _ptr(plan.perm_prob), _ptr(plan.route_pos), _ptr(plan.offsets),
+                     _ptr(plan.tile_offsets), e, _ptr(w13), _ptr(w2), f, _ptr(scratch), _ptr(out),
+                     _ptr(device_status(x.device)), _stream())
     return out
 
 

@@ -88,6 +88,20 @@ int32_t llmyb_moe_grouped_swiglu(const void* x, int32_t n_tokens, int32_t d_mode
                                  const void* w2, int32_t ffn, void* scratch, void* out,
                                  int32_t* dev_status, void* stream);
 
+/* Scratch bytes needed by llmyb_moe_decode_swiglu. */
+int64_t llmyb_moe_decode_scratch_bytes(int32_t n_tokens, int32_t top_k, int32_t d_model,
+                                       int32_t ffn);
+
+/* Same contract as llmyb_moe_grouped_swiglu for small token counts (decode):
+ * streams every routed expert's weights once (CUDA-core dot products, token
+ * rows staged in shared memory); experts with no routed rows read nothing.
+ * D, F multiples of 128, at most 2048. */
+int32_t llmyb_moe_decode_swiglu(const void* x, int32_t n_tokens, int32_t d_model, int32_t top_k,
+                                const int32_t* perm_token, const float* perm_prob,
+                                const int32_t* route_pos, const int32_t* expert_offsets,
+                                int32_t n_experts, const void* w13, const void* w2, int32_t ffn,
+                                void* scratch, void* out, void* stream);
+
 /* ------------------------------------------------------ gated delta rule
  * Replaces GatedDeltaNet's recurrence (model/layers/gated_deltanet.py:140-149
  * and the seams _triton_gdn_scan/_triton_gdn_step at :179-235), the Triton
@@ -174,6 +188,12 @@ int32_t llmyb_csa_local_decode(const void* q, int64_t q_stride, const void* knew
                                void* kcache, void* vcache, const int32_t* positions,
                                int32_t batch, int32_t heads, int32_t head_dim, int32_t d_model,
                                int32_t window, void* out, int64_t out_stride, void* stream);
+
+/* ------------------------------------------------------------- diagnostics
+ * Number of kernel launches this library has issued since it was loaded
+ * (host-side count; a captured CUDA graph replays the launches counted while
+ * it was captured).  No counterpart in the reference. */
+int64_t llmyb_launch_count(void);
 
 /* --------------------------------------------------------- residual stream
  * PhysicalBlock's residual glue with mHC disabled (model/model.py:119-126,

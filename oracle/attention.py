@@ -12,6 +12,12 @@ from __future__ import annotations
 import numpy as np
 
 
+def _fp(x):
+    """float32 inputs stay float32 (timed CPU baseline); everything else is float64."""
+    x = np.asarray(x)
+    return x if x.dtype == np.float32 else x.astype(np.float64)
+
+
 def _softmax(x, axis=-1):
     m = np.max(x, axis=axis, keepdims=True)
     e = np.exp(x - m)
@@ -26,7 +32,7 @@ def band_mask(t_len: int, window: int) -> np.ndarray:
 
 def banded_attention(q, k, v, window: int, scale: float | None = None) -> np.ndarray:
     """q,k [B,T,H,D]; v [B,T,H or 1,Dv] -> [B,T,H,Dv] (sample_standalone.py:70-85)."""
-    q, k, v = (np.asarray(a, dtype=np.float64) for a in (q, k, v))
+    q, k, v = (_fp(a) for a in (q, k, v))
     b_, t_, h_, d_ = q.shape
     if v.shape[2] == 1 and h_ > 1:
         v = np.broadcast_to(v, (b_, t_, h_, v.shape[-1]))
@@ -43,7 +49,7 @@ def csa_local(q, k, v_shared, window: int) -> np.ndarray:
     window = max(1, min(local_window, T)) as in csa.py:42; probabilities are
     averaged over heads before the shared value product (csa.py:74-75).
     """
-    q, k, v = (np.asarray(a, dtype=np.float64) for a in (q, k, v_shared))
+    q, k, v = (_fp(a) for a in (q, k, v_shared))
     b_, t_, h_, d_ = q.shape
     w = max(1, min(window, t_))
     s = np.einsum("bthd,bshd->bhts", q, k) / np.sqrt(d_)
@@ -56,7 +62,7 @@ def csa_local_step(q, k_win, v_win, valid=None) -> np.ndarray:
     """CSA decode (csa.py:172-206): q [B,H,Dh]; k_win [B,L,H,Dh]; v_win [B,L,D];
     valid [B,L] bool (history validity).  The caller passes the last
     min(local_window, L) positions, current token last."""
-    q, k, v = (np.asarray(a, dtype=np.float64) for a in (q, k_win, v_win))
+    q, k, v = (_fp(a) for a in (q, k_win, v_win))
     s = np.einsum("bhd,blhd->bhl", q, k) / np.sqrt(q.shape[-1])
     if valid is not None:
         s = np.where(np.asarray(valid)[:, None, :], s, -np.inf)
@@ -67,7 +73,7 @@ def csa_local_step(q, k_win, v_win, valid=None) -> np.ndarray:
 def csa_layer(hidden, p: dict, n_heads: int, window: int) -> np.ndarray:
     """CompressedSelectiveAttention.forward with the remote branch disabled
     (temporal_compression beyond the sequence): out(local_out(local))."""
-    x = np.asarray(hidden, dtype=np.float64)
+    x = _fp(hidden)
     b_, t_, _ = x.shape
     q = (x @ p["query"].T).reshape(b_, t_, n_heads, -1)
     k = (x @ p["key"].T).reshape(b_, t_, n_heads, -1)

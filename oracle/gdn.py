@@ -14,13 +14,19 @@ from __future__ import annotations
 import numpy as np
 
 
+def _fp(x):
+    """float32 inputs stay float32 (timed CPU baseline); everything else is float64."""
+    x = np.asarray(x)
+    return x if x.dtype == np.float32 else x.astype(np.float64)
+
+
 def sigmoid(x):
-    return 1.0 / (1.0 + np.exp(-np.asarray(x, dtype=np.float64)))
+    return 1.0 / (1.0 + np.exp(-_fp(x)))
 
 
 def l2norm_heads(x: np.ndarray) -> np.ndarray:
     """x * rsqrt(max(sum(x^2), 1e-12)) over the last dim (gated_deltanet.py:128-129)."""
-    x = np.asarray(x, dtype=np.float64)
+    x = _fp(x)
     return x / np.sqrt(np.maximum((x * x).sum(-1, keepdims=True), 1e-12))
 
 
@@ -32,15 +38,15 @@ def gdn_recurrent(q, k, v, beta, gate, reset, alpha, state):
     sigmoid(decay_logit)) or per token [B,T,H]; state [B,H,K,V].
     Returns out [B,T,H,V] (= (q^T S_t) * gate_t) and the final state, float64.
     """
-    q, k, v, gate = (np.asarray(a, dtype=np.float64) for a in (q, k, v, gate))
-    beta = np.asarray(beta, dtype=np.float64)
+    q, k, v, gate = (_fp(a) for a in (q, k, v, gate))
+    beta = _fp(beta)
     if beta.ndim == 4:
         beta = beta[..., 0]
     b_, t_, h_, _ = q.shape
-    alpha = np.asarray(alpha, dtype=np.float64)
+    alpha = _fp(alpha)
     alpha = np.broadcast_to(alpha if alpha.ndim == 3 else alpha[None, None, :], (b_, t_, h_))
-    s = np.array(state, dtype=np.float64, copy=True)
-    out = np.empty(v.shape, dtype=np.float64)
+    s = np.array(_fp(state), copy=True)
+    out = np.empty(v.shape, dtype=v.dtype)
     for t in range(t_):
         if reset is not None:
             s[np.asarray(reset)[:, t]] = 0.0
@@ -66,16 +72,16 @@ def gdn_chunked(q, k, v, beta, gate, reset, log_alpha, state, chunk: int = 64):
     A reset at token r drops S_0 and every earlier token for t >= r (segment
     masks).  log_alpha is [H] or [B,T,H]; everything in float64.
     """
-    q, k, v, gate = (np.asarray(a, dtype=np.float64) for a in (q, k, v, gate))
-    beta = np.asarray(beta, dtype=np.float64)
+    q, k, v, gate = (_fp(a) for a in (q, k, v, gate))
+    beta = _fp(beta)
     if beta.ndim == 4:
         beta = beta[..., 0]
     b_, t_, h_, kd = q.shape
-    la = np.asarray(log_alpha, dtype=np.float64)
+    la = _fp(log_alpha)
     la = np.broadcast_to(la if la.ndim == 3 else la[None, None, :], (b_, t_, h_))
     rs = np.zeros((b_, t_), dtype=bool) if reset is None else np.asarray(reset, dtype=bool)
-    s = np.array(state, dtype=np.float64, copy=True)
-    out = np.empty(v.shape, dtype=np.float64)
+    s = np.array(_fp(state), copy=True)
+    out = np.empty(v.shape, dtype=v.dtype)
     for c0 in range(0, t_, chunk):
         c1 = min(t_, c0 + chunk)
         n = c1 - c0
@@ -112,12 +118,12 @@ def causal_conv(hidden, weight, reset=None, history=None):
     With history [B,K-1,D] (decode, :257-268) the taps read the history
     (zeroed for rows whose reset flag is set).
     """
-    x = np.asarray(hidden, dtype=np.float64)
-    w = np.asarray(weight, dtype=np.float64).reshape(x.shape[-1], -1)
+    x = _fp(hidden)
+    w = _fp(weight).reshape(x.shape[-1], -1)
     kk = w.shape[1]
     b_, t_, d_ = x.shape
     if history is not None:
-        hist = np.asarray(history, dtype=np.float64)
+        hist = _fp(history)
         if reset is not None:
             hist = np.where(np.asarray(reset)[:, 0][:, None, None], 0.0, hist)
         full = np.concatenate([hist[:, -(kk - 1):], x], axis=1)
@@ -145,7 +151,7 @@ def gdn_layer(hidden, p: dict, state, reset=None, conv_history=None):
     conv [D,1,4], decay_logit [H]; heads/key_dim/value_dim from shapes.
     Returns (out [B,T,D], final state [B,H,K,V]).
     """
-    x = np.asarray(hidden, dtype=np.float64)
+    x = _fp(hidden)
     b_, t_, _ = x.shape
     h_ = p["decay_logit"].shape[0]
     q = (x @ p["q_proj"].T).reshape(b_, t_, h_, -1)

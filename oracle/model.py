@@ -10,22 +10,31 @@ from __future__ import annotations
 
 import numpy as np
 
+
+def _fp(x):
+    """float32 inputs stay float32 (timed CPU baseline); everything else is float64."""
+    x = np.asarray(x)
+    return x if x.dtype == np.float32 else x.astype(np.float64)
+
 from . import attention, gdn, routing
 
 
 def rmsnorm(x, w, eps=1e-6):
     """norms.py:13-16."""
-    x = np.asarray(x, dtype=np.float64)
+    x = _fp(x)
     r = 1.0 / np.sqrt((x * x).mean(-1, keepdims=True) + eps)
-    return x * r * (1.0 if w is None else np.asarray(w, dtype=np.float64))
+    return x * r * (1.0 if w is None else _fp(w))
 
 
 class OracleModel:
-    def __init__(self, cfg, sd):
-        """cfg: hybrid_llm_b200.config.HybridConfig-like; sd: name -> array-like."""
+    def __init__(self, cfg, sd, dtype=np.float64):
+        """cfg: hybrid_llm_b200.config.HybridConfig-like; sd: name -> array-like.
+        dtype float32 is used for the timed CPU baseline, float64 for parity."""
         self.cfg = cfg
+        self.dtype = dtype
         self.p = {k: np.asarray(v.detach().cpu().numpy() if hasattr(v, "detach") else v,
-                                dtype=np.float64) for k, v in sd.items()}
+                                dtype=dtype) for k, v in sd.items()}
+        self._experts: dict[int, tuple] = {}
 
     def _gdn_params(self, j):
         p = f"recurrent_core.{j}.mixer."
@@ -47,11 +56,14 @@ class OracleModel:
         r = rmsnorm(flat, self.p[p + "router.norm.weight"], c.rms_eps)
         logits = r @ self.p[p + "router.logits.weight"].T
         idx, prob = routing.router_topk(logits.astype(np.float32), c.moe_top_k)
-        e = c.moe_experts
-        wg = np.stack([self.p[f"{p}experts.{x}.gate_proj.weight"] for x in range(e)])
-        wu = np.stack([self.p[f"{p}experts.{x}.up_proj.weight"] for x in range(e)])
-        wd = np.stack([self.p[f"{p}experts.{x}.down_proj.weight"] for x in range(e)])
-        return routing.moe_forward(flat, idx, prob, wg, wu, wd).reshape(*lead, -1), logits
+        if j not in self._experts:
+            e = c.moe_experts
+            self._experts[j] = tuple(
+                np.stack([self.p[f"{p}experts.{x}.{n}_proj.weight"] for x in range(e)])
+                for n in ("gate", "up", "down"))
+        wg, wu, wd = self._experts[j]
+        out = routing.moe_forward(flat, idx, prob, wg, wu, wd, dtype=self.dtype)
+        return out.reshape(*lead, -1), logits
 
     def new_state(self, batch):
         c = self.cfg
@@ -59,14 +71,15 @@ class OracleModel:
         for i in range(c.num_loops):
             for j in range(c.n_blocks):
                 if c.block_kind(j) == "gdn":
-                    st["gdn"][(i, j)] = np.zeros((batch, c.gdn_heads, c.gdn_key_dim, c.gdn_value_dim))
+                    st["gdn"][(i, j)] = np.zeros((batch, c.gdn_heads, c.gdn_key_dim, c.gdn_value_dim),
+                                                 dtype=self.dtype)
         return st
 
     def run_stack(self, streams, state, loops=None, router_logits=None):
         """Recurrent core over streams [B,T,D] (model/model.py:618-687)."""
         c = self.cfg
         loops = c.num_loops if loops is None else loops
-        x = np.asarray(streams, dtype=np.float64)
+        x = _fp(streams)
         t = x.shape[1]
         for i in range(loops):
             for j in range(c.n_blocks):
@@ -115,7 +128,8 @@ class OracleModel:
                 if c.block_kind(j) == "gdn":
                     hist = state["conv"][(i, j)]
                     if hist.shape[1] < c.conv_kernel - 1:
-                        pad = np.zeros((hist.shape[0], c.conv_kernel - 1 - hist.shape[1], hist.shape[2]))
+                        pad = np.zeros((hist.shape[0], c.conv_kernel - 1 - hist.shape[1], hist.shape[2]),
+                                       dtype=hist.dtype)
                         hist = np.concatenate([pad, hist], axis=1)
                     mixed, s = gdn.gdn_layer(normed, self._gdn_params(j), state["gdn"][(i, j)],
                                              conv_history=hist)

@@ -56,23 +56,23 @@ def silu(x: np.ndarray) -> np.ndarray:
 
 
 def moe_forward(flat: np.ndarray, idx: np.ndarray, prob: np.ndarray, w_gate: np.ndarray,
-                w_up: np.ndarray, w_down: np.ndarray) -> np.ndarray:
+                w_up: np.ndarray, w_down: np.ndarray, dtype=np.float64) -> np.ndarray:
     """out[t] = sum_s prob[t,s] * W_down[e] (silu(W_gate[e] x_t) * (W_up[e] x_t)), e = idx[t,s].
 
     moe.py:72-81 computes exactly this (padded bmm, silu(g)*u, bmm, gather,
     probability scale, index_add), in float64 here.
     """
-    x = np.asarray(flat, dtype=np.float64)
+    x = np.asarray(flat, dtype=dtype)
     idx = np.asarray(idx, dtype=np.int64)
-    prob = np.asarray(prob, dtype=np.float64)
+    prob = np.asarray(prob, dtype=dtype)
     n, k = idx.shape
     out = np.zeros_like(x)
     for e in np.unique(idx):
         tok, slot = np.nonzero(idx == e)
         xe = x[tok]
-        g = xe @ np.asarray(w_gate[e], dtype=np.float64).T
-        u = xe @ np.asarray(w_up[e], dtype=np.float64).T
-        y = (silu(g) * u) @ np.asarray(w_down[e], dtype=np.float64).T
+        g = xe @ np.asarray(w_gate[e], dtype=dtype).T
+        u = xe @ np.asarray(w_up[e], dtype=dtype).T
+        y = (silu(g) * u) @ np.asarray(w_down[e], dtype=dtype).T
         np.add.at(out, tok, y * prob[tok, slot][:, None])
     return out
 

@@ -25,13 +25,13 @@ def _case(n, d, e, k, f, seed, zipf=False):
     return x, logits, bias, wg, wu, wd
 
 
-def _run(x, logits, bias, wg, wu, wd, k):
+def _run(x, logits, bias, wg, wu, wd, k, path="auto"):
     from hybrid_llm_b200 import kernels
     dev = "cuda"
     plan = kernels.route(torch.from_numpy(logits).to(dev), k,
                          None if bias is None else torch.from_numpy(bias).to(dev))
     w13 = kernels.pack_w13(wg.to(dev), wu.to(dev))
-    out = kernels.moe_grouped(x.to(dev), plan, w13, wd.to(dev))
+    out = kernels.moe_grouped(x.to(dev), plan, w13, wd.to(dev), path=path)
     torch.cuda.synchronize()
     kernels.check_device_status()
     return out, plan
@@ -44,12 +44,13 @@ def _errors(out, ref):
     return err.max() / np.abs(ref).max(), err.mean() / np.abs(ref).mean()
 
 
+@pytest.mark.parametrize("path", ["grouped", "decode"])
 @pytest.mark.parametrize("n,d,e,k,f", [(300, 256, 8, 2, 128), (1, 768, 16, 2, 1024),
                                        (5, 512, 8, 2, 1024), (700, 256, 4, 4, 256),
-                                       (129, 1024, 32, 4, 512)])
-def test_moe_matches_oracle(cuda, n, d, e, k, f):
+                                       (129, 1024, 32, 4, 512), (64, 2048, 64, 8, 1024)])
+def test_moe_matches_oracle(cuda, n, d, e, k, f, path):
     x, logits, bias, wg, wu, wd = _case(n, d, e, k, f, seed=n + d)
-    out, plan = _run(x, logits, bias, wg, wu, wd, k)
+    out, plan = _run(x, logits, bias, wg, wu, wd, k, path=path)
     idx, prob = routing.router_topk(logits, k, bias)
     ref = routing.moe_forward(x.float().numpy(), idx, prob, wg.float().numpy(),
                               wu.float().numpy(), wd.float().numpy())
