@@ -36,16 +36,19 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "llmyb_moe_plan_scratch_bytes": (I64, [I32, I32]),
     "llmyb_moe_plan": (I32, [P, P, I32, I32, I32, I32, P, P, P, P, P, P, P, P, P, P]),
     "llmyb_route": (I32, [P, P, I32, I32, I32, I32, P, P, P, P, P, P, P, P, P, P, P]),
+    "llmyb_route_fused": (I32, [P, P, I32, I32, P, P, P, F32, I32, I32, I32, P, P, P, P, P, P, P, P,
+                                P, P]),
     # MoE expert FFN
     "llmyb_moe_pack_w13": (I32, [P, P, I32, I32, I32, P, P]),
     "llmyb_moe_grouped_scratch_bytes": (I64, [I32, I32, I32, I32]),
     "llmyb_moe_grouped_swiglu": (I32, [P, I32, I32, I32, P, P, P, P, P, I32, P, P, I32, P, P, P, P]),
     "llmyb_moe_decode_scratch_bytes": (I64, [I32, I32, I32, I32]),
     "llmyb_moe_decode_swiglu": (I32, [P, I32, I32, I32, P, P, P, P, I32, P, P, I32, P, P, P]),
+    "llmyb_moe_decode_experts": (I32, [P, I32, I32, I32, P, P, P, I32, P, P, I32, P, P, P]),
     # gated delta rule
     "llmyb_gdn_activate": (I32, [P, I64, I32, I32, I32, I32, P, P]),
     "llmyb_gdn_step": (I32, [P, I64, P, I64, P, I64, P, I64, P, I64, P, P, P, I32, I32, I32, I32,
-                             P, P, I64, P]),
+                             P, P, I64, I32, P, P]),
     "llmyb_gdn_prefill_scratch_bytes": (I64, [I32, I32, I32, I32, I32]),
     "llmyb_gdn_prefill": (I32, [P, I64, P, I64, P, I64, P, I64, P, I64, P, P, P, I32, I32, I32,
                                 I32, I32, P, P, I64, P, P]),
@@ -63,6 +66,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     # residual stream
     "llmyb_embed": (I32, [P, I64, P, I64, I32, P, P, P, P]),
     "llmyb_add_rmsnorm": (I32, [P, P, I64, I32, P, F32, I32, P, P, P]),
+    "llmyb_add_rmsnorm_routed": (I32, [P, P, P, I32, I64, I32, P, F32, I32, P, P, P]),
     "llmyb_rmsnorm_bf16": (I32, [P, I64, I32, P, F32, P, P]),
     # sampling
     "llmyb_sample": (I32, [P, I64, I32, I32, P, I64, F32, P, I32, F32, I32, F32, P, P, P, I32, P, P]),

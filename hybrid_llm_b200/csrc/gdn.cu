@@ -74,6 +74,8 @@ struct GdnIO {
   const float* decay_logit;                      // [H] (alpha = sigmoid), or null
   const float* log_alpha;                        // [B*T, H] per-token log decay, or null
   const uint8_t* reset;                          // [B*T] or null
+  const float* beta_bias;                        // raw inputs: beta = sigmoid(beta + bias)
+  int raw;  // 1: q/k/gate/beta are raw projections (activated in the kernel)
 };
 
 __device__ __forceinline__ float alpha_of(const GdnIO& io, int64_t tok, int h, int H) {
@@ -100,9 +102,33 @@ __global__ void __launch_bounds__(128) gdn_step_kernel(GdnIO io, int H, int VD,
     s_k[i] = bf2f(io.k[tok * io.sk + h * KD + i]);
   }
   __syncthreads();
+  if (io.raw) {
+    // q, k <- x * rsqrt(max(sum x^2, 1e-12)) per head (gated_deltanet.py:128-129)
+    float sq = 0.f, sk = 0.f;
+    for (int i = threadIdx.x; i < KD; i += 128) {
+      sq += s_q[i] * s_q[i];
+      sk += s_k[i] * s_k[i];
+    }
+    sq = warp_sum(sq);
+    sk = warp_sum(sk);
+    if (lane == 0) {
+      s_red[0][warp] = sq;
+      s_red[1][warp] = sk;
+    }
+    __syncthreads();
+    const float nq = rsqrtf(fmaxf(s_red[0][0] + s_red[0][1] + s_red[0][2] + s_red[0][3], 1e-12f));
+    const float nk = rsqrtf(fmaxf(s_red[1][0] + s_red[1][1] + s_red[1][2] + s_red[1][3], 1e-12f));
+    __syncthreads();
+    for (int i = threadIdx.x; i < KD; i += 128) {
+      s_q[i] *= nq;
+      s_k[i] *= nk;
+    }
+    __syncthreads();
+  }
   const bool rst = io.reset != nullptr && io.reset[tok] != 0;
   const float a = alpha_of(io, tok, h, H);
-  const float beta = bf2f(io.beta[tok * io.sb + h]);
+  float beta = bf2f(io.beta[tok * io.sb + h]);
+  if (io.raw) beta = sigmoidf_(beta + (io.beta_bias ? io.beta_bias[h] : 0.f));
   float* S = state + ((static_cast<int64_t>(b) * H + h) * KD) * VD + v0 + lane;
   float s[RPW];
   float pred = 0.f;
@@ -130,7 +156,8 @@ __global__ void __launch_bounds__(128) gdn_step_kernel(GdnIO io, int H, int VD,
   if (warp == 0) {
     o = s_red[0][lane] + s_red[1][lane] + s_red[2][lane] + s_red[3][lane];
     // reference order: out.to(hidden dtype) * gate (gated_deltanet.py:149)
-    const float gt = bf2f(io.gate[tok * io.sg + h * VD + v0 + lane]);
+    float gt = bf2f(io.gate[tok * io.sg + h * VD + v0 + lane]);
+    if (io.raw) gt = sigmoidf_(gt);
     out[tok * so + h * VD + v0 + lane] = f2bf(bf2f(f2bf(o)) * gt);
   }
 }
@@ -614,7 +641,7 @@ __global__ void gdn_conv_gate_kernel(const __nv_bfloat16* __restrict__ x,
                                      const float* __restrict__ conv_w, __nv_bfloat16* history,
                                      const uint8_t* __restrict__ reset, int B, int T, int D,
                                      __nv_bfloat16* __restrict__ out,
-                                     __nv_bfloat16* __restrict__ residual) {
+                                     __nv_bfloat16* __restrict__ residual, int roll1) {
   const int64_t total = static_cast<int64_t>(B) * T * D;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -649,6 +676,14 @@ __global__ void gdn_conv_gate_kernel(const __nv_bfloat16* __restrict__ x,
       acc += conv_w[d * 4 + j] * xv;
     }
     const float yv = bf2f(y_proj[i]) * sigmoidf_(acc);
+    if (roll1) {
+      // T == 1: this thread owns channel d of row b, so it can shift in place
+      __nv_bfloat16* hb = history + static_cast<int64_t>(b) * 3 * D + d;
+      const __nv_bfloat16 h1 = hb[D], h2 = hb[2 * D];
+      hb[0] = h1;
+      hb[D] = h2;
+      hb[2 * D] = x[i];
+    }
     if (residual != nullptr) {
       residual[i] = f2bf(bf2f(residual[i]) + bf2f(f2bf(yv)));
     } else {
@@ -701,6 +736,8 @@ GdnIO make_io(const void* q, int64_t sq, const void* k, int64_t sk, const void* 
   io.decay_logit = decay_logit;
   io.log_alpha = log_alpha;
   io.reset = reset;
+  io.beta_bias = nullptr;
+  io.raw = 0;
   return io;
 }
 
@@ -774,16 +811,21 @@ LLMYB_API int32_t llmyb_gdn_activate(void* proj, int64_t n_tokens, int32_t width
   return launch_status();
 }
 
-// One decode token per row: state [B,H,K,V] fp32 updated in place.
+// One decode token per row: state [B,H,K,V] fp32 updated in place.  With
+// raw_inputs the q/k/gate/beta operands are the raw projections and the
+// kernel applies the activations of llmyb_gdn_activate itself.
 LLMYB_API int32_t llmyb_gdn_step(const void* q, int64_t q_stride, const void* k, int64_t k_stride,
                                  const void* v, int64_t v_stride, const void* gate,
                                  int64_t gate_stride, const void* beta, int64_t beta_stride,
                                  const float* decay_logit, const float* log_alpha,
                                  const uint8_t* reset, int32_t batch, int32_t heads,
                                  int32_t key_dim, int32_t value_dim, float* state, void* out,
-                                 int64_t out_stride, void* stream) {
-  const GdnIO io = make_io(q, q_stride, k, k_stride, v, v_stride, gate, gate_stride, beta,
-                           beta_stride, decay_logit, log_alpha, reset);
+                                 int64_t out_stride, int32_t raw_inputs, const float* beta_bias,
+                                 void* stream) {
+  GdnIO io = make_io(q, q_stride, k, k_stride, v, v_stride, gate, gate_stride, beta,
+                     beta_stride, decay_logit, log_alpha, reset);
+  io.raw = raw_inputs ? 1 : 0;
+  io.beta_bias = beta_bias;
   int32_t st = check_io(io, key_dim, value_dim);
   if (st) return st;
   if (!state || !out || batch < 0 || heads <= 0) return LLMYB_EINVAL;
@@ -853,9 +895,10 @@ LLMYB_API int32_t llmyb_gdn_conv_gate(const void* x, const void* y_proj, const f
   gdn_conv_gate_kernel<<<grid, 256, 0, s>>>(
       static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(y_proj), conv_w,
       static_cast<__nv_bfloat16*>(history), reset, batch, seq, d_model,
-      static_cast<__nv_bfloat16*>(out), static_cast<__nv_bfloat16*>(residual));
+      static_cast<__nv_bfloat16*>(out), static_cast<__nv_bfloat16*>(residual),
+      (roll_history && seq == 1) ? 1 : 0);
   count_launch();
-  if (roll_history) {
+  if (roll_history && seq != 1) {
     gdn_conv_roll_kernel<<<batch, 256, 3 * d_model * sizeof(__nv_bfloat16), s>>>(
         static_cast<const __nv_bfloat16*>(x), static_cast<__nv_bfloat16*>(history), seq, d_model);
     count_launch();

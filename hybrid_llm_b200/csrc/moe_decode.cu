@@ -189,32 +189,13 @@ LLMYB_API int64_t llmyb_moe_decode_scratch_bytes(int32_t n_tokens, int32_t top_k
   return al(rows * ffn * 2) + al(rows * d_model * 2);
 }
 
-// Weight-streaming variant of llmyb_moe_grouped_swiglu for small token counts
-// (same inputs, same plan, w13 from llmyb_moe_pack_w13).  D, F multiples of
-// 128 and at most 2048.
-LLMYB_API int32_t llmyb_moe_decode_swiglu(const void* x, int32_t n_tokens, int32_t d_model,
-                                          int32_t top_k, const int32_t* perm_token,
-                                          const float* perm_prob, const int32_t* route_pos,
-                                          const int32_t* expert_offsets, int32_t n_experts,
-                                          const void* w13, const void* w2, int32_t ffn,
-                                          void* scratch, void* out, void* stream) {
-  if (n_tokens < 0 || d_model <= 0 || top_k <= 0 || n_experts <= 0 || ffn <= 0) return LLMYB_EINVAL;
-  if (n_tokens == 0) return LLMYB_OK;
-  if (!x || !perm_token || !perm_prob || !route_pos || !expert_offsets || !w13 || !w2 ||
-      !scratch || !out)
-    return LLMYB_EINVAL;
-  if (d_model % 128 != 0 || ffn % 128 != 0 || d_model > 8 * 32 * kMaxChunk ||
-      ffn > 8 * 32 * kMaxChunk)
-    return LLMYB_EUNSUPPORTED;
-  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out) |
-       reinterpret_cast<uintptr_t>(w13) | reinterpret_cast<uintptr_t>(w2) |
-       reinterpret_cast<uintptr_t>(scratch)) & 15u)
-    return LLMYB_EUNSUPPORTED;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const int64_t rows = static_cast<int64_t>(n_tokens) * top_k;
-  auto al = [](int64_t b) { return (b + 255) / 256 * 256; };
-  auto* h = static_cast<__nv_bfloat16*>(scratch);
-  auto* y = reinterpret_cast<__nv_bfloat16*>(static_cast<uint8_t*>(scratch) + al(rows * ffn * 2));
+namespace llmyb {
+namespace {
+int32_t launch_experts(const void* x, int32_t n_tokens, int32_t d_model, int32_t top_k,
+                       const int32_t* perm_token, const float* perm_prob,
+                       const int32_t* expert_offsets, int32_t n_experts, const void* w13,
+                       const void* w2, int32_t ffn, __nv_bfloat16* h, __nv_bfloat16* y,
+                       cudaStream_t s) {
   const int up_smem = kTok * d_model * 2, down_smem = kTok * ffn * 2;
   static int up_attr = 0, down_attr = 0;
   if (up_smem > 48 * 1024 && up_smem > up_attr) {
@@ -236,10 +217,71 @@ LLMYB_API int32_t llmyb_moe_decode_swiglu(const void* x, int32_t n_tokens, int32
   moe_decode_down_kernel<<<n_experts * (d_model / kWarps), 256, down_smem, s>>>(
       h, perm_prob, expert_offsets, static_cast<const __nv_bfloat16*>(w2), d_model, ffn, y);
   count_launch();
+  return launch_status();
+}
+
+int32_t check_decode_args(const void* x, int32_t n_tokens, int32_t d_model, int32_t top_k,
+                          int32_t n_experts, int32_t ffn, const void* w13, const void* w2,
+                          const void* a, const void* b) {
+  if (n_tokens < 0 || d_model <= 0 || top_k <= 0 || n_experts <= 0 || ffn <= 0) return LLMYB_EINVAL;
+  if (!x || !w13 || !w2 || !a || !b) return LLMYB_EINVAL;
+  if (d_model % 128 != 0 || ffn % 128 != 0 || d_model > 8 * 32 * kMaxChunk ||
+      ffn > 8 * 32 * kMaxChunk)
+    return LLMYB_EUNSUPPORTED;
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w13) |
+       reinterpret_cast<uintptr_t>(w2) | reinterpret_cast<uintptr_t>(a) |
+       reinterpret_cast<uintptr_t>(b)) & 15u)
+    return LLMYB_EUNSUPPORTED;
+  return LLMYB_OK;
+}
+}  // namespace
+}  // namespace llmyb
+
+// Weight-streaming variant of llmyb_moe_grouped_swiglu for small token counts
+// (same inputs, same plan, w13 from llmyb_moe_pack_w13).  D, F multiples of
+// 128 and at most 2048.
+LLMYB_API int32_t llmyb_moe_decode_swiglu(const void* x, int32_t n_tokens, int32_t d_model,
+                                          int32_t top_k, const int32_t* perm_token,
+                                          const float* perm_prob, const int32_t* route_pos,
+                                          const int32_t* expert_offsets, int32_t n_experts,
+                                          const void* w13, const void* w2, int32_t ffn,
+                                          void* scratch, void* out, void* stream) {
+  int32_t st = check_decode_args(x, n_tokens, d_model, top_k, n_experts, ffn, w13, w2, scratch,
+                                 out);
+  if (st) return st;
+  if (n_tokens == 0) return LLMYB_OK;
+  if (!perm_token || !perm_prob || !route_pos || !expert_offsets) return LLMYB_EINVAL;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t rows = static_cast<int64_t>(n_tokens) * top_k;
+  auto al = [](int64_t b) { return (b + 255) / 256 * 256; };
+  auto* h = static_cast<__nv_bfloat16*>(scratch);
+  auto* y = reinterpret_cast<__nv_bfloat16*>(static_cast<uint8_t*>(scratch) + al(rows * ffn * 2));
+  st = launch_experts(x, n_tokens, d_model, top_k, perm_token, perm_prob, expert_offsets,
+                      n_experts, w13, w2, ffn, h, y, s);
+  if (st) return st;
   const int64_t work = static_cast<int64_t>(n_tokens) * (d_model / 8);
   moe_decode_combine_kernel<<<static_cast<int>(std::min<int64_t>(ceil_div(work, 256), 1184)), 256,
                               0, s>>>(y, route_pos, n_tokens, top_k, d_model,
                                       static_cast<__nv_bfloat16*>(out));
   count_launch();
   return launch_status();
+}
+
+// The two expert kernels of llmyb_moe_decode_swiglu without the combine:
+// y_rows [N*k, D] receives p * expert(x) for every route in plan order, to be
+// summed per token by llmyb_add_rmsnorm_routed.  h_scratch holds [N*k, F].
+LLMYB_API int32_t llmyb_moe_decode_experts(const void* x, int32_t n_tokens, int32_t d_model,
+                                           int32_t top_k, const int32_t* perm_token,
+                                           const float* perm_prob, const int32_t* expert_offsets,
+                                           int32_t n_experts, const void* w13, const void* w2,
+                                           int32_t ffn, void* h_scratch, void* y_rows,
+                                           void* stream) {
+  int32_t st = check_decode_args(x, n_tokens, d_model, top_k, n_experts, ffn, w13, w2, h_scratch,
+                                 y_rows);
+  if (st) return st;
+  if (n_tokens == 0) return LLMYB_OK;
+  if (!perm_token || !perm_prob || !expert_offsets) return LLMYB_EINVAL;
+  return launch_experts(x, n_tokens, d_model, top_k, perm_token, perm_prob, expert_offsets,
+                        n_experts, w13, w2, ffn, static_cast<__nv_bfloat16*>(h_scratch),
+                        static_cast<__nv_bfloat16*>(y_rows), static_cast<cudaStream_t>(stream));
 }

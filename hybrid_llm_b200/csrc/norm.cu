@@ -30,10 +30,12 @@ __global__ void embed_kernel(const int64_t* __restrict__ ids, const __nv_bfloat1
 
 // streams += delta (optional); y = streams * rsqrt(mean(streams^2) + eps) * w
 // (normalize = 0: y = streams, the plain residual value)
+// With route_pos the delta of row n is the sum of the k routed expert rows
+// delta[route_pos[n*k + s]] (the MoE combine fused into the residual add).
 __global__ void __launch_bounds__(256) add_rmsnorm_kernel(
-    float* __restrict__ streams, const __nv_bfloat16* __restrict__ delta, int D,
-    const float* __restrict__ weight, float eps, int normalize,
-    __nv_bfloat16* __restrict__ out_bf16, float* __restrict__ out_f32) {
+    float* __restrict__ streams, const __nv_bfloat16* __restrict__ delta,
+    const int* __restrict__ route_pos, int k, int D, const float* __restrict__ weight, float eps,
+    int normalize, __nv_bfloat16* __restrict__ out_bf16, float* __restrict__ out_f32) {
   __shared__ float red[8];
   const int64_t n = blockIdx.x;
   float* x = streams + n * D;
@@ -41,7 +43,12 @@ __global__ void __launch_bounds__(256) add_rmsnorm_kernel(
   for (int d = threadIdx.x; d < D; d += 256) {
     float v = x[d];
     if (delta != nullptr) {
-      v += bf2f(delta[n * D + d]);
+      if (route_pos != nullptr) {
+        for (int s = 0; s < k; ++s)
+          v += bf2f(delta[static_cast<int64_t>(route_pos[n * k + s]) * D + d]);
+      } else {
+        v += bf2f(delta[n * D + d]);
+      }
       x[d] = v;
     }
     ss += v * v;
@@ -118,8 +125,26 @@ LLMYB_API int32_t llmyb_add_rmsnorm(float* streams, const void* delta, int64_t n
   if (n_tokens == 0) return LLMYB_OK;
   add_rmsnorm_kernel<<<static_cast<unsigned>(n_tokens), 256, 0,
                        static_cast<cudaStream_t>(stream)>>>(
-      streams, static_cast<const __nv_bfloat16*>(delta), d_model, weight, eps, normalize,
-      static_cast<__nv_bfloat16*>(out_bf16), out_f32);
+      streams, static_cast<const __nv_bfloat16*>(delta), nullptr, 0, d_model, weight, eps,
+      normalize, static_cast<__nv_bfloat16*>(out_bf16), out_f32);
+  count_launch();
+  return launch_status();
+}
+
+// streams += sum_s y_rows[route_pos[n*k + s]] (bf16 expert rows, fp32 sum),
+// then RMSNorm as llmyb_add_rmsnorm.
+LLMYB_API int32_t llmyb_add_rmsnorm_routed(float* streams, const void* y_rows,
+                                           const int32_t* route_pos, int32_t top_k,
+                                           int64_t n_tokens, int32_t d_model, const float* weight,
+                                           float eps, int32_t normalize, void* out_bf16,
+                                           float* out_f32, void* stream) {
+  if (!streams || !y_rows || !route_pos || top_k <= 0 || n_tokens < 0 || d_model <= 0)
+    return LLMYB_EINVAL;
+  if (n_tokens == 0) return LLMYB_OK;
+  add_rmsnorm_kernel<<<static_cast<unsigned>(n_tokens), 256, 0,
+                       static_cast<cudaStream_t>(stream)>>>(
+      streams, static_cast<const __nv_bfloat16*>(y_rows), route_pos, top_k, d_model, weight, eps,
+      normalize, static_cast<__nv_bfloat16*>(out_bf16), out_f32);
   count_launch();
   return launch_status();
 }

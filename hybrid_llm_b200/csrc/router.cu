@@ -123,9 +123,10 @@ __global__ void __launch_bounds__(256) plan_hist_kernel(const int64_t* __restric
   for (int e = threadIdx.x; e < E; e += blockDim.x) hist[e * gridDim.x + blockIdx.x] = s_hist_dyn[e];
 }
 
-// Block-wide exclusive scan of one int per thread (blockDim.x == 1024).
+// Block-wide exclusive scan of one int per thread (blockDim.x a multiple of 32).
 __device__ int block_exclusive_scan(int v, int* s_warp, int& total) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nwarps = blockDim.x >> 5;
   int x = v;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
@@ -135,7 +136,7 @@ __device__ int block_exclusive_scan(int v, int* s_warp, int& total) {
   if (lane == 31) s_warp[warp] = x;
   __syncthreads();
   if (warp == 0) {
-    int w = s_warp[lane];
+    int w = lane < nwarps ? s_warp[lane] : 0;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
       const int y = __shfl_up_sync(0xffffffffu, w, o);
@@ -144,7 +145,7 @@ __device__ int block_exclusive_scan(int v, int* s_warp, int& total) {
     s_warp[lane] = w;
   }
   __syncthreads();
-  total = s_warp[31];
+  total = s_warp[nwarps - 1];
   const int excl = x - v + (warp > 0 ? s_warp[warp - 1] : 0);
   __syncthreads();
   return excl;
@@ -335,6 +336,108 @@ __global__ void __launch_bounds__(1024) route_small_kernel(
   }
 }
 
+// Decode-step router, one CTA of 256 threads: for every token
+//   streams += delta;  m = RMSNorm_ffn(streams)          (bf16 copy -> m_bf)
+//   r = RMSNorm_router(m);  logits = W_r r               (fp32)
+// followed by top-k + softmax and the in-order dispatch plan exactly as
+// route_small_kernel (model/model.py:214-241, context_router.py:62-74,
+// moe.py:42-60).  Dynamic shared memory: r rows [8][D] | logits [N][E].
+__global__ void __launch_bounds__(256) router_fused_kernel(
+    float* __restrict__ streams, const __nv_bfloat16* __restrict__ delta, int N, int D,
+    const float* __restrict__ ffn_w, const float* __restrict__ rn_w, const float* __restrict__ Wr,
+    float eps, int E, int k, int tile_m, __nv_bfloat16* __restrict__ m_bf,
+    int64_t* __restrict__ topk_idx, float* __restrict__ topk_prob, int* __restrict__ counts,
+    int* __restrict__ offsets, int* __restrict__ tile_offsets, int* __restrict__ perm_token,
+    float* __restrict__ perm_prob, int* __restrict__ route_pos) {
+  extern __shared__ float s_dyn[];
+  __shared__ int s_idx[256 * kMaxTopK / 4];
+  __shared__ float s_prob[256 * kMaxTopK / 4];
+  __shared__ int s_cnt[kMaxExperts];
+  __shared__ int s_warp[32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  float* r = s_dyn + warp * D;
+  float* s_logits = s_dyn + 8 * D;
+  for (int n = warp; n < N; n += 8) {
+    float* x = streams + static_cast<int64_t>(n) * D;
+    float ss = 0.f;
+    for (int d = lane; d < D; d += 32) {
+      float v = x[d];
+      if (delta != nullptr) {
+        v += bf2f(delta[static_cast<int64_t>(n) * D + d]);
+        x[d] = v;
+      }
+      r[d] = v;
+      ss += v * v;
+    }
+    const float inv = rsqrtf(warp_sum(ss) / static_cast<float>(D) + eps);
+    float ss2 = 0.f;
+    for (int d = lane; d < D; d += 32) {
+      const float m = r[d] * inv * ffn_w[d];
+      m_bf[static_cast<int64_t>(n) * D + d] = f2bf(m);
+      r[d] = m;
+      ss2 += m * m;
+    }
+    const float inv2 = rsqrtf(warp_sum(ss2) / static_cast<float>(D) + eps);
+    for (int d = lane; d < D; d += 32) r[d] = r[d] * inv2 * rn_w[d];
+    __syncwarp();
+    for (int e = 0; e < E; ++e) {
+      const float* w = Wr + static_cast<int64_t>(e) * D;
+      float acc = 0.f;
+      for (int d = lane; d < D; d += 32) acc += r[d] * __ldg(w + d);
+      acc = warp_sum(acc);
+      if (lane == 0) s_logits[n * E + e] = acc;
+    }
+    __syncwarp();
+  }
+  for (int e = threadIdx.x; e < E; e += blockDim.x) s_cnt[e] = 0;
+  __syncthreads();
+  for (int t = warp; t < N; t += 8) {
+    int idx;
+    float val;
+    warp_topk_row(s_logits + t * E, nullptr, E, k, lane, idx, val);
+    const float p = warp_topk_softmax(val, k, lane);
+    if (lane < k) {
+      s_idx[t * k + lane] = idx;
+      s_prob[t * k + lane] = p;
+      topk_idx[static_cast<int64_t>(t) * k + lane] = idx;
+      topk_prob[static_cast<int64_t>(t) * k + lane] = p;
+      atomicAdd(&s_cnt[idx], 1);
+    }
+  }
+  __syncthreads();
+  const int c = threadIdx.x < E ? s_cnt[threadIdx.x] : 0;
+  int total = 0;
+  const int off = block_exclusive_scan(c, s_warp, total);
+  const int tiles = threadIdx.x < E ? static_cast<int>(ceil_div(c, tile_m)) : 0;
+  int total_tiles = 0;
+  const int toff = block_exclusive_scan(tiles, s_warp, total_tiles);
+  if (threadIdx.x < E) {
+    counts[threadIdx.x] = c;
+    offsets[threadIdx.x] = off;
+    tile_offsets[threadIdx.x] = toff;
+    s_cnt[threadIdx.x] = off;
+  }
+  if (threadIdx.x == 0) {
+    offsets[E] = total;
+    tile_offsets[E] = total_tiles;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    for (int t = 0; t < N; ++t) {
+      if (lane < k) {
+        const int rr = t * k + lane;
+        const int e = s_idx[rr];
+        const int pos = s_cnt[e];
+        s_cnt[e] = pos + 1;
+        perm_token[pos] = t;
+        perm_prob[pos] = s_prob[rr];
+        route_pos[rr] = pos;
+      }
+      __syncwarp();
+    }
+  }
+}
+
 int32_t check_route_args(int N, int E, int k, int tile_m) {
   if (N < 0 || E <= 0 || k <= 0 || k > E || tile_m <= 0) return LLMYB_EINVAL;
   if (k > kMaxTopK || E > kMaxExperts) return LLMYB_EUNSUPPORTED;
@@ -449,4 +552,46 @@ LLMYB_API int32_t llmyb_route(const float* logits, const float* bias, int32_t n_
   return plan_tail(topk_idx, topk_prob, n_tokens, n_experts, top_k, tile_m, expert_counts,
                    expert_offsets, tile_offsets, perm_token, perm_prob, route_pos, sort_order,
                    hist, s);
+}
+
+// Decode-step router fused with the residual add and the two RMSNorms that
+// precede it (see router_fused_kernel).  streams [N, D] fp32 in/out; delta
+// [N, D] bf16 (nullable); ffn_norm / router_norm [D] fp32; w_router [E, D]
+// fp32; writes m_bf [N, D] bf16 (the expert input) and the dispatch plan.
+// Limited to N <= 256, N*k <= 2048 and N*E*D <= 2^22 (a single CTA).
+LLMYB_API int32_t llmyb_route_fused(float* streams, const void* delta, int32_t n_tokens,
+                                    int32_t d_model, const float* ffn_norm,
+                                    const float* router_norm, const float* w_router, float eps,
+                                    int32_t n_experts, int32_t top_k, int32_t tile_m, void* m_bf,
+                                    int64_t* topk_idx, float* topk_prob, int32_t* expert_counts,
+                                    int32_t* expert_offsets, int32_t* tile_offsets,
+                                    int32_t* perm_token, float* perm_prob, int32_t* route_pos,
+                                    void* stream) {
+  int32_t st = check_route_args(n_tokens, n_experts, top_k, tile_m);
+  if (st) return st;
+  if (!streams || !ffn_norm || !router_norm || !w_router || !m_bf || !topk_idx || !topk_prob ||
+      !expert_counts || !expert_offsets || !tile_offsets || !perm_token || !perm_prob || !route_pos)
+    return LLMYB_EINVAL;
+  if (n_tokens == 0) {
+    return empty_plan(n_experts, expert_counts, expert_offsets, tile_offsets,
+                      static_cast<cudaStream_t>(stream));
+  }
+  if (n_tokens > 256 || n_tokens * top_k > 256 * kMaxTopK / 4 ||
+      static_cast<int64_t>(n_tokens) * n_experts * d_model > (1 << 22))
+    return LLMYB_EUNSUPPORTED;
+  const int bytes = (8 * d_model + n_tokens * n_experts) * static_cast<int>(sizeof(float));
+  if (bytes > 200 * 1024) return LLMYB_EUNSUPPORTED;
+  static int attr = 0;
+  if (bytes > 48 * 1024 && bytes > attr) {
+    cudaError_t e = cudaFuncSetAttribute(router_fused_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e != cudaSuccess) return e;
+    attr = bytes;
+  }
+  router_fused_kernel<<<1, 256, bytes, static_cast<cudaStream_t>(stream)>>>(
+      streams, static_cast<const __nv_bfloat16*>(delta), n_tokens, d_model, ffn_norm, router_norm,
+      w_router, eps, n_experts, top_k, tile_m, static_cast<__nv_bfloat16*>(m_bf), topk_idx,
+      topk_prob, expert_counts, expert_offsets, tile_offsets, perm_token, perm_prob, route_pos);
+  count_launch();
+  return launch_status();
 }

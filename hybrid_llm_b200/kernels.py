@@ -155,6 +155,69 @@ def moe_plan(topk_idx: torch.Tensor, topk_prob: torch.Tensor, n_experts: int, *,
     return RoutePlan(idx, prob, **b)
 
 
+def route_fused(streams: torch.Tensor, delta: torch.Tensor | None, ffn_norm: torch.Tensor,
+                router_norm: torch.Tensor, w_router: torch.Tensor, k: int, eps: float,
+                m_bf: torch.Tensor) -> RoutePlan:
+    """Decode router: streams += delta; m_bf = RMSNorm_ffn(streams); top-k over
+    w_router . RMSNorm_router(m) (fp32) and the dispatch plan, one launch."""
+    _require_cuda(streams, delta, ffn_norm, router_norm, w_router, m_bf)
+    _inplace(streams, "streams")
+    _inplace(m_bf, "m_bf")
+    n, d = streams.shape
+    e = w_router.shape[0]
+    dev = streams.device
+    idx = torch.empty(n, k, dtype=torch.int64, device=dev)
+    prob = torch.empty(n, k, dtype=torch.float32, device=dev)
+    b = _plan_buffers(n, e, k, dev, False)
+    delta = None if delta is None else delta.contiguous()
+    _native.call("llmyb_route_fused", _ptr(streams), _ptr(delta), n, d, _ptr(ffn_norm),
+                 _ptr(router_norm), _ptr(w_router), float(eps), e, k, TILE_M, _ptr(m_bf),
+                 _ptr(idx), _ptr(prob), _ptr(b["counts"]), _ptr(b["offsets"]),
+                 _ptr(b["tile_offsets"]), _ptr(b["perm_token"]), _ptr(b["perm_prob"]),
+                 _ptr(b["route_pos"]), _stream())
+    return RoutePlan(idx, prob, **b)
+
+
+def route_fused_supported(n: int, e: int, k: int, d: int) -> bool:
+    return n <= 256 and n * k <= 2048 and n * e * d <= (1 << 22) and e <= 256 and k <= 32
+
+
+def moe_decode_experts(x: torch.Tensor, plan: RoutePlan, w13: torch.Tensor, w2: torch.Tensor,
+                       y_rows: torch.Tensor | None = None,
+                       h_scratch: torch.Tensor | None = None) -> torch.Tensor:
+    """Routed expert outputs p * expert(x) per route in plan order ([N*k, D] bf16),
+    to be combined by add_rmsnorm_routed."""
+    _require_cuda(x, w13, w2)
+    x = x.contiguous()
+    n, d = x.shape
+    k = plan.topk_idx.shape[1]
+    e, f2, _ = w13.shape
+    f = f2 // 2
+    if y_rows is None:
+        y_rows = torch.empty(n * k, d, dtype=torch.bfloat16, device=x.device)
+    if h_scratch is None:
+        h_scratch = torch.empty(n * k, f, dtype=torch.bfloat16, device=x.device)
+    _native.call("llmyb_moe_decode_experts", _ptr(x), n, d, k, _ptr(plan.perm_token),
+                 _ptr(plan.perm_prob), _ptr(plan.offsets), e, _ptr(w13), _ptr(w2), f,
+                 _ptr(h_scratch), _ptr(y_rows), _stream())
+    return y_rows
+
+
+def add_rmsnorm_routed(streams: torch.Tensor, y_rows: torch.Tensor, plan: RoutePlan,
+                       weight: torch.Tensor | None, eps: float, *,
+                       out_bf16: torch.Tensor | None = None, out_f32: torch.Tensor | None = None,
+                       normalize: bool = True) -> None:
+    """streams += sum_s y_rows[route_pos[t, s]]; then RMSNorm as add_rmsnorm."""
+    _require_cuda(streams, y_rows, weight)
+    _inplace(streams, "streams")
+    d = streams.shape[-1]
+    n = streams.numel() // d
+    k = plan.topk_idx.shape[1]
+    _native.call("llmyb_add_rmsnorm_routed", _ptr(streams), _ptr(y_rows), _ptr(plan.route_pos), k,
+                 n, d, _ptr(weight), float(eps), int(normalize), _ptr(out_bf16), _ptr(out_f32),
+                 _stream())
+
+
 def pack_w13(w_gate: torch.Tensor, w_up: torch.Tensor) -> torch.Tensor:
     """Interleave [E,F,D] gate/up stacks into the [E,2F,D] GEMM1 operand."""
     _require_cuda(w_gate, w_up)
@@ -244,9 +307,10 @@ def gdn_activate(proj: torch.Tensor, heads: int, key_dim: int, value_dim: int,
 
 
 def gdn_step(q, k, v, gate, beta, state, *, decay_logit=None, log_alpha=None, reset=None,
-             out=None):
-    """One decode token per row.  q,k [B,H,K]; v,gate [B,H,V]; beta [B,H] (all bf16,
-    already activated); state [B,H,K,V] fp32 updated in place; returns out [B,H,V] bf16."""
+             out=None, raw_inputs: bool = False, beta_bias=None):
+    """One decode token per row.  q,k [B,H,K]; v,gate [B,H,V]; beta [B,H] (bf16; already
+    activated, or raw projections with raw_inputs=True and beta_bias [H]); state
+    [B,H,K,V] fp32 updated in place; returns out [B,H,V] bf16."""
     _require_cuda(q, k, v, gate, beta, state)
     bsz, h, kd = q.shape
     vd = v.shape[-1]
@@ -263,9 +327,10 @@ def gdn_step(q, k, v, gate, beta, state, *, decay_logit=None, log_alpha=None, re
     _inplace(state, "state")
     decay_logit = None if decay_logit is None else decay_logit.to(torch.float32).contiguous()
     log_alpha = None if log_alpha is None else log_alpha.to(torch.float32).contiguous()
+    bb = None if beta_bias is None else beta_bias.to(torch.float32).contiguous()
     _native.call("llmyb_gdn_step", qp, qs, kp, ks, vp, vs, gp, gs, bp, bs, _ptr(decay_logit),
                  _ptr(log_alpha), _ptr(r), bsz, h, kd, vd, _ptr(state), _ptr(out),
-                 out.stride(-3), _stream())
+                 out.stride(-3), int(raw_inputs), _ptr(bb), _stream())
     return out
 
 

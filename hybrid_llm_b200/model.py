@@ -182,45 +182,65 @@ class LoopedHybridModel:
     @torch.no_grad()
     def decode_step(self, input_ids: torch.Tensor, state: RecurrentState,
                     num_loops: int | None = None) -> torch.Tensor:
-        """One token per row (LoopedHybridMoEForCausalLM.decode_step, model/model.py:787-915).
+        """One token per row (LoopedHybridMoEForCausalLM.decode_step, model/model.py:787-915,
+        with the loop output carried as in sample_standalone.py's copy).
 
         input_ids [B] or [B, 1] on the device.  Updates `state` in place
         (GDN states, conv histories, ring caches, positions) and returns the
         logits [B, V] (bf16).  Allocation-stable, so it can be captured in a
-        CUDA graph after one warm-up call.
+        CUDA graph after one warm-up call.  Per block: fused residual+norm,
+        one projection GEMM, the mixer kernel(s), one output GEMM, the fused
+        residual+norm+router+plan, two expert kernels; the MoE combine is
+        folded into the next block's residual add.
         """
         c = self.cfg
         ids = input_ids.reshape(-1)
         bsz = ids.shape[0]
         loops = c.num_loops if num_loops is None else int(num_loops)
         d = c.d_model
+        fused_router = kernels.route_fused_supported(bsz, c.moe_experts, c.moe_top_k, d)
         streams = kernels.embed(ids, self.w.embed, self.w.stream_seed)
         normed = torch.empty(bsz, d, dtype=torch.bfloat16, device=self.device)
         m_bf = torch.empty_like(normed)
         m_f32 = torch.empty_like(streams)
-        pending = None
+        y_rows, plan = None, None
         for i in range(loops):
             for j, blk in enumerate(self.w.blocks):
                 key = state_key(i, j)
-                kernels.add_rmsnorm(streams, pending, blk.mixer_norm, c.rms_eps, out_bf16=normed)
+                if y_rows is None:
+                    kernels.add_rmsnorm(streams, None, blk.mixer_norm, c.rms_eps, out_bf16=normed)
+                else:
+                    kernels.add_rmsnorm_routed(streams, y_rows, plan, blk.mixer_norm, c.rms_eps,
+                                               out_bf16=normed)
                 if isinstance(blk.mixer, GdnBlock):
                     mixed = self._gdn_step(blk.mixer, normed, state, key, bsz)
                 else:
                     mixed = self._csa_step(blk.mixer, normed, state, key, bsz)
-                kernels.add_rmsnorm(streams, mixed, blk.ffn_norm, c.rms_eps, out_bf16=m_bf,
-                                    out_f32=m_f32)
-                pending = self._moe(blk, m_bf, m_f32)
-        kernels.add_rmsnorm(streams, pending, None, c.rms_eps, normalize=False)
-        logits = self._head(streams)
+                if fused_router:
+                    plan = kernels.route_fused(streams, mixed, blk.ffn_norm, blk.moe.router_norm,
+                                               blk.moe.router, c.moe_top_k, c.rms_eps, m_bf)
+                else:
+                    kernels.add_rmsnorm(streams, mixed, blk.ffn_norm, c.rms_eps, out_bf16=m_bf,
+                                        out_f32=m_f32)
+                    r_in = torch.empty_like(m_f32)
+                    kernels.add_rmsnorm(m_f32, None, blk.moe.router_norm, c.rms_eps, out_f32=r_in)
+                    plan = kernels.route(torch.mm(r_in, blk.moe.router.t()), c.moe_top_k)
+                y_rows = kernels.moe_decode_experts(m_bf, plan, blk.moe.w13, blk.moe.w2)
+        sb = torch.empty(bsz, d, dtype=torch.bfloat16, device=self.device)
+        kernels.add_rmsnorm_routed(streams, y_rows, plan, None, c.rms_eps, out_bf16=sb,
+                                   normalize=False)
+        collapsed = torch.mm(sb, self.w.collapse.t())
+        h = kernels.rmsnorm_bf16(collapsed, self.w.final_norm, c.rms_eps)
+        logits = torch.mm(h, self.w.embed.t())
         state.positions.add_(1)
         return logits
 
     def _gdn_step(self, g: GdnBlock, normed, state: RecurrentState, key: str, bsz: int):
         c = self.cfg
         proj = torch.mm(normed, g.w_in.t())
-        kernels.gdn_activate(proj, c.gdn_heads, c.gdn_key_dim, c.gdn_value_dim, g.beta_bias)
         q, k, v, gate, beta = self._gdn_views(proj, (bsz,))
-        o = kernels.gdn_step(q, k, v, gate, beta, state.gdn_states[key], decay_logit=g.decay_logit)
+        o = kernels.gdn_step(q, k, v, gate, beta, state.gdn_states[key], decay_logit=g.decay_logit,
+                             raw_inputs=True, beta_bias=g.beta_bias)
         y = torch.mm(o.view(bsz, -1), g.w_out.t())
         return kernels.gdn_conv_gate(normed.view(bsz, 1, -1), y.view(bsz, 1, -1), g.conv,
                                      history=state.gdn_conv_histories[key],
@@ -233,7 +253,7 @@ class LoopedHybridModel:
         local = kernels.csa_local_decode(proj[:, :hd], proj[:, hd:2 * hd], proj[:, 2 * hd:],
                                          state.local_k[key], state.local_v[key], state.positions,
                                          c.csa_heads)
-        return torch.mm(torch.mm(local, a.local_out.t()), a.out.t())
+        return torch.mm(local, a.w_o.t())
 
 
 class GreedyDecoder:

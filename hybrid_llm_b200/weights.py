@@ -12,7 +12,10 @@ the layer modules), so a reference checkpoint's tensors load directly:
 Device layout: the GDN q/k/v/gate/beta projections are fused into one
 [P, D] matrix (P padded to a multiple of 8 for 16-byte rows), the CSA
 query/key/value into one [2*H*Dh + D, D] matrix, and the experts into the
-interleaved gate/up stack w13 [E, 2F, D] plus w2 [E, D, F] (bf16).
+interleaved gate/up stack w13 [E, 2F, D] plus w2 [E, D, F] (bf16).  The CSA
+output path out(local_out(x)) (csa.py:132) is also kept as the single
+product matrix w_o = W_out W_local_out (formed in fp32) for decode, which
+halves its weight traffic per token.
 
 ``synthetic_state_dict`` draws the random-init weights of the benchmark
 workloads: every tensor with two or more dimensions ~ N(0, 0.02), norm
@@ -119,6 +122,7 @@ class CsaBlock:
     w_in: torch.Tensor       # [2*H*Dh + D, D] bf16: query | key | value
     local_out: torch.Tensor  # [D, D] bf16
     out: torch.Tensor        # [D, D] bf16
+    w_o: torch.Tensor        # [D, D] bf16 = out @ local_out (computed in fp32), for decode
 
 
 @dataclass
@@ -168,10 +172,12 @@ class ModelWeights:
                     decay_logit=f32(p + "mixer.decay_logit"), w_out=bf(p + "mixer.out_proj.weight"),
                     conv=f32(p + "mixer.conv.weight").reshape(cfg.d_model, -1).contiguous())
             else:
+                w_o = (f32(p + "mixer.out.weight") @ f32(p + "mixer.local_out.weight"))
                 mixer = CsaBlock(
                     w_in=torch.cat([bf(p + "mixer.query.weight"), bf(p + "mixer.key.weight"),
                                     bf(p + "mixer.value.weight")]).contiguous(),
-                    local_out=bf(p + "mixer.local_out.weight"), out=bf(p + "mixer.out.weight"))
+                    local_out=bf(p + "mixer.local_out.weight"), out=bf(p + "mixer.out.weight"),
+                    w_o=w_o.to(torch.bfloat16).contiguous())
             e = cfg.moe_experts
             gate = torch.stack([sd[f"{p}moe.experts.{x}.gate_proj.weight"].to(dev, torch.bfloat16)
                                 for x in range(e)])

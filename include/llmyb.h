@@ -63,6 +63,19 @@ int32_t llmyb_route(const float* logits, const float* bias, int32_t n_tokens, in
                     int32_t* perm_token, float* perm_prob, int32_t* route_pos,
                     int64_t* sort_order, void* scratch, void* stream);
 
+/* Decode-step router fused with what precedes it in PhysicalBlock.forward_step
+ * (model/model.py:214-241): streams [N,D] fp32 += delta [N,D] bf16
+ * (nullable); m = RMSNorm(streams) * ffn_norm -> m_bf [N,D] bf16 (expert
+ * input); logits = w_router [E,D] . (RMSNorm(m) * router_norm) in fp32;
+ * then top-k/softmax and the plan as llmyb_route.  One CTA: N <= 256,
+ * N*k <= 2048, N*E*D <= 2^22. */
+int32_t llmyb_route_fused(float* streams, const void* delta, int32_t n_tokens, int32_t d_model,
+                          const float* ffn_norm, const float* router_norm, const float* w_router,
+                          float eps, int32_t n_experts, int32_t top_k, int32_t tile_m, void* m_bf,
+                          int64_t* topk_idx, float* topk_prob, int32_t* expert_counts,
+                          int32_t* expert_offsets, int32_t* tile_offsets, int32_t* perm_token,
+                          float* perm_prob, int32_t* route_pos, void* stream);
+
 /* --------------------------------------------------------------- MoE FFN
  * Replaces _moe_dispatch_fused's expert math (model/layers/moe.py:68-81),
  * triton_moe_dispatch (runpod/kernels/triton_swiglu_moe.py:160-266) and the
@@ -102,6 +115,16 @@ int32_t llmyb_moe_decode_swiglu(const void* x, int32_t n_tokens, int32_t d_model
                                 int32_t n_experts, const void* w13, const void* w2, int32_t ffn,
                                 void* scratch, void* out, void* stream);
 
+/* The two expert kernels of llmyb_moe_decode_swiglu without its combine:
+ * y_rows [N*k, D] bf16 gets p * expert(x) for each route in plan order
+ * (summed per token by llmyb_add_rmsnorm_routed); h_scratch holds [N*k, F]
+ * bf16. */
+int32_t llmyb_moe_decode_experts(const void* x, int32_t n_tokens, int32_t d_model, int32_t top_k,
+                                 const int32_t* perm_token, const float* perm_prob,
+                                 const int32_t* expert_offsets, int32_t n_experts,
+                                 const void* w13, const void* w2, int32_t ffn, void* h_scratch,
+                                 void* y_rows, void* stream);
+
 /* ------------------------------------------------------ gated delta rule
  * Replaces GatedDeltaNet's recurrence (model/layers/gated_deltanet.py:140-149
  * and the seams _triton_gdn_scan/_triton_gdn_step at :179-235), the Triton
@@ -119,13 +142,16 @@ int32_t llmyb_gdn_activate(void* proj, int64_t n_tokens, int32_t width, int32_t 
                            void* stream);
 
 /* One token per row (decode): state [B,H,K,V] fp32 updated in place;
- * out (row stride out_stride) = ((S^T q) rounded to bf16) * gate. */
+ * out (row stride out_stride) = ((S^T q) rounded to bf16) * gate.  With
+ * raw_inputs != 0 q/k/gate/beta are the raw projections and the kernel
+ * applies the activations of llmyb_gdn_activate (beta_bias [H] fp32). */
 int32_t llmyb_gdn_step(const void* q, int64_t q_stride, const void* k, int64_t k_stride,
                        const void* v, int64_t v_stride, const void* gate, int64_t gate_stride,
                        const void* beta, int64_t beta_stride, const float* decay_logit,
                        const float* log_alpha, const uint8_t* reset, int32_t batch,
                        int32_t heads, int32_t key_dim, int32_t value_dim, float* state,
-                       void* out, int64_t out_stride, void* stream);
+                       void* out, int64_t out_stride, int32_t raw_inputs,
+                       const float* beta_bias, void* stream);
 
 /* Scratch bytes needed by llmyb_gdn_prefill. */
 int64_t llmyb_gdn_prefill_scratch_bytes(int32_t batch, int32_t seq, int32_t heads,
@@ -212,6 +238,14 @@ int32_t llmyb_embed(const int64_t* ids, int64_t n_tokens, const void* table, int
 int32_t llmyb_add_rmsnorm(float* streams, const void* delta, int64_t n_tokens, int32_t d_model,
                           const float* weight, float eps, int32_t normalize, void* out_bf16,
                           float* out_f32, void* stream);
+
+/* llmyb_add_rmsnorm whose delta for row n is the sum of the k routed expert
+ * rows y_rows[route_pos[n*k + s]] (the MoE combine fused into the residual
+ * add; y_rows from llmyb_moe_decode_experts). */
+int32_t llmyb_add_rmsnorm_routed(float* streams, const void* y_rows, const int32_t* route_pos,
+                                 int32_t top_k, int64_t n_tokens, int32_t d_model,
+                                 const float* weight, float eps, int32_t normalize,
+                                 void* out_bf16, float* out_f32, void* stream);
 
 /* RMSNorm of a bf16 tensor [N, D] (final_norm before the tied LM head). */
 int32_t llmyb_rmsnorm_bf16(const void* x, int64_t n_tokens, int32_t d_model, const float* weight,
