@@ -338,10 +338,12 @@ def run_ours(args) -> None:
             dist.barrier()
         torch.cuda.synchronize()
         a, b = _events()
+        torch.cuda.nvtx.range_push("decode_timed")
         a.record()
         for _ in range(args.steps):
             dec.step()
         b.record()
+        torch.cuda.nvtx.range_pop()
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
@@ -417,10 +419,14 @@ def decode_bytes_per_step(model, cfg) -> float:
     state of every block-loop, the tied LM head."""
     d = cfg.d_model
     dense = 0
+    nb = lambda t: t.numel() * t.element_size()
     for blk in model.w.blocks:
         m = blk.mixer
-        dense += sum(t.numel() * t.element_size() for t in vars(m).values())
-        dense += blk.moe.router.numel() * 4
+        if blk.kind == "gdn":
+            dense += nb(m.w_in) + nb(m.w_out) + nb(m.conv)
+        else:
+            dense += nb(m.w_in) + nb(m.w_o)  # decode uses the pre-multiplied output matrix
+        dense += nb(blk.moe.router)
     dense *= cfg.num_loops
     expert = 3 * cfg.moe_hidden * d * 2 * cfg.moe_top_k * cfg.n_blocks * cfg.num_loops
     n_csa = sum(1 for j in range(cfg.n_blocks) if cfg.block_kind(j) == "csa") * cfg.num_loops

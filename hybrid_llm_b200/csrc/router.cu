@@ -355,39 +355,56 @@ __global__ void __launch_bounds__(256) router_fused_kernel(
   __shared__ int s_cnt[kMaxExperts];
   __shared__ int s_warp[32];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  float* r = s_dyn + warp * D;
-  float* s_logits = s_dyn + 8 * D;
-  for (int n = warp; n < N; n += 8) {
-    float* x = streams + static_cast<int64_t>(n) * D;
-    float ss = 0.f;
-    for (int d = lane; d < D; d += 32) {
-      float v = x[d];
-      if (delta != nullptr) {
-        v += bf2f(delta[static_cast<int64_t>(n) * D + d]);
-        x[d] = v;
+  float* s_r = s_dyn;                 // [8][D] normalised router inputs
+  float* s_logits = s_dyn + 8 * D;    // [N][E]
+  const int nvec = D / 4;
+  for (int n0 = 0; n0 < N; n0 += 8) {
+    // ---- residual add and the two RMSNorms, one token per warp
+    const int n = n0 + warp;
+    float* r = s_r + warp * D;
+    if (n < N) {
+      float* x = streams + static_cast<int64_t>(n) * D;
+      float ss = 0.f;
+      for (int d = lane; d < D; d += 32) {
+        float v = x[d];
+        if (delta != nullptr) {
+          v += bf2f(delta[static_cast<int64_t>(n) * D + d]);
+          x[d] = v;
+        }
+        r[d] = v;
+        ss += v * v;
       }
-      r[d] = v;
-      ss += v * v;
+      const float inv = rsqrtf(warp_sum(ss) / static_cast<float>(D) + eps);
+      float ss2 = 0.f;
+      for (int d = lane; d < D; d += 32) {
+        const float m = r[d] * inv * ffn_w[d];
+        m_bf[static_cast<int64_t>(n) * D + d] = f2bf(m);
+        r[d] = m;
+        ss2 += m * m;
+      }
+      const float inv2 = rsqrtf(warp_sum(ss2) / static_cast<float>(D) + eps);
+      for (int d = lane; d < D; d += 32) r[d] = r[d] * inv2 * rn_w[d];
     }
-    const float inv = rsqrtf(warp_sum(ss) / static_cast<float>(D) + eps);
-    float ss2 = 0.f;
-    for (int d = lane; d < D; d += 32) {
-      const float m = r[d] * inv * ffn_w[d];
-      m_bf[static_cast<int64_t>(n) * D + d] = f2bf(m);
-      r[d] = m;
-      ss2 += m * m;
-    }
-    const float inv2 = rsqrtf(warp_sum(ss2) / static_cast<float>(D) + eps);
-    for (int d = lane; d < D; d += 32) r[d] = r[d] * inv2 * rn_w[d];
-    __syncwarp();
-    for (int e = 0; e < E; ++e) {
-      const float* w = Wr + static_cast<int64_t>(e) * D;
+    __syncthreads();
+    // ---- logits: 16 threads per (token, expert) pair, all row loads in flight
+    const int nt = min(8, N - n0);
+    const int g = threadIdx.x >> 4, gl = threadIdx.x & 15;
+    for (int pr = g; pr < nt * E; pr += 16) {
+      const int t = pr / E, e = pr - t * E;
+      const float4* w = reinterpret_cast<const float4*>(Wr + static_cast<int64_t>(e) * D);
+      const float4* rr = reinterpret_cast<const float4*>(s_r + t * D);
       float acc = 0.f;
-      for (int d = lane; d < D; d += 32) acc += r[d] * __ldg(w + d);
-      acc = warp_sum(acc);
-      if (lane == 0) s_logits[n * E + e] = acc;
+#pragma unroll 8
+      for (int c = gl; c < nvec; c += 16) {
+        const float4 a = __ldg(w + c);
+        const float4 b = rr[c];
+        acc += a.x * b.x + a.y * b.y + a.z * b.z + a.w * b.w;
+      }
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+      if (gl == 0) s_logits[(n0 + t) * E + e] = acc;
     }
-    __syncwarp();
+    __syncthreads();
   }
   for (int e = threadIdx.x; e < E; e += blockDim.x) s_cnt[e] = 0;
   __syncthreads();
@@ -558,7 +575,7 @@ LLMYB_API int32_t llmyb_route(const float* logits, const float* bias, int32_t n_
 // precede it (see router_fused_kernel).  streams [N, D] fp32 in/out; delta
 // [N, D] bf16 (nullable); ffn_norm / router_norm [D] fp32; w_router [E, D]
 // fp32; writes m_bf [N, D] bf16 (the expert input) and the dispatch plan.
-// Limited to N <= 256, N*k <= 2048 and N*E*D <= 2^22 (a single CTA).
+// Limited to N*E <= 256 (token, expert) pairs and N*k <= 2048 (a single CTA).
 LLMYB_API int32_t llmyb_route_fused(float* streams, const void* delta, int32_t n_tokens,
                                     int32_t d_model, const float* ffn_norm,
                                     const float* router_norm, const float* w_router, float eps,
@@ -576,8 +593,8 @@ LLMYB_API int32_t llmyb_route_fused(float* streams, const void* delta, int32_t n
     return empty_plan(n_experts, expert_counts, expert_offsets, tile_offsets,
                       static_cast<cudaStream_t>(stream));
   }
-  if (n_tokens > 256 || n_tokens * top_k > 256 * kMaxTopK / 4 ||
-      static_cast<int64_t>(n_tokens) * n_experts * d_model > (1 << 22))
+  if (n_tokens > 256 || n_tokens * top_k > 256 * kMaxTopK / 4 || n_tokens * n_experts > 256 ||
+      d_model % 4 != 0 || (reinterpret_cast<uintptr_t>(w_router) & 15u))
     return LLMYB_EUNSUPPORTED;
   const int bytes = (8 * d_model + n_tokens * n_experts) * static_cast<int>(sizeof(float));
   if (bytes > 200 * 1024) return LLMYB_EUNSUPPORTED;

@@ -179,7 +179,7 @@ def route_fused(streams: torch.Tensor, delta: torch.Tensor | None, ffn_norm: tor
 
 
 def route_fused_supported(n: int, e: int, k: int, d: int) -> bool:
-    return n <= 256 and n * k <= 2048 and n * e * d <= (1 << 22) and e <= 256 and k <= 32
+    return n * e <= 256 and n * k <= 2048 and d % 4 == 0 and e <= 256 and k <= 32
 
 
 def moe_decode_experts(x: torch.Tensor, plan: RoutePlan, w13: torch.Tensor, w2: torch.Tensor,

@@ -67,8 +67,8 @@ int32_t llmyb_route(const float* logits, const float* bias, int32_t n_tokens, in
  * (model/model.py:214-241): streams [N,D] fp32 += delta [N,D] bf16
  * (nullable); m = RMSNorm(streams) * ffn_norm -> m_bf [N,D] bf16 (expert
  * input); logits = w_router [E,D] . (RMSNorm(m) * router_norm) in fp32;
- * then top-k/softmax and the plan as llmyb_route.  One CTA: N <= 256,
- * N*k <= 2048, N*E*D <= 2^22. */
+ * then top-k/softmax and the plan as llmyb_route.  One CTA: N*E <= 256,
+ * N*k <= 2048, D % 4 == 0. */
 int32_t llmyb_route_fused(float* streams, const void* delta, int32_t n_tokens, int32_t d_model,
                           const float* ffn_norm, const float* router_norm, const float* w_router,
                           float eps, int32_t n_experts, int32_t top_k, int32_t tile_m, void* m_bf,

@@ -164,3 +164,33 @@ def test_conv_history_roll(cuda):
                           out=torch.empty_like(x), roll_history=True)
     torch.cuda.synchronize()
     assert torch.equal(history[:, :2], old[:, 1:]) and torch.equal(history[:, 2:], x)
+
+
+def test_gdn_step_raw_inputs_equal_activated_inputs(cuda):
+    """llmyb_gdn_step with raw projections (in-kernel activation) = activate + step."""
+    from hybrid_llm_b200 import kernels
+    rng = np.random.default_rng(5)
+    b, h, kd, vd = 3, 4, 128, 64
+    width = 2 * h * (kd + vd) + h
+    width += (-width) % 8
+    proj = _bf(rng.normal(0, 1, (b, width))).cuda()
+    bias = torch.from_numpy(rng.normal(0, 0.5, h).astype(np.float32)).cuda()
+    dl = torch.from_numpy(rng.uniform(0.5, 3, h).astype(np.float32)).cuda()
+    st0 = torch.from_numpy(rng.normal(0, 0.3, (b, h, kd, vd)).astype(np.float32)).cuda()
+
+    def views(pr):
+        hk, hv = h * kd, h * vd
+        return (pr[:, :hk].unflatten(-1, (h, kd)), pr[:, hk:2 * hk].unflatten(-1, (h, kd)),
+                pr[:, 2 * hk:2 * hk + hv].unflatten(-1, (h, vd)),
+                pr[:, 2 * hk + hv:2 * hk + 2 * hv].unflatten(-1, (h, vd)),
+                pr[:, 2 * hk + 2 * hv:2 * hk + 2 * hv + h])
+
+    s_raw = st0.clone()
+    o_raw = kernels.gdn_step(*views(proj), s_raw, decay_logit=dl, raw_inputs=True, beta_bias=bias)
+    act = proj.clone()
+    kernels.gdn_activate(act, h, kd, vd, bias)
+    s_act = st0.clone()
+    o_act = kernels.gdn_step(*views(act), s_act, decay_logit=dl)
+    torch.cuda.synchronize()
+    assert _rel(_f(o_raw), _f(o_act)) < 2e-2
+    assert _rel(s_raw.cpu().numpy(), s_act.cpu().numpy()) < 1e-2
