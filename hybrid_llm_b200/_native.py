@@ -36,6 +36,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "llmyb_moe_plan_scratch_bytes": (I64, [I32, I32]),
     "llmyb_moe_plan": (I32, [P, P, I32, I32, I32, I32, P, P, P, P, P, P, P, P, P, P]),
     "llmyb_route": (I32, [P, P, I32, I32, I32, I32, P, P, P, P, P, P, P, P, P, P, P]),
+    "llmyb_route_noalloc": (I32, [P, P, I32, I32, I32, I32, P, P, P, P, P, P, P, P, P, P]),
+    "llmyb_route_noalloc_max_scratch_ints": (I64, []),
     "llmyb_route_fused": (I32, [P, P, I32, I32, P, P, P, F32, I32, I32, I32, P, P, P, P, P, P, P, P,
                                 P, P]),
     # MoE expert FFN

@@ -20,6 +20,8 @@
 // batches (N <= 256) so that a decode step costs one launch.
 #include "common.cuh"
 
+#include <mutex>
+
 namespace llmyb {
 namespace {
 
@@ -534,18 +536,16 @@ LLMYB_API int32_t llmyb_moe_plan(const int64_t* topk_idx, const float* topk_prob
                    hist, s);
 }
 
-// Router top-k + softmax + dispatch plan from fp32 logits (plus an optional
-// per-expert bias added before selection).
-LLMYB_API int32_t llmyb_route(const float* logits, const float* bias, int32_t n_tokens,
-                              int32_t n_experts, int32_t top_k, int32_t tile_m, int64_t* topk_idx,
-                              float* topk_prob, int32_t* expert_counts, int32_t* expert_offsets,
-                              int32_t* tile_offsets, int32_t* perm_token, float* perm_prob,
-                              int32_t* route_pos, int64_t* sort_order, void* scratch,
-                              void* stream) {
+namespace llmyb {
+namespace {
+int32_t route_impl(const float* logits, const float* bias, int32_t n_tokens, int32_t n_experts,
+                   int32_t top_k, int32_t tile_m, int64_t* topk_idx, float* topk_prob,
+                   int32_t* expert_counts, int32_t* expert_offsets, int32_t* tile_offsets,
+                   int32_t* perm_token, float* perm_prob, int32_t* route_pos, int64_t* sort_order,
+                   void* scratch, cudaStream_t s) {
   int32_t st = check_route_args(n_tokens, n_experts, top_k, tile_m);
   if (st) return st;
   if (!expert_counts || !expert_offsets || !tile_offsets) return LLMYB_EINVAL;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (n_tokens == 0) return empty_plan(n_experts, expert_counts, expert_offsets, tile_offsets, s);
   if (!logits || !topk_idx || !topk_prob || !perm_token || !perm_prob || !route_pos)
     return LLMYB_EINVAL;
@@ -569,6 +569,21 @@ LLMYB_API int32_t llmyb_route(const float* logits, const float* bias, int32_t n_
   return plan_tail(topk_idx, topk_prob, n_tokens, n_experts, top_k, tile_m, expert_counts,
                    expert_offsets, tile_offsets, perm_token, perm_prob, route_pos, sort_order,
                    hist, s);
+}
+}  // namespace
+}  // namespace llmyb
+
+// Router top-k + softmax + dispatch plan from fp32 logits (plus an optional
+// per-expert bias added before selection).
+LLMYB_API int32_t llmyb_route(const float* logits, const float* bias, int32_t n_tokens,
+                              int32_t n_experts, int32_t top_k, int32_t tile_m, int64_t* topk_idx,
+                              float* topk_prob, int32_t* expert_counts, int32_t* expert_offsets,
+                              int32_t* tile_offsets, int32_t* perm_token, float* perm_prob,
+                              int32_t* route_pos, int64_t* sort_order, void* scratch,
+                              void* stream) {
+  return route_impl(logits, bias, n_tokens, n_experts, top_k, tile_m, topk_idx, topk_prob,
+                    expert_counts, expert_offsets, tile_offsets, perm_token, perm_prob, route_pos,
+                    sort_order, scratch, static_cast<cudaStream_t>(stream));
 }
 
 // Decode-step router fused with the residual add and the two RMSNorms that
@@ -611,4 +626,75 @@ LLMYB_API int32_t llmyb_route_fused(float* streams, const void* delta, int32_t n
       topk_prob, expert_counts, expert_offsets, tile_offsets, perm_token, perm_prob, route_pos);
   count_launch();
   return launch_status();
+}
+
+// ----------------------------------------------------------------------------
+// Allocation-free routing.
+//
+// Some callers cannot call cudaMalloc at all: code that runs while the
+// device heap is owned by another allocator, inference servers that reserve
+// all memory up front and hand out only input/output buffers, and hosts that
+// must not grow memory after start-up.  llmyb_route needs a caller-provided
+// scratch buffer (llmyb_moe_plan_scratch_bytes) for its per-chunk expert
+// histogram; llmyb_route_noalloc keeps that histogram in a fixed array that
+// lives in this library's own device memory instead, so such callers pass
+// only inputs and outputs.
+//
+// The array holds kNoAllocScratchInts ints (256 KiB) and is held on every
+// device that loads the library until the process exits.  A call needs
+// ceil(n_tokens / 256) * n_experts + 1 ints of it; larger calls are rejected
+// with LLMYB_EUNSUPPORTED.  Every call shares the one array per device, so
+// two calls that overlap on the GPU (for example on two streams) race and
+// must be serialised by the caller.  The histogram is fully rewritten by each
+// call before it is read, so nothing carries over from the previous call.
+constexpr int kNoAllocScratchInts = 1 << 16;
+static __device__ __align__(256) int g_route_scratch[kNoAllocScratchInts];
+
+namespace {
+std::mutex g_route_scratch_mu;
+constexpr int kMaxDevices = 64;
+void* g_route_scratch_addr[kMaxDevices] = {};
+
+// Device address of g_route_scratch on the current device.  In host code the
+// array's name only stands in for the symbol, so the address is looked up once
+// per device (on the first call made with that device current).
+int32_t route_scratch_address(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return static_cast<int32_t>(e);
+  if (dev < 0 || dev >= kMaxDevices) return LLMYB_EUNSUPPORTED;
+  std::lock_guard<std::mutex> lock(g_route_scratch_mu);
+  if (g_route_scratch_addr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_route_scratch);
+    if (e != cudaSuccess) return static_cast<int32_t>(e);
+    g_route_scratch_addr[dev] = p;
+  }
+  *out = g_route_scratch_addr[dev];
+  return LLMYB_OK;
+}
+}  // namespace
+
+LLMYB_API int64_t llmyb_route_noalloc_max_scratch_ints(void) { return kNoAllocScratchInts; }
+
+// llmyb_route without the scratch argument (see the block comment above).
+// The first call on a device looks up the array's device address; make that
+// first call before capturing any CUDA graph that contains this entry point.
+LLMYB_API int32_t llmyb_route_noalloc(const float* logits, const float* bias, int32_t n_tokens,
+                                      int32_t n_experts, int32_t top_k, int32_t tile_m,
+                                      int64_t* topk_idx, float* topk_prob,
+                                      int32_t* expert_counts, int32_t* expert_offsets,
+                                      int32_t* tile_offsets, int32_t* perm_token,
+                                      float* perm_prob, int32_t* route_pos, int64_t* sort_order,
+                                      void* stream) {
+  int32_t st = check_route_args(n_tokens, n_experts, top_k, tile_m);
+  if (st) return st;
+  const int64_t need = ceil_div(n_tokens, kChunk) * n_experts + 1;
+  if (need > kNoAllocScratchInts) return LLMYB_EUNSUPPORTED;
+  void* scratch = nullptr;
+  st = route_scratch_address(&scratch);
+  if (st) return st;
+  return route_impl(logits, bias, n_tokens, n_experts, top_k, tile_m, topk_idx, topk_prob,
+                    expert_counts, expert_offsets, tile_offsets, perm_token, perm_prob, route_pos,
+                    sort_order, scratch, static_cast<cudaStream_t>(stream));
 }

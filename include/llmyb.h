@@ -63,6 +63,27 @@ int32_t llmyb_route(const float* logits, const float* bias, int32_t n_tokens, in
                     int32_t* perm_token, float* perm_prob, int32_t* route_pos,
                     int64_t* sort_order, void* scratch, void* stream);
 
+/* llmyb_route for callers that cannot allocate device memory (a host that
+ * hands the library only its input/output buffers, a server whose memory is
+ * reserved up front, code running while another allocator owns the heap).
+ * No counterpart in the reference.  Same arguments and results as
+ * llmyb_route without `scratch`: the expert histogram lives in a fixed
+ * 256 KiB array inside the library (held on every device that loads the
+ * library until exit).  Calls needing more than
+ * llmyb_route_noalloc_max_scratch_ints() ints (ceil(N/256)*E + 1) return
+ * LLMYB_EUNSUPPORTED.  All calls on a device share the array, so calls that
+ * overlap on the GPU race; each call rewrites it fully before reading it.
+ * The first call on a device looks up the array's address: make it before
+ * capturing a CUDA graph that uses this entry point. */
+int32_t llmyb_route_noalloc(const float* logits, const float* bias, int32_t n_tokens,
+                            int32_t n_experts, int32_t top_k, int32_t tile_m, int64_t* topk_idx,
+                            float* topk_prob, int32_t* expert_counts, int32_t* expert_offsets,
+                            int32_t* tile_offsets, int32_t* perm_token, float* perm_prob,
+                            int32_t* route_pos, int64_t* sort_order, void* stream);
+
+/* Capacity of llmyb_route_noalloc's fixed scratch array, in ints. */
+int64_t llmyb_route_noalloc_max_scratch_ints(void);
+
 /* Decode-step router fused with what precedes it in PhysicalBlock.forward_step
  * (model/model.py:214-241): streams [N,D] fp32 += delta [N,D] bf16
  * (nullable); m = RMSNorm(streams) * ffn_norm -> m_bf [N,D] bf16 (expert
