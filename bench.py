@@ -181,7 +181,7 @@ def _events():
     return torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
 
 
-def secondary_moe(p: dict) -> dict:
+def secondary_moe(p: dict, reps: int = 10) -> dict:
     """Isolated MoE layer: 16384 x 1024 bf16, 32 experts top-4, F=512, Zipf bias."""
     import numpy as np
     import torch
@@ -212,7 +212,7 @@ def secondary_moe(p: dict) -> dict:
     for _ in range(3):
         plan = layer()
     times = []
-    for _ in range(10):
+    for _ in range(max(1, reps)):
         flush.zero_()
         a, b = _events()
         a.record()
@@ -230,7 +230,7 @@ def secondary_moe(p: dict) -> dict:
             "expert_load": counts}
 
 
-def secondary_prefill(p: dict) -> dict:
+def secondary_prefill(p: dict, reps: int = 5) -> dict:
     """Long-context prefill kernels: banded attention and the GDN chunked scan."""
     import numpy as np
     import torch
@@ -244,7 +244,7 @@ def secondary_prefill(p: dict) -> dict:
     for _ in range(3):
         kernels.banded_attention(q, k, v, w, out=out)
     times = []
-    for _ in range(5):
+    for _ in range(max(1, reps)):
         a, e_ = _events()
         a.record()
         kernels.banded_attention(q, k, v, w, out=out)
@@ -269,7 +269,7 @@ def secondary_prefill(p: dict) -> dict:
         st.zero_()
         kernels.gdn_prefill(qn, kn, v, gate, beta, st, log_alpha=la, out=o, scratch=scratch)
     times = []
-    for _ in range(5):
+    for _ in range(max(1, reps)):
         st.zero_()
         a, e_ = _events()
         a.record()
@@ -445,11 +445,18 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--only", choices=["moe_layer", "long_prefill"], default=None,
+                    help="run one secondary workload alone (used for kernel profiles)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.only:
+        import torch
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+        fn = {"moe_layer": secondary_moe, "long_prefill": secondary_prefill}[args.only]
+        print(json.dumps({"only": args.only, **fn(peaks(), reps=args.steps)}), flush=True)
     else:
         run_ours(args)
 
