@@ -167,25 +167,29 @@ struct PrepOut {
   __nv_bfloat16* U;   // [B*T, H, VD]
   __nv_bfloat16* Kw;  // [B*T, H, KD]
   __nv_bfloat16* Aqk; // [B, H, nC, C, C]
-  float* qscale;      // [B*T, H]
-  float* kscale;      // [B*T, H]
+  float* qscale;      // [B, H, T]
+  float* kscale;      // [B, H, T]
   float* sdecay;      // [B, H, nC]
 };
 
+constexpr int cmax(int a, int b) { return a > b ? a : b; }
+constexpr int round16(int x) { return (x + 15) / 16 * 16; }
+
+// Shared memory of the prep kernel, with the phases' buffers aliased so that
+// three CTAs fit on an SM:
+//   qrv : Q (for KK^T / QK^T), then R (blocked inverse), then V (U = T1 V)
+//   at  : A (the (I + A) factor), then T1 | T2 (scaled bf16 copies of T)
 template <int KD, int VD>
 struct PrepSmem {
   static constexpr int LK = KD + 8, LV = VD + 8, LT = kC + 8, LF = kC + 1;
+  static constexpr int QRV = round16(cmax(cmax(kC * LK * 2, kC * LF * 4), kC * LV * 2));
+  static constexpr int AT = round16(cmax(kC * LF * 4, 2 * kC * LT * 2));
   __nv_bfloat16 K[kC * LK];
-  __nv_bfloat16 Q[kC * LK];
-  __nv_bfloat16 V[kC * LV];
-  __nv_bfloat16 T1[kC * LT];  // bf16(T diag(beta))
-  __nv_bfloat16 T2[kC * LT];  // bf16(T diag(beta Gamma_prev seg0))
-  float A[kC * LF];           // strictly lower (I + A) factor
-  float Tm[kC * LF];          // T = (I + A)^-1
-  float R[kC * LF];           // blocked substitution workspace
+  alignas(16) uint8_t qrv[QRV];
+  alignas(16) uint8_t at[AT];
+  float Tm[kC * LF];  // T = (I + A)^-1
   float g[kC], gprev[kC], beta[kC];
   int seg[kC];
-  int n;
 };
 
 template <int KD, int VD>
@@ -194,6 +198,12 @@ __global__ void __launch_bounds__(128) gdn_chunk_prep_kernel(GdnIO io, int B, in
   using SM = PrepSmem<KD, VD>;
   extern __shared__ uint8_t smem_raw[];
   SM& sm = *reinterpret_cast<SM*>(smem_raw);
+  __nv_bfloat16* sQ = reinterpret_cast<__nv_bfloat16*>(sm.qrv);
+  float* sR = reinterpret_cast<float*>(sm.qrv);
+  __nv_bfloat16* sV = reinterpret_cast<__nv_bfloat16*>(sm.qrv);
+  float* sA = reinterpret_cast<float*>(sm.at);
+  __nv_bfloat16* sT1 = reinterpret_cast<__nv_bfloat16*>(sm.at);
+  __nv_bfloat16* sT2 = sT1 + kC * SM::LT;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int nC = static_cast<int>(ceil_div(T, kC));
   const int c = blockIdx.x % nC;
@@ -202,24 +212,17 @@ __global__ void __launch_bounds__(128) gdn_chunk_prep_kernel(GdnIO io, int B, in
   const int t0 = c * kC;
   const int n = min(kC, T - t0);
   const int64_t tok0 = static_cast<int64_t>(b) * T + t0;
+  const int64_t bh = static_cast<int64_t>(b) * H + h;
 
-  // ---- load K, Q, V (zero rows beyond n)
+  // ---- K, Q (zero rows beyond n) and the per-token scalars
   for (int i = tid; i < kC * (KD / 8); i += 128) {
     const int r = i / (KD / 8), cc = (i % (KD / 8)) * 8;
-    uint4 kv = make_uint4(0, 0, 0, 0), qv = kv;
-    if (r < n) {
-      kv = *reinterpret_cast<const uint4*>(io.k + (tok0 + r) * io.sk + h * KD + cc);
-      qv = *reinterpret_cast<const uint4*>(io.q + (tok0 + r) * io.sq + h * KD + cc);
-    }
-    *reinterpret_cast<uint4*>(&sm.K[r * SM::LK + cc]) = kv;
-    *reinterpret_cast<uint4*>(&sm.Q[r * SM::LK + cc]) = qv;
+    const bool ok = r < n;
+    const int64_t tok = tok0 + (ok ? r : 0);
+    mma::cp_async16(&sm.K[r * SM::LK + cc], io.k + tok * io.sk + h * KD + cc, ok);
+    mma::cp_async16(&sQ[r * SM::LK + cc], io.q + tok * io.sq + h * KD + cc, ok);
   }
-  for (int i = tid; i < kC * (VD / 8); i += 128) {
-    const int r = i / (VD / 8), cc = (i % (VD / 8)) * 8;
-    uint4 vv = make_uint4(0, 0, 0, 0);
-    if (r < n) vv = *reinterpret_cast<const uint4*>(io.v + (tok0 + r) * io.sv + h * VD + cc);
-    *reinterpret_cast<uint4*>(&sm.V[r * SM::LV + cc]) = vv;
-  }
+  mma::cp_async_commit();
   if (tid == 0) {
     float g = 0.f;
     int seg = 0;
@@ -238,8 +241,8 @@ __global__ void __launch_bounds__(128) gdn_chunk_prep_kernel(GdnIO io, int B, in
       sm.beta[t] = bt;
       sm.seg[t] = seg;
     }
-    sm.n = n;
   }
+  mma::cp_async_wait<0>();
   __syncthreads();
 
   // ---- KK^T and QK^T for rows 16*warp .. +15 (all 64 columns)
@@ -252,7 +255,7 @@ __global__ void __launch_bounds__(128) gdn_chunk_prep_kernel(GdnIO io, int B, in
   for (int ks = 0; ks < KD; ks += 16) {
     uint32_t ak[4], aq[4];
     mma::load_a(ak, sm.K, SM::LK, warp * 16, ks);
-    mma::load_a(aq, sm.Q, SM::LK, warp * 16, ks);
+    mma::load_a(aq, sQ, SM::LK, warp * 16, ks);
 #pragma unroll
     for (int nb = 0; nb < 8; nb += 2) {
       uint32_t bb[4];
@@ -263,21 +266,29 @@ __global__ void __launch_bounds__(128) gdn_chunk_prep_kernel(GdnIO io, int B, in
       mma::mma_bf16(qk[nb + 1], aq, bb[2], bb[3]);
     }
   }
-  // ---- masks and scales; A to smem (fp32), Aqk to global (bf16)
-  __nv_bfloat16* aqk_out = po.Aqk + ((static_cast<int64_t>(b) * H + h) * nC + c) * kC * kC;
+  __syncthreads();  // Q is dead from here on (its space becomes R)
+  // ---- masks and scales; A to shared memory (fp32), Aqk to global (bf16)
+  __nv_bfloat16* aqk_out = po.Aqk + (bh * nC + c) * kC * kC;
   {
     const int r0 = warp * 16 + (lane >> 2);
 #pragma unroll
     for (int nb = 0; nb < 8; ++nb) {
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int t = r0 + (e >> 1) * 8;
-        const int i = nb * 8 + (lane & 3) * 2 + (e & 1);
-        const bool same = sm.seg[t] == sm.seg[i];
-        sm.A[t * SM::LF + i] =
-            (i < t && same) ? sm.beta[t] * expf(sm.gprev[t] - sm.g[i]) * kk[nb][e] : 0.f;
-        const float m = (i <= t && same && t < n) ? expf(sm.g[t] - sm.g[i]) * qk[nb][e] : 0.f;
-        aqk_out[t * kC + i] = f2bf(m);
+      for (int half = 0; half < 2; ++half) {
+        const int t = r0 + half * 8;
+        const int i = nb * 8 + (lane & 3) * 2;
+        float mv[2];
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const int ii = i + u;
+          const bool same = sm.seg[t] == sm.seg[ii];
+          sA[t * SM::LF + ii] =
+              (ii < t && same) ? sm.beta[t] * expf(sm.gprev[t] - sm.g[ii]) * kk[nb][half * 2 + u]
+                               : 0.f;
+          mv[u] = (ii <= t && same && t < n) ? expf(sm.g[t] - sm.g[ii]) * qk[nb][half * 2 + u]
+                                             : 0.f;
+        }
+        *reinterpret_cast<uint32_t*>(aqk_out + t * kC + i) = pack_bf16x2(mv[0], mv[1]);
       }
     }
   }
@@ -291,56 +302,59 @@ __global__ void __launch_bounds__(128) gdn_chunk_prep_kernel(GdnIO io, int B, in
     for (int t = 0; t < 16; ++t) {
       float acc = (t == j) ? 1.f : 0.f;
       for (int i = 0; i < t; ++i)
-        acc -= sm.A[(base + t) * SM::LF + base + i] * sm.Tm[(base + i) * SM::LF + base + j];
+        acc -= sA[(base + t) * SM::LF + base + i] * sm.Tm[(base + i) * SM::LF + base + j];
       sm.Tm[(base + t) * SM::LF + base + j] = acc;
     }
   }
-  // zero the strictly upper blocks
   for (int i = tid; i < kC * kC; i += 128) {
     const int r = i / kC, cc = i % kC;
     if ((cc >> 4) > (r >> 4)) sm.Tm[r * SM::LF + cc] = 0.f;
   }
   __syncthreads();
   for (int bi = 1; bi < 4; ++bi) {
-    // R_ij = sum_{k=j}^{i-1} A_ik T_kj for all j < i  (rows of block bi, cols < 16*bi)
     for (int idx = tid; idx < 16 * 16 * bi; idx += 128) {
       const int r = bi * 16 + idx / (16 * bi);
       const int cc = idx % (16 * bi);
       float acc = 0.f;
       for (int kq = (cc >> 4) * 16; kq < bi * 16; ++kq)
-        acc += sm.A[r * SM::LF + kq] * sm.Tm[kq * SM::LF + cc];
-      sm.R[r * SM::LF + cc] = acc;
+        acc += sA[r * SM::LF + kq] * sm.Tm[kq * SM::LF + cc];
+      sR[r * SM::LF + cc] = acc;
     }
     __syncthreads();
     for (int idx = tid; idx < 16 * 16 * bi; idx += 128) {
       const int r = bi * 16 + idx / (16 * bi);
       const int cc = idx % (16 * bi);
       float acc = 0.f;
-      for (int kq = bi * 16; kq <= r; ++kq) acc += sm.Tm[r * SM::LF + kq] * sm.R[kq * SM::LF + cc];
+      for (int kq = bi * 16; kq <= r; ++kq) acc += sm.Tm[r * SM::LF + kq] * sR[kq * SM::LF + cc];
       sm.Tm[r * SM::LF + cc] = -acc;
     }
     __syncthreads();
   }
 
-  // ---- scaled bf16 copies of T; per-token scales
+  // ---- V into the R space (R is dead); T1/T2 into the A space (A is dead)
+  for (int i = tid; i < kC * (VD / 8); i += 128) {
+    const int r = i / (VD / 8), cc = (i % (VD / 8)) * 8;
+    const bool ok = r < n;
+    mma::cp_async16(&sV[r * SM::LV + cc], io.v + (tok0 + (ok ? r : 0)) * io.sv + h * VD + cc, ok);
+  }
+  mma::cp_async_commit();
   for (int i = tid; i < kC * kC; i += 128) {
     const int r = i / kC, cc = i % kC;
     const float tv = sm.Tm[r * SM::LF + cc];
-    sm.T1[r * SM::LT + cc] = f2bf(tv * sm.beta[cc]);
+    sT1[r * SM::LT + cc] = f2bf(tv * sm.beta[cc]);
     const float s2 = sm.seg[cc] == 0 ? sm.beta[cc] * expf(sm.gprev[cc]) : 0.f;
-    sm.T2[r * SM::LT + cc] = f2bf(tv * s2);
+    sT2[r * SM::LT + cc] = f2bf(tv * s2);
   }
   if (tid < kC) {
     const int t = tid;
     const int last = n - 1;
     if (t < n) {
-      po.qscale[(tok0 + t) * H + h] = sm.seg[t] == 0 ? expf(sm.g[t]) : 0.f;
-      po.kscale[(tok0 + t) * H + h] = sm.seg[t] == sm.seg[last] ? expf(sm.g[last] - sm.g[t]) : 0.f;
+      po.qscale[bh * T + t0 + t] = sm.seg[t] == 0 ? expf(sm.g[t]) : 0.f;
+      po.kscale[bh * T + t0 + t] = sm.seg[t] == sm.seg[last] ? expf(sm.g[last] - sm.g[t]) : 0.f;
     }
-    if (t == 0)
-      po.sdecay[(static_cast<int64_t>(b) * H + h) * nC + c] =
-          sm.seg[last] == 0 ? expf(sm.g[last]) : 0.f;
+    if (t == 0) po.sdecay[bh * nC + c] = sm.seg[last] == 0 ? expf(sm.g[last]) : 0.f;
   }
+  mma::cp_async_wait<0>();
   __syncthreads();
 
   // ---- U = T1 V  (64 x VD), Kw = T2 K (64 x KD): rows 16*warp..
@@ -348,8 +362,8 @@ __global__ void __launch_bounds__(128) gdn_chunk_prep_kernel(GdnIO io, int B, in
     uint32_t a1[4][4], a2[4][4];
 #pragma unroll
     for (int ks = 0; ks < 4; ++ks) {
-      mma::load_a(a1[ks], sm.T1, SM::LT, warp * 16, ks * 16);
-      mma::load_a(a2[ks], sm.T2, SM::LT, warp * 16, ks * 16);
+      mma::load_a(a1[ks], sT1, SM::LT, warp * 16, ks * 16);
+      mma::load_a(a2[ks], sT2, SM::LT, warp * 16, ks * 16);
     }
     const int r = warp * 16 + (lane >> 2);
 #pragma unroll
@@ -358,7 +372,7 @@ __global__ void __launch_bounds__(128) gdn_chunk_prep_kernel(GdnIO io, int B, in
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks) {
         uint32_t bb[4];
-        mma::load_b_kn(bb, sm.V, SM::LV, ks * 16, nb * 8);
+        mma::load_b_kn(bb, sV, SM::LV, ks * 16, nb * 8);
         mma::mma_bf16(acc0, a1[ks], bb[0], bb[1]);
         mma::mma_bf16(acc1, a1[ks], bb[2], bb[3]);
       }
@@ -398,28 +412,70 @@ __global__ void __launch_bounds__(128) gdn_chunk_prep_kernel(GdnIO io, int B, in
 }
 
 // ----------------------------------------------------------- chunk scan
+// Per (row, head, VC-wide value slice).  The chunk operands (Kw, Q, K, Aqk,
+// U and gate slices, per-token scales) are double-buffered with cp.async so
+// that chunk c+1 streams in while chunk c runs its four small matmuls.
 template <int KD, int VC>
 struct ScanSmem {
   static constexpr int LK = KD + 8, LVC = VC + 8, LT = kC + 8;
-  __nv_bfloat16 Kw[kC * LK];
-  __nv_bfloat16 Q[kC * LK];
-  __nv_bfloat16 K[kC * LK];
-  __nv_bfloat16 Aqk[kC * LT];
+  struct Stage {
+    __nv_bfloat16 Kw[kC * LK];
+    __nv_bfloat16 Q[kC * LK];
+    __nv_bfloat16 K[kC * LK];
+    __nv_bfloat16 Aqk[kC * LT];
+    __nv_bfloat16 U[kC * LVC];
+    __nv_bfloat16 G[kC * LVC];
+    float qs[kC], ks[kC];
+    float sd, pad[3];
+  };
+  Stage st[2];
   __nv_bfloat16 Sh[KD * LVC], Sl[KD * LVC];   // state hi/lo
   __nv_bfloat16 Wh[kC * LVC], Wl[kC * LVC];   // W hi/lo
   __nv_bfloat16 Xh[kC * LVC], Xl[kC * LVC];   // diag(kscale) W hi/lo
-  float U[kC * VC];
-  float gate[kC * VC];
-  float qs[kC], ks[kC];
-  float sd;
 };
 
 __device__ __forceinline__ void split_store(__nv_bfloat16* hi, __nv_bfloat16* lo, int idx, float x0,
                                             float x1) {
-  const __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
-  const float2 hf = __bfloat1622float2(h);
-  *reinterpret_cast<__nv_bfloat162*>(hi + idx) = h;
+  const __nv_bfloat162 hh = __floats2bfloat162_rn(x0, x1);
+  const float2 hf = __bfloat1622float2(hh);
+  *reinterpret_cast<__nv_bfloat162*>(hi + idx) = hh;
   *reinterpret_cast<__nv_bfloat162*>(lo + idx) = __floats2bfloat162_rn(x0 - hf.x, x1 - hf.y);
+}
+
+template <int KD, int VD, int VC>
+__device__ __forceinline__ void scan_issue_chunk(typename ScanSmem<KD, VC>::Stage& sg,
+                                                 const GdnIO& io, const PrepOut& po, int b, int h,
+                                                 int H, int T, int nC, int c, int v0, int tid) {
+  using SM = ScanSmem<KD, VC>;
+  const int t0 = c * kC;
+  const int n = min(kC, T - t0);
+  const int64_t tok0 = static_cast<int64_t>(b) * T + t0;
+  const int64_t bh = static_cast<int64_t>(b) * H + h;
+  for (int i = tid; i < kC * (KD / 8); i += 128) {
+    const int r = i / (KD / 8), cc = (i % (KD / 8)) * 8;
+    const bool ok = r < n;
+    const int64_t tok = tok0 + (ok ? r : 0);
+    mma::cp_async16(&sg.Kw[r * SM::LK + cc], po.Kw + (tok * H + h) * KD + cc, ok);
+    mma::cp_async16(&sg.Q[r * SM::LK + cc], io.q + tok * io.sq + h * KD + cc, ok);
+    mma::cp_async16(&sg.K[r * SM::LK + cc], io.k + tok * io.sk + h * KD + cc, ok);
+  }
+  const __nv_bfloat16* aq = po.Aqk + (bh * nC + c) * kC * kC;
+  for (int i = tid; i < kC * (kC / 8); i += 128) {
+    const int r = i / (kC / 8), cc = (i % (kC / 8)) * 8;
+    mma::cp_async16(&sg.Aqk[r * SM::LT + cc], aq + r * kC + cc, true);
+  }
+  for (int i = tid; i < kC * (VC / 8); i += 128) {
+    const int r = i / (VC / 8), cc = (i % (VC / 8)) * 8;
+    const bool ok = r < n;
+    const int64_t tok = tok0 + (ok ? r : 0);
+    mma::cp_async16(&sg.U[r * SM::LVC + cc], po.U + (tok * H + h) * VD + v0 + cc, ok);
+    mma::cp_async16(&sg.G[r * SM::LVC + cc], io.gate + tok * io.sg + h * VD + v0 + cc, ok);
+  }
+  if (tid < kC) {
+    sg.qs[tid] = tid < n ? po.qscale[bh * T + t0 + tid] : 0.f;
+    sg.ks[tid] = tid < n ? po.kscale[bh * T + t0 + tid] : 0.f;
+  }
+  if (tid == 0) sg.sd = po.sdecay[bh * nC + c];
 }
 
 template <int KD, int VD, int VC>
@@ -441,6 +497,9 @@ __global__ void __launch_bounds__(128) gdn_chunk_scan_kernel(GdnIO io, int B, in
   const int nC = static_cast<int>(ceil_div(T, kC));
   const int r_lo = lane >> 2, cq = (lane & 3) * 2;
 
+  scan_issue_chunk<KD, VD, VC>(sm.st[0], io, po, b, h, H, T, nC, 0, v0, tid);
+  mma::cp_async_commit();
+
   // ---- state rows [warp*KD/4, +KD/4) x VC columns in accumulator layout
   float* Sg = state + (static_cast<int64_t>(b) * H + h) * KD * VD + v0;
   float sacc[MT][NB][4];
@@ -456,10 +515,15 @@ __global__ void __launch_bounds__(128) gdn_chunk_scan_kernel(GdnIO io, int B, in
       }
 
   for (int c = 0; c < nC; ++c) {
+    typename SM::Stage& sg = sm.st[c & 1];
     const int t0 = c * kC;
     const int n = min(kC, T - t0);
     const int64_t tok0 = static_cast<int64_t>(b) * T + t0;
-    // ---- publish S (hi/lo) and load the chunk operands
+    if (c + 1 < nC) {
+      scan_issue_chunk<KD, VD, VC>(sm.st[(c + 1) & 1], io, po, b, h, H, T, nC, c + 1, v0, tid);
+      mma::cp_async_commit();
+    }
+    // ---- publish S (hi/lo) for this chunk's products
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
@@ -470,42 +534,7 @@ __global__ void __launch_bounds__(128) gdn_chunk_scan_kernel(GdnIO io, int B, in
           split_store(sm.Sh, sm.Sl, kr * SM::LVC + nb * 8 + cq, sacc[mt][nb][half * 2],
                       sacc[mt][nb][half * 2 + 1]);
         }
-    for (int i = tid; i < kC * (KD / 8); i += 128) {
-      const int r = i / (KD / 8), cc = (i % (KD / 8)) * 8;
-      uint4 a = make_uint4(0, 0, 0, 0), qv = a, kv = a;
-      if (r < n) {
-        const int64_t tok = tok0 + r;
-        a = *reinterpret_cast<const uint4*>(po.Kw + (tok * H + h) * KD + cc);
-        qv = *reinterpret_cast<const uint4*>(io.q + tok * io.sq + h * KD + cc);
-        kv = *reinterpret_cast<const uint4*>(io.k + tok * io.sk + h * KD + cc);
-      }
-      *reinterpret_cast<uint4*>(&sm.Kw[r * SM::LK + cc]) = a;
-      *reinterpret_cast<uint4*>(&sm.Q[r * SM::LK + cc]) = qv;
-      *reinterpret_cast<uint4*>(&sm.K[r * SM::LK + cc]) = kv;
-    }
-    const __nv_bfloat16* aq = po.Aqk + ((static_cast<int64_t>(b) * H + h) * nC + c) * kC * kC;
-    for (int i = tid; i < kC * (kC / 8); i += 128) {
-      const int r = i / (kC / 8), cc = (i % (kC / 8)) * 8;
-      *reinterpret_cast<uint4*>(&sm.Aqk[r * SM::LT + cc]) =
-          *reinterpret_cast<const uint4*>(aq + r * kC + cc);
-    }
-    for (int i = tid; i < kC * VC; i += 128) {
-      const int r = i / VC, cc = i % VC;
-      float u = 0.f, g = 0.f;
-      if (r < n) {
-        const int64_t tok = tok0 + r;
-        u = bf2f(po.U[(tok * H + h) * VD + v0 + cc]);
-        g = bf2f(io.gate[tok * io.sg + h * VD + v0 + cc]);
-      }
-      sm.U[i] = u;
-      sm.gate[i] = g;
-    }
-    if (tid < kC) {
-      const int64_t tok = tok0 + tid;
-      sm.qs[tid] = tid < n ? po.qscale[tok * H + h] : 0.f;
-      sm.ks[tid] = tid < n ? po.kscale[tok * H + h] : 0.f;
-    }
-    if (tid == 0) sm.sd = po.sdecay[(static_cast<int64_t>(b) * H + h) * nC + c];
+    if (c + 1 < nC) mma::cp_async_wait<1>(); else mma::cp_async_wait<0>();
     __syncthreads();
 
     // ---- W = U - Kw S and QS for rows 16*warp..
@@ -517,8 +546,8 @@ __global__ void __launch_bounds__(128) gdn_chunk_scan_kernel(GdnIO io, int B, in
 #pragma unroll
     for (int kk = 0; kk < KD; kk += 16) {
       uint32_t akw[4], aqq[4];
-      mma::load_a(akw, sm.Kw, SM::LK, warp * 16, kk);
-      mma::load_a(aqq, sm.Q, SM::LK, warp * 16, kk);
+      mma::load_a(akw, sg.Kw, SM::LK, warp * 16, kk);
+      mma::load_a(aqq, sg.Q, SM::LK, warp * 16, kk);
 #pragma unroll
       for (int nb = 0; nb < NB; nb += 2) {
         uint32_t bh[4], bl[4];
@@ -540,12 +569,13 @@ __global__ void __launch_bounds__(128) gdn_chunk_scan_kernel(GdnIO io, int B, in
       for (int half = 0; half < 2; ++half) {
         const int t = warp * 16 + r_lo + half * 8;
         const int col = nb * 8 + cq;
-        const float w0 = sm.U[t * VC + col] - w[nb][half * 2];
-        const float w1 = sm.U[t * VC + col + 1] - w[nb][half * 2 + 1];
+        const float2 u = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(&sg.U[t * SM::LVC + col]));
+        const float w0 = u.x - w[nb][half * 2];
+        const float w1 = u.y - w[nb][half * 2 + 1];
         w[nb][half * 2] = w0;
         w[nb][half * 2 + 1] = w1;
         split_store(sm.Wh, sm.Wl, t * SM::LVC + col, w0, w1);
-        split_store(sm.Xh, sm.Xl, t * SM::LVC + col, w0 * sm.ks[t], w1 * sm.ks[t]);
+        split_store(sm.Xh, sm.Xl, t * SM::LVC + col, w0 * sg.ks[t], w1 * sg.ks[t]);
       }
     __syncthreads();
 
@@ -558,7 +588,7 @@ __global__ void __launch_bounds__(128) gdn_chunk_scan_kernel(GdnIO io, int B, in
 #pragma unroll
     for (int kk = 0; kk < kC; kk += 16) {
       uint32_t aa[4];
-      mma::load_a(aa, sm.Aqk, SM::LT, warp * 16, kk);
+      mma::load_a(aa, sg.Aqk, SM::LT, warp * 16, kk);
 #pragma unroll
       for (int nb = 0; nb < NB; nb += 2) {
         uint32_t bh[4], bl[4];
@@ -577,18 +607,18 @@ __global__ void __launch_bounds__(128) gdn_chunk_scan_kernel(GdnIO io, int B, in
         const int t = warp * 16 + r_lo + half * 8;
         if (t < n) {
           const int col = nb * 8 + cq;
-          const float o0 = sm.qs[t] * qsacc[nb][half * 2] + o[nb][half * 2];
-          const float o1 = sm.qs[t] * qsacc[nb][half * 2 + 1] + o[nb][half * 2 + 1];
+          const float o0 = sg.qs[t] * qsacc[nb][half * 2] + o[nb][half * 2];
+          const float o1 = sg.qs[t] * qsacc[nb][half * 2 + 1] + o[nb][half * 2 + 1];
+          const float2 gt =
+              unpack_bf16x2(*reinterpret_cast<const uint32_t*>(&sg.G[t * SM::LVC + col]));
           // reference order: out.to(hidden dtype) * gate
-          const float r0 = bf2f(f2bf(o0)) * sm.gate[t * VC + col];
-          const float r1 = bf2f(f2bf(o1)) * sm.gate[t * VC + col + 1];
           *reinterpret_cast<uint32_t*>(out + (tok0 + t) * so + h * VD + v0 + col) =
-              pack_bf16x2(r0, r1);
+              pack_bf16x2(bf2f(f2bf(o0)) * gt.x, bf2f(f2bf(o1)) * gt.y);
         }
       }
 
     // ---- S <- sd * S + K^T diag(ks) W   (rows warp*KD/4 ..)
-    const float sd = sm.sd;
+    const float sd = sg.sd;
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
@@ -600,7 +630,7 @@ __global__ void __launch_bounds__(128) gdn_chunk_scan_kernel(GdnIO io, int B, in
 #pragma unroll
       for (int mt = 0; mt < MT; ++mt) {
         uint32_t ak[4];
-        mma::load_a_t(ak, sm.K, SM::LK, warp * (KD / 4) + mt * 16, kk);
+        mma::load_a_t(ak, sg.K, SM::LK, warp * (KD / 4) + mt * 16, kk);
 #pragma unroll
         for (int nb = 0; nb < NB; nb += 2) {
           uint32_t bh[4], bl[4];
