@@ -43,7 +43,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     # MoE expert FFN
     "llmyb_moe_pack_w13": (I32, [P, P, I32, I32, I32, P, P]),
     "llmyb_moe_grouped_scratch_bytes": (I64, [I32, I32, I32, I32]),
-    "llmyb_moe_grouped_swiglu": (I32, [P, I32, I32, I32, P, P, P, P, P, I32, P, P, I32, P, P, P, P]),
+    "llmyb_moe_grouped_swiglu": (I32, [P, I32, I32, I32, P, P, P, P, P, I32, I32, P, P, I32, P, P, P,
+                                       P]),
     "llmyb_moe_decode_scratch_bytes": (I64, [I32, I32, I32, I32]),
     "llmyb_moe_decode_swiglu": (I32, [P, I32, I32, I32, P, P, P, P, I32, P, P, I32, P, P, P]),
     "llmyb_moe_decode_experts": (I32, [P, I32, I32, I32, P, P, P, I32, P, P, I32, P, P, P]),

@@ -265,6 +265,241 @@ __global__ void __launch_bounds__(256, 1) moe_gemm_kernel(
   }
 }
 
+// ------------------------------------------------------------------------
+// CTA-pair variant: a cluster of two CTAs computes a 256 x 256 tile with
+// tcgen05.mma.cta_group::2.  Each CTA stages 128 A rows and 128 B rows per
+// 64-wide K block (32 KB, 6 stages), so the per-SM operand traffic per FLOP is
+// half that of the single-CTA 128 x 256 tile.  The even CTA issues the MMAs;
+// its commits arrive on the barriers of both CTAs (multicast commit); the odd
+// CTA's TMA completions are counted on the even CTA's "full" barrier and its
+// epilogue warps arrive remotely on the even CTA's "tmem empty" barrier.
+// Loads are plain (no multicast): every operand is read from local HBM.
+constexpr int PBM = 128, PBN = 256, PBK = 64, PST = 6;
+constexpr int P_A_BYTES = PBM * PBK * 2;         // 16 KB
+constexpr int P_B_BYTES = (PBN / 2) * PBK * 2;   // 16 KB
+constexpr int P_STAGE = P_A_BYTES + P_B_BYTES;   // 32 KB
+constexpr int P_SMEM = PST * P_STAGE + 1024 + 256;
+
+__device__ __forceinline__ TileInfo map_tile_pair(int tile, int n_tiles, const int* tile_offsets,
+                                                  const int* expert_offsets, int E) {
+  TileInfo ti;
+  const int m_global = tile / n_tiles;
+  ti.n_tile = tile - m_global * n_tiles;
+  int lo = 0, hi = E - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (__ldg(tile_offsets + mid) <= m_global) lo = mid; else hi = mid - 1;
+  }
+  ti.expert = lo;
+  const int m_local = m_global - __ldg(tile_offsets + lo);
+  const int e_begin = __ldg(expert_offsets + lo), e_end = __ldg(expert_offsets + lo + 1);
+  ti.row0 = e_begin + m_local * 2 * PBM;
+  ti.rows_valid = min(2 * PBM, e_end - ti.row0);
+  return ti;
+}
+
+template <int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1) moe_gemm_pair_kernel(
+    const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+    const int* __restrict__ expert_offsets, const int* __restrict__ tile_offsets, int E, int K,
+    int n_weight_rows, __nv_bfloat16* __restrict__ out, int out_ld,
+    const float* __restrict__ row_scale, int32_t* dev_status) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + PST * P_STAGE);
+  uint64_t* empty = full + PST;
+  uint64_t* tmem_full = empty + PST;
+  uint64_t* tmem_empty = tmem_full + 2;
+  uint64_t* mma_done = tmem_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = sm100::cluster_ctarank();
+  const bool leader = rank == 0;
+  const int cluster = blockIdx.x >> 1, nclusters = gridDim.x >> 1;
+  const int n_tiles = n_weight_rows / PBN;
+  const int total_tiles = __ldg(tile_offsets + E) * n_tiles;
+  const int kblocks = K / PBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < PST; ++s) {
+      sm100::mbar_init(&full[s], 1);
+      sm100::mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      sm100::mbar_init(&tmem_full[a], 1);
+      sm100::mbar_init(&tmem_empty[a], 8);  // 4 epilogue warps x 2 CTAs
+    }
+    sm100::mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    sm100::fence_mbar_init();
+    sm100::tma_prefetch_desc(&map_a);
+    sm100::tma_prefetch_desc(&map_b);
+  }
+  if (warp == 2) sm100::tmem_alloc_pair(tmem_slot, TMEM_COLS);
+  sm100::tc_fence_before();
+  sm100::cluster_sync();  // barriers of both CTAs initialised, TMEM allocated
+  sm100::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------- producer
+    int stage = 0;
+    uint32_t phase = 0;
+    uint32_t issued[PST] = {0, 0, 0, 0, 0, 0};
+    bool ok = true;
+    for (int tile = cluster; tile < total_tiles && ok; tile += nclusters) {
+      const TileInfo ti = map_tile_pair(tile, n_tiles, tile_offsets, expert_offsets, E);
+      const int arow = ti.row0 + static_cast<int>(rank) * PBM;
+      const int brow = ti.expert * n_weight_rows + ti.n_tile * PBN + static_cast<int>(rank) * (PBN / 2);
+      for (int kb = 0; kb < kblocks; ++kb) {
+        if (!sm100::mbar_wait_warp(&empty[stage], phase ^ 1u, dev_status, abort_flag)) {
+          ok = false;
+          break;
+        }
+        if (lane == 0) {
+          uint8_t* sa = smem + stage * P_STAGE;
+          uint8_t* sb = sa + P_A_BYTES;
+          const uint32_t full_leader = sm100::mapa_shared(sm100::smem_u32(&full[stage]), 0);
+          if (leader) sm100::mbar_arrive_expect_tx(&full[stage], 2 * P_STAGE);
+          sm100::tma_load_2d_pair(&map_a, full_leader, sa, kb * PBK, arow);
+          sm100::tma_load_2d_pair(&map_b, full_leader, sb, kb * PBK, brow);
+        }
+        issued[stage]++;
+        if (++stage == PST) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+    // every stage this CTA filled has been consumed by the pair's MMAs once the
+    // matching "empty" phase completes
+    for (int s = 0; s < PST; ++s)
+      if (issued[s] > 0) sm100::mbar_wait_warp(&empty[s], (issued[s] - 1u) & 1u, dev_status, nullptr);
+  } else if (warp == 1 && leader) {
+    // ------------------------------------------------------- MMA issuer
+    constexpr uint32_t idesc = sm100::make_idesc_bf16_f32(2 * PBM, PBN);
+    int stage = 0;
+    uint32_t phase = 0;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    bool ok = true;
+    for (int tile = cluster; tile < total_tiles && ok; tile += nclusters) {
+      if (!sm100::mbar_wait_warp(&tmem_empty[acc], acc_phase ^ 1u, dev_status, abort_flag)) break;
+      sm100::tc_fence_after();
+      const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * PBN);
+      for (int kb = 0; kb < kblocks; ++kb) {
+        if (!sm100::mbar_wait_warp(&full[stage], phase, dev_status, abort_flag)) {
+          ok = false;
+          break;
+        }
+        sm100::tc_fence_after();
+        if (lane == 0) {
+          const uint32_t sa = sm100::smem_u32(smem + stage * P_STAGE);
+          const uint64_t adesc = sm100::make_sw128_kmajor_desc(sa);
+          const uint64_t bdesc = sm100::make_sw128_kmajor_desc(sa + P_A_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < PBK / 16; ++kk)
+            sm100::umma_bf16_ss_pair(d_tmem, adesc + 2u * kk, bdesc + 2u * kk, idesc,
+                                     (kb | kk) != 0 ? 1u : 0u);
+          sm100::umma_commit_pair(&empty[stage], 0x3);
+        }
+        __syncwarp();
+        if (++stage == PST) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (!ok) break;
+      if (lane == 0) sm100::umma_commit_pair(&tmem_full[acc], 0x3);
+      __syncwarp();
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+    if (lane == 0) sm100::umma_commit_pair(mma_done, 0x1);
+    __syncwarp();
+    sm100::mbar_wait_warp(mma_done, 0, dev_status, nullptr);
+  } else if (warp >= 4) {
+    // --------------------------------------------------------- epilogue
+    const int q = warp & 3;
+    const int r = q * 32 + lane;
+    const uint32_t empty_leader0 = sm100::mapa_shared(sm100::smem_u32(&tmem_empty[0]), 0);
+    const uint32_t empty_leader1 = sm100::mapa_shared(sm100::smem_u32(&tmem_empty[1]), 0);
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = cluster; tile < total_tiles; tile += nclusters) {
+      const TileInfo ti = map_tile_pair(tile, n_tiles, tile_offsets, expert_offsets, E);
+      if (!sm100::mbar_wait_warp(&tmem_full[acc], acc_phase, dev_status, abort_flag)) break;
+      sm100::tc_fence_after();
+      const uint32_t t_row = tmem_base + static_cast<uint32_t>(acc * PBN) +
+                             (static_cast<uint32_t>(q * 32) << 16);
+      const int my_rows = ti.rows_valid - static_cast<int>(rank) * PBM;
+      const bool valid = r < my_rows;
+      const int64_t row = static_cast<int64_t>(ti.row0) + static_cast<int>(rank) * PBM + r;
+      if (EPI == kSwiGLU) {
+        __nv_bfloat16* dst = out + row * out_ld + ti.n_tile * (PBN / 2);
+#pragma unroll 1
+        for (int c0 = 0; c0 < PBN / 2; c0 += 32) {
+          uint32_t g[32], u[32];
+          sm100::tmem_ld_32x32b_x32(t_row + c0, g);
+          sm100::tmem_ld_32x32b_x32(t_row + PBN / 2 + c0, u);
+          sm100::tmem_ld_wait();
+          if (valid) {
+            uint4 pk[4];
+            uint32_t* pw = reinterpret_cast<uint32_t*>(pk);
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+              pw[j] = pack_bf16x2(silu_mul(__uint_as_float(g[2 * j]), __uint_as_float(u[2 * j])),
+                                  silu_mul(__uint_as_float(g[2 * j + 1]),
+                                           __uint_as_float(u[2 * j + 1])));
+            uint4* d4 = reinterpret_cast<uint4*>(dst + c0);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) d4[j] = pk[j];
+          }
+        }
+      } else {
+        const float scale = valid ? __ldg(row_scale + row) : 0.0f;
+        __nv_bfloat16* dst = out + row * out_ld + ti.n_tile * PBN;
+#pragma unroll 1
+        for (int c0 = 0; c0 < PBN; c0 += 32) {
+          uint32_t a[32];
+          sm100::tmem_ld_32x32b_x32(t_row + c0, a);
+          sm100::tmem_ld_wait();
+          if (valid) {
+            uint4 pk[4];
+            uint32_t* pw = reinterpret_cast<uint32_t*>(pk);
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+              pw[j] = pack_bf16x2(__uint_as_float(a[2 * j]) * scale,
+                                  __uint_as_float(a[2 * j + 1]) * scale);
+            uint4* d4 = reinterpret_cast<uint4*>(dst + c0);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) d4[j] = pk[j];
+          }
+        }
+      }
+      sm100::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) sm100::mbar_arrive_cluster(acc == 0 ? empty_leader0 : empty_leader1);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::cluster_sync();  // no CTA leaves while its peer may still signal its barriers
+  if (warp == 2) {
+    sm100::tc_fence_after();
+    sm100::tmem_dealloc_pair(tmem_base, TMEM_COLS);
+  }
+}
+
 // x_perm[pos, :] = x[perm_token[pos], :]   (16-byte vectors)
 __global__ void gather_rows_kernel(const __nv_bfloat16* __restrict__ x,
                                    const int* __restrict__ perm_token, int64_t rows, int D,
@@ -347,6 +582,12 @@ int32_t ensure_gemm_attrs() {
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, GEMM_SMEM);
   if (e1 != cudaSuccess) return e1;
   if (e2 != cudaSuccess) return e2;
+  cudaError_t e3 = cudaFuncSetAttribute(moe_gemm_pair_kernel<kSwiGLU>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM);
+  cudaError_t e4 = cudaFuncSetAttribute(moe_gemm_pair_kernel<kScale>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM);
+  if (e3 != cudaSuccess) return e3;
+  if (e4 != cudaSuccess) return e4;
   gemm_attr_set = true;
   return LLMYB_OK;
 }
@@ -384,9 +625,9 @@ LLMYB_API int64_t llmyb_moe_grouped_scratch_bytes(int32_t n_tokens, int32_t top_
 LLMYB_API int32_t llmyb_moe_grouped_swiglu(
     const __nv_bfloat16* x, int32_t n_tokens, int32_t d_model, int32_t top_k,
     const int32_t* perm_token, const float* perm_prob, const int32_t* route_pos,
-    const int32_t* expert_offsets, const int32_t* tile_offsets, int32_t n_experts,
-    const __nv_bfloat16* w13, const __nv_bfloat16* w2, int32_t ffn, void* scratch,
-    __nv_bfloat16* out, int32_t* dev_status, void* stream) {
+    const int32_t* expert_offsets, const int32_t* tile_offsets, int32_t tile_m,
+    int32_t n_experts, const __nv_bfloat16* w13, const __nv_bfloat16* w2, int32_t ffn,
+    void* scratch, __nv_bfloat16* out, int32_t* dev_status, void* stream) {
   if (n_tokens < 0 || d_model <= 0 || top_k <= 0 || n_experts <= 0 || ffn <= 0)
     return LLMYB_EINVAL;
   if (n_tokens == 0) return LLMYB_OK;
@@ -395,6 +636,7 @@ LLMYB_API int32_t llmyb_moe_grouped_swiglu(
     return LLMYB_EINVAL;
   if (d_model % BN != 0 || ffn % (BN / 2) != 0 || ffn % BK != 0 || d_model % BK != 0)
     return LLMYB_EUNSUPPORTED;
+  if (tile_m != BM && tile_m != 2 * PBM) return LLMYB_EINVAL;
   if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out) |
        reinterpret_cast<uintptr_t>(scratch)) & 15u)
     return LLMYB_EINVAL;
@@ -414,27 +656,45 @@ LLMYB_API int32_t llmyb_moe_grouped_swiglu(
                                                                          d_model, x_perm);
   count_launch();
 
+  const bool pair = tile_m == 2 * PBM;
+  const uint32_t b_box = pair ? PBN / 2 : BN;
   CUtensorMap ma1, mb1, ma2, mb2;
   if (!make_bf16_2d_map(&ma1, x_perm, rows, d_model, d_model, BM, BK) ||
       !make_bf16_2d_map(&mb1, w13, static_cast<uint64_t>(n_experts) * 2 * ffn, d_model, d_model,
-                        BN, BK) ||
+                        b_box, BK) ||
       !make_bf16_2d_map(&ma2, h_perm, rows, ffn, ffn, BM, BK) ||
-      !make_bf16_2d_map(&mb2, w2, static_cast<uint64_t>(n_experts) * d_model, ffn, ffn, BN, BK))
+      !make_bf16_2d_map(&mb2, w2, static_cast<uint64_t>(n_experts) * d_model, ffn, ffn, b_box,
+                        BK))
     return LLMYB_EUNSUPPORTED;
 
   // upper bound of the m-tile count without reading device memory
-  const int64_t m_tiles_max = ceil_div(rows, BM) + n_experts;
+  const int64_t m_tiles_max = ceil_div(rows, tile_m) + n_experts;
   const int sms = num_sms();
-  const int grid1 = static_cast<int>(std::min<int64_t>(sms, m_tiles_max * (2 * ffn / BN)));
-  const int grid2 = static_cast<int>(std::min<int64_t>(sms, m_tiles_max * (d_model / BN)));
-  moe_gemm_kernel<kSwiGLU><<<grid1, 256, GEMM_SMEM, s>>>(ma1, mb1, expert_offsets, tile_offsets,
-                                                          n_experts, d_model, 2 * ffn, h_perm,
-                                                          ffn, nullptr, dev_status);
-  count_launch();
-  moe_gemm_kernel<kScale><<<grid2, 256, GEMM_SMEM, s>>>(ma2, mb2, expert_offsets, tile_offsets,
-                                                         n_experts, ffn, d_model, y_perm,
-                                                         d_model, perm_prob, dev_status);
-  count_launch();
+  if (pair) {
+    const int clusters = sms / 2;
+    const int grid1 = 2 * static_cast<int>(std::min<int64_t>(clusters, m_tiles_max * (2 * ffn / PBN)));
+    const int grid2 = 2 * static_cast<int>(std::min<int64_t>(clusters, m_tiles_max * (d_model / PBN)));
+    moe_gemm_pair_kernel<kSwiGLU><<<grid1, 256, P_SMEM, s>>>(
+        ma1, mb1, expert_offsets, tile_offsets, n_experts, d_model, 2 * ffn, h_perm, ffn, nullptr,
+        dev_status);
+    count_launch();
+    moe_gemm_pair_kernel<kScale><<<grid2, 256, P_SMEM, s>>>(
+        ma2, mb2, expert_offsets, tile_offsets, n_experts, ffn, d_model, y_perm, d_model,
+        perm_prob, dev_status);
+    count_launch();
+  } else {
+    const int grid1 = static_cast<int>(std::min<int64_t>(sms, m_tiles_max * (2 * ffn / BN)));
+    const int grid2 = static_cast<int>(std::min<int64_t>(sms, m_tiles_max * (d_model / BN)));
+    moe_gemm_kernel<kSwiGLU><<<grid1, 256, GEMM_SMEM, s>>>(ma1, mb1, expert_offsets,
+                                                            tile_offsets, n_experts, d_model,
+                                                            2 * ffn, h_perm, ffn, nullptr,
+                                                            dev_status);
+    count_launch();
+    moe_gemm_kernel<kScale><<<grid2, 256, GEMM_SMEM, s>>>(ma2, mb2, expert_offsets, tile_offsets,
+                                                           n_experts, ffn, d_model, y_perm,
+                                                           d_model, perm_prob, dev_status);
+    count_launch();
+  }
   combine_rows_kernel<<<grid_for(static_cast<int64_t>(n_tokens) * (d_model / 8), 256), 256, 0,
                         s>>>(y_perm, route_pos, n_tokens, top_k, d_model, out);
   count_launch();

@@ -13,7 +13,7 @@ import torch
 
 from . import _native
 
-TILE_M = 128  # rows per grouped-GEMM tile; the plan's tile_offsets use it
+TILE_M = 256  # rows per grouped-GEMM tile (a CTA pair); the plan's tile_offsets use it
 
 _status: dict[int, torch.Tensor] = {}
 
@@ -82,6 +82,7 @@ class RoutePlan:
     perm_prob: torch.Tensor     # [N*k] fp32, route probability of each permuted row
     route_pos: torch.Tensor     # [N*k] int32, permuted row of route t*k+s
     sort_order: torch.Tensor | None  # [N*k] int64, flat route id of each permuted row
+    tile_m: int = TILE_M             # rows per tile behind tile_offsets
 
     @property
     def n_experts(self) -> int:
@@ -105,7 +106,7 @@ def _plan_scratch(n: int, e: int, device) -> torch.Tensor:
 
 
 def route(logits: torch.Tensor, k: int, bias: torch.Tensor | None = None, *,
-          with_sort_order: bool = False) -> RoutePlan:
+          with_sort_order: bool = False, tile_m: int = TILE_M) -> RoutePlan:
     """Top-k + softmax + dispatch plan from fp32 router logits [N, E]."""
     _require_cuda(logits, bias)
     if logits.dtype != torch.float32 or logits.dim() != 2:
@@ -119,11 +120,11 @@ def route(logits: torch.Tensor, k: int, bias: torch.Tensor | None = None, *,
     prob = torch.empty(n, k, dtype=torch.float32, device=dev)
     b = _plan_buffers(n, e, k, dev, with_sort_order)
     scratch = _plan_scratch(n, e, dev)
-    _native.call("llmyb_route", _ptr(logits), _ptr(bias), n, e, k, TILE_M, _ptr(idx), _ptr(prob),
+    _native.call("llmyb_route", _ptr(logits), _ptr(bias), n, e, k, tile_m, _ptr(idx), _ptr(prob),
                  _ptr(b["counts"]), _ptr(b["offsets"]), _ptr(b["tile_offsets"]),
                  _ptr(b["perm_token"]), _ptr(b["perm_prob"]), _ptr(b["route_pos"]),
                  _ptr(b["sort_order"]), _ptr(scratch), _stream())
-    return RoutePlan(idx, prob, **b)
+    return RoutePlan(idx, prob, **b, tile_m=tile_m)
 
 
 def router_topk(logits: torch.Tensor, k: int, bias: torch.Tensor | None = None):
@@ -139,7 +140,7 @@ def router_topk(logits: torch.Tensor, k: int, bias: torch.Tensor | None = None):
 
 
 def moe_plan(topk_idx: torch.Tensor, topk_prob: torch.Tensor, n_experts: int, *,
-             with_sort_order: bool = False) -> RoutePlan:
+             with_sort_order: bool = False, tile_m: int = TILE_M) -> RoutePlan:
     """Dispatch plan for externally computed top-k routes (moe.py:42-60)."""
     _require_cuda(topk_idx, topk_prob)
     idx = topk_idx.to(torch.int64).contiguous()
@@ -148,11 +149,11 @@ def moe_plan(topk_idx: torch.Tensor, topk_prob: torch.Tensor, n_experts: int, *,
     dev = idx.device
     b = _plan_buffers(n, n_experts, k, dev, with_sort_order)
     scratch = _plan_scratch(n, n_experts, dev)
-    _native.call("llmyb_moe_plan", _ptr(idx), _ptr(prob), n, n_experts, k, TILE_M,
+    _native.call("llmyb_moe_plan", _ptr(idx), _ptr(prob), n, n_experts, k, tile_m,
                  _ptr(b["counts"]), _ptr(b["offsets"]), _ptr(b["tile_offsets"]),
                  _ptr(b["perm_token"]), _ptr(b["perm_prob"]), _ptr(b["route_pos"]),
                  _ptr(b["sort_order"]), _ptr(scratch), _ptr(device_status(dev)), _stream())
-    return RoutePlan(idx, prob, **b)
+    return RoutePlan(idx, prob, **b, tile_m=tile_m)
 
 
 def route_fused(streams: torch.Tensor, delta: torch.Tensor | None, ffn_norm: torch.Tensor,
@@ -266,8 +267,8 @@ def moe_grouped(x: torch.Tensor, plan: RoutePlan, w13: torch.Tensor, w2: torch.T
     else:
         _native.call("llmyb_moe_grouped_swiglu", _ptr(x), n, d, k, _ptr(plan.perm_token),
                      _ptr(plan.perm_prob), _ptr(plan.route_pos), _ptr(plan.offsets),
-                     _ptr(plan.tile_offsets), e, _ptr(w13), _ptr(w2), f, _ptr(scratch), _ptr(out),
-                     _ptr(device_status(x.device)), _stream())
+                     _ptr(plan.tile_offsets), plan.tile_m, e, _ptr(w13), _ptr(w2), f,
+                     _ptr(scratch), _ptr(out), _ptr(device_status(x.device)), _stream())
     return out
 
 

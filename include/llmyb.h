@@ -114,13 +114,14 @@ int64_t llmyb_moe_grouped_scratch_bytes(int32_t n_tokens, int32_t top_k, int32_t
 /* out[t] = sum_s p[t,s] * W2[e] (silu(Wg[e] x_t) * (Wu[e] x_t)), bf16 in/out,
  * fp32 accumulation, tcgen05 grouped GEMM over the plan's expert groups.
  * x [N,D], w13 from llmyb_moe_pack_w13, w2 [E,D,F]; D % 256 == 0,
- * F % 128 == 0. */
+ * F % 128 == 0.  tile_m is the plan's tile size: 256 selects the CTA-pair
+ * kernel (tcgen05.mma.cta_group::2, 256x256 tiles), 128 the single-CTA one. */
 int32_t llmyb_moe_grouped_swiglu(const void* x, int32_t n_tokens, int32_t d_model, int32_t top_k,
                                  const int32_t* perm_token, const float* perm_prob,
                                  const int32_t* route_pos, const int32_t* expert_offsets,
-                                 const int32_t* tile_offsets, int32_t n_experts, const void* w13,
-                                 const void* w2, int32_t ffn, void* scratch, void* out,
-                                 int32_t* dev_status, void* stream);
+                                 const int32_t* tile_offsets, int32_t tile_m, int32_t n_experts,
+                                 const void* w13, const void* w2, int32_t ffn, void* scratch,
+                                 void* out, int32_t* dev_status, void* stream);
 
 /* Scratch bytes needed by llmyb_moe_decode_swiglu. */
 int64_t llmyb_moe_decode_scratch_bytes(int32_t n_tokens, int32_t top_k, int32_t d_model,

@@ -28,8 +28,11 @@ def _case(n, d, e, k, f, seed, zipf=False):
 def _run(x, logits, bias, wg, wu, wd, k, path="auto"):
     from hybrid_llm_b200 import kernels
     dev = "cuda"
+    tile_m = 128 if path == "grouped128" else kernels.TILE_M
+    if path == "grouped128":
+        path = "grouped"
     plan = kernels.route(torch.from_numpy(logits).to(dev), k,
-                         None if bias is None else torch.from_numpy(bias).to(dev))
+                         None if bias is None else torch.from_numpy(bias).to(dev), tile_m=tile_m)
     w13 = kernels.pack_w13(wg.to(dev), wu.to(dev))
     out = kernels.moe_grouped(x.to(dev), plan, w13, wd.to(dev), path=path)
     torch.cuda.synchronize()
@@ -44,7 +47,7 @@ def _errors(out, ref):
     return err.max() / np.abs(ref).max(), err.mean() / np.abs(ref).mean()
 
 
-@pytest.mark.parametrize("path", ["grouped", "decode"])
+@pytest.mark.parametrize("path", ["grouped", "grouped128", "decode"])
 @pytest.mark.parametrize("n,d,e,k,f", [(300, 256, 8, 2, 128), (1, 768, 16, 2, 1024),
                                        (5, 512, 8, 2, 1024), (700, 256, 4, 4, 256),
                                        (129, 1024, 32, 4, 512), (64, 2048, 64, 8, 1024)])
@@ -72,11 +75,12 @@ def _torch_reference(x, plan, wg, wu, wd):
     return out
 
 
-def test_moe_isolated_layer_full_size(cuda):
+@pytest.mark.parametrize("path", ["grouped", "grouped128"])
+def test_moe_isolated_layer_full_size(cuda, path):
     """16384 tokens x 1024, 32 experts top-4, F=512, Zipf-skewed routing."""
     x, logits, bias, wg, wu, wd = _case(16384, 1024, 32, 4, 512, seed=3, zipf=True)
     dev = "cuda"
-    out, plan = _run(x, logits, bias, wg, wu, wd, 4)
+    out, plan = _run(x, logits, bias, wg, wu, wd, 4, path=path)
     ref = _torch_reference(x.to(dev), plan, wg.to(dev), wu.to(dev), wd.to(dev))
     err = (out.float() - ref).abs()
     assert float(err.max() / ref.abs().max()) < MAX_REL

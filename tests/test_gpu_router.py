@@ -25,7 +25,7 @@ def _run_route(logits, k, bias=None, fused=True, dev="cuda"):
 
 
 def _check_plan(got, idx, prob, e):
-    ref = routing.dispatch_plan(idx, e)
+    ref = routing.dispatch_plan(idx, e, tile_m=got["tile_m"])
     np.testing.assert_array_equal(got["topk_idx"], idx)
     np.testing.assert_allclose(got["topk_prob"], prob, rtol=2e-6, atol=1e-7)
     np.testing.assert_array_equal(got["counts"], ref["counts"])
