@@ -21,8 +21,8 @@
 //              stage into a TMEM accumulator; two accumulators of 256 columns
 //              so the epilogue of tile i overlaps the main loop of tile i+1.
 //   warp 2     TMEM allocation owner.
-//   warps 4-7  epilogue: tcgen05.ld 32 lanes x 32 columns, fused SwiGLU or
-//              probability scale, bf16 stores.
+//   warps 4-7  epilogue: tcgen05.ld 32 lanes x 32 columns (one chunk ahead of
+//              the math), fused SwiGLU or probability scale, bf16 stores.
 // For GEMM1 the weight rows are pre-interleaved (llmyb_moe_pack_w13) so that
 // every 256-wide N tile holds 128 gate rows followed by the matching 128 up
 // rows, which keeps silu(gate) * up inside one accumulator.
@@ -66,6 +66,75 @@ __device__ __forceinline__ TileInfo map_tile(int tile, int n_tiles, const int* t
   ti.row0 = e_begin + m_local * BM;
   ti.rows_valid = min(BM, e_end - ti.row0);
   return ti;
+}
+
+__device__ __forceinline__ float swiglu_fast(uint32_t g_bits, uint32_t u_bits) {
+  const float g = __uint_as_float(g_bits), u = __uint_as_float(u_bits);
+  return __fdividef(g * u, 1.0f + __expf(-g));
+}
+
+// Epilogue of one warp: its 32 accumulator rows (TMEM lanes) x 256 fp32
+// columns starting at t_row, written as bf16 into this lane's output row dst.
+//   kSwiGLU: columns [0,128) hold gate, [128,256) up -> 128 outputs
+//            silu(g) * u = g u / (1 + e^-g) with the fast exp / divide
+//            intrinsics (relative error ~1e-6, far below bf16 rounding).
+//   kScale : 256 outputs, each times the row's route probability.
+// The TMEM loads of chunk i+1 are in flight while chunk i is converted and
+// stored (double-buffered registers).
+template <int EPI>
+__device__ __forceinline__ void epilogue_rows(uint32_t t_row, bool valid, float scale,
+                                              __nv_bfloat16* dst) {
+  static_assert(BN == 256, "epilogue assumes 256 accumulator columns");
+  if constexpr (EPI == kSwiGLU) {
+    constexpr int NCH = BN / 2 / 32;
+    uint32_t g[2][32], u[2][32];
+    sm100::tmem_ld_32x32b_x32(t_row, g[0]);
+    sm100::tmem_ld_32x32b_x32(t_row + BN / 2, u[0]);
+#pragma unroll
+    for (int i = 0; i < NCH; ++i) {
+      const int b = i & 1;
+      sm100::tmem_ld_wait();
+      sm100::tmem_regs_ready(g[b]);
+      sm100::tmem_regs_ready(u[b]);
+      if (i + 1 < NCH) {
+        sm100::tmem_ld_32x32b_x32(t_row + 32 * (i + 1), g[b ^ 1]);
+        sm100::tmem_ld_32x32b_x32(t_row + BN / 2 + 32 * (i + 1), u[b ^ 1]);
+      }
+      if (valid) {
+        uint4 pk[4];
+        uint32_t* pw = reinterpret_cast<uint32_t*>(pk);
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          pw[j] = pack_bf16x2(swiglu_fast(g[b][2 * j], u[b][2 * j]),
+                              swiglu_fast(g[b][2 * j + 1], u[b][2 * j + 1]));
+        uint4* d4 = reinterpret_cast<uint4*>(dst + 32 * i);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) d4[j] = pk[j];
+      }
+    }
+  } else {
+    constexpr int NCH = BN / 32;
+    uint32_t a[2][32];
+    sm100::tmem_ld_32x32b_x32(t_row, a[0]);
+#pragma unroll
+    for (int i = 0; i < NCH; ++i) {
+      const int b = i & 1;
+      sm100::tmem_ld_wait();
+      sm100::tmem_regs_ready(a[b]);
+      if (i + 1 < NCH) sm100::tmem_ld_32x32b_x32(t_row + 32 * (i + 1), a[b ^ 1]);
+      if (valid) {
+        uint4 pk[4];
+        uint32_t* pw = reinterpret_cast<uint32_t*>(pk);
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          pw[j] = pack_bf16x2(__uint_as_float(a[b][2 * j]) * scale,
+                              __uint_as_float(a[b][2 * j + 1]) * scale);
+        uint4* d4 = reinterpret_cast<uint4*>(dst + 32 * i);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) d4[j] = pk[j];
+      }
+    }
+  }
 }
 
 template <int EPI>
@@ -205,50 +274,9 @@ __global__ void __launch_bounds__(256, 1) moe_gemm_kernel(
                              (static_cast<uint32_t>(q * 32) << 16);
       const bool valid = r < ti.rows_valid;
       const int64_t row = static_cast<int64_t>(ti.row0) + r;
-      if (EPI == kSwiGLU) {
-        __nv_bfloat16* dst = out + row * out_ld + ti.n_tile * (BN / 2);
-#pragma unroll 1
-        for (int c0 = 0; c0 < BN / 2; c0 += 32) {
-          uint32_t g[32], u[32];
-          sm100::tmem_ld_32x32b_x32(t_row + c0, g);
-          sm100::tmem_ld_32x32b_x32(t_row + BN / 2 + c0, u);
-          sm100::tmem_ld_wait();
-          if (valid) {
-            uint4 pk[4];
-            uint32_t* pw = reinterpret_cast<uint32_t*>(pk);
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              const float h0 = silu_mul(__uint_as_float(g[2 * j]), __uint_as_float(u[2 * j]));
-              const float h1 =
-                  silu_mul(__uint_as_float(g[2 * j + 1]), __uint_as_float(u[2 * j + 1]));
-              pw[j] = pack_bf16x2(h0, h1);
-            }
-            uint4* d4 = reinterpret_cast<uint4*>(dst + c0);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) d4[j] = pk[j];
-          }
-        }
-      } else {
-        const float scale = valid ? __ldg(row_scale + row) : 0.0f;
-        __nv_bfloat16* dst = out + row * out_ld + ti.n_tile * BN;
-#pragma unroll 1
-        for (int c0 = 0; c0 < BN; c0 += 32) {
-          uint32_t a[32];
-          sm100::tmem_ld_32x32b_x32(t_row + c0, a);
-          sm100::tmem_ld_wait();
-          if (valid) {
-            uint4 pk[4];
-            uint32_t* pw = reinterpret_cast<uint32_t*>(pk);
-#pragma unroll
-            for (int j = 0; j < 16; ++j)
-              pw[j] = pack_bf16x2(__uint_as_float(a[2 * j]) * scale,
-                                  __uint_as_float(a[2 * j + 1]) * scale);
-            uint4* d4 = reinterpret_cast<uint4*>(dst + c0);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) d4[j] = pk[j];
-          }
-        }
-      }
+      const float scale = (EPI == kScale && valid) ? __ldg(row_scale + row) : 0.0f;
+      __nv_bfloat16* dst = out + row * out_ld + ti.n_tile * (EPI == kSwiGLU ? BN / 2 : BN);
+      epilogue_rows<EPI>(t_row, valid, scale, dst);
       sm100::tc_fence_before();
       sm100::mbar_arrive(&tmem_empty[acc]);
       if (++acc == 2) {
@@ -440,48 +468,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1) moe_gemm_pai
       const int my_rows = ti.rows_valid - static_cast<int>(rank) * PBM;
       const bool valid = r < my_rows;
       const int64_t row = static_cast<int64_t>(ti.row0) + static_cast<int>(rank) * PBM + r;
-      if (EPI == kSwiGLU) {
-        __nv_bfloat16* dst = out + row * out_ld + ti.n_tile * (PBN / 2);
-#pragma unroll 1
-        for (int c0 = 0; c0 < PBN / 2; c0 += 32) {
-          uint32_t g[32], u[32];
-          sm100::tmem_ld_32x32b_x32(t_row + c0, g);
-          sm100::tmem_ld_32x32b_x32(t_row + PBN / 2 + c0, u);
-          sm100::tmem_ld_wait();
-          if (valid) {
-            uint4 pk[4];
-            uint32_t* pw = reinterpret_cast<uint32_t*>(pk);
-#pragma unroll
-            for (int j = 0; j < 16; ++j)
-              pw[j] = pack_bf16x2(silu_mul(__uint_as_float(g[2 * j]), __uint_as_float(u[2 * j])),
-                                  silu_mul(__uint_as_float(g[2 * j + 1]),
-                                           __uint_as_float(u[2 * j + 1])));
-            uint4* d4 = reinterpret_cast<uint4*>(dst + c0);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) d4[j] = pk[j];
-          }
-        }
-      } else {
-        const float scale = valid ? __ldg(row_scale + row) : 0.0f;
-        __nv_bfloat16* dst = out + row * out_ld + ti.n_tile * PBN;
-#pragma unroll 1
-        for (int c0 = 0; c0 < PBN; c0 += 32) {
-          uint32_t a[32];
-          sm100::tmem_ld_32x32b_x32(t_row + c0, a);
-          sm100::tmem_ld_wait();
-          if (valid) {
-            uint4 pk[4];
-            uint32_t* pw = reinterpret_cast<uint32_t*>(pk);
-#pragma unroll
-            for (int j = 0; j < 16; ++j)
-              pw[j] = pack_bf16x2(__uint_as_float(a[2 * j]) * scale,
-                                  __uint_as_float(a[2 * j + 1]) * scale);
-            uint4* d4 = reinterpret_cast<uint4*>(dst + c0);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) d4[j] = pk[j];
-          }
-        }
-      }
+      const float scale = (EPI == kScale && valid) ? __ldg(row_scale + row) : 0.0f;
+      __nv_bfloat16* dst = out + row * out_ld + ti.n_tile * (EPI == kSwiGLU ? PBN / 2 : PBN);
+      epilogue_rows<EPI>(t_row, valid, scale, dst);
       sm100::tc_fence_before();
       __syncwarp();
       if (lane == 0) sm100::mbar_arrive_cluster(acc == 0 ? empty_leader0 : empty_leader1);

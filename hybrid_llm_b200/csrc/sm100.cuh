@@ -207,6 +207,16 @@ __device__ __forceinline__ void tmem_ld_wait() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// Registers written by tcgen05.ld hold valid data only after tcgen05.wait::ld.
+// Passing them through an empty volatile asm placed after the wait makes every
+// later use depend on that point, so the compiler cannot hoist a use above the
+// wait when loads are software-pipelined.
+template <int N>
+__device__ __forceinline__ void tmem_regs_ready(uint32_t (&r)[N]) {
+#pragma unroll
+  for (int i = 0; i < N; ++i) asm volatile("" : "+r"(r[i])::"memory");
+}
+
 __device__ __forceinline__ bool elect_one() {
   uint32_t pred = 0;
   asm volatile(
