@@ -93,7 +93,7 @@ __global__ void __launch_bounds__(256) moe_decode_up_kernel(
 __global__ void __launch_bounds__(256) moe_decode_down_kernel(
     const __nv_bfloat16* __restrict__ h_perm, const float* __restrict__ perm_prob,
     const int* __restrict__ expert_offsets, const __nv_bfloat16* __restrict__ w2, int D, int F,
-    __nv_bfloat16* __restrict__ y_perm) {
+    const int* __restrict__ out_row, __nv_bfloat16* __restrict__ y_perm) {
   extern __shared__ __nv_bfloat16 s_h[];  // [kTok][F]
   const int dblocks = D / kWarps;
   const int e = blockIdx.x / dblocks;
@@ -139,7 +139,8 @@ __global__ void __launch_bounds__(256) moe_decode_down_kernel(
       acc = warp_sum(acc);
       if (lane == 0) {
         const int pos = base + t;
-        y_perm[static_cast<int64_t>(pos) * D + d] = f2bf(acc * __ldg(perm_prob + pos));
+        const int64_t orow = out_row != nullptr ? __ldg(out_row + pos) : pos;
+        y_perm[orow * D + d] = f2bf(acc * __ldg(perm_prob + pos));
       }
     }
   }
@@ -195,7 +196,7 @@ int32_t launch_experts(const void* x, int32_t n_tokens, int32_t d_model, int32_t
                        const int32_t* perm_token, const float* perm_prob,
                        const int32_t* expert_offsets, int32_t n_experts, const void* w13,
                        const void* w2, int32_t ffn, __nv_bfloat16* h, __nv_bfloat16* y,
-                       cudaStream_t s) {
+                       const int32_t* out_row, cudaStream_t s) {
   const int up_smem = kTok * d_model * 2, down_smem = kTok * ffn * 2;
   static int up_attr = 0, down_attr = 0;
   if (up_smem > 48 * 1024 && up_smem > up_attr) {
@@ -215,7 +216,8 @@ int32_t launch_experts(const void* x, int32_t n_tokens, int32_t d_model, int32_t
       static_cast<const __nv_bfloat16*>(w13), d_model, ffn, h);
   count_launch();
   moe_decode_down_kernel<<<n_experts * (d_model / kWarps), 256, down_smem, s>>>(
-      h, perm_prob, expert_offsets, static_cast<const __nv_bfloat16*>(w2), d_model, ffn, y);
+      h, perm_prob, expert_offsets, static_cast<const __nv_bfloat16*>(w2), d_model, ffn, out_row,
+      y);
   count_launch();
   return launch_status();
 }
@@ -257,7 +259,7 @@ LLMYB_API int32_t llmyb_moe_decode_swiglu(const void* x, int32_t n_tokens, int32
   auto* h = static_cast<__nv_bfloat16*>(scratch);
   auto* y = reinterpret_cast<__nv_bfloat16*>(static_cast<uint8_t*>(scratch) + al(rows * ffn * 2));
   st = launch_experts(x, n_tokens, d_model, top_k, perm_token, perm_prob, expert_offsets,
-                      n_experts, w13, w2, ffn, h, y, s);
+                      n_experts, w13, w2, ffn, h, y, nullptr, s);
   if (st) return st;
   const int64_t work = static_cast<int64_t>(n_tokens) * (d_model / 8);
   moe_decode_combine_kernel<<<static_cast<int>(std::min<int64_t>(ceil_div(work, 256), 1184)), 256,
@@ -283,5 +285,26 @@ LLMYB_API int32_t llmyb_moe_decode_experts(const void* x, int32_t n_tokens, int3
   if (!perm_token || !perm_prob || !expert_offsets) return LLMYB_EINVAL;
   return launch_experts(x, n_tokens, d_model, top_k, perm_token, perm_prob, expert_offsets,
                         n_experts, w13, w2, ffn, static_cast<__nv_bfloat16*>(h_scratch),
-                        static_cast<__nv_bfloat16*>(y_rows), static_cast<cudaStream_t>(stream));
+                        static_cast<__nv_bfloat16*>(y_rows), nullptr,
+                        static_cast<cudaStream_t>(stream));
+}
+
+// llmyb_moe_decode_experts with the output row of every plan position given
+// by out_row [n_rows] (y_out[out_row[pos]] = p * expert(x)[pos]).  Used by the
+// expert-parallel path to write expert outputs straight into the return
+// segments (ep.cu).  h_scratch holds [n_rows, F]; n_rows bounds the plan.
+LLMYB_API int32_t llmyb_moe_decode_experts_to(const void* x, int32_t n_rows, int32_t d_model,
+                                              const int32_t* perm_token, const float* perm_prob,
+                                              const int32_t* expert_offsets, int32_t n_experts,
+                                              const void* w13, const void* w2, int32_t ffn,
+                                              void* h_scratch, void* y_out,
+                                              const int32_t* out_row, void* stream) {
+  int32_t st = check_decode_args(x, n_rows, d_model, 1, n_experts, ffn, w13, w2, h_scratch, y_out);
+  if (st) return st;
+  if (n_rows == 0) return LLMYB_OK;
+  if (!perm_token || !perm_prob || !expert_offsets || !out_row) return LLMYB_EINVAL;
+  return launch_experts(x, n_rows, d_model, 1, perm_token, perm_prob, expert_offsets, n_experts,
+                        w13, w2, ffn, static_cast<__nv_bfloat16*>(h_scratch),
+                        static_cast<__nv_bfloat16*>(y_out), out_row,
+                        static_cast<cudaStream_t>(stream));
 }

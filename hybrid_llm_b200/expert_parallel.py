@@ -1,0 +1,127 @@
+"""Expert parallelism: the routed experts sharded over the ranks of a process group.
+
+The reference runs every expert on one device (model/layers/moe.py:29-82).
+Here rank q of W holds experts [q*El, (q+1)*El) (El = E / W), token rows stay
+on the rank that owns their sequence (the attention / GDN mixers run data
+parallel), and each MoE call moves the routed rows to the experts and the
+expert outputs back:
+
+    plan  = kernels.route(...)                       local routing, all E experts
+    y, rp = ep.run(x, plan, w13_local, w2_local)     dispatch, experts, return
+    kernels.add_rmsnorm_routed(streams, y, replace(plan, route_pos=rp), ...)
+
+``run`` packs W fixed-size dispatch segments (capacity C = max_tokens * k
+rows each, so no sizes travel to the host and the step can be replayed as a
+CUDA graph), exchanges them with ``all_to_all_single`` (NCCL between GPUs),
+builds the expert-ordered plan of the received rows, runs the local experts
+with their outputs written straight into the return segments, and exchanges
+those back.  The combine is the routed residual add of the next block.  For a
+route the expert math, its rounding and the order of the k-term sum are those
+of the single-device path, so results are identical for any W.
+
+``ops`` supplies the four device steps; the default runs the llmyb CUDA
+kernels and raises for CPU tensors (there is no CPU fallback).
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, replace
+
+import torch
+import torch.distributed as dist
+
+from . import kernels
+
+
+class CudaEpOps:
+    """The device steps of an expert-parallel MoE call (csrc/ep.cu, moe_decode.cu)."""
+
+    header_rows = staticmethod(kernels.ep_header_rows)
+    dispatch_pack = staticmethod(kernels.ep_dispatch_pack)
+    recv_plan = staticmethod(kernels.ep_recv_plan)
+
+    @staticmethod
+    def experts_to(recv, n_rows, perm_token_l, perm_prob_l, offsets_l, w13, w2, h_scratch, y_out,
+                   out_row) -> None:
+        kernels.moe_decode_experts_to(recv, n_rows, perm_token_l, perm_prob_l, offsets_l, w13, w2,
+                                      h_scratch, y_out, out_row)
+
+
+@dataclass
+class EpResult:
+    y_rows: torch.Tensor      # [W*C, D] bf16: expert outputs of this rank's routes
+    route_pos: torch.Tensor   # [n_routes] int32: row of y_rows for route t*k+s
+
+    def plan_for_combine(self, plan: kernels.RoutePlan) -> kernels.RoutePlan:
+        return replace(plan, route_pos=self.route_pos)
+
+
+class ExpertParallel:
+    """Buffers and call sequence of expert-parallel MoE calls on one rank.
+
+    n_experts: E (divisible by the world size); top_k: k; max_tokens: the most
+    tokens this rank routes in one call (sets the capacity C = max_tokens * k).
+    """
+
+    def __init__(self, n_experts: int, top_k: int, d_model: int, ffn: int, max_tokens: int, *,
+                 group: dist.ProcessGroup | None = None, device: torch.device | str | None = None,
+                 ops=None):
+        if not dist.is_initialized():
+            raise RuntimeError("ExpertParallel needs an initialised torch.distributed group")
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if n_experts % self.world != 0:
+            raise ValueError(f"{n_experts} experts do not split over {self.world} ranks")
+        self.n_experts, self.top_k, self.d_model, self.ffn = n_experts, top_k, d_model, ffn
+        self.experts_per_rank = n_experts // self.world
+        self.capacity = int(max_tokens) * int(top_k)
+        self.ops = CudaEpOps if ops is None else ops
+        self.device = torch.device(device) if device is not None else torch.device(
+            "cuda", torch.cuda.current_device())
+        w, c, d = self.world, self.capacity, d_model
+        self.header = int(self.ops.header_rows(self.experts_per_rank, c, d))
+        bf = dict(dtype=torch.bfloat16, device=self.device)
+        i32 = dict(dtype=torch.int32, device=self.device)
+        self.send = torch.zeros(w * (self.header + c), d, **bf)
+        self.recv = torch.zeros_like(self.send)
+        self.ret_send = torch.zeros(w * c, d, **bf)
+        self.ret_recv = torch.zeros_like(self.ret_send)
+        self.offsets_l = torch.zeros(self.experts_per_rank + 1, **i32)
+        self.perm_token_l = torch.zeros(w * c, **i32)
+        self.perm_prob_l = torch.zeros(w * c, dtype=torch.float32, device=self.device)
+        self.out_row = torch.zeros(w * c, **i32)
+        self.h_scratch = torch.zeros(w * c, ffn, **bf)
+        self.ret_route_pos = torch.zeros(c, **i32)
+
+    @property
+    def expert_range(self) -> tuple[int, int]:
+        lo = self.rank * self.experts_per_rank
+        return lo, lo + self.experts_per_rank
+
+    def _exchange(self, out: torch.Tensor, inp: torch.Tensor) -> None:
+        dist.all_to_all_single(out, inp, group=self.group)
+
+    def run(self, x: torch.Tensor, plan: kernels.RoutePlan, w13_local: torch.Tensor,
+            w2_local: torch.Tensor) -> EpResult:
+        """Routed expert outputs for this rank's routes.
+
+        x [N, D] bf16 (the normalised MoE input), plan from kernels.route over
+        all E experts (N*k <= capacity); w13_local [El, 2F, D] / w2_local
+        [El, D, F] this rank's experts.  Collective: every rank of the group
+        must call it, in the same order.
+        """
+        n_routes = plan.perm_token.numel()
+        if n_routes > self.capacity:
+            raise ValueError(f"{n_routes} routes exceed the capacity {self.capacity}")
+        if w13_local.shape[0] != self.experts_per_rank:
+            raise ValueError("w13_local must hold this rank's experts only")
+        rp = self.ret_route_pos[:n_routes]
+        self.ops.dispatch_pack(x, plan, self.n_experts, self.world, self.capacity, self.send, rp)
+        self._exchange(self.recv, self.send)
+        self.ops.recv_plan(self.recv, self.world, self.capacity, self.experts_per_rank,
+                           self.offsets_l, self.perm_token_l, self.perm_prob_l, self.out_row)
+        self.ops.experts_to(self.recv, self.world * self.capacity, self.perm_token_l,
+                            self.perm_prob_l, self.offsets_l, w13_local, w2_local, self.h_scratch,
+                            self.ret_send, self.out_row)
+        self._exchange(self.ret_recv, self.ret_send)
+        return EpResult(self.ret_recv, rp)

@@ -204,6 +204,61 @@ def moe_decode_experts(x: torch.Tensor, plan: RoutePlan, w13: torch.Tensor, w2: 
     return y_rows
 
 
+def moe_decode_experts_to(x: torch.Tensor, n_rows: int, perm_token: torch.Tensor,
+                          perm_prob: torch.Tensor, offsets: torch.Tensor, w13: torch.Tensor,
+                          w2: torch.Tensor, h_scratch: torch.Tensor, y_out: torch.Tensor,
+                          out_row: torch.Tensor) -> None:
+    """y_out[out_row[pos]] = p * expert(x[perm_token[pos]]) over an explicit plan
+    of at most n_rows positions (offsets [E+1] on the device)."""
+    _require_cuda(x, perm_token, perm_prob, offsets, w13, w2, h_scratch, y_out, out_row)
+    _inplace(y_out, "y_out")
+    _inplace(h_scratch, "h_scratch")
+    e, f2, d = w13.shape
+    if x.shape[-1] != d or h_scratch.numel() < n_rows * (f2 // 2):
+        raise ValueError("moe_decode_experts_to: shape mismatch")
+    _native.call("llmyb_moe_decode_experts_to", _ptr(x), int(n_rows), d, _ptr(perm_token),
+                 _ptr(perm_prob), _ptr(offsets), e, _ptr(w13), _ptr(w2), f2 // 2,
+                 _ptr(h_scratch), _ptr(y_out), _ptr(out_row), _stream())
+
+
+def ep_header_rows(experts_per_rank: int, capacity: int, d_model: int) -> int:
+    """Header rows of an expert-parallel dispatch segment."""
+    h = int(_native.lib().llmyb_ep_header_rows(experts_per_rank, capacity, d_model))
+    if h < 0:
+        raise ValueError("ep_header_rows: invalid arguments")
+    return h
+
+
+def ep_dispatch_pack(x: torch.Tensor, plan: RoutePlan, n_experts: int, world: int,
+                     capacity: int, send: torch.Tensor, ret_route_pos: torch.Tensor) -> None:
+    """Pack the W dispatch segments (send [W*(H+C), D]) from a local plan and
+    write the return-buffer row of every route into ret_route_pos."""
+    _require_cuda(x, send, ret_route_pos)
+    x = x.contiguous()
+    _inplace(send, "send")
+    _inplace(ret_route_pos, "ret_route_pos")
+    n_routes = plan.perm_token.numel()
+    if ret_route_pos.numel() < n_routes:
+        raise ValueError("ret_route_pos too small")
+    _native.call("llmyb_ep_dispatch_pack", _ptr(x), x.shape[-1], _ptr(plan.offsets),
+                 _ptr(plan.perm_token), _ptr(plan.perm_prob), _ptr(plan.route_pos), n_routes,
+                 int(n_experts), int(world), int(capacity), _ptr(send), _ptr(ret_route_pos),
+                 _stream())
+
+
+def ep_recv_plan(recv: torch.Tensor, world: int, capacity: int, experts_per_rank: int,
+                 offsets_l: torch.Tensor, perm_token_l: torch.Tensor, perm_prob_l: torch.Tensor,
+                 out_row: torch.Tensor) -> None:
+    """Expert-ordered plan over the received dispatch segments."""
+    _require_cuda(recv, offsets_l, perm_token_l, perm_prob_l, out_row)
+    for t, n in ((offsets_l, "offsets_l"), (perm_token_l, "perm_token_l"),
+                 (perm_prob_l, "perm_prob_l"), (out_row, "out_row")):
+        _inplace(t, n)
+    _native.call("llmyb_ep_recv_plan", _ptr(recv), recv.shape[-1], int(world), int(capacity),
+                 int(experts_per_rank), _ptr(offsets_l), _ptr(perm_token_l), _ptr(perm_prob_l),
+                 _ptr(out_row), _stream())
+
+
 def add_rmsnorm_routed(streams: torch.Tensor, y_rows: torch.Tensor, plan: RoutePlan,
                        weight: torch.Tensor | None, eps: float, *,
                        out_bf16: torch.Tensor | None = None, out_f32: torch.Tensor | None = None,

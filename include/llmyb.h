@@ -147,6 +147,51 @@ int32_t llmyb_moe_decode_experts(const void* x, int32_t n_tokens, int32_t d_mode
                                  const void* w13, const void* w2, int32_t ffn, void* h_scratch,
                                  void* y_rows, void* stream);
 
+/* llmyb_moe_decode_experts over an explicit plan of n_rows positions (top_k 1)
+ * whose outputs go to y_out[out_row[pos]] instead of y_out[pos]: the
+ * expert-parallel path writes each expert output straight into the return
+ * segment of the rank that sent the row.  h_scratch holds [n_rows, F] bf16.
+ * No counterpart in the reference (its experts all run on one device). */
+int32_t llmyb_moe_decode_experts_to(const void* x, int32_t n_rows, int32_t d_model,
+                                    const int32_t* perm_token, const float* perm_prob,
+                                    const int32_t* expert_offsets, int32_t n_experts,
+                                    const void* w13, const void* w2, int32_t ffn, void* h_scratch,
+                                    void* y_out, const int32_t* out_row, void* stream);
+
+/* -------------------------------------------------- expert parallelism
+ * No counterpart in the reference: it runs model/layers/moe.py:29-82 with all
+ * experts on one device.  These deploy the same routed SwiGLU over W ranks,
+ * rank q owning experts [q*El, (q+1)*El) (El = E / W).  Per MoE call:
+ *   llmyb_ep_dispatch_pack  -> all-to-all of W equal dispatch segments
+ *   llmyb_ep_recv_plan      -> llmyb_moe_decode_experts_to (into return segments)
+ *   all-to-all of W equal return segments -> llmyb_add_rmsnorm_routed with
+ *   ret_route_pos (the combine).
+ * A dispatch segment is H + C bf16 rows of D elements: header rows [0, H)
+ * hold int32 counts[El] then fp32 probs[C]; rows [H, H+C) the routed token
+ * rows in plan (expert) order.  A return segment is C rows.  C (capacity) is
+ * at least the sender's route count N*k. */
+int32_t llmyb_ep_header_rows(int32_t experts_per_rank, int32_t capacity, int32_t d_model);
+
+/* Pack the W dispatch segments into send [W, H+C, D] from the local plan of
+ * llmyb_route (offsets [E+1], perm_token, perm_prob, route_pos [n_routes]);
+ * ret_route_pos [n_routes] gets the row of the return buffer [W*C, D] that
+ * will hold each route's expert output. */
+int32_t llmyb_ep_dispatch_pack(const void* x, int32_t d_model, const int32_t* offsets,
+                               const int32_t* perm_token, const float* perm_prob,
+                               const int32_t* route_pos, int32_t n_routes, int32_t n_experts,
+                               int32_t world, int32_t capacity, void* send,
+                               int32_t* ret_route_pos, void* stream);
+
+/* Expert-ordered plan over the received segments recv [W, H+C, D]:
+ * offsets_l [El+1]; perm_token_l (row of recv viewed as [W*(H+C), D]),
+ * perm_prob_l and out_row (row of the return buffer [W*C, D]) [W*C], the
+ * first offsets_l[El] entries valid.  Rows of one expert are ordered by
+ * source rank, then by the source's plan order.  W <= 64, El <= 256,
+ * W*El <= 4096. */
+int32_t llmyb_ep_recv_plan(const void* recv, int32_t d_model, int32_t world, int32_t capacity,
+                           int32_t experts_per_rank, int32_t* offsets_l, int32_t* perm_token_l,
+                           float* perm_prob_l, int32_t* out_row, void* stream);
+
 /* ------------------------------------------------------ gated delta rule
  * Replaces GatedDeltaNet's recurrence (model/layers/gated_deltanet.py:140-149
  * and the seams _triton_gdn_scan/_triton_gdn_step at :179-235), the Triton
