@@ -287,6 +287,97 @@ def secondary_prefill(p: dict, reps: int = 5) -> dict:
             "prefill_tok_s": b * t / (ta + tg)}
 
 
+def ep_decode_bytes_per_step(cfg, batch_local: int, world: int, weights) -> float:
+    """Algorithmic HBM bytes one rank touches per decode step of the large
+    expert-parallel config: its expert shard (every local expert is routed
+    to at batch 64 x top-8 over 64 experts), the dense block weights (kept on
+    every rank), the KV windows and GDN states of its own sequences, the head."""
+    d = cfg.d_model
+    nb = lambda t: t.numel() * t.element_size()
+    dense = 0
+    for blk in weights.blocks:
+        m = blk.mixer
+        dense += (nb(m.w_in) + nb(m.w_out) + nb(m.conv)) if blk.kind == "gdn" else \
+            (nb(m.w_in) + nb(m.w_o))
+        dense += nb(blk.moe.router) + nb(blk.moe.w13) + nb(blk.moe.w2)
+    dense *= cfg.num_loops
+    n_csa = sum(1 for j in range(cfg.n_blocks) if cfg.block_kind(j) == "csa") * cfg.num_loops
+    n_gdn = cfg.n_blocks * cfg.num_loops - n_csa
+    kv = batch_local * n_csa * cfg.csa_window * (cfg.csa_heads * cfg.csa_head_dim + d) * 2
+    gdn_state = batch_local * n_gdn * cfg.gdn_heads * cfg.gdn_key_dim * cfg.gdn_value_dim * 4 * 2
+    head = cfg.vocab_size * d * 2 + d * d * 2
+    return float(dense + kv + gdn_state + head)
+
+
+def secondary_ep_decode(p: dict, steps: int = 10, warmup: int = 3, global_batch: int = 64,
+                        context: int = 4096) -> dict:
+    """Large expert-parallel config decode: d 2048, 24 blocks, 64 experts top-8,
+    3 loops, vocab 64000, global batch 64 split over the ranks; experts sharded
+    64/W per rank (ExpertParallel, all-to-all over NCCL) for W > 1.  The
+    4096-token context is a synthetic recurrent state (RecurrentState.
+    fill_synthetic): decode cost does not depend on the context's values.
+    Collective when torch.distributed is initialised: every rank calls it."""
+    import torch
+    import torch.distributed as dist
+
+    from hybrid_llm_b200 import kernels
+    from hybrid_llm_b200.config import large_ep_config
+    from hybrid_llm_b200.expert_parallel import ExpertParallel
+    from hybrid_llm_b200.model import GreedyDecoder, LoopedHybridModel
+    from hybrid_llm_b200.state import RecurrentState
+    from hybrid_llm_b200.weights import ModelWeights, synthetic_state_dict
+
+    world = dist.get_world_size() if dist.is_initialized() else 1
+    rank = dist.get_rank() if dist.is_initialized() else 0
+    cfg = large_ep_config()
+    bl = global_batch // world
+    ep = None
+    if world > 1:
+        ep = ExpertParallel(cfg.moe_experts, cfg.moe_top_k, cfg.d_model, cfg.moe_hidden, bl)
+    weights = ModelWeights.from_state_dict(cfg, synthetic_state_dict(cfg, seed=0, device="cuda"),
+                                           "cuda", expert_range=None if ep is None else ep.expert_range)
+    model = LoopedHybridModel(weights, ep=ep)
+    state = RecurrentState(cfg, bl, "cuda")
+    state.fill_synthetic(context, seed=rank)
+    dec = GreedyDecoder(model, state, use_graph=False)
+    g = torch.Generator(device="cpu").manual_seed(rank)
+    dec.prime(torch.randint(0, cfg.vocab_size, (bl,), generator=g).cuda())
+    for _ in range(warmup):
+        dec.step()
+    torch.cuda.synchronize()
+    n0 = kernels.launch_count()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    a, b = _events()
+    torch.cuda.nvtx.range_push("ep_decode_timed")
+    a.record()
+    for _ in range(steps):
+        dec.step()
+    b.record()
+    torch.cuda.nvtx.range_pop()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    t_ms = a.elapsed_time(b)
+    launches = (kernels.launch_count() - n0) // steps
+    if world > 1:
+        tt = torch.tensor([t_ms], device="cuda")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        t_ms = float(tt.item())
+    step_s = t_ms * 1e-3 / steps
+    touched = ep_decode_bytes_per_step(cfg, bl, world, weights)
+    achieved = touched / step_s / 1e9
+    return {"workload": "large expert-parallel config: d 2048, 24 blocks, 64 experts top-8, "
+                        "3 loops, vocab 64000, batch 64, 4096-token synthetic context",
+            "n_gpus": world, "batch_per_rank": bl, "parallelism": f"ep{world}" if world > 1 else
+            "single", "exchange": "NCCL all_to_all_single" if world > 1 else None,
+            "graph": False, "tok_s": global_batch / step_s, "ms_per_step": step_s * 1e3,
+            "llmyb_launches_per_step": launches,
+            "hbm_bytes_per_step_per_rank": touched, "achieved_gbs_per_rank": achieved,
+            "frac_of_hbm": achieved / p["hbm_gbs"]}
+
+
 def run_ours(args) -> None:
     import numpy as np
     import torch
@@ -445,13 +536,26 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--only", choices=["moe_layer", "long_prefill"], default=None,
+    ap.add_argument("--only", choices=["moe_layer", "long_prefill", "ep_decode"], default=None,
                     help="run one secondary workload alone (used for kernel profiles)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.only == "ep_decode":
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+        if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+        res = secondary_ep_decode(peaks(), steps=args.steps, warmup=args.warmup)
+        if not dist.is_initialized() or dist.get_rank() == 0:
+            print(json.dumps({"only": args.only, **res}), flush=True)
+        if dist.is_initialized():
+            dist.destroy_process_group()
     elif args.only:
         import torch
         torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))

@@ -45,6 +45,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "llmyb_moe_grouped_scratch_bytes": (I64, [I32, I32, I32, I32]),
     "llmyb_moe_grouped_swiglu": (I32, [P, I32, I32, I32, P, P, P, P, P, I32, I32, P, P, I32, P, P, P,
                                        P]),
+    "llmyb_moe_grouped_experts_to": (I32, [P, I32, I32, P, P, P, P, I32, I32, P, P, I32, P, P, P, P,
+                                           P]),
     "llmyb_moe_decode_scratch_bytes": (I64, [I32, I32, I32, I32]),
     "llmyb_moe_decode_swiglu": (I32, [P, I32, I32, I32, P, P, P, P, I32, P, P, I32, P, P, P]),
     "llmyb_moe_decode_experts": (I32, [P, I32, I32, I32, P, P, P, I32, P, P, I32, P, P, P]),
@@ -52,7 +54,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     # expert parallelism
     "llmyb_ep_header_rows": (I32, [I32, I32, I32]),
     "llmyb_ep_dispatch_pack": (I32, [P, I32, P, P, P, P, I32, I32, I32, I32, P, P, P]),
-    "llmyb_ep_recv_plan": (I32, [P, I32, I32, I32, I32, P, P, P, P, P]),
+    "llmyb_ep_recv_plan": (I32, [P, I32, I32, I32, I32, I32, P, P, P, P, P, P]),
     # gated delta rule
     "llmyb_gdn_activate": (I32, [P, I64, I32, I32, I32, I32, P, P]),
     "llmyb_gdn_step": (I32, [P, I64, P, I64, P, I64, P, I64, P, I64, P, P, P, I32, I32, I32, I32,

@@ -91,9 +91,9 @@ __global__ void ep_pack_kernel(const __nv_bfloat16* __restrict__ x, int D,
 // source rank, then by their order in the source's segment (which is the
 // source's plan order), so the layout is deterministic.
 __global__ void __launch_bounds__(256) ep_recv_plan_kernel(
-    const __nv_bfloat16* __restrict__ recv, int D, int W, int C, int H, int El,
-    int* __restrict__ offsets_l, int* __restrict__ perm_token_l, float* __restrict__ perm_prob_l,
-    int* __restrict__ out_row) {
+    const __nv_bfloat16* __restrict__ recv, int D, int W, int C, int H, int El, int tile_m,
+    int* __restrict__ offsets_l, int* __restrict__ tile_offsets_l, int* __restrict__ perm_token_l,
+    float* __restrict__ perm_prob_l, int* __restrict__ out_row) {
   __shared__ int s_base[kMaxPlanCells];   // [W][El] first row of expert e in p's segment
   __shared__ int s_src[kMaxPlanCells];    // [W][El] rows of expert e from ranks < p
   __shared__ int s_off[257];              // local expert offsets (El <= 256)
@@ -134,8 +134,17 @@ __global__ void __launch_bounds__(256) ep_recv_plan_kernel(
     for (int e = 0; e < El; ++e) s_off[e + 1] += s_off[e];
   }
   __syncthreads();
-  if (blockIdx.x == 0)
+  if (blockIdx.x == 0) {
     for (int e = threadIdx.x; e <= El; e += blockDim.x) offsets_l[e] = s_off[e];
+    if (tile_offsets_l != nullptr && threadIdx.x == 0) {
+      int t = 0;
+      tile_offsets_l[0] = 0;
+      for (int e = 0; e < El; ++e) {
+        t += (s_off[e + 1] - s_off[e] + tile_m - 1) / tile_m;
+        tile_offsets_l[e + 1] = t;
+      }
+    }
+  }
   const int64_t tid = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t slot = tid; slot < static_cast<int64_t>(W) * C; slot += stride) {
@@ -198,15 +207,18 @@ LLMYB_API int32_t llmyb_ep_dispatch_pack(const void* x, int32_t d_model, const i
 }
 
 // Expert-ordered plan over the received dispatch segments: offsets_l [El+1],
+// tile_offsets_l [El+1] (tile_m-row tiles per expert, nullable),
 // perm_token_l / perm_prob_l / out_row [W*C] (first offsets_l[El] entries
 // valid).  perm_token_l indexes recv viewed as [W*(H+C), D]; out_row is the
 // row of the return buffer [W*C, D] for each plan position.
 LLMYB_API int32_t llmyb_ep_recv_plan(const void* recv, int32_t d_model, int32_t world,
-                                     int32_t capacity, int32_t experts_per_rank,
-                                     int32_t* offsets_l, int32_t* perm_token_l,
-                                     float* perm_prob_l, int32_t* out_row, void* stream) {
+                                     int32_t capacity, int32_t experts_per_rank, int32_t tile_m,
+                                     int32_t* offsets_l, int32_t* tile_offsets_l,
+                                     int32_t* perm_token_l, float* perm_prob_l, int32_t* out_row,
+                                     void* stream) {
   if (!recv || !offsets_l || !perm_token_l || !perm_prob_l || !out_row) return LLMYB_EINVAL;
-  if (d_model <= 0 || world <= 0 || capacity <= 0 || experts_per_rank <= 0) return LLMYB_EINVAL;
+  if (d_model <= 0 || world <= 0 || capacity <= 0 || experts_per_rank <= 0 || tile_m <= 0)
+    return LLMYB_EINVAL;
   if (world > 64 || experts_per_rank > 256 || world * experts_per_rank > kMaxPlanCells)
     return LLMYB_EUNSUPPORTED;
   const int H = llmyb_ep_header_rows(experts_per_rank, capacity, d_model);
@@ -215,7 +227,7 @@ LLMYB_API int32_t llmyb_ep_recv_plan(const void* recv, int32_t d_model, int32_t 
   const int grid = static_cast<int>(std::min<int64_t>(std::max<int64_t>(ceil_div(slots, 256), 1), 296));
   ep_recv_plan_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const __nv_bfloat16*>(recv), d_model, world, capacity, H, experts_per_rank,
-      offsets_l, perm_token_l, perm_prob_l, out_row);
+      tile_m, offsets_l, tile_offsets_l, perm_token_l, perm_prob_l, out_row);
   count_launch();
   return launch_status();
 }

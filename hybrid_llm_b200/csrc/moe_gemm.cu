@@ -142,7 +142,7 @@ __global__ void __launch_bounds__(256, 1) moe_gemm_kernel(
     const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
     const int* __restrict__ expert_offsets, const int* __restrict__ tile_offsets, int E, int K,
     int n_weight_rows, __nv_bfloat16* __restrict__ out, int out_ld,
-    const float* __restrict__ row_scale, int32_t* dev_status) {
+    const float* __restrict__ row_scale, const int* __restrict__ out_row, int32_t* dev_status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -275,7 +275,8 @@ __global__ void __launch_bounds__(256, 1) moe_gemm_kernel(
       const bool valid = r < ti.rows_valid;
       const int64_t row = static_cast<int64_t>(ti.row0) + r;
       const float scale = (EPI == kScale && valid) ? __ldg(row_scale + row) : 0.0f;
-      __nv_bfloat16* dst = out + row * out_ld + ti.n_tile * (EPI == kSwiGLU ? BN / 2 : BN);
+      const int64_t orow = (out_row != nullptr && valid) ? __ldg(out_row + row) : row;
+      __nv_bfloat16* dst = out + orow * out_ld + ti.n_tile * (EPI == kSwiGLU ? BN / 2 : BN);
       epilogue_rows<EPI>(t_row, valid, scale, dst);
       sm100::tc_fence_before();
       sm100::mbar_arrive(&tmem_empty[acc]);
@@ -331,7 +332,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1) moe_gemm_pai
     const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
     const int* __restrict__ expert_offsets, const int* __restrict__ tile_offsets, int E, int K,
     int n_weight_rows, __nv_bfloat16* __restrict__ out, int out_ld,
-    const float* __restrict__ row_scale, int32_t* dev_status) {
+    const float* __restrict__ row_scale, const int* __restrict__ out_row, int32_t* dev_status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -469,7 +470,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1) moe_gemm_pai
       const bool valid = r < my_rows;
       const int64_t row = static_cast<int64_t>(ti.row0) + static_cast<int>(rank) * PBM + r;
       const float scale = (EPI == kScale && valid) ? __ldg(row_scale + row) : 0.0f;
-      __nv_bfloat16* dst = out + row * out_ld + ti.n_tile * (EPI == kSwiGLU ? PBN / 2 : PBN);
+      const int64_t orow = (out_row != nullptr && valid) ? __ldg(out_row + row) : row;
+      __nv_bfloat16* dst = out + orow * out_ld + ti.n_tile * (EPI == kSwiGLU ? PBN / 2 : PBN);
       epilogue_rows<EPI>(t_row, valid, scale, dst);
       sm100::tc_fence_before();
       __syncwarp();
@@ -489,11 +491,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1) moe_gemm_pai
   }
 }
 
-// x_perm[pos, :] = x[perm_token[pos], :]   (16-byte vectors)
+// x_perm[pos, :] = x[perm_token[pos], :]   (16-byte vectors), pos < rows and,
+// when valid_rows is given, pos < *valid_rows (a count held on the device)
 __global__ void gather_rows_kernel(const __nv_bfloat16* __restrict__ x,
                                    const int* __restrict__ perm_token, int64_t rows, int D,
-                                   __nv_bfloat16* __restrict__ x_perm) {
+                                   __nv_bfloat16* __restrict__ x_perm,
+                                   const int* __restrict__ valid_rows) {
   const int vec = D / 8;
+  if (valid_rows != nullptr) rows = min(rows, static_cast<int64_t>(__ldg(valid_rows)));
   const int64_t total = rows * vec;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -581,6 +586,64 @@ int32_t ensure_gemm_attrs() {
   return LLMYB_OK;
 }
 
+// gather -> GEMM1 (SwiGLU) -> GEMM2 (probability scale) for a plan of `rows`
+// positions; GEMM2 writes y[out_row ? out_row[pos] : pos].  valid_count: the
+// gather stops at expert_offsets[E] (read on the device) instead of `rows`.
+int32_t run_grouped(const __nv_bfloat16* x, int32_t d_model, int64_t rows,
+                    const int32_t* perm_token, const float* perm_prob,
+                    const int32_t* expert_offsets, const int32_t* tile_offsets, int32_t tile_m,
+                    int32_t n_experts, const __nv_bfloat16* w13, const __nv_bfloat16* w2,
+                    int32_t ffn, __nv_bfloat16* x_perm, __nv_bfloat16* h_perm, __nv_bfloat16* y,
+                    const int32_t* out_row, bool valid_count, int32_t* dev_status,
+                    cudaStream_t s) {
+  int32_t st = ensure_gemm_attrs();
+  if (st) return st;
+  gather_rows_kernel<<<grid_for(rows * (d_model / 8), 256), 256, 0, s>>>(
+      x, perm_token, rows, d_model, x_perm, valid_count ? expert_offsets + n_experts : nullptr);
+  count_launch();
+
+  const bool pair = tile_m == 2 * PBM;
+  const uint32_t b_box = pair ? PBN / 2 : BN;
+  CUtensorMap ma1, mb1, ma2, mb2;
+  if (!make_bf16_2d_map(&ma1, x_perm, rows, d_model, d_model, BM, BK) ||
+      !make_bf16_2d_map(&mb1, w13, static_cast<uint64_t>(n_experts) * 2 * ffn, d_model, d_model,
+                        b_box, BK) ||
+      !make_bf16_2d_map(&ma2, h_perm, rows, ffn, ffn, BM, BK) ||
+      !make_bf16_2d_map(&mb2, w2, static_cast<uint64_t>(n_experts) * d_model, ffn, ffn, b_box,
+                        BK))
+    return LLMYB_EUNSUPPORTED;
+
+  // upper bound of the m-tile count without reading device memory
+  const int64_t m_tiles_max = ceil_div(rows, tile_m) + n_experts;
+  const int sms = num_sms();
+  if (pair) {
+    const int clusters = sms / 2;
+    const int grid1 = 2 * static_cast<int>(std::min<int64_t>(clusters, m_tiles_max * (2 * ffn / PBN)));
+    const int grid2 = 2 * static_cast<int>(std::min<int64_t>(clusters, m_tiles_max * (d_model / PBN)));
+    moe_gemm_pair_kernel<kSwiGLU><<<grid1, 256, P_SMEM, s>>>(
+        ma1, mb1, expert_offsets, tile_offsets, n_experts, d_model, 2 * ffn, h_perm, ffn, nullptr,
+        nullptr, dev_status);
+    count_launch();
+    moe_gemm_pair_kernel<kScale><<<grid2, 256, P_SMEM, s>>>(
+        ma2, mb2, expert_offsets, tile_offsets, n_experts, ffn, d_model, y, d_model, perm_prob,
+        out_row, dev_status);
+    count_launch();
+  } else {
+    const int grid1 = static_cast<int>(std::min<int64_t>(sms, m_tiles_max * (2 * ffn / BN)));
+    const int grid2 = static_cast<int>(std::min<int64_t>(sms, m_tiles_max * (d_model / BN)));
+    moe_gemm_kernel<kSwiGLU><<<grid1, 256, GEMM_SMEM, s>>>(ma1, mb1, expert_offsets,
+                                                            tile_offsets, n_experts, d_model,
+                                                            2 * ffn, h_perm, ffn, nullptr, nullptr,
+                                                            dev_status);
+    count_launch();
+    moe_gemm_kernel<kScale><<<grid2, 256, GEMM_SMEM, s>>>(ma2, mb2, expert_offsets, tile_offsets,
+                                                           n_experts, ffn, d_model, y, d_model,
+                                                           perm_prob, out_row, dev_status);
+    count_launch();
+  }
+  return launch_status();
+}
+
 }  // namespace
 }  // namespace llmyb
 
@@ -640,52 +703,43 @@ LLMYB_API int32_t llmyb_moe_grouped_swiglu(
   __nv_bfloat16* h_perm = reinterpret_cast<__nv_bfloat16*>(sp + al(rows * d_model * 2));
   __nv_bfloat16* y_perm =
       reinterpret_cast<__nv_bfloat16*>(sp + al(rows * d_model * 2) + al(rows * ffn * 2));
-
-  gather_rows_kernel<<<grid_for(rows * (d_model / 8), 256), 256, 0, s>>>(x, perm_token, rows,
-                                                                         d_model, x_perm);
-  count_launch();
-
-  const bool pair = tile_m == 2 * PBM;
-  const uint32_t b_box = pair ? PBN / 2 : BN;
-  CUtensorMap ma1, mb1, ma2, mb2;
-  if (!make_bf16_2d_map(&ma1, x_perm, rows, d_model, d_model, BM, BK) ||
-      !make_bf16_2d_map(&mb1, w13, static_cast<uint64_t>(n_experts) * 2 * ffn, d_model, d_model,
-                        b_box, BK) ||
-      !make_bf16_2d_map(&ma2, h_perm, rows, ffn, ffn, BM, BK) ||
-      !make_bf16_2d_map(&mb2, w2, static_cast<uint64_t>(n_experts) * d_model, ffn, ffn, b_box,
-                        BK))
-    return LLMYB_EUNSUPPORTED;
-
-  // upper bound of the m-tile count without reading device memory
-  const int64_t m_tiles_max = ceil_div(rows, tile_m) + n_experts;
-  const int sms = num_sms();
-  if (pair) {
-    const int clusters = sms / 2;
-    const int grid1 = 2 * static_cast<int>(std::min<int64_t>(clusters, m_tiles_max * (2 * ffn / PBN)));
-    const int grid2 = 2 * static_cast<int>(std::min<int64_t>(clusters, m_tiles_max * (d_model / PBN)));
-    moe_gemm_pair_kernel<kSwiGLU><<<grid1, 256, P_SMEM, s>>>(
-        ma1, mb1, expert_offsets, tile_offsets, n_experts, d_model, 2 * ffn, h_perm, ffn, nullptr,
-        dev_status);
-    count_launch();
-    moe_gemm_pair_kernel<kScale><<<grid2, 256, P_SMEM, s>>>(
-        ma2, mb2, expert_offsets, tile_offsets, n_experts, ffn, d_model, y_perm, d_model,
-        perm_prob, dev_status);
-    count_launch();
-  } else {
-    const int grid1 = static_cast<int>(std::min<int64_t>(sms, m_tiles_max * (2 * ffn / BN)));
-    const int grid2 = static_cast<int>(std::min<int64_t>(sms, m_tiles_max * (d_model / BN)));
-    moe_gemm_kernel<kSwiGLU><<<grid1, 256, GEMM_SMEM, s>>>(ma1, mb1, expert_offsets,
-                                                            tile_offsets, n_experts, d_model,
-                                                            2 * ffn, h_perm, ffn, nullptr,
-                                                            dev_status);
-    count_launch();
-    moe_gemm_kernel<kScale><<<grid2, 256, GEMM_SMEM, s>>>(ma2, mb2, expert_offsets, tile_offsets,
-                                                           n_experts, ffn, d_model, y_perm,
-                                                           d_model, perm_prob, dev_status);
-    count_launch();
-  }
+  st = run_grouped(x, d_model, rows, perm_token, perm_prob, expert_offsets, tile_offsets, tile_m,
+                   n_experts, w13, w2, ffn, x_perm, h_perm, y_perm, nullptr, false, dev_status, s);
+  if (st) return st;
   combine_rows_kernel<<<grid_for(static_cast<int64_t>(n_tokens) * (d_model / 8), 256), 256, 0,
                         s>>>(y_perm, route_pos, n_tokens, top_k, d_model, out);
   count_launch();
   return launch_status();
+}
+
+// Routed expert outputs per plan position on the tcgen05 grouped GEMMs, without
+// the combine: y_out[out_row ? out_row[pos] : pos] = perm_prob[pos] *
+// expert(x[perm_token[pos]]) for pos < expert_offsets[E] (read on the device;
+// n_rows bounds it and sizes the scratch of llmyb_moe_grouped_scratch_bytes(
+// n_rows, 1, D, F)).  tile_offsets counts tile_m-row tiles per expert.
+LLMYB_API int32_t llmyb_moe_grouped_experts_to(
+    const __nv_bfloat16* x, int32_t d_model, int32_t n_rows, const int32_t* perm_token,
+    const float* perm_prob, const int32_t* expert_offsets, const int32_t* tile_offsets,
+    int32_t tile_m, int32_t n_experts, const __nv_bfloat16* w13, const __nv_bfloat16* w2,
+    int32_t ffn, void* scratch, __nv_bfloat16* y_out, const int32_t* out_row,
+    int32_t* dev_status, void* stream) {
+  if (n_rows < 0 || d_model <= 0 || n_experts <= 0 || ffn <= 0) return LLMYB_EINVAL;
+  if (n_rows == 0) return LLMYB_OK;
+  if (!x || !perm_token || !perm_prob || !expert_offsets || !tile_offsets || !w13 || !w2 ||
+      !scratch || !y_out || !dev_status)
+    return LLMYB_EINVAL;
+  if (d_model % BN != 0 || ffn % (BN / 2) != 0 || ffn % BK != 0 || d_model % BK != 0)
+    return LLMYB_EUNSUPPORTED;
+  if (tile_m != BM && tile_m != 2 * PBM) return LLMYB_EINVAL;
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y_out) |
+       reinterpret_cast<uintptr_t>(scratch)) & 15u)
+    return LLMYB_EINVAL;
+  const int64_t rows = n_rows;
+  auto al = [](int64_t b) { return (b + 255) / 256 * 256; };
+  uint8_t* sp = static_cast<uint8_t*>(scratch);
+  __nv_bfloat16* x_perm = reinterpret_cast<__nv_bfloat16*>(sp);
+  __nv_bfloat16* h_perm = reinterpret_cast<__nv_bfloat16*>(sp + al(rows * d_model * 2));
+  return run_grouped(x, d_model, rows, perm_token, perm_prob, expert_offsets, tile_offsets, tile_m,
+                     n_experts, w13, w2, ffn, x_perm, h_perm, y_out, out_row, true, dev_status,
+                     static_cast<cudaStream_t>(stream));
 }

@@ -33,17 +33,38 @@ from . import kernels
 
 
 class CudaEpOps:
-    """The device steps of an expert-parallel MoE call (csrc/ep.cu, moe_decode.cu)."""
+    """The device steps of an expert-parallel MoE call (csrc/ep.cu, moe_gemm.cu,
+    moe_decode.cu); each takes the ExpertParallel whose buffers it fills."""
 
     header_rows = staticmethod(kernels.ep_header_rows)
-    dispatch_pack = staticmethod(kernels.ep_dispatch_pack)
-    recv_plan = staticmethod(kernels.ep_recv_plan)
 
     @staticmethod
-    def experts_to(recv, n_rows, perm_token_l, perm_prob_l, offsets_l, w13, w2, h_scratch, y_out,
-                   out_row) -> None:
-        kernels.moe_decode_experts_to(recv, n_rows, perm_token_l, perm_prob_l, offsets_l, w13, w2,
-                                      h_scratch, y_out, out_row)
+    def scratch_bytes(ep: "ExpertParallel") -> int:
+        # the grouped path's scratch also covers the decode kernels' [rows, F]
+        return kernels.grouped_scratch_bytes(ep.world * ep.capacity, ep.d_model, ep.ffn)
+
+    @staticmethod
+    def dispatch_pack(ep: "ExpertParallel", x, plan, ret_route_pos) -> None:
+        kernels.ep_dispatch_pack(x, plan, ep.n_experts, ep.world, ep.capacity, ep.send,
+                                 ret_route_pos)
+
+    @staticmethod
+    def recv_plan(ep: "ExpertParallel") -> None:
+        kernels.ep_recv_plan(ep.recv, ep.world, ep.capacity, ep.experts_per_rank, ep.offsets_l,
+                             ep.perm_token_l, ep.perm_prob_l, ep.out_row,
+                             tile_offsets_l=ep.tile_offsets_l, tile_m=ep.tile_m)
+
+    @staticmethod
+    def experts_to(ep: "ExpertParallel", w13, w2, grouped: bool) -> None:
+        rows = ep.world * ep.capacity
+        if grouped:
+            kernels.moe_grouped_experts_to(ep.recv, rows, ep.perm_token_l, ep.perm_prob_l,
+                                           ep.offsets_l, ep.tile_offsets_l, ep.tile_m, w13, w2,
+                                           ep.scratch, ep.ret_send, ep.out_row)
+        else:
+            kernels.moe_decode_experts_to(ep.recv, rows, ep.perm_token_l, ep.perm_prob_l,
+                                          ep.offsets_l, w13, w2, ep.scratch.view(torch.bfloat16),
+                                          ep.ret_send, ep.out_row)
 
 
 @dataclass
@@ -90,7 +111,10 @@ class ExpertParallel:
         self.perm_token_l = torch.zeros(w * c, **i32)
         self.perm_prob_l = torch.zeros(w * c, dtype=torch.float32, device=self.device)
         self.out_row = torch.zeros(w * c, **i32)
-        self.h_scratch = torch.zeros(w * c, ffn, **bf)
+        self.tile_offsets_l = torch.zeros(self.experts_per_rank + 1, **i32)
+        self.tile_m = 128
+        self.scratch = torch.zeros(int(self.ops.scratch_bytes(self)), dtype=torch.uint8,
+                                   device=self.device)
         self.ret_route_pos = torch.zeros(c, **i32)
 
     @property
@@ -102,13 +126,16 @@ class ExpertParallel:
         dist.all_to_all_single(out, inp, group=self.group)
 
     def run(self, x: torch.Tensor, plan: kernels.RoutePlan, w13_local: torch.Tensor,
-            w2_local: torch.Tensor) -> EpResult:
+            w2_local: torch.Tensor, path: str = "auto") -> EpResult:
         """Routed expert outputs for this rank's routes.
 
         x [N, D] bf16 (the normalised MoE input), plan from kernels.route over
         all E experts (N*k <= capacity); w13_local [El, 2F, D] / w2_local
-        [El, D, F] this rank's experts.  Collective: every rank of the group
-        must call it, in the same order.
+        [El, D, F] this rank's experts.  path: "grouped" (tcgen05 GEMMs),
+        "decode" (weight streaming) or "auto", which picks from the capacity
+        so that every rank makes the same choice (W*C rows over W*El experts,
+        the single-device rule at a full batch).  Collective: every rank of
+        the group must call it, in the same order.
         """
         n_routes = plan.perm_token.numel()
         if n_routes > self.capacity:
@@ -116,12 +143,13 @@ class ExpertParallel:
         if w13_local.shape[0] != self.experts_per_rank:
             raise ValueError("w13_local must hold this rank's experts only")
         rp = self.ret_route_pos[:n_routes]
-        self.ops.dispatch_pack(x, plan, self.n_experts, self.world, self.capacity, self.send, rp)
+        self.ops.dispatch_pack(self, x, plan, rp)
         self._exchange(self.recv, self.send)
-        self.ops.recv_plan(self.recv, self.world, self.capacity, self.experts_per_rank,
-                           self.offsets_l, self.perm_token_l, self.perm_prob_l, self.out_row)
-        self.ops.experts_to(self.recv, self.world * self.capacity, self.perm_token_l,
-                            self.perm_prob_l, self.offsets_l, w13_local, w2_local, self.h_scratch,
-                            self.ret_send, self.out_row)
+        self.ops.recv_plan(self)
+        if path not in ("auto", "grouped", "decode"):
+            raise ValueError(f"unknown expert path {path!r}")
+        grouped = path == "grouped" or (
+            path == "auto" and kernels.use_grouped_rows(self.capacity, self.experts_per_rank))
+        self.ops.experts_to(self, w13_local, w2_local, grouped)
         self._exchange(self.ret_recv, self.ret_send)
         return EpResult(self.ret_recv, rp)

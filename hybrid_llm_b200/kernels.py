@@ -158,7 +158,7 @@ def moe_plan(topk_idx: torch.Tensor, topk_prob: torch.Tensor, n_experts: int, *,
 
 def route_fused(streams: torch.Tensor, delta: torch.Tensor | None, ffn_norm: torch.Tensor,
                 router_norm: torch.Tensor, w_router: torch.Tensor, k: int, eps: float,
-                m_bf: torch.Tensor) -> RoutePlan:
+                m_bf: torch.Tensor, tile_m: int = TILE_M) -> RoutePlan:
     """Decode router: streams += delta; m_bf = RMSNorm_ffn(streams); top-k over
     w_router . RMSNorm_router(m) (fp32) and the dispatch plan, one launch."""
     _require_cuda(streams, delta, ffn_norm, router_norm, w_router, m_bf)
@@ -172,11 +172,11 @@ def route_fused(streams: torch.Tensor, delta: torch.Tensor | None, ffn_norm: tor
     b = _plan_buffers(n, e, k, dev, False)
     delta = None if delta is None else delta.contiguous()
     _native.call("llmyb_route_fused", _ptr(streams), _ptr(delta), n, d, _ptr(ffn_norm),
-                 _ptr(router_norm), _ptr(w_router), float(eps), e, k, TILE_M, _ptr(m_bf),
+                 _ptr(router_norm), _ptr(w_router), float(eps), e, k, int(tile_m), _ptr(m_bf),
                  _ptr(idx), _ptr(prob), _ptr(b["counts"]), _ptr(b["offsets"]),
                  _ptr(b["tile_offsets"]), _ptr(b["perm_token"]), _ptr(b["perm_prob"]),
                  _ptr(b["route_pos"]), _stream())
-    return RoutePlan(idx, prob, **b)
+    return RoutePlan(idx, prob, **b, tile_m=tile_m)
 
 
 def route_fused_supported(n: int, e: int, k: int, d: int) -> bool:
@@ -248,15 +248,67 @@ def ep_dispatch_pack(x: torch.Tensor, plan: RoutePlan, n_experts: int, world: in
 
 def ep_recv_plan(recv: torch.Tensor, world: int, capacity: int, experts_per_rank: int,
                  offsets_l: torch.Tensor, perm_token_l: torch.Tensor, perm_prob_l: torch.Tensor,
-                 out_row: torch.Tensor) -> None:
+                 out_row: torch.Tensor, tile_offsets_l: torch.Tensor | None = None,
+                 tile_m: int = 128) -> None:
     """Expert-ordered plan over the received dispatch segments."""
-    _require_cuda(recv, offsets_l, perm_token_l, perm_prob_l, out_row)
+    _require_cuda(recv, offsets_l, perm_token_l, perm_prob_l, out_row, tile_offsets_l)
     for t, n in ((offsets_l, "offsets_l"), (perm_token_l, "perm_token_l"),
                  (perm_prob_l, "perm_prob_l"), (out_row, "out_row")):
         _inplace(t, n)
     _native.call("llmyb_ep_recv_plan", _ptr(recv), recv.shape[-1], int(world), int(capacity),
-                 int(experts_per_rank), _ptr(offsets_l), _ptr(perm_token_l), _ptr(perm_prob_l),
-                 _ptr(out_row), _stream())
+                 int(experts_per_rank), int(tile_m), _ptr(offsets_l), _ptr(tile_offsets_l),
+                 _ptr(perm_token_l), _ptr(perm_prob_l), _ptr(out_row), _stream())
+
+
+def grouped_scratch_bytes(n_rows: int, d_model: int, ffn: int) -> int:
+    """Scratch of moe_grouped_experts_to for a plan of n_rows positions."""
+    return int(_native.lib().llmyb_moe_grouped_scratch_bytes(int(n_rows), 1, int(d_model), int(ffn)))
+
+
+def use_grouped_rows(n_rows: int, n_experts: int) -> bool:
+    """Routed rows per expert at which the tcgen05 grouped GEMMs beat the
+    weight-streaming decode kernels (whose CUDA-core work grows with rows)."""
+    return n_rows >= 2 * n_experts
+
+
+def moe_grouped_experts_to(x: torch.Tensor, n_rows: int, perm_token: torch.Tensor,
+                           perm_prob: torch.Tensor, offsets: torch.Tensor,
+                           tile_offsets: torch.Tensor, tile_m: int, w13: torch.Tensor,
+                           w2: torch.Tensor, scratch: torch.Tensor, y_out: torch.Tensor,
+                           out_row: torch.Tensor | None = None) -> None:
+    """y_out[out_row[pos] or pos] = p * expert(x[perm_token[pos]]) on the tcgen05
+    grouped GEMMs, pos < offsets[E] (read on the device)."""
+    _require_cuda(x, perm_token, perm_prob, offsets, tile_offsets, w13, w2, scratch, y_out, out_row)
+    _inplace(y_out, "y_out")
+    x = x.contiguous()
+    e, f2, d = w13.shape
+    if scratch.numel() < grouped_scratch_bytes(n_rows, d, f2 // 2):
+        raise ValueError("moe_grouped_experts_to: scratch too small")
+    _native.call("llmyb_moe_grouped_experts_to", _ptr(x), d, int(n_rows), _ptr(perm_token),
+                 _ptr(perm_prob), _ptr(offsets), _ptr(tile_offsets), int(tile_m), e, _ptr(w13),
+                 _ptr(w2), f2 // 2, _ptr(scratch), _ptr(y_out), _ptr(out_row),
+                 _ptr(device_status(x.device)), _stream())
+
+
+def moe_experts_rows(x: torch.Tensor, plan: RoutePlan, w13: torch.Tensor, w2: torch.Tensor,
+                     y_rows: torch.Tensor | None = None, path: str = "auto") -> torch.Tensor:
+    """Routed expert outputs p * expert(x) per route in plan order ([N*k, D]
+    bf16, for add_rmsnorm_routed).  path "grouped": tcgen05 GEMMs over the
+    plan's tile_m-row tiles; "decode": weight-streaming kernels; "auto": the
+    grouped GEMMs when the plan has several rows per expert."""
+    n_rows = plan.perm_token.numel()
+    e = w13.shape[0]
+    if path not in ("auto", "grouped", "decode"):
+        raise ValueError(f"unknown expert path {path!r}")
+    if path == "decode" or (path == "auto" and not use_grouped_rows(n_rows, e)):
+        return moe_decode_experts(x, plan, w13, w2, y_rows=y_rows)
+    if y_rows is None:
+        y_rows = torch.empty(n_rows, x.shape[-1], dtype=torch.bfloat16, device=x.device)
+    scratch = torch.empty(grouped_scratch_bytes(n_rows, x.shape[-1], w2.shape[-1]),
+                          dtype=torch.uint8, device=x.device)
+    moe_grouped_experts_to(x, n_rows, plan.perm_token, plan.perm_prob, plan.offsets,
+                           plan.tile_offsets, plan.tile_m, w13, w2, scratch, y_rows)
+    return y_rows
 
 
 def add_rmsnorm_routed(streams: torch.Tensor, y_rows: torch.Tensor, plan: RoutePlan,

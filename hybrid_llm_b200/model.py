@@ -41,10 +41,21 @@ class HybridOutput:
 
 
 class LoopedHybridModel:
-    def __init__(self, weights: ModelWeights):
+    """ep: an ExpertParallel group when the weights hold one rank's expert
+    shard (ModelWeights.from_state_dict(..., expert_range=ep.expert_range));
+    every rank of the group then runs the same calls on its own sequences."""
+
+    def __init__(self, weights: ModelWeights, ep=None):
         self.w = weights
         self.cfg: HybridConfig = weights.cfg
         self.device = weights.embed.device
+        self.ep = ep
+        # decode expert kernels: "auto", "grouped" (tcgen05 GEMMs) or "decode"
+        # (weight streaming); a fixed choice makes runs comparable bit for bit
+        self.expert_path = "auto"
+        shard = weights.blocks[0].moe.w13.shape[0] if weights.blocks else None
+        if ep is not None and shard != ep.experts_per_rank:
+            raise ValueError("expert-parallel model needs the weights of this rank's experts only")
 
     # ------------------------------------------------------------- helpers
     def _gdn_views(self, proj: torch.Tensor, lead: tuple[int, ...]):
@@ -66,7 +77,19 @@ class LoopedHybridModel:
         kernels.add_rmsnorm(m_f32, None, blk.moe.router_norm, c.rms_eps, out_f32=r_in)
         logits = torch.mm(r_in, blk.moe.router.t())
         plan = kernels.route(logits, c.moe_top_k)
+        if self.ep is not None:
+            res = self.ep.run(m_bf, plan, blk.moe.w13, blk.moe.w2)
+            return res.y_rows, res.plan_for_combine(plan)
         return kernels.moe_grouped(m_bf, plan, blk.moe.w13, blk.moe.w2)
+
+    def _add_pending(self, streams, pending, weight, **out) -> None:
+        """streams += pending (a bf16 delta, or routed expert rows + plan, whose
+        per-token sum is the MoE combine), then RMSNorm into `out`."""
+        if isinstance(pending, tuple):
+            kernels.add_rmsnorm_routed(streams, pending[0], pending[1], weight, self.cfg.rms_eps,
+                                       **out)
+        else:
+            kernels.add_rmsnorm(streams, pending, weight, self.cfg.rms_eps, **out)
 
     def _head(self, streams: torch.Tensor) -> torch.Tensor:
         """mhc_collapse -> final_norm -> tied LM head (model/model.py:699-707)."""
@@ -129,7 +152,7 @@ class LoopedHybridModel:
         for i in range(loops):
             for j, blk in enumerate(self.w.blocks):
                 key = state_key(i, j)
-                kernels.add_rmsnorm(streams, pending, blk.mixer_norm, c.rms_eps, out_bf16=normed)
+                self._add_pending(streams, pending, blk.mixer_norm, out_bf16=normed)
                 if isinstance(blk.mixer, GdnBlock):
                     mixed = self._gdn_prefill(blk.mixer, normed, state, key, bsz, t, reset)
                 else:
@@ -137,7 +160,7 @@ class LoopedHybridModel:
                 kernels.add_rmsnorm(streams, mixed, blk.ffn_norm, c.rms_eps, out_bf16=m_bf,
                                     out_f32=m_f32)
                 pending = self._moe(blk, m_bf, m_f32)
-        kernels.add_rmsnorm(streams, pending, None, c.rms_eps, normalize=False)
+        self._add_pending(streams, pending, None, normalize=False)
 
     def _gdn_prefill(self, g: GdnBlock, normed, state: RecurrentState, key: str, bsz: int, t: int,
                      reset) -> torch.Tensor:
@@ -199,6 +222,8 @@ class LoopedHybridModel:
         loops = c.num_loops if num_loops is None else int(num_loops)
         d = c.d_model
         fused_router = kernels.route_fused_supported(bsz, c.moe_experts, c.moe_top_k, d)
+        # 128-row tiles for the grouped expert GEMMs at a few rows per expert
+        tile_m = 128
         streams = kernels.embed(ids, self.w.embed, self.w.stream_seed)
         normed = torch.empty(bsz, d, dtype=torch.bfloat16, device=self.device)
         m_bf = torch.empty_like(normed)
@@ -218,14 +243,21 @@ class LoopedHybridModel:
                     mixed = self._csa_step(blk.mixer, normed, state, key, bsz)
                 if fused_router:
                     plan = kernels.route_fused(streams, mixed, blk.ffn_norm, blk.moe.router_norm,
-                                               blk.moe.router, c.moe_top_k, c.rms_eps, m_bf)
+                                               blk.moe.router, c.moe_top_k, c.rms_eps, m_bf,
+                                               tile_m=tile_m)
                 else:
                     kernels.add_rmsnorm(streams, mixed, blk.ffn_norm, c.rms_eps, out_bf16=m_bf,
                                         out_f32=m_f32)
                     r_in = torch.empty_like(m_f32)
                     kernels.add_rmsnorm(m_f32, None, blk.moe.router_norm, c.rms_eps, out_f32=r_in)
-                    plan = kernels.route(torch.mm(r_in, blk.moe.router.t()), c.moe_top_k)
-                y_rows = kernels.moe_decode_experts(m_bf, plan, blk.moe.w13, blk.moe.w2)
+                    plan = kernels.route(torch.mm(r_in, blk.moe.router.t()), c.moe_top_k,
+                                         tile_m=tile_m)
+                if self.ep is not None:
+                    res = self.ep.run(m_bf, plan, blk.moe.w13, blk.moe.w2, path=self.expert_path)
+                    y_rows, plan = res.y_rows, res.plan_for_combine(plan)
+                else:
+                    y_rows = kernels.moe_experts_rows(m_bf, plan, blk.moe.w13, blk.moe.w2,
+                                                      path=self.expert_path)
         sb = torch.empty(bsz, d, dtype=torch.bfloat16, device=self.device)
         kernels.add_rmsnorm_routed(streams, y_rows, plan, None, c.rms_eps, out_bf16=sb,
                                    normalize=False)

@@ -51,6 +51,20 @@ class RecurrentState:
                                                     dtype=torch.bfloat16, device=self.device)
         self.positions = torch.zeros(batch, dtype=torch.int32, device=self.device)
 
+    def fill_synthetic(self, position: int, seed: int = 0) -> None:
+        """Stand-in for a prefilled context of `position` tokens (benchmarks
+        whose cost does not depend on the context's values): ring caches and
+        conv histories ~ N(0, 1), GDN states ~ N(0, 0.05), positions =
+        position.  Drawn on the device from a seeded generator."""
+        g = torch.Generator(device=self.device)
+        g.manual_seed(int(seed))
+        for t in (*self.local_k.values(), *self.local_v.values(),
+                  *self.gdn_conv_histories.values()):
+            t.copy_(torch.randn(t.shape, generator=g, device=self.device, dtype=torch.float32))
+        for t in self.gdn_states.values():
+            t.normal_(0.0, 0.05, generator=g)
+        self.positions.fill_(int(position))
+
     def reset_rows(self, rows: torch.Tensor) -> None:
         """Clear the state of the selected rows (recurrent_state.py:218-244)."""
         mask = rows.to(device=self.device, dtype=torch.bool)

@@ -153,8 +153,12 @@ class ModelWeights:
 
     @classmethod
     def from_state_dict(cls, cfg: HybridConfig, sd: Mapping[str, torch.Tensor],
-                        device: str | torch.device = "cuda") -> "ModelWeights":
+                        device: str | torch.device = "cuda",
+                        expert_range: tuple[int, int] | None = None) -> "ModelWeights":
+        """expert_range (lo, hi): keep only experts lo..hi-1 (one rank's shard
+        under expert parallelism); the router keeps all experts."""
         dev = torch.device(device)
+        lo, hi = (0, cfg.moe_experts) if expert_range is None else expert_range
         bf = lambda n: sd[n].to(device=dev, dtype=torch.bfloat16).contiguous()
         f32 = lambda n: sd[n].to(device=dev, dtype=torch.float32).contiguous()
         blocks = []
@@ -178,15 +182,14 @@ class ModelWeights:
                                     bf(p + "mixer.value.weight")]).contiguous(),
                     local_out=bf(p + "mixer.local_out.weight"), out=bf(p + "mixer.out.weight"),
                     w_o=w_o.to(torch.bfloat16).contiguous())
-            e = cfg.moe_experts
             gate = torch.stack([sd[f"{p}moe.experts.{x}.gate_proj.weight"].to(dev, torch.bfloat16)
-                                for x in range(e)])
+                                for x in range(lo, hi)])
             up = torch.stack([sd[f"{p}moe.experts.{x}.up_proj.weight"].to(dev, torch.bfloat16)
-                              for x in range(e)])
+                              for x in range(lo, hi)])
             w13 = kernels.pack_w13(gate, up)
             del gate, up
             w2 = torch.stack([sd[f"{p}moe.experts.{x}.down_proj.weight"].to(dev, torch.bfloat16)
-                              for x in range(e)]).contiguous()
+                              for x in range(lo, hi)]).contiguous()
             moe = MoeBlock(router_norm=f32(p + "moe.router.norm.weight"),
                            router=f32(p + "moe.router.logits.weight"), w13=w13, w2=w2)
             blocks.append(Block(cfg.block_kind(j), f32(p + "mixer_norm.weight"),

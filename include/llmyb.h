@@ -123,6 +123,22 @@ int32_t llmyb_moe_grouped_swiglu(const void* x, int32_t n_tokens, int32_t d_mode
                                  const void* w13, const void* w2, int32_t ffn, void* scratch,
                                  void* out, int32_t* dev_status, void* stream);
 
+/* The gather and the two grouped GEMMs of llmyb_moe_grouped_swiglu without its
+ * combine, over an explicit plan: y_out[out_row ? out_row[pos] : pos] =
+ * perm_prob[pos] * expert(x[perm_token[pos]]) for pos < expert_offsets[E]
+ * (read on the device; n_rows >= that count bounds the plan).  tile_offsets
+ * counts tile_m-row tiles per expert (tile_m 128 or 256).  scratch: at least
+ * llmyb_moe_grouped_scratch_bytes(n_rows, 1, D, F) bytes.  The tensor-core
+ * path for decode batches with several rows per expert (its outputs feed
+ * llmyb_add_rmsnorm_routed or the expert-parallel return segments).  No
+ * counterpart in the reference (moe.py:29-82 always combines). */
+int32_t llmyb_moe_grouped_experts_to(const void* x, int32_t d_model, int32_t n_rows,
+                                     const int32_t* perm_token, const float* perm_prob,
+                                     const int32_t* expert_offsets, const int32_t* tile_offsets,
+                                     int32_t tile_m, int32_t n_experts, const void* w13,
+                                     const void* w2, int32_t ffn, void* scratch, void* y_out,
+                                     const int32_t* out_row, int32_t* dev_status, void* stream);
+
 /* Scratch bytes needed by llmyb_moe_decode_swiglu. */
 int64_t llmyb_moe_decode_scratch_bytes(int32_t n_tokens, int32_t top_k, int32_t d_model,
                                        int32_t ffn);
@@ -183,14 +199,16 @@ int32_t llmyb_ep_dispatch_pack(const void* x, int32_t d_model, const int32_t* of
                                int32_t* ret_route_pos, void* stream);
 
 /* Expert-ordered plan over the received segments recv [W, H+C, D]:
- * offsets_l [El+1]; perm_token_l (row of recv viewed as [W*(H+C), D]),
- * perm_prob_l and out_row (row of the return buffer [W*C, D]) [W*C], the
- * first offsets_l[El] entries valid.  Rows of one expert are ordered by
- * source rank, then by the source's plan order.  W <= 64, El <= 256,
- * W*El <= 4096. */
+ * offsets_l [El+1]; tile_offsets_l [El+1] (prefix of ceil(rows / tile_m)
+ * per expert, for llmyb_moe_grouped_experts_to; nullable); perm_token_l (row
+ * of recv viewed as [W*(H+C), D]), perm_prob_l and out_row (row of the
+ * return buffer [W*C, D]) [W*C], the first offsets_l[El] entries valid.
+ * Rows of one expert are ordered by source rank, then by the source's plan
+ * order.  W <= 64, El <= 256, W*El <= 4096. */
 int32_t llmyb_ep_recv_plan(const void* recv, int32_t d_model, int32_t world, int32_t capacity,
-                           int32_t experts_per_rank, int32_t* offsets_l, int32_t* perm_token_l,
-                           float* perm_prob_l, int32_t* out_row, void* stream);
+                           int32_t experts_per_rank, int32_t tile_m, int32_t* offsets_l,
+                           int32_t* tile_offsets_l, int32_t* perm_token_l, float* perm_prob_l,
+                           int32_t* out_row, void* stream);
 
 /* ------------------------------------------------------ gated delta rule
  * Replaces GatedDeltaNet's recurrence (model/layers/gated_deltanet.py:140-149

@@ -40,40 +40,39 @@ def pack_w13(gate_bits: np.ndarray, up_bits: np.ndarray) -> np.ndarray:
 
 
 class OracleOps:
-    """The four device steps of ExpertParallel.run, restated by oracle/ep.py on CPU tensors."""
+    """The device steps of ExpertParallel.run, restated by oracle/ep.py on CPU tensors."""
 
     header_rows = staticmethod(oep.header_rows)
 
     @staticmethod
-    def dispatch_pack(x, plan, n_experts, world, capacity, send, ret_route_pos):
-        d = x.shape[1]
-        el = n_experts // world
-        h = oep.header_rows(el, capacity, d)
+    def scratch_bytes(ep) -> int:
+        return 16
+
+    @staticmethod
+    def dispatch_pack(ep, x, plan, ret_route_pos):
+        d, w, c = ep.d_model, ep.world, ep.capacity
         oep.dispatch_pack(_bits(x), plan.offsets.numpy(), plan.perm_token.numpy(),
-                          plan.perm_prob.numpy(), plan.route_pos.numpy(), n_experts, world,
-                          capacity, _bits(send).reshape(world, h + capacity, d),
-                          ret_route_pos.numpy())
+                          plan.perm_prob.numpy(), plan.route_pos.numpy(), ep.n_experts, w, c,
+                          _bits(ep.send).reshape(w, ep.header + c, d), ret_route_pos.numpy())
 
     @staticmethod
-    def recv_plan(recv, world, capacity, el, offsets_l, perm_token_l, perm_prob_l, out_row):
-        d = recv.shape[1]
-        h = oep.header_rows(el, capacity, d)
-        off, pt, pp, orow = oep.recv_plan(_bits(recv).reshape(world, h + capacity, d), world,
-                                          capacity, el)
-        offsets_l.copy_(torch.from_numpy(off.astype(np.int32)))
+    def recv_plan(ep):
+        d, w, c = ep.d_model, ep.world, ep.capacity
+        off, pt, pp, orow = oep.recv_plan(_bits(ep.recv).reshape(w, ep.header + c, d), w, c,
+                                          ep.experts_per_rank)
+        ep.offsets_l.copy_(torch.from_numpy(off.astype(np.int32)))
         n = len(pt)
-        perm_token_l[:n] = torch.from_numpy(pt.astype(np.int32))
-        perm_prob_l[:n] = torch.from_numpy(pp)
-        out_row[:n] = torch.from_numpy(orow.astype(np.int32))
+        ep.perm_token_l[:n] = torch.from_numpy(pt.astype(np.int32))
+        ep.perm_prob_l[:n] = torch.from_numpy(pp)
+        ep.out_row[:n] = torch.from_numpy(orow.astype(np.int32))
 
     @staticmethod
-    def experts_to(recv, n_rows, perm_token_l, perm_prob_l, offsets_l, w13, w2, h_scratch, y_out,
-                   out_row):
+    def experts_to(ep, w13, w2, grouped):
         gate, up = unpack_w13(_bits(w13))
-        n = int(offsets_l[-1])
-        oep.experts_to(_bits(recv), offsets_l.numpy(), perm_token_l.numpy()[:n],
-                       perm_prob_l.numpy()[:n], out_row.numpy()[:n], oep.bf16_value(gate),
-                       oep.bf16_value(up), oep.bf16_value(_bits(w2)), _bits(y_out))
+        n = int(ep.offsets_l[-1])
+        oep.experts_to(_bits(ep.recv), ep.offsets_l.numpy(), ep.perm_token_l.numpy()[:n],
+                       ep.perm_prob_l.numpy()[:n], ep.out_row.numpy()[:n], oep.bf16_value(gate),
+                       oep.bf16_value(up), oep.bf16_value(_bits(w2)), _bits(ep.ret_send))
 
 
 E, K, D, F = 8, 2, 64, 256

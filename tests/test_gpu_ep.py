@@ -39,26 +39,35 @@ def _setup(dev, world, e, k, d, f, n_per_rank, seed=0, skew=False):
         logits = torch.randn(n_per_rank[r], e, generator=g)
         if skew:
             logits[:, : e // world] += 50.0
-        plans.append(kernels.route(logits.to(dev), k))
+        plans.append(kernels.route(logits.to(dev), k, tile_m=128))
         xs.append(x)
     return w13, wd, xs, plans
 
 
-def _single_device(x, plan, w13, wd, d):
+def _single_device(x, plan, w13, wd, d, grouped=False):
     from hybrid_llm_b200 import kernels
-    y = kernels.moe_decode_experts(x, plan, w13, wd)
+    if grouped:
+        n = plan.perm_token.numel()
+        y = torch.empty(n, d, dtype=torch.bfloat16, device=x.device)
+        scratch = torch.empty(kernels.grouped_scratch_bytes(n, d, wd.shape[-1]), dtype=torch.uint8,
+                              device=x.device)
+        kernels.moe_grouped_experts_to(x, n, plan.perm_token, plan.perm_prob, plan.offsets,
+                                       plan.tile_offsets, 128, w13, wd, scratch, y)
+    else:
+        y = kernels.moe_decode_experts(x, plan, w13, wd)
     streams = torch.zeros(x.shape[0], d, dtype=torch.float32, device=x.device)
     kernels.add_rmsnorm_routed(streams, y, plan, None, 1e-6, normalize=False)
     return streams
 
 
+@pytest.mark.parametrize("grouped", [False, True])
 @pytest.mark.parametrize("world,e,k,d,f,n,skew", [
     (2, 8, 2, 256, 256, [5, 9], False),
     (4, 16, 4, 512, 384, [7, 1, 0, 12], False),
     (4, 16, 4, 256, 256, [6, 6, 6, 6], True),
     (8, 64, 8, 2048, 1024, [8] * 8, False),     # the large expert-parallel config's shapes
 ])
-def test_ep_kernels_emulated_ranks(cuda, world, e, k, d, f, n, skew):
+def test_ep_kernels_emulated_ranks(cuda, world, e, k, d, f, n, skew, grouped):
     from hybrid_llm_b200 import kernels
     from dataclasses import replace
     w13, wd, xs, plans = _setup(cuda, world, e, k, d, f, n, skew=skew)
@@ -98,7 +107,9 @@ def test_ep_kernels_emulated_ranks(cuda, world, e, k, d, f, n, skew):
         pt = torch.zeros(world * cap, dtype=torch.int32, device=cuda)
         pp = torch.zeros(world * cap, dtype=torch.float32, device=cuda)
         orow = torch.zeros(world * cap, dtype=torch.int32, device=cuda)
-        kernels.ep_recv_plan(recvs[q], world, cap, el, off, pt, pp, orow)
+        toff = torch.zeros(el + 1, dtype=torch.int32, device=cuda)
+        kernels.ep_recv_plan(recvs[q], world, cap, el, off, pt, pp, orow, tile_offsets_l=toff,
+                             tile_m=128)
         w_off, w_pt, w_pp, w_or = oep.recv_plan(_bits(recvs[q]).reshape(world, h + cap, d), world,
                                                 cap, el)
         m = int(w_off[-1])
@@ -106,10 +117,19 @@ def test_ep_kernels_emulated_ranks(cuda, world, e, k, d, f, n, skew):
         assert pt[:m].cpu().numpy().tolist() == w_pt.tolist()
         assert np.array_equal(pp[:m].cpu().numpy(), w_pp)
         assert orow[:m].cpu().numpy().tolist() == w_or.tolist()
+        cnt = np.diff(w_off)
+        assert toff.cpu().numpy().tolist() == np.concatenate([[0], np.cumsum((cnt + 127) // 128)]).tolist()
         ret = torch.zeros(world * cap, d, dtype=torch.bfloat16, device=cuda)
-        hs = torch.zeros(world * cap, f, dtype=torch.bfloat16, device=cuda)
-        kernels.moe_decode_experts_to(recvs[q], world * cap, pt, pp, off, w13[q * el:(q + 1) * el],
-                                      wd[q * el:(q + 1) * el], hs, ret, orow)
+        we13, we2 = w13[q * el:(q + 1) * el], wd[q * el:(q + 1) * el]
+        if grouped:
+            scratch = torch.empty(kernels.grouped_scratch_bytes(world * cap, d, f),
+                                  dtype=torch.uint8, device=cuda)
+            kernels.moe_grouped_experts_to(recvs[q], world * cap, pt, pp, off, toff, 128, we13,
+                                           we2, scratch, ret, orow)
+        else:
+            hs = torch.zeros(world * cap, f, dtype=torch.bfloat16, device=cuda)
+            kernels.moe_decode_experts_to(recvs[q], world * cap, pt, pp, off, we13, we2, hs, ret,
+                                          orow)
         rets.append(ret.view(world, cap, d))
     for r in range(world):
         if n[r] == 0:
@@ -118,7 +138,7 @@ def test_ep_kernels_emulated_ranks(cuda, world, e, k, d, f, n, skew):
         streams = torch.zeros(n[r], d, dtype=torch.float32, device=cuda)
         kernels.add_rmsnorm_routed(streams, ret_recv, replace(plans[r], route_pos=rps[r]), None,
                                    1e-6, normalize=False)
-        want = _single_device(xs[r], plans[r], w13, wd, d)
+        want = _single_device(xs[r], plans[r], w13, wd, d, grouped)
         assert torch.equal(streams, want), f"rank {r}: expert-parallel != single device"
 
 
@@ -143,13 +163,14 @@ def _nccl_worker(rank, world, port, errors):
         w13, wd, xs, plans = _setup(dev, world, e, k, d, f, n, seed=3)
         ep = ExpertParallel(e, k, d, f, max(n), device=dev)
         lo, hi = ep.expert_range
-        for _ in range(2):
-            res = ep.run(xs[rank], plans[rank], w13[lo:hi].contiguous(), wd[lo:hi].contiguous())
+        for path in ("decode", "grouped", "decode"):
+            res = ep.run(xs[rank], plans[rank], w13[lo:hi].contiguous(), wd[lo:hi].contiguous(),
+                         path=path)
             from hybrid_llm_b200 import kernels
             streams = torch.zeros(n[rank], d, dtype=torch.float32, device=dev)
             kernels.add_rmsnorm_routed(streams, res.y_rows, res.plan_for_combine(plans[rank]), None,
                                        1e-6, normalize=False)
-            want = _single_device(xs[rank], plans[rank], w13, wd, d)
+            want = _single_device(xs[rank], plans[rank], w13, wd, d, grouped=path == "grouped")
             assert torch.equal(streams, want), f"rank {rank}: NCCL expert-parallel != single device"
         torch.cuda.synchronize()
         dist.barrier()
@@ -168,5 +189,71 @@ def test_ep_nccl_two_or_more_gpus(cuda):
     ctx = mp.get_context("spawn")
     errors = ctx.SimpleQueue()
     mp.start_processes(_nccl_worker, args=(world, _free_port(), errors), nprocs=world, join=True,
+                       start_method="spawn")
+    assert errors.empty(), errors.get()
+
+
+def _model_worker(rank, world, port, errors):
+    import torch.distributed as dist
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        from datetime import timedelta
+        dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                                timeout=timedelta(seconds=60))
+        from hybrid_llm_b200.config import HybridConfig
+        from hybrid_llm_b200.expert_parallel import ExpertParallel
+        from hybrid_llm_b200.model import LoopedHybridModel
+        from hybrid_llm_b200.state import RecurrentState
+        from hybrid_llm_b200.weights import ModelWeights, synthetic_state_dict
+        cfg = HybridConfig(vocab_size=512, d_model=256, recurrent_layout=("csa_moe", "gdn_moe") * 2,
+                           num_loops=2, gdn_heads=2, gdn_key_dim=64, gdn_value_dim=64, csa_heads=4,
+                           csa_head_dim=64, csa_window=16, moe_experts=8, moe_top_k=2,
+                           moe_hidden=256, name="ep-test")
+        bsz, t = 2, 24
+        sd = synthetic_state_dict(cfg, seed=5, device=dev, std=0.05)
+        full = LoopedHybridModel(ModelWeights.from_state_dict(cfg, sd, dev))
+        ep = ExpertParallel(cfg.moe_experts, cfg.moe_top_k, cfg.d_model, cfg.moe_hidden, bsz * t,
+                            device=dev)
+        shard = LoopedHybridModel(ModelWeights.from_state_dict(cfg, sd, dev,
+                                                               expert_range=ep.expert_range), ep=ep)
+        g = torch.Generator(device="cpu").manual_seed(100 + rank)
+        ids = torch.randint(0, cfg.vocab_size, (bsz, t), generator=g).to(dev)
+        out_full = full.forward(ids, last_logits_only=True)
+        out_ep = shard.forward(ids, last_logits_only=True)
+        a, b = out_full.logits.float(), out_ep.logits.float()
+        err = (a - b).abs().max().item() / max(a.abs().max().item(), 1e-6)
+        assert err < 2e-2, f"rank {rank}: expert-parallel prefill logits off by {err:.3g}"
+        # decode from the same state with the same expert kernels: bit-identical logits
+        for path in ("decode", "grouped"):
+            full.expert_path = shard.expert_path = path
+            st_full = RecurrentState(cfg, bsz, dev)
+            st_full.load_state_dict(out_full.state.state_dict())
+            st_ep = RecurrentState(cfg, bsz, dev)
+            st_ep.load_state_dict(out_full.state.state_dict())
+            tok = a[:, -1].argmax(-1)
+            for _ in range(4):
+                la = full.decode_step(tok, st_full)
+                lb = shard.decode_step(tok, st_ep)
+                assert torch.equal(la, lb), f"rank {rank}: {path} expert-parallel decode differs"
+                tok = la.float().argmax(-1)
+        torch.cuda.synchronize()
+        dist.barrier()
+        dist.destroy_process_group()
+    except BaseException as exc:
+        errors.put(f"rank {rank}: {exc!r}")
+        raise
+
+
+def test_ep_model_decode_two_or_more_gpus(cuda):
+    import torch.multiprocessing as mp
+    world = torch.cuda.device_count()
+    if world < 2:
+        pytest.skip("needs two or more GPUs")
+    world = 2
+    ctx = mp.get_context("spawn")
+    errors = ctx.SimpleQueue()
+    mp.start_processes(_model_worker, args=(world, _free_port(), errors), nprocs=world, join=True,
                        start_method="spawn")
     assert errors.empty(), errors.get()

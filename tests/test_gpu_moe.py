@@ -94,3 +94,40 @@ def test_moe_repeated_calls_identical(cuda):
     a, _ = _run(x, logits, bias, wg, wu, wd, 2)
     b, _ = _run(x, logits, bias, wg, wu, wd, 2)
     assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("grouped", [True, False])
+@pytest.mark.parametrize("n,d,e,k,f", [(64, 2048, 64, 8, 1024), (37, 512, 8, 2, 384),
+                                       (300, 256, 16, 4, 256)])
+def test_moe_expert_rows_match_oracle(cuda, n, d, e, k, f, grouped):
+    """Per-route expert rows (decode-batch path) combined by the routed residual add."""
+    from hybrid_llm_b200 import kernels
+    x, logits, bias, wg, wu, wd = _case(n, d, e, k, f, seed=11 + n)
+    plan = kernels.route(torch.from_numpy(logits).to(cuda), k, tile_m=128)
+    w13 = kernels.pack_w13(wg.to(cuda), wu.to(cuda))
+    xd, wdd = x.to(cuda), wd.to(cuda)
+    rows = plan.perm_token.numel()
+    if grouped:
+        y = torch.empty(rows, d, dtype=torch.bfloat16, device=cuda)
+        scratch = torch.empty(kernels.grouped_scratch_bytes(rows, d, f), dtype=torch.uint8,
+                              device=cuda)
+        kernels.moe_grouped_experts_to(xd, rows, plan.perm_token, plan.perm_prob, plan.offsets,
+                                       plan.tile_offsets, 128, w13, wdd, scratch, y)
+    else:
+        y = kernels.moe_decode_experts(xd, plan, w13, wdd)
+    streams = torch.zeros(n, d, dtype=torch.float32, device=cuda)
+    kernels.add_rmsnorm_routed(streams, y, plan, None, 1e-6, normalize=False)
+    torch.cuda.synchronize()
+    kernels.check_device_status()
+    idx, prob = routing.router_topk(logits, k, None)
+    ref = routing.moe_forward(x.float().numpy(), idx, prob, wg.float().numpy(),
+                              wu.float().numpy(), wd.float().numpy())
+    mx, mean = _errors(streams, ref)
+    assert mx < MAX_REL and mean < MEAN_REL, (mx, mean)
+    # the row map: writing row pos to out_row[pos] permutes the rows exactly
+    if grouped:
+        perm = torch.randperm(rows, device=cuda).to(torch.int32)
+        y2 = torch.empty_like(y)
+        kernels.moe_grouped_experts_to(xd, rows, plan.perm_token, plan.perm_prob, plan.offsets,
+                                       plan.tile_offsets, 128, w13, wdd, scratch, y2, perm)
+        assert torch.equal(y2[perm.long()], y)
