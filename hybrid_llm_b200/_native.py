@@ -40,6 +40,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "llmyb_route_noalloc_max_scratch_ints": (I64, []),
     "llmyb_route_fused": (I32, [P, P, I32, I32, P, P, P, F32, I32, I32, I32, P, P, P, P, P, P, P, P,
                                 P, P]),
+    "llmyb_route_decode": (I32, [P, P, I32, I32, P, P, P, F32, I32, I32, I32, P, P, P, P, P, P, P,
+                                 P, P, P, P]),
     # MoE expert FFN
     "llmyb_moe_pack_w13": (I32, [P, P, I32, I32, I32, P, P]),
     "llmyb_moe_grouped_scratch_bytes": (I64, [I32, I32, I32, I32]),

@@ -408,7 +408,9 @@ constexpr int kMaxChunks = 8;  // 16-byte chunks of a K row per lane: H*DH <= 20
 // loads in flight per warp (the kernel is bound by the K/V window bytes).
 // Dynamic shared memory: q [H*DH] | scores [H][kpc] | m, l, M, L [H] |
 // p [kpc] | partial out [groups][D].
-__global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(256)
+// Four CTAs per SM (64 registers): a batch of 64 rows is 64 clusters of 8,
+// which must all be resident at once to run in a single wave.
+__global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(256, 4)
     csa_decode_kernel(const __nv_bfloat16* __restrict__ q, int64_t sq,
                       const __nv_bfloat16* __restrict__ knew, int64_t skn,
                       const __nv_bfloat16* __restrict__ vnew, int64_t svn,
@@ -418,6 +420,8 @@ __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(256)
   extern __shared__ float dsm[];
   cg::cluster_group cluster = cg::this_cluster();
   const int crank = static_cast<int>(cluster.block_rank());
+  // q stays bf16 (its input precision): lane c reads q chunk c as 16 bytes,
+  // consecutive lanes consecutive chunks, so the reads are conflict-free
   const int b = blockIdx.x / kClusterCtas;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int kpc = (Wc + kClusterCtas - 1) / kClusterCtas;  // keys per CTA
@@ -426,8 +430,8 @@ __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(256)
   const int seg = DH / 8;            // lanes per head within one pass (8 or 16)
   const int vch = D / 8;             // 16-byte chunks per V row
   const int groups = max(1, 256 / vch);
-  float* s_q = dsm;
-  float* s_sc = s_q + HD;
+  __nv_bfloat16* s_q = reinterpret_cast<__nv_bfloat16*>(dsm);
+  float* s_sc = dsm + HD / 2;
   float* s_m = s_sc + H * kpc;
   float* s_l = s_m + H;
   float* s_M = s_l + H;
@@ -443,7 +447,8 @@ __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(256)
   const int nk = max(0, min(j_end, n_valid) - j_begin);  // valid keys of this CTA
   const int64_t cache_row = static_cast<int64_t>(b) * Wc;
 
-  for (int i = tid; i < HD; i += 256) s_q[i] = bf2f(q[b * sq + i]);
+  for (int c = tid; c < nch; c += 256)
+    reinterpret_cast<uint4*>(s_q)[c] = reinterpret_cast<const uint4*>(q + b * sq)[c];
   __syncthreads();
   // ---- scores: one key per warp iteration, the whole K row in flight
   for (int jl = warp; jl < nk; jl += 8) {
@@ -461,11 +466,13 @@ __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(256)
       float acc = 0.f;
       if (c < nch) {
         const uint32_t w[4] = {kv[i].x, kv[i].y, kv[i].z, kv[i].w};
-        const float* qq = s_q + c * 8;
+        const uint4 q4 = reinterpret_cast<const uint4*>(s_q)[c];
+        const uint32_t qw[4] = {q4.x, q4.y, q4.z, q4.w};
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const float2 f = unpack_bf16x2(w[e]);
-          acc += qq[2 * e] * f.x + qq[2 * e + 1] * f.y;
+          const float2 qf = unpack_bf16x2(qw[e]);
+          acc += qf.x * f.x + qf.y * f.y;
         }
       }
       if (32 * i < nch) {
@@ -715,7 +722,7 @@ LLMYB_API int32_t llmyb_csa_local_decode(const void* q, int64_t q_stride, const 
     return LLMYB_EUNSUPPORTED;
   const int kpc = (window + kClusterCtas - 1) / kClusterCtas;
   const int groups = std::max(1, 256 / (d_model / 8));
-  const int bytes = (hd + heads * kpc + 4 * heads + kpc + groups * d_model) * 4;
+  const int bytes = (hd / 2 + heads * kpc + 4 * heads + kpc + groups * d_model) * 4;
   if (bytes > 227 * 1024) return LLMYB_EUNSUPPORTED;
   static int attr_bytes = 0;
   if (bytes > attr_bytes) {

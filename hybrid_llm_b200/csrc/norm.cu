@@ -67,6 +67,129 @@ __global__ void __launch_bounds__(256) add_rmsnorm_kernel(
   }
 }
 
+// add_rmsnorm_kernel for D % 8 == 0 with 16-byte rows: thread i owns the
+// 8-element vectors i, i+256, ... (at most VMAX of them, kept in registers
+// between the sum of squares and the scaled write); the routed delta rows of
+// a vector are loaded together.  The per-element sum order (stream value,
+// then the k routed rows in slot order) is that of add_rmsnorm_kernel.
+template <int VMAX>
+__global__ void __launch_bounds__(256) add_rmsnorm_vec_kernel(
+    float* __restrict__ streams, const __nv_bfloat16* __restrict__ delta,
+    const int* __restrict__ route_pos, int k, int D, const float* __restrict__ weight, float eps,
+    int normalize, __nv_bfloat16* __restrict__ out_bf16, float* __restrict__ out_f32) {
+  __shared__ float red[8];
+  const int64_t n = blockIdx.x;
+  const int nv = D >> 3;
+  float4* x4 = reinterpret_cast<float4*>(streams + n * D);
+  float v[VMAX][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < VMAX; ++j) {
+    const int c = threadIdx.x + j * 256;
+    if (c >= nv) continue;
+    const float4 a = x4[2 * c], b = x4[2 * c + 1];
+    v[j][0] = a.x; v[j][1] = a.y; v[j][2] = a.z; v[j][3] = a.w;
+    v[j][4] = b.x; v[j][5] = b.y; v[j][6] = b.z; v[j][7] = b.w;
+    if (delta != nullptr) {
+      if (route_pos != nullptr) {
+#pragma unroll 4
+        for (int s = 0; s < k; ++s) {
+          const int64_t pos = __ldg(route_pos + n * k + s);
+          const uint4 u = __ldg(reinterpret_cast<const uint4*>(delta + pos * D) + c);
+          const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float2 f = unpack_bf16x2(w[q]);
+            v[j][2 * q] += f.x;
+            v[j][2 * q + 1] += f.y;
+          }
+        }
+      } else {
+        const uint4 u = __ldg(reinterpret_cast<const uint4*>(delta + n * D) + c);
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float2 f = unpack_bf16x2(w[q]);
+          v[j][2 * q] += f.x;
+          v[j][2 * q + 1] += f.y;
+        }
+      }
+      x4[2 * c] = make_float4(v[j][0], v[j][1], v[j][2], v[j][3]);
+      x4[2 * c + 1] = make_float4(v[j][4], v[j][5], v[j][6], v[j][7]);
+    }
+#pragma unroll
+    for (int q = 0; q < 8; ++q) ss += v[j][q] * v[j][q];
+  }
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) tot += red[i];
+  const float r = normalize ? rsqrtf(tot / static_cast<float>(D) + eps) : 1.f;
+#pragma unroll
+  for (int j = 0; j < VMAX; ++j) {
+    const int c = threadIdx.x + j * 256;
+    if (c >= nv) continue;
+    float y[8];
+    if (normalize) {
+      float w8[8] = {1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f};
+      if (weight != nullptr) {
+        const float4 wa = __ldg(reinterpret_cast<const float4*>(weight) + 2 * c);
+        const float4 wb = __ldg(reinterpret_cast<const float4*>(weight) + 2 * c + 1);
+        w8[0] = wa.x; w8[1] = wa.y; w8[2] = wa.z; w8[3] = wa.w;
+        w8[4] = wb.x; w8[5] = wb.y; w8[6] = wb.z; w8[7] = wb.w;
+      }
+#pragma unroll
+      for (int q = 0; q < 8; ++q) y[q] = v[j][q] * r * w8[q];
+    } else {
+#pragma unroll
+      for (int q = 0; q < 8; ++q) y[q] = v[j][q];
+    }
+    if (out_bf16 != nullptr) {
+      uint4 o;
+      o.x = pack_bf16x2(y[0], y[1]);
+      o.y = pack_bf16x2(y[2], y[3]);
+      o.z = pack_bf16x2(y[4], y[5]);
+      o.w = pack_bf16x2(y[6], y[7]);
+      reinterpret_cast<uint4*>(out_bf16 + n * D)[c] = o;
+    }
+    if (out_f32 != nullptr) {
+      float4* o4 = reinterpret_cast<float4*>(out_f32 + n * D);
+      o4[2 * c] = make_float4(y[0], y[1], y[2], y[3]);
+      o4[2 * c + 1] = make_float4(y[4], y[5], y[6], y[7]);
+    }
+  }
+}
+
+// Launch the vectorised kernel when D and every pointer allow 16-byte rows.
+int32_t launch_add_rmsnorm(float* streams, const __nv_bfloat16* delta, const int* route_pos, int k,
+                           int64_t n, int D, const float* weight, float eps, int normalize,
+                           __nv_bfloat16* out_bf16, float* out_f32, cudaStream_t s) {
+  const uintptr_t align = reinterpret_cast<uintptr_t>(streams) |
+                          reinterpret_cast<uintptr_t>(delta) |
+                          reinterpret_cast<uintptr_t>(weight) |
+                          reinterpret_cast<uintptr_t>(out_bf16) |
+                          reinterpret_cast<uintptr_t>(out_f32);
+  const unsigned grid = static_cast<unsigned>(n);
+  if (D % 8 == 0 && (align & 15u) == 0 && D <= 8 * 256 * 4) {
+    if (D <= 8 * 256)
+      add_rmsnorm_vec_kernel<1><<<grid, 256, 0, s>>>(streams, delta, route_pos, k, D, weight, eps,
+                                                      normalize, out_bf16, out_f32);
+    else if (D <= 8 * 256 * 2)
+      add_rmsnorm_vec_kernel<2><<<grid, 256, 0, s>>>(streams, delta, route_pos, k, D, weight, eps,
+                                                      normalize, out_bf16, out_f32);
+    else
+      add_rmsnorm_vec_kernel<4><<<grid, 256, 0, s>>>(streams, delta, route_pos, k, D, weight, eps,
+                                                      normalize, out_bf16, out_f32);
+  } else {
+    add_rmsnorm_kernel<<<grid, 256, 0, s>>>(streams, delta, route_pos, k, D, weight, eps,
+                                            normalize, out_bf16, out_f32);
+  }
+  count_launch();
+  return launch_status();
+}
+
 // RMSNorm of a bf16 input (used on the collapsed stream before the LM head)
 __global__ void __launch_bounds__(256) rmsnorm_bf16_kernel(const __nv_bfloat16* __restrict__ x, int D,
                                                            const float* __restrict__ weight,
@@ -123,12 +246,10 @@ LLMYB_API int32_t llmyb_add_rmsnorm(float* streams, const void* delta, int64_t n
                                     void* stream) {
   if (!streams || n_tokens < 0 || d_model <= 0) return LLMYB_EINVAL;
   if (n_tokens == 0) return LLMYB_OK;
-  add_rmsnorm_kernel<<<static_cast<unsigned>(n_tokens), 256, 0,
-                       static_cast<cudaStream_t>(stream)>>>(
-      streams, static_cast<const __nv_bfloat16*>(delta), nullptr, 0, d_model, weight, eps,
-      normalize, static_cast<__nv_bfloat16*>(out_bf16), out_f32);
-  count_launch();
-  return launch_status();
+  return launch_add_rmsnorm(streams, static_cast<const __nv_bfloat16*>(delta), nullptr, 0,
+                            n_tokens, d_model, weight, eps, normalize,
+                            static_cast<__nv_bfloat16*>(out_bf16), out_f32,
+                            static_cast<cudaStream_t>(stream));
 }
 
 // streams += sum_s y_rows[route_pos[n*k + s]] (bf16 expert rows, fp32 sum),
@@ -141,12 +262,10 @@ LLMYB_API int32_t llmyb_add_rmsnorm_routed(float* streams, const void* y_rows,
   if (!streams || !y_rows || !route_pos || top_k <= 0 || n_tokens < 0 || d_model <= 0)
     return LLMYB_EINVAL;
   if (n_tokens == 0) return LLMYB_OK;
-  add_rmsnorm_kernel<<<static_cast<unsigned>(n_tokens), 256, 0,
-                       static_cast<cudaStream_t>(stream)>>>(
-      streams, static_cast<const __nv_bfloat16*>(y_rows), route_pos, top_k, d_model, weight, eps,
-      normalize, static_cast<__nv_bfloat16*>(out_bf16), out_f32);
-  count_launch();
-  return launch_status();
+  return launch_add_rmsnorm(streams, static_cast<const __nv_bfloat16*>(y_rows), route_pos, top_k,
+                            n_tokens, d_model, weight, eps, normalize,
+                            static_cast<__nv_bfloat16*>(out_bf16), out_f32,
+                            static_cast<cudaStream_t>(stream));
 }
 
 LLMYB_API int32_t llmyb_rmsnorm_bf16(const void* x, int64_t n_tokens, int32_t d_model,

@@ -275,22 +275,63 @@ __global__ void __launch_bounds__(256) plan_scatter_kernel(
   }
 }
 
-// Fused single-CTA route for small batches (decode): top-k, softmax, counts,
-// offsets, tile offsets and the in-order permutation in one launch.
-__global__ void __launch_bounds__(1024) route_small_kernel(
-    const float* __restrict__ logits, const float* __restrict__ bias, int N, int E, int k,
-    int tile_m, int64_t* __restrict__ topk_idx, float* __restrict__ topk_prob,
-    int* __restrict__ counts, int* __restrict__ offsets, int* __restrict__ tile_offsets,
-    int* __restrict__ perm_token, float* __restrict__ perm_prob, int* __restrict__ route_pos,
-    int64_t* __restrict__ sort_order) {
-  __shared__ int s_idx[256 * kMaxTopK / 4];  // N*k <= 2048
-  __shared__ float s_prob[256 * kMaxTopK / 4];
-  __shared__ int s_cnt[kMaxExperts];
-  __shared__ int s_warp[32];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+// Stable scatter of the R = N*k routes of a plan by one warp.  Route r =
+// t*k + s goes to expert s_idx[r]; s_base[e] holds the next free position of
+// expert e (the expert offsets on entry) and is advanced.  Chunks of 32
+// consecutive routes are placed at once: equal experts inside a chunk are
+// ranked by lane order (__match_any_sync), so positions follow (token, slot)
+// order within every expert.
+__device__ __forceinline__ void warp_stable_scatter(const int* s_idx, const float* s_prob, int R,
+                                                    int k, int* s_base, int* __restrict__ perm_token,
+                                                    float* __restrict__ perm_prob,
+                                                    int* __restrict__ route_pos,
+                                                    int64_t* __restrict__ sort_order, int lane) {
+  for (int r0 = 0; r0 < R; r0 += 32) {
+    const int r = r0 + lane;
+    const bool active = r < R;
+    const int e = active ? s_idx[r] : -1 - lane;  // inactive lanes match nobody
+    const unsigned peers = __match_any_sync(0xffffffffu, e);
+    const int rank = __popc(peers & ((1u << lane) - 1u));
+    const int pos = active ? s_base[e] + rank : 0;
+    __syncwarp();
+    if (active && rank == __popc(peers) - 1) s_base[e] = pos + 1;
+    __syncwarp();
+    if (active) {
+      perm_token[pos] = r / k;
+      perm_prob[pos] = s_prob[r];
+      route_pos[r] = pos;
+      if (sort_order != nullptr) sort_order[pos] = r;
+    }
+  }
+}
+
+__device__ __forceinline__ void cta_plan_tail(int N, int E, int k, int tile_m, const int* s_idx,
+                                              const float* s_prob, int* s_cnt, int* s_warp,
+                                              int* __restrict__ counts, int* __restrict__ offsets,
+                                              int* __restrict__ tile_offsets,
+                                              int* __restrict__ perm_token,
+                                              float* __restrict__ perm_prob,
+                                              int* __restrict__ route_pos,
+                                              int64_t* __restrict__ sort_order);
+
+// Top-k, softmax, counts, offsets, tile offsets and the stable permutation
+// of N tokens whose logits [N, E] are `logits` (global or shared memory);
+// called by all threads of one CTA (blockDim a multiple of 32, >= E).
+__device__ __forceinline__ void cta_topk_plan(const float* logits, const float* __restrict__ bias,
+                                              int N, int E, int k, int tile_m, int* s_idx,
+                                              float* s_prob, int* s_cnt, int* s_warp,
+                                              int64_t* __restrict__ topk_idx,
+                                              float* __restrict__ topk_prob,
+                                              int* __restrict__ counts, int* __restrict__ offsets,
+                                              int* __restrict__ tile_offsets,
+                                              int* __restrict__ perm_token,
+                                              float* __restrict__ perm_prob,
+                                              int* __restrict__ route_pos,
+                                              int64_t* __restrict__ sort_order) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
   for (int e = threadIdx.x; e < E; e += blockDim.x) s_cnt[e] = 0;
   __syncthreads();
-  for (int t = warp; t < N; t += 32) {
+  for (int t = warp; t < N; t += nwarps) {
     int idx;
     float val;
     warp_topk_row(logits + static_cast<int64_t>(t) * E, bias, E, k, lane, idx, val);
@@ -304,6 +345,21 @@ __global__ void __launch_bounds__(1024) route_small_kernel(
     }
   }
   __syncthreads();
+  cta_plan_tail(N, E, k, tile_m, s_idx, s_prob, s_cnt, s_warp, counts, offsets, tile_offsets,
+                perm_token, perm_prob, route_pos, sort_order);
+}
+
+// Counts -> offsets, tile offsets and the stable permutation (one CTA;
+// s_cnt[e] holds the route count of expert e on entry).
+__device__ __forceinline__ void cta_plan_tail(int N, int E, int k, int tile_m, const int* s_idx,
+                                              const float* s_prob, int* s_cnt, int* s_warp,
+                                              int* __restrict__ counts, int* __restrict__ offsets,
+                                              int* __restrict__ tile_offsets,
+                                              int* __restrict__ perm_token,
+                                              float* __restrict__ perm_prob,
+                                              int* __restrict__ route_pos,
+                                              int64_t* __restrict__ sort_order) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int c = threadIdx.x < E ? s_cnt[threadIdx.x] : 0;
   int total = 0;
   const int off = block_exclusive_scan(c, s_warp, total);
@@ -321,29 +377,149 @@ __global__ void __launch_bounds__(1024) route_small_kernel(
     tile_offsets[E] = total_tiles;
   }
   __syncthreads();
-  if (warp == 0) {
-    for (int t = 0; t < N; ++t) {
-      if (lane < k) {
-        const int r = t * k + lane;
-        const int e = s_idx[r];
-        const int pos = s_cnt[e];
-        s_cnt[e] = pos + 1;
-        perm_token[pos] = t;
-        perm_prob[pos] = s_prob[r];
-        route_pos[r] = pos;
-        if (sort_order != nullptr) sort_order[pos] = r;
-      }
-      __syncwarp();
+  if (warp == 0)
+    warp_stable_scatter(s_idx, s_prob, N * k, k, s_cnt, perm_token, perm_prob, route_pos,
+                        sort_order, lane);
+}
+
+// Fused single-CTA route for small batches (decode): top-k, softmax, counts,
+// offsets, tile offsets and the in-order permutation in one launch.
+__global__ void __launch_bounds__(1024) route_small_kernel(
+    const float* __restrict__ logits, const float* __restrict__ bias, int N, int E, int k,
+    int tile_m, int64_t* __restrict__ topk_idx, float* __restrict__ topk_prob,
+    int* __restrict__ counts, int* __restrict__ offsets, int* __restrict__ tile_offsets,
+    int* __restrict__ perm_token, float* __restrict__ perm_prob, int* __restrict__ route_pos,
+    int64_t* __restrict__ sort_order) {
+  __shared__ int s_idx[256 * kMaxTopK / 4];  // N*k <= 2048
+  __shared__ float s_prob[256 * kMaxTopK / 4];
+  __shared__ int s_cnt[kMaxExperts];
+  __shared__ int s_warp[32];
+  cta_topk_plan(logits, bias, N, E, k, tile_m, s_idx, s_prob, s_cnt, s_warp, topk_idx, topk_prob,
+                counts, offsets, tile_offsets, perm_token, perm_prob, route_pos, sort_order);
+}
+
+// Dispatch plan of N*k <= 2048 routes whose top-k (from router_topk_kernel)
+// is already in topk_idx / topk_prob: one CTA of 1024 threads.
+__global__ void __launch_bounds__(1024) plan_small_kernel(
+    const int64_t* __restrict__ topk_idx, const float* __restrict__ topk_prob, int N, int E,
+    int k, int tile_m, int* __restrict__ counts, int* __restrict__ offsets,
+    int* __restrict__ tile_offsets, int* __restrict__ perm_token, float* __restrict__ perm_prob,
+    int* __restrict__ route_pos, int64_t* __restrict__ sort_order) {
+  __shared__ int s_idx[256 * kMaxTopK / 4];
+  __shared__ float s_prob[256 * kMaxTopK / 4];
+  __shared__ int s_cnt[kMaxExperts];
+  __shared__ int s_warp[32];
+  for (int e = threadIdx.x; e < E; e += blockDim.x) s_cnt[e] = 0;
+  __syncthreads();
+  for (int r = threadIdx.x; r < N * k; r += blockDim.x) {
+    const int e = static_cast<int>(topk_idx[r]);
+    s_idx[r] = e;
+    s_prob[r] = topk_prob[r];
+    atomicAdd(&s_cnt[e], 1);
+  }
+  __syncthreads();
+  cta_plan_tail(N, E, k, tile_m, s_idx, s_prob, s_cnt, s_warp, counts, offsets, tile_offsets,
+                perm_token, perm_prob, route_pos, sort_order);
+}
+
+// Sum over the 256 threads of a CTA in a fixed order (s_red: 8 floats).
+__device__ __forceinline__ float block_sum_256(float v, float* s_red) {
+  v = warp_sum(v);
+  __syncthreads();  // previous readers of s_red are done
+  if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) tot += s_red[i];
+  return tot;
+}
+
+// Router input of one token by a CTA of 256 threads, float4 vectors (VMAX
+// per thread: D <= 1024 * VMAX, D % 4 == 0):
+//   streams[n] += delta[n] (nullable)
+//   m = streams[n] * rsqrt(mean(streams[n]^2) + eps) * ffn_w   -> m_bf (bf16)
+//   r = m * rsqrt(mean(m^2) + eps) * rn_w                      -> r_out (fp32)
+// (PhysicalBlock ffn_norm, then ContextAwareRouter.norm on the fp32 value,
+// context_router.py:62).  Every caller gets identical values.
+template <int VMAX>
+__device__ __forceinline__ void cta_router_input(float* __restrict__ streams,
+                                                 const __nv_bfloat16* __restrict__ delta, int n,
+                                                 int D, const float* __restrict__ ffn_w,
+                                                 const float* __restrict__ rn_w, float eps,
+                                                 __nv_bfloat16* __restrict__ m_bf, float* r_out,
+                                                 float* s_red) {
+  const int nv = D >> 2;
+  float4* x4 = reinterpret_cast<float4*>(streams + static_cast<int64_t>(n) * D);
+  const uint2* d2 = delta != nullptr
+                        ? reinterpret_cast<const uint2*>(delta + static_cast<int64_t>(n) * D)
+                        : nullptr;
+  uint2* m2 = reinterpret_cast<uint2*>(m_bf + static_cast<int64_t>(n) * D);
+  float4 v[VMAX];
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < VMAX; ++j) {
+    const int c = threadIdx.x + 256 * j;
+    if (c >= nv) continue;
+    float4 a = x4[c];
+    if (d2 != nullptr) {
+      const uint2 u = __ldg(d2 + c);
+      const float2 lo = unpack_bf16x2(u.x), hi = unpack_bf16x2(u.y);
+      a.x += lo.x;
+      a.y += lo.y;
+      a.z += hi.x;
+      a.w += hi.y;
+      x4[c] = a;
     }
+    v[j] = a;
+    ss += a.x * a.x + a.y * a.y + a.z * a.z + a.w * a.w;
+  }
+  const float inv = rsqrtf(block_sum_256(ss, s_red) / static_cast<float>(D) + eps);
+  float ss2 = 0.f;
+#pragma unroll
+  for (int j = 0; j < VMAX; ++j) {
+    const int c = threadIdx.x + 256 * j;
+    if (c >= nv) continue;
+    const float4 w = __ldg(reinterpret_cast<const float4*>(ffn_w) + c);
+    float4 m = v[j];
+    m.x = m.x * inv * w.x;
+    m.y = m.y * inv * w.y;
+    m.z = m.z * inv * w.z;
+    m.w = m.w * inv * w.w;
+    m2[c] = make_uint2(pack_bf16x2(m.x, m.y), pack_bf16x2(m.z, m.w));
+    v[j] = m;
+    ss2 += m.x * m.x + m.y * m.y + m.z * m.z + m.w * m.w;
+  }
+  const float inv2 = rsqrtf(block_sum_256(ss2, s_red) / static_cast<float>(D) + eps);
+#pragma unroll
+  for (int j = 0; j < VMAX; ++j) {
+    const int c = threadIdx.x + 256 * j;
+    if (c >= nv) continue;
+    const float4 w = __ldg(reinterpret_cast<const float4*>(rn_w) + c);
+    const float4 m = v[j];
+    reinterpret_cast<float4*>(r_out)[c] =
+        make_float4(m.x * inv2 * w.x, m.y * inv2 * w.y, m.z * inv2 * w.z, m.w * inv2 * w.w);
   }
 }
 
-// Decode-step router, one CTA of 256 threads: for every token
-//   streams += delta;  m = RMSNorm_ffn(streams)          (bf16 copy -> m_bf)
-//   r = RMSNorm_router(m);  logits = W_r r               (fp32)
-// followed by top-k + softmax and the in-order dispatch plan exactly as
-// route_small_kernel (model/model.py:214-241, context_router.py:62-74,
-// moe.py:42-60).  Dynamic shared memory: r rows [8][D] | logits [N][E].
+// Logit dot(r, Wr[e]) by one warp: lane-strided float4 products, then the
+// xor tree of warp_sum (fp32, the same order for every caller).
+__device__ __forceinline__ float warp_logit(const float* __restrict__ Wr, int e, const float* r,
+                                            int D, int lane) {
+  const float4* w = reinterpret_cast<const float4*>(Wr + static_cast<int64_t>(e) * D);
+  const float4* x = reinterpret_cast<const float4*>(r);
+  float acc = 0.f;
+#pragma unroll 8
+  for (int c = lane; c < (D >> 2); c += 32) {
+    const float4 a = __ldg(w + c);
+    const float4 b = x[c];
+    acc += a.x * b.x + a.y * b.y + a.z * b.z + a.w * b.w;
+  }
+  return warp_sum(acc);
+}
+
+// Decode-step router in one CTA (small N*E): router input of each token,
+// logits (one warp per (token, expert) pair), then top-k and plan.
+template <int VMAX>
 __global__ void __launch_bounds__(256) router_fused_kernel(
     float* __restrict__ streams, const __nv_bfloat16* __restrict__ delta, int N, int D,
     const float* __restrict__ ffn_w, const float* __restrict__ rn_w, const float* __restrict__ Wr,
@@ -356,105 +532,70 @@ __global__ void __launch_bounds__(256) router_fused_kernel(
   __shared__ float s_prob[256 * kMaxTopK / 4];
   __shared__ int s_cnt[kMaxExperts];
   __shared__ int s_warp[32];
+  __shared__ float s_red[8];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  float* s_r = s_dyn;                 // [8][D] normalised router inputs
-  float* s_logits = s_dyn + 8 * D;    // [N][E]
-  const int nvec = D / 4;
-  for (int n0 = 0; n0 < N; n0 += 8) {
-    // ---- residual add and the two RMSNorms, one token per warp
-    const int n = n0 + warp;
-    float* r = s_r + warp * D;
-    if (n < N) {
-      float* x = streams + static_cast<int64_t>(n) * D;
-      float ss = 0.f;
-      for (int d = lane; d < D; d += 32) {
-        float v = x[d];
-        if (delta != nullptr) {
-          v += bf2f(delta[static_cast<int64_t>(n) * D + d]);
-          x[d] = v;
-        }
-        r[d] = v;
-        ss += v * v;
-      }
-      const float inv = rsqrtf(warp_sum(ss) / static_cast<float>(D) + eps);
-      float ss2 = 0.f;
-      for (int d = lane; d < D; d += 32) {
-        const float m = r[d] * inv * ffn_w[d];
-        m_bf[static_cast<int64_t>(n) * D + d] = f2bf(m);
-        r[d] = m;
-        ss2 += m * m;
-      }
-      const float inv2 = rsqrtf(warp_sum(ss2) / static_cast<float>(D) + eps);
-      for (int d = lane; d < D; d += 32) r[d] = r[d] * inv2 * rn_w[d];
-    }
-    __syncthreads();
-    // ---- logits: 16 threads per (token, expert) pair, all row loads in flight
-    const int nt = min(8, N - n0);
-    const int g = threadIdx.x >> 4, gl = threadIdx.x & 15;
-    for (int pr = g; pr < nt * E; pr += 16) {
-      const int t = pr / E, e = pr - t * E;
-      const float4* w = reinterpret_cast<const float4*>(Wr + static_cast<int64_t>(e) * D);
-      const float4* rr = reinterpret_cast<const float4*>(s_r + t * D);
-      float acc = 0.f;
-#pragma unroll 8
-      for (int c = gl; c < nvec; c += 16) {
-        const float4 a = __ldg(w + c);
-        const float4 b = rr[c];
-        acc += a.x * b.x + a.y * b.y + a.z * b.z + a.w * b.w;
-      }
-#pragma unroll
-      for (int o = 8; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-      if (gl == 0) s_logits[(n0 + t) * E + e] = acc;
-    }
-    __syncthreads();
-  }
-  for (int e = threadIdx.x; e < E; e += blockDim.x) s_cnt[e] = 0;
+  float* s_r = s_dyn;               // [N][D] router inputs
+  float* s_logits = s_dyn + N * D;  // [N][E]
+  for (int n = 0; n < N; ++n)
+    cta_router_input<VMAX>(streams, delta, n, D, ffn_w, rn_w, eps, m_bf, s_r + n * D, s_red);
   __syncthreads();
-  for (int t = warp; t < N; t += 8) {
-    int idx;
-    float val;
-    warp_topk_row(s_logits + t * E, nullptr, E, k, lane, idx, val);
-    const float p = warp_topk_softmax(val, k, lane);
-    if (lane < k) {
-      s_idx[t * k + lane] = idx;
-      s_prob[t * k + lane] = p;
-      topk_idx[static_cast<int64_t>(t) * k + lane] = idx;
-      topk_prob[static_cast<int64_t>(t) * k + lane] = p;
-      atomicAdd(&s_cnt[idx], 1);
-    }
+  for (int p = warp; p < N * E; p += 8) {
+    const int t = p / E, e = p - t * E;
+    const float l = warp_logit(Wr, e, s_r + t * D, D, lane);
+    if (lane == 0) s_logits[p] = l;
   }
   __syncthreads();
-  const int c = threadIdx.x < E ? s_cnt[threadIdx.x] : 0;
-  int total = 0;
-  const int off = block_exclusive_scan(c, s_warp, total);
-  const int tiles = threadIdx.x < E ? static_cast<int>(ceil_div(c, tile_m)) : 0;
-  int total_tiles = 0;
-  const int toff = block_exclusive_scan(tiles, s_warp, total_tiles);
-  if (threadIdx.x < E) {
-    counts[threadIdx.x] = c;
-    offsets[threadIdx.x] = off;
-    tile_offsets[threadIdx.x] = toff;
-    s_cnt[threadIdx.x] = off;
-  }
-  if (threadIdx.x == 0) {
-    offsets[E] = total;
-    tile_offsets[E] = total_tiles;
-  }
-  __syncthreads();
-  if (warp == 0) {
-    for (int t = 0; t < N; ++t) {
-      if (lane < k) {
-        const int rr = t * k + lane;
-        const int e = s_idx[rr];
-        const int pos = s_cnt[e];
-        s_cnt[e] = pos + 1;
-        perm_token[pos] = t;
-        perm_prob[pos] = s_prob[rr];
-        route_pos[rr] = pos;
-      }
-      __syncwarp();
-    }
-  }
+  cta_topk_plan(s_logits, nullptr, N, E, k, tile_m, s_idx, s_prob, s_cnt, s_warp, topk_idx,
+                topk_prob, counts, offsets, tile_offsets, perm_token, perm_prob, route_pos,
+                nullptr);
+}
+
+// Multi-CTA decode router, step 1: router input of one token per CTA.
+template <int VMAX>
+__global__ void __launch_bounds__(256) router_input_kernel(
+    float* __restrict__ streams, const __nv_bfloat16* __restrict__ delta, int D,
+    const float* __restrict__ ffn_w, const float* __restrict__ rn_w, float eps,
+    __nv_bfloat16* __restrict__ m_bf, float* __restrict__ r) {
+  __shared__ float s_red[8];
+  cta_router_input<VMAX>(streams, delta, blockIdx.x, D, ffn_w, rn_w, eps, m_bf,
+                         r + static_cast<int64_t>(blockIdx.x) * D, s_red);
+}
+
+// Multi-CTA decode router, step 2: one warp per (token, expert) logit.
+__global__ void __launch_bounds__(256) router_pair_logits_kernel(const float* __restrict__ r,
+                                                                 const float* __restrict__ Wr,
+                                                                 int N, int D, int E,
+                                                                 float* __restrict__ logits) {
+  const int lane = threadIdx.x & 31;
+  const int p = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (p >= N * E) return;  // whole warps leave together
+  const int t = p / E, e = p - t * E;
+  const float l = warp_logit(Wr, e, r + static_cast<int64_t>(t) * D, D, lane);
+  if (lane == 0) logits[p] = l;
+}
+
+}  // namespace
+}  // namespace llmyb
+
+namespace llmyb {
+namespace {
+
+// float4 vectors per thread of the router-input routine (0: D unsupported)
+int router_vmax(int D) {
+  if (D <= 0 || D % 4 != 0) return 0;
+  if (D <= 1024) return 1;
+  if (D <= 2048) return 2;
+  if (D <= 4096) return 4;
+  if (D <= 8192) return 8;
+  return 0;
+}
+
+bool router_aligned(const void* streams, const void* delta, const void* ffn_norm,
+                    const void* router_norm, const void* w_router, const void* m_bf) {
+  return ((reinterpret_cast<uintptr_t>(streams) | reinterpret_cast<uintptr_t>(ffn_norm) |
+           reinterpret_cast<uintptr_t>(router_norm) | reinterpret_cast<uintptr_t>(w_router)) &
+          15u) == 0 &&
+         ((reinterpret_cast<uintptr_t>(delta) | reinterpret_cast<uintptr_t>(m_bf)) & 7u) == 0;
 }
 
 int32_t check_route_args(int N, int E, int k, int tile_m) {
@@ -549,11 +690,22 @@ int32_t route_impl(const float* logits, const float* bias, int32_t n_tokens, int
   if (n_tokens == 0) return empty_plan(n_experts, expert_counts, expert_offsets, tile_offsets, s);
   if (!logits || !topk_idx || !topk_prob || !perm_token || !perm_prob || !route_pos)
     return LLMYB_EINVAL;
-  if (n_tokens <= 256 && n_tokens * top_k <= 256 * kMaxTopK / 4) {
+  if (n_tokens <= 32 && n_tokens * top_k <= 256 * kMaxTopK / 4) {
     route_small_kernel<<<1, 1024, 0, s>>>(logits, bias, n_tokens, n_experts, top_k, tile_m,
                                           topk_idx, topk_prob, expert_counts, expert_offsets,
                                           tile_offsets, perm_token, perm_prob, route_pos,
                                           sort_order);
+    count_launch();
+    return launch_status();
+  }
+  if (n_tokens <= 256 && n_tokens * top_k <= 256 * kMaxTopK / 4) {
+    // top-k spread over CTAs (one token per warp), then the plan in one CTA
+    router_topk_kernel<<<static_cast<int>(ceil_div(n_tokens, 8)), 256, 0, s>>>(
+        logits, bias, n_tokens, n_experts, top_k, topk_idx, topk_prob);
+    count_launch();
+    plan_small_kernel<<<1, 1024, 0, s>>>(topk_idx, topk_prob, n_tokens, n_experts, top_k, tile_m,
+                                         expert_counts, expert_offsets, tile_offsets, perm_token,
+                                         perm_prob, route_pos, sort_order);
     count_launch();
     return launch_status();
   }
@@ -608,22 +760,35 @@ LLMYB_API int32_t llmyb_route_fused(float* streams, const void* delta, int32_t n
     return empty_plan(n_experts, expert_counts, expert_offsets, tile_offsets,
                       static_cast<cudaStream_t>(stream));
   }
+  const int vmax = router_vmax(d_model);
   if (n_tokens > 256 || n_tokens * top_k > 256 * kMaxTopK / 4 || n_tokens * n_experts > 256 ||
-      d_model % 4 != 0 || (reinterpret_cast<uintptr_t>(w_router) & 15u))
+      vmax == 0 || !router_aligned(streams, delta, ffn_norm, router_norm, w_router, m_bf))
     return LLMYB_EUNSUPPORTED;
-  const int bytes = (8 * d_model + n_tokens * n_experts) * static_cast<int>(sizeof(float));
-  if (bytes > 200 * 1024) return LLMYB_EUNSUPPORTED;
-  static int attr = 0;
-  if (bytes > 48 * 1024 && bytes > attr) {
-    cudaError_t e = cudaFuncSetAttribute(router_fused_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-    if (e != cudaSuccess) return e;
-    attr = bytes;
+  const int bytes = (n_tokens * d_model + n_tokens * n_experts) * static_cast<int>(sizeof(float));
+  if (bytes > 190 * 1024) return LLMYB_EUNSUPPORTED;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  auto launch = [&](auto kernel, int slot) -> int32_t {
+    static int attr[4] = {0, 0, 0, 0};
+    if (bytes > attr[slot]) {  // static + dynamic shared memory may pass 48 KB
+      cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           bytes);
+      if (e != cudaSuccess) return e;
+      attr[slot] = bytes;
+    }
+    kernel<<<1, 256, bytes, s>>>(streams, static_cast<const __nv_bfloat16*>(delta), n_tokens,
+                                 d_model, ffn_norm, router_norm, w_router, eps, n_experts, top_k,
+                                 tile_m, static_cast<__nv_bfloat16*>(m_bf), topk_idx, topk_prob,
+                                 expert_counts, expert_offsets, tile_offsets, perm_token,
+                                 perm_prob, route_pos);
+    return LLMYB_OK;
+  };
+  switch (vmax) {
+    case 1: st = launch(router_fused_kernel<1>, 0); break;
+    case 2: st = launch(router_fused_kernel<2>, 1); break;
+    case 4: st = launch(router_fused_kernel<4>, 2); break;
+    default: st = launch(router_fused_kernel<8>, 3); break;
   }
-  router_fused_kernel<<<1, 256, bytes, static_cast<cudaStream_t>(stream)>>>(
-      streams, static_cast<const __nv_bfloat16*>(delta), n_tokens, d_model, ffn_norm, router_norm,
-      w_router, eps, n_experts, top_k, tile_m, static_cast<__nv_bfloat16*>(m_bf), topk_idx,
-      topk_prob, expert_counts, expert_offsets, tile_offsets, perm_token, perm_prob, route_pos);
+  if (st) return st;
   count_launch();
   return launch_status();
 }
@@ -697,4 +862,58 @@ LLMYB_API int32_t llmyb_route_noalloc(const float* logits, const float* bias, in
   return route_impl(logits, bias, n_tokens, n_experts, top_k, tile_m, topk_idx, topk_prob,
                     expert_counts, expert_offsets, tile_offsets, perm_token, perm_prob, route_pos,
                     sort_order, scratch, static_cast<cudaStream_t>(stream));
+}
+
+// llmyb_route_fused for any decode batch N <= 256 (N*k <= 2048) in three
+// launches: the router input of each token (one CTA per token), the logits
+// (one warp per (token, expert) pair), then top-k, softmax and the dispatch
+// plan in one CTA.  scratch [N*(D+E)] fp32 holds the router inputs and the
+// logits.  The same routines as llmyb_route_fused, so the same results.
+LLMYB_API int32_t llmyb_route_decode(float* streams, const void* delta, int32_t n_tokens,
+                                     int32_t d_model, const float* ffn_norm,
+                                     const float* router_norm, const float* w_router, float eps,
+                                     int32_t n_experts, int32_t top_k, int32_t tile_m, void* m_bf,
+                                     float* logits_scratch, int64_t* topk_idx, float* topk_prob,
+                                     int32_t* expert_counts, int32_t* expert_offsets,
+                                     int32_t* tile_offsets, int32_t* perm_token,
+                                     float* perm_prob, int32_t* route_pos, void* stream) {
+  int32_t st = check_route_args(n_tokens, n_experts, top_k, tile_m);
+  if (st) return st;
+  if (!streams || !ffn_norm || !router_norm || !w_router || !m_bf || !logits_scratch ||
+      !topk_idx || !topk_prob || !expert_counts || !expert_offsets || !tile_offsets ||
+      !perm_token || !perm_prob || !route_pos)
+    return LLMYB_EINVAL;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (n_tokens == 0) return empty_plan(n_experts, expert_counts, expert_offsets, tile_offsets, s);
+  const int vmax = router_vmax(d_model);
+  if (n_tokens > 256 || n_tokens * top_k > 256 * kMaxTopK / 4 || vmax == 0 ||
+      !router_aligned(streams, delta, ffn_norm, router_norm, w_router, m_bf) ||
+      (reinterpret_cast<uintptr_t>(logits_scratch) & 15u))
+    return LLMYB_EUNSUPPORTED;
+  float* r = logits_scratch;
+  float* logits = logits_scratch + static_cast<int64_t>(n_tokens) * d_model;
+  const auto* dl = static_cast<const __nv_bfloat16*>(delta);
+  auto* mb = static_cast<__nv_bfloat16*>(m_bf);
+  switch (vmax) {
+    case 1: router_input_kernel<1><<<n_tokens, 256, 0, s>>>(streams, dl, d_model, ffn_norm,
+                                                            router_norm, eps, mb, r); break;
+    case 2: router_input_kernel<2><<<n_tokens, 256, 0, s>>>(streams, dl, d_model, ffn_norm,
+                                                            router_norm, eps, mb, r); break;
+    case 4: router_input_kernel<4><<<n_tokens, 256, 0, s>>>(streams, dl, d_model, ffn_norm,
+                                                            router_norm, eps, mb, r); break;
+    default: router_input_kernel<8><<<n_tokens, 256, 0, s>>>(streams, dl, d_model, ffn_norm,
+                                                             router_norm, eps, mb, r); break;
+  }
+  count_launch();
+  router_pair_logits_kernel<<<static_cast<int>(ceil_div(n_tokens * n_experts, 8)), 256, 0, s>>>(
+      r, w_router, n_tokens, d_model, n_experts, logits);
+  count_launch();
+  router_topk_kernel<<<static_cast<int>(ceil_div(n_tokens, 8)), 256, 0, s>>>(
+      logits, nullptr, n_tokens, n_experts, top_k, topk_idx, topk_prob);
+  count_launch();
+  plan_small_kernel<<<1, 1024, 0, s>>>(topk_idx, topk_prob, n_tokens, n_experts, top_k, tile_m,
+                                       expert_counts, expert_offsets, tile_offsets, perm_token,
+                                       perm_prob, route_pos, nullptr);
+  count_launch();
+  return launch_status();
 }

@@ -158,9 +158,12 @@ def moe_plan(topk_idx: torch.Tensor, topk_prob: torch.Tensor, n_experts: int, *,
 
 def route_fused(streams: torch.Tensor, delta: torch.Tensor | None, ffn_norm: torch.Tensor,
                 router_norm: torch.Tensor, w_router: torch.Tensor, k: int, eps: float,
-                m_bf: torch.Tensor, tile_m: int = TILE_M) -> RoutePlan:
+                m_bf: torch.Tensor, tile_m: int = TILE_M, variant: str = "auto") -> RoutePlan:
     """Decode router: streams += delta; m_bf = RMSNorm_ffn(streams); top-k over
-    w_router . RMSNorm_router(m) (fp32) and the dispatch plan, one launch."""
+    w_router . RMSNorm_router(m) (fp32) and the dispatch plan.  variant
+    "single": one CTA, one launch (N*E <= 256); "multi": route_decode (three
+    launches, any N <= 256); "auto": single for N <= 4 and N*E <= 64.  Both
+    variants give bit-identical results."""
     _require_cuda(streams, delta, ffn_norm, router_norm, w_router, m_bf)
     _inplace(streams, "streams")
     _inplace(m_bf, "m_bf")
@@ -171,6 +174,11 @@ def route_fused(streams: torch.Tensor, delta: torch.Tensor | None, ffn_norm: tor
     prob = torch.empty(n, k, dtype=torch.float32, device=dev)
     b = _plan_buffers(n, e, k, dev, False)
     delta = None if delta is None else delta.contiguous()
+    if variant == "multi" or (variant == "auto" and (n * e > 64 or n > 4)):
+        # the single CTA normalises its tokens one after another and runs
+        # 8 logit warps: worth one launch only for a few (token, expert) pairs
+        return route_decode(streams, delta, ffn_norm, router_norm, w_router, k, eps, m_bf,
+                            tile_m=tile_m)
     _native.call("llmyb_route_fused", _ptr(streams), _ptr(delta), n, d, _ptr(ffn_norm),
                  _ptr(router_norm), _ptr(w_router), float(eps), e, k, int(tile_m), _ptr(m_bf),
                  _ptr(idx), _ptr(prob), _ptr(b["counts"]), _ptr(b["offsets"]),
@@ -179,8 +187,32 @@ def route_fused(streams: torch.Tensor, delta: torch.Tensor | None, ffn_norm: tor
     return RoutePlan(idx, prob, **b, tile_m=tile_m)
 
 
+def route_decode(streams: torch.Tensor, delta: torch.Tensor | None, ffn_norm: torch.Tensor,
+                 router_norm: torch.Tensor, w_router: torch.Tensor, k: int, eps: float,
+                 m_bf: torch.Tensor, tile_m: int = TILE_M) -> RoutePlan:
+    """route_fused with one CTA per token for the logits (any N <= 256), then
+    one top-k/plan launch; bit-identical to the single-CTA route_fused."""
+    _require_cuda(streams, delta, ffn_norm, router_norm, w_router, m_bf)
+    _inplace(streams, "streams")
+    _inplace(m_bf, "m_bf")
+    n, d = streams.shape
+    e = w_router.shape[0]
+    dev = streams.device
+    idx = torch.empty(n, k, dtype=torch.int64, device=dev)
+    prob = torch.empty(n, k, dtype=torch.float32, device=dev)
+    b = _plan_buffers(n, e, k, dev, False)
+    delta = None if delta is None else delta.contiguous()
+    logits = torch.empty(n * (d + e), dtype=torch.float32, device=dev)
+    _native.call("llmyb_route_decode", _ptr(streams), _ptr(delta), n, d, _ptr(ffn_norm),
+                 _ptr(router_norm), _ptr(w_router), float(eps), e, k, int(tile_m), _ptr(m_bf),
+                 _ptr(logits), _ptr(idx), _ptr(prob), _ptr(b["counts"]), _ptr(b["offsets"]),
+                 _ptr(b["tile_offsets"]), _ptr(b["perm_token"]), _ptr(b["perm_prob"]),
+                 _ptr(b["route_pos"]), _stream())
+    return RoutePlan(idx, prob, **b, tile_m=tile_m)
+
+
 def route_fused_supported(n: int, e: int, k: int, d: int) -> bool:
-    return n * e <= 256 and n * k <= 2048 and d % 4 == 0 and e <= 256 and k <= 32
+    return n <= 256 and n * k <= 2048 and d % 4 == 0 and d <= 8192 and e <= 256 and k <= 32
 
 
 def moe_decode_experts(x: torch.Tensor, plan: RoutePlan, w13: torch.Tensor, w2: torch.Tensor,

@@ -97,6 +97,20 @@ int32_t llmyb_route_fused(float* streams, const void* delta, int32_t n_tokens, i
                           int32_t* expert_offsets, int32_t* tile_offsets, int32_t* perm_token,
                           float* perm_prob, int32_t* route_pos, void* stream);
 
+/* llmyb_route_fused for decode batches of any size up to N = 256 (N*k <=
+ * 2048, E <= 256, D % 4 == 0, D <= 8192) in three launches: the router input
+ * of each token (one CTA per token), the logits (one warp per (token,
+ * expert) pair), then top-k, softmax and the plan in one CTA.
+ * logits_scratch holds N*(D+E) fp32 (router inputs, then logits).  Results
+ * are bit-identical to llmyb_route_fused wherever both apply. */
+int32_t llmyb_route_decode(float* streams, const void* delta, int32_t n_tokens, int32_t d_model,
+                           const float* ffn_norm, const float* router_norm,
+                           const float* w_router, float eps, int32_t n_experts, int32_t top_k,
+                           int32_t tile_m, void* m_bf, float* logits_scratch, int64_t* topk_idx,
+                           float* topk_prob, int32_t* expert_counts, int32_t* expert_offsets,
+                           int32_t* tile_offsets, int32_t* perm_token, float* perm_prob,
+                           int32_t* route_pos, void* stream);
+
 /* --------------------------------------------------------------- MoE FFN
  * Replaces _moe_dispatch_fused's expert math (model/layers/moe.py:68-81),
  * triton_moe_dispatch (runpod/kernels/triton_swiglu_moe.py:160-266) and the

@@ -94,3 +94,65 @@ def test_plan_flags_out_of_range_expert(cuda):
     torch.cuda.synchronize()
     with pytest.raises(RuntimeError, match="invalid argument"):
         kernels.check_device_status()
+
+
+def _decode_router_inputs(n, d, e, seed):
+    rng = np.random.default_rng(seed)
+    streams = rng.normal(0, 1, (n, d)).astype(np.float32)
+    delta = rng.normal(0, 0.5, (n, d)).astype(np.float32)
+    ffn_w = rng.uniform(0.5, 1.5, d).astype(np.float32)
+    rn_w = rng.uniform(0.5, 1.5, d).astype(np.float32)
+    w_r = rng.normal(0, 0.02, (e, d)).astype(np.float32)
+    return streams, delta, ffn_w, rn_w, w_r
+
+
+def _decode_route(fn, streams, delta, ffn_w, rn_w, w_r, k, eps=1e-6):
+    from hybrid_llm_b200 import kernels
+    st = torch.from_numpy(streams).cuda()
+    dl = torch.from_numpy(delta).cuda().bfloat16()
+    m_bf = torch.empty(st.shape, dtype=torch.bfloat16, device="cuda")
+    plan = fn(st, dl, torch.from_numpy(ffn_w).cuda(), torch.from_numpy(rn_w).cuda(),
+              torch.from_numpy(w_r).cuda(), k, eps, m_bf, tile_m=128)
+    torch.cuda.synchronize()
+    return st, m_bf, plan
+
+
+@pytest.mark.parametrize("n,d,e,k", [(1, 768, 16, 2), (4, 512, 64, 8), (16, 2048, 16, 2)])
+def test_route_decode_matches_single_cta(cuda, n, d, e, k):
+    """The multi-CTA decode router equals the one-CTA fused router bit for bit."""
+    from hybrid_llm_b200 import kernels
+    args = _decode_router_inputs(n, d, e, seed=n + e)
+    a = _decode_route(lambda *x, **kw: kernels.route_fused(*x, **kw, variant="single"), *args, k)
+    b = _decode_route(kernels.route_decode, *args, k)
+    assert torch.equal(a[0], b[0]) and torch.equal(a[1], b[1])
+    for f in ("topk_idx", "topk_prob", "counts", "offsets", "tile_offsets", "perm_token",
+              "perm_prob", "route_pos"):
+        assert torch.equal(getattr(a[2], f), getattr(b[2], f)), f
+
+
+@pytest.mark.parametrize("n,d,e,k", [(64, 2048, 64, 8), (256, 768, 16, 2), (33, 1024, 256, 32)])
+def test_route_decode_matches_oracle(cuda, n, d, e, k):
+    """Residual add, the two RMSNorms and the fp32 router logits against fp64:
+    indices equal wherever the k-th and (k+1)-th logits are not within 1e-4."""
+    from hybrid_llm_b200 import kernels
+    streams, delta, ffn_w, rn_w, w_r = _decode_router_inputs(n, d, e, seed=7 * n + d)
+    st, m_bf, plan = _decode_route(kernels.route_fused, streams, delta, ffn_w, rn_w, w_r, k)
+    x = streams.astype(np.float64) + torch.from_numpy(delta).bfloat16().double().numpy()
+    np.testing.assert_allclose(st.cpu().numpy(), x, rtol=1e-6, atol=1e-6)
+    m = x / np.sqrt((x * x).mean(-1, keepdims=True) + 1e-6) * ffn_w
+    np.testing.assert_allclose(m_bf.float().cpu().numpy(), m, rtol=1e-2, atol=1e-2)
+    r = m / np.sqrt((m * m).mean(-1, keepdims=True) + 1e-6) * rn_w
+    logits = r @ w_r.astype(np.float64).T
+    idx, prob = routing.router_topk(logits.astype(np.float32), k)
+    got = plan.topk_idx.cpu().numpy()
+    srt = -np.sort(-logits, axis=-1)
+    clear = (srt[:, k - 1] - srt[:, k]) > 1e-4 if k < e else np.ones(n, bool)
+    assert clear.mean() > 0.8
+    np.testing.assert_array_equal(np.sort(got[clear], -1), np.sort(idx[clear], -1))
+    np.testing.assert_allclose(plan.topk_prob.cpu().numpy()[clear], prob[clear], rtol=1e-4,
+                               atol=1e-5)
+    ref = routing.dispatch_plan(got, e, tile_m=128)
+    for f in ("counts", "offsets", "tile_offsets", "perm_token", "route_pos"):
+        np.testing.assert_array_equal(getattr(plan, f).cpu().numpy(), ref[f], err_msg=f)
+    np.testing.assert_array_equal(plan.perm_prob.cpu().numpy(),
+                                  plan.topk_prob.cpu().numpy().reshape(-1)[ref["sort_order"]])
