@@ -72,7 +72,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "llmyb_csa_local_prefill": (I32, [P, I64, P, I64, P, I64, I32, I32, I32, I32, I32, I32, P, I64,
                                       P, P]),
     "llmyb_csa_local_decode": (I32, [P, I64, P, I64, P, I64, P, P, P, I32, I32, I32, I32, I32, P,
-                                     I64, P]),
+                                     I64, P, P]),
     # diagnostics
     "llmyb_launch_count": (I64, []),
     # residual stream

@@ -32,6 +32,7 @@
 
 #include "common.cuh"
 #include "mma.cuh"
+#include "sm100.cuh"
 
 #include <algorithm>
 
@@ -410,13 +411,19 @@ constexpr int kMaxChunks = 8;  // 16-byte chunks of a K row per lane: H*DH <= 20
 // p [kpc] | partial out [groups][D].
 // Four CTAs per SM (64 registers): a batch of 64 rows is 64 clusters of 8,
 // which must all be resident at once to run in a single wave.
-__global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(256, 4)
+// STAGED (small batches): the CTA's K and V ring rows are brought into
+// shared memory by two bulk copies issued at entry, so the score and value
+// loops read shared memory instead of waiting on one global round trip per
+// key; the arithmetic is that of the unstaged kernel.
+template <bool STAGED>
+__global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(256, STAGED ? 1 : 4)
     csa_decode_kernel(const __nv_bfloat16* __restrict__ q, int64_t sq,
                       const __nv_bfloat16* __restrict__ knew, int64_t skn,
                       const __nv_bfloat16* __restrict__ vnew, int64_t svn,
                       __nv_bfloat16* __restrict__ kcache, __nv_bfloat16* __restrict__ vcache,
                       const int* __restrict__ positions, int H, int DH, int D, int Wc,
-                      float scale_log2, __nv_bfloat16* __restrict__ out, int64_t so) {
+                      float scale_log2, __nv_bfloat16* __restrict__ out, int64_t so,
+                      int32_t* dev_status) {
   extern __shared__ float dsm[];
   cg::cluster_group cluster = cg::this_cluster();
   const int crank = static_cast<int>(cluster.block_rank());
@@ -438,6 +445,11 @@ __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(256, 4)
   float* s_L = s_M + H;
   float* s_p = s_L + H;
   float* s_o = s_p + kpc;            // [groups][D]
+  // STAGED only: K rows [kpc][HD], V rows [kpc][D] (bf16), two mbarriers
+  __nv_bfloat16* s_k = reinterpret_cast<__nv_bfloat16*>(
+      dsm + ((HD / 2 + H * kpc + 4 * H + kpc + groups * D + 3) & ~3));  // 16-byte aligned
+  __nv_bfloat16* s_v = s_k + static_cast<int64_t>(kpc) * HD;
+  uint64_t* s_bar = reinterpret_cast<uint64_t*>(s_v + static_cast<int64_t>(kpc) * D);
 
   const int pos = positions[b];
   const int n_valid = min(pos + 1, Wc);
@@ -446,19 +458,42 @@ __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(256, 4)
   const int j_end = min(Wc, j_begin + kpc);
   const int nk = max(0, min(j_end, n_valid) - j_begin);  // valid keys of this CTA
   const int64_t cache_row = static_cast<int64_t>(b) * Wc;
+  // rows j of K / V are read at kb + j*HD / vb + j*D (global ring, or the
+  // staged copy of this CTA's keys)
+  const __nv_bfloat16* kb = kcache + cache_row * HD;
+  const __nv_bfloat16* vb = vcache + cache_row * D;
+  bool staged_ok = true;
+  if (STAGED) {
+    if (tid == 0) {
+      sm100::mbar_init(&s_bar[0], 1);
+      sm100::mbar_init(&s_bar[1], 1);
+      sm100::fence_mbar_init();
+      if (nk > 0) {
+        const uint32_t kbytes = static_cast<uint32_t>(nk) * HD * 2;
+        const uint32_t vbytes = static_cast<uint32_t>(nk) * D * 2;
+        sm100::mbar_arrive_expect_tx(&s_bar[0], kbytes);
+        sm100::bulk_load(s_k, kcache + (cache_row + j_begin) * HD, kbytes, &s_bar[0]);
+        sm100::mbar_arrive_expect_tx(&s_bar[1], vbytes);
+        sm100::bulk_load(s_v, vcache + (cache_row + j_begin) * D, vbytes, &s_bar[1]);
+      }
+    }
+    kb = s_k - static_cast<int64_t>(j_begin) * HD;
+    vb = s_v - static_cast<int64_t>(j_begin) * D;
+  }
 
   for (int c = tid; c < nch; c += 256)
     reinterpret_cast<uint4*>(s_q)[c] = reinterpret_cast<const uint4*>(q + b * sq)[c];
   __syncthreads();
+  if (STAGED && nk > 0) staged_ok = sm100::mbar_wait(&s_bar[0], 0, dev_status, nullptr);
   // ---- scores: one key per warp iteration, the whole K row in flight
   for (int jl = warp; jl < nk; jl += 8) {
     const int j = j_begin + jl;
-    const __nv_bfloat16* kr = (j == cur_slot) ? knew + b * skn : kcache + (cache_row + j) * HD;
+    const __nv_bfloat16* kr = (j == cur_slot) ? knew + b * skn : kb + static_cast<int64_t>(j) * HD;
     uint4 kv[kMaxChunks];
 #pragma unroll
     for (int i = 0; i < kMaxChunks; ++i) {
       const int c = lane + 32 * i;
-      if (c < nch) kv[i] = __ldg(reinterpret_cast<const uint4*>(kr) + c);
+      if (c < nch) kv[i] = reinterpret_cast<const uint4*>(kr)[c];
     }
 #pragma unroll
     for (int i = 0; i < kMaxChunks; ++i) {
@@ -527,6 +562,7 @@ __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(256, 4)
   }
   __syncthreads();
   // ---- partial output: thread = (key group, 16-byte column chunk)
+  if (STAGED && nk > 0 && staged_ok) staged_ok = sm100::mbar_wait(&s_bar[1], 0, dev_status, nullptr);
   {
     const int g = tid / vch, c = tid - g * vch;
     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
@@ -536,8 +572,8 @@ __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(256, 4)
       for (; j < nk; j += groups) {
         const int jj = j_begin + j;
         const __nv_bfloat16* vr =
-            (jj == cur_slot) ? vnew + b * svn : vcache + (cache_row + jj) * D;
-        const uint4 v4 = __ldg(reinterpret_cast<const uint4*>(vr) + c);
+            (jj == cur_slot) ? vnew + b * svn : vb + static_cast<int64_t>(jj) * D;
+        const uint4 v4 = reinterpret_cast<const uint4*>(vr)[c];
         const float p = s_p[j];
         const uint32_t w[4] = {v4.x, v4.y, v4.z, v4.w};
 #pragma unroll
@@ -565,6 +601,10 @@ __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(256, 4)
     float acc = 0.f;
     for (int r = 0; r < kClusterCtas; ++r) acc += *cluster.map_shared_rank(&s_o[d], r);
     out[b * so + d] = f2bf(acc);
+  }
+  if (STAGED && nk > 0) {  // no bulk copy may still be writing when the CTA exits
+    sm100::mbar_wait(&s_bar[0], 0, dev_status, nullptr);
+    sm100::mbar_wait(&s_bar[1], 0, dev_status, nullptr);
   }
   cluster.sync();  // keep shared memory alive until every peer finished reading
 }
@@ -707,7 +747,8 @@ LLMYB_API int32_t llmyb_csa_local_decode(const void* q, int64_t q_stride, const 
                                          int64_t vnew_stride, void* kcache, void* vcache,
                                          const int32_t* positions, int32_t batch, int32_t heads,
                                          int32_t head_dim, int32_t d_model, int32_t window,
-                                         void* out, int64_t out_stride, void* stream) {
+                                         void* out, int64_t out_stride, int32_t* dev_status,
+                                         void* stream) {
   if (!q || !knew || !vnew || !kcache || !vcache || !positions || !out || batch < 0 ||
       heads <= 0 || head_dim <= 0 || window <= 0)
     return LLMYB_EINVAL;
@@ -722,20 +763,32 @@ LLMYB_API int32_t llmyb_csa_local_decode(const void* q, int64_t q_stride, const 
     return LLMYB_EUNSUPPORTED;
   const int kpc = (window + kClusterCtas - 1) / kClusterCtas;
   const int groups = std::max(1, 256 / (d_model / 8));
-  const int bytes = (hd / 2 + heads * kpc + 4 * heads + kpc + groups * d_model) * 4;
+  const int base_floats = (hd / 2 + heads * kpc + 4 * heads + kpc + groups * d_model + 3) & ~3;
+  const int64_t staged_bytes =
+      static_cast<int64_t>(base_floats) * 4 + static_cast<int64_t>(kpc) * (hd + d_model) * 2 + 16;
+  // small batches: one cluster per row is far from filling the GPU, so each
+  // CTA stages its keys in shared memory (one CTA per SM) to cut latency
+  const bool staged = batch <= 32 && staged_bytes <= 220 * 1024;
+  const int bytes = staged ? static_cast<int>(staged_bytes) : base_floats * 4;
   if (bytes > 227 * 1024) return LLMYB_EUNSUPPORTED;
-  static int attr_bytes = 0;
-  if (bytes > attr_bytes) {
-    int32_t st = set_smem(csa_decode_kernel, bytes);
-    if (st) return st;
-    attr_bytes = bytes;
-  }
-  csa_decode_kernel<<<batch * kClusterCtas, 256, bytes, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __nv_bfloat16*>(q), q_stride, static_cast<const __nv_bfloat16*>(knew),
-      knew_stride, static_cast<const __nv_bfloat16*>(vnew), vnew_stride,
-      static_cast<__nv_bfloat16*>(kcache), static_cast<__nv_bfloat16*>(vcache), positions, heads,
-      head_dim, d_model, window, kLog2e / sqrtf(static_cast<float>(head_dim)),
-      static_cast<__nv_bfloat16*>(out), out_stride);
+  auto launch = [&](auto kernel, int& attr_bytes) -> int32_t {
+    if (bytes > attr_bytes) {
+      int32_t st = set_smem(kernel, bytes);
+      if (st) return st;
+      attr_bytes = bytes;
+    }
+    kernel<<<batch * kClusterCtas, 256, bytes, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<const __nv_bfloat16*>(q), q_stride, static_cast<const __nv_bfloat16*>(knew),
+        knew_stride, static_cast<const __nv_bfloat16*>(vnew), vnew_stride,
+        static_cast<__nv_bfloat16*>(kcache), static_cast<__nv_bfloat16*>(vcache), positions,
+        heads, head_dim, d_model, window, kLog2e / sqrtf(static_cast<float>(head_dim)),
+        static_cast<__nv_bfloat16*>(out), out_stride, dev_status);
+    return LLMYB_OK;
+  };
+  static int attr_staged = 0, attr_plain = 0;
+  const int32_t st = staged ? launch(csa_decode_kernel<true>, attr_staged)
+                            : launch(csa_decode_kernel<false>, attr_plain);
+  if (st) return st;
   count_launch();
   return launch_status();
 }

@@ -24,20 +24,50 @@ namespace llmyb {
 namespace {
 
 constexpr int kTok = 16;        // token rows staged per pass
+
+// Expert of grid slot `slot`.  Compacted grids (compact != 0) give each
+// routed expert a run of CTAs: slot a is the a-th expert with rows, found from
+// the plan offsets on the device (-1: fewer experts have rows than slots);
+// otherwise slot e is expert e.  Called by all threads; returns to all.
+__device__ __forceinline__ int slot_expert(const int* __restrict__ expert_offsets, int E, int slot,
+                                           int compact) {
+  if (!compact) return slot;
+  __shared__ int s_e;
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
+    int found = -1, seen = 0;
+    for (int e0 = 0; e0 < E && found < 0; e0 += 32) {
+      const int e = e0 + lane;
+      const bool act = e < E && __ldg(expert_offsets + e + 1) > __ldg(expert_offsets + e);
+      const unsigned m = __ballot_sync(0xffffffffu, act);
+      const int need = slot - seen;  // index among this chunk's active experts
+      if (need < __popc(m)) {
+        unsigned mm = m;
+        for (int i = 0; i < need; ++i) mm &= mm - 1;  // drop the lowest `need` bits
+        found = e0 + __ffs(mm) - 1;
+      }
+      seen += __popc(m);
+    }
+    if (lane == 0) s_e = found;
+  }
+  __syncthreads();
+  return s_e;
+}
 constexpr int kWarps = 8;       // features (up) or columns (down) per CTA
 constexpr int kMaxChunk = 8;    // 16-byte chunks per lane and row: D, F <= 2048
 
 __global__ void __launch_bounds__(256) moe_decode_up_kernel(
     const __nv_bfloat16* __restrict__ x, const int* __restrict__ perm_token,
     const int* __restrict__ expert_offsets, const __nv_bfloat16* __restrict__ w13, int D, int F,
-    __nv_bfloat16* __restrict__ h_perm) {
+    int E, int compact, __nv_bfloat16* __restrict__ h_perm) {
   extern __shared__ __nv_bfloat16 s_x[];  // [kTok][D]
   const int fblocks = F / kWarps;
-  const int e = blockIdx.x / fblocks;
+  const int e = slot_expert(expert_offsets, E, blockIdx.x / fblocks, compact);
+  if (e < 0) return;
   const int r0 = __ldg(expert_offsets + e), r1 = __ldg(expert_offsets + e + 1);
   if (r1 <= r0) return;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int f = (blockIdx.x - e * fblocks) * kWarps + warp;
+  const int f = (blockIdx.x % fblocks) * kWarps + warp;
   const int nch = D / 8;
   // interleaved stack: feature f of tile j = f/128 -> gate row 256j + f%128, up row +128
   const int64_t grow = static_cast<int64_t>(e) * 2 * F + (f / 128) * 256 + (f % 128);
@@ -93,14 +123,15 @@ __global__ void __launch_bounds__(256) moe_decode_up_kernel(
 __global__ void __launch_bounds__(256) moe_decode_down_kernel(
     const __nv_bfloat16* __restrict__ h_perm, const float* __restrict__ perm_prob,
     const int* __restrict__ expert_offsets, const __nv_bfloat16* __restrict__ w2, int D, int F,
-    const int* __restrict__ out_row, __nv_bfloat16* __restrict__ y_perm) {
+    int E, int compact, const int* __restrict__ out_row, __nv_bfloat16* __restrict__ y_perm) {
   extern __shared__ __nv_bfloat16 s_h[];  // [kTok][F]
   const int dblocks = D / kWarps;
-  const int e = blockIdx.x / dblocks;
+  const int e = slot_expert(expert_offsets, E, blockIdx.x / dblocks, compact);
+  if (e < 0) return;
   const int r0 = __ldg(expert_offsets + e), r1 = __ldg(expert_offsets + e + 1);
   if (r1 <= r0) return;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int d = (blockIdx.x - e * dblocks) * kWarps + warp;
+  const int d = (blockIdx.x % dblocks) * kWarps + warp;
   const int nch = F / 8;
   const uint4* wr = reinterpret_cast<const uint4*>(w2 + (static_cast<int64_t>(e) * D + d) * F);
   uint4 w4[kMaxChunk];
@@ -211,13 +242,18 @@ int32_t launch_experts(const void* x, int32_t n_tokens, int32_t d_model, int32_t
     if (e != cudaSuccess) return e;
     down_attr = down_smem;
   }
-  moe_decode_up_kernel<<<n_experts * (ffn / kWarps), 256, up_smem, s>>>(
+  // at most n_rows experts have rows: a grid over those slots only, each
+  // finding its expert on the device, when that is smaller than all E
+  const int64_t rows = static_cast<int64_t>(n_tokens) * top_k;
+  const int slots = static_cast<int>(std::min<int64_t>(n_experts, rows));
+  const int compact = slots < n_experts ? 1 : 0;
+  moe_decode_up_kernel<<<slots * (ffn / kWarps), 256, up_smem, s>>>(
       static_cast<const __nv_bfloat16*>(x), perm_token, expert_offsets,
-      static_cast<const __nv_bfloat16*>(w13), d_model, ffn, h);
+      static_cast<const __nv_bfloat16*>(w13), d_model, ffn, n_experts, compact, h);
   count_launch();
-  moe_decode_down_kernel<<<n_experts * (d_model / kWarps), 256, down_smem, s>>>(
-      h, perm_prob, expert_offsets, static_cast<const __nv_bfloat16*>(w2), d_model, ffn, out_row,
-      y);
+  moe_decode_down_kernel<<<slots * (d_model / kWarps), 256, down_smem, s>>>(
+      h, perm_prob, expert_offsets, static_cast<const __nv_bfloat16*>(w2), d_model, ffn,
+      n_experts, compact, out_row, y);
   count_launch();
   return launch_status();
 }

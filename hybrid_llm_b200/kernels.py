@@ -588,7 +588,8 @@ def csa_local_decode(q, knew, vnew, kcache, vcache, positions, heads: int, out=N
         out = torch.empty(bsz, dm, dtype=torch.bfloat16, device=q.device)
     _native.call("llmyb_csa_local_decode", _ptr(q), q.stride(0), _ptr(knew), knew.stride(0),
                  _ptr(vnew), vnew.stride(0), _ptr(kcache), _ptr(vcache), _ptr(positions), bsz,
-                 heads, hd // heads, dm, w, _ptr(out), out.stride(0), _stream())
+                 heads, hd // heads, dm, w, _ptr(out), out.stride(0),
+                 _ptr(device_status(q.device)), _stream())
     return out
 
 

@@ -307,12 +307,14 @@ int32_t llmyb_csa_local_prefill(const void* q, int64_t q_stride, const void* k, 
  * kcache [B, window, H*DH], vcache [B, window, D] hold token p at slot
  * p % window; positions[b] is the new token's position.  Writes the new K/V
  * into the ring and attends over the last min(positions[b]+1, window)
- * tokens. */
+ * tokens.  dev_status (nullable) gets LLMYB_ETIMEOUT if a staged copy of
+ * the ring rows (small batches) does not arrive within a second. */
 int32_t llmyb_csa_local_decode(const void* q, int64_t q_stride, const void* knew,
                                int64_t knew_stride, const void* vnew, int64_t vnew_stride,
                                void* kcache, void* vcache, const int32_t* positions,
                                int32_t batch, int32_t heads, int32_t head_dim, int32_t d_model,
-                               int32_t window, void* out, int64_t out_stride, void* stream);
+                               int32_t window, void* out, int64_t out_stride,
+                               int32_t* dev_status, void* stream);
 
 /* ------------------------------------------------------------- diagnostics
  * Number of kernel launches this library has issued since it was loaded

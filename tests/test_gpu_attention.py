@@ -112,3 +112,28 @@ def test_csa_local_decode_matches_oracle(cuda, b, h, dh, dm, w, pos):
                                    np.broadcast_to(valid, (b, w)))
     assert _rel(_f(out), ref) < REL
     assert torch.equal(kcd[:, slot].cpu(), kn) and torch.equal(vcd[:, slot].cpu(), vn)
+
+
+@pytest.mark.parametrize("h,dh,dm,w", [(12, 64, 768, 512), (4, 128, 256, 40), (16, 128, 2048, 256)])
+def test_csa_local_decode_staged_equals_plain(cuda, h, dh, dm, w):
+    """Batches of up to 32 rows stage each CTA's ring rows in shared memory;
+    larger batches read them from global memory.  Same rows, same results."""
+    from hybrid_llm_b200 import kernels
+    b = 40
+    rng = np.random.default_rng(h * w)
+    hd = h * dh
+    kc = _bf(rng.normal(size=(b, w, hd))).cuda()
+    vc = _bf(rng.normal(size=(b, w, dm))).cuda()
+    q = _bf(rng.normal(size=(b, hd))).cuda()
+    kn, vn = _bf(rng.normal(size=(b, hd))).cuda(), _bf(rng.normal(size=(b, dm))).cuda()
+    positions = torch.from_numpy(rng.integers(0, 3 * w, b).astype(np.int32)).cuda()
+    k1, v1 = kc.clone(), vc.clone()
+    plain = kernels.csa_local_decode(q, kn, vn, k1, v1, positions, h)       # 40 rows: plain
+    k2, v2 = kc.clone(), vc.clone()
+    staged = torch.cat([kernels.csa_local_decode(q[i:i + 8], kn[i:i + 8], vn[i:i + 8],
+                                                 k2[i:i + 8], v2[i:i + 8], positions[i:i + 8], h)
+                        for i in range(0, b, 8)])                             # 8 rows: staged
+    torch.cuda.synchronize()
+    kernels.check_device_status()
+    assert torch.equal(plain, staged)
+    assert torch.equal(k1, k2) and torch.equal(v1, v2)
