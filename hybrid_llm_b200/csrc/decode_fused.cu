@@ -1,0 +1,390 @@
+// Fused decode-step kernels for small batches (up to 8 tokens).
+//
+// A batch-1 decode step of the looped hybrid stack is a chain of a few
+// hundred dependent launches of a few microseconds each: the time goes to
+// launch gaps and global-memory round trips, not to bytes.  Per block these
+// two kernels replace four or five launches of the unfused path:
+//
+//   [A] llmyb_decode_norm_gemv   residual add (+ the routed MoE combine of the
+//                                previous block) and RMSNorm, recomputed by
+//                                every CTA for its own use, then the block's
+//                                input projection GEMV (one warp per row)
+//   [B] mixer                    gdn_step / csa_local_decode
+//   [C] llmyb_decode_out_router  output projection GEMV (+ the GDN conv gate
+//                                for its columns) by all CTAs; the last CTA to
+//                                finish adds the result to the residual
+//                                stream and runs the router and the plan
+//   [D],[E] routed experts       moe_decode up / down
+//
+// Reference: PhysicalBlock.forward_step (model/model.py:214-241), the GDN
+// conv gate (model/layers/gated_deltanet.py:257-268), CSA's output path
+// (model/layers/csa.py:132) and ContextAwareRouter (context_router.py:62-74).
+// The norms reproduce llmyb_add_rmsnorm's vector kernel and the router phase
+// runs the routines of router.cu, so both give the values of the unfused path
+// for the same inputs; the projections are warp-per-row GEMVs (fp32 sums of
+// bf16 products, bf16 outputs like the cuBLAS GEMMs they replace).
+#include "common.cuh"
+#include "router_device.cuh"
+
+#include <algorithm>
+
+namespace llmyb {
+namespace {
+
+using namespace rdev;
+
+constexpr int kMaxTokens = 8;
+
+// Dot products of one weight row (bf16, K = 256*KCH at most, K % 8 == 0)
+// with the B bf16 rows of s_x [B][K] (shared memory), summed over the warp:
+// every lane returns the B sums.  All weight loads are issued before the
+// first multiply.
+template <int BM, int KCH>
+__device__ __forceinline__ void warp_row_dot(const __nv_bfloat16* __restrict__ wrow, int K, int B,
+                                             const __nv_bfloat16* s_x, int lane, float (&acc)[BM]) {
+  const int nch = K >> 3;
+  uint4 w[KCH];
+#pragma unroll
+  for (int i = 0; i < KCH; ++i) {
+    const int c = lane + 32 * i;
+    if (c < nch) w[i] = __ldg(reinterpret_cast<const uint4*>(wrow) + c);
+  }
+#pragma unroll
+  for (int b = 0; b < BM; ++b) acc[b] = 0.f;
+#pragma unroll
+  for (int i = 0; i < KCH; ++i) {
+    const int c = lane + 32 * i;
+    if (c >= nch) continue;
+    const uint32_t ww[4] = {w[i].x, w[i].y, w[i].z, w[i].w};
+#pragma unroll
+    for (int b = 0; b < BM; ++b) {
+      if (b >= B) break;
+      const uint4 x4 = reinterpret_cast<const uint4*>(s_x + b * K)[c];
+      const uint32_t xx[4] = {x4.x, x4.y, x4.z, x4.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 wf = unpack_bf16x2(ww[e]);
+        const float2 xf = unpack_bf16x2(xx[e]);
+        acc[b] += wf.x * xf.x + wf.y * xf.y;
+      }
+    }
+  }
+#pragma unroll
+  for (int b = 0; b < BM; ++b) acc[b] = warp_sum(acc[b]);
+}
+
+// Residual add + RMSNorm of token row b into s_x (bf16), by a CTA of 256
+// threads with 8-element vectors (D <= 2048): the arithmetic of
+// add_rmsnorm_vec_kernel<1> (norm.cu).  CTA 0 also stores the updated
+// residual row and the normalised row.
+__device__ __forceinline__ void cta_add_norm_row(
+    const float* __restrict__ streams_in, const __nv_bfloat16* __restrict__ delta,
+    const int* __restrict__ route_pos, int k, int b, int D, const float* __restrict__ weight,
+    float eps, __nv_bfloat16* s_x, float* s_red, float* __restrict__ streams_out,
+    __nv_bfloat16* __restrict__ normed_out, bool writer) {
+  const int nv = D >> 3;
+  const int c = threadIdx.x;
+  float v[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  float ss = 0.f;
+  if (c < nv) {
+    const float4* x4 = reinterpret_cast<const float4*>(streams_in + static_cast<int64_t>(b) * D);
+    const float4 a = x4[2 * c], bb = x4[2 * c + 1];
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = bb.x; v[5] = bb.y; v[6] = bb.z; v[7] = bb.w;
+    if (delta != nullptr) {
+      if (route_pos != nullptr) {
+        for (int s = 0; s < k; ++s) {
+          const int64_t pos = __ldg(route_pos + static_cast<int64_t>(b) * k + s);
+          const uint4 u = __ldg(reinterpret_cast<const uint4*>(delta + pos * D) + c);
+          const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float2 f = unpack_bf16x2(w[q]);
+            v[2 * q] += f.x;
+            v[2 * q + 1] += f.y;
+          }
+        }
+      } else {
+        const uint4 u =
+            __ldg(reinterpret_cast<const uint4*>(delta + static_cast<int64_t>(b) * D) + c);
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float2 f = unpack_bf16x2(w[q]);
+          v[2 * q] += f.x;
+          v[2 * q + 1] += f.y;
+        }
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < 8; ++q) ss += v[q] * v[q];
+  }
+  ss = warp_sum(ss);
+  __syncthreads();  // earlier readers of s_red are done
+  if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) tot += s_red[i];
+  const float r = rsqrtf(tot / static_cast<float>(D) + eps);
+  if (c < nv) {
+    const float4 wa = __ldg(reinterpret_cast<const float4*>(weight) + 2 * c);
+    const float4 wb = __ldg(reinterpret_cast<const float4*>(weight) + 2 * c + 1);
+    const float w8[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+    float y[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) y[q] = v[q] * r * w8[q];
+    uint4 o;
+    o.x = pack_bf16x2(y[0], y[1]);
+    o.y = pack_bf16x2(y[2], y[3]);
+    o.z = pack_bf16x2(y[4], y[5]);
+    o.w = pack_bf16x2(y[6], y[7]);
+    reinterpret_cast<uint4*>(s_x + b * D)[c] = o;
+    if (writer) {
+      float4* so = reinterpret_cast<float4*>(streams_out + static_cast<int64_t>(b) * D);
+      so[2 * c] = make_float4(v[0], v[1], v[2], v[3]);
+      so[2 * c + 1] = make_float4(v[4], v[5], v[6], v[7]);
+      if (normed_out != nullptr)
+        reinterpret_cast<uint4*>(normed_out + static_cast<int64_t>(b) * D)[c] = o;
+    }
+  }
+}
+
+// [A] out[b, n] = W[n, :] . RMSNorm(streams_in[b] + delta[b]) for the CTA's
+// 8 rows (one per warp).
+template <int BM, int KCH>
+__global__ void __launch_bounds__(256) decode_norm_gemv_kernel(
+    const float* __restrict__ streams_in, const __nv_bfloat16* __restrict__ delta,
+    const int* __restrict__ route_pos, int k, int B, int D, const float* __restrict__ norm_w,
+    float eps, const __nv_bfloat16* __restrict__ W, int N, __nv_bfloat16* __restrict__ out,
+    int64_t out_ld, float* __restrict__ streams_out, __nv_bfloat16* __restrict__ normed_out) {
+  extern __shared__ __align__(16) uint8_t smem_a[];
+  __shared__ float s_red[8];
+  __nv_bfloat16* s_x = reinterpret_cast<__nv_bfloat16*>(smem_a);  // [B][D]
+  const bool writer = blockIdx.x == 0;
+  for (int b = 0; b < B; ++b)
+    cta_add_norm_row(streams_in, delta, route_pos, k, b, D, norm_w, eps, s_x, s_red, streams_out,
+                     normed_out, writer);
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const int n = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (n >= N) return;  // whole warps
+  float acc[BM];
+  warp_row_dot<BM, KCH>(W + static_cast<int64_t>(n) * D, D, B, s_x, lane, acc);
+  if (lane == 0)
+#pragma unroll
+    for (int b = 0; b < BM; ++b)
+      if (b < B) out[b * out_ld + n] = f2bf(acc[b]);
+}
+
+// [C] mixed[b, d] = W[d, :] . in[b] (bf16), with the GDN conv gate applied
+// per column when conv_w is given; the last CTA then runs
+// streams += mixed, the two RMSNorms, the router logits, top-k and the plan.
+template <int BM, int KCH, int VMAX>
+__global__ void __launch_bounds__(256) decode_out_router_kernel(
+    const __nv_bfloat16* __restrict__ in, int64_t in_ld, int K, const __nv_bfloat16* __restrict__ W,
+    int B, int D, const float* __restrict__ conv_w, const __nv_bfloat16* __restrict__ normed,
+    __nv_bfloat16* history, __nv_bfloat16* mixed, int* counter, float* __restrict__ streams,
+    const float* __restrict__ ffn_w, const float* __restrict__ rn_w,
+    const float* __restrict__ w_router, float eps, int E, int top_k, int tile_m,
+    __nv_bfloat16* __restrict__ m_bf, int64_t* __restrict__ topk_idx,
+    float* __restrict__ topk_prob, int* __restrict__ counts, int* __restrict__ offsets,
+    int* __restrict__ tile_offsets, int* __restrict__ perm_token, float* __restrict__ perm_prob,
+    int* __restrict__ route_pos) {
+  extern __shared__ __align__(16) uint8_t smem_c[];
+  __shared__ float s_red[8];
+  __shared__ int s_idx[kMaxTokens * kMaxTopK];
+  __shared__ float s_prob[kMaxTokens * kMaxTopK];
+  __shared__ int s_cnt[kMaxExperts];
+  __shared__ int s_warp[32];
+  __shared__ int s_last;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  // ---- output projection rows of this CTA
+  __nv_bfloat16* s_in = reinterpret_cast<__nv_bfloat16*>(smem_c);  // [B][K]
+  for (int i = threadIdx.x; i < B * (K >> 3); i += 256) {
+    const int b = i / (K >> 3), c = i - b * (K >> 3);
+    reinterpret_cast<uint4*>(s_in + b * K)[c] =
+        __ldg(reinterpret_cast<const uint4*>(in + b * in_ld) + c);
+  }
+  __syncthreads();
+  const int n = blockIdx.x * 8 + warp;
+  if (n < D) {
+    float acc[BM];
+    warp_row_dot<BM, KCH>(W + static_cast<int64_t>(n) * K, K, B, s_in, lane, acc);
+    if (lane < B) {
+      float y = 0.f;
+#pragma unroll
+      for (int b = 0; b < BM; ++b)
+        if (b == lane) y = acc[b];
+      const int b = lane;
+      float yv = bf2f(f2bf(y));  // the projection output is bf16
+      if (conv_w != nullptr) {
+        // conv gate of the decode step (gdn_conv_gate_kernel with T == 1)
+        __nv_bfloat16* hb = history + static_cast<int64_t>(b) * 3 * D + n;
+        const __nv_bfloat16 xb = normed[static_cast<int64_t>(b) * D + n];
+        const __nv_bfloat16 h0 = hb[0], h1 = hb[D], h2 = hb[2 * D];
+        float cacc = 0.f;
+        cacc += conv_w[n * 4 + 0] * bf2f(h0);
+        cacc += conv_w[n * 4 + 1] * bf2f(h1);
+        cacc += conv_w[n * 4 + 2] * bf2f(h2);
+        cacc += conv_w[n * 4 + 3] * bf2f(xb);
+        yv = yv * sigmoidf_(cacc);
+        hb[0] = h1;
+        hb[D] = h2;
+        hb[2 * D] = xb;
+      }
+      mixed[static_cast<int64_t>(b) * D + n] = f2bf(yv);
+    }
+  }
+  // ---- the last CTA to finish runs the router on the complete rows
+  __threadfence();  // this thread's mixed / history writes are visible GPU-wide
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = atomicAdd(counter, 1) == static_cast<int>(gridDim.x) - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  float* s_r = reinterpret_cast<float*>(smem_c);  // [B][D], reuses the input rows
+  float* s_logits = s_r + B * D;                  // [B][E]
+  for (int b = 0; b < B; ++b)
+    cta_router_input<VMAX, true>(streams, mixed, b, D, ffn_w, rn_w, eps, m_bf, s_r + b * D, s_red);
+  __syncthreads();
+  for (int p = warp; p < B * E; p += 8) {
+    const int t = p / E, e = p - t * E;
+    const float l = warp_logit(w_router, e, s_r + t * D, D, lane);
+    if (lane == 0) s_logits[p] = l;
+  }
+  __syncthreads();
+  cta_topk_plan(s_logits, nullptr, B, E, top_k, tile_m, s_idx, s_prob, s_cnt, s_warp, topk_idx,
+                topk_prob, counts, offsets, tile_offsets, perm_token, perm_prob, route_pos,
+                nullptr);
+  if (threadIdx.x == 0) *counter = 0;  // ready for the next launch
+}
+
+int kch_for(int K) {
+  if (K <= 0 || K % 8 != 0) return 0;
+  if (K <= 768) return 3;
+  if (K <= 1024) return 4;
+  if (K <= 2048) return 8;
+  return 0;
+}
+
+int bm_for(int B) { return B <= 1 ? 1 : (B <= 4 ? 4 : 8); }
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+template <typename Kern>
+int32_t ensure_smem(Kern kernel, int bytes, int& attr) {
+  if (bytes <= attr) return LLMYB_OK;
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) return e;
+  attr = bytes;
+  return LLMYB_OK;
+}
+
+}  // namespace
+}  // namespace llmyb
+
+using namespace llmyb;
+
+LLMYB_API int32_t llmyb_decode_norm_gemv(const float* streams_in, const void* delta,
+                                         const int32_t* route_pos, int32_t top_k,
+                                         int32_t n_tokens, int32_t d_model, const float* norm_w,
+                                         float eps, const void* w, int32_t n_out, void* out,
+                                         int64_t out_ld, float* streams_out, void* normed_out,
+                                         void* stream) {
+  if (!streams_in || !norm_w || !w || !out || !streams_out || n_tokens < 0 || d_model <= 0 ||
+      n_out <= 0 || out_ld < n_out || (route_pos && (!delta || top_k <= 0)))
+    return LLMYB_EINVAL;
+  if (n_tokens == 0) return LLMYB_OK;
+  const int kch = kch_for(d_model);
+  if (n_tokens > kMaxTokens || kch == 0 || streams_in == streams_out || !aligned16(streams_in) ||
+      !aligned16(delta) || !aligned16(norm_w) || !aligned16(w) || !aligned16(streams_out) ||
+      !aligned16(normed_out))
+    return LLMYB_EUNSUPPORTED;
+  const int bytes = n_tokens * d_model * 2;
+  const int grid = static_cast<int>(ceil_div(n_out, 8));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const auto* dl = static_cast<const __nv_bfloat16*>(delta);
+  const auto* wb = static_cast<const __nv_bfloat16*>(w);
+  auto* ob = static_cast<__nv_bfloat16*>(out);
+  auto* nb = static_cast<__nv_bfloat16*>(normed_out);
+  static int attr[3][3] = {};
+  const int bm = bm_for(n_tokens);
+  const int bi = bm == 1 ? 0 : (bm == 4 ? 1 : 2), ki = kch == 3 ? 0 : (kch == 4 ? 1 : 2);
+  int32_t st = LLMYB_OK;
+#define LLMYB_NG(BMV, KCHV)                                                                     \
+  do {                                                                                          \
+    st = ensure_smem(decode_norm_gemv_kernel<BMV, KCHV>, bytes, attr[bi][ki]);                  \
+    if (st) return st;                                                                          \
+    decode_norm_gemv_kernel<BMV, KCHV><<<grid, 256, bytes, s>>>(                                 \
+        streams_in, dl, route_pos, top_k, n_tokens, d_model, norm_w, eps, wb, n_out, ob, out_ld, \
+        streams_out, nb);                                                                       \
+  } while (0)
+  if (bm == 1) {
+    if (kch == 3) LLMYB_NG(1, 3); else if (kch == 4) LLMYB_NG(1, 4); else LLMYB_NG(1, 8);
+  } else if (bm == 4) {
+    if (kch == 3) LLMYB_NG(4, 3); else if (kch == 4) LLMYB_NG(4, 4); else LLMYB_NG(4, 8);
+  } else {
+    if (kch == 3) LLMYB_NG(8, 3); else if (kch == 4) LLMYB_NG(8, 4); else LLMYB_NG(8, 8);
+  }
+#undef LLMYB_NG
+  count_launch();
+  return launch_status();
+}
+
+LLMYB_API int32_t llmyb_decode_out_router(
+    const void* in, int64_t in_ld, int32_t k_in, const void* w, int32_t n_tokens,
+    int32_t d_model, const float* conv_w, const void* normed, void* history, void* mixed,
+    int32_t* counter, float* streams, const float* ffn_norm, const float* router_norm,
+    const float* w_router, float eps, int32_t n_experts, int32_t top_k, int32_t tile_m,
+    void* m_bf, int64_t* topk_idx, float* topk_prob, int32_t* expert_counts,
+    int32_t* expert_offsets, int32_t* tile_offsets, int32_t* perm_token, float* perm_prob,
+    int32_t* route_pos, void* stream) {
+  if (!in || !w || !mixed || !counter || !streams || !ffn_norm || !router_norm || !w_router ||
+      !m_bf || !topk_idx || !topk_prob || !expert_counts || !expert_offsets || !tile_offsets ||
+      !perm_token || !perm_prob || !route_pos || n_tokens < 0 || d_model <= 0 || k_in <= 0 ||
+      in_ld < k_in || n_experts <= 0 || top_k <= 0 || top_k > n_experts || tile_m <= 0 ||
+      (conv_w && (!normed || !history)))
+    return LLMYB_EINVAL;
+  if (n_tokens == 0) return LLMYB_EINVAL;
+  const int kch = kch_for(k_in);
+  if (n_tokens > kMaxTokens || kch == 0 || d_model % 8 != 0 || d_model > 2048 ||
+      top_k > kMaxTopK || n_experts > kMaxExperts || in_ld % 8 != 0 || !aligned16(in) ||
+      !aligned16(w) || !aligned16(streams) || !aligned16(ffn_norm) || !aligned16(router_norm) ||
+      !aligned16(w_router) || !aligned16(mixed) || (reinterpret_cast<uintptr_t>(m_bf) & 7u))
+    return LLMYB_EUNSUPPORTED;
+  const int bytes = std::max(n_tokens * k_in * 2, (n_tokens * d_model + n_tokens * n_experts) * 4);
+  const int grid = static_cast<int>(ceil_div(d_model, 8));
+  const int vmax = d_model <= 1024 ? 1 : 2;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  static int attr[3][3][2] = {};
+  const int bm = bm_for(n_tokens);
+  const int bi = bm == 1 ? 0 : (bm == 4 ? 1 : 2), ki = kch == 3 ? 0 : (kch == 4 ? 1 : 2);
+  int32_t st = LLMYB_OK;
+#define LLMYB_OR(BMV, KCHV, VM)                                                                 \
+  do {                                                                                          \
+    st = ensure_smem(decode_out_router_kernel<BMV, KCHV, VM>, bytes, attr[bi][ki][VM - 1]);     \
+    if (st) return st;                                                                          \
+    decode_out_router_kernel<BMV, KCHV, VM><<<grid, 256, bytes, s>>>(                            \
+        static_cast<const __nv_bfloat16*>(in), in_ld, k_in,                                     \
+        static_cast<const __nv_bfloat16*>(w), n_tokens, d_model, conv_w,                        \
+        static_cast<const __nv_bfloat16*>(normed), static_cast<__nv_bfloat16*>(history),        \
+        static_cast<__nv_bfloat16*>(mixed), counter, streams, ffn_norm, router_norm, w_router,  \
+        eps, n_experts, top_k, tile_m, static_cast<__nv_bfloat16*>(m_bf), topk_idx, topk_prob,  \
+        expert_counts, expert_offsets, tile_offsets, perm_token, perm_prob, route_pos);         \
+  } while (0)
+#define LLMYB_OR_K(BMV, VM)                                                                     \
+  do {                                                                                          \
+    if (kch == 3) LLMYB_OR(BMV, 3, VM); else if (kch == 4) LLMYB_OR(BMV, 4, VM);                \
+    else LLMYB_OR(BMV, 8, VM);                                                                  \
+  } while (0)
+  if (vmax == 1) {
+    if (bm == 1) LLMYB_OR_K(1, 1); else if (bm == 4) LLMYB_OR_K(4, 1); else LLMYB_OR_K(8, 1);
+  } else {
+    if (bm == 1) LLMYB_OR_K(1, 2); else if (bm == 4) LLMYB_OR_K(4, 2); else LLMYB_OR_K(8, 2);
+  }
+#undef LLMYB_OR_K
+#undef LLMYB_OR
+  count_launch();
+  return launch_status();
+}

@@ -358,6 +358,60 @@ def add_rmsnorm_routed(streams: torch.Tensor, y_rows: torch.Tensor, plan: RouteP
                  _stream())
 
 
+def decode_fused_supported(n: int, d: int, e: int, k: int, *k_ins: int) -> bool:
+    """Shapes the fused small-batch decode kernels take: up to 8 tokens, one
+    CTA for the router (N*E <= 64), D and every projection input width a
+    multiple of 8 and at most 2048."""
+    return (1 <= n <= 8 and n * e <= 64 and k <= 32 and d % 8 == 0 and d <= 2048
+            and all(x % 8 == 0 and 0 < x <= 2048 for x in k_ins))
+
+
+def decode_norm_gemv(streams_in: torch.Tensor, delta: torch.Tensor | None, plan: RoutePlan | None,
+                     norm_w: torch.Tensor, eps: float, w: torch.Tensor, out: torch.Tensor,
+                     streams_out: torch.Tensor, normed_out: torch.Tensor | None = None) -> None:
+    """[A] streams_out = streams_in + delta (or the routed sum over plan.route_pos);
+    out = w . RMSNorm(streams_out) * norm_w (bf16), every CTA normalising for itself."""
+    _require_cuda(streams_in, delta, norm_w, w, out, streams_out, normed_out)
+    for t_, nm in ((out, "out"), (streams_out, "streams_out")):
+        _inplace(t_, nm)
+    n, d = streams_in.shape
+    route_pos, k = (plan.route_pos, plan.topk_idx.shape[1]) if plan is not None else (None, 0)
+    _native.call("llmyb_decode_norm_gemv", _ptr(streams_in), _ptr(delta), _ptr(route_pos), k, n, d,
+                 _ptr(norm_w), float(eps), _ptr(w), w.shape[0], _ptr(out), out.stride(0),
+                 _ptr(streams_out), _ptr(normed_out), _stream())
+
+
+def decode_out_router(inp: torch.Tensor, w: torch.Tensor, streams: torch.Tensor,
+                      ffn_norm: torch.Tensor, router_norm: torch.Tensor, w_router: torch.Tensor,
+                      k: int, eps: float, m_bf: torch.Tensor, counter: torch.Tensor, *,
+                      conv_w: torch.Tensor | None = None, normed: torch.Tensor | None = None,
+                      history: torch.Tensor | None = None, tile_m: int = TILE_M) -> RoutePlan:
+    """[C] mixed = w . inp (+ the GDN conv gate with conv_w / normed / history,
+    history rolled); streams += mixed; m_bf = RMSNorm_ffn(streams); routes and
+    plan as route_fused.  counter: int32 [1] zero word reused across calls."""
+    _require_cuda(inp, w, streams, ffn_norm, router_norm, w_router, m_bf, counter, conv_w, normed,
+                  history)
+    _rows(inp, "inp")
+    _inplace(streams, "streams")
+    _inplace(m_bf, "m_bf")
+    if history is not None:
+        _inplace(history, "history")
+    n, d = streams.shape
+    e = w_router.shape[0]
+    dev = streams.device
+    idx = torch.empty(n, k, dtype=torch.int64, device=dev)
+    prob = torch.empty(n, k, dtype=torch.float32, device=dev)
+    b = _plan_buffers(n, e, k, dev, False)
+    mixed = torch.empty(n, d, dtype=torch.bfloat16, device=dev)
+    _native.call("llmyb_decode_out_router", _ptr(inp), inp.stride(0), inp.shape[1], _ptr(w), n, d,
+                 _ptr(conv_w), _ptr(normed), _ptr(history), _ptr(mixed), _ptr(counter),
+                 _ptr(streams), _ptr(ffn_norm), _ptr(router_norm), _ptr(w_router), float(eps), e, k,
+                 int(tile_m), _ptr(m_bf), _ptr(idx), _ptr(prob), _ptr(b["counts"]),
+                 _ptr(b["offsets"]), _ptr(b["tile_offsets"]), _ptr(b["perm_token"]),
+                 _ptr(b["perm_prob"]), _ptr(b["route_pos"]), _stream())
+    return RoutePlan(idx, prob, **b, tile_m=tile_m)
+
+
 def pack_w13(w_gate: torch.Tensor, w_up: torch.Tensor) -> torch.Tensor:
     """Interleave [E,F,D] gate/up stacks into the [E,2F,D] GEMM1 operand."""
     _require_cuda(w_gate, w_up)

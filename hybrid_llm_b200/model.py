@@ -53,6 +53,10 @@ class LoopedHybridModel:
         # decode expert kernels: "auto", "grouped" (tcgen05 GEMMs) or "decode"
         # (weight streaming); a fixed choice makes runs comparable bit for bit
         self.expert_path = "auto"
+        # small-batch decode on the fused kernels (decode_norm_gemv /
+        # decode_out_router) when the shapes allow; False forces the unfused path
+        self.decode_fused = True
+        self._counter = torch.zeros(1, dtype=torch.int32, device=self.device)
         shard = weights.blocks[0].moe.w13.shape[0] if weights.blocks else None
         if ep is not None and shard != ep.experts_per_rank:
             raise ValueError("expert-parallel model needs the weights of this rank's experts only")
@@ -221,6 +225,9 @@ class LoopedHybridModel:
         bsz = ids.shape[0]
         loops = c.num_loops if num_loops is None else int(num_loops)
         d = c.d_model
+        if self.decode_fused and kernels.decode_fused_supported(
+                bsz, d, c.moe_experts, c.moe_top_k, c.gdn_heads * c.gdn_value_dim, d):
+            return self._decode_fused(ids, state, loops)
         fused_router = kernels.route_fused_supported(bsz, c.moe_experts, c.moe_top_k, d)
         # 128-row tiles for the grouped expert GEMMs at a few rows per expert
         tile_m = 128
@@ -252,12 +259,20 @@ class LoopedHybridModel:
                     kernels.add_rmsnorm(m_f32, None, blk.moe.router_norm, c.rms_eps, out_f32=r_in)
                     plan = kernels.route(torch.mm(r_in, blk.moe.router.t()), c.moe_top_k,
                                          tile_m=tile_m)
-                if self.ep is not None:
-                    res = self.ep.run(m_bf, plan, blk.moe.w13, blk.moe.w2, path=self.expert_path)
-                    y_rows, plan = res.y_rows, res.plan_for_combine(plan)
-                else:
-                    y_rows = kernels.moe_experts_rows(m_bf, plan, blk.moe.w13, blk.moe.w2,
-                                                      path=self.expert_path)
+                y_rows, plan = self._experts(blk, m_bf, plan)
+        return self._decode_head(streams, y_rows, plan, state)
+
+    def _experts(self, blk: Block, m_bf: torch.Tensor, plan: kernels.RoutePlan):
+        """Routed expert rows of a decode step and the plan that combines them."""
+        if self.ep is not None:
+            res = self.ep.run(m_bf, plan, blk.moe.w13, blk.moe.w2, path=self.expert_path)
+            return res.y_rows, res.plan_for_combine(plan)
+        return kernels.moe_experts_rows(m_bf, plan, blk.moe.w13, blk.moe.w2,
+                                        path=self.expert_path), plan
+
+    def _decode_head(self, streams, y_rows, plan, state: RecurrentState) -> torch.Tensor:
+        c = self.cfg
+        bsz, d = streams.shape
         sb = torch.empty(bsz, d, dtype=torch.bfloat16, device=self.device)
         kernels.add_rmsnorm_routed(streams, y_rows, plan, None, c.rms_eps, out_bf16=sb,
                                    normalize=False)
@@ -266,6 +281,47 @@ class LoopedHybridModel:
         logits = torch.mm(h, self.w.embed.t())
         state.positions.add_(1)
         return logits
+
+    def _decode_fused(self, ids: torch.Tensor, state: RecurrentState, loops: int) -> torch.Tensor:
+        """decode_step on the fused small-batch kernels: per block [A] residual
+        add + norm + input projection, the mixer kernel, [C] output projection
+        (+ conv gate) + residual + norms + router + plan, the two expert
+        kernels.  The residual stream alternates between two buffers because
+        every CTA of [A] reads the old value while one CTA writes the new."""
+        c = self.cfg
+        bsz, d = ids.shape[0], c.d_model
+        cur = kernels.embed(ids, self.w.embed, self.w.stream_seed)
+        nxt = torch.empty_like(cur)
+        normed = torch.empty(bsz, d, dtype=torch.bfloat16, device=self.device)
+        m_bf = torch.empty_like(normed)
+        hd = c.csa_heads * c.csa_head_dim
+        y_rows, plan = None, None
+        for i in range(loops):
+            for j, blk in enumerate(self.w.blocks):
+                key = state_key(i, j)
+                mix = blk.mixer
+                proj = torch.empty(bsz, mix.w_in.shape[0], dtype=torch.bfloat16, device=self.device)
+                kernels.decode_norm_gemv(cur, y_rows, plan, blk.mixer_norm, c.rms_eps, mix.w_in,
+                                         proj, nxt, normed)
+                cur, nxt = nxt, cur
+                router = (cur, blk.ffn_norm, blk.moe.router_norm, blk.moe.router, c.moe_top_k,
+                          c.rms_eps, m_bf, self._counter)
+                if isinstance(mix, GdnBlock):
+                    q, k, v, gate, beta = self._gdn_views(proj, (bsz,))
+                    o = kernels.gdn_step(q, k, v, gate, beta, state.gdn_states[key],
+                                         decay_logit=mix.decay_logit, raw_inputs=True,
+                                         beta_bias=mix.beta_bias)
+                    plan = kernels.decode_out_router(
+                        o.view(bsz, -1), mix.w_out, *router, conv_w=mix.conv, normed=normed,
+                        history=state.gdn_conv_histories[key], tile_m=128)
+                else:
+                    local = kernels.csa_local_decode(proj[:, :hd], proj[:, hd:2 * hd],
+                                                     proj[:, 2 * hd:], state.local_k[key],
+                                                     state.local_v[key], state.positions,
+                                                     c.csa_heads)
+                    plan = kernels.decode_out_router(local, mix.w_o, *router, tile_m=128)
+                y_rows, plan = self._experts(blk, m_bf, plan)
+        return self._decode_head(cur, y_rows, plan, state)
 
     def _gdn_step(self, g: GdnBlock, normed, state: RecurrentState, key: str, bsz: int):
         c = self.cfg

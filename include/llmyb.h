@@ -348,6 +348,40 @@ int32_t llmyb_add_rmsnorm_routed(float* streams, const void* y_rows, const int32
                                  const float* weight, float eps, int32_t normalize,
                                  void* out_bf16, float* out_f32, void* stream);
 
+/* ------------------------------------------------ fused small-batch decode
+ * Two kernels that shorten the launch chain of a decode step at 1..8 tokens
+ * (PhysicalBlock.forward_step, model/model.py:214-241).  No counterpart in
+ * the reference, whose decode step runs the layers' eager forward_step.
+ *
+ * llmyb_decode_norm_gemv: x = streams_in + delta (delta: bf16 rows, or with
+ * route_pos the sum of the k routed rows delta[route_pos[n*k+s]]; nullable);
+ * out[n, :] = w [n_out, D] . (RMSNorm(x) * norm_w) in bf16 (row stride
+ * out_ld).  streams_out (a different buffer than streams_in) gets x and
+ * normed_out (nullable) the normalised rows.  n_tokens <= 8, D <= 2048,
+ * D % 8 == 0; 16-byte aligned pointers. */
+int32_t llmyb_decode_norm_gemv(const float* streams_in, const void* delta,
+                               const int32_t* route_pos, int32_t top_k, int32_t n_tokens,
+                               int32_t d_model, const float* norm_w, float eps, const void* w,
+                               int32_t n_out, void* out, int64_t out_ld, float* streams_out,
+                               void* normed_out, void* stream);
+
+/* llmyb_decode_out_router: mixed = w [D, k_in] . in [N, k_in] (bf16; with
+ * conv_w the GDN decode conv gate of llmyb_gdn_conv_gate is applied per
+ * column, normed = the block input, history rolled); then, by the last CTA
+ * to finish, the work of llmyb_route_fused with delta = mixed: streams +=
+ * mixed, m_bf, top-k and the plan.  mixed [N, D] bf16 is scratch; counter is
+ * an int32 zero-initialised word the kernel leaves at zero.  N <= 8, N*E
+ * small (one CTA routes), D <= 2048, k_in <= 2048. */
+int32_t llmyb_decode_out_router(const void* in, int64_t in_ld, int32_t k_in, const void* w,
+                                int32_t n_tokens, int32_t d_model, const float* conv_w,
+                                const void* normed, void* history, void* mixed, int32_t* counter,
+                                float* streams, const float* ffn_norm, const float* router_norm,
+                                const float* w_router, float eps, int32_t n_experts, int32_t top_k,
+                                int32_t tile_m, void* m_bf, int64_t* topk_idx, float* topk_prob,
+                                int32_t* expert_counts, int32_t* expert_offsets,
+                                int32_t* tile_offsets, int32_t* perm_token, float* perm_prob,
+                                int32_t* route_pos, void* stream);
+
 /* RMSNorm of a bf16 tensor [N, D] (final_norm before the tied LM head). */
 int32_t llmyb_rmsnorm_bf16(const void* x, int64_t n_tokens, int32_t d_model, const float* weight,
                            float eps, void* out, void* stream);

@@ -88,3 +88,103 @@ def test_decode_equals_prefill_of_extended_sequence(cuda):
     step = m.decode_step(ids[:, -1], o.state).float().cpu().numpy()
     full = m.forward(ids, last_logits_only=True).logits[:, -1].float().cpu().numpy()
     assert _rel(step, full) < LOGIT_REL
+
+
+def test_fused_decode_matches_unfused(cuda):
+    """The fused small-batch decode kernels against the unfused decode path,
+    from the same state with the same tokens (teacher forced)."""
+    from hybrid_llm_b200.state import RecurrentState
+    m = _model(inputs.mini_config())
+    ids = torch.from_numpy(inputs.mini_prompt()).cuda()
+    o = m.forward(ids, last_logits_only=True)
+    states = []
+    for _ in range(2):
+        st = RecurrentState(m.cfg, ids.shape[0], "cuda")
+        st.load_state_dict(o.state.state_dict())
+        states.append(st)
+    tok = o.logits[:, -1].float().argmax(-1)
+    for _ in range(4):
+        m.decode_fused = False
+        a = m.decode_step(tok, states[0]).float().cpu().numpy()
+        m.decode_fused = True
+        b = m.decode_step(tok, states[1]).float().cpu().numpy()
+        assert _rel(b, a) < 1e-2, _rel(b, a)
+        tok = torch.from_numpy(a.argmax(-1)).cuda()
+    for key in states[0].gdn_conv_histories:
+        assert torch.equal(states[0].gdn_conv_histories[key], states[1].gdn_conv_histories[key])
+
+
+@pytest.mark.parametrize("n,d,p", [(1, 768, 3088), (3, 2048, 6144), (8, 512, 1024)])
+def test_decode_norm_gemv(cuda, n, d, p):
+    """[A]: residual + routed combine + RMSNorm as add_rmsnorm_routed (bit for
+    bit), then the projection against torch's GEMM of the same bf16 rows."""
+    from hybrid_llm_b200 import kernels
+    g = torch.Generator(device="cuda").manual_seed(n + d)
+    streams = torch.randn(n, d, device="cuda", generator=g)
+    k = 2
+    logits = torch.randn(n, 8, device="cuda", generator=g)
+    plan = kernels.route(logits, k, tile_m=128)
+    y_rows = torch.randn(n * k, d, device="cuda", generator=g).bfloat16()
+    w_norm = torch.rand(d, device="cuda", generator=g) + 0.5
+    w = (torch.randn(p, d, device="cuda", generator=g) * 0.02).bfloat16()
+    out = torch.empty(n, p, dtype=torch.bfloat16, device="cuda")
+    s_out = torch.empty_like(streams)
+    normed = torch.empty(n, d, dtype=torch.bfloat16, device="cuda")
+    kernels.decode_norm_gemv(streams, y_rows, plan, w_norm, 1e-6, w, out, s_out, normed)
+    ref_s = streams.clone()
+    ref_n = torch.empty_like(normed)
+    kernels.add_rmsnorm_routed(ref_s, y_rows, plan, w_norm, 1e-6, out_bf16=ref_n)
+    torch.cuda.synchronize()
+    assert torch.equal(s_out, ref_s) and torch.equal(normed, ref_n)
+    ref = (ref_n.float() @ w.float().t())
+    assert float((out.float() - ref).abs().max() / ref.abs().max()) < 1e-2
+
+
+@pytest.mark.parametrize("gdn", [True, False])
+def test_decode_out_router(cuda, gdn):
+    """[C]: projection (+ conv gate) into the residual stream, then the
+    router: the stream update against torch, routes against fp64 top-k."""
+    from hybrid_llm_b200 import kernels
+    from oracle import routing
+    n, d, kin, e, k = 2, 768, 768, 16, 2
+    g = torch.Generator(device="cuda").manual_seed(5 + gdn)
+    inp = torch.randn(n, kin, device="cuda", generator=g).bfloat16()
+    w = (torch.randn(d, kin, device="cuda", generator=g) * 0.03).bfloat16()
+    streams = torch.randn(n, d, device="cuda", generator=g)
+    ffn = torch.rand(d, device="cuda", generator=g) + 0.5
+    rn = torch.rand(d, device="cuda", generator=g) + 0.5
+    wr = torch.randn(e, d, device="cuda", generator=g) * 0.02
+    m_bf = torch.empty(n, d, dtype=torch.bfloat16, device="cuda")
+    counter = torch.zeros(1, dtype=torch.int32, device="cuda")
+    extra = {}
+    if gdn:
+        conv = torch.randn(d, 4, device="cuda", generator=g) * 0.5
+        normed = torch.randn(n, d, device="cuda", generator=g).bfloat16()
+        hist = torch.randn(n, 3, d, device="cuda", generator=g).bfloat16()
+        hist0 = hist.clone()
+        extra = dict(conv_w=conv, normed=normed, history=hist)
+    s0 = streams.clone()
+    plan = kernels.decode_out_router(inp, w, streams, ffn, rn, wr, k, 1e-6, m_bf, counter,
+                                     tile_m=128, **extra)
+    torch.cuda.synchronize()
+    y = (inp.float() @ w.float().t()).bfloat16().float()
+    if gdn:
+        taps = torch.cat([hist0.float(), normed.float()[:, None]], 1)      # [n, 4, d]
+        y = (y * torch.sigmoid((taps * conv.t()[None]).sum(1))).bfloat16().float()
+        assert torch.equal(hist[:, 0], hist0[:, 1]) and torch.equal(hist[:, 1], hist0[:, 2])
+        assert torch.equal(hist[:, 2], normed)
+    delta = streams - s0
+    assert float((delta - y).abs().max() / y.abs().max()) < 2e-2
+    assert int(counter.item()) == 0
+    x = streams.double().cpu().numpy()
+    mm = x / np.sqrt((x * x).mean(-1, keepdims=True) + 1e-6) * ffn.double().cpu().numpy()
+    r = mm / np.sqrt((mm * mm).mean(-1, keepdims=True) + 1e-6) * rn.double().cpu().numpy()
+    logits = r @ wr.double().cpu().numpy().T
+    idx, _ = routing.router_topk(logits.astype(np.float32), k)
+    srt = -np.sort(-logits, -1)
+    clear = srt[:, k - 1] - srt[:, k] > 1e-4
+    got = plan.topk_idx.cpu().numpy()
+    np.testing.assert_array_equal(np.sort(got[clear], -1), np.sort(idx[clear], -1))
+    ref = routing.dispatch_plan(got, e, tile_m=128)
+    for f in ("counts", "offsets", "tile_offsets", "perm_token", "route_pos"):
+        np.testing.assert_array_equal(getattr(plan, f).cpu().numpy(), ref[f], err_msg=f)
