@@ -481,6 +481,10 @@ __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(256, STAG
     vb = s_v - static_cast<int64_t>(j_begin) * D;
   }
 
+  // the ring rows and positions were written two or more launches ago; the
+  // query and the new key / value come from the projection kernel
+  pdl_wait();
+  pdl_trigger();
   for (int c = tid; c < nch; c += 256)
     reinterpret_cast<uint4*>(s_q)[c] = reinterpret_cast<const uint4*>(q + b * sq)[c];
   __syncthreads();
@@ -777,13 +781,13 @@ LLMYB_API int32_t llmyb_csa_local_decode(const void* q, int64_t q_stride, const 
       if (st) return st;
       attr_bytes = bytes;
     }
-    kernel<<<batch * kClusterCtas, 256, bytes, static_cast<cudaStream_t>(stream)>>>(
+    return static_cast<int32_t>(launch_pdl(
+        kernel, dim3(batch * kClusterCtas), dim3(256), bytes, static_cast<cudaStream_t>(stream),
         static_cast<const __nv_bfloat16*>(q), q_stride, static_cast<const __nv_bfloat16*>(knew),
         knew_stride, static_cast<const __nv_bfloat16*>(vnew), vnew_stride,
         static_cast<__nv_bfloat16*>(kcache), static_cast<__nv_bfloat16*>(vcache), positions,
         heads, head_dim, d_model, window, kLog2e / sqrtf(static_cast<float>(head_dim)),
-        static_cast<__nv_bfloat16*>(out), out_stride, dev_status);
-    return LLMYB_OK;
+        static_cast<__nv_bfloat16*>(out), out_stride, dev_status));
   };
   static int attr_staged = 0, attr_plain = 0;
   const int32_t st = staged ? launch(csa_decode_kernel<true>, attr_staged)

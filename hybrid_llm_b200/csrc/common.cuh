@@ -34,6 +34,35 @@ inline int32_t launch_status() {
   return e == cudaSuccess ? LLMYB_OK : static_cast<int32_t>(e);
 }
 
+// Programmatic dependent launch.  A kernel launched by launch_pdl() may start
+// while its predecessor in the stream is still running.  Before pdl_wait() it
+// may only read data that no kernel still in flight writes: weights, or
+// buffers last written two or more launches earlier (each kernel passes its
+// own pdl_wait() before it triggers, so those writers have completed).
+// pdl_wait() returns once the predecessor has completed and its writes are
+// visible; pdl_trigger() then lets the successor launch.  For a kernel
+// launched without the attribute both are no-ops.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t s, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 __device__ __forceinline__ float bf2f(__nv_bfloat16 v) { return __bfloat162float(v); }
 __device__ __forceinline__ __nv_bfloat16 f2bf(float v) { return __float2bfloat16_rn(v); }
 

@@ -35,20 +35,26 @@ using namespace rdev;
 
 constexpr int kMaxTokens = 8;
 
-// Dot products of one weight row (bf16, K = 256*KCH at most, K % 8 == 0)
-// with the B bf16 rows of s_x [B][K] (shared memory), summed over the warp:
-// every lane returns the B sums.  All weight loads are issued before the
-// first multiply.
-template <int BM, int KCH>
-__device__ __forceinline__ void warp_row_dot(const __nv_bfloat16* __restrict__ wrow, int K, int B,
-                                             const __nv_bfloat16* s_x, int lane, float (&acc)[BM]) {
+// One weight row (bf16, K = 256*KCH at most, K % 8 == 0) into registers:
+// lane holds 16-byte chunks lane, lane+32, ...  Issued at kernel entry, so
+// the weight round trip overlaps the preparation of the input rows.
+template <int KCH>
+__device__ __forceinline__ void warp_load_row(const __nv_bfloat16* __restrict__ wrow, int K,
+                                              int lane, uint4 (&w)[KCH]) {
   const int nch = K >> 3;
-  uint4 w[KCH];
 #pragma unroll
   for (int i = 0; i < KCH; ++i) {
     const int c = lane + 32 * i;
     if (c < nch) w[i] = __ldg(reinterpret_cast<const uint4*>(wrow) + c);
   }
+}
+
+// Dot products of the loaded row with the B bf16 rows of s_x [B][K] (shared
+// memory), summed over the warp: every lane returns the B sums.
+template <int BM, int KCH>
+__device__ __forceinline__ void warp_row_dot(const uint4 (&w)[KCH], int K, int B,
+                                             const __nv_bfloat16* s_x, int lane, float (&acc)[BM]) {
+  const int nch = K >> 3;
 #pragma unroll
   for (int b = 0; b < BM; ++b) acc[b] = 0.f;
 #pragma unroll
@@ -161,16 +167,20 @@ __global__ void __launch_bounds__(256) decode_norm_gemv_kernel(
   extern __shared__ __align__(16) uint8_t smem_a[];
   __shared__ float s_red[8];
   __nv_bfloat16* s_x = reinterpret_cast<__nv_bfloat16*>(smem_a);  // [B][D]
+  const int lane = threadIdx.x & 31;
+  const int n = blockIdx.x * 8 + (threadIdx.x >> 5);
+  uint4 w[KCH];
+  if (n < N) warp_load_row<KCH>(W + static_cast<int64_t>(n) * D, D, lane, w);
+  pdl_wait();  // the residual stream and the routed rows come from earlier kernels
+  pdl_trigger();
   const bool writer = blockIdx.x == 0;
   for (int b = 0; b < B; ++b)
     cta_add_norm_row(streams_in, delta, route_pos, k, b, D, norm_w, eps, s_x, s_red, streams_out,
                      normed_out, writer);
   __syncthreads();
-  const int lane = threadIdx.x & 31;
-  const int n = blockIdx.x * 8 + (threadIdx.x >> 5);
   if (n >= N) return;  // whole warps
   float acc[BM];
-  warp_row_dot<BM, KCH>(W + static_cast<int64_t>(n) * D, D, B, s_x, lane, acc);
+  warp_row_dot<BM, KCH>(w, D, B, s_x, lane, acc);
   if (lane == 0)
 #pragma unroll
     for (int b = 0; b < BM; ++b)
@@ -199,6 +209,25 @@ __global__ void __launch_bounds__(256) decode_out_router_kernel(
   __shared__ int s_warp[32];
   __shared__ int s_last;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int n = blockIdx.x * 8 + warp;
+  uint4 w[KCH];
+  if (n < D) warp_load_row<KCH>(W + static_cast<int64_t>(n) * K, K, lane, w);
+  // the router's weights go to L2 now, one slice per CTA, so that the last
+  // CTA finds them there
+  {
+    const int64_t rbytes = static_cast<int64_t>(E) * D * 4;
+    const int64_t per = (rbytes + gridDim.x - 1) / gridDim.x;
+    const char* base = reinterpret_cast<const char*>(w_router);
+    for (int64_t o = blockIdx.x * per + threadIdx.x * 128; o < min(rbytes, (blockIdx.x + 1) * per);
+         o += 256 * 128)
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(base + o));
+    if (blockIdx.x == 0 && threadIdx.x * 128 < D * 4) {
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<const char*>(ffn_w) + threadIdx.x * 128));
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<const char*>(rn_w) + threadIdx.x * 128));
+    }
+  }
+  pdl_wait();  // the projection input comes from the mixer kernel
+  pdl_trigger();
   // ---- output projection rows of this CTA
   __nv_bfloat16* s_in = reinterpret_cast<__nv_bfloat16*>(smem_c);  // [B][K]
   for (int i = threadIdx.x; i < B * (K >> 3); i += 256) {
@@ -207,10 +236,9 @@ __global__ void __launch_bounds__(256) decode_out_router_kernel(
         __ldg(reinterpret_cast<const uint4*>(in + b * in_ld) + c);
   }
   __syncthreads();
-  const int n = blockIdx.x * 8 + warp;
   if (n < D) {
     float acc[BM];
-    warp_row_dot<BM, KCH>(W + static_cast<int64_t>(n) * K, K, B, s_in, lane, acc);
+    warp_row_dot<BM, KCH>(w, K, B, s_in, lane, acc);
     if (lane < B) {
       float y = 0.f;
 #pragma unroll
@@ -254,9 +282,15 @@ __global__ void __launch_bounds__(256) decode_out_router_kernel(
     if (lane == 0) s_logits[p] = l;
   }
   __syncthreads();
-  cta_topk_plan(s_logits, nullptr, B, E, top_k, tile_m, s_idx, s_prob, s_cnt, s_warp, topk_idx,
-                topk_prob, counts, offsets, tile_offsets, perm_token, perm_prob, route_pos,
-                nullptr);
+  if (B * top_k <= 64) {
+    if (warp == 0)
+      warp_topk_plan(s_logits, B, E, top_k, tile_m, s_idx, s_prob, s_cnt, topk_idx, topk_prob,
+                     counts, offsets, tile_offsets, perm_token, perm_prob, route_pos, lane);
+  } else {
+    cta_topk_plan(s_logits, nullptr, B, E, top_k, tile_m, s_idx, s_prob, s_cnt, s_warp, topk_idx,
+                  topk_prob, counts, offsets, tile_offsets, perm_token, perm_prob, route_pos,
+                  nullptr);
+  }
   if (threadIdx.x == 0) *counter = 0;  // ready for the next launch
 }
 
@@ -316,9 +350,10 @@ LLMYB_API int32_t llmyb_decode_norm_gemv(const float* streams_in, const void* de
   do {                                                                                          \
     st = ensure_smem(decode_norm_gemv_kernel<BMV, KCHV>, bytes, attr[bi][ki]);                  \
     if (st) return st;                                                                          \
-    decode_norm_gemv_kernel<BMV, KCHV><<<grid, 256, bytes, s>>>(                                 \
-        streams_in, dl, route_pos, top_k, n_tokens, d_model, norm_w, eps, wb, n_out, ob, out_ld, \
-        streams_out, nb);                                                                       \
+    st = launch_pdl(decode_norm_gemv_kernel<BMV, KCHV>, dim3(grid), dim3(256), bytes, s,         \
+                    streams_in, dl, route_pos, top_k, n_tokens, d_model, norm_w, eps, wb, n_out, \
+                    ob, out_ld, streams_out, nb);                                                \
+    if (st) return st;                                                                          \
   } while (0)
   if (bm == 1) {
     if (kch == 3) LLMYB_NG(1, 3); else if (kch == 4) LLMYB_NG(1, 4); else LLMYB_NG(1, 8);
@@ -365,13 +400,14 @@ LLMYB_API int32_t llmyb_decode_out_router(
   do {                                                                                          \
     st = ensure_smem(decode_out_router_kernel<BMV, KCHV, VM>, bytes, attr[bi][ki][VM - 1]);     \
     if (st) return st;                                                                          \
-    decode_out_router_kernel<BMV, KCHV, VM><<<grid, 256, bytes, s>>>(                            \
+    st = launch_pdl(decode_out_router_kernel<BMV, KCHV, VM>, dim3(grid), dim3(256), bytes, s,    \
         static_cast<const __nv_bfloat16*>(in), in_ld, k_in,                                     \
         static_cast<const __nv_bfloat16*>(w), n_tokens, d_model, conv_w,                        \
         static_cast<const __nv_bfloat16*>(normed), static_cast<__nv_bfloat16*>(history),        \
         static_cast<__nv_bfloat16*>(mixed), counter, streams, ffn_norm, router_norm, w_router,  \
         eps, n_experts, top_k, tile_m, static_cast<__nv_bfloat16*>(m_bf), topk_idx, topk_prob,  \
         expert_counts, expert_offsets, tile_offsets, perm_token, perm_prob, route_pos);         \
+    if (st) return st;                                                                          \
   } while (0)
 #define LLMYB_OR_K(BMV, VM)                                                                     \
   do {                                                                                          \

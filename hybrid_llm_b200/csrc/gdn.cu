@@ -91,6 +91,8 @@ __global__ void __launch_bounds__(128) gdn_step_kernel(GdnIO io, int H, int VD,
   constexpr int RPW = KD / 4;  // state rows per warp
   __shared__ float s_q[KD], s_k[KD];
   __shared__ float s_red[4][32];
+  pdl_wait();  // q/k/v/gate/beta come from the projection kernel
+  pdl_trigger();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int nvc = VD / 32;
   const int b = blockIdx.x / (H * nvc);
@@ -864,9 +866,12 @@ LLMYB_API int32_t llmyb_gdn_step(const void* q, int64_t q_stride, const void* k,
   const int grid = batch * heads * (value_dim / 32);
   auto* o = static_cast<__nv_bfloat16*>(out);
   if (key_dim == 64)
-    gdn_step_kernel<64><<<grid, 128, 0, s>>>(io, heads, value_dim, state, o, out_stride);
+    st = launch_pdl(gdn_step_kernel<64>, dim3(grid), dim3(128), 0, s, io, heads, value_dim, state,
+                    o, out_stride);
   else
-    gdn_step_kernel<128><<<grid, 128, 0, s>>>(io, heads, value_dim, state, o, out_stride);
+    st = launch_pdl(gdn_step_kernel<128>, dim3(grid), dim3(128), 0, s, io, heads, value_dim, state,
+                    o, out_stride);
+  if (st) return st;
   count_launch();
   return launch_status();
 }

@@ -61,6 +61,8 @@ __global__ void __launch_bounds__(256) moe_decode_up_kernel(
     const int* __restrict__ expert_offsets, const __nv_bfloat16* __restrict__ w13, int D, int F,
     int E, int compact, __nv_bfloat16* __restrict__ h_perm) {
   extern __shared__ __nv_bfloat16 s_x[];  // [kTok][D]
+  pdl_wait();  // the plan and the expert input come from the router
+  pdl_trigger();
   const int fblocks = F / kWarps;
   const int e = slot_expert(expert_offsets, E, blockIdx.x / fblocks, compact);
   if (e < 0) return;
@@ -125,6 +127,8 @@ __global__ void __launch_bounds__(256) moe_decode_down_kernel(
     const int* __restrict__ expert_offsets, const __nv_bfloat16* __restrict__ w2, int D, int F,
     int E, int compact, const int* __restrict__ out_row, __nv_bfloat16* __restrict__ y_perm) {
   extern __shared__ __nv_bfloat16 s_h[];  // [kTok][F]
+  pdl_wait();  // h comes from the up kernel
+  pdl_trigger();
   const int dblocks = D / kWarps;
   const int e = slot_expert(expert_offsets, E, blockIdx.x / dblocks, compact);
   if (e < 0) return;
@@ -247,13 +251,17 @@ int32_t launch_experts(const void* x, int32_t n_tokens, int32_t d_model, int32_t
   const int64_t rows = static_cast<int64_t>(n_tokens) * top_k;
   const int slots = static_cast<int>(std::min<int64_t>(n_experts, rows));
   const int compact = slots < n_experts ? 1 : 0;
-  moe_decode_up_kernel<<<slots * (ffn / kWarps), 256, up_smem, s>>>(
-      static_cast<const __nv_bfloat16*>(x), perm_token, expert_offsets,
-      static_cast<const __nv_bfloat16*>(w13), d_model, ffn, n_experts, compact, h);
+  cudaError_t e = launch_pdl(moe_decode_up_kernel, dim3(slots * (ffn / kWarps)), dim3(256),
+                             up_smem, s, static_cast<const __nv_bfloat16*>(x), perm_token,
+                             expert_offsets, static_cast<const __nv_bfloat16*>(w13), d_model, ffn,
+                             n_experts, compact, h);
+  if (e != cudaSuccess) return e;
   count_launch();
-  moe_decode_down_kernel<<<slots * (d_model / kWarps), 256, down_smem, s>>>(
-      h, perm_prob, expert_offsets, static_cast<const __nv_bfloat16*>(w2), d_model, ffn,
-      n_experts, compact, out_row, y);
+  e = launch_pdl(moe_decode_down_kernel, dim3(slots * (d_model / kWarps)), dim3(256), down_smem, s,
+                 static_cast<const __nv_bfloat16*>(h), perm_prob, expert_offsets,
+                 static_cast<const __nv_bfloat16*>(w2), d_model, ffn, n_experts, compact, out_row,
+                 y);
+  if (e != cudaSuccess) return e;
   count_launch();
   return launch_status();
 }

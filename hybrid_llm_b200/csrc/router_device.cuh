@@ -210,6 +210,68 @@ __device__ __forceinline__ void cta_plan_tail(int N, int E, int k, int tile_m, c
                         sort_order, lane);
 }
 
+// Top-k, softmax and the whole plan of N tokens by one warp, for decode
+// batches with few routes: the CTA-wide scans of cta_topk_plan and their
+// barriers cost more than the work there.  Same results as cta_topk_plan.
+// s_idx / s_prob hold N*k entries, s_base E entries (shared memory).
+__device__ __forceinline__ void warp_topk_plan(const float* logits, int N, int E, int k,
+                                               int tile_m, int* s_idx, float* s_prob, int* s_base,
+                                               int64_t* __restrict__ topk_idx,
+                                               float* __restrict__ topk_prob,
+                                               int* __restrict__ counts, int* __restrict__ offsets,
+                                               int* __restrict__ tile_offsets,
+                                               int* __restrict__ perm_token,
+                                               float* __restrict__ perm_prob,
+                                               int* __restrict__ route_pos, int lane) {
+  for (int t = 0; t < N; ++t) {
+    int idx;
+    float val;
+    warp_topk_row(logits + static_cast<int64_t>(t) * E, nullptr, E, k, lane, idx, val);
+    const float p = warp_topk_softmax(val, k, lane);
+    if (lane < k) {
+      s_idx[t * k + lane] = idx;
+      s_prob[t * k + lane] = p;
+      topk_idx[static_cast<int64_t>(t) * k + lane] = idx;
+      topk_prob[static_cast<int64_t>(t) * k + lane] = p;
+    }
+  }
+  __syncwarp();
+  const int R = N * k;
+  int run = 0, trun = 0;
+  for (int e0 = 0; e0 < E; e0 += 32) {
+    const int e = e0 + lane;
+    int c = 0;
+    if (e < E)
+      for (int r = 0; r < R; ++r) c += s_idx[r] == e ? 1 : 0;
+    const int tl = e < E ? static_cast<int>(ceil_div(c, tile_m)) : 0;
+    int x = c, y = tl;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int xx = __shfl_up_sync(0xffffffffu, x, o);
+      const int yy = __shfl_up_sync(0xffffffffu, y, o);
+      if (lane >= o) {
+        x += xx;
+        y += yy;
+      }
+    }
+    if (e < E) {
+      counts[e] = c;
+      offsets[e] = run + x - c;
+      tile_offsets[e] = trun + y - tl;
+      s_base[e] = run + x - c;
+    }
+    run += __shfl_sync(0xffffffffu, x, 31);
+    trun += __shfl_sync(0xffffffffu, y, 31);
+  }
+  if (lane == 0) {
+    offsets[E] = run;
+    tile_offsets[E] = trun;
+  }
+  __syncwarp();
+  warp_stable_scatter(s_idx, s_prob, R, k, s_base, perm_token, perm_prob, route_pos, nullptr,
+                      lane);
+}
+
 // Sum over the 256 threads of a CTA in a fixed order (s_red: 8 floats).
 __device__ __forceinline__ float block_sum_256(float v, float* s_red) {
   v = warp_sum(v);
