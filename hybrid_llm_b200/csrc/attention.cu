@@ -415,8 +415,10 @@ constexpr int kMaxChunks = 8;  // 16-byte chunks of a K row per lane: H*DH <= 20
 // shared memory by two bulk copies issued at entry, so the score and value
 // loops read shared memory instead of waiting on one global round trip per
 // key; the arithmetic is that of the unstaged kernel.
-template <bool STAGED>
-__global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(256, STAGED ? 1 : 4)
+// NT threads per CTA (512 for the staged variant: more warps to hide the
+// latency of a batch-1 step); KCH 16-byte K chunks per lane (H*DH <= 256*KCH).
+template <bool STAGED, int NT, int KCH>
+__global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(NT, STAGED ? 1 : 4)
     csa_decode_kernel(const __nv_bfloat16* __restrict__ q, int64_t sq,
                       const __nv_bfloat16* __restrict__ knew, int64_t skn,
                       const __nv_bfloat16* __restrict__ vnew, int64_t svn,
@@ -436,7 +438,8 @@ __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(256, STAG
   const int nch = HD / 8;            // 16-byte chunks per K row
   const int seg = DH / 8;            // lanes per head within one pass (8 or 16)
   const int vch = D / 8;             // 16-byte chunks per V row
-  const int groups = max(1, 256 / vch);
+  const int groups = max(1, NT / vch);
+  constexpr int NW = NT / 32;
   __nv_bfloat16* s_q = reinterpret_cast<__nv_bfloat16*>(dsm);
   float* s_sc = dsm + HD / 2;
   float* s_m = s_sc + H * kpc;
@@ -485,22 +488,22 @@ __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(256, STAG
   // query and the new key / value come from the projection kernel
   pdl_wait();
   pdl_trigger();
-  for (int c = tid; c < nch; c += 256)
+  for (int c = tid; c < nch; c += NT)
     reinterpret_cast<uint4*>(s_q)[c] = reinterpret_cast<const uint4*>(q + b * sq)[c];
   __syncthreads();
   if (STAGED && nk > 0) staged_ok = sm100::mbar_wait(&s_bar[0], 0, dev_status, nullptr);
   // ---- scores: one key per warp iteration, the whole K row in flight
-  for (int jl = warp; jl < nk; jl += 8) {
+  for (int jl = warp; jl < nk; jl += NW) {
     const int j = j_begin + jl;
     const __nv_bfloat16* kr = (j == cur_slot) ? knew + b * skn : kb + static_cast<int64_t>(j) * HD;
-    uint4 kv[kMaxChunks];
+    uint4 kv[KCH];
 #pragma unroll
-    for (int i = 0; i < kMaxChunks; ++i) {
+    for (int i = 0; i < KCH; ++i) {
       const int c = lane + 32 * i;
       if (c < nch) kv[i] = reinterpret_cast<const uint4*>(kr)[c];
     }
 #pragma unroll
-    for (int i = 0; i < kMaxChunks; ++i) {
+    for (int i = 0; i < KCH; ++i) {
       const int c = lane + 32 * i;
       float acc = 0.f;
       if (c < nch) {
@@ -529,7 +532,7 @@ __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(256, STAG
     }
   }
   __syncthreads();
-  for (int hh = warp; hh < H; hh += 8) {
+  for (int hh = warp; hh < H; hh += NW) {
     float mx = -INFINITY;
     for (int j = lane; j < nk; j += 32) mx = fmaxf(mx, s_sc[hh * kpc + j]);
     mx = warp_max(mx);
@@ -544,7 +547,7 @@ __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(256, STAG
   }
   cluster.sync();
   // ---- cluster-wide per-head max / sum
-  for (int hh = warp; hh < H; hh += 8) {
+  for (int hh = warp; hh < H; hh += NW) {
     float mloc = -INFINITY, lloc = 0.f;
     if (lane < kClusterCtas) {
       mloc = *cluster.map_shared_rank(&s_m[hh], lane);
@@ -559,7 +562,7 @@ __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(256, STAG
   }
   __syncthreads();
   // ---- head-averaged probabilities of this CTA's keys
-  for (int j = tid; j < nk; j += 256) {
+  for (int j = tid; j < nk; j += NT) {
     float p = 0.f;
     for (int hh = 0; hh < H; ++hh) p += exp2f(s_sc[hh * kpc + j] - s_M[hh]) / s_L[hh];
     s_p[j] = p / static_cast<float>(H);
@@ -592,7 +595,7 @@ __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(256, STAG
   }
   __syncthreads();
   if (groups > 1) {
-    for (int d = tid; d < D; d += 256) {
+    for (int d = tid; d < D; d += NT) {
       float acc = s_o[d];
       for (int g = 1; g < groups; ++g) acc += s_o[g * D + d];
       s_o[d] = acc;
@@ -601,7 +604,7 @@ __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(256, STAG
   cluster.sync();
   // ---- reduce this CTA's column slice over the cluster
   const int cols = D / kClusterCtas;
-  for (int d = crank * cols + tid; d < (crank + 1) * cols; d += 256) {
+  for (int d = crank * cols + tid; d < (crank + 1) * cols; d += NT) {
     float acc = 0.f;
     for (int r = 0; r < kClusterCtas; ++r) acc += *cluster.map_shared_rank(&s_o[d], r);
     out[b * so + d] = f2bf(acc);
@@ -766,32 +769,44 @@ LLMYB_API int32_t llmyb_csa_local_decode(const void* q, int64_t q_stride, const 
       knew_stride % 8 != 0 || vnew_stride % 8 != 0)
     return LLMYB_EUNSUPPORTED;
   const int kpc = (window + kClusterCtas - 1) / kClusterCtas;
-  const int groups = std::max(1, 256 / (d_model / 8));
-  const int base_floats = (hd / 2 + heads * kpc + 4 * heads + kpc + groups * d_model + 3) & ~3;
-  const int64_t staged_bytes =
-      static_cast<int64_t>(base_floats) * 4 + static_cast<int64_t>(kpc) * (hd + d_model) * 2 + 16;
+  auto base_floats = [&](int nt) {
+    const int groups = std::max(1, nt / (d_model / 8));
+    return (hd / 2 + heads * kpc + 4 * heads + kpc + groups * d_model + 3) & ~3;
+  };
+  const int64_t staged_bytes = static_cast<int64_t>(base_floats(512)) * 4 +
+                               static_cast<int64_t>(kpc) * (hd + d_model) * 2 + 16;
   // small batches: one cluster per row is far from filling the GPU, so each
-  // CTA stages its keys in shared memory (one CTA per SM) to cut latency
+  // CTA stages its keys in shared memory (one CTA of 512 threads per SM)
   const bool staged = batch <= 32 && staged_bytes <= 220 * 1024;
-  const int bytes = staged ? static_cast<int>(staged_bytes) : base_floats * 4;
+  const int bytes = staged ? static_cast<int>(staged_bytes) : base_floats(256) * 4;
+  const int kch = hd <= 768 ? 3 : (hd <= 1024 ? 4 : 8);
   if (bytes > 227 * 1024) return LLMYB_EUNSUPPORTED;
-  auto launch = [&](auto kernel, int& attr_bytes) -> int32_t {
+  auto launch = [&](auto kernel, int nt, int& attr_bytes) -> int32_t {
     if (bytes > attr_bytes) {
       int32_t st = set_smem(kernel, bytes);
       if (st) return st;
       attr_bytes = bytes;
     }
     return static_cast<int32_t>(launch_pdl(
-        kernel, dim3(batch * kClusterCtas), dim3(256), bytes, static_cast<cudaStream_t>(stream),
+        kernel, dim3(batch * kClusterCtas), dim3(nt), bytes, static_cast<cudaStream_t>(stream),
         static_cast<const __nv_bfloat16*>(q), q_stride, static_cast<const __nv_bfloat16*>(knew),
         knew_stride, static_cast<const __nv_bfloat16*>(vnew), vnew_stride,
         static_cast<__nv_bfloat16*>(kcache), static_cast<__nv_bfloat16*>(vcache), positions,
         heads, head_dim, d_model, window, kLog2e / sqrtf(static_cast<float>(head_dim)),
         static_cast<__nv_bfloat16*>(out), out_stride, dev_status));
   };
-  static int attr_staged = 0, attr_plain = 0;
-  const int32_t st = staged ? launch(csa_decode_kernel<true>, attr_staged)
-                            : launch(csa_decode_kernel<false>, attr_plain);
+  static int attr[2][3] = {};
+  const int ki = kch == 3 ? 0 : (kch == 4 ? 1 : 2);
+  int32_t st;
+  if (staged) {
+    st = kch == 3 ? launch(csa_decode_kernel<true, 512, 3>, 512, attr[0][ki])
+       : kch == 4 ? launch(csa_decode_kernel<true, 512, 4>, 512, attr[0][ki])
+                  : launch(csa_decode_kernel<true, 512, 8>, 512, attr[0][ki]);
+  } else {
+    st = kch == 3 ? launch(csa_decode_kernel<false, 256, 3>, 256, attr[1][ki])
+       : kch == 4 ? launch(csa_decode_kernel<false, 256, 4>, 256, attr[1][ki])
+                  : launch(csa_decode_kernel<false, 256, 8>, 256, attr[1][ki]);
+  }
   if (st) return st;
   count_launch();
   return launch_status();

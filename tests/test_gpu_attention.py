@@ -116,8 +116,10 @@ def test_csa_local_decode_matches_oracle(cuda, b, h, dh, dm, w, pos):
 
 @pytest.mark.parametrize("h,dh,dm,w", [(12, 64, 768, 512), (4, 128, 256, 40), (16, 128, 2048, 256)])
 def test_csa_local_decode_staged_equals_plain(cuda, h, dh, dm, w):
-    """Batches of up to 32 rows stage each CTA's ring rows in shared memory;
-    larger batches read them from global memory.  Same rows, same results."""
+    """Batches of up to 32 rows stage each CTA's ring rows in shared memory
+    (512 threads); larger batches read them from global memory (256 threads).
+    Same ring updates; outputs equal up to the order of the fp32 value sums
+    (at most one bf16 unit in the last place)."""
     from hybrid_llm_b200 import kernels
     b = 40
     rng = np.random.default_rng(h * w)
@@ -135,5 +137,7 @@ def test_csa_local_decode_staged_equals_plain(cuda, h, dh, dm, w):
                         for i in range(0, b, 8)])                             # 8 rows: staged
     torch.cuda.synchronize()
     kernels.check_device_status()
-    assert torch.equal(plain, staged)
+    ulp = plain.float().abs() * 2.0 ** -7 + 1e-30
+    assert bool(((plain.float() - staged.float()).abs() <= ulp).all())
+    assert float((plain == staged).float().mean()) > 0.9
     assert torch.equal(k1, k2) and torch.equal(v1, v2)
