@@ -176,6 +176,68 @@ def run_reference(args) -> None:
 
 
 # ------------------------------------------------------------- our path
+# DRAM traffic of one decode_out_router_kernel launch at the small-llmy decode
+# shape, measured with ncu (dram__bytes_read.sum + dram__bytes_write.sum, one
+# launch of a GDN block and of a CSA block: 1,302,528 and 1,320,192 bytes).
+OUT_ROUTER_TRAFFIC = 1_311_360
+
+
+def out_router_roofline(model, p: dict, reps: int = 50) -> dict:
+    """Roofline of the decode step's dominant kernel (decode_out_router_kernel:
+    output projection + residual + norms + router of one block, the largest
+    share of the step's launch list) at the benchmark's decode shape.  Its
+    average launch duration is timed with CUDA events over a CUDA graph of
+    `reps` launches on the stream it runs on; the inputs are scratch copies,
+    so the decode state is untouched."""
+    import torch
+
+    from hybrid_llm_b200 import kernels
+    from hybrid_llm_b200.weights import CsaBlock
+
+    cfg = model.cfg
+    d = cfg.d_model
+    blk = next(b for b in model.w.blocks if isinstance(b.mixer, CsaBlock))
+    g = torch.Generator(device="cuda").manual_seed(3)
+    inp = torch.randn(1, d, device="cuda", generator=g).bfloat16()
+    streams = torch.randn(1, d, device="cuda", generator=g)
+    m_bf = torch.empty(1, d, dtype=torch.bfloat16, device="cuda")
+    counter = torch.zeros(1, dtype=torch.int32, device="cuda")
+    call = lambda: kernels.decode_out_router(inp, blk.mixer.w_o, streams, blk.ffn_norm,
+                                             blk.moe.router_norm, blk.moe.router, cfg.moe_top_k,
+                                             cfg.rms_eps, m_bf, counter, tile_m=128)
+    call()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        call()
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for _ in range(reps):
+            call()
+    graph.replay()
+    torch.cuda.synchronize()
+    a, b = _events()
+    a.record()
+    for _ in range(5):
+        graph.replay()
+    b.record()
+    torch.cuda.synchronize()
+    dt = a.elapsed_time(b) * 1e-3 / (5 * reps)
+    nb = lambda t: t.numel() * t.element_size()
+    alg = (nb(blk.mixer.w_o) + nb(blk.moe.router) + nb(blk.ffn_norm) + nb(blk.moe.router_norm)
+           + nb(inp) + 2 * nb(streams) + nb(m_bf))
+    achieved = alg / dt / 1e9
+    return {"bound": "hbm", "achieved": achieved, "peak": p["hbm_gbs"], "unit": "GB/s",
+            "frac": achieved / p["hbm_gbs"], "traffic": OUT_ROUTER_TRAFFIC,
+            "kernel": "decode_out_router_kernel (CSA block, batch 1): output projection GEMV + "
+                      "residual + two RMSNorms + router logits/top-k/plan in the last CTA",
+            "algorithmic_bytes_per_launch": alg, "avg_launch_us": dt * 1e6,
+            "timing": f"CUDA events over a graph of {reps} launches x 5 replays",
+            "peak_source": p["source"]}
+
+
 def _events():
     import torch
     return torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -471,15 +533,16 @@ def run_ours(args) -> None:
            "h2d_bytes_per_step": host_in.numel() * 8,
            "d2h_bytes_per_step": host_out.numel() * 8 + host_lp.numel() * 4}
 
-    # roofline of the dominant kernel family: the decode step is HBM-bound on
-    # the weights it streams; measured per step over the timed region
+    # roofline of the whole step (weights and state touched per token) and of
+    # the dominant kernel of the step's launch list
     touched = decode_bytes_per_step(model, cfg)
     achieved = touched / (t_ms * 1e-3 / args.steps) / 1e9
-    roofline = {"bound": "hbm", "achieved": achieved, "peak": p["hbm_gbs"], "unit": "GB/s",
-                "frac": achieved / p["hbm_gbs"], "traffic": None,
-                "kernel": "whole decode step (one CUDA graph); algorithmic bytes = weights and "
-                          "state touched per token",
-                "algorithmic_bytes_per_step": touched, "peak_source": p["source"]}
+    step_roofline = {"bound": "hbm", "achieved": achieved, "peak": p["hbm_gbs"], "unit": "GB/s",
+                     "frac": achieved / p["hbm_gbs"],
+                     "what": "whole decode step (one CUDA graph); algorithmic bytes = weights "
+                             "and state touched per token",
+                     "algorithmic_bytes_per_step": touched}
+    roofline = out_router_roofline(model, p)
 
     line = {
         "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
@@ -490,12 +553,20 @@ def run_ours(args) -> None:
                    "parallelism": f"replicas{world}" if world > 1 else "single",
                    "l2": "no flush: >1 GB of weights, about 0.3 GB touched per step (> 126 MB L2)"},
         "e2e": e2e, "gpu_launches": launches_per_step * args.steps, "roofline": roofline,
+        "step_roofline": step_roofline,
         "clocks": clocks.summary(), "prefill_tok_s_c2": bsz * prompt_len / prefill_s,
     }
-    if rank == 0 and world == 1 and not args.no_secondary:
-        del dec, out
+    del dec, out, model
+    torch.cuda.empty_cache()
+    secondary = {}
+    if not args.no_ep:  # every rank: expert parallel over the whole group when N > 1
+        secondary["large_ep_decode"] = secondary_ep_decode(p, steps=10, warmup=3)
         torch.cuda.empty_cache()
-        line["secondary"] = {"moe_layer": secondary_moe(p), "long_prefill": secondary_prefill(p)}
+    if rank == 0 and world == 1 and not args.no_secondary:
+        secondary["moe_layer"] = secondary_moe(p)
+        secondary["long_prefill"] = secondary_prefill(p)
+    if secondary:
+        line["secondary"] = secondary
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_decode_baseline(steps=3, warmup=1)
     if rank == 0:
@@ -536,6 +607,8 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-ep", action="store_true",
+                    help="skip the large expert-parallel decode measurement")
     ap.add_argument("--only", choices=["moe_layer", "long_prefill", "ep_decode"], default=None,
                     help="run one secondary workload alone (used for kernel profiles)")
     args = ap.parse_args()
