@@ -56,7 +56,14 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     # expert parallelism
     "llmyb_ep_header_rows": (I32, [I32, I32, I32]),
     "llmyb_ep_dispatch_pack": (I32, [P, I32, P, P, P, P, I32, I32, I32, I32, P, P, P]),
-    "llmyb_ep_recv_plan": (I32, [P, I32, I32, I32, I32, I32, P, P, P, P, P, P]),
+    "llmyb_ep_recv_plan": (I32, [P, I32, I32, I32, I32, I32, P, P, P, P, P, P, P, P, P]),
+    "llmyb_ep_shared_alloc": (I32, [I64, P, P]),
+    "llmyb_ep_shared_open": (I32, [P, P]),
+    "llmyb_ep_shared_close": (I32, [P]),
+    "llmyb_ep_shared_free": (I32, [P]),
+    "llmyb_ep_dispatch_p2p": (I32, [P, I32, P, P, P, P, I32, I32, I32, I32, P, P, P, P, P]),
+    "llmyb_ep_return_p2p": (I32, [P, P, I32, I32, I32, I32, P, P, P, P]),
+    "llmyb_ep_wait": (I32, [P, I32, P, P, P]),
     # gated delta rule
     "llmyb_gdn_activate": (I32, [P, I64, I32, I32, I32, I32, P, P]),
     "llmyb_gdn_step": (I32, [P, I64, P, I64, P, I64, P, I64, P, I64, P, P, P, I32, I32, I32, I32,

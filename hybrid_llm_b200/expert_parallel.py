@@ -12,10 +12,17 @@ expert outputs back:
 
 ``run`` packs W fixed-size dispatch segments (capacity C = max_tokens * k
 rows each, so no sizes travel to the host and the step can be replayed as a
-CUDA graph), exchanges them with ``all_to_all_single`` (NCCL between GPUs),
-builds the expert-ordered plan of the received rows, runs the local experts
-with their outputs written straight into the return segments, and exchanges
-those back.  The combine is the routed residual add of the next block.  For a
+CUDA graph), exchanges them, builds the expert-ordered plan of the received
+rows, runs the local experts with their outputs written straight into the
+return segments, and exchanges those back.  Two exchanges:
+
+* ``"nccl"``: ``all_to_all_single`` of the segments (the baseline);
+* ``"p2p"``: every rank maps the others' receive / return buffers (CUDA IPC,
+  one process per GPU on one node); the pack kernel stores each segment
+  straight into its destination over NVLink and the return kernel stores the
+  expert outputs back, each send published by a per-round flag that the
+  receiving kernel waits on (bounded).  No collective call is left in the
+  step, so it can be captured in a CUDA graph.  The combine is the routed residual add of the next block.  For a
 route the expert math, its rounding and the order of the k-term sum are those
 of the single-device path, so results are identical for any W.
 
@@ -24,12 +31,85 @@ kernels and raises for CPU tensors (there is no CPU fallback).
 """
 from __future__ import annotations
 
+import ctypes
 from dataclasses import dataclass, replace
 
 import torch
 import torch.distributed as dist
 
-from . import kernels
+from . import _native, kernels
+
+
+class _CudaMemory:
+    """Device memory seen through __cuda_array_interface__ (bytes), so that a
+    buffer allocated by the library can be viewed as a torch tensor."""
+
+    def __init__(self, ptr: int, nbytes: int):
+        self.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1",
+                                         "data": (ptr, False), "version": 2, "strides": None}
+
+
+class PeerBuffers:
+    """One CUDA-IPC buffer per rank, mapped by every other rank of the group.
+
+    Layout: receive segments [W, H+C, D] bf16 | return segments [W, C, D] bf16
+    | dispatch flags [W] int32 | return flags [W] int32.  Collective: every
+    rank constructs it together (handles travel through the process group)."""
+
+    def __init__(self, world: int, rank: int, seg_rows: int, capacity: int, d_model: int,
+                 device: torch.device, group=None):
+        self.world, self.rank = world, rank
+        al = lambda b: (b + 255) // 256 * 256
+        self.recv_bytes = world * seg_rows * d_model * 2
+        self.ret_off = al(self.recv_bytes)
+        self.flags_off = self.ret_off + al(world * capacity * d_model * 2)
+        self.nbytes = self.flags_off + al(2 * world * 4)
+        lib = _native.lib()
+        ptr = ctypes.c_void_p()
+        handle = (ctypes.c_char * 64)()
+        _native.check(lib.llmyb_ep_shared_alloc(self.nbytes, ctypes.addressof(ptr),
+                                                ctypes.addressof(handle)), "llmyb_ep_shared_alloc")
+        self.base = ptr.value
+        handles = [None] * world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        self.peer_base = []
+        self._opened = []
+        for q in range(world):
+            if q == rank:
+                self.peer_base.append(self.base)
+                continue
+            h = (ctypes.c_char * 64).from_buffer_copy(handles[q])
+            pp = ctypes.c_void_p()
+            _native.check(lib.llmyb_ep_shared_open(ctypes.addressof(h), ctypes.addressof(pp)),
+                          "llmyb_ep_shared_open")
+            self.peer_base.append(pp.value)
+            self._opened.append(pp.value)
+        mem = torch.as_tensor(_CudaMemory(self.base, self.nbytes), device=device)
+        self.local = mem  # keeps the view object alive
+        self.recv = mem[:self.recv_bytes].view(torch.bfloat16).view(world * seg_rows, d_model)
+        self.ret_recv = mem[self.ret_off:self.ret_off + world * capacity * d_model * 2].view(
+            torch.bfloat16).view(world * capacity, d_model)
+        flags = mem[self.flags_off:self.flags_off + 2 * world * 4].view(torch.int32)
+        self.dispatch_flags, self.return_flags = flags[:world], flags[world:]
+        # host tables of peer addresses (this rank's slots in every peer's buffer)
+        vp = ctypes.c_void_p * world
+        self.dispatch_segs = vp(*[b + rank * seg_rows * d_model * 2 for b in self.peer_base])
+        self.dispatch_flag_ptrs = vp(*[b + self.flags_off + rank * 4 for b in self.peer_base])
+        self.return_segs = vp(*[b + self.ret_off + rank * capacity * d_model * 2
+                                for b in self.peer_base])
+        self.return_flag_ptrs = vp(*[b + self.flags_off + (world + rank) * 4
+                                     for b in self.peer_base])
+
+    def close(self) -> None:
+        lib = _native.lib()
+        for p in self._opened:
+            lib.llmyb_ep_shared_close(p)
+        self._opened = []
+        if self.base:
+            torch.cuda.synchronize()
+            self.recv = self.ret_recv = self.local = None
+            lib.llmyb_ep_shared_free(self.base)
+            self.base = 0
 
 
 class CudaEpOps:
@@ -45,14 +125,31 @@ class CudaEpOps:
 
     @staticmethod
     def dispatch_pack(ep: "ExpertParallel", x, plan, ret_route_pos) -> None:
-        kernels.ep_dispatch_pack(x, plan, ep.n_experts, ep.world, ep.capacity, ep.send,
-                                 ret_route_pos)
+        if ep.peers is not None:
+            pb = ep.peers
+            kernels.ep_dispatch_p2p(x, plan, ep.n_experts, ep.world, ep.capacity,
+                                    ctypes.addressof(pb.dispatch_segs),
+                                    ctypes.addressof(pb.dispatch_flag_ptrs), ep.sync,
+                                    ret_route_pos)
+        else:
+            kernels.ep_dispatch_pack(x, plan, ep.n_experts, ep.world, ep.capacity, ep.send,
+                                     ret_route_pos)
 
     @staticmethod
     def recv_plan(ep: "ExpertParallel") -> None:
+        wait = ep.peers.dispatch_flags if ep.peers is not None else None
         kernels.ep_recv_plan(ep.recv, ep.world, ep.capacity, ep.experts_per_rank, ep.offsets_l,
                              ep.perm_token_l, ep.perm_prob_l, ep.out_row,
-                             tile_offsets_l=ep.tile_offsets_l, tile_m=ep.tile_m)
+                             tile_offsets_l=ep.tile_offsets_l, tile_m=ep.tile_m,
+                             wait_flags=wait, sync=ep.sync if wait is not None else None)
+
+    @staticmethod
+    def return_push(ep: "ExpertParallel") -> None:
+        pb = ep.peers
+        kernels.ep_return_p2p(ep.ret_send, ep.recv, ep.world, ep.capacity, ep.experts_per_rank,
+                              ctypes.addressof(pb.return_segs),
+                              ctypes.addressof(pb.return_flag_ptrs), ep.sync)
+        kernels.ep_wait(pb.return_flags, ep.world, ep.sync)
 
     @staticmethod
     def experts_to(ep: "ExpertParallel", w13, w2, grouped: bool) -> None:
@@ -85,7 +182,7 @@ class ExpertParallel:
 
     def __init__(self, n_experts: int, top_k: int, d_model: int, ffn: int, max_tokens: int, *,
                  group: dist.ProcessGroup | None = None, device: torch.device | str | None = None,
-                 ops=None):
+                 ops=None, exchange: str = "nccl"):
         if not dist.is_initialized():
             raise RuntimeError("ExpertParallel needs an initialised torch.distributed group")
         self.group = group
@@ -103,10 +200,21 @@ class ExpertParallel:
         self.header = int(self.ops.header_rows(self.experts_per_rank, c, d))
         bf = dict(dtype=torch.bfloat16, device=self.device)
         i32 = dict(dtype=torch.int32, device=self.device)
-        self.send = torch.zeros(w * (self.header + c), d, **bf)
-        self.recv = torch.zeros_like(self.send)
+        if exchange not in ("nccl", "p2p"):
+            raise ValueError(f"unknown exchange {exchange!r}")
+        self.exchange = exchange
+        self.peers = None
         self.ret_send = torch.zeros(w * c, d, **bf)
-        self.ret_recv = torch.zeros_like(self.ret_send)
+        if exchange == "p2p":
+            # receive / return segments live in the IPC buffer the peers store into
+            self.peers = PeerBuffers(w, self.rank, self.header + c, c, d, self.device, group)
+            self.send = None
+            self.recv, self.ret_recv = self.peers.recv, self.peers.ret_recv
+            self.sync = torch.zeros(3, **i32)
+        else:
+            self.send = torch.zeros(w * (self.header + c), d, **bf)
+            self.recv = torch.zeros_like(self.send)
+            self.ret_recv = torch.zeros_like(self.ret_send)
         self.offsets_l = torch.zeros(self.experts_per_rank + 1, **i32)
         self.perm_token_l = torch.zeros(w * c, **i32)
         self.perm_prob_l = torch.zeros(w * c, dtype=torch.float32, device=self.device)
@@ -144,12 +252,22 @@ class ExpertParallel:
             raise ValueError("w13_local must hold this rank's experts only")
         rp = self.ret_route_pos[:n_routes]
         self.ops.dispatch_pack(self, x, plan, rp)
-        self._exchange(self.recv, self.send)
+        if self.peers is None:
+            self._exchange(self.recv, self.send)
         self.ops.recv_plan(self)
         if path not in ("auto", "grouped", "decode"):
             raise ValueError(f"unknown expert path {path!r}")
         grouped = path == "grouped" or (
             path == "auto" and kernels.use_grouped_rows(self.capacity, self.experts_per_rank))
         self.ops.experts_to(self, w13_local, w2_local, grouped)
-        self._exchange(self.ret_recv, self.ret_send)
+        if self.peers is None:
+            self._exchange(self.ret_recv, self.ret_send)
+        else:
+            self.ops.return_push(self)
         return EpResult(self.ret_recv, rp)
+
+    def close(self) -> None:
+        """Unmap the peers' buffers and free this rank's (peer-memory exchange)."""
+        if self.peers is not None:
+            self.peers.close()
+            self.peers = None

@@ -281,15 +281,50 @@ def ep_dispatch_pack(x: torch.Tensor, plan: RoutePlan, n_experts: int, world: in
 def ep_recv_plan(recv: torch.Tensor, world: int, capacity: int, experts_per_rank: int,
                  offsets_l: torch.Tensor, perm_token_l: torch.Tensor, perm_prob_l: torch.Tensor,
                  out_row: torch.Tensor, tile_offsets_l: torch.Tensor | None = None,
-                 tile_m: int = 128) -> None:
-    """Expert-ordered plan over the received dispatch segments."""
-    _require_cuda(recv, offsets_l, perm_token_l, perm_prob_l, out_row, tile_offsets_l)
+                 tile_m: int = 128, wait_flags: torch.Tensor | None = None,
+                 sync: torch.Tensor | None = None) -> None:
+    """Expert-ordered plan over the received dispatch segments (after a bounded
+    wait for the peers' dispatch flags when wait_flags is given)."""
+    _require_cuda(recv, offsets_l, perm_token_l, perm_prob_l, out_row, tile_offsets_l, wait_flags,
+                  sync)
     for t, n in ((offsets_l, "offsets_l"), (perm_token_l, "perm_token_l"),
                  (perm_prob_l, "perm_prob_l"), (out_row, "out_row")):
         _inplace(t, n)
+    status = device_status(recv.device) if wait_flags is not None else None
     _native.call("llmyb_ep_recv_plan", _ptr(recv), recv.shape[-1], int(world), int(capacity),
                  int(experts_per_rank), int(tile_m), _ptr(offsets_l), _ptr(tile_offsets_l),
-                 _ptr(perm_token_l), _ptr(perm_prob_l), _ptr(out_row), _stream())
+                 _ptr(perm_token_l), _ptr(perm_prob_l), _ptr(out_row), _ptr(wait_flags),
+                 _ptr(sync), _ptr(status), _stream())
+
+
+def ep_dispatch_p2p(x: torch.Tensor, plan: RoutePlan, n_experts: int, world: int, capacity: int,
+                    peer_segs: int, peer_flags: int, sync: torch.Tensor,
+                    ret_route_pos: torch.Tensor) -> None:
+    """Dispatch segments stored straight into the peers' receive buffers.
+    peer_segs / peer_flags: host addresses of arrays of W device pointers."""
+    _require_cuda(x, sync, ret_route_pos)
+    x = x.contiguous()
+    n_routes = plan.perm_token.numel()
+    _native.call("llmyb_ep_dispatch_p2p", _ptr(x), x.shape[-1], _ptr(plan.offsets),
+                 _ptr(plan.perm_token), _ptr(plan.perm_prob), _ptr(plan.route_pos), n_routes,
+                 int(n_experts), int(world), int(capacity), peer_segs, peer_flags, _ptr(sync),
+                 _ptr(ret_route_pos), _stream())
+
+
+def ep_return_p2p(ret_send: torch.Tensor, recv: torch.Tensor, world: int, capacity: int,
+                  experts_per_rank: int, peer_segs: int, peer_flags: int,
+                  sync: torch.Tensor) -> None:
+    """Expert outputs pushed back into the source ranks' return buffers."""
+    _require_cuda(ret_send, recv, sync)
+    _native.call("llmyb_ep_return_p2p", _ptr(ret_send), _ptr(recv), ret_send.shape[-1], int(world),
+                 int(capacity), int(experts_per_rank), peer_segs, peer_flags, _ptr(sync), _stream())
+
+
+def ep_wait(flags: torch.Tensor, world: int, sync: torch.Tensor) -> None:
+    """Bounded device-side wait for the current exchange round's flags."""
+    _require_cuda(flags, sync)
+    _native.call("llmyb_ep_wait", _ptr(flags), int(world), _ptr(sync),
+                 _ptr(device_status(flags.device)), _stream())
 
 
 def grouped_scratch_bytes(n_rows: int, d_model: int, ffn: int) -> int:

@@ -222,7 +222,45 @@ int32_t llmyb_ep_dispatch_pack(const void* x, int32_t d_model, const int32_t* of
 int32_t llmyb_ep_recv_plan(const void* recv, int32_t d_model, int32_t world, int32_t capacity,
                            int32_t experts_per_rank, int32_t tile_m, int32_t* offsets_l,
                            int32_t* tile_offsets_l, int32_t* perm_token_l, float* perm_prob_l,
-                           int32_t* out_row, void* stream);
+                           int32_t* out_row, const int32_t* wait_flags, const int32_t* sync,
+                           int32_t* dev_status, void* stream);
+
+/* Peer-memory exchange (one process per GPU on one node, W <= 8): each rank
+ * allocates one buffer the others map with CUDA IPC - its receive segments,
+ * its return segments and two flag arrays of W int32 (dispatch, return).
+ * Sends are plain stores over NVLink; the last CTA of a send stores the
+ * exchange round into every peer's flag (release, system scope); receivers
+ * wait on their own flags (acquire, bounded by one second: LLMYB_ETIMEOUT).
+ * sync = int32[3] per rank (round, two CTA tickets), zero-initialised.
+ * With wait_flags, llmyb_ep_recv_plan first waits for the dispatch flags; a
+ * header whose counts exceed the capacity is treated as empty
+ * (LLMYB_EINVAL in dev_status). */
+int32_t llmyb_ep_shared_alloc(int64_t bytes, void** dev_ptr, void* handle);
+int32_t llmyb_ep_shared_open(const void* handle, void** dev_ptr);
+int32_t llmyb_ep_shared_close(void* dev_ptr);
+int32_t llmyb_ep_shared_free(void* dev_ptr);
+
+/* llmyb_ep_dispatch_pack into the peers' receive buffers: peer_segs[q] is
+ * this rank's segment in rank q's buffer, peer_flags[q] this rank's dispatch
+ * flag there (host arrays of W device pointers).  Starts a new round. */
+int32_t llmyb_ep_dispatch_p2p(const void* x, int32_t d_model, const int32_t* offsets,
+                              const int32_t* perm_token, const float* perm_prob,
+                              const int32_t* route_pos, int32_t n_routes, int32_t n_experts,
+                              int32_t world, int32_t capacity, void* const* peer_segs,
+                              int32_t* const* peer_flags, int32_t* sync, int32_t* ret_route_pos,
+                              void* stream);
+
+/* Return push: the expert outputs of the rows rank q sent (ret_send rows
+ * [q*C, q*C + n_q), n_q from q's header in recv) into peer_segs[q], then the
+ * round into peer_flags[q] (this rank's return flag there). */
+int32_t llmyb_ep_return_p2p(const void* ret_send, const void* recv, int32_t d_model,
+                            int32_t world, int32_t capacity, int32_t experts_per_rank,
+                            void* const* peer_segs, int32_t* const* peer_flags, int32_t* sync,
+                            void* stream);
+
+/* Bounded wait (one CTA) until flags[0..W) hold the current round. */
+int32_t llmyb_ep_wait(const int32_t* flags, int32_t world, const int32_t* sync,
+                      int32_t* dev_status, void* stream);
 
 /* ------------------------------------------------------ gated delta rule
  * Replaces GatedDeltaNet's recurrence (model/layers/gated_deltanet.py:140-149

@@ -161,17 +161,23 @@ def _nccl_worker(rank, world, port, errors):
         e, k, d, f = 16, 4, 512, 256
         n = [3 + 2 * r for r in range(world)]
         w13, wd, xs, plans = _setup(dev, world, e, k, d, f, n, seed=3)
-        ep = ExpertParallel(e, k, d, f, max(n), device=dev)
-        lo, hi = ep.expert_range
-        for path in ("decode", "grouped", "decode"):
-            res = ep.run(xs[rank], plans[rank], w13[lo:hi].contiguous(), wd[lo:hi].contiguous(),
-                         path=path)
-            from hybrid_llm_b200 import kernels
-            streams = torch.zeros(n[rank], d, dtype=torch.float32, device=dev)
-            kernels.add_rmsnorm_routed(streams, res.y_rows, res.plan_for_combine(plans[rank]), None,
-                                       1e-6, normalize=False)
-            want = _single_device(xs[rank], plans[rank], w13, wd, d, grouped=path == "grouped")
-            assert torch.equal(streams, want), f"rank {rank}: NCCL expert-parallel != single device"
+        from hybrid_llm_b200 import kernels
+        for exchange in ("nccl", "p2p"):
+            ep = ExpertParallel(e, k, d, f, max(n), device=dev, exchange=exchange)
+            lo, hi = ep.expert_range
+            for path in ("decode", "grouped", "decode"):
+                res = ep.run(xs[rank], plans[rank], w13[lo:hi].contiguous(),
+                             wd[lo:hi].contiguous(), path=path)
+                streams = torch.zeros(n[rank], d, dtype=torch.float32, device=dev)
+                kernels.add_rmsnorm_routed(streams, res.y_rows, res.plan_for_combine(plans[rank]),
+                                           None, 1e-6, normalize=False)
+                want = _single_device(xs[rank], plans[rank], w13, wd, d, grouped=path == "grouped")
+                assert torch.equal(streams, want), \
+                    f"rank {rank}: {exchange} expert-parallel != single device"
+            torch.cuda.synchronize()
+            kernels.check_device_status()
+            dist.barrier()
+            ep.close()
         torch.cuda.synchronize()
         dist.barrier()
         dist.destroy_process_group()
@@ -215,7 +221,7 @@ def _model_worker(rank, world, port, errors):
         sd = synthetic_state_dict(cfg, seed=5, device=dev, std=0.05)
         full = LoopedHybridModel(ModelWeights.from_state_dict(cfg, sd, dev))
         ep = ExpertParallel(cfg.moe_experts, cfg.moe_top_k, cfg.d_model, cfg.moe_hidden, bsz * t,
-                            device=dev)
+                            device=dev, exchange="p2p")
         shard = LoopedHybridModel(ModelWeights.from_state_dict(cfg, sd, dev,
                                                                expert_range=ep.expert_range), ep=ep)
         g = torch.Generator(device="cpu").manual_seed(100 + rank)
@@ -238,8 +244,22 @@ def _model_worker(rank, world, port, errors):
                 lb = shard.decode_step(tok, st_ep)
                 assert torch.equal(la, lb), f"rank {rank}: {path} expert-parallel decode differs"
                 tok = la.float().argmax(-1)
+        # the peer-memory exchange inside a captured CUDA graph
+        from hybrid_llm_b200.model import GreedyDecoder
+        toks = []
+        for use_graph in (False, True):
+            st = RecurrentState(cfg, bsz, dev)
+            st.load_state_dict(out_full.state.state_dict())
+            dec = GreedyDecoder(shard, st, use_graph=use_graph)
+            dec.prime(a[:, -1].argmax(-1))
+            toks.append(torch.stack([dec.step().clone() for _ in range(4)], 1))
+            del dec
+        assert torch.equal(toks[0], toks[1]), f"rank {rank}: graph decode differs"
         torch.cuda.synchronize()
+        from hybrid_llm_b200 import kernels
+        kernels.check_device_status()
         dist.barrier()
+        ep.close()
         dist.destroy_process_group()
     except BaseException as exc:
         errors.put(f"rank {rank}: {exc!r}")
