@@ -372,13 +372,15 @@ def ep_decode_bytes_per_step(cfg, batch_local: int, world: int, weights) -> floa
 
 
 def secondary_ep_decode(p: dict, steps: int = 10, warmup: int = 3, global_batch: int = 64,
-                        context: int = 4096) -> dict:
+                        context: int = 4096, exchange: str = "p2p") -> dict:
     """Large expert-parallel config decode: d 2048, 24 blocks, 64 experts top-8,
     3 loops, vocab 64000, global batch 64 split over the ranks; experts sharded
     64/W per rank (ExpertParallel, all-to-all over NCCL) for W > 1.  The
     4096-token context is a synthetic recurrent state (RecurrentState.
     fill_synthetic): decode cost does not depend on the context's values.
-    Collective when torch.distributed is initialised: every rank calls it."""
+    exchange "p2p" (peer-memory, the step replayed as one CUDA graph) or
+    "nccl" (all_to_all_single, eager).  Collective when torch.distributed is
+    initialised: every rank calls it."""
     import torch
     import torch.distributed as dist
 
@@ -395,16 +397,24 @@ def secondary_ep_decode(p: dict, steps: int = 10, warmup: int = 3, global_batch:
     bl = global_batch // world
     ep = None
     if world > 1:
-        ep = ExpertParallel(cfg.moe_experts, cfg.moe_top_k, cfg.d_model, cfg.moe_hidden, bl)
+        ep = ExpertParallel(cfg.moe_experts, cfg.moe_top_k, cfg.d_model, cfg.moe_hidden, bl,
+                            exchange=exchange)
+    use_graph = ep is None or exchange == "p2p"
     weights = ModelWeights.from_state_dict(cfg, synthetic_state_dict(cfg, seed=0, device="cuda"),
                                            "cuda", expert_range=None if ep is None else ep.expert_range)
     model = LoopedHybridModel(weights, ep=ep)
     state = RecurrentState(cfg, bl, "cuda")
     state.fill_synthetic(context, seed=rank)
-    dec = GreedyDecoder(model, state, use_graph=False)
+    dec = GreedyDecoder(model, state, use_graph=use_graph)
     g = torch.Generator(device="cpu").manual_seed(rank)
     dec.prime(torch.randint(0, cfg.vocab_size, (bl,), generator=g).cuda())
-    for _ in range(warmup):
+    # graph replays launch nothing through the library: count one eager step
+    n0 = kernels.launch_count()
+    dec.use_graph = False
+    dec.step()
+    per_step = kernels.launch_count() - n0
+    dec.use_graph = use_graph
+    for _ in range(warmup):  # the first graph step captures
         dec.step()
     torch.cuda.synchronize()
     n0 = kernels.launch_count()
@@ -422,19 +432,26 @@ def secondary_ep_decode(p: dict, steps: int = 10, warmup: int = 3, global_batch:
     if world > 1:
         dist.barrier()
     t_ms = a.elapsed_time(b)
-    launches = (kernels.launch_count() - n0) // steps
+    launches = per_step if use_graph else (kernels.launch_count() - n0) // steps
+    kernels.check_device_status()
     if world > 1:
         tt = torch.tensor([t_ms], device="cuda")
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         t_ms = float(tt.item())
+    del dec
+    if ep is not None:
+        dist.barrier()
+        ep.close()
     step_s = t_ms * 1e-3 / steps
     touched = ep_decode_bytes_per_step(cfg, bl, world, weights)
     achieved = touched / step_s / 1e9
     return {"workload": "large expert-parallel config: d 2048, 24 blocks, 64 experts top-8, "
                         "3 loops, vocab 64000, batch 64, 4096-token synthetic context",
             "n_gpus": world, "batch_per_rank": bl, "parallelism": f"ep{world}" if world > 1 else
-            "single", "exchange": "NCCL all_to_all_single" if world > 1 else None,
-            "graph": False, "tok_s": global_batch / step_s, "ms_per_step": step_s * 1e3,
+            "single", "exchange": None if world == 1 else (
+                "peer-memory stores over NVLink (CUDA IPC), flags" if exchange == "p2p"
+                else "NCCL all_to_all_single"),
+            "graph": use_graph, "tok_s": global_batch / step_s, "ms_per_step": step_s * 1e3,
             "llmyb_launches_per_step": launches,
             "hbm_bytes_per_step_per_rank": touched, "achieved_gbs_per_rank": achieved,
             "frac_of_hbm": achieved / p["hbm_gbs"]}
@@ -609,6 +626,8 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-ep", action="store_true",
                     help="skip the large expert-parallel decode measurement")
+    ap.add_argument("--ep-exchange", choices=["p2p", "nccl"], default="p2p",
+                    help="expert-parallel exchange of --only ep_decode")
     ap.add_argument("--only", choices=["moe_layer", "long_prefill", "ep_decode"], default=None,
                     help="run one secondary workload alone (used for kernel profiles)")
     args = ap.parse_args()
@@ -624,7 +643,8 @@ def main() -> None:
         torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
         if int(os.environ.get("WORLD_SIZE", "1")) > 1:
             dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
-        res = secondary_ep_decode(peaks(), steps=args.steps, warmup=args.warmup)
+        res = secondary_ep_decode(peaks(), steps=args.steps, warmup=args.warmup,
+                                  exchange=args.ep_exchange)
         if not dist.is_initialized() or dist.get_rank() == 0:
             print(json.dumps({"only": args.only, **res}), flush=True)
         if dist.is_initialized():
