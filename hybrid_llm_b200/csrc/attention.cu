@@ -409,6 +409,41 @@ constexpr int kMaxChunks = 8;  // 16-byte chunks of a K row per lane: H*DH <= 20
 // loads in flight per warp (the kernel is bound by the K/V window bytes).
 // Dynamic shared memory: q [H*DH] | scores [H][kpc] | m, l, M, L [H] |
 // p [kpc] | partial out [groups][D].
+// Per-head sums of one key's scores.  Lane L holds in v[i] its partial
+// q.k over 16-byte chunk L + 32 i; chunk i of a group of SEG lanes (one head
+// of DH = 8 SEG elements) belongs to head (L / SEG) + (32 / SEG) i.  A
+// reduce-scatter over the SEG lanes (each level keeps half of the values and
+// adds the partner's other half) leaves every lane one head's full sum with
+// log2(KP) + ... = log2(SEG) levels and KP - 1 + (levels beyond log2 KP)
+// shuffles instead of KP log2(SEG).  ifin: the chunk index the lane ends with.
+template <int SEG, int KP>
+__device__ __forceinline__ float head_reduce(float (&v)[KP], int lane, int& ifin) {
+  ifin = 0;
+  int n = KP;
+#pragma unroll
+  for (int m = SEG / 2; m >= 1; m >>= 1) {
+    if (n > 1) {
+      const bool up = (lane & m) != 0;
+      const int half = n / 2;
+#pragma unroll
+      for (int t = 0; t < KP / 2; ++t) {
+        if (t < half) {
+          const float send = up ? v[t] : v[t + half];
+          const float keep = up ? v[t + half] : v[t];
+          v[t] = keep + __shfl_xor_sync(0xffffffffu, send, m);
+        }
+      }
+      if (up) ifin += half;
+      n = half;
+    } else {
+      v[0] += __shfl_xor_sync(0xffffffffu, v[0], m);
+    }
+  }
+  return v[0];
+}
+
+constexpr int pow2_ceil(int x) { return x <= 1 ? 1 : 2 * pow2_ceil((x + 1) / 2); }
+
 // Four CTAs per SM (64 registers): a batch of 64 rows is 64 clusters of 8,
 // which must all be resident at once to run in a single wave.
 // STAGED (small batches): the CTA's K and V ring rows are brought into
@@ -416,8 +451,9 @@ constexpr int kMaxChunks = 8;  // 16-byte chunks of a K row per lane: H*DH <= 20
 // loops read shared memory instead of waiting on one global round trip per
 // key; the arithmetic is that of the unstaged kernel.
 // NT threads per CTA (512 for the staged variant: more warps to hide the
-// latency of a batch-1 step); KCH 16-byte K chunks per lane (H*DH <= 256*KCH).
-template <bool STAGED, int NT, int KCH>
+// latency of a batch-1 step); KCH 16-byte K chunks per lane (H*DH <= 256*KCH);
+// SEG = DH / 8 lanes per head.
+template <bool STAGED, int NT, int KCH, int SEG>
 __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(NT, STAGED ? 1 : 4)
     csa_decode_kernel(const __nv_bfloat16* __restrict__ q, int64_t sq,
                       const __nv_bfloat16* __restrict__ knew, int64_t skn,
@@ -492,8 +528,16 @@ __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(NT, STAGE
     reinterpret_cast<uint4*>(s_q)[c] = reinterpret_cast<const uint4*>(q + b * sq)[c];
   __syncthreads();
   if (STAGED && nk > 0) staged_ok = sm100::mbar_wait(&s_bar[0], 0, dev_status, nullptr);
-  // ---- scores: one key per warp iteration, the whole K row in flight
-  for (int jl = warp; jl < nk; jl += NW) {
+  // ---- scores: one key per warp iteration, the whole K row in flight.  Each
+  // CTA starts at a different key of its range: all CTAs begin together and
+  // their ranges start 1 MB apart, so in-order streams would hit the same
+  // DRAM channels at the same time.
+  const int rot = nk > 0 ? static_cast<int>((static_cast<unsigned>(b) * 131u +
+                                             static_cast<unsigned>(crank) * 37u) %
+                                            static_cast<unsigned>(nk))
+                         : 0;
+  for (int it = warp; it < nk; it += NW) {
+    const int jl = it + rot < nk ? it + rot : it + rot - nk;
     const int j = j_begin + jl;
     const __nv_bfloat16* kr = (j == cur_slot) ? knew + b * skn : kb + static_cast<int64_t>(j) * HD;
     uint4 kv[KCH];
@@ -502,11 +546,13 @@ __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(NT, STAGE
       const int c = lane + 32 * i;
       if (c < nch) kv[i] = reinterpret_cast<const uint4*>(kr)[c];
     }
+    constexpr int KP = pow2_ceil(KCH);
+    float pv[KP];
 #pragma unroll
-    for (int i = 0; i < KCH; ++i) {
+    for (int i = 0; i < KP; ++i) {
       const int c = lane + 32 * i;
-      float acc = 0.f;
-      if (c < nch) {
+      pv[i] = 0.f;
+      if (i < KCH && c < nch) {
         const uint32_t w[4] = {kv[i].x, kv[i].y, kv[i].z, kv[i].w};
         const uint4 q4 = reinterpret_cast<const uint4*>(s_q)[c];
         const uint32_t qw[4] = {q4.x, q4.y, q4.z, q4.w};
@@ -514,14 +560,15 @@ __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(NT, STAGE
         for (int e = 0; e < 4; ++e) {
           const float2 f = unpack_bf16x2(w[e]);
           const float2 qf = unpack_bf16x2(qw[e]);
-          acc += qf.x * f.x + qf.y * f.y;
+          pv[i] += qf.x * f.x + qf.y * f.y;
         }
       }
-      if (32 * i < nch) {
-        for (int o = 1; o < seg; o <<= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-        if (c < nch && (c % seg) == 0) s_sc[(c / seg) * kpc + jl] = acc * scale_log2;
-      }
     }
+    int ifin;
+    const float score = head_reduce<SEG, KP>(pv, lane, ifin);
+    constexpr int dup = KP < SEG ? SEG / KP - 1 : 0;  // lanes holding the same head
+    if ((lane & dup) == 0 && (lane & ~(SEG - 1)) + 32 * ifin < nch)
+      s_sc[((lane + 32 * ifin) / SEG) * kpc + jl] = score * scale_log2;
     if (j == cur_slot) {  // append the current token to the ring
       for (int c = lane; c < nch; c += 32)
         reinterpret_cast<uint4*>(kcache + (cache_row + j) * HD)[c] =
@@ -575,7 +622,28 @@ __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(NT, STAGE
     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     if (g < groups) {
       int j = g;
-#pragma unroll 4
+      // eight keys' chunks in flight per thread, then their products in key order
+      for (; j + 7 * groups < nk; j += 8 * groups) {
+        uint4 v8[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int jj = j_begin + j + u * groups;
+          const __nv_bfloat16* vr =
+              (jj == cur_slot) ? vnew + b * svn : vb + static_cast<int64_t>(jj) * D;
+          v8[u] = reinterpret_cast<const uint4*>(vr)[c];
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const float p = s_p[j + u * groups];
+          const uint32_t w[4] = {v8[u].x, v8[u].y, v8[u].z, v8[u].w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = unpack_bf16x2(w[e]);
+            acc[2 * e] += p * f.x;
+            acc[2 * e + 1] += p * f.y;
+          }
+        }
+      }
       for (; j < nk; j += groups) {
         const int jj = j_begin + j;
         const __nv_bfloat16* vr =
@@ -780,6 +848,7 @@ LLMYB_API int32_t llmyb_csa_local_decode(const void* q, int64_t q_stride, const 
   const bool staged = batch <= 32 && staged_bytes <= 220 * 1024;
   const int bytes = staged ? static_cast<int>(staged_bytes) : base_floats(256) * 4;
   const int kch = hd <= 768 ? 3 : (hd <= 1024 ? 4 : 8);
+  const bool seg16 = head_dim == 128;
   if (bytes > 227 * 1024) return LLMYB_EUNSUPPORTED;
   auto launch = [&](auto kernel, int nt, int& attr_bytes) -> int32_t {
     if (bytes > attr_bytes) {
@@ -795,18 +864,21 @@ LLMYB_API int32_t llmyb_csa_local_decode(const void* q, int64_t q_stride, const 
         heads, head_dim, d_model, window, kLog2e / sqrtf(static_cast<float>(head_dim)),
         static_cast<__nv_bfloat16*>(out), out_stride, dev_status));
   };
-  static int attr[2][3] = {};
+  static int attr[2][3][2] = {};
   const int ki = kch == 3 ? 0 : (kch == 4 ? 1 : 2);
   int32_t st;
-  if (staged) {
-    st = kch == 3 ? launch(csa_decode_kernel<true, 512, 3>, 512, attr[0][ki])
-       : kch == 4 ? launch(csa_decode_kernel<true, 512, 4>, 512, attr[0][ki])
-                  : launch(csa_decode_kernel<true, 512, 8>, 512, attr[0][ki]);
-  } else {
-    st = kch == 3 ? launch(csa_decode_kernel<false, 256, 3>, 256, attr[1][ki])
-       : kch == 4 ? launch(csa_decode_kernel<false, 256, 4>, 256, attr[1][ki])
-                  : launch(csa_decode_kernel<false, 256, 8>, 256, attr[1][ki]);
-  }
+#define LLMYB_CSA(ST, NTV, SEGV)                                                         \
+  (kch == 3 ? launch(csa_decode_kernel<ST, NTV, 3, SEGV>, NTV,                          \
+                     attr[ST ? 0 : 1][ki][SEGV == 16])                                   \
+   : kch == 4 ? launch(csa_decode_kernel<ST, NTV, 4, SEGV>, NTV,                        \
+                       attr[ST ? 0 : 1][ki][SEGV == 16])                                 \
+              : launch(csa_decode_kernel<ST, NTV, 8, SEGV>, NTV,                        \
+                       attr[ST ? 0 : 1][ki][SEGV == 16]))
+  if (staged)
+    st = seg16 ? LLMYB_CSA(true, 512, 16) : LLMYB_CSA(true, 512, 8);
+  else
+    st = seg16 ? LLMYB_CSA(false, 256, 16) : LLMYB_CSA(false, 256, 8);
+#undef LLMYB_CSA
   if (st) return st;
   count_launch();
   return launch_status();

@@ -40,7 +40,8 @@ constexpr int A_STAGE_BYTES = BM * BK * 2;  // 16 KB
 constexpr int B_STAGE_BYTES = BN * BK * 2;  // 32 KB
 constexpr int STAGE_BYTES = A_STAGE_BYTES + B_STAGE_BYTES;
 constexpr int TMEM_COLS = 512;              // 2 accumulators x 256 fp32 columns
-constexpr int GEMM_SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+constexpr int EPI_SCRATCH = 4 * 32 * 64;  // per epilogue warp: 32 rows x 64 bytes, transposing
+constexpr int GEMM_SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/ + EPI_SCRATCH;
 
 enum Epilogue { kSwiGLU = 0, kScale = 1 };
 
@@ -81,9 +82,31 @@ __device__ __forceinline__ float swiglu_fast(uint32_t g_bits, uint32_t u_bits) {
 //   kScale : 256 outputs, each times the row's route probability.
 // The TMEM loads of chunk i+1 are in flight while chunk i is converted and
 // stored (double-buffered registers).
+// One 32-column bf16 chunk of the warp's 32 rows (pk: this lane's row, 64 B)
+// to global memory through shared memory: lane L stages its row, then each
+// store instruction writes 8 whole 64-byte row pieces (4 lanes per row) rather
+// than 32 scattered 16-byte pieces.  Parts are XOR-swizzled so that both the
+// staging writes and the reads are free of bank conflicts.
+__device__ __forceinline__ void store_chunk_rows(const uint4 (&pk)[4], bool valid,
+                                                 __nv_bfloat16* dst, uint4* scratch, int lane) {
+  __syncwarp();
+#pragma unroll
+  for (int j = 0; j < 4; ++j) scratch[lane * 4 + (j ^ ((lane >> 1) & 3))] = pk[j];
+  __syncwarp();
+  const uint64_t my_dst = reinterpret_cast<uint64_t>(dst);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int r = i * 8 + (lane >> 2), j = lane & 3;
+    const uint64_t rd = __shfl_sync(0xffffffffu, my_dst, r);
+    const int rv = __shfl_sync(0xffffffffu, valid ? 1 : 0, r);
+    const uint4 v = scratch[r * 4 + (j ^ ((r >> 1) & 3))];
+    if (rv) reinterpret_cast<uint4*>(rd)[j] = v;
+  }
+}
+
 template <int EPI>
 __device__ __forceinline__ void epilogue_rows(uint32_t t_row, bool valid, float scale,
-                                              __nv_bfloat16* dst) {
+                                              __nv_bfloat16* dst, uint4* scratch, int lane) {
   static_assert(BN == 256, "epilogue assumes 256 accumulator columns");
   if constexpr (EPI == kSwiGLU) {
     constexpr int NCH = BN / 2 / 32;
@@ -100,17 +123,13 @@ __device__ __forceinline__ void epilogue_rows(uint32_t t_row, bool valid, float 
         sm100::tmem_ld_32x32b_x32(t_row + 32 * (i + 1), g[b ^ 1]);
         sm100::tmem_ld_32x32b_x32(t_row + BN / 2 + 32 * (i + 1), u[b ^ 1]);
       }
-      if (valid) {
-        uint4 pk[4];
-        uint32_t* pw = reinterpret_cast<uint32_t*>(pk);
+      uint4 pk[4];
+      uint32_t* pw = reinterpret_cast<uint32_t*>(pk);
 #pragma unroll
-        for (int j = 0; j < 16; ++j)
-          pw[j] = pack_bf16x2(swiglu_fast(g[b][2 * j], u[b][2 * j]),
-                              swiglu_fast(g[b][2 * j + 1], u[b][2 * j + 1]));
-        uint4* d4 = reinterpret_cast<uint4*>(dst + 32 * i);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) d4[j] = pk[j];
-      }
+      for (int j = 0; j < 16; ++j)
+        pw[j] = pack_bf16x2(swiglu_fast(g[b][2 * j], u[b][2 * j]),
+                            swiglu_fast(g[b][2 * j + 1], u[b][2 * j + 1]));
+      store_chunk_rows(pk, valid, dst + 32 * i, scratch, lane);
     }
   } else {
     constexpr int NCH = BN / 32;
@@ -122,17 +141,13 @@ __device__ __forceinline__ void epilogue_rows(uint32_t t_row, bool valid, float 
       sm100::tmem_ld_wait();
       sm100::tmem_regs_ready(a[b]);
       if (i + 1 < NCH) sm100::tmem_ld_32x32b_x32(t_row + 32 * (i + 1), a[b ^ 1]);
-      if (valid) {
-        uint4 pk[4];
-        uint32_t* pw = reinterpret_cast<uint32_t*>(pk);
+      uint4 pk[4];
+      uint32_t* pw = reinterpret_cast<uint32_t*>(pk);
 #pragma unroll
-        for (int j = 0; j < 16; ++j)
-          pw[j] = pack_bf16x2(__uint_as_float(a[b][2 * j]) * scale,
-                              __uint_as_float(a[b][2 * j + 1]) * scale);
-        uint4* d4 = reinterpret_cast<uint4*>(dst + 32 * i);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) d4[j] = pk[j];
-      }
+      for (int j = 0; j < 16; ++j)
+        pw[j] = pack_bf16x2(__uint_as_float(a[b][2 * j]) * scale,
+                            __uint_as_float(a[b][2 * j + 1]) * scale);
+      store_chunk_rows(pk, valid, dst + 32 * i, scratch, lane);
     }
   }
 }
@@ -263,6 +278,7 @@ __global__ void __launch_bounds__(256, 1) moe_gemm_kernel(
   } else if (warp >= 4) {
     // --------------------------------------------------------- epilogue
     const int q = warp & 3;  // TMEM lane quarter this warp may access
+    uint4* epi_scratch = reinterpret_cast<uint4*>(smem + STAGES * STAGE_BYTES + 256) + q * 128;
     const int r = q * 32 + lane;
     int acc = 0;
     uint32_t acc_phase = 0;
@@ -277,7 +293,7 @@ __global__ void __launch_bounds__(256, 1) moe_gemm_kernel(
       const float scale = (EPI == kScale && valid) ? __ldg(row_scale + row) : 0.0f;
       const int64_t orow = (out_row != nullptr && valid) ? __ldg(out_row + row) : row;
       __nv_bfloat16* dst = out + orow * out_ld + ti.n_tile * (EPI == kSwiGLU ? BN / 2 : BN);
-      epilogue_rows<EPI>(t_row, valid, scale, dst);
+      epilogue_rows<EPI>(t_row, valid, scale, dst, epi_scratch, lane);
       sm100::tc_fence_before();
       sm100::mbar_arrive(&tmem_empty[acc]);
       if (++acc == 2) {
@@ -307,7 +323,7 @@ constexpr int PBM = 128, PBN = 256, PBK = 64, PST = 6;
 constexpr int P_A_BYTES = PBM * PBK * 2;         // 16 KB
 constexpr int P_B_BYTES = (PBN / 2) * PBK * 2;   // 16 KB
 constexpr int P_STAGE = P_A_BYTES + P_B_BYTES;   // 32 KB
-constexpr int P_SMEM = PST * P_STAGE + 1024 + 256;
+constexpr int P_SMEM = PST * P_STAGE + 1024 + 256 + EPI_SCRATCH;
 
 __device__ __forceinline__ TileInfo map_tile_pair(int tile, int n_tiles, const int* tile_offsets,
                                                   const int* expert_offsets, int E) {
@@ -456,6 +472,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1) moe_gemm_pai
     // --------------------------------------------------------- epilogue
     const int q = warp & 3;
     const int r = q * 32 + lane;
+    uint4* epi_scratch = reinterpret_cast<uint4*>(smem + PST * P_STAGE + 256) + q * 128;
     const uint32_t empty_leader0 = sm100::mapa_shared(sm100::smem_u32(&tmem_empty[0]), 0);
     const uint32_t empty_leader1 = sm100::mapa_shared(sm100::smem_u32(&tmem_empty[1]), 0);
     int acc = 0;
@@ -472,7 +489,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1) moe_gemm_pai
       const float scale = (EPI == kScale && valid) ? __ldg(row_scale + row) : 0.0f;
       const int64_t orow = (out_row != nullptr && valid) ? __ldg(out_row + row) : row;
       __nv_bfloat16* dst = out + orow * out_ld + ti.n_tile * (EPI == kSwiGLU ? PBN / 2 : PBN);
-      epilogue_rows<EPI>(t_row, valid, scale, dst);
+      epilogue_rows<EPI>(t_row, valid, scale, dst, epi_scratch, lane);
       sm100::tc_fence_before();
       __syncwarp();
       if (lane == 0) sm100::mbar_arrive_cluster(acc == 0 ? empty_leader0 : empty_leader1);
