@@ -203,8 +203,8 @@ def out_router_roofline(model, p: dict, reps: int = 50) -> dict:
     m_bf = torch.empty(1, d, dtype=torch.bfloat16, device="cuda")
     counter = torch.zeros(1, dtype=torch.int32, device="cuda")
     call = lambda: kernels.decode_out_router(inp, blk.mixer.w_o, streams, blk.ffn_norm,
-                                             blk.moe.router_norm, blk.moe.router, cfg.moe_top_k,
-                                             cfg.rms_eps, m_bf, counter, tile_m=128)
+                                             blk.moe.router_folded, cfg.moe_top_k, cfg.rms_eps,
+                                             m_bf, counter, tile_m=128)
     call()
     s = torch.cuda.Stream()
     s.wait_stream(torch.cuda.current_stream())
@@ -226,13 +226,14 @@ def out_router_roofline(model, p: dict, reps: int = 50) -> dict:
     torch.cuda.synchronize()
     dt = a.elapsed_time(b) * 1e-3 / (5 * reps)
     nb = lambda t: t.numel() * t.element_size()
-    alg = (nb(blk.mixer.w_o) + nb(blk.moe.router) + nb(blk.ffn_norm) + nb(blk.moe.router_norm)
-           + nb(inp) + 2 * nb(streams) + nb(m_bf))
+    alg = (nb(blk.mixer.w_o) + nb(blk.moe.router_folded) + nb(blk.ffn_norm) + nb(inp)
+           + 2 * nb(streams) + nb(m_bf))
     achieved = alg / dt / 1e9
     return {"bound": "hbm", "achieved": achieved, "peak": p["hbm_gbs"], "unit": "GB/s",
             "frac": achieved / p["hbm_gbs"], "traffic": OUT_ROUTER_TRAFFIC,
             "kernel": "decode_out_router_kernel (CSA block, batch 1): output projection GEMV + "
-                      "residual + two RMSNorms + router logits/top-k/plan in the last CTA",
+                      "residual + norm and router-logit shares per CTA, top-k/plan in the last "
+                      "CTA",
             "algorithmic_bytes_per_launch": alg, "avg_launch_us": dt * 1e6,
             "timing": f"CUDA events over a graph of {reps} launches x 5 replays",
             "peak_source": p["source"]}

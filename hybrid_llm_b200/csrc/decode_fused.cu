@@ -188,44 +188,37 @@ __global__ void __launch_bounds__(256) decode_norm_gemv_kernel(
 }
 
 // [C] mixed[b, d] = W[d, :] . in[b] (bf16), with the GDN conv gate applied
-// per column when conv_w is given; the last CTA then runs
-// streams += mixed, the two RMSNorms, the router logits, top-k and the plan.
-template <int BM, int KCH, int VMAX>
+// per column when conv_w is given, and streams += mixed, by the CTA owning
+// column d.  The router input r = RMSNorm_rn(RMSNorm_ffn(x)) is a per-token
+// scaling of x (x = the updated residual row):
+//   inv1 = rsqrt(sum(x^2)/D + eps), inv2 = rsqrt(inv1^2 sum((x ffn_w)^2)/D + eps),
+//   logits[e] = inv1 inv2 sum_d w_fold[e, d] x[d],   w_fold = W_r * ffn_w * rn_w,
+// so every CTA adds its columns' share of the two sums of squares and of the E
+// logits to `partials` [grid][B][2+E]; the last CTA to finish sums them in CTA
+// order, forms m_bf = x inv1 ffn_w and runs top-k and the plan (one warp).
+template <int BM, int KCH>
 __global__ void __launch_bounds__(256) decode_out_router_kernel(
     const __nv_bfloat16* __restrict__ in, int64_t in_ld, int K, const __nv_bfloat16* __restrict__ W,
     int B, int D, const float* __restrict__ conv_w, const __nv_bfloat16* __restrict__ normed,
-    __nv_bfloat16* history, __nv_bfloat16* mixed, int* counter, float* __restrict__ streams,
-    const float* __restrict__ ffn_w, const float* __restrict__ rn_w,
-    const float* __restrict__ w_router, float eps, int E, int top_k, int tile_m,
+    __nv_bfloat16* history, float* __restrict__ partials, int* counter,
+    float* __restrict__ streams, const float* __restrict__ ffn_w,
+    const float* __restrict__ w_fold, float eps, int E, int top_k, int tile_m,
     __nv_bfloat16* __restrict__ m_bf, int64_t* __restrict__ topk_idx,
     float* __restrict__ topk_prob, int* __restrict__ counts, int* __restrict__ offsets,
     int* __restrict__ tile_offsets, int* __restrict__ perm_token, float* __restrict__ perm_prob,
     int* __restrict__ route_pos) {
   extern __shared__ __align__(16) uint8_t smem_c[];
-  __shared__ float s_red[8];
+  __shared__ float s_x[kMaxTokens][8];
   __shared__ int s_idx[kMaxTokens * kMaxTopK];
   __shared__ float s_prob[kMaxTokens * kMaxTopK];
   __shared__ int s_cnt[kMaxExperts];
-  __shared__ int s_warp[32];
+  __shared__ float s_scale[kMaxTokens][2];
   __shared__ int s_last;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int n = blockIdx.x * 8 + warp;
+  const int NV = 2 + E;
   uint4 w[KCH];
   if (n < D) warp_load_row<KCH>(W + static_cast<int64_t>(n) * K, K, lane, w);
-  // the router's weights go to L2 now, one slice per CTA, so that the last
-  // CTA finds them there
-  {
-    const int64_t rbytes = static_cast<int64_t>(E) * D * 4;
-    const int64_t per = (rbytes + gridDim.x - 1) / gridDim.x;
-    const char* base = reinterpret_cast<const char*>(w_router);
-    for (int64_t o = blockIdx.x * per + threadIdx.x * 128; o < min(rbytes, (blockIdx.x + 1) * per);
-         o += 256 * 128)
-      asm volatile("prefetch.global.L2 [%0];" ::"l"(base + o));
-    if (blockIdx.x == 0 && threadIdx.x * 128 < D * 4) {
-      asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<const char*>(ffn_w) + threadIdx.x * 128));
-      asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<const char*>(rn_w) + threadIdx.x * 128));
-    }
-  }
   pdl_wait();  // the projection input comes from the mixer kernel
   pdl_trigger();
   // ---- output projection rows of this CTA
@@ -235,6 +228,7 @@ __global__ void __launch_bounds__(256) decode_out_router_kernel(
     reinterpret_cast<uint4*>(s_in + b * K)[c] =
         __ldg(reinterpret_cast<const uint4*>(in + b * in_ld) + c);
   }
+  if (threadIdx.x < kMaxTokens * 8) s_x[threadIdx.x >> 3][threadIdx.x & 7] = 0.f;
   __syncthreads();
   if (n < D) {
     float acc[BM];
@@ -261,36 +255,78 @@ __global__ void __launch_bounds__(256) decode_out_router_kernel(
         hb[D] = h2;
         hb[2 * D] = xb;
       }
-      mixed[static_cast<int64_t>(b) * D + n] = f2bf(yv);
+      // residual add with the bf16 sub-layer output (as llmyb_add_rmsnorm)
+      float* sp = streams + static_cast<int64_t>(b) * D + n;
+      const float x = *sp + bf2f(f2bf(yv));
+      *sp = x;
+      s_x[b][warp] = x;
     }
   }
-  // ---- the last CTA to finish runs the router on the complete rows
-  __threadfence();  // this thread's mixed / history writes are visible GPU-wide
+  __syncthreads();
+  // ---- this CTA's share of the sums of squares and of the logits
+  for (int t = threadIdx.x; t < B * NV; t += 256) {
+    const int b = t / NV, j = t - b * NV;
+    float acc = 0.f;
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      const int d = blockIdx.x * 8 + c;
+      if (d >= D) break;
+      const float x = s_x[b][c];
+      if (j == 0) {
+        acc += x * x;
+      } else if (j == 1) {
+        const float xf = x * __ldg(ffn_w + d);
+        acc += xf * xf;
+      } else {
+        acc += __ldg(w_fold + static_cast<int64_t>(j - 2) * D + d) * x;
+      }
+    }
+    partials[(static_cast<int64_t>(blockIdx.x) * B + b) * NV + j] = acc;
+  }
+  // ---- the last CTA to finish combines the shares and routes
+  __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) s_last = atomicAdd(counter, 1) == static_cast<int>(gridDim.x) - 1;
   __syncthreads();
   if (!s_last) return;
   __threadfence();
-  float* s_r = reinterpret_cast<float*>(smem_c);  // [B][D], reuses the input rows
-  float* s_logits = s_r + B * D;                  // [B][E]
-  for (int b = 0; b < B; ++b)
-    cta_router_input<VMAX, true>(streams, mixed, b, D, ffn_w, rn_w, eps, m_bf, s_r + b * D, s_red);
-  __syncthreads();
-  for (int p = warp; p < B * E; p += 8) {
-    const int t = p / E, e = p - t * E;
-    const float l = warp_logit(w_router, e, s_r + t * D, D, lane);
-    if (lane == 0) s_logits[p] = l;
+  float* s_tot = reinterpret_cast<float*>(smem_c);  // [B][NV]
+  // one warp per value: lanes take every 32nd CTA, then a fixed xor tree
+  for (int t = warp; t < B * NV; t += 8) {
+    float acc = 0.f;
+    for (int g = lane; g < static_cast<int>(gridDim.x); g += 32)
+      acc += __ldcg(partials + static_cast<int64_t>(g) * B * NV + t);
+    acc = warp_sum(acc);
+    if (lane == 0) s_tot[t] = acc;
   }
   __syncthreads();
-  if (B * top_k <= 64) {
-    if (warp == 0)
-      warp_topk_plan(s_logits, B, E, top_k, tile_m, s_idx, s_prob, s_cnt, topk_idx, topk_prob,
-                     counts, offsets, tile_offsets, perm_token, perm_prob, route_pos, lane);
-  } else {
-    cta_topk_plan(s_logits, nullptr, B, E, top_k, tile_m, s_idx, s_prob, s_cnt, s_warp, topk_idx,
-                  topk_prob, counts, offsets, tile_offsets, perm_token, perm_prob, route_pos,
-                  nullptr);
+  if (threadIdx.x < B) {
+    const int b = threadIdx.x;
+    const float inv1 = rsqrtf(s_tot[b * NV] / static_cast<float>(D) + eps);
+    const float inv2 = rsqrtf(inv1 * inv1 * s_tot[b * NV + 1] / static_cast<float>(D) + eps);
+    s_scale[b][0] = inv1;
+    s_scale[b][1] = inv1 * inv2;
   }
+  __syncthreads();
+  float* s_logits = s_tot + B * NV;  // [B][E]
+  for (int t = threadIdx.x; t < B * E; t += 256) {
+    const int b = t / E, e = t - b * E;
+    s_logits[t] = s_scale[b][1] * s_tot[b * NV + 2 + e];
+  }
+  // m = x * inv1 * ffn_w (bf16), 4 columns per thread step
+  for (int i = threadIdx.x; i < B * (D >> 2); i += 256) {
+    const int b = i / (D >> 2), c = i - b * (D >> 2);
+    const float4 x = __ldcg(reinterpret_cast<const float4*>(streams + static_cast<int64_t>(b) * D) + c);
+    const float4 f = __ldg(reinterpret_cast<const float4*>(ffn_w) + c);
+    const float inv1 = s_scale[b][0];
+    reinterpret_cast<uint2*>(m_bf + static_cast<int64_t>(b) * D)[c] =
+        make_uint2(pack_bf16x2(x.x * inv1 * f.x, x.y * inv1 * f.y),
+                   pack_bf16x2(x.z * inv1 * f.z, x.w * inv1 * f.w));
+  }
+  __syncthreads();
+  if (warp == 0)
+    warp_topk_plan(s_logits, B, E, top_k, tile_m, s_idx, s_prob, s_cnt, topk_idx, topk_prob,
+                   counts, offsets, tile_offsets, perm_token, perm_prob, route_pos, lane);
   if (threadIdx.x == 0) *counter = 0;  // ready for the next launch
 }
 
@@ -369,57 +405,52 @@ LLMYB_API int32_t llmyb_decode_norm_gemv(const float* streams_in, const void* de
 
 LLMYB_API int32_t llmyb_decode_out_router(
     const void* in, int64_t in_ld, int32_t k_in, const void* w, int32_t n_tokens,
-    int32_t d_model, const float* conv_w, const void* normed, void* history, void* mixed,
-    int32_t* counter, float* streams, const float* ffn_norm, const float* router_norm,
-    const float* w_router, float eps, int32_t n_experts, int32_t top_k, int32_t tile_m,
-    void* m_bf, int64_t* topk_idx, float* topk_prob, int32_t* expert_counts,
-    int32_t* expert_offsets, int32_t* tile_offsets, int32_t* perm_token, float* perm_prob,
-    int32_t* route_pos, void* stream) {
-  if (!in || !w || !mixed || !counter || !streams || !ffn_norm || !router_norm || !w_router ||
-      !m_bf || !topk_idx || !topk_prob || !expert_counts || !expert_offsets || !tile_offsets ||
-      !perm_token || !perm_prob || !route_pos || n_tokens < 0 || d_model <= 0 || k_in <= 0 ||
+    int32_t d_model, const float* conv_w, const void* normed, void* history, float* partials,
+    int32_t* counter, float* streams, const float* ffn_norm, const float* w_router_folded,
+    float eps, int32_t n_experts, int32_t top_k, int32_t tile_m, void* m_bf, int64_t* topk_idx,
+    float* topk_prob, int32_t* expert_counts, int32_t* expert_offsets, int32_t* tile_offsets,
+    int32_t* perm_token, float* perm_prob, int32_t* route_pos, void* stream) {
+  if (!in || !w || !partials || !counter || !streams || !ffn_norm || !w_router_folded || !m_bf ||
+      !topk_idx || !topk_prob || !expert_counts || !expert_offsets || !tile_offsets ||
+      !perm_token || !perm_prob || !route_pos || n_tokens <= 0 || d_model <= 0 || k_in <= 0 ||
       in_ld < k_in || n_experts <= 0 || top_k <= 0 || top_k > n_experts || tile_m <= 0 ||
       (conv_w && (!normed || !history)))
     return LLMYB_EINVAL;
-  if (n_tokens == 0) return LLMYB_EINVAL;
   const int kch = kch_for(k_in);
   if (n_tokens > kMaxTokens || kch == 0 || d_model % 8 != 0 || d_model > 2048 ||
-      top_k > kMaxTopK || n_experts > kMaxExperts || in_ld % 8 != 0 || !aligned16(in) ||
-      !aligned16(w) || !aligned16(streams) || !aligned16(ffn_norm) || !aligned16(router_norm) ||
-      !aligned16(w_router) || !aligned16(mixed) || (reinterpret_cast<uintptr_t>(m_bf) & 7u))
+      top_k > kMaxTopK || n_experts > kMaxExperts || n_tokens * top_k > 64 || in_ld % 8 != 0 ||
+      !aligned16(in) || !aligned16(w) || !aligned16(streams) || !aligned16(ffn_norm) ||
+      (reinterpret_cast<uintptr_t>(m_bf) & 7u))
     return LLMYB_EUNSUPPORTED;
-  const int bytes = std::max(n_tokens * k_in * 2, (n_tokens * d_model + n_tokens * n_experts) * 4);
+  const int nv = 2 + n_experts;
+  const int bytes =
+      std::max(n_tokens * k_in * 2, (n_tokens * nv + n_tokens * n_experts) * 4);
   const int grid = static_cast<int>(ceil_div(d_model, 8));
-  const int vmax = d_model <= 1024 ? 1 : 2;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  static int attr[3][3][2] = {};
+  static int attr[3][3] = {};
   const int bm = bm_for(n_tokens);
   const int bi = bm == 1 ? 0 : (bm == 4 ? 1 : 2), ki = kch == 3 ? 0 : (kch == 4 ? 1 : 2);
   int32_t st = LLMYB_OK;
-#define LLMYB_OR(BMV, KCHV, VM)                                                                 \
+#define LLMYB_OR(BMV, KCHV)                                                                     \
   do {                                                                                          \
-    st = ensure_smem(decode_out_router_kernel<BMV, KCHV, VM>, bytes, attr[bi][ki][VM - 1]);     \
+    st = ensure_smem(decode_out_router_kernel<BMV, KCHV>, bytes, attr[bi][ki]);                 \
     if (st) return st;                                                                          \
-    st = launch_pdl(decode_out_router_kernel<BMV, KCHV, VM>, dim3(grid), dim3(256), bytes, s,    \
+    st = launch_pdl(decode_out_router_kernel<BMV, KCHV>, dim3(grid), dim3(256), bytes, s,        \
         static_cast<const __nv_bfloat16*>(in), in_ld, k_in,                                     \
         static_cast<const __nv_bfloat16*>(w), n_tokens, d_model, conv_w,                        \
         static_cast<const __nv_bfloat16*>(normed), static_cast<__nv_bfloat16*>(history),        \
-        static_cast<__nv_bfloat16*>(mixed), counter, streams, ffn_norm, router_norm, w_router,  \
-        eps, n_experts, top_k, tile_m, static_cast<__nv_bfloat16*>(m_bf), topk_idx, topk_prob,  \
-        expert_counts, expert_offsets, tile_offsets, perm_token, perm_prob, route_pos);         \
+        partials, counter, streams, ffn_norm, w_router_folded, eps, n_experts, top_k, tile_m,   \
+        static_cast<__nv_bfloat16*>(m_bf), topk_idx, topk_prob, expert_counts, expert_offsets,  \
+        tile_offsets, perm_token, perm_prob, route_pos);                                        \
     if (st) return st;                                                                          \
   } while (0)
-#define LLMYB_OR_K(BMV, VM)                                                                     \
-  do {                                                                                          \
-    if (kch == 3) LLMYB_OR(BMV, 3, VM); else if (kch == 4) LLMYB_OR(BMV, 4, VM);                \
-    else LLMYB_OR(BMV, 8, VM);                                                                  \
-  } while (0)
-  if (vmax == 1) {
-    if (bm == 1) LLMYB_OR_K(1, 1); else if (bm == 4) LLMYB_OR_K(4, 1); else LLMYB_OR_K(8, 1);
+  if (bm == 1) {
+    if (kch == 3) LLMYB_OR(1, 3); else if (kch == 4) LLMYB_OR(1, 4); else LLMYB_OR(1, 8);
+  } else if (bm == 4) {
+    if (kch == 3) LLMYB_OR(4, 3); else if (kch == 4) LLMYB_OR(4, 4); else LLMYB_OR(4, 8);
   } else {
-    if (bm == 1) LLMYB_OR_K(1, 2); else if (bm == 4) LLMYB_OR_K(4, 2); else LLMYB_OR_K(8, 2);
+    if (kch == 3) LLMYB_OR(8, 3); else if (kch == 4) LLMYB_OR(8, 4); else LLMYB_OR(8, 8);
   }
-#undef LLMYB_OR_K
 #undef LLMYB_OR
   count_launch();
   return launch_status();

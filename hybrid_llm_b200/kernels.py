@@ -394,9 +394,9 @@ def add_rmsnorm_routed(streams: torch.Tensor, y_rows: torch.Tensor, plan: RouteP
 
 
 def decode_fused_supported(n: int, d: int, e: int, k: int, *k_ins: int) -> bool:
-    """Shapes the fused small-batch decode kernels take: up to 8 tokens, one
-    CTA for the router (N*E <= 64), D and every projection input width a
-    multiple of 8 and at most 2048."""
+    """Shapes the fused small-batch decode kernels take: up to 8 tokens and 64
+    (token, expert) pairs (the last CTA combines N*(2+E) partial sums), D and
+    every projection input width a multiple of 8 and at most 2048."""
     return (1 <= n <= 8 and n * e <= 64 and k <= 32 and d % 8 == 0 and d <= 2048
             and all(x % 8 == 0 and 0 < x <= 2048 for x in k_ins))
 
@@ -416,15 +416,23 @@ def decode_norm_gemv(streams_in: torch.Tensor, delta: torch.Tensor | None, plan:
                  _ptr(streams_out), _ptr(normed_out), _stream())
 
 
+def fold_router(w_router: torch.Tensor, ffn_norm: torch.Tensor,
+                router_norm: torch.Tensor) -> torch.Tensor:
+    """W_r * ffn_norm * router_norm (fp32 [E, D]): the router weights of
+    decode_out_router, whose two RMSNorms reduce to per-token scales."""
+    return (w_router.float() * ffn_norm.float()[None, :] * router_norm.float()[None, :]).contiguous()
+
+
 def decode_out_router(inp: torch.Tensor, w: torch.Tensor, streams: torch.Tensor,
-                      ffn_norm: torch.Tensor, router_norm: torch.Tensor, w_router: torch.Tensor,
-                      k: int, eps: float, m_bf: torch.Tensor, counter: torch.Tensor, *,
+                      ffn_norm: torch.Tensor, w_router_folded: torch.Tensor, k: int, eps: float,
+                      m_bf: torch.Tensor, counter: torch.Tensor, *,
                       conv_w: torch.Tensor | None = None, normed: torch.Tensor | None = None,
                       history: torch.Tensor | None = None, tile_m: int = TILE_M) -> RoutePlan:
     """[C] mixed = w . inp (+ the GDN conv gate with conv_w / normed / history,
     history rolled); streams += mixed; m_bf = RMSNorm_ffn(streams); routes and
-    plan as route_fused.  counter: int32 [1] zero word reused across calls."""
-    _require_cuda(inp, w, streams, ffn_norm, router_norm, w_router, m_bf, counter, conv_w, normed,
+    plan (fold_router weights).  counter: int32 [1] zero word reused across
+    calls."""
+    _require_cuda(inp, w, streams, ffn_norm, w_router_folded, m_bf, counter, conv_w, normed,
                   history)
     _rows(inp, "inp")
     _inplace(streams, "streams")
@@ -432,15 +440,15 @@ def decode_out_router(inp: torch.Tensor, w: torch.Tensor, streams: torch.Tensor,
     if history is not None:
         _inplace(history, "history")
     n, d = streams.shape
-    e = w_router.shape[0]
+    e = w_router_folded.shape[0]
     dev = streams.device
     idx = torch.empty(n, k, dtype=torch.int64, device=dev)
     prob = torch.empty(n, k, dtype=torch.float32, device=dev)
     b = _plan_buffers(n, e, k, dev, False)
-    mixed = torch.empty(n, d, dtype=torch.bfloat16, device=dev)
+    partials = torch.empty((d + 7) // 8 * n * (2 + e), dtype=torch.float32, device=dev)
     _native.call("llmyb_decode_out_router", _ptr(inp), inp.stride(0), inp.shape[1], _ptr(w), n, d,
-                 _ptr(conv_w), _ptr(normed), _ptr(history), _ptr(mixed), _ptr(counter),
-                 _ptr(streams), _ptr(ffn_norm), _ptr(router_norm), _ptr(w_router), float(eps), e, k,
+                 _ptr(conv_w), _ptr(normed), _ptr(history), _ptr(partials), _ptr(counter),
+                 _ptr(streams), _ptr(ffn_norm), _ptr(w_router_folded), float(eps), e, k,
                  int(tile_m), _ptr(m_bf), _ptr(idx), _ptr(prob), _ptr(b["counts"]),
                  _ptr(b["offsets"]), _ptr(b["tile_offsets"]), _ptr(b["perm_token"]),
                  _ptr(b["perm_prob"]), _ptr(b["route_pos"]), _stream())

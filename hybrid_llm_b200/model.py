@@ -304,8 +304,8 @@ class LoopedHybridModel:
                 kernels.decode_norm_gemv(cur, y_rows, plan, blk.mixer_norm, c.rms_eps, mix.w_in,
                                          proj, nxt, normed)
                 cur, nxt = nxt, cur
-                router = (cur, blk.ffn_norm, blk.moe.router_norm, blk.moe.router, c.moe_top_k,
-                          c.rms_eps, m_bf, self._counter)
+                router = (cur, blk.ffn_norm, blk.moe.router_folded, c.moe_top_k, c.rms_eps, m_bf,
+                          self._counter)
                 if isinstance(mix, GdnBlock):
                     q, k, v, gate, beta = self._gdn_views(proj, (bsz,))
                     o = kernels.gdn_step(q, k, v, gate, beta, state.gdn_states[key],

@@ -131,6 +131,7 @@ class MoeBlock:
     router: torch.Tensor       # [E, D] fp32
     w13: torch.Tensor          # [E, 2F, D] bf16 (interleaved gate/up)
     w2: torch.Tensor           # [E, D, F] bf16
+    router_folded: torch.Tensor | None = None  # [E, D] fp32 = router * ffn_norm * router_norm
 
 
 @dataclass
@@ -192,6 +193,8 @@ class ModelWeights:
                               for x in range(lo, hi)]).contiguous()
             moe = MoeBlock(router_norm=f32(p + "moe.router.norm.weight"),
                            router=f32(p + "moe.router.logits.weight"), w13=w13, w2=w2)
+            moe.router_folded = kernels.fold_router(moe.router, f32(p + "ffn_norm.weight"),
+                                                    moe.router_norm)
             blocks.append(Block(cfg.block_kind(j), f32(p + "mixer_norm.weight"),
                                 f32(p + "ffn_norm.weight"), mixer, moe))
         return cls(cfg=cfg, embed=bf("embed_tokens.weight"),

@@ -405,18 +405,22 @@ int32_t llmyb_decode_norm_gemv(const float* streams_in, const void* delta,
 
 /* llmyb_decode_out_router: mixed = w [D, k_in] . in [N, k_in] (bf16; with
  * conv_w the GDN decode conv gate of llmyb_gdn_conv_gate is applied per
- * column, normed = the block input, history rolled); then, by the last CTA
- * to finish, the work of llmyb_route_fused with delta = mixed: streams +=
- * mixed, m_bf, top-k and the plan.  mixed [N, D] bf16 is scratch; counter is
- * an int32 zero-initialised word the kernel leaves at zero.  N <= 8, N*E
- * small (one CTA routes), D <= 2048, k_in <= 2048. */
+ * column, normed = the block input, history rolled); streams += mixed; then
+ * the work of llmyb_route_fused: m_bf = RMSNorm_ffn(streams), logits of
+ * RMSNorm_router(m), top-k and the plan.  The two RMSNorms are per-token
+ * scales, so the router weights arrive folded: w_router_folded = W_r *
+ * ffn_norm * router_norm (fp32 [E, D], per layer); every CTA adds its
+ * columns' share of the sums of squares and logits to partials
+ * (ceil(D/8) * N * (2+E) fp32 scratch) and the last CTA to finish combines
+ * them in a fixed order.  counter: int32 zero word the kernel leaves at zero.
+ * N <= 8, N*k <= 64, D <= 2048, k_in <= 2048. */
 int32_t llmyb_decode_out_router(const void* in, int64_t in_ld, int32_t k_in, const void* w,
                                 int32_t n_tokens, int32_t d_model, const float* conv_w,
-                                const void* normed, void* history, void* mixed, int32_t* counter,
-                                float* streams, const float* ffn_norm, const float* router_norm,
-                                const float* w_router, float eps, int32_t n_experts, int32_t top_k,
-                                int32_t tile_m, void* m_bf, int64_t* topk_idx, float* topk_prob,
-                                int32_t* expert_counts, int32_t* expert_offsets,
+                                const void* normed, void* history, float* partials,
+                                int32_t* counter, float* streams, const float* ffn_norm,
+                                const float* w_router_folded, float eps, int32_t n_experts,
+                                int32_t top_k, int32_t tile_m, void* m_bf, int64_t* topk_idx,
+                                float* topk_prob, int32_t* expert_counts, int32_t* expert_offsets,
                                 int32_t* tile_offsets, int32_t* perm_token, float* perm_prob,
                                 int32_t* route_pos, void* stream);
 

@@ -164,8 +164,8 @@ def test_decode_out_router(cuda, gdn):
         hist0 = hist.clone()
         extra = dict(conv_w=conv, normed=normed, history=hist)
     s0 = streams.clone()
-    plan = kernels.decode_out_router(inp, w, streams, ffn, rn, wr, k, 1e-6, m_bf, counter,
-                                     tile_m=128, **extra)
+    plan = kernels.decode_out_router(inp, w, streams, ffn, kernels.fold_router(wr, ffn, rn), k,
+                                     1e-6, m_bf, counter, tile_m=128, **extra)
     torch.cuda.synchronize()
     y = (inp.float() @ w.float().t()).bfloat16().float()
     if gdn:
