@@ -718,38 +718,6 @@ bool aligned16(const void* p, int64_t stride) {
 
 using namespace llmyb;
 
-// Per-head banded attention: q,k [B*T, H*D] (token stride sq/sk), v with
-// v_heads in {1, H} heads of width D, out [B*T, H*D] (stride so).
-LLMYB_API int32_t llmyb_banded_attention(const void* q, int64_t q_stride, const void* k,
-                                         int64_t k_stride, const void* v, int64_t v_stride,
-                                         int32_t v_heads, int32_t batch, int32_t seq,
-                                         int32_t heads, int32_t head_dim, int32_t window,
-                                         float scale, void* out, int64_t out_stride,
-                                         void* stream) {
-  if (!q || !k || !v || !out || batch < 0 || seq < 0 || heads <= 0 || window <= 0)
-    return LLMYB_EINVAL;
-  if (v_heads != 1 && v_heads != heads) return LLMYB_EINVAL;
-  if (batch == 0 || seq == 0) return LLMYB_OK;
-  if (!aligned16(q, q_stride) || !aligned16(k, k_stride) || !aligned16(v, v_stride) ||
-      !aligned16(out, out_stride))
-    return LLMYB_EUNSUPPORTED;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  auto Q = static_cast<const __nv_bfloat16*>(q);
-  auto K = static_cast<const __nv_bfloat16*>(k);
-  auto V = static_cast<const __nv_bfloat16*>(v);
-  auto O = static_cast<__nv_bfloat16*>(out);
-  switch (head_dim) {
-    case 64:
-      return launch_band<64, false>(Q, q_stride, K, k_stride, V, v_stride, v_heads, batch, seq,
-                                    heads, window, scale, O, out_stride, nullptr, nullptr, s);
-    case 128:
-      return launch_band<128, false>(Q, q_stride, K, k_stride, V, v_stride, v_heads, batch, seq,
-                                     heads, window, scale, O, out_stride, nullptr, nullptr, s);
-    default:
-      return LLMYB_EUNSUPPORTED;
-  }
-}
-
 LLMYB_API int64_t llmyb_csa_prefill_scratch_bytes(int32_t batch, int32_t seq, int32_t heads) {
   if (batch < 0 || seq < 0 || heads <= 0) return -1;
   return static_cast<int64_t>(batch) * seq * heads * 2 * sizeof(float);

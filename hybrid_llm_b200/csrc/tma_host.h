@@ -40,6 +40,26 @@ inline bool make_bf16_2d_map(CUtensorMap* map, const void* base, uint64_t rows, 
   return r == CUDA_SUCCESS;
 }
 
+// Token-major bf16 tensor [batch][rows][cols] (row stride ld elements, batch
+// stride rows * ld) tiled into boxes of [1, box_rows, 64 cols] with the
+// 128-byte swizzle.  Rows past `rows` read as zeros, so a box never crosses
+// into the next batch entry.
+inline bool make_bf16_3d_map(CUtensorMap* map, const void* base, uint64_t batch, uint64_t rows,
+                             uint64_t cols, uint64_t ld, uint32_t box_rows) {
+  auto enc = tensor_map_encoder();
+  if (enc == nullptr) return false;
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0 || (ld * 2) % 16 != 0) return false;
+  cuuint64_t dims[3] = {cols, rows, batch};
+  cuuint64_t strides[2] = {ld * 2, rows * ld * 2};
+  cuuint32_t box[3] = {64, box_rows, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims,
+                   strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 inline int num_sms() {
   static int n = []() {
     int dev = 0, v = 0;

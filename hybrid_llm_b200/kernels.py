@@ -645,7 +645,8 @@ def banded_attention(q, k, v, window: int, scale: float | None = None, out=None)
         out = torch.empty(bsz, t, h, d, dtype=torch.bfloat16, device=q.device)
     scale = d ** -0.5 if scale is None else float(scale)
     _native.call("llmyb_banded_attention", qp, qs, kp, ks, vp, vs, v.shape[2], bsz, t, h, d,
-                 int(window), scale, _ptr(out), out.stride(1), _stream())
+                 int(window), scale, _ptr(out), out.stride(1), _ptr(device_status(q.device)),
+                 _stream())
     return out
 
 

@@ -324,11 +324,14 @@ int32_t llmyb_gdn_conv_gate(const void* x, const void* y_proj, const float* conv
  * j <= t and t - j < window.  Token-major bf16 tensors with token strides. */
 
 /* Per-head attention: q,k [B*T, H*D], v with v_heads in {1, H} heads of
- * width D, out [B*T, H*D]; D in {64, 128}; scale multiplies q.k. */
+ * width D, out [B*T, H*D]; D in {64, 128}; scale (> 0) multiplies q.k.  tcgen05
+ * kernel (128-query tiles, TMA-staged K/V, only in-band key blocks);
+ * dev_status (nullable) receives LLMYB_ETIMEOUT if a pipeline wait expires. */
 int32_t llmyb_banded_attention(const void* q, int64_t q_stride, const void* k, int64_t k_stride,
                                const void* v, int64_t v_stride, int32_t v_heads, int32_t batch,
                                int32_t seq, int32_t heads, int32_t head_dim, int32_t window,
-                               float scale, void* out, int64_t out_stride, void* stream);
+                               float scale, void* out, int64_t out_stride, int32_t* dev_status,
+                               void* stream);
 
 /* Scratch bytes needed by llmyb_csa_local_prefill (per-head row max / sum). */
 int64_t llmyb_csa_prefill_scratch_bytes(int32_t batch, int32_t seq, int32_t heads);

@@ -33,9 +33,38 @@ def test_banded_attention_matches_oracle(cuda, b, t, h, d, w, hv):
     q, k = _bf(rng.normal(size=(b, t, h, d))), _bf(rng.normal(size=(b, t, h, d)))
     v = _bf(rng.normal(size=(b, t, hv, d)))
     out = kernels.banded_attention(q.cuda(), k.cuda(), v.cuda(), w)
-    torch.cuda.synchronize()
+    kernels.check_device_status()
     ref = attention.banded_attention(_f(q), _f(k), _f(v), w)
     assert _rel(_f(out), ref) < REL
+
+
+def _torch_band(q, k, v, w):
+    """fp32 dense-masked softmax attention on the GPU: q,k [B,T,H,D], v [B,T,H|1,D]."""
+    qf, kf, vf = (x.float().transpose(1, 2) for x in (q, k, v))
+    t = q.shape[1]
+    i = torch.arange(t, device=q.device)
+    vis = (i[None, :] <= i[:, None]) & (i[:, None] - i[None, :] < w)
+    s = (qf @ kf.transpose(-1, -2)) * q.shape[-1] ** -0.5
+    s = s.masked_fill(~vis, float("-inf"))
+    return (torch.softmax(s, -1) @ vf).transpose(1, 2)
+
+
+@pytest.mark.parametrize("b,t,h,d,w,hv", [(4, 2048, 8, 64, 700, 1), (3, 1500, 8, 128, 256, 8),
+                                          (2, 1024, 20, 128, 128, 20), (1, 4096, 2, 128, 4096, 2)])
+def test_banded_attention_many_units_per_cta(cuda, b, t, h, d, w, hv):
+    """More (row, head, query-tile) units than SMs: the persistent loop, the
+    double-buffered Q tiles and the running-max rescale across units."""
+    from hybrid_llm_b200 import kernels
+    g = torch.Generator(device="cuda").manual_seed(t + w)
+    q, k = (torch.randn(b, t, h, d, device="cuda", generator=g).bfloat16() for _ in range(2))
+    v = torch.randn(b, t, hv, d, device="cuda", generator=g).bfloat16()
+    # a few large scores so that the running max moves by more than 2^8 mid-band
+    q[:, ::97] *= 6
+    out = kernels.banded_attention(q, k, v, w)
+    kernels.check_device_status()
+    ref = _torch_band(q, k, v, w)
+    err = (out.float() - ref).abs().max().item() / ref.abs().max().item()
+    assert err < REL, err
 
 
 @pytest.mark.parametrize("tag", list(inputs.BAND_CASES))
@@ -59,7 +88,7 @@ def test_banded_attention_long_context_full_size(cuda):
     g = torch.Generator(device="cuda").manual_seed(0)
     q, k, v = (torch.randn(b, t, h, d, device="cuda", generator=g).bfloat16() for _ in range(3))
     out = kernels.banded_attention(q, k, v, w)
-    torch.cuda.synchronize()
+    kernels.check_device_status()
     rows = np.array([0, 1, 63, 64, 1023, 1024, 1025, 4000, 8191])
     for bi, hi in [(0, 0), (7, 15)]:
         qq = _f(q[bi, rows, hi])
