@@ -35,6 +35,7 @@ namespace llmyb {
 namespace {
 
 constexpr int kC = 64;  // chunk length
+constexpr float kLog2e = 1.4426950408889634f;
 
 // ------------------------------------------------------------- activation
 // In place on the fused projection [N, width] = [q | k | v | gate | beta]:
@@ -190,8 +191,12 @@ struct PrepSmem {
   alignas(16) uint8_t qrv[QRV];
   alignas(16) uint8_t at[AT];
   float Tm[kC * LF];  // T = (I + A)^-1
-  float g[kC], gprev[kC], beta[kC];
+  // per token: inclusive / exclusive cumulative log2-decay, beta, segment, and
+  // the T2 column scale beta * Gamma_{t-1} (0 past a reset)
+  float g[kC], gprev[kC], beta[kC], s2[kC];
   int seg[kC];
+  float wsum[2];
+  int wseg[2];
 };
 
 template <int KD, int VD>
@@ -225,24 +230,48 @@ __global__ void __launch_bounds__(128) gdn_chunk_prep_kernel(GdnIO io, int B, in
     mma::cp_async16(&sQ[r * SM::LK + cc], io.q + tok * io.sq + h * KD + cc, ok);
   }
   mma::cp_async_commit();
-  if (tid == 0) {
-    float g = 0.f;
-    int seg = 0;
-    for (int t = 0; t < kC; ++t) {
-      float la = 0.f, bt = 0.f;
-      if (t < n) {
-        const int64_t tok = tok0 + t;
-        la = io.log_alpha != nullptr ? io.log_alpha[tok * H + h]
-                                     : logf(sigmoidf_(io.decay_logit[h]));
-        bt = bf2f(io.beta[tok * io.sb + h]);
-        if (io.reset != nullptr && io.reset[tok] != 0) seg += 1;
-      }
-      sm.gprev[t] = g;
-      g += la;
-      sm.g[t] = g;
-      sm.beta[t] = bt;
-      sm.seg[t] = seg;
+  // per-token scalars, one thread per token; cumulative sums by warp scans
+  // (decays in log2 units, so every Gamma ratio below is one exp2)
+  float la = 0.f, la_own = 0.f, bt = 0.f;
+  int rs = 0;
+  if (tid < kC) {
+    const int t = tid;
+    if (t < n) {
+      const int64_t tok = tok0 + t;
+      la = (io.log_alpha != nullptr ? io.log_alpha[tok * H + h]
+                                    : logf(sigmoidf_(io.decay_logit[h]))) * kLog2e;
+      bt = bf2f(io.beta[tok * io.sb + h]);
+      rs = (io.reset != nullptr && io.reset[tok] != 0) ? 1 : 0;
     }
+    la_own = la;
+    float gs = la;
+    int ss = rs;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float gu = __shfl_up_sync(0xffffffffu, gs, o);
+      const int su = __shfl_up_sync(0xffffffffu, ss, o);
+      if (lane >= o) {
+        gs += gu;
+        ss += su;
+      }
+    }
+    if (lane == 31) {
+      sm.wsum[warp] = gs;
+      sm.wseg[warp] = ss;
+    }
+    la = gs;  // inclusive within the warp
+    rs = ss;
+  }
+  __syncthreads();
+  if (tid < kC) {
+    const int t = tid;
+    const float g = la + (warp == 1 ? sm.wsum[0] : 0.f);
+    const int seg = rs + (warp == 1 ? sm.wseg[0] : 0);
+    sm.g[t] = g;
+    sm.gprev[t] = g - la_own;
+    sm.beta[t] = bt;
+    sm.seg[t] = seg;
+    sm.s2[t] = seg == 0 ? bt * fast_exp2(g - la_own) : 0.f;
   }
   mma::cp_async_wait<0>();
   __syncthreads();
@@ -285,10 +314,12 @@ __global__ void __launch_bounds__(128) gdn_chunk_prep_kernel(GdnIO io, int B, in
           const int ii = i + u;
           const bool same = sm.seg[t] == sm.seg[ii];
           sA[t * SM::LF + ii] =
-              (ii < t && same) ? sm.beta[t] * expf(sm.gprev[t] - sm.g[ii]) * kk[nb][half * 2 + u]
-                               : 0.f;
-          mv[u] = (ii <= t && same && t < n) ? expf(sm.g[t] - sm.g[ii]) * qk[nb][half * 2 + u]
-                                             : 0.f;
+              (ii < t && same)
+                  ? sm.beta[t] * fast_exp2(sm.gprev[t] - sm.g[ii]) * kk[nb][half * 2 + u]
+                  : 0.f;
+          mv[u] = (ii <= t && same && t < n)
+                      ? fast_exp2(sm.g[t] - sm.g[ii]) * qk[nb][half * 2 + u]
+                      : 0.f;
         }
         *reinterpret_cast<uint32_t*>(aqk_out + t * kC + i) = pack_bf16x2(mv[0], mv[1]);
       }
@@ -300,13 +331,18 @@ __global__ void __launch_bounds__(128) gdn_chunk_prep_kernel(GdnIO io, int B, in
   // substitution (one thread per column), then off-diagonal blocks
   // T_ij = -T_ii * sum_{k=j}^{i-1} A_ik T_kj, block row by block row.
   if (tid < 64) {
+    // column j of diagonal block blk in registers (zero above the diagonal)
     const int blk = tid >> 4, j = tid & 15, base = blk * 16;
+    float col[16];
+#pragma unroll
     for (int t = 0; t < 16; ++t) {
       float acc = (t == j) ? 1.f : 0.f;
-      for (int i = 0; i < t; ++i)
-        acc -= sA[(base + t) * SM::LF + base + i] * sm.Tm[(base + i) * SM::LF + base + j];
-      sm.Tm[(base + t) * SM::LF + base + j] = acc;
+#pragma unroll
+      for (int i = 0; i < t; ++i) acc -= sA[(base + t) * SM::LF + base + i] * col[i];
+      col[t] = acc;
     }
+#pragma unroll
+    for (int t = 0; t < 16; ++t) sm.Tm[(base + t) * SM::LF + base + j] = col[t];
   }
   for (int i = tid; i < kC * kC; i += 128) {
     const int r = i / kC, cc = i % kC;
@@ -314,21 +350,28 @@ __global__ void __launch_bounds__(128) gdn_chunk_prep_kernel(GdnIO io, int B, in
   }
   __syncthreads();
   for (int bi = 1; bi < 4; ++bi) {
+    // R = A[bi, <bi] T[<bi, <bi], then T[bi, <bi] = -T[bi, bi] R (16-wide
+    // unrolled dot products, four partial sums each)
     for (int idx = tid; idx < 16 * 16 * bi; idx += 128) {
       const int r = bi * 16 + idx / (16 * bi);
       const int cc = idx % (16 * bi);
-      float acc = 0.f;
-      for (int kq = (cc >> 4) * 16; kq < bi * 16; ++kq)
-        acc += sA[r * SM::LF + kq] * sm.Tm[kq * SM::LF + cc];
-      sR[r * SM::LF + cc] = acc;
+      float a4[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int kb = cc >> 4; kb < bi; ++kb) {
+#pragma unroll
+        for (int k = 0; k < 16; ++k)
+          a4[k & 3] += sA[r * SM::LF + kb * 16 + k] * sm.Tm[(kb * 16 + k) * SM::LF + cc];
+      }
+      sR[r * SM::LF + cc] = (a4[0] + a4[1]) + (a4[2] + a4[3]);
     }
     __syncthreads();
     for (int idx = tid; idx < 16 * 16 * bi; idx += 128) {
       const int r = bi * 16 + idx / (16 * bi);
       const int cc = idx % (16 * bi);
-      float acc = 0.f;
-      for (int kq = bi * 16; kq <= r; ++kq) acc += sm.Tm[r * SM::LF + kq] * sR[kq * SM::LF + cc];
-      sm.Tm[r * SM::LF + cc] = -acc;
+      float a4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int k = 0; k < 16; ++k)
+        a4[k & 3] += sm.Tm[r * SM::LF + bi * 16 + k] * sR[(bi * 16 + k) * SM::LF + cc];
+      sm.Tm[r * SM::LF + cc] = -((a4[0] + a4[1]) + (a4[2] + a4[3]));
     }
     __syncthreads();
   }
@@ -344,17 +387,17 @@ __global__ void __launch_bounds__(128) gdn_chunk_prep_kernel(GdnIO io, int B, in
     const int r = i / kC, cc = i % kC;
     const float tv = sm.Tm[r * SM::LF + cc];
     sT1[r * SM::LT + cc] = f2bf(tv * sm.beta[cc]);
-    const float s2 = sm.seg[cc] == 0 ? sm.beta[cc] * expf(sm.gprev[cc]) : 0.f;
-    sT2[r * SM::LT + cc] = f2bf(tv * s2);
+    sT2[r * SM::LT + cc] = f2bf(tv * sm.s2[cc]);
   }
   if (tid < kC) {
     const int t = tid;
     const int last = n - 1;
     if (t < n) {
-      po.qscale[bh * T + t0 + t] = sm.seg[t] == 0 ? expf(sm.g[t]) : 0.f;
-      po.kscale[bh * T + t0 + t] = sm.seg[t] == sm.seg[last] ? expf(sm.g[last] - sm.g[t]) : 0.f;
+      po.qscale[bh * T + t0 + t] = sm.seg[t] == 0 ? fast_exp2(sm.g[t]) : 0.f;
+      po.kscale[bh * T + t0 + t] =
+          sm.seg[t] == sm.seg[last] ? fast_exp2(sm.g[last] - sm.g[t]) : 0.f;
     }
-    if (t == 0) po.sdecay[bh * nC + c] = sm.seg[last] == 0 ? expf(sm.g[last]) : 0.f;
+    if (t == 0) po.sdecay[bh * nC + c] = sm.seg[last] == 0 ? fast_exp2(sm.g[last]) : 0.f;
   }
   mma::cp_async_wait<0>();
   __syncthreads();
