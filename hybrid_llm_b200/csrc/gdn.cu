@@ -457,7 +457,9 @@ __global__ void __launch_bounds__(128) gdn_chunk_prep_kernel(GdnIO io, int B, in
 }
 
 // ----------------------------------------------------------- chunk scan
-// Per (row, head, VC-wide value slice).  The chunk operands (Kw, Q, K, Aqk,
+// Per (row, head, NG*VC-wide value slice): NG groups of four warps, each
+// group owning VC value columns, share the chunk operands (Kw, Q, K, Aqk),
+// which are loaded once per CTA.  The chunk operands (Kw, Q, K, Aqk,
 // U and gate slices, per-token scales) are double-buffered with cp.async so
 // that chunk c+1 streams in while chunk c runs its four small matmuls.
 template <int KD, int VC>
@@ -469,7 +471,6 @@ struct ScanSmem {
     __nv_bfloat16 K[kC * LK];
     __nv_bfloat16 Aqk[kC * LT];
     __nv_bfloat16 U[kC * LVC];
-    __nv_bfloat16 G[kC * LVC];
     float qs[kC], ks[kC];
     float sd, pad[3];
   };
@@ -487,7 +488,7 @@ __device__ __forceinline__ void split_store(__nv_bfloat16* hi, __nv_bfloat16* lo
   *reinterpret_cast<__nv_bfloat162*>(lo + idx) = __floats2bfloat162_rn(x0 - hf.x, x1 - hf.y);
 }
 
-template <int KD, int VD, int VC>
+template <int KD, int VD, int VC, int NT>
 __device__ __forceinline__ void scan_issue_chunk(typename ScanSmem<KD, VC>::Stage& sg,
                                                  const GdnIO& io, const PrepOut& po, int b, int h,
                                                  int H, int T, int nC, int c, int v0, int tid) {
@@ -496,7 +497,7 @@ __device__ __forceinline__ void scan_issue_chunk(typename ScanSmem<KD, VC>::Stag
   const int n = min(kC, T - t0);
   const int64_t tok0 = static_cast<int64_t>(b) * T + t0;
   const int64_t bh = static_cast<int64_t>(b) * H + h;
-  for (int i = tid; i < kC * (KD / 8); i += 128) {
+  for (int i = tid; i < kC * (KD / 8); i += NT) {
     const int r = i / (KD / 8), cc = (i % (KD / 8)) * 8;
     const bool ok = r < n;
     const int64_t tok = tok0 + (ok ? r : 0);
@@ -505,16 +506,15 @@ __device__ __forceinline__ void scan_issue_chunk(typename ScanSmem<KD, VC>::Stag
     mma::cp_async16(&sg.K[r * SM::LK + cc], io.k + tok * io.sk + h * KD + cc, ok);
   }
   const __nv_bfloat16* aq = po.Aqk + (bh * nC + c) * kC * kC;
-  for (int i = tid; i < kC * (kC / 8); i += 128) {
+  for (int i = tid; i < kC * (kC / 8); i += NT) {
     const int r = i / (kC / 8), cc = (i % (kC / 8)) * 8;
     mma::cp_async16(&sg.Aqk[r * SM::LT + cc], aq + r * kC + cc, true);
   }
-  for (int i = tid; i < kC * (VC / 8); i += 128) {
+  for (int i = tid; i < kC * (VC / 8); i += NT) {
     const int r = i / (VC / 8), cc = (i % (VC / 8)) * 8;
     const bool ok = r < n;
     const int64_t tok = tok0 + (ok ? r : 0);
     mma::cp_async16(&sg.U[r * SM::LVC + cc], po.U + (tok * H + h) * VD + v0 + cc, ok);
-    mma::cp_async16(&sg.G[r * SM::LVC + cc], io.gate + tok * io.sg + h * VD + v0 + cc, ok);
   }
   if (tid < kC) {
     sg.qs[tid] = tid < n ? po.qscale[bh * T + t0 + tid] : 0.f;
@@ -523,30 +523,35 @@ __device__ __forceinline__ void scan_issue_chunk(typename ScanSmem<KD, VC>::Stag
   if (tid == 0) sg.sd = po.sdecay[bh * nC + c];
 }
 
-template <int KD, int VD, int VC>
-__global__ void __launch_bounds__(128) gdn_chunk_scan_kernel(GdnIO io, int B, int T, int H,
-                                                             PrepOut po, float* __restrict__ state,
-                                                             __nv_bfloat16* __restrict__ out,
-                                                             int64_t so) {
-  using SM = ScanSmem<KD, VC>;
-  constexpr int NB = VC / 8;        // n-blocks of the value slice
+template <int KD, int VD, int VC, int NG>
+__global__ void __launch_bounds__(128 * NG) gdn_chunk_scan_kernel(GdnIO io, int B, int T, int H,
+                                                                  PrepOut po,
+                                                                  float* __restrict__ state,
+                                                                  __nv_bfloat16* __restrict__ out,
+                                                                  int64_t so) {
+  constexpr int VS = NG * VC;       // value columns of the CTA
+  constexpr int NT = 128 * NG;
+  using SM = ScanSmem<KD, VS>;
+  constexpr int NB = VC / 8;        // n-blocks of a group's value slice
   constexpr int MT = KD / 64;       // 16-row state tiles per warp (KD/4 rows per warp)
   extern __shared__ uint8_t smem_raw[];
   SM& sm = *reinterpret_cast<SM*>(smem_raw);
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int nvs = VD / VC;
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int warp = (tid >> 5) & 3;  // warp within its group
+  const int cb = (tid >> 7) * VC;   // the group's first column within the CTA slice
+  const int nvs = VD / VS;
   const int vs = blockIdx.x % nvs;
   const int h = (blockIdx.x / nvs) % H;
   const int b = blockIdx.x / (nvs * H);
-  const int v0 = vs * VC;
+  const int v0 = vs * VS;
   const int nC = static_cast<int>(ceil_div(T, kC));
   const int r_lo = lane >> 2, cq = (lane & 3) * 2;
 
-  scan_issue_chunk<KD, VD, VC>(sm.st[0], io, po, b, h, H, T, nC, 0, v0, tid);
+  scan_issue_chunk<KD, VD, VS, NT>(sm.st[0], io, po, b, h, H, T, nC, 0, v0, tid);
   mma::cp_async_commit();
 
   // ---- state rows [warp*KD/4, +KD/4) x VC columns in accumulator layout
-  float* Sg = state + (static_cast<int64_t>(b) * H + h) * KD * VD + v0;
+  float* Sg = state + (static_cast<int64_t>(b) * H + h) * KD * VD + v0 + cb;
   float sacc[MT][NB][4];
 #pragma unroll
   for (int mt = 0; mt < MT; ++mt)
@@ -565,9 +570,20 @@ __global__ void __launch_bounds__(128) gdn_chunk_scan_kernel(GdnIO io, int B, in
     const int n = min(kC, T - t0);
     const int64_t tok0 = static_cast<int64_t>(b) * T + t0;
     if (c + 1 < nC) {
-      scan_issue_chunk<KD, VD, VC>(sm.st[(c + 1) & 1], io, po, b, h, H, T, nC, c + 1, v0, tid);
+      scan_issue_chunk<KD, VD, VS, NT>(sm.st[(c + 1) & 1], io, po, b, h, H, T, nC, c + 1, v0, tid);
       mma::cp_async_commit();
     }
+    // this thread's gate values of the chunk (used by the output phase)
+    uint32_t gv[NB][2];
+#pragma unroll
+    for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        const int t = warp * 16 + r_lo + half * 8;
+        gv[nb][half] = t < n ? __ldg(reinterpret_cast<const unsigned int*>(
+                                   io.gate + (tok0 + t) * io.sg + h * VD + v0 + cb + nb * 8 + cq))
+                             : 0u;
+      }
     // ---- publish S (hi/lo) for this chunk's products
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt)
@@ -576,7 +592,7 @@ __global__ void __launch_bounds__(128) gdn_chunk_scan_kernel(GdnIO io, int B, in
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
           const int kr = warp * (KD / 4) + mt * 16 + r_lo + half * 8;
-          split_store(sm.Sh, sm.Sl, kr * SM::LVC + nb * 8 + cq, sacc[mt][nb][half * 2],
+          split_store(sm.Sh, sm.Sl, kr * SM::LVC + cb + nb * 8 + cq, sacc[mt][nb][half * 2],
                       sacc[mt][nb][half * 2 + 1]);
         }
     if (c + 1 < nC) mma::cp_async_wait<1>(); else mma::cp_async_wait<0>();
@@ -596,8 +612,8 @@ __global__ void __launch_bounds__(128) gdn_chunk_scan_kernel(GdnIO io, int B, in
 #pragma unroll
       for (int nb = 0; nb < NB; nb += 2) {
         uint32_t bh[4], bl[4];
-        mma::load_b_kn(bh, sm.Sh, SM::LVC, kk, nb * 8);
-        mma::load_b_kn(bl, sm.Sl, SM::LVC, kk, nb * 8);
+        mma::load_b_kn(bh, sm.Sh, SM::LVC, kk, cb + nb * 8);
+        mma::load_b_kn(bl, sm.Sl, SM::LVC, kk, cb + nb * 8);
         mma::mma_bf16(w[nb], akw, bh[0], bh[1]);
         mma::mma_bf16(w[nb + 1], akw, bh[2], bh[3]);
         mma::mma_bf16(w[nb], akw, bl[0], bl[1]);
@@ -613,7 +629,7 @@ __global__ void __launch_bounds__(128) gdn_chunk_scan_kernel(GdnIO io, int B, in
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
         const int t = warp * 16 + r_lo + half * 8;
-        const int col = nb * 8 + cq;
+        const int col = cb + nb * 8 + cq;
         const float2 u = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(&sg.U[t * SM::LVC + col]));
         const float w0 = u.x - w[nb][half * 2];
         const float w1 = u.y - w[nb][half * 2 + 1];
@@ -637,8 +653,8 @@ __global__ void __launch_bounds__(128) gdn_chunk_scan_kernel(GdnIO io, int B, in
 #pragma unroll
       for (int nb = 0; nb < NB; nb += 2) {
         uint32_t bh[4], bl[4];
-        mma::load_b_kn(bh, sm.Wh, SM::LVC, kk, nb * 8);
-        mma::load_b_kn(bl, sm.Wl, SM::LVC, kk, nb * 8);
+        mma::load_b_kn(bh, sm.Wh, SM::LVC, kk, cb + nb * 8);
+        mma::load_b_kn(bl, sm.Wl, SM::LVC, kk, cb + nb * 8);
         mma::mma_bf16(o[nb], aa, bh[0], bh[1]);
         mma::mma_bf16(o[nb + 1], aa, bh[2], bh[3]);
         mma::mma_bf16(o[nb], aa, bl[0], bl[1]);
@@ -651,11 +667,10 @@ __global__ void __launch_bounds__(128) gdn_chunk_scan_kernel(GdnIO io, int B, in
       for (int half = 0; half < 2; ++half) {
         const int t = warp * 16 + r_lo + half * 8;
         if (t < n) {
-          const int col = nb * 8 + cq;
+          const int col = cb + nb * 8 + cq;
           const float o0 = sg.qs[t] * qsacc[nb][half * 2] + o[nb][half * 2];
           const float o1 = sg.qs[t] * qsacc[nb][half * 2 + 1] + o[nb][half * 2 + 1];
-          const float2 gt =
-              unpack_bf16x2(*reinterpret_cast<const uint32_t*>(&sg.G[t * SM::LVC + col]));
+          const float2 gt = unpack_bf16x2(gv[nb][half]);
           // reference order: out.to(hidden dtype) * gate
           *reinterpret_cast<uint32_t*>(out + (tok0 + t) * so + h * VD + v0 + col) =
               pack_bf16x2(bf2f(f2bf(o0)) * gt.x, bf2f(f2bf(o1)) * gt.y);
@@ -679,8 +694,8 @@ __global__ void __launch_bounds__(128) gdn_chunk_scan_kernel(GdnIO io, int B, in
 #pragma unroll
         for (int nb = 0; nb < NB; nb += 2) {
           uint32_t bh[4], bl[4];
-          mma::load_b_kn(bh, sm.Xh, SM::LVC, kk, nb * 8);
-          mma::load_b_kn(bl, sm.Xl, SM::LVC, kk, nb * 8);
+          mma::load_b_kn(bh, sm.Xh, SM::LVC, kk, cb + nb * 8);
+          mma::load_b_kn(bl, sm.Xl, SM::LVC, kk, cb + nb * 8);
           mma::mma_bf16(sacc[mt][nb], ak, bh[0], bh[1]);
           mma::mma_bf16(sacc[mt][nb + 1], ak, bh[2], bh[3]);
           mma::mma_bf16(sacc[mt][nb], ak, bl[0], bl[1]);
@@ -849,20 +864,20 @@ int32_t launch_prefill(const GdnIO& io, int B, int T, int H, void* scratch, floa
   po.sdecay = reinterpret_cast<float*>(base + L.sd);
   const int nC = static_cast<int>(ceil_div(T, kC));
   constexpr int kPrepSmem = sizeof(PrepSmem<KD, VD>);
-  constexpr int VC = 32;
-  constexpr int kScanSmem = sizeof(ScanSmem<KD, VC>);
+  constexpr int VC = 32, NG = 2;  // two 32-column groups per CTA
+  constexpr int kScanSmem = sizeof(ScanSmem<KD, VC * NG>);
   static bool attrs = false;
   if (!attrs) {
     int32_t st = set_smem(gdn_chunk_prep_kernel<KD, VD>, kPrepSmem);
     if (st) return st;
-    st = set_smem(gdn_chunk_scan_kernel<KD, VD, VC>, kScanSmem);
+    st = set_smem(gdn_chunk_scan_kernel<KD, VD, VC, NG>, kScanSmem);
     if (st) return st;
     attrs = true;
   }
   gdn_chunk_prep_kernel<KD, VD><<<B * H * nC, 128, kPrepSmem, s>>>(io, B, T, H, po);
   count_launch();
-  gdn_chunk_scan_kernel<KD, VD, VC><<<B * H * (VD / VC), 128, kScanSmem, s>>>(io, B, T, H, po,
-                                                                             state, out, so);
+  gdn_chunk_scan_kernel<KD, VD, VC, NG><<<B * H * (VD / (VC * NG)), 128 * NG, kScanSmem, s>>>(
+      io, B, T, H, po, state, out, so);
   count_launch();
   return launch_status();
 }
