@@ -23,10 +23,14 @@
 // runs the routines of router.cu, so both give the values of the unfused path
 // for the same inputs; the projections are warp-per-row GEMVs (fp32 sums of
 // bf16 products, bf16 outputs like the cuBLAS GEMMs they replace).
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 #include "router_device.cuh"
 
 #include <algorithm>
+
+namespace cg = cooperative_groups;
 
 namespace llmyb {
 namespace {
@@ -330,6 +334,173 @@ __global__ void __launch_bounds__(256) decode_out_router_kernel(
   if (threadIdx.x == 0) *counter = 0;  // ready for the next launch
 }
 
+// [C] as one cluster of 8 CTAs x 16 warps (residual widths D = 128 * RPW):
+// the same per-column work, but every warp holds RPW weight rows in
+// registers (loaded before the dependency wait, together with this CTA's
+// slice of the folded router weights, the FFN norm weights, the conv taps
+// and the residual rows), the CTAs' shares of the sums are combined through
+// distributed shared memory in rank order (no global partials, fences or
+// atomics), and every CTA writes m_bf for its own columns; CTA 0 routes.
+constexpr int kOrCtas = 8, kOrWarps = 16;
+
+template <int BM, int KCH, int RPW>
+__global__ void __cluster_dims__(kOrCtas, 1, 1) __launch_bounds__(kOrWarps * 32, 1)
+    decode_out_router_cluster_kernel(
+        const __nv_bfloat16* __restrict__ in, int64_t in_ld, int K,
+        const __nv_bfloat16* __restrict__ W, int B, int D, const float* __restrict__ conv_w,
+        const __nv_bfloat16* __restrict__ normed, __nv_bfloat16* history,
+        float* __restrict__ streams, const float* __restrict__ ffn_w,
+        const float* __restrict__ w_fold, float eps, int E, int top_k, int tile_m,
+        __nv_bfloat16* __restrict__ m_bf, int64_t* __restrict__ topk_idx,
+        float* __restrict__ topk_prob, int* __restrict__ counts, int* __restrict__ offsets,
+        int* __restrict__ tile_offsets, int* __restrict__ perm_token,
+        float* __restrict__ perm_prob, int* __restrict__ route_pos) {
+  constexpr int kCols = kOrWarps * RPW;  // residual columns of this CTA
+  constexpr int kThreads = kOrWarps * 32;
+  constexpr int kMaxNV = 2 + 64;         // B * E <= 64 on this path
+  // dynamic: s_in [B][K] bf16 | s_wf [E][kCols] fp32
+  extern __shared__ __align__(16) uint8_t smem_c[];
+  __shared__ float s_x[kMaxTokens][kCols];      // updated residual (this CTA's columns)
+  __shared__ float s_res[kMaxTokens][kCols];    // residual before the update
+  __shared__ float s_tap[kMaxTokens][4][kCols]; // conv taps: history 0..2, normed
+  __shared__ float s_conv[kCols][4];
+  __shared__ float s_ffn[kCols];
+  __shared__ float s_part[kMaxTokens * kMaxNV];  // this CTA's shares, read by the peers
+  __shared__ float s_tot[kMaxTokens * kMaxNV];
+  __shared__ float s_logits[64];
+  __shared__ float s_scale[kMaxTokens][2];
+  __shared__ int s_idx[kMaxTokens * kMaxTopK];
+  __shared__ float s_prob[kMaxTokens * kMaxTopK];
+  __shared__ int s_cnt[kMaxExperts];
+  cg::cluster_group cluster = cg::this_cluster();
+  const int cta = static_cast<int>(cluster.block_rank());
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int c0 = cta * kCols;
+  const int NV = 2 + E;
+  __nv_bfloat16* s_in = reinterpret_cast<__nv_bfloat16*>(smem_c);
+  float* s_wf = reinterpret_cast<float*>(smem_c + ((B * K * 2 + 15) & ~15));
+
+  // ---- before the dependency wait: weights, and buffers written two or more
+  // launches earlier (the residual and the normalised input by [A], history)
+  uint4 w[RPW][KCH];
+#pragma unroll
+  for (int r = 0; r < RPW; ++r)
+    warp_load_row<KCH>(W + static_cast<int64_t>(c0 + warp * RPW + r) * K, K, lane, w[r]);
+  for (int i = threadIdx.x; i < E * kCols; i += kThreads) {
+    const int e = i / kCols, c = i - e * kCols;
+    s_wf[i] = __ldg(w_fold + static_cast<int64_t>(e) * D + c0 + c);
+  }
+  for (int c = threadIdx.x; c < kCols; c += kThreads) {
+    s_ffn[c] = __ldg(ffn_w + c0 + c);
+    if (conv_w != nullptr)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) s_conv[c][j] = __ldg(conv_w + (c0 + c) * 4 + j);
+  }
+  for (int i = threadIdx.x; i < B * kCols; i += kThreads) {
+    const int b = i / kCols, c = i - b * kCols;
+    const int64_t o = static_cast<int64_t>(b) * D + c0 + c;
+    s_res[b][c] = streams[o];
+    if (conv_w != nullptr) {
+      const __nv_bfloat16* hb = history + static_cast<int64_t>(b) * 3 * D + c0 + c;
+      s_tap[b][0][c] = bf2f(hb[0]);
+      s_tap[b][1][c] = bf2f(hb[D]);
+      s_tap[b][2][c] = bf2f(hb[2 * D]);
+      s_tap[b][3][c] = bf2f(normed[o]);
+    }
+  }
+  pdl_wait();  // the projection input comes from the mixer kernel
+  pdl_trigger();
+  for (int i = threadIdx.x; i < B * (K >> 3); i += kThreads) {
+    const int b = i / (K >> 3), c = i - b * (K >> 3);
+    reinterpret_cast<uint4*>(s_in + b * K)[c] =
+        __ldg(reinterpret_cast<const uint4*>(in + b * in_ld) + c);
+  }
+  __syncthreads();
+  // ---- output projection rows (+ conv gate) and the residual update
+#pragma unroll
+  for (int r = 0; r < RPW; ++r) {
+    const int c = warp * RPW + r, n = c0 + c;
+    float acc[BM];
+    warp_row_dot<BM, KCH>(w[r], K, B, s_in, lane, acc);
+    if (lane < B) {
+      float y = 0.f;
+#pragma unroll
+      for (int b = 0; b < BM; ++b)
+        if (b == lane) y = acc[b];
+      const int b = lane;
+      float yv = bf2f(f2bf(y));  // the projection output is bf16
+      if (conv_w != nullptr) {
+        float cacc = 0.f;
+        cacc += s_conv[c][0] * s_tap[b][0][c];
+        cacc += s_conv[c][1] * s_tap[b][1][c];
+        cacc += s_conv[c][2] * s_tap[b][2][c];
+        cacc += s_conv[c][3] * s_tap[b][3][c];
+        yv = yv * sigmoidf_(cacc);
+        __nv_bfloat16* hb = history + static_cast<int64_t>(b) * 3 * D + n;
+        hb[0] = f2bf(s_tap[b][1][c]);
+        hb[D] = f2bf(s_tap[b][2][c]);
+        hb[2 * D] = f2bf(s_tap[b][3][c]);
+      }
+      const float x = s_res[b][c] + bf2f(f2bf(yv));
+      streams[static_cast<int64_t>(b) * D + n] = x;
+      s_x[b][c] = x;
+    }
+  }
+  __syncthreads();
+  // ---- this CTA's shares: one warp per (token, value), lanes over columns
+  for (int t = warp; t < B * NV; t += kOrWarps) {
+    const int b = t / NV, j = t - b * NV;
+    float acc = 0.f;
+    for (int c = lane; c < kCols; c += 32) {
+      const float x = s_x[b][c];
+      if (j == 0) {
+        acc += x * x;
+      } else if (j == 1) {
+        const float xf = x * s_ffn[c];
+        acc += xf * xf;
+      } else {
+        acc += s_wf[(j - 2) * kCols + c] * x;
+      }
+    }
+    acc = warp_sum(acc);
+    if (lane == 0) s_part[t] = acc;
+  }
+  cluster.sync();
+  // ---- every CTA sums the shares in rank order (the same totals everywhere)
+  for (int t = threadIdx.x; t < B * NV; t += kThreads) {
+    float acc = 0.f;
+    for (int q = 0; q < kOrCtas; ++q) acc += cluster.map_shared_rank(s_part, q)[t];
+    s_tot[t] = acc;
+  }
+  __syncthreads();
+  if (threadIdx.x < B) {
+    const int b = threadIdx.x;
+    const float inv1 = rsqrtf(s_tot[b * NV] / static_cast<float>(D) + eps);
+    const float inv2 = rsqrtf(inv1 * inv1 * s_tot[b * NV + 1] / static_cast<float>(D) + eps);
+    s_scale[b][0] = inv1;
+    s_scale[b][1] = inv1 * inv2;
+  }
+  __syncthreads();
+  // m = x * inv1 * ffn_w (bf16) for this CTA's columns, two per thread
+  for (int i = threadIdx.x; i < B * (kCols >> 1); i += kThreads) {
+    const int b = i / (kCols >> 1), c = 2 * (i - b * (kCols >> 1));
+    const float inv1 = s_scale[b][0];
+    *reinterpret_cast<uint32_t*>(m_bf + static_cast<int64_t>(b) * D + c0 + c) =
+        pack_bf16x2(s_x[b][c] * inv1 * s_ffn[c], s_x[b][c + 1] * inv1 * s_ffn[c + 1]);
+  }
+  if (cta == 0) {
+    for (int t = threadIdx.x; t < B * E; t += kThreads) {
+      const int b = t / E, e = t - b * E;
+      s_logits[t] = s_scale[b][1] * s_tot[b * NV + 2 + e];
+    }
+    __syncthreads();
+    if (warp == 0)
+      warp_topk_plan(s_logits, B, E, top_k, tile_m, s_idx, s_prob, s_cnt, topk_idx, topk_prob,
+                     counts, offsets, tile_offsets, perm_token, perm_prob, route_pos, lane);
+  }
+  cluster.sync();  // keep this CTA's shares alive until every peer has read them
+}
+
 int kch_for(int K) {
   if (K <= 0 || K % 8 != 0) return 0;
   if (K <= 768) return 3;
@@ -423,12 +594,48 @@ LLMYB_API int32_t llmyb_decode_out_router(
       (reinterpret_cast<uintptr_t>(m_bf) & 7u))
     return LLMYB_EUNSUPPORTED;
   const int nv = 2 + n_experts;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int bm = bm_for(n_tokens);
+  // one-cluster form: D = 768 (6 rows per warp, K <= 1024) or D = 1024 (8 rows per
+  // warp, K <= 768: the weight rows stay in registers), B * E <= 64
+  const int rpw_c = d_model % (kOrCtas * kOrWarps) == 0 ? d_model / (kOrCtas * kOrWarps) : 0;
+  if (((rpw_c == 6 && kch <= 4) || (rpw_c == 8 && kch == 3)) &&
+      n_tokens * n_experts <= 64) {
+    const int rpw = d_model / (kOrCtas * kOrWarps);
+    const int cbytes = ((n_tokens * k_in * 2 + 15) & ~15) + n_experts * (kOrWarps * rpw) * 4;
+    static int cattr[3][2][2] = {};
+    const int bi = bm == 1 ? 0 : (bm == 4 ? 1 : 2), ki = kch == 3 ? 0 : 1, ri = rpw == 6 ? 0 : 1;
+    int32_t st = LLMYB_OK;
+#define LLMYB_ORC(BMV, KCHV, RPWV)                                                              \
+  do {                                                                                          \
+    st = ensure_smem(decode_out_router_cluster_kernel<BMV, KCHV, RPWV>, cbytes,                 \
+                     cattr[bi][ki][ri]);                                                        \
+    if (st) return st;                                                                          \
+    st = launch_pdl(decode_out_router_cluster_kernel<BMV, KCHV, RPWV>, dim3(kOrCtas),            \
+        dim3(kOrWarps * 32), cbytes, s, static_cast<const __nv_bfloat16*>(in), in_ld, k_in,     \
+        static_cast<const __nv_bfloat16*>(w), n_tokens, d_model, conv_w,                        \
+        static_cast<const __nv_bfloat16*>(normed), static_cast<__nv_bfloat16*>(history),        \
+        streams, ffn_norm, w_router_folded, eps, n_experts, top_k, tile_m,                      \
+        static_cast<__nv_bfloat16*>(m_bf), topk_idx, topk_prob, expert_counts, expert_offsets,  \
+        tile_offsets, perm_token, perm_prob, route_pos);                                        \
+    if (st) return st;                                                                          \
+  } while (0)
+#define LLMYB_ORC_R(BMV)                                                                        \
+  do {                                                                                          \
+    if (rpw == 8) LLMYB_ORC(BMV, 3, 8);                                                         \
+    else if (kch == 3) LLMYB_ORC(BMV, 3, 6);                                                    \
+    else LLMYB_ORC(BMV, 4, 6);                                                                  \
+  } while (0)
+    if (bm == 1) LLMYB_ORC_R(1); else if (bm == 4) LLMYB_ORC_R(4); else LLMYB_ORC_R(8);
+#undef LLMYB_ORC_R
+#undef LLMYB_ORC
+    count_launch();
+    return launch_status();
+  }
   const int bytes =
       std::max(n_tokens * k_in * 2, (n_tokens * nv + n_tokens * n_experts) * 4);
   const int grid = static_cast<int>(ceil_div(d_model, 8));
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
   static int attr[3][3] = {};
-  const int bm = bm_for(n_tokens);
   const int bi = bm == 1 ? 0 : (bm == 4 ? 1 : 2), ki = kch == 3 ? 0 : (kch == 4 ? 1 : 2);
   int32_t st = LLMYB_OK;
 #define LLMYB_OR(BMV, KCHV)                                                                     \
