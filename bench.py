@@ -176,14 +176,14 @@ def run_reference(args) -> None:
 
 
 # ------------------------------------------------------------- our path
-# DRAM traffic of one decode_out_router_kernel launch at the small-llmy decode
-# shape, measured with ncu (dram__bytes_read.sum + dram__bytes_write.sum, one
-# launch of a GDN block and of a CSA block: 1,302,528 and 1,320,192 bytes).
-OUT_ROUTER_TRAFFIC = 1_311_360
+# DRAM traffic of one decode_out_router_cluster_kernel launch at the small-llmy
+# decode shape, measured with ncu (dram__bytes_read.sum + dram__bytes_write.sum,
+# caches flushed before the launch; two launches: 1,305,344 and 1,323,520 bytes).
+OUT_ROUTER_TRAFFIC = 1_314_432
 
 
 def out_router_roofline(model, p: dict, reps: int = 50) -> dict:
-    """Roofline of the decode step's dominant kernel (decode_out_router_kernel:
+    """Roofline of the decode step's dominant kernel (decode_out_router_cluster_kernel:
     output projection + residual + norms + router of one block, the largest
     share of the step's launch list) at the benchmark's decode shape.  Its
     average launch duration is timed with CUDA events over a CUDA graph of
@@ -231,9 +231,9 @@ def out_router_roofline(model, p: dict, reps: int = 50) -> dict:
     achieved = alg / dt / 1e9
     return {"bound": "hbm", "achieved": achieved, "peak": p["hbm_gbs"], "unit": "GB/s",
             "frac": achieved / p["hbm_gbs"], "traffic": OUT_ROUTER_TRAFFIC,
-            "kernel": "decode_out_router_kernel (CSA block, batch 1): output projection GEMV + "
-                      "residual + norm and router-logit shares per CTA, top-k/plan in the last "
-                      "CTA",
+            "kernel": "decode_out_router_cluster_kernel (CSA block, batch 1): one 8-CTA cluster; "
+                      "output projection GEMV + residual + norm and router-logit shares per CTA, "
+                      "combined through distributed shared memory; top-k/plan in CTA 0",
             "algorithmic_bytes_per_launch": alg, "avg_launch_us": dt * 1e6,
             "timing": f"CUDA events over a graph of {reps} launches x 5 replays",
             "peak_source": p["source"]}

@@ -127,8 +127,9 @@ __global__ void __launch_bounds__(256) moe_decode_down_kernel(
     const int* __restrict__ expert_offsets, const __nv_bfloat16* __restrict__ w2, int D, int F,
     int E, int compact, const int* __restrict__ out_row, __nv_bfloat16* __restrict__ y_perm) {
   extern __shared__ __nv_bfloat16 s_h[];  // [kTok][F]
-  pdl_wait();  // h comes from the up kernel
-  pdl_trigger();
+  // The plan (expert_offsets, perm_prob, out_row) was written two or more
+  // launches earlier (the up kernel runs in between), so the expert and its
+  // weight rows are fetched before waiting for h.
   const int dblocks = D / kWarps;
   const int e = slot_expert(expert_offsets, E, blockIdx.x / dblocks, compact);
   if (e < 0) return;
@@ -144,6 +145,8 @@ __global__ void __launch_bounds__(256) moe_decode_down_kernel(
     const int c = lane + 32 * i;
     if (c < nch) w4[i] = __ldg(wr + c);
   }
+  pdl_wait();  // h comes from the up kernel
+  pdl_trigger();
   for (int base = r0; base < r1; base += kTok) {
     const int nt = min(kTok, r1 - base);
     __syncthreads();
