@@ -92,14 +92,20 @@ __global__ void __launch_bounds__(128) gdn_step_kernel(GdnIO io, int H, int VD,
   constexpr int RPW = KD / 4;  // state rows per warp
   __shared__ float s_q[KD], s_k[KD];
   __shared__ float s_red[4][32];
-  pdl_wait();  // q/k/v/gate/beta come from the projection kernel
-  pdl_trigger();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int nvc = VD / 32;
   const int b = blockIdx.x / (H * nvc);
   const int h = (blockIdx.x / nvc) % H;
   const int v0 = (blockIdx.x % nvc) * 32;
   const int64_t tok = b;  // one token per row
+  // the state was last written by this kernel one token earlier: it streams in
+  // while the projection kernel still runs
+  float* S = state + ((static_cast<int64_t>(b) * H + h) * KD) * VD + v0 + lane;
+  float s[RPW];
+#pragma unroll
+  for (int r = 0; r < RPW; ++r) s[r] = S[static_cast<int64_t>(warp * RPW + r) * VD];
+  pdl_wait();  // q/k/v/gate/beta come from the projection kernel
+  pdl_trigger();
   for (int i = threadIdx.x; i < KD; i += 128) {
     s_q[i] = bf2f(io.q[tok * io.sq + h * KD + i]);
     s_k[i] = bf2f(io.k[tok * io.sk + h * KD + i]);
@@ -132,13 +138,11 @@ __global__ void __launch_bounds__(128) gdn_step_kernel(GdnIO io, int H, int VD,
   const float a = alpha_of(io, tok, h, H);
   float beta = bf2f(io.beta[tok * io.sb + h]);
   if (io.raw) beta = sigmoidf_(beta + (io.beta_bias ? io.beta_bias[h] : 0.f));
-  float* S = state + ((static_cast<int64_t>(b) * H + h) * KD) * VD + v0 + lane;
-  float s[RPW];
   float pred = 0.f;
 #pragma unroll
   for (int r = 0; r < RPW; ++r) {
     const int kr = warp * RPW + r;
-    s[r] = rst ? 0.f : S[static_cast<int64_t>(kr) * VD];
+    if (rst) s[r] = 0.f;
     pred += s_k[kr] * s[r];
   }
   s_red[warp][lane] = pred;
