@@ -143,6 +143,18 @@ class Block:
     moe: MoeBlock
 
 
+def _experts(sd: Mapping[str, torch.Tensor], p: str, name: str, lo: int, hi: int,
+             dev: torch.device) -> torch.Tensor:
+    """Experts lo..hi-1 of one projection as [hi-lo, rows, cols] bf16: from the
+    per-expert parameters (moe.experts.<e>.<name>.weight) or from one stacked
+    tensor (moe.experts.<name>.weight, the .llmy converter's layout)."""
+    stacked = sd.get(f"{p}moe.experts.{name}.weight")
+    if stacked is not None:
+        return stacked[lo:hi].to(dev, torch.bfloat16)
+    return torch.stack([sd[f"{p}moe.experts.{x}.{name}.weight"].to(dev, torch.bfloat16)
+                        for x in range(lo, hi)])
+
+
 @dataclass
 class ModelWeights:
     cfg: HybridConfig
@@ -183,14 +195,11 @@ class ModelWeights:
                                     bf(p + "mixer.value.weight")]).contiguous(),
                     local_out=bf(p + "mixer.local_out.weight"), out=bf(p + "mixer.out.weight"),
                     w_o=w_o.to(torch.bfloat16).contiguous())
-            gate = torch.stack([sd[f"{p}moe.experts.{x}.gate_proj.weight"].to(dev, torch.bfloat16)
-                                for x in range(lo, hi)])
-            up = torch.stack([sd[f"{p}moe.experts.{x}.up_proj.weight"].to(dev, torch.bfloat16)
-                              for x in range(lo, hi)])
+            gate = _experts(sd, p, "gate_proj", lo, hi, dev)
+            up = _experts(sd, p, "up_proj", lo, hi, dev)
             w13 = kernels.pack_w13(gate, up)
             del gate, up
-            w2 = torch.stack([sd[f"{p}moe.experts.{x}.down_proj.weight"].to(dev, torch.bfloat16)
-                              for x in range(lo, hi)]).contiguous()
+            w2 = _experts(sd, p, "down_proj", lo, hi, dev).contiguous()
             moe = MoeBlock(router_norm=f32(p + "moe.router.norm.weight"),
                            router=f32(p + "moe.router.logits.weight"), w13=w13, w2=w2)
             moe.router_folded = kernels.fold_router(moe.router, f32(p + "ffn_norm.weight"),
@@ -201,6 +210,21 @@ class ModelWeights:
                    stream_seed=f32("stream_seed").reshape(-1).contiguous(),
                    collapse=bf("mhc_collapse.weight"), final_norm=f32("final_norm.weight"),
                    blocks=blocks)
+
+    @classmethod
+    def from_llmy(cls, path, device: str | torch.device = "cuda",
+                  expert_range: tuple[int, int] | None = None) -> "ModelWeights":
+        """Load a checkpoint in the reference engine's ``.llmy`` format
+        (llmy_cuda/tools/convert_checkpoint.py): its embedded configuration
+        through HybridConfig.from_v6, its (expert-stacked) tensors through
+        from_state_dict."""
+        from .llmy_format import read_llmy
+        f = read_llmy(path)
+        try:
+            cfg = HybridConfig.from_v6(f.config)
+            return cls.from_state_dict(cfg, f.tensors, device, expert_range=expert_range)
+        finally:
+            f.close()
 
     def nbytes(self) -> int:
         total = 0

@@ -128,6 +128,15 @@ def mini_config():
                         name="mini")
 
 
+def llmy_config():
+    """A small looped hybrid model for the .llmy format fixture."""
+    from hybrid_llm_b200.config import HybridConfig
+    return HybridConfig(vocab_size=256, d_model=128, recurrent_layout=("csa_moe", "gdn_moe"),
+                        num_loops=2, gdn_heads=2, gdn_key_dim=64, gdn_value_dim=64, csa_heads=2,
+                        csa_head_dim=64, csa_window=16, moe_experts=4, moe_top_k=2, moe_hidden=128,
+                        name="llmy-tiny")
+
+
 def mini_prompt():
     rng = np.random.default_rng(7000)
     return rng.integers(0, 1000, size=(2, 50)).astype(np.int64)
