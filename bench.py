@@ -11,9 +11,11 @@ graph replay, the sampled token feeding the next step on the device.
   e2e     the same through the public decode API with a pinned-host token
           round trip every step (H2D of the input id, D2H of the sampled id
           and its log-probability)
-  secondary  isolated-MoE-layer TFLOPS (16384 tokens x 1024, 32 experts top-4,
-          Zipf-skewed routing), long-context prefill (banded attention and the
-          GDN chunked scan at B=8, T=8192), small-model prefill tokens/s
+  secondary  the single looped block ([1, 256, 512], 2 loops), isolated-MoE-
+          layer TFLOPS (16384 tokens x 1024, 32 experts top-4, Zipf-skewed
+          routing), long-context prefill (banded attention and the GDN chunked
+          scan at B=8, T=8192), the large expert-parallel decode (batch 64),
+          small-model prefill tokens/s
   cpu_baseline  the CPU port of the reference algorithm (oracle/) timed on
           this host on a bounded sample of the same decode workload
 
@@ -242,6 +244,41 @@ def out_router_roofline(model, p: dict, reps: int = 50) -> dict:
 def _events():
     import torch
     return torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+
+def secondary_block(p: dict, reps: int = 20) -> dict:
+    """Single looped hybrid block workload: hidden states [1, 256, 512] ~ N(0, 1)
+    through the csa_moe + gdn_moe core, 2 loops (random N(0, 0.02) weights).
+    The reference runs it in fp32 on the CPU; here bf16 operands with fp32
+    accumulation and an fp32 residual stream."""
+    import numpy as np
+    import torch
+
+    from hybrid_llm_b200.config import single_block_config
+    from hybrid_llm_b200.model import LoopedHybridModel
+    from hybrid_llm_b200.weights import ModelWeights, synthetic_state_dict
+
+    cfg = single_block_config()
+    model = LoopedHybridModel(ModelWeights.from_state_dict(
+        cfg, synthetic_state_dict(cfg, seed=0, device="cuda"), "cuda"))
+    x = torch.from_numpy(np.random.default_rng(1).normal(0, 1, (1, 256, cfg.d_model))
+                         .astype(np.float32)).cuda()
+    for _ in range(3):
+        model.run_stack(x)
+    times = []
+    for _ in range(max(1, reps)):
+        a, b = _events()
+        a.record()
+        model.run_stack(x)
+        b.record()
+        torch.cuda.synchronize()
+        times.append(a.elapsed_time(b))
+    t = float(np.median(times)) * 1e-3
+    # MoE 2*T*k*3*D*F per block application (the dominant term), 2 blocks x 2 loops
+    flops = 4 * 2.0 * 256 * cfg.moe_top_k * 3 * cfg.d_model * cfg.moe_hidden
+    return {"workload": "single looped block [1, 256, 512], csa_moe + gdn_moe, 2 loops",
+            "ms": t * 1e3, "tok_s": 256 / t, "moe_tflops": flops / t / 1e12,
+            "note": "latency-bound (256 tokens); timed with CUDA events, median"}
 
 
 def secondary_moe(p: dict, reps: int = 10) -> dict:
@@ -582,6 +619,7 @@ def run_ours(args) -> None:
         secondary["large_ep_decode"] = secondary_ep_decode(p, steps=10, warmup=3)
         torch.cuda.empty_cache()
     if rank == 0 and world == 1 and not args.no_secondary:
+        secondary["single_block"] = secondary_block(p)
         secondary["moe_layer"] = secondary_moe(p)
         secondary["long_prefill"] = secondary_prefill(p)
     if secondary:
@@ -630,7 +668,8 @@ def main() -> None:
                     help="skip the large expert-parallel decode measurement")
     ap.add_argument("--ep-exchange", choices=["p2p", "nccl"], default="p2p",
                     help="expert-parallel exchange of --only ep_decode")
-    ap.add_argument("--only", choices=["moe_layer", "long_prefill", "ep_decode"], default=None,
+    ap.add_argument("--only", choices=["single_block", "moe_layer", "long_prefill", "ep_decode"],
+                    default=None,
                     help="run one secondary workload alone (used for kernel profiles)")
     ap.add_argument("--prefill-batch", type=int, default=8,
                     help="batch of the long-context prefill workload (profiles use 1)")
@@ -658,6 +697,8 @@ def main() -> None:
         torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
         if args.only == "long_prefill":
             res = secondary_prefill(peaks(), reps=args.steps, batch=args.prefill_batch)
+        elif args.only == "single_block":
+            res = secondary_block(peaks(), reps=args.steps)
         else:
             res = secondary_moe(peaks(), reps=args.steps)
         print(json.dumps({"only": args.only, **res}), flush=True)

@@ -258,7 +258,8 @@ class ExpertParallel:
         if path not in ("auto", "grouped", "decode"):
             raise ValueError(f"unknown expert path {path!r}")
         grouped = path == "grouped" or (
-            path == "auto" and kernels.use_grouped_rows(self.capacity, self.experts_per_rank))
+            path == "auto" and kernels.use_grouped_rows(self.capacity, self.experts_per_rank,
+                                                        self.d_model, self.ffn))
         self.ops.experts_to(self, w13_local, w2_local, grouped)
         if self.peers is None:
             self._exchange(self.ret_recv, self.ret_send)

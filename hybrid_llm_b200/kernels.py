@@ -332,9 +332,19 @@ def grouped_scratch_bytes(n_rows: int, d_model: int, ffn: int) -> int:
     return int(_native.lib().llmyb_moe_grouped_scratch_bytes(int(n_rows), 1, int(d_model), int(ffn)))
 
 
-def use_grouped_rows(n_rows: int, n_experts: int) -> bool:
+def grouped_shape_ok(d_model: int, ffn: int) -> bool:
+    """Shapes the tcgen05 grouped GEMMs tile: 256-column output tiles of both
+    products (d_model % 256, 2 * ffn % 256) and 64-wide K blocks."""
+    return d_model % 256 == 0 and ffn % 128 == 0
+
+
+def use_grouped_rows(n_rows: int, n_experts: int, d_model: int | None = None,
+                     ffn: int | None = None) -> bool:
     """Routed rows per expert at which the tcgen05 grouped GEMMs beat the
-    weight-streaming decode kernels (whose CUDA-core work grows with rows)."""
+    weight-streaming decode kernels (whose CUDA-core work grows with rows),
+    for shapes the grouped GEMMs support."""
+    if d_model is not None and ffn is not None and not grouped_shape_ok(d_model, ffn):
+        return False
     return n_rows >= 2 * n_experts
 
 
@@ -367,7 +377,8 @@ def moe_experts_rows(x: torch.Tensor, plan: RoutePlan, w13: torch.Tensor, w2: to
     e = w13.shape[0]
     if path not in ("auto", "grouped", "decode"):
         raise ValueError(f"unknown expert path {path!r}")
-    if path == "decode" or (path == "auto" and not use_grouped_rows(n_rows, e)):
+    if path == "decode" or (path == "auto" and not use_grouped_rows(n_rows, e, x.shape[-1],
+                                                                    w2.shape[-1])):
         return moe_decode_experts(x, plan, w13, w2, y_rows=y_rows)
     if y_rows is None:
         y_rows = torch.empty(n_rows, x.shape[-1], dtype=torch.bfloat16, device=x.device)
@@ -487,8 +498,9 @@ def moe_grouped(x: torch.Tensor, plan: RoutePlan, w13: torch.Tensor, w2: torch.T
     if out is None:
         out = torch.empty(n, d, dtype=torch.bfloat16, device=x.device)
     if path == "auto":
-        path = "decode" if (n * k < 32 * e and d <= 2048 and f <= 2048
-                            and d % 128 == 0 and f % 128 == 0) else "grouped"
+        decode_ok = d <= 2048 and f <= 2048 and d % 128 == 0 and f % 128 == 0
+        path = "decode" if decode_ok and (n * k < 32 * e or not grouped_shape_ok(d, f)) \
+            else "grouped"
     lib = _native.lib()
     if path == "decode":
         need = int(lib.llmyb_moe_decode_scratch_bytes(n, k, d, f))
