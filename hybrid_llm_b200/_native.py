@@ -70,7 +70,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
                              P, P, I64, I32, P, P]),
     "llmyb_gdn_prefill_scratch_bytes": (I64, [I32, I32, I32, I32, I32]),
     "llmyb_gdn_prefill": (I32, [P, I64, P, I64, P, I64, P, I64, P, I64, P, P, P, I32, I32, I32,
-                                I32, I32, P, P, I64, P, P]),
+                                I32, I32, P, P, I64, P, P, P]),
     "llmyb_gdn_conv_gate": (I32, [P, P, P, P, P, I32, I32, I32, P, P, I32, P]),
     # banded attention
     "llmyb_banded_attention": (I32, [P, I64, P, I64, P, I64, I32, I32, I32, I32, I32, I32, F32, P,

@@ -28,6 +28,8 @@
 // and fed to the tensor cores as a bf16 hi/lo pair.
 #include "common.cuh"
 #include "mma.cuh"
+#include "sm100.cuh"
+#include "tma_host.h"
 
 #include <algorithm>
 
@@ -173,6 +175,7 @@ __global__ void __launch_bounds__(128) gdn_step_kernel(GdnIO io, int H, int VD,
 struct PrepOut {
   __nv_bfloat16* U;   // [B*T, H, VD]
   __nv_bfloat16* Kw;  // [B*T, H, KD]
+  __nv_bfloat16* Qs;  // [B*T, H, KD] qscale * q (tcgen05 scan only; else null)
   __nv_bfloat16* Aqk; // [B, H, nC, C, C]
   float* qscale;      // [B, H, T]
   float* kscale;      // [B, H, T]
@@ -279,6 +282,24 @@ __global__ void __launch_bounds__(128) gdn_chunk_prep_kernel(GdnIO io, int B, in
   }
   mma::cp_async_wait<0>();
   __syncthreads();
+  if (po.Qs != nullptr) {
+    // Qs = diag(qscale) Q (0 before the chunk's first reset), for the tcgen05
+    // scan's single output accumulator
+    for (int i = tid; i < n * (KD / 8); i += 128) {
+      const int r = i / (KD / 8), cc = (i % (KD / 8)) * 8;
+      const float sc = sm.seg[r] == 0 ? fast_exp2(sm.g[r]) : 0.f;
+      const uint4 v = *reinterpret_cast<const uint4*>(&sQ[r * SM::LK + cc]);
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+      uint4 o;
+      uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = unpack_bf16x2(w[j]);
+        ow[j] = pack_bf16x2(f.x * sc, f.y * sc);
+      }
+      *reinterpret_cast<uint4*>(po.Qs + ((tok0 + r) * H + h) * KD + cc) = o;
+    }
+  }
 
   // ---- KK^T and QK^T for rows 16*warp .. +15 (all 64 columns)
   float kk[8][4], qk[8][4];
@@ -804,6 +825,359 @@ __global__ void gdn_conv_roll_kernel(const __nv_bfloat16* __restrict__ x,
     history[static_cast<int64_t>(b) * 3 * D + i] = s_roll[i];
 }
 
+// ------------------------------------------------- chunk scan on tcgen05
+// K = 128, value slices of 64 columns; one CTA per (row, head, slice).
+//   warp 0     TMA: per chunk [Kw; Qs] (Qs = diag(qscale) q, from the prep
+//              kernel), K, [0; Aqk] and the U slice, two stages
+//   warp 1     MMA (one thread), per chunk:
+//                D1  = [Kw; Qs] S            (rows 0-63: Kw S, rows 64-127: Qs S)
+//                D1 += [0; Aqk] W            (rows 64-127 become O)
+//                D2  = K^T diag(ks) W        (the state update)
+//              S, W and X = diag(ks) W are fed as bf16 hi + lo pairs (two
+//              MMAs each), so the products keep about 16 mantissa bits.
+//   warps 2-5  state warps, one TMEM lane each (= key row of S, and token
+//              row of D1): the fp32 state slice S[key][64] lives in their
+//              registers for the whole sequence.  After D1: W = U - Kw S and
+//              X = ks W (token rows) into shared memory as MMA operands;
+//              after D1/D2: S <- sd S + D2, S hi/lo into shared memory, and O
+//              (D1 rows 64-127) times the gate to global memory.
+// Operands written by threads use the 128-byte-swizzled MN-major layout of
+// an MMA B operand (row = K index, 64 N-columns per row).  TMEM: D1 columns
+// [0, 64), D2 [64, 128).  Every wait is bounded (1 s) and unwinds on timeout.
+namespace scan_tc {
+constexpr int kVS = 64;                                     // value columns per CTA
+constexpr int kA1 = 0;                                      // [Kw; Qs]: 2 x (128 rows x 64) bf16
+constexpr int kA2 = 32768;                                  // K [64 tok][128 keys]: 2 x 8 KB
+constexpr int kA3 = 49152;                                  // [0; Aqk]: 128 rows x 64
+constexpr int kU = 65536;                                   // U [64 tok][64 cols]
+constexpr int kStage = 73728;
+constexpr uint32_t kTx = 2 * 8192 + 2 * 8192 + 2 * 8192 + 8192 + 8192;
+constexpr int kS = 2 * kStage;                              // S hi | S lo  [128][64] bf16
+constexpr int kW = kS + 32768;                              // W hi | W lo | X hi | X lo  [64][64]
+constexpr int kBar = kW + 32768;
+constexpr int kSmem = kBar + 256 + 1024;
+constexpr uint32_t kTmemCols = 128;
+
+// one 64-element row, scale * v (fp32 bit patterns), as bf16 hi and lo parts
+// into two swizzled operand tiles
+__device__ __forceinline__ void store_row_hilo(uint8_t* hi, uint8_t* lo, int row,
+                                               const uint32_t (&v)[2][32], float scale) {
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    uint4 h, l;
+    uint32_t* hw = reinterpret_cast<uint32_t*>(&h);
+    uint32_t* lw = reinterpret_cast<uint32_t*>(&l);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int c0 = 8 * j + 2 * e;
+      const float a = __uint_as_float(v[c0 >> 5][c0 & 31]) * scale;
+      const float b = __uint_as_float(v[(c0 + 1) >> 5][(c0 + 1) & 31]) * scale;
+      const __nv_bfloat162 hh = __floats2bfloat162_rn(a, b);
+      const float2 hf = __bfloat1622float2(hh);
+      hw[e] = *reinterpret_cast<const uint32_t*>(&hh);
+      lw[e] = pack_bf16x2(a - hf.x, b - hf.y);
+    }
+    const int off = row * 128 + ((j ^ (row & 7)) << 4);
+    *reinterpret_cast<uint4*>(hi + off) = h;
+    *reinterpret_cast<uint4*>(lo + off) = l;
+  }
+}
+}  // namespace scan_tc
+
+__global__ void __launch_bounds__(192, 1) gdn_scan_tc_kernel(
+    const __grid_constant__ CUtensorMap map_kw, const __grid_constant__ CUtensorMap map_qs,
+    const __grid_constant__ CUtensorMap map_k, const __grid_constant__ CUtensorMap map_aqk,
+    const __grid_constant__ CUtensorMap map_u, const float* __restrict__ kscale,
+    const float* __restrict__ sdecay, const __nv_bfloat16* __restrict__ gate, int64_t sg,
+    int B, int T, int H, int VD, float* __restrict__ state, __nv_bfloat16* __restrict__ out,
+    int64_t so, int32_t* dev_status) {
+  using namespace scan_tc;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kBar);
+  uint64_t* st_full = bars;       // [2]
+  uint64_t* st_empty = bars + 2;  // [2]
+  uint64_t* s_ready = bars + 4;
+  uint64_t* d1_full = bars + 5;
+  uint64_t* w_ready = bars + 6;
+  uint64_t* d23_full = bars + 7;
+  uint64_t* mma_done = bars + 8;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 9);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nvs = VD / kVS;
+  const int vs = blockIdx.x % nvs;
+  const int h = (blockIdx.x / nvs) % H;
+  const int b = blockIdx.x / (nvs * H);
+  const int v0 = vs * kVS;
+  const int nC = (T + kC - 1) / kC;
+  const int64_t bh = static_cast<int64_t>(b) * H + h;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      sm100::mbar_init(&st_full[i], 1);
+      sm100::mbar_init(&st_empty[i], 3);  // MMA commit + the two warps that read U
+    }
+    sm100::mbar_init(s_ready, 4);
+    sm100::mbar_init(d1_full, 1);
+    sm100::mbar_init(w_ready, 2);
+    sm100::mbar_init(d23_full, 1);
+    sm100::mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    sm100::fence_mbar_init();
+    sm100::tma_prefetch_desc(&map_kw);
+    sm100::tma_prefetch_desc(&map_qs);
+    sm100::tma_prefetch_desc(&map_k);
+    sm100::tma_prefetch_desc(&map_aqk);
+    sm100::tma_prefetch_desc(&map_u);
+  }
+  // the zero rows of [0; Aqk] (TMA writes only rows 64-127)
+  for (int i = threadIdx.x; i < 2 * 8192 / 16; i += blockDim.x) {
+    const int st = i / 512, o = (i % 512) * 16;
+    *reinterpret_cast<uint4*>(smem + st * kStage + kA3 + o) = make_uint4(0, 0, 0, 0);
+  }
+  sm100::fence_proxy_async_smem();
+  if (warp == 1) sm100::tmem_alloc(tmem_slot, kTmemCols);
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------- TMA
+    uint32_t issued = 0;
+    for (int c = 0; c < nC; ++c) {
+      const int s = c & 1;
+      if (!sm100::mbar_wait_warp(&st_empty[s], ((c >> 1) & 1) ^ 1u, dev_status, abort_flag)) break;
+      if (lane == 0) {
+        uint8_t* st = smem + s * kStage;
+        const int t0 = c * kC;
+        sm100::mbar_arrive_expect_tx(&st_full[s], kTx);
+#pragma unroll
+        for (int x = 0; x < 2; ++x) {
+          sm100::tma_load_4d(&map_kw, &st_full[s], st + kA1 + x * 16384, x * 64, h, t0, b);
+          sm100::tma_load_4d(&map_qs, &st_full[s], st + kA1 + x * 16384 + 8192, x * 64, h, t0, b);
+          sm100::tma_load_3d(&map_k, &st_full[s], st + kA2 + x * 8192, h * 128 + x * 64, t0, b);
+        }
+        sm100::tma_load_2d(&map_aqk, &st_full[s], st + kA3 + 8192, 0,
+                           static_cast<int32_t>((bh * nC + c) * kC));
+        sm100::tma_load_4d(&map_u, &st_full[s], st + kU, v0, h, t0, b);
+      }
+      ++issued;
+    }
+    for (uint32_t i = 1; i <= 2; ++i)
+      if (issued >= i)
+        sm100::mbar_wait_warp(&st_full[(issued - i) & 1], ((issued - i) >> 1) & 1, dev_status,
+                              nullptr);
+  } else if (warp == 1) {
+    // ------------------------------------------------------------- MMA
+    constexpr uint32_t idesc = sm100::make_idesc_bf16_f32(128, kVS) | sm100::kIdescBMajorMN;
+    constexpr uint32_t idesc_t = idesc | (1u << 15);  // A (K^T) MN-major too
+    const uint32_t t_d1 = tmem_base, t_d2 = tmem_base + 64;
+    const uint32_t s_hi = sm100::smem_u32(smem + kS), s_lo = s_hi + 16384;
+    const uint32_t w_hi = sm100::smem_u32(smem + kW), w_lo = w_hi + 8192;
+    const uint32_t x_hi = w_hi + 16384, x_lo = w_hi + 24576;
+    for (int c = 0; c < nC; ++c) {
+      const int s = c & 1;
+      const uint32_t st = sm100::smem_u32(smem + s * kStage);
+      if (!sm100::mbar_wait_warp(&st_full[s], (c >> 1) & 1, dev_status, abort_flag) ||
+          !sm100::mbar_wait_warp(s_ready, c & 1, dev_status, abort_flag))
+        break;
+      sm100::tc_fence_after();
+      if (lane == 0) {
+#pragma unroll 1
+        for (int part = 0; part < 2; ++part) {
+          const uint32_t sb = part == 0 ? s_hi : s_lo;
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            const uint64_t ad =
+                sm100::make_sw128_kmajor_desc(st + kA1 + (kk >> 2) * 16384 + (kk & 3) * 32);
+            const uint64_t bd = sm100::make_sw128_desc(sb + kk * 2048, 8192, 1024);
+            sm100::umma_bf16_ss(t_d1, ad, bd, idesc, (part | kk) != 0 ? 1u : 0u);
+          }
+        }
+        sm100::umma_commit(d1_full);
+      }
+      __syncwarp();
+      if (!sm100::mbar_wait_warp(w_ready, c & 1, dev_status, abort_flag)) break;
+      sm100::tc_fence_after();
+      if (lane == 0) {
+#pragma unroll 1
+        for (int part = 0; part < 2; ++part) {
+          const uint32_t wb = part == 0 ? w_hi : w_lo, xb = part == 0 ? x_hi : x_lo;
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            // D1 rows 64-127 += Aqk W (rows 0-63 of [0; Aqk] are zero)
+            const uint64_t a3 = sm100::make_sw128_kmajor_desc(st + kA3 + kk * 32);
+            sm100::umma_bf16_ss(t_d1, a3, sm100::make_sw128_desc(wb + kk * 2048, 8192, 1024),
+                                idesc, 1u);
+            // D2 = K^T X: A = K [token][key] read MN-major (64-key blocks 8 KB apart)
+            const uint64_t a2 = sm100::make_sw128_desc(st + kA2 + kk * 2048, 8192, 1024);
+            sm100::umma_bf16_ss(t_d2, a2, sm100::make_sw128_desc(xb + kk * 2048, 8192, 1024),
+                                idesc_t, (part | kk) != 0 ? 1u : 0u);
+          }
+        }
+        sm100::umma_commit(d23_full);
+        sm100::umma_commit(&st_empty[s]);
+      }
+      __syncwarp();
+    }
+    if (lane == 0) sm100::umma_commit(mma_done);
+    __syncwarp();
+    sm100::mbar_wait_warp(mma_done, 0, dev_status, nullptr);
+  } else {
+    // ------------------------------------------------------ state warps
+    const int q = warp & 3;
+    const int row = q * 32 + lane;  // TMEM lane: key row of S / D2, row of D1
+    const uint32_t t_lane = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
+    uint8_t* s_hi = smem + kS;
+    uint8_t* s_lo = s_hi + 16384;
+    uint8_t* w_hi = smem + kW;
+    uint8_t* w_lo = w_hi + 8192;
+    uint8_t* x_hi = w_hi + 16384;
+    uint8_t* x_lo = w_hi + 24576;
+    float* Sg = state + (bh * 128 + row) * VD + v0;
+    uint32_t S[2][32];  // fp32 bit patterns of S[row][v0 .. v0 + 63]
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const uint4 v = reinterpret_cast<const uint4*>(Sg)[j];
+      S[j >> 3][(4 * j) & 31] = v.x;
+      S[j >> 3][(4 * j + 1) & 31] = v.y;
+      S[j >> 3][(4 * j + 2) & 31] = v.z;
+      S[j >> 3][(4 * j + 3) & 31] = v.w;
+    }
+    store_row_hilo(s_hi, s_lo, row, S, 1.f);
+    sm100::fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) sm100::mbar_arrive(s_ready);
+    bool ok = true;
+    // the chunk's decay scalars, fetched one chunk ahead (off the serial chain)
+    float ks_cur = row < 64 && row < T ? __ldg(kscale + bh * T + row) : 0.f;
+    float sd_cur = __ldg(sdecay + bh * nC);
+    for (int c = 0; c < nC && ok; ++c) {
+      const int s = c & 1;
+      const int t0 = c * kC;
+      const int n = min(kC, T - t0);
+      float ks_next = 0.f, sd_next = 0.f;
+      if (c + 1 < nC) {
+        if (row < 64 && t0 + kC + row < T) ks_next = __ldg(kscale + bh * T + t0 + kC + row);
+        sd_next = __ldg(sdecay + bh * nC + c + 1);
+      }
+      // ---- W = U - Kw S and X = ks W (token rows, warps of lane quarters 0-1)
+      // (U of this stage is complete once its "full" phase is)
+      if (row < 64 && !sm100::mbar_wait_warp(&st_full[s], (c >> 1) & 1, dev_status, abort_flag))
+        break;
+      if (!sm100::mbar_wait_warp(d1_full, c & 1, dev_status, abort_flag)) break;
+      sm100::tc_fence_after();
+      if (row < 64) {
+        uint32_t p[2][32];
+        sm100::tmem_ld_32x32b_x32(t_lane, p[0]);
+        sm100::tmem_ld_32x32b_x32(t_lane + 32, p[1]);
+        const int t = row;
+        const float ks = ks_cur;
+        sm100::tmem_ld_wait();
+        sm100::tmem_regs_ready(p[0]);
+        sm100::tmem_regs_ready(p[1]);
+        const uint8_t* urow = smem + s * kStage + kU + t * 128;
+        // W = U - Kw S in place of the loaded product
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const uint4 u = *reinterpret_cast<const uint4*>(urow + ((j ^ (t & 7)) << 4));
+          const uint32_t uw[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 uf = unpack_bf16x2(uw[e]);
+            const int col = 8 * j + 2 * e;
+            uint32_t& p0 = p[col >> 5][col & 31];
+            uint32_t& p1 = p[(col + 1) >> 5][(col + 1) & 31];
+            p0 = __float_as_uint(uf.x - __uint_as_float(p0));
+            p1 = __float_as_uint(uf.y - __uint_as_float(p1));
+          }
+        }
+        store_row_hilo(w_hi, w_lo, t, p, 1.f);
+        store_row_hilo(x_hi, x_lo, t, p, ks);  // X = diag(ks) W
+        sm100::fence_proxy_async_smem();
+        sm100::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          sm100::mbar_arrive(w_ready);
+          sm100::mbar_arrive(&st_empty[s]);  // U read
+        }
+      }
+      // ---- S <- sd S + D2; O = D1 rows 64-127 (read before D1 is released)
+      if (!sm100::mbar_wait_warp(d23_full, c & 1, dev_status, abort_flag)) break;
+      sm100::tc_fence_after();
+      const float sd = sd_cur;
+      {
+        uint32_t d2[2][32];
+        sm100::tmem_ld_32x32b_x32(t_lane + 64, d2[0]);
+        sm100::tmem_ld_32x32b_x32(t_lane + 96, d2[1]);
+        sm100::tmem_ld_wait();
+        sm100::tmem_regs_ready(d2[0]);
+        sm100::tmem_regs_ready(d2[1]);
+#pragma unroll
+        for (int j = 0; j < 64; ++j)
+          S[j >> 5][j & 31] = __float_as_uint(sd * __uint_as_float(S[j >> 5][j & 31]) +
+                                              __uint_as_float(d2[j >> 5][j & 31]));
+      }
+      if (c + 1 < nC) store_row_hilo(s_hi, s_lo, row, S, 1.f);
+      uint32_t o[2][32];
+      if (row >= 64) {
+        sm100::tmem_ld_32x32b_x32(t_lane, o[0]);
+        sm100::tmem_ld_32x32b_x32(t_lane + 32, o[1]);
+        sm100::tmem_ld_wait();
+        sm100::tmem_regs_ready(o[0]);
+        sm100::tmem_regs_ready(o[1]);
+      }
+      sm100::fence_proxy_async_smem();
+      sm100::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) sm100::mbar_arrive(s_ready);
+      if (row >= 64) {
+        const int t = row - 64;
+        if (t < n) {
+          uint4* dst = reinterpret_cast<uint4*>(out + (b * static_cast<int64_t>(T) + t0 + t) * so +
+                                                h * VD + v0);
+          const uint4* gr = reinterpret_cast<const uint4*>(
+              gate + (b * static_cast<int64_t>(T) + t0 + t) * sg + h * VD + v0);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const uint4 g4 = __ldg(gr + j);
+            const uint32_t gw[4] = {g4.x, g4.y, g4.z, g4.w};
+            uint4 r4;
+            uint32_t* rw = reinterpret_cast<uint32_t*>(&r4);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int col = 8 * j + 2 * e;
+              const float2 g2 = unpack_bf16x2(gw[e]);
+              // reference order: out.to(hidden dtype) * gate
+              const float o0 = bf2f(f2bf(__uint_as_float(o[col >> 5][col & 31])));
+              const float o1 = bf2f(f2bf(__uint_as_float(o[(col + 1) >> 5][(col + 1) & 31])));
+              rw[e] = pack_bf16x2(o0 * g2.x, o1 * g2.y);
+            }
+            dst[j] = r4;
+          }
+        }
+      }
+      ks_cur = ks_next;
+      sd_cur = sd_next;
+    }
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      reinterpret_cast<uint4*>(Sg)[j] =
+          make_uint4(S[j >> 3][(4 * j) & 31], S[j >> 3][(4 * j + 1) & 31],
+                     S[j >> 3][(4 * j + 2) & 31], S[j >> 3][(4 * j + 3) & 31]);
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    sm100::tc_fence_after();
+    sm100::tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
 template <typename K>
 int32_t set_smem(K kernel, int bytes) {
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
@@ -836,7 +1210,7 @@ GdnIO make_io(const void* q, int64_t sq, const void* k, int64_t sk, const void* 
 }
 
 struct ScratchLayout {
-  int64_t u, kw, aqk, qs, ks, sd, total;
+  int64_t u, kw, aqk, qs, ks, sd, qsq, total;
 };
 
 ScratchLayout scratch_layout(int B, int T, int H, int KD, int VD) {
@@ -850,13 +1224,23 @@ ScratchLayout scratch_layout(int B, int T, int H, int KD, int VD) {
   s.qs = s.aqk + al(static_cast<int64_t>(B) * H * nC * kC * kC * 2);
   s.ks = s.qs + al(bt * H * 4);
   s.sd = s.ks + al(bt * H * 4);
-  s.total = s.sd + al(static_cast<int64_t>(B) * H * nC * 4);
+  s.qsq = s.sd + al(static_cast<int64_t>(B) * H * nC * 4);
+  // the scaled q of the tcgen05 scan (K = 128 only)
+  s.total = s.qsq + (KD == 128 && VD % 64 == 0 ? al(bt * H * KD * 2) : 0);
   return s;
+}
+
+// the tcgen05 scan's operand and alignment requirements (else the mma.sync scan)
+bool scan_tc_ok(const GdnIO& io, int KD, int VD, const void* state, const void* out,
+                int64_t so) {
+  const auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  return KD == 128 && VD % scan_tc::kVS == 0 && io.sg % 8 == 0 && so % 8 == 0 && io.sk % 8 == 0 &&
+         a16(io.gate) && a16(out) && a16(state) && a16(io.k);
 }
 
 template <int KD, int VD>
 int32_t launch_prefill(const GdnIO& io, int B, int T, int H, void* scratch, float* state,
-                       __nv_bfloat16* out, int64_t so, cudaStream_t s) {
+                       __nv_bfloat16* out, int64_t so, int32_t* dev_status, cudaStream_t s) {
   const ScratchLayout L = scratch_layout(B, T, H, KD, VD);
   uint8_t* base = static_cast<uint8_t*>(scratch);
   PrepOut po;
@@ -866,6 +1250,8 @@ int32_t launch_prefill(const GdnIO& io, int B, int T, int H, void* scratch, floa
   po.qscale = reinterpret_cast<float*>(base + L.qs);
   po.kscale = reinterpret_cast<float*>(base + L.ks);
   po.sdecay = reinterpret_cast<float*>(base + L.sd);
+  const bool tc = scan_tc_ok(io, KD, VD, state, out, so) && L.total > L.qsq;
+  po.Qs = tc ? reinterpret_cast<__nv_bfloat16*>(base + L.qsq) : nullptr;
   const int nC = static_cast<int>(ceil_div(T, kC));
   constexpr int kPrepSmem = sizeof(PrepSmem<KD, VD>);
   constexpr int VC = 32, NG = 2;  // two 32-column groups per CTA
@@ -880,6 +1266,26 @@ int32_t launch_prefill(const GdnIO& io, int B, int T, int H, void* scratch, floa
   }
   gdn_chunk_prep_kernel<KD, VD><<<B * H * nC, 128, kPrepSmem, s>>>(io, B, T, H, po);
   count_launch();
+  if (tc) {
+    static bool tc_attr = false;
+    if (!tc_attr) {
+      int32_t st = set_smem(gdn_scan_tc_kernel, scan_tc::kSmem);
+      if (st) return st;
+      tc_attr = true;
+    }
+    CUtensorMap mkw, mqs, mk, maqk, mu;
+    if (!make_bf16_4d_map(&mkw, po.Kw, B, T, H, KD, kC) ||
+        !make_bf16_4d_map(&mqs, po.Qs, B, T, H, KD, kC) ||
+        !make_bf16_3d_map(&mk, io.k, B, T, static_cast<uint64_t>(H) * KD, io.sk, kC) ||
+        !make_bf16_2d_map(&maqk, po.Aqk, static_cast<uint64_t>(B) * H * nC * kC, kC, kC, kC, kC) ||
+        !make_bf16_4d_map(&mu, po.U, B, T, H, VD, kC))
+      return LLMYB_EUNSUPPORTED;
+    gdn_scan_tc_kernel<<<B * H * (VD / scan_tc::kVS), 192, scan_tc::kSmem, s>>>(
+        mkw, mqs, mk, maqk, mu, po.kscale, po.sdecay, io.gate, io.sg, B, T, H, VD, state, out, so,
+        dev_status);
+    count_launch();
+    return launch_status();
+  }
   gdn_chunk_scan_kernel<KD, VD, VC, NG><<<B * H * (VD / (VC * NG)), 128 * NG, kScanSmem, s>>>(
       io, B, T, H, po, state, out, so);
   count_launch();
@@ -953,7 +1359,8 @@ LLMYB_API int32_t llmyb_gdn_prefill(const void* q, int64_t q_stride, const void*
                                     const float* log_alpha, const uint8_t* reset, int32_t batch,
                                     int32_t seq, int32_t heads, int32_t key_dim,
                                     int32_t value_dim, float* state, void* out,
-                                    int64_t out_stride, void* scratch, void* stream) {
+                                    int64_t out_stride, void* scratch, int32_t* dev_status,
+                                    void* stream) {
   const GdnIO io = make_io(q, q_stride, k, k_stride, v, v_stride, gate, gate_stride, beta,
                            beta_stride, decay_logit, log_alpha, reset);
   int32_t st = check_io(io, key_dim, value_dim);
@@ -967,12 +1374,12 @@ LLMYB_API int32_t llmyb_gdn_prefill(const void* q, int64_t q_stride, const void*
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   auto* o = static_cast<__nv_bfloat16*>(out);
   if (key_dim == 64 && value_dim == 64)
-    return launch_prefill<64, 64>(io, batch, seq, heads, scratch, state, o, out_stride, s);
+    return launch_prefill<64, 64>(io, batch, seq, heads, scratch, state, o, out_stride, dev_status, s);
   if (key_dim == 128 && value_dim == 128)
-    return launch_prefill<128, 128>(io, batch, seq, heads, scratch, state, o, out_stride, s);
+    return launch_prefill<128, 128>(io, batch, seq, heads, scratch, state, o, out_stride, dev_status, s);
   if (key_dim == 64 && value_dim == 128)
-    return launch_prefill<64, 128>(io, batch, seq, heads, scratch, state, o, out_stride, s);
-  return launch_prefill<128, 64>(io, batch, seq, heads, scratch, state, o, out_stride, s);
+    return launch_prefill<64, 128>(io, batch, seq, heads, scratch, state, o, out_stride, dev_status, s);
+  return launch_prefill<128, 64>(io, batch, seq, heads, scratch, state, o, out_stride, dev_status, s);
 }
 
 // Conv gate + (optional) residual add + (optional) history roll; see

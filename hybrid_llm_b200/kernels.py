@@ -606,7 +606,7 @@ def gdn_prefill(q, k, v, gate, beta, state, *, decay_logit=None, log_alpha=None,
     decay_logit = None if decay_logit is None else decay_logit.to(torch.float32).contiguous()
     _native.call("llmyb_gdn_prefill", qp, qs, kp, ks, vp, vs, gp, gs, bp, bs, _ptr(decay_logit),
                  _ptr(la), _ptr(r), bsz, t, h, kd, vd, _ptr(state), _ptr(out), out.stride(-3),
-                 _ptr(scratch), _stream())
+                 _ptr(scratch), _ptr(device_status(q.device)), _stream())
     return out
 
 

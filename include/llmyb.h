@@ -295,14 +295,17 @@ int64_t llmyb_gdn_prefill_scratch_bytes(int32_t batch, int32_t seq, int32_t head
                                         int32_t key_dim, int32_t value_dim);
 
 /* Chunked (C = 64) scan over [B, T] tokens with resets: state [B,H,K,V] fp32
- * holds the initial state on entry and the final state on exit. */
+ * holds the initial state on entry and the final state on exit.  For K = 128
+ * (16-byte aligned gate/out/state/k rows) the scan runs on tcgen05 with the
+ * state in registers of its state warps; dev_status (nullable) receives
+ * LLMYB_ETIMEOUT if one of its pipeline waits expires. */
 int32_t llmyb_gdn_prefill(const void* q, int64_t q_stride, const void* k, int64_t k_stride,
                           const void* v, int64_t v_stride, const void* gate, int64_t gate_stride,
                           const void* beta, int64_t beta_stride, const float* decay_logit,
                           const float* log_alpha, const uint8_t* reset, int32_t batch,
                           int32_t seq, int32_t heads, int32_t key_dim, int32_t value_dim,
                           float* state, void* out, int64_t out_stride, void* scratch,
-                          void* stream);
+                          int32_t* dev_status, void* stream);
 
 /* GDN epilogue (gated_deltanet.py:254-276): y = y_proj * sigmoid(conv4(x)),
  * depthwise causal conv over the block input x [B,T,D] with weight [D,4]
