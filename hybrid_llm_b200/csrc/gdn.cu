@@ -835,12 +835,13 @@ __global__ void gdn_conv_roll_kernel(const __nv_bfloat16* __restrict__ x,
 //                D2  = K^T diag(ks) W        (the state update)
 //              S, W and X = diag(ks) W are fed as bf16 hi + lo pairs (two
 //              MMAs each), so the products keep about 16 mantissa bits.
-//   warps 2-5  state warps, one TMEM lane each (= key row of S, and token
-//              row of D1): the fp32 state slice S[key][64] lives in their
-//              registers for the whole sequence.  After D1: W = U - Kw S and
-//              X = ks W (token rows) into shared memory as MMA operands;
-//              after D1/D2: S <- sd S + D2, S hi/lo into shared memory, and O
-//              (D1 rows 64-127) times the gate to global memory.
+//   warps 2-9  state warps, two per TMEM lane quarter, each owning 32 of the
+//              64 columns of its lane's row (= key row of S, and token row of
+//              D1): the fp32 state slice S[key][..] lives in their registers
+//              for the whole sequence.  After D1: W = U - Kw S and X = ks W
+//              (token rows) into shared memory as MMA operands; after D1/D2:
+//              S <- sd S + D2, S hi/lo into shared memory, and O (D1 rows
+//              64-127) times the gate to global memory.
 // Operands written by threads use the 128-byte-swizzled MN-major layout of
 // an MMA B operand (row = K index, 64 N-columns per row).  TMEM: D1 columns
 // [0, 64), D2 [64, 128).  Every wait is bounded (1 s) and unwinds on timeout.
@@ -858,20 +859,21 @@ constexpr int kBar = kW + 32768;
 constexpr int kSmem = kBar + 256 + 1024;
 constexpr uint32_t kTmemCols = 128;
 
-// one 64-element row, scale * v (fp32 bit patterns), as bf16 hi and lo parts
-// into two swizzled operand tiles
-__device__ __forceinline__ void store_row_hilo(uint8_t* hi, uint8_t* lo, int row,
-                                               const uint32_t (&v)[2][32], float scale) {
+// one half row (32 elements, columns 32 half ..), scale * v (fp32 bit
+// patterns), as bf16 hi and lo parts into two swizzled operand tiles
+__device__ __forceinline__ void store_row_hilo(uint8_t* hi, uint8_t* lo, int row, int half,
+                                               const uint32_t (&v)[32], float scale) {
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
+  for (int jj = 0; jj < 4; ++jj) {
+    const int j = 4 * half + jj;
     uint4 h, l;
     uint32_t* hw = reinterpret_cast<uint32_t*>(&h);
     uint32_t* lw = reinterpret_cast<uint32_t*>(&l);
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      const int c0 = 8 * j + 2 * e;
-      const float a = __uint_as_float(v[c0 >> 5][c0 & 31]) * scale;
-      const float b = __uint_as_float(v[(c0 + 1) >> 5][(c0 + 1) & 31]) * scale;
+      const int c0 = 8 * jj + 2 * e;
+      const float a = __uint_as_float(v[c0]) * scale;
+      const float b = __uint_as_float(v[c0 + 1]) * scale;
       const __nv_bfloat162 hh = __floats2bfloat162_rn(a, b);
       const float2 hf = __bfloat1622float2(hh);
       hw[e] = *reinterpret_cast<const uint32_t*>(&hh);
@@ -884,7 +886,7 @@ __device__ __forceinline__ void store_row_hilo(uint8_t* hi, uint8_t* lo, int row
 }
 }  // namespace scan_tc
 
-__global__ void __launch_bounds__(192, 1) gdn_scan_tc_kernel(
+__global__ void __launch_bounds__(320, 1) gdn_scan_tc_kernel(
     const __grid_constant__ CUtensorMap map_kw, const __grid_constant__ CUtensorMap map_qs,
     const __grid_constant__ CUtensorMap map_k, const __grid_constant__ CUtensorMap map_aqk,
     const __grid_constant__ CUtensorMap map_u, const float* __restrict__ kscale,
@@ -918,11 +920,11 @@ __global__ void __launch_bounds__(192, 1) gdn_scan_tc_kernel(
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; ++i) {
       sm100::mbar_init(&st_full[i], 1);
-      sm100::mbar_init(&st_empty[i], 3);  // MMA commit + the two warps that read U
+      sm100::mbar_init(&st_empty[i], 5);  // MMA commit + the four warps that read U
     }
-    sm100::mbar_init(s_ready, 4);
+    sm100::mbar_init(s_ready, 8);
     sm100::mbar_init(d1_full, 1);
-    sm100::mbar_init(w_ready, 2);
+    sm100::mbar_init(w_ready, 4);
     sm100::mbar_init(d23_full, 1);
     sm100::mbar_init(mma_done, 1);
     *abort_flag = 0;
@@ -1030,25 +1032,26 @@ __global__ void __launch_bounds__(192, 1) gdn_scan_tc_kernel(
   } else {
     // ------------------------------------------------------ state warps
     const int q = warp & 3;
-    const int row = q * 32 + lane;  // TMEM lane: key row of S / D2, row of D1
-    const uint32_t t_lane = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
+    const int half = (warp - 2) >> 2;  // columns [32 half, 32 half + 32)
+    const int row = q * 32 + lane;     // TMEM lane: key row of S / D2, row of D1
+    const uint32_t t_lane = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + 32 * half;
     uint8_t* s_hi = smem + kS;
     uint8_t* s_lo = s_hi + 16384;
     uint8_t* w_hi = smem + kW;
     uint8_t* w_lo = w_hi + 8192;
     uint8_t* x_hi = w_hi + 16384;
     uint8_t* x_lo = w_hi + 24576;
-    float* Sg = state + (bh * 128 + row) * VD + v0;
-    uint32_t S[2][32];  // fp32 bit patterns of S[row][v0 .. v0 + 63]
+    float* Sg = state + (bh * 128 + row) * VD + v0 + 32 * half;
+    uint32_t S[32];  // fp32 bit patterns of S[row][v0 + 32 half ..]
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
+    for (int j = 0; j < 8; ++j) {
       const uint4 v = reinterpret_cast<const uint4*>(Sg)[j];
-      S[j >> 3][(4 * j) & 31] = v.x;
-      S[j >> 3][(4 * j + 1) & 31] = v.y;
-      S[j >> 3][(4 * j + 2) & 31] = v.z;
-      S[j >> 3][(4 * j + 3) & 31] = v.w;
+      S[4 * j] = v.x;
+      S[4 * j + 1] = v.y;
+      S[4 * j + 2] = v.z;
+      S[4 * j + 3] = v.w;
     }
-    store_row_hilo(s_hi, s_lo, row, S, 1.f);
+    store_row_hilo(s_hi, s_lo, row, half, S, 1.f);
     sm100::fence_proxy_async_smem();
     __syncwarp();
     if (lane == 0) sm100::mbar_arrive(s_ready);
@@ -1065,39 +1068,37 @@ __global__ void __launch_bounds__(192, 1) gdn_scan_tc_kernel(
         if (row < 64 && t0 + kC + row < T) ks_next = __ldg(kscale + bh * T + t0 + kC + row);
         sd_next = __ldg(sdecay + bh * nC + c + 1);
       }
-      // ---- W = U - Kw S and X = ks W (token rows, warps of lane quarters 0-1)
+      // ---- W = U - Kw S and X = ks W (token rows: lane quarters 0-1)
       // (U of this stage is complete once its "full" phase is)
       if (row < 64 && !sm100::mbar_wait_warp(&st_full[s], (c >> 1) & 1, dev_status, abort_flag))
         break;
       if (!sm100::mbar_wait_warp(d1_full, c & 1, dev_status, abort_flag)) break;
       sm100::tc_fence_after();
       if (row < 64) {
-        uint32_t p[2][32];
-        sm100::tmem_ld_32x32b_x32(t_lane, p[0]);
-        sm100::tmem_ld_32x32b_x32(t_lane + 32, p[1]);
+        uint32_t p[32];
+        sm100::tmem_ld_32x32b_x32(t_lane, p);
         const int t = row;
-        const float ks = ks_cur;
-        sm100::tmem_ld_wait();
-        sm100::tmem_regs_ready(p[0]);
-        sm100::tmem_regs_ready(p[1]);
         const uint8_t* urow = smem + s * kStage + kU + t * 128;
+        uint4 u4[4];
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj)
+          u4[jj] = *reinterpret_cast<const uint4*>(urow + (((4 * half + jj) ^ (t & 7)) << 4));
+        sm100::tmem_ld_wait();
+        sm100::tmem_regs_ready(p);
         // W = U - Kw S in place of the loaded product
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const uint4 u = *reinterpret_cast<const uint4*>(urow + ((j ^ (t & 7)) << 4));
-          const uint32_t uw[4] = {u.x, u.y, u.z, u.w};
+        for (int jj = 0; jj < 4; ++jj) {
+          const uint32_t uw[4] = {u4[jj].x, u4[jj].y, u4[jj].z, u4[jj].w};
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const float2 uf = unpack_bf16x2(uw[e]);
-            const int col = 8 * j + 2 * e;
-            uint32_t& p0 = p[col >> 5][col & 31];
-            uint32_t& p1 = p[(col + 1) >> 5][(col + 1) & 31];
-            p0 = __float_as_uint(uf.x - __uint_as_float(p0));
-            p1 = __float_as_uint(uf.y - __uint_as_float(p1));
+            const int col = 8 * jj + 2 * e;
+            p[col] = __float_as_uint(uf.x - __uint_as_float(p[col]));
+            p[col + 1] = __float_as_uint(uf.y - __uint_as_float(p[col + 1]));
           }
         }
-        store_row_hilo(w_hi, w_lo, t, p, 1.f);
-        store_row_hilo(x_hi, x_lo, t, p, ks);  // X = diag(ks) W
+        store_row_hilo(w_hi, w_lo, t, half, p, 1.f);
+        store_row_hilo(x_hi, x_lo, t, half, p, ks_cur);  // X = diag(ks) W
         sm100::fence_proxy_async_smem();
         sm100::tc_fence_before();
         __syncwarp();
@@ -1109,28 +1110,19 @@ __global__ void __launch_bounds__(192, 1) gdn_scan_tc_kernel(
       // ---- S <- sd S + D2; O = D1 rows 64-127 (read before D1 is released)
       if (!sm100::mbar_wait_warp(d23_full, c & 1, dev_status, abort_flag)) break;
       sm100::tc_fence_after();
-      const float sd = sd_cur;
+      uint32_t o[32];
       {
-        uint32_t d2[2][32];
-        sm100::tmem_ld_32x32b_x32(t_lane + 64, d2[0]);
-        sm100::tmem_ld_32x32b_x32(t_lane + 96, d2[1]);
+        uint32_t d2[32];
+        sm100::tmem_ld_32x32b_x32(t_lane + 64, d2);
+        if (row >= 64) sm100::tmem_ld_32x32b_x32(t_lane, o);
         sm100::tmem_ld_wait();
-        sm100::tmem_regs_ready(d2[0]);
-        sm100::tmem_regs_ready(d2[1]);
+        sm100::tmem_regs_ready(d2);
+        if (row >= 64) sm100::tmem_regs_ready(o);
 #pragma unroll
-        for (int j = 0; j < 64; ++j)
-          S[j >> 5][j & 31] = __float_as_uint(sd * __uint_as_float(S[j >> 5][j & 31]) +
-                                              __uint_as_float(d2[j >> 5][j & 31]));
+        for (int j = 0; j < 32; ++j)
+          S[j] = __float_as_uint(sd_cur * __uint_as_float(S[j]) + __uint_as_float(d2[j]));
       }
-      if (c + 1 < nC) store_row_hilo(s_hi, s_lo, row, S, 1.f);
-      uint32_t o[2][32];
-      if (row >= 64) {
-        sm100::tmem_ld_32x32b_x32(t_lane, o[0]);
-        sm100::tmem_ld_32x32b_x32(t_lane + 32, o[1]);
-        sm100::tmem_ld_wait();
-        sm100::tmem_regs_ready(o[0]);
-        sm100::tmem_regs_ready(o[1]);
-      }
+      if (c + 1 < nC) store_row_hilo(s_hi, s_lo, row, half, S, 1.f);
       sm100::fence_proxy_async_smem();
       sm100::tc_fence_before();
       __syncwarp();
@@ -1138,26 +1130,26 @@ __global__ void __launch_bounds__(192, 1) gdn_scan_tc_kernel(
       if (row >= 64) {
         const int t = row - 64;
         if (t < n) {
-          uint4* dst = reinterpret_cast<uint4*>(out + (b * static_cast<int64_t>(T) + t0 + t) * so +
-                                                h * VD + v0);
-          const uint4* gr = reinterpret_cast<const uint4*>(
-              gate + (b * static_cast<int64_t>(T) + t0 + t) * sg + h * VD + v0);
+          const int64_t orow = b * static_cast<int64_t>(T) + t0 + t;
+          uint4* dst = reinterpret_cast<uint4*>(out + orow * so + h * VD + v0 + 32 * half);
+          const uint4* gr =
+              reinterpret_cast<const uint4*>(gate + orow * sg + h * VD + v0 + 32 * half);
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const uint4 g4 = __ldg(gr + j);
+          for (int jj = 0; jj < 4; ++jj) {
+            const uint4 g4 = __ldg(gr + jj);
             const uint32_t gw[4] = {g4.x, g4.y, g4.z, g4.w};
             uint4 r4;
             uint32_t* rw = reinterpret_cast<uint32_t*>(&r4);
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-              const int col = 8 * j + 2 * e;
+              const int col = 8 * jj + 2 * e;
               const float2 g2 = unpack_bf16x2(gw[e]);
               // reference order: out.to(hidden dtype) * gate
-              const float o0 = bf2f(f2bf(__uint_as_float(o[col >> 5][col & 31])));
-              const float o1 = bf2f(f2bf(__uint_as_float(o[(col + 1) >> 5][(col + 1) & 31])));
+              const float o0 = bf2f(f2bf(__uint_as_float(o[col])));
+              const float o1 = bf2f(f2bf(__uint_as_float(o[col + 1])));
               rw[e] = pack_bf16x2(o0 * g2.x, o1 * g2.y);
             }
-            dst[j] = r4;
+            dst[jj] = r4;
           }
         }
       }
@@ -1165,10 +1157,9 @@ __global__ void __launch_bounds__(192, 1) gdn_scan_tc_kernel(
       sd_cur = sd_next;
     }
 #pragma unroll
-    for (int j = 0; j < 16; ++j)
-      reinterpret_cast<uint4*>(Sg)[j] =
-          make_uint4(S[j >> 3][(4 * j) & 31], S[j >> 3][(4 * j + 1) & 31],
-                     S[j >> 3][(4 * j + 2) & 31], S[j >> 3][(4 * j + 3) & 31]);
+    for (int j = 0; j < 8; ++j)
+      reinterpret_cast<uint4*>(Sg)[j] = make_uint4(S[4 * j], S[4 * j + 1], S[4 * j + 2],
+                                                   S[4 * j + 3]);
   }
   sm100::tc_fence_before();
   __syncthreads();
@@ -1280,7 +1271,7 @@ int32_t launch_prefill(const GdnIO& io, int B, int T, int H, void* scratch, floa
         !make_bf16_2d_map(&maqk, po.Aqk, static_cast<uint64_t>(B) * H * nC * kC, kC, kC, kC, kC) ||
         !make_bf16_4d_map(&mu, po.U, B, T, H, VD, kC))
       return LLMYB_EUNSUPPORTED;
-    gdn_scan_tc_kernel<<<B * H * (VD / scan_tc::kVS), 192, scan_tc::kSmem, s>>>(
+    gdn_scan_tc_kernel<<<B * H * (VD / scan_tc::kVS), 320, scan_tc::kSmem, s>>>(
         mkw, mqs, mk, maqk, mu, po.kscale, po.sdecay, io.gate, io.sg, B, T, H, VD, state, out, so,
         dev_status);
     count_launch();
