@@ -206,6 +206,27 @@ struct PrepSmem {
   int wseg[2];
 };
 
+// Output tile [64][W] bf16 staged in shared memory with the 16-byte pieces
+// of row t XOR-swizzled by t (conflict-free fragment writes and row reads).
+template <int W>
+__device__ __forceinline__ void stage_pair(uint8_t* tile, int t, int col, uint32_t v) {
+  constexpr int kCh = W / 8;
+  const int ch = (col >> 3) ^ (t & (kCh - 1));
+  *reinterpret_cast<uint32_t*>(tile + t * (W * 2) + ch * 16 + (col & 7) * 2) = v;
+}
+
+// rows t < n of the staged tile to dst + t * ld (16-byte stores)
+template <int W>
+__device__ __forceinline__ void store_staged(const uint8_t* tile, __nv_bfloat16* dst, int64_t ld,
+                                             int n, int tid) {
+  constexpr int kCh = W / 8;
+  for (int i = tid; i < n * kCh; i += 128) {
+    const int t = i / kCh, ch = i - t * kCh;
+    const uint4 v = *reinterpret_cast<const uint4*>(tile + t * (W * 2) + ((ch ^ (t & (kCh - 1))) * 16));
+    *reinterpret_cast<uint4*>(dst + t * ld + ch * 8) = v;
+  }
+}
+
 template <int KD, int VD>
 __global__ void __launch_bounds__(128) gdn_chunk_prep_kernel(GdnIO io, int B, int T, int H,
                                                              PrepOut po) {
@@ -237,6 +258,17 @@ __global__ void __launch_bounds__(128) gdn_chunk_prep_kernel(GdnIO io, int B, in
     mma::cp_async16(&sQ[r * SM::LK + cc], io.q + tok * io.sq + h * KD + cc, ok);
   }
   mma::cp_async_commit();
+  // V into registers now (it lands in shared memory after the triangular
+  // solve, whose space it reuses), so its latency overlaps the whole solve
+  constexpr int kVPer = kC * (VD / 8) / 128;
+  uint4 vreg[kVPer];
+#pragma unroll
+  for (int u = 0; u < kVPer; ++u) {
+    const int i = tid + 128 * u;
+    const int r = i / (VD / 8), cc = (i % (VD / 8)) * 8;
+    vreg[u] = r < n ? __ldg(reinterpret_cast<const uint4*>(io.v + (tok0 + r) * io.sv + h * VD + cc))
+                    : make_uint4(0, 0, 0, 0);
+  }
   // per-token scalars, one thread per token; cumulative sums by warp scans
   // (decays in log2 units, so every Gamma ratio below is one exp2)
   float la = 0.f, la_own = 0.f, bt = 0.f;
@@ -402,12 +434,12 @@ __global__ void __launch_bounds__(128) gdn_chunk_prep_kernel(GdnIO io, int B, in
   }
 
   // ---- V into the R space (R is dead); T1/T2 into the A space (A is dead)
-  for (int i = tid; i < kC * (VD / 8); i += 128) {
+#pragma unroll
+  for (int u = 0; u < kVPer; ++u) {
+    const int i = tid + 128 * u;
     const int r = i / (VD / 8), cc = (i % (VD / 8)) * 8;
-    const bool ok = r < n;
-    mma::cp_async16(&sV[r * SM::LV + cc], io.v + (tok0 + (ok ? r : 0)) * io.sv + h * VD + cc, ok);
+    *reinterpret_cast<uint4*>(&sV[r * SM::LV + cc]) = vreg[u];
   }
-  mma::cp_async_commit();
   for (int i = tid; i < kC * kC; i += 128) {
     const int r = i / kC, cc = i % kC;
     const float tv = sm.Tm[r * SM::LF + cc];
@@ -427,8 +459,10 @@ __global__ void __launch_bounds__(128) gdn_chunk_prep_kernel(GdnIO io, int B, in
   mma::cp_async_wait<0>();
   __syncthreads();
 
-  // ---- U = T1 V  (64 x VD), Kw = T2 K (64 x KD): rows 16*warp..
+  // ---- U = T1 V  (64 x VD), Kw = T2 K (64 x KD): rows 16*warp.., staged in
+  // the (dead) T space and written as whole 16-byte row pieces
   {
+    uint8_t* s_out = reinterpret_cast<uint8_t*>(sm.Tm);
     uint32_t a1[4][4], a2[4][4];
 #pragma unroll
     for (int ks = 0; ks < 4; ++ks) {
@@ -449,14 +483,14 @@ __global__ void __launch_bounds__(128) gdn_chunk_prep_kernel(GdnIO io, int B, in
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
         const int t = r + half * 8;
-        if (t < n) {
-          const int col = nb * 8 + (lane & 3) * 2;
-          __nv_bfloat16* dst = po.U + ((tok0 + t) * H + h) * VD + col;
-          *reinterpret_cast<uint32_t*>(dst) = pack_bf16x2(acc0[half * 2], acc0[half * 2 + 1]);
-          *reinterpret_cast<uint32_t*>(dst + 8) = pack_bf16x2(acc1[half * 2], acc1[half * 2 + 1]);
-        }
+        const int col = nb * 8 + (lane & 3) * 2;
+        stage_pair<VD>(s_out, t, col, pack_bf16x2(acc0[half * 2], acc0[half * 2 + 1]));
+        stage_pair<VD>(s_out, t, col + 8, pack_bf16x2(acc1[half * 2], acc1[half * 2 + 1]));
       }
     }
+    __syncthreads();
+    store_staged<VD>(s_out, po.U + (tok0 * H + h) * VD, static_cast<int64_t>(H) * VD, n, tid);
+    __syncthreads();
 #pragma unroll
     for (int nb = 0; nb < KD / 8; nb += 2) {
       float acc0[4] = {0, 0, 0, 0}, acc1[4] = {0, 0, 0, 0};
@@ -470,14 +504,13 @@ __global__ void __launch_bounds__(128) gdn_chunk_prep_kernel(GdnIO io, int B, in
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
         const int t = r + half * 8;
-        if (t < n) {
-          const int col = nb * 8 + (lane & 3) * 2;
-          __nv_bfloat16* dst = po.Kw + ((tok0 + t) * H + h) * KD + col;
-          *reinterpret_cast<uint32_t*>(dst) = pack_bf16x2(acc0[half * 2], acc0[half * 2 + 1]);
-          *reinterpret_cast<uint32_t*>(dst + 8) = pack_bf16x2(acc1[half * 2], acc1[half * 2 + 1]);
-        }
+        const int col = nb * 8 + (lane & 3) * 2;
+        stage_pair<KD>(s_out, t, col, pack_bf16x2(acc0[half * 2], acc0[half * 2 + 1]));
+        stage_pair<KD>(s_out, t, col + 8, pack_bf16x2(acc1[half * 2], acc1[half * 2 + 1]));
       }
     }
+    __syncthreads();
+    store_staged<KD>(s_out, po.Kw + (tok0 * H + h) * KD, static_cast<int64_t>(H) * KD, n, tid);
   }
 }
 
