@@ -323,10 +323,34 @@ def secondary_moe(p: dict, reps: int = 10) -> dict:
     t = float(np.median(times)) * 1e-3
     flops = 2.0 * n * k * 3 * f * d
     counts = plan.counts.cpu().tolist()
+    # the routed experts alone (same plan): gather + the two tcgen05 grouped GEMMs
+    rows = n * k
+    y_rows = torch.empty(rows, d, device="cuda", dtype=torch.bfloat16)
+    escratch = torch.empty(kernels.grouped_scratch_bytes(rows, d, f), dtype=torch.uint8,
+                           device="cuda")
+    experts = lambda: kernels.moe_grouped_experts_to(
+        x, rows, plan.perm_token, plan.perm_prob, plan.offsets, plan.tile_offsets, plan.tile_m,
+        w13, wd, escratch, y_rows)
+    for _ in range(3):
+        experts()
+    etimes = []
+    for _ in range(max(1, reps)):
+        flush.zero_()
+        a, b = _events()
+        a.record()
+        experts()
+        b.record()
+        torch.cuda.synchronize()
+        etimes.append(a.elapsed_time(b))
+    te = float(np.median(etimes)) * 1e-3
     return {"workload": "isolated MoE layer 16384x1024, 32 experts top-4, F=512, Zipf(1.1) bias",
             "ms": t * 1e3, "tflops": flops / t / 1e12,
             "frac_of_bf16_peak": flops / t / 1e12 / p["bf16_tflops"],
             "includes": "router logits GEMM + top-k/plan + gather + 2 grouped GEMMs + combine",
+            "experts_ms": te * 1e3, "experts_tflops": flops / te / 1e12,
+            "experts_frac_of_bf16_peak": flops / te / 1e12 / p["bf16_tflops"],
+            "experts_includes": "row gather + GEMM1 (SwiGLU epilogue) + GEMM2 (probability "
+                                "epilogue), L2 flushed before each call",
             "expert_load": counts}
 
 

@@ -406,31 +406,52 @@ __global__ void __launch_bounds__(128) gdn_chunk_prep_kernel(GdnIO io, int B, in
     if ((cc >> 4) > (r >> 4)) sm.Tm[r * SM::LF + cc] = 0.f;
   }
   __syncthreads();
-  for (int bi = 1; bi < 4; ++bi) {
-    // R = A[bi, <bi] T[<bi, <bi], then T[bi, <bi] = -T[bi, bi] R (16-wide
-    // unrolled dot products, four partial sums each)
-    for (int idx = tid; idx < 16 * 16 * bi; idx += 128) {
-      const int r = bi * 16 + idx / (16 * bi);
-      const int cc = idx % (16 * bi);
-      float a4[4] = {0.f, 0.f, 0.f, 0.f};
-      for (int kb = cc >> 4; kb < bi; ++kb) {
-#pragma unroll
-        for (int k = 0; k < 16; ++k)
-          a4[k & 3] += sA[r * SM::LF + kb * 16 + k] * sm.Tm[(kb * 16 + k) * SM::LF + cc];
+  // off-diagonal blocks, block row by block row, on the tensor cores in tf32
+  // (10-bit mantissas, finer than the bf16 rounding T gets afterwards):
+  // R = A[bi, <bi] T[<bi, <bi], then T[bi, <bi] = -T[bi, bi] R; warp w takes
+  // the 8-column output tiles w, w+4, ...
+  {
+    const int g = lane >> 2, tq = lane & 3;
+    for (int bi = 1; bi < 4; ++bi) {
+      const int r0 = bi * 16;
+      for (int nt = warp; nt < 2 * bi; nt += 4) {
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int ks = 0; ks < 2 * bi; ++ks) {  // T is zero above its diagonal blocks
+          const uint32_t a[4] = {
+              mma::to_tf32(sA[(r0 + g) * SM::LF + 8 * ks + tq]),
+              mma::to_tf32(sA[(r0 + g + 8) * SM::LF + 8 * ks + tq]),
+              mma::to_tf32(sA[(r0 + g) * SM::LF + 8 * ks + tq + 4]),
+              mma::to_tf32(sA[(r0 + g + 8) * SM::LF + 8 * ks + tq + 4])};
+          const uint32_t bb[2] = {mma::to_tf32(sm.Tm[(8 * ks + tq) * SM::LF + 8 * nt + g]),
+                                  mma::to_tf32(sm.Tm[(8 * ks + tq + 4) * SM::LF + 8 * nt + g])};
+          mma::mma_tf32(acc, a, bb);
+        }
+        sR[(r0 + g) * SM::LF + 8 * nt + 2 * tq] = acc[0];
+        sR[(r0 + g) * SM::LF + 8 * nt + 2 * tq + 1] = acc[1];
+        sR[(r0 + g + 8) * SM::LF + 8 * nt + 2 * tq] = acc[2];
+        sR[(r0 + g + 8) * SM::LF + 8 * nt + 2 * tq + 1] = acc[3];
       }
-      sR[r * SM::LF + cc] = (a4[0] + a4[1]) + (a4[2] + a4[3]);
-    }
-    __syncthreads();
-    for (int idx = tid; idx < 16 * 16 * bi; idx += 128) {
-      const int r = bi * 16 + idx / (16 * bi);
-      const int cc = idx % (16 * bi);
-      float a4[4] = {0.f, 0.f, 0.f, 0.f};
+      __syncthreads();
+      for (int nt = warp; nt < 2 * bi; nt += 4) {
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int k = 0; k < 16; ++k)
-        a4[k & 3] += sm.Tm[r * SM::LF + bi * 16 + k] * sR[(bi * 16 + k) * SM::LF + cc];
-      sm.Tm[r * SM::LF + cc] = -((a4[0] + a4[1]) + (a4[2] + a4[3]));
+        for (int ks = 0; ks < 2; ++ks) {
+          const uint32_t a[4] = {
+              mma::to_tf32(sm.Tm[(r0 + g) * SM::LF + r0 + 8 * ks + tq]),
+              mma::to_tf32(sm.Tm[(r0 + g + 8) * SM::LF + r0 + 8 * ks + tq]),
+              mma::to_tf32(sm.Tm[(r0 + g) * SM::LF + r0 + 8 * ks + tq + 4]),
+              mma::to_tf32(sm.Tm[(r0 + g + 8) * SM::LF + r0 + 8 * ks + tq + 4])};
+          const uint32_t bb[2] = {mma::to_tf32(sR[(r0 + 8 * ks + tq) * SM::LF + 8 * nt + g]),
+                                  mma::to_tf32(sR[(r0 + 8 * ks + tq + 4) * SM::LF + 8 * nt + g])};
+          mma::mma_tf32(acc, a, bb);
+        }
+        sm.Tm[(r0 + g) * SM::LF + 8 * nt + 2 * tq] = -acc[0];
+        sm.Tm[(r0 + g) * SM::LF + 8 * nt + 2 * tq + 1] = -acc[1];
+        sm.Tm[(r0 + g + 8) * SM::LF + 8 * nt + 2 * tq] = -acc[2];
+        sm.Tm[(r0 + g + 8) * SM::LF + 8 * nt + 2 * tq + 1] = -acc[3];
+      }
+      __syncthreads();
     }
-    __syncthreads();
   }
 
   // ---- V into the R space (R is dead); T1/T2 into the A space (A is dead)

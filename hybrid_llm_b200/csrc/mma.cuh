@@ -83,6 +83,26 @@ __device__ __forceinline__ void load_b_kn(uint32_t (&b)[4], const __nv_bfloat16*
 }
 
 // 16-byte asynchronous global -> shared copy; src_bytes = 0 zero-fills.
+// fp32 -> tf32 (round to nearest, ties away), kept in a 32-bit register
+__device__ __forceinline__ uint32_t to_tf32(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return r;
+}
+
+// D (16x8 fp32) += A (16x8 tf32, row-major) B (8x8 tf32), mma.m16n8k8 fragments:
+//   a[0]: (g, t)  a[1]: (g+8, t)  a[2]: (g, t+4)  a[3]: (g+8, t+4)
+//   b[0]: (k=t, n=g)  b[1]: (k=t+4, n=g)
+//   d[0..1]: (g, 2t..2t+1)  d[2..3]: (g+8, 2t..)      with g = lane / 4, t = lane % 4.
+__device__ __forceinline__ void mma_tf32(float (&d)[4], const uint32_t (&a)[4],
+                                         const uint32_t (&b)[2]) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+
 __device__ __forceinline__ void cp_async16(void* dst, const void* src, bool valid) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_addr(dst)), "l"(src),
                "r"(valid ? 16 : 0)
