@@ -887,8 +887,10 @@ __global__ void gdn_conv_roll_kernel(const __nv_bfloat16* __restrict__ x,
 //                D1  = [Kw; Qs] S            (rows 0-63: Kw S, rows 64-127: Qs S)
 //                D1 += [0; Aqk] W            (rows 64-127 become O)
 //                D2  = K^T diag(ks) W        (the state update)
-//              S, W and X = diag(ks) W are fed as bf16 hi + lo pairs (two
-//              MMAs each), so the products keep about 16 mantissa bits.
+//              S, W and X = diag(ks) W are bf16 hi + lo pairs stored as the
+//              two 64-column blocks of one N = 128 operand, so each product is
+//              one MMA per K step with the hi and lo results side by side in
+//              TMEM (summed by the state warps): about 16 mantissa bits.
 //   warps 2-9  state warps, two per TMEM lane quarter, each owning 32 of the
 //              64 columns of its lane's row (= key row of S, and token row of
 //              D1): the fp32 state slice S[key][..] lives in their registers
@@ -898,7 +900,8 @@ __global__ void gdn_conv_roll_kernel(const __nv_bfloat16* __restrict__ x,
 //              64-127) times the gate to global memory.
 // Operands written by threads use the 128-byte-swizzled MN-major layout of
 // an MMA B operand (row = K index, 64 N-columns per row).  TMEM: D1 columns
-// [0, 64), D2 [64, 128).  Every wait is bounded (1 s) and unwinds on timeout.
+// [0, 128) (hi | lo), D2 [128, 256).  Every wait is bounded (1 s) and unwinds
+// on timeout.
 namespace scan_tc {
 constexpr int kVS = 64;                                     // value columns per CTA
 constexpr int kA1 = 0;                                      // [Kw; Qs]: 2 x (128 rows x 64) bf16
@@ -911,7 +914,7 @@ constexpr int kS = 2 * kStage;                              // S hi | S lo  [128
 constexpr int kW = kS + 32768;                              // W hi | W lo | X hi | X lo  [64][64]
 constexpr int kBar = kW + 32768;
 constexpr int kSmem = kBar + 256 + 1024;
-constexpr uint32_t kTmemCols = 128;
+constexpr uint32_t kTmemCols = 256;
 
 // one half row (32 elements, columns 32 half ..), scale * v (fp32 bit
 // patterns), as bf16 hi and lo parts into two swizzled operand tiles
@@ -1029,9 +1032,10 @@ __global__ void __launch_bounds__(320, 1) gdn_scan_tc_kernel(
                               nullptr);
   } else if (warp == 1) {
     // ------------------------------------------------------------- MMA
-    constexpr uint32_t idesc = sm100::make_idesc_bf16_f32(128, kVS) | sm100::kIdescBMajorMN;
+    // N = 128: the hi and lo 64-column blocks of S / W / X in one operand
+    constexpr uint32_t idesc = sm100::make_idesc_bf16_f32(128, 2 * kVS) | sm100::kIdescBMajorMN;
     constexpr uint32_t idesc_t = idesc | (1u << 15);  // A (K^T) MN-major too
-    const uint32_t t_d1 = tmem_base, t_d2 = tmem_base + 64;
+    const uint32_t t_d1 = tmem_base, t_d2 = tmem_base + 128;
     const uint32_t s_hi = sm100::smem_u32(smem + kS), s_lo = s_hi + 16384;
     const uint32_t w_hi = sm100::smem_u32(smem + kW), w_lo = w_hi + 8192;
     const uint32_t x_hi = w_hi + 16384, x_lo = w_hi + 24576;
@@ -1043,16 +1047,12 @@ __global__ void __launch_bounds__(320, 1) gdn_scan_tc_kernel(
         break;
       sm100::tc_fence_after();
       if (lane == 0) {
-#pragma unroll 1
-        for (int part = 0; part < 2; ++part) {
-          const uint32_t sb = part == 0 ? s_hi : s_lo;
 #pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {
-            const uint64_t ad =
-                sm100::make_sw128_kmajor_desc(st + kA1 + (kk >> 2) * 16384 + (kk & 3) * 32);
-            const uint64_t bd = sm100::make_sw128_desc(sb + kk * 2048, 8192, 1024);
-            sm100::umma_bf16_ss(t_d1, ad, bd, idesc, (part | kk) != 0 ? 1u : 0u);
-          }
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint64_t ad =
+              sm100::make_sw128_kmajor_desc(st + kA1 + (kk >> 2) * 16384 + (kk & 3) * 32);
+          const uint64_t bd = sm100::make_sw128_desc(s_hi + kk * 2048, s_lo - s_hi, 1024);
+          sm100::umma_bf16_ss(t_d1, ad, bd, idesc, kk != 0 ? 1u : 0u);
         }
         sm100::umma_commit(d1_full);
       }
@@ -1060,20 +1060,16 @@ __global__ void __launch_bounds__(320, 1) gdn_scan_tc_kernel(
       if (!sm100::mbar_wait_warp(w_ready, c & 1, dev_status, abort_flag)) break;
       sm100::tc_fence_after();
       if (lane == 0) {
-#pragma unroll 1
-        for (int part = 0; part < 2; ++part) {
-          const uint32_t wb = part == 0 ? w_hi : w_lo, xb = part == 0 ? x_hi : x_lo;
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            // D1 rows 64-127 += Aqk W (rows 0-63 of [0; Aqk] are zero)
-            const uint64_t a3 = sm100::make_sw128_kmajor_desc(st + kA3 + kk * 32);
-            sm100::umma_bf16_ss(t_d1, a3, sm100::make_sw128_desc(wb + kk * 2048, 8192, 1024),
-                                idesc, 1u);
-            // D2 = K^T X: A = K [token][key] read MN-major (64-key blocks 8 KB apart)
-            const uint64_t a2 = sm100::make_sw128_desc(st + kA2 + kk * 2048, 8192, 1024);
-            sm100::umma_bf16_ss(t_d2, a2, sm100::make_sw128_desc(xb + kk * 2048, 8192, 1024),
-                                idesc_t, (part | kk) != 0 ? 1u : 0u);
-          }
+        for (int kk = 0; kk < 4; ++kk) {
+          // D1 rows 64-127 += Aqk W (rows 0-63 of [0; Aqk] are zero)
+          const uint64_t a3 = sm100::make_sw128_kmajor_desc(st + kA3 + kk * 32);
+          sm100::umma_bf16_ss(t_d1, a3, sm100::make_sw128_desc(w_hi + kk * 2048, w_lo - w_hi, 1024),
+                              idesc, 1u);
+          // D2 = K^T X: A = K [token][key] read MN-major (64-key blocks 8 KB apart)
+          const uint64_t a2 = sm100::make_sw128_desc(st + kA2 + kk * 2048, 8192, 1024);
+          sm100::umma_bf16_ss(t_d2, a2, sm100::make_sw128_desc(x_hi + kk * 2048, x_lo - x_hi, 1024),
+                              idesc_t, kk != 0 ? 1u : 0u);
         }
         sm100::umma_commit(d23_full);
         sm100::umma_commit(&st_empty[s]);
@@ -1129,8 +1125,9 @@ __global__ void __launch_bounds__(320, 1) gdn_scan_tc_kernel(
       if (!sm100::mbar_wait_warp(d1_full, c & 1, dev_status, abort_flag)) break;
       sm100::tc_fence_after();
       if (row < 64) {
-        uint32_t p[32];
+        uint32_t p[32], plo[32];
         sm100::tmem_ld_32x32b_x32(t_lane, p);
+        sm100::tmem_ld_32x32b_x32(t_lane + 64, plo);
         const int t = row;
         const uint8_t* urow = smem + s * kStage + kU + t * 128;
         uint4 u4[4];
@@ -1139,6 +1136,10 @@ __global__ void __launch_bounds__(320, 1) gdn_scan_tc_kernel(
           u4[jj] = *reinterpret_cast<const uint4*>(urow + (((4 * half + jj) ^ (t & 7)) << 4));
         sm100::tmem_ld_wait();
         sm100::tmem_regs_ready(p);
+        sm100::tmem_regs_ready(plo);
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          p[j] = __float_as_uint(__uint_as_float(p[j]) + __uint_as_float(plo[j]));
         // W = U - Kw S in place of the loaded product
 #pragma unroll
         for (int jj = 0; jj < 4; ++jj) {
@@ -1166,15 +1167,27 @@ __global__ void __launch_bounds__(320, 1) gdn_scan_tc_kernel(
       sm100::tc_fence_after();
       uint32_t o[32];
       {
-        uint32_t d2[32];
-        sm100::tmem_ld_32x32b_x32(t_lane + 64, d2);
-        if (row >= 64) sm100::tmem_ld_32x32b_x32(t_lane, o);
+        uint32_t d2[32], d2lo[32];
+        sm100::tmem_ld_32x32b_x32(t_lane + 128, d2);
+        sm100::tmem_ld_32x32b_x32(t_lane + 192, d2lo);
         sm100::tmem_ld_wait();
         sm100::tmem_regs_ready(d2);
-        if (row >= 64) sm100::tmem_regs_ready(o);
+        sm100::tmem_regs_ready(d2lo);
 #pragma unroll
         for (int j = 0; j < 32; ++j)
-          S[j] = __float_as_uint(sd_cur * __uint_as_float(S[j]) + __uint_as_float(d2[j]));
+          S[j] = __float_as_uint(sd_cur * __uint_as_float(S[j]) +
+                                 (__uint_as_float(d2[j]) + __uint_as_float(d2lo[j])));
+      }
+      if (row >= 64) {
+        uint32_t olo[32];
+        sm100::tmem_ld_32x32b_x32(t_lane, o);
+        sm100::tmem_ld_32x32b_x32(t_lane + 64, olo);
+        sm100::tmem_ld_wait();
+        sm100::tmem_regs_ready(o);
+        sm100::tmem_regs_ready(olo);
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          o[j] = __float_as_uint(__uint_as_float(o[j]) + __uint_as_float(olo[j]));
       }
       if (c + 1 < nC) store_row_hilo(s_hi, s_lo, row, half, S, 1.f);
       sm100::fence_proxy_async_smem();
