@@ -50,8 +50,9 @@ class LoopedHybridModel:
         self.cfg: HybridConfig = weights.cfg
         self.device = weights.embed.device
         self.ep = ep
-        # decode expert kernels: "auto", "grouped" (tcgen05 GEMMs) or "decode"
-        # (weight streaming); a fixed choice makes runs comparable bit for bit
+        # expert kernels of prefill and decode: "auto", "grouped" (tcgen05 GEMMs)
+        # or "decode" (weight streaming); a fixed choice makes a single-device
+        # and an expert-parallel run comparable bit for bit
         self.expert_path = "auto"
         # small-batch decode on the fused kernels (decode_norm_gemv /
         # decode_out_router) when the shapes allow; False forces the unfused path
@@ -73,18 +74,17 @@ class LoopedHybridModel:
         beta = proj[..., 2 * hk + 2 * hv:2 * hk + 2 * hv + h]
         return q, k, v, gate, beta
 
-    def _moe(self, blk: Block, m_bf: torch.Tensor, m_f32: torch.Tensor) -> torch.Tensor:
-        """SparseMoE.forward without shared experts (moe.py:172-204)."""
+    def _moe(self, blk: Block, m_bf: torch.Tensor, m_f32: torch.Tensor):
+        """SparseMoE.forward without shared experts (moe.py:172-204): the routed
+        expert rows and the plan whose per-token sum is the combine (added to
+        the residual stream by the next add_rmsnorm_routed)."""
         c = self.cfg
         r_in = torch.empty_like(m_f32)
         # ContextAwareRouter: local = RMSNorm(hidden); logits = W local (context_router.py:62-72)
         kernels.add_rmsnorm(m_f32, None, blk.moe.router_norm, c.rms_eps, out_f32=r_in)
         logits = torch.mm(r_in, blk.moe.router.t())
         plan = kernels.route(logits, c.moe_top_k)
-        if self.ep is not None:
-            res = self.ep.run(m_bf, plan, blk.moe.w13, blk.moe.w2)
-            return res.y_rows, res.plan_for_combine(plan)
-        return kernels.moe_grouped(m_bf, plan, blk.moe.w13, blk.moe.w2)
+        return self._experts(blk, m_bf, plan)
 
     def _add_pending(self, streams, pending, weight, **out) -> None:
         """streams += pending (a bf16 delta, or routed expert rows + plan, whose
@@ -263,7 +263,7 @@ class LoopedHybridModel:
         return self._decode_head(streams, y_rows, plan, state)
 
     def _experts(self, blk: Block, m_bf: torch.Tensor, plan: kernels.RoutePlan):
-        """Routed expert rows of a decode step and the plan that combines them."""
+        """Routed expert rows and the plan that combines them (prefill and decode)."""
         if self.ep is not None:
             res = self.ep.run(m_bf, plan, blk.moe.w13, blk.moe.w2, path=self.expert_path)
             return res.y_rows, res.plan_for_combine(plan)

@@ -226,24 +226,26 @@ def _model_worker(rank, world, port, errors):
                                                                expert_range=ep.expert_range), ep=ep)
         g = torch.Generator(device="cpu").manual_seed(100 + rank)
         ids = torch.randint(0, cfg.vocab_size, (bsz, t), generator=g).to(dev)
-        out_full = full.forward(ids, last_logits_only=True)
-        out_ep = shard.forward(ids, last_logits_only=True)
-        a, b = out_full.logits.float(), out_ep.logits.float()
-        err = (a - b).abs().max().item() / max(a.abs().max().item(), 1e-6)
-        assert err < 2e-2, f"rank {rank}: expert-parallel prefill logits off by {err:.3g}"
-        # decode from the same state with the same expert kernels: bit-identical logits
+        # with the same expert kernels on both sides the expert-parallel rows are
+        # bit-identical to the single-device ones, and so are prefill and decode
         for path in ("decode", "grouped"):
             full.expert_path = shard.expert_path = path
+            out_full = full.forward(ids, last_logits_only=True)
+            out_ep = shard.forward(ids, last_logits_only=True)
+            assert torch.equal(out_full.logits, out_ep.logits), \
+                f"rank {rank}: {path} expert-parallel prefill differs"
+            a = out_full.logits.float()
             st_full = RecurrentState(cfg, bsz, dev)
             st_full.load_state_dict(out_full.state.state_dict())
             st_ep = RecurrentState(cfg, bsz, dev)
-            st_ep.load_state_dict(out_full.state.state_dict())
+            st_ep.load_state_dict(out_ep.state.state_dict())
             tok = a[:, -1].argmax(-1)
             for _ in range(4):
                 la = full.decode_step(tok, st_full)
                 lb = shard.decode_step(tok, st_ep)
                 assert torch.equal(la, lb), f"rank {rank}: {path} expert-parallel decode differs"
                 tok = la.float().argmax(-1)
+        shard.expert_path = "auto"
         # the peer-memory exchange inside a captured CUDA graph
         from hybrid_llm_b200.model import GreedyDecoder
         toks = []
