@@ -92,6 +92,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "llmyb_rmsnorm_bf16": (I32, [P, I64, I32, P, F32, P, P]),
     # sampling
     "llmyb_sample": (I32, [P, I64, I32, I32, P, I64, F32, P, I32, F32, I32, F32, P, P, P, I32, P, P]),
+    # engine host sampler (returns the token, not a status)
+    "llmyb_engine_sample": (I32, [P, I32, F32, I32, F32, F32, P, I32, C.POINTER(U64)]),
 }
 
 _lock = threading.Lock()

@@ -72,6 +72,12 @@ class RecurrentState:
             t[mask] = 0
         self.positions[mask] = 0
 
+    def zero_(self) -> None:
+        """Zero every state tensor and position (a fresh conversation)."""
+        for t in (*self.gdn_states.values(), *self.gdn_conv_histories.values(),
+                  *self.local_k.values(), *self.local_v.values(), self.positions):
+            t.zero_()
+
     def nbytes(self) -> int:
         tensors = (*self.gdn_states.values(), *self.gdn_conv_histories.values(),
                    *self.local_k.values(), *self.local_v.values(), self.positions)

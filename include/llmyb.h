@@ -436,9 +436,8 @@ int32_t llmyb_rmsnorm_bf16(const void* x, int64_t n_tokens, int32_t d_model, con
 
 /* ---------------------------------------------------------------- sampling
  * Replaces _sample_next_token / the sampling block of sample()
- * (sample_standalone.py:5383-5423, :5596-5636), the native sampler
- * (llmy_cuda/src/kernels/sample.cu:116-234) and llmy_sample
- * (llmy_cuda/include/llmy.h:64-68).  logits [B,V] fp32 (row stride ld);
+ * (sample_standalone.py:5383-5423, :5596-5636) and the native sampler
+ * (llmy_cuda/src/kernels/sample.cu:116-234).  logits [B,V] fp32 (row stride ld);
  * seen [B, ceil(V/32)] bitmask of generated ids (repetition penalty) or null;
  * blocked ids forced to -inf or null; temperature <= 1e-4 is greedy; top_k 0
  * disables top-k (else <= 1024); 0 < top_p < 1 enables nucleus filtering;
@@ -451,6 +450,20 @@ int32_t llmyb_sample(const float* logits, int64_t ld, int32_t batch, int32_t voc
                      const int32_t* blocked, int32_t n_blocked, float temperature, int32_t top_k,
                      float top_p, const float* uniforms, int64_t* out_tokens, float* out_logprob,
                      int32_t update_seen, int32_t* dev_status, void* stream);
+
+/* Host function (no device work).  Replaces llmy_sample
+ * (llmy_cuda/include/llmy.h:62-68, llmy_cuda/src/llmy.cpp:132-202), the
+ * engine's CPU sampler for one row of HOST logits [vocab] fp32: repetition
+ * penalty once per entry of recent[n_recent] (ids outside the vocabulary
+ * skipped), top_k <= 0 or > vocab = whole vocabulary, capped at 256;
+ * temperature <= 0 is greedy; 0 < top_p < 1 keeps the shortest prefix whose
+ * cumulative probability reaches top_p; one xorshift64 step of *rng_state gives
+ * u = (state >> 11) / 2^53.  Returns the token id (0 when vocab <= 0, -1 for a
+ * null logits / rng_state, or a null recent with n_recent > 0).  Equal logits
+ * are ordered by index. */
+int32_t llmyb_engine_sample(const float* logits, int32_t vocab, float temperature, int32_t top_k,
+                            float top_p, float repetition_penalty, const int32_t* recent,
+                            int32_t n_recent, uint64_t* rng_state);
 
 #ifdef __cplusplus
 }

@@ -79,3 +79,77 @@ def sample_next_token(logits, generated, *, temp, top_k, top_p, rep, uniforms, b
         toks.append(t)
         lps.append(lp)
     return np.array(toks, dtype=np.int64), np.array(lps)
+
+
+# ----------------------------------------------------------------------------
+# The reference engine's host sampler, llmy_sample (llmy_cuda/src/llmy.cpp:132-202).
+# Single-precision arithmetic in the reference's order (sequential float sums),
+# xorshift64 state (13, 7, 17) and u = (state >> 11) / 2^53.  The reference
+# orders equal logits by std::partial_sort, which leaves their order open; this
+# restatement (and the build) put the lower index first.
+_M64 = (1 << 64) - 1
+
+
+def xorshift64(state: int) -> int:
+    state ^= (state << 13) & _M64
+    state ^= state >> 7
+    state ^= (state << 17) & _M64
+    return state & _M64
+
+
+def engine_host_sample(logits, temperature: float, top_k: int, top_p: float,
+                       repetition_penalty: float, recent, rng_state: int):
+    """Returns (token, rng_state after the call)."""
+    f32 = np.float32
+    work = np.array(logits, dtype=np.float32).reshape(-1)
+    vocab = work.size
+    if vocab <= 0:
+        return 0, rng_state
+    if top_k <= 0 or top_k > vocab:
+        top_k = vocab
+    top_k = min(top_k, 256)
+    rep = f32(repetition_penalty)
+    if rep != f32(1.0) and len(recent) > 0:
+        for r in recent:                      # every occurrence applies again
+            r = int(r)
+            if 0 <= r < vocab:
+                v = work[r]
+                work[r] = v / rep if v > f32(0.0) else v * rep
+    order = np.lexsort((np.arange(vocab), -work))[:top_k]
+    temperature = f32(temperature)
+    if not (temperature > f32(0.0)):
+        return int(order[0]), rng_state
+    maxv = work[order[0]]
+    probs = np.empty(top_k, dtype=np.float32)
+    total = f32(0.0)
+    for i in range(top_k):
+        z = f32(f32(work[order[i]] - maxv) / temperature)
+        e = f32(np.exp(np.float64(z)))         # correctly rounded single-precision exp
+        probs[i] = e
+        total = f32(total + e)
+    for i in range(top_k):
+        probs[i] = f32(probs[i] / total)
+    cutoff = top_k
+    top_p = f32(top_p)
+    if f32(0.0) < top_p < f32(1.0):
+        cdf = f32(0.0)
+        for i in range(top_k):
+            cdf = f32(cdf + probs[i])
+            if cdf >= top_p:
+                cutoff = i + 1
+                break
+    renorm = f32(0.0)
+    for i in range(cutoff):
+        renorm = f32(renorm + probs[i])
+    for i in range(cutoff):
+        probs[i] = f32(probs[i] / renorm)
+    rng_state = xorshift64(int(rng_state))
+    u = float(rng_state >> 11) / float(1 << 53)
+    acc = f32(0.0)
+    chosen = int(order[cutoff - 1])
+    for i in range(cutoff):
+        acc = f32(acc + probs[i])
+        if u < float(acc):
+            chosen = int(order[i])
+            break
+    return chosen, rng_state
