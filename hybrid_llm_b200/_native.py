@@ -94,6 +94,9 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "llmyb_sample": (I32, [P, I64, I32, I32, P, I64, F32, P, I32, F32, I32, F32, P, P, P, I32, P, P]),
     # engine host sampler (returns the token, not a status)
     "llmyb_engine_sample": (I32, [P, I32, F32, I32, F32, F32, P, I32, C.POINTER(U64)]),
+    # engine device entry points
+    "llmyb_mhc_sinkhorn4": (I32, [P, P, I32, I32, P]),
+    "llmyb_moe_selected_fp32": (I32, [P, P, P, P, P, P, P, P, I32, I32, I32, I32, P]),
 }
 
 _lock = threading.Lock()

@@ -19,6 +19,8 @@ caller of the reference engine switches by changing the import:
                                              llmy.h:64-68 / llmy.cpp:132-202
     llmy_last_executed_loops(state), llmy_sync()
                                              llmy.h:71-72
+    llmy_mhc_sinkhorn4, llmy_moe_selected_fp32
+                                             llmy.h:74-88 (device buffers, int status)
 
 A model is the checkpoint in the engine's ``.llmy`` format loaded onto one GPU
 (``ModelWeights.from_llmy``) and served by LoopedHybridModel: prefill runs the
@@ -261,6 +263,41 @@ def llmy_sample(logits, vocab_size: int, temperature: float, top_k: int, top_p: 
     if arr is not None:
         arr.reshape(-1)[0] = holder.value
     return int(tok)
+
+
+# ------------------------------------------------------- device entry points
+def _addr(p) -> int | None:
+    if p is None:
+        return None
+    if isinstance(p, torch.Tensor):
+        if not p.is_cuda:
+            raise ValueError("device pointers only: pass CUDA tensors or raw addresses")
+        return p.data_ptr()
+    return int(p)
+
+
+def _stream_handle(stream) -> int | None:
+    if stream is None:
+        return None
+    if isinstance(stream, torch.cuda.Stream):
+        return stream.cuda_stream
+    return int(stream)
+
+
+def llmy_mhc_sinkhorn4(input, output, matrices: int, iterations: int, stream=None) -> int:
+    """Sinkhorn normalisation of fp32 [matrices, 4, 4] device data (CUDA tensors
+    or raw addresses); returns the status (0 = success, 1 = invalid value)."""
+    return int(_native.lib().llmyb_mhc_sinkhorn4(_addr(input), _addr(output), int(matrices),
+                                                  int(iterations), _stream_handle(stream)))
+
+
+def llmy_moe_selected_fp32(x, idx, prob, gate_up, down, activation, route_output, out,
+                           D: int, H: int, E: int, k: int, stream=None) -> int:
+    """One token through its k routed experts, fp32, on device buffers (CUDA
+    tensors or raw addresses); returns the status (0 = success)."""
+    return int(_native.lib().llmyb_moe_selected_fp32(
+        *(_addr(t) for t in (x, idx, prob, gate_up, down, activation, route_output, out)),
+        int(D), int(H), int(E), int(k), _stream_handle(stream)))
 
 
 # ---------------------------------------------------------------- diagnostics

@@ -791,3 +791,47 @@ def rmsnorm_bf16(x: torch.Tensor, weight: torch.Tensor | None, eps: float,
     _native.call("llmyb_rmsnorm_bf16", _ptr(x), x.numel() // d, d, _ptr(weight), float(eps),
                  _ptr(out), _stream())
     return out
+
+
+# ------------------------------------------------------------ engine device ops
+def mhc_sinkhorn4(logits: torch.Tensor, iterations: int = 20,
+                  out: torch.Tensor | None = None) -> torch.Tensor:
+    """Sinkhorn-normalised exp of fp32 [..., 4, 4] matrices (mhc.py:12-17):
+    `iterations` rounds of row then column log-normalisation."""
+    _require_cuda(logits, out)
+    if logits.dtype != torch.float32 or tuple(logits.shape[-2:]) != (4, 4):
+        raise ValueError("mhc_sinkhorn4 takes fp32 [..., 4, 4] matrices")
+    x = logits.contiguous()
+    if out is None:
+        out = torch.empty_like(x)
+    elif not out.is_contiguous() or out.shape != x.shape or out.dtype != torch.float32:
+        raise ValueError("out must be a contiguous fp32 tensor of the input's shape")
+    n = x.numel() // 16
+    if n == 0:
+        return out
+    _native.call("llmyb_mhc_sinkhorn4", _ptr(x), _ptr(out), n, int(iterations), _stream())
+    return out
+
+
+def moe_selected_fp32(x: torch.Tensor, idx: torch.Tensor, prob: torch.Tensor,
+                      gate_up: torch.Tensor, down: torch.Tensor) -> torch.Tensor:
+    """One token through its k routed experts, fp32 (llmy_moe_selected_fp32):
+    x [D], idx [k] int64, prob [k], gate_up [E, 2H, D] (gate rows then up rows),
+    down [E, D, H].  Returns out [D]."""
+    _require_cuda(x, idx, prob, gate_up, down)
+    e, h2, d = gate_up.shape
+    h = h2 // 2
+    k = idx.numel()
+    if (x.numel() != d or tuple(down.shape) != (e, d, h) or prob.numel() != k
+            or idx.dtype != torch.int64 or x.dtype != torch.float32
+            or gate_up.dtype != torch.float32 or down.dtype != torch.float32
+            or prob.dtype != torch.float32):
+        raise ValueError("moe_selected_fp32: shapes or dtypes do not match")
+    x, idx, prob = x.contiguous(), idx.contiguous(), prob.contiguous()
+    gate_up, down = gate_up.contiguous(), down.contiguous()
+    act = torch.empty(k, h, dtype=torch.float32, device=x.device)
+    route = torch.empty(k, d, dtype=torch.float32, device=x.device)
+    out = torch.empty(d, dtype=torch.float32, device=x.device)
+    _native.call("llmyb_moe_selected_fp32", _ptr(x), _ptr(idx), _ptr(prob), _ptr(gate_up),
+                 _ptr(down), _ptr(act), _ptr(route), _ptr(out), d, h, e, k, _stream())
+    return out

@@ -465,6 +465,25 @@ int32_t llmyb_engine_sample(const float* logits, int32_t vocab, float temperatur
                             float top_p, float repetition_penalty, const int32_t* recent,
                             int32_t n_recent, uint64_t* rng_state);
 
+/* Replaces llmy_mhc_sinkhorn4 (llmy_cuda/include/llmy.h:74-78; the operation
+ * of model/layers/mhc.py:12-17): output[m] = exp(A) after `iterations` rounds
+ * of A -= logsumexp over each row, then over each column, for fp32 [matrices,
+ * 4, 4] device arrays (16-byte aligned).  LLMYB_EINVAL for null pointers,
+ * matrices <= 0 or iterations < 0. */
+int32_t llmyb_mhc_sinkhorn4(const float* input, float* output, int32_t matrices,
+                            int32_t iterations, void* stream);
+
+/* Replaces llmy_moe_selected_fp32 (llmy_cuda/include/llmy.h:80-88): one
+ * token x [D] through its k routed experts idx [k] (int64; ids outside [0, E)
+ * contribute zero) with weights prob [k], fp32: activation [k, H] =
+ * silu(gate_e x) * (up_e x) with gate_up [E, 2H, D] (gate rows, then up rows),
+ * route_output [k, D] = prob * down_e activation with down [E, D, H], and
+ * out [D] = the sum of the k route outputs in route order.  Device pointers. */
+int32_t llmyb_moe_selected_fp32(const float* x, const int64_t* idx, const float* prob,
+                                const float* gate_up, const float* down, float* activation,
+                                float* route_output, float* out, int32_t D, int32_t H, int32_t E,
+                                int32_t k, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -163,3 +163,87 @@ def test_engine_generation_loop(cuda):
         ref.append(nxt)
         nxt = int(m.model.decode_step(torch.tensor([nxt], device=cuda), st)[0].float().argmax())
     assert toks == ref
+
+
+# ------------------------------------------------ engine device entry points
+def _ops():
+    return np.load(GOLDEN / "engine_ops.npz")
+
+
+def test_sinkhorn_oracle_matches_reference():
+    from oracle import mhc
+    z = _ops()
+    for it in (0, 1, 5, 20):
+        want = z[f"sk_out_{it}"]
+        got = mhc.sinkhorn(z["sk_in"], it)
+        assert np.allclose(got, want, rtol=2e-6, atol=1e-6), it
+    # the last step normalises columns: each column sums to one
+    s = mhc.sinkhorn(z["sk_in"], 20)
+    assert np.allclose(s.sum(-2), 1, atol=1e-6)
+
+
+def test_moe_selected_oracle_matches_reference():
+    from oracle import routing
+    z = _ops()
+    gu = z["moe_gate_up"]
+    h = gu.shape[1] // 2
+    got = routing.moe_forward(z["moe_x"][None], z["moe_idx"][None], z["moe_prob"][None],
+                              gu[:, :h], gu[:, h:], z["moe_down"])[0]
+    assert np.allclose(got, z["moe_out"], rtol=1e-5, atol=1e-6)
+
+
+@pytest.mark.gpu
+def test_sinkhorn4_kernel(cuda):
+    """fp32 tolerance: accurate expf/logf in a different summation order than
+    torch.logsumexp (rtol 2e-6 on the golden, 1e-5 on a large random batch)."""
+    from hybrid_llm_b200 import kernels
+    from oracle import mhc
+    z = _ops()
+    x = torch.from_numpy(z["sk_in"]).to(cuda)
+    for it in (0, 1, 5, 20):
+        got = kernels.mhc_sinkhorn4(x, it).cpu().numpy()
+        assert np.allclose(got, z[f"sk_out_{it}"], rtol=2e-6, atol=1e-6), it
+    big = torch.randn(3, 1000, 4, 4, device=cuda) * 3
+    got = kernels.mhc_sinkhorn4(big, 20).cpu().numpy()
+    assert np.allclose(got, mhc.sinkhorn(big.cpu().numpy(), 20), rtol=1e-5, atol=1e-6)
+    # the engine-ABI form: raw buffers, status codes
+    out = torch.empty_like(x)
+    assert engine.llmy_mhc_sinkhorn4(x, out, x.shape[0], 20) == 0
+    assert np.allclose(out.cpu().numpy(), z["sk_out_20"], rtol=2e-6, atol=1e-6)
+    assert engine.llmy_mhc_sinkhorn4(x, out, 0, 20) == 1
+    assert engine.llmy_mhc_sinkhorn4(x, out, 4, -1) == 1
+    assert engine.llmy_mhc_sinkhorn4(None, out, 4, 3) == 1
+    torch.cuda.synchronize()
+
+
+@pytest.mark.gpu
+def test_moe_selected_fp32_kernel(cuda):
+    from hybrid_llm_b200 import kernels
+    from oracle import routing
+    z = _ops()
+    t = {k: torch.from_numpy(np.ascontiguousarray(z[k])).to(cuda)
+         for k in ("moe_x", "moe_idx", "moe_prob", "moe_gate_up", "moe_down")}
+    got = kernels.moe_selected_fp32(t["moe_x"], t["moe_idx"], t["moe_prob"], t["moe_gate_up"],
+                                    t["moe_down"]).cpu().numpy()
+    assert np.allclose(got, z["moe_out"], rtol=1e-5, atol=1e-6)
+    # an odd width (scalar loads), an expert id outside [0, E) contributes zero
+    rng = np.random.default_rng(3)
+    e, d, h = 5, 37, 23
+    x = rng.normal(size=d).astype(np.float32)
+    gu = (rng.normal(size=(e, 2 * h, d)) * 0.2).astype(np.float32)
+    dn = (rng.normal(size=(e, d, h)) * 0.2).astype(np.float32)
+    idx = np.array([4, -1, 1, 7], dtype=np.int64)
+    prob = np.array([0.4, 0.3, 0.2, 0.1], dtype=np.float32)
+    act = torch.empty(4, h, device=cuda)
+    route = torch.empty(4, d, device=cuda)
+    out = torch.empty(d, device=cuda)
+    dev = [torch.from_numpy(a).to(cuda) for a in (x, idx, prob, gu, dn)]
+    assert engine.llmy_moe_selected_fp32(*dev, act, route, out, d, h, e, 4) == 0
+    keep = idx[[0, 2]]
+    want = routing.moe_forward(x[None], keep[None], prob[[0, 2]][None], gu[:, :h], gu[:, h:], dn)[0]
+    assert np.allclose(out.cpu().numpy(), want, rtol=1e-5, atol=1e-6)
+    r = route.cpu().numpy()
+    assert not r[1].any() and not r[3].any()
+    assert np.array_equal(out.cpu().numpy(), ((r[0] + r[1]) + r[2]) + r[3])
+    assert engine.llmy_moe_selected_fp32(*dev, act, route, out, d, h, e, 0) == 1
+    torch.cuda.synchronize()
