@@ -2,10 +2,12 @@
 
 Mirrors the parts of the reference V6Config (model/config.py:107-191) that the
 B200 path implements: a recurrent core of ``gdn_moe`` / ``csa_moe`` blocks run
-``num_loops`` times, mHC disabled (one residual stream), plain top-k softmax
-router (no context path), no shared experts, CSA with its remote compressed
-branch disabled (temporal_compression beyond any sequence), no stem/tail
-blocks.  ``from_v6`` converts a reference config (dataclass or mapping) and
+``num_loops`` times, with either one plain residual stream (mHC disabled,
+``mhc_streams == 0``) or multi-stream hyper-connections (``mhc_streams`` = 1, 2
+or 4 live streams, input-dependent maps, shared across loops, streams carried
+across loop boundaries), plain top-k softmax router (no context path), no
+shared experts, CSA with its remote compressed branch disabled
+(temporal_compression beyond any sequence), no stem/tail blocks.  ``from_v6`` converts a reference config (dataclass or mapping) and
 rejects anything outside that subset instead of silently changing the model.
 """
 from __future__ import annotations
@@ -31,6 +33,8 @@ class HybridConfig:
     moe_hidden: int
     conv_kernel: int = 4
     rms_eps: float = 1e-6
+    mhc_streams: int = 0          # 0: plain residual; S > 0: S-stream hyper-connections
+    mhc_iterations: int = 10      # Sinkhorn iterations of the residual map
     name: str = field(default="custom", compare=False)
 
     def __post_init__(self) -> None:
@@ -43,6 +47,15 @@ class HybridConfig:
             raise ValueError("moe_top_k cannot exceed moe_experts")
         if self.conv_kernel != 4:
             raise ValueError("the GDN conv gate kernel implements kernel size 4")
+        if self.mhc_streams not in (0, 1, 2, 4):
+            raise ValueError("hyper-connections are implemented for 1, 2 or 4 streams")
+        if self.mhc_iterations < 0:
+            raise ValueError("mhc_iterations must be >= 0")
+
+    @property
+    def streams(self) -> int:
+        """Residual streams carried per token (1 without hyper-connections)."""
+        return max(1, self.mhc_streams)
 
     @property
     def n_blocks(self) -> int:
@@ -57,8 +70,18 @@ class HybridConfig:
         get = (lambda o, k: o[k]) if isinstance(cfg, dict) else getattr
         sub = lambda name: get(cfg, name)
         sget = lambda o, k: o[k] if isinstance(o, dict) else getattr(o, k)
-        if sget(sub("mhc"), "enabled") and sget(sub("mhc"), "streams") != 1:
-            raise ValueError("multi-stream hyper-connections are not implemented (mhc.enabled)")
+        mhc = sub("mhc")
+        mget = lambda k, default: (mhc.get(k, default) if isinstance(mhc, dict)
+                                   else getattr(mhc, k, default))
+        mhc_streams, mhc_iters = 0, 10
+        if mget("enabled", True):
+            mhc_streams, mhc_iters = int(mget("streams", 4)), int(mget("sinkhorn_iterations", 10))
+            if not mget("shared_across_loops", True):
+                raise ValueError("per-loop hyper-connection weights are not implemented")
+            if not mget("preserve_streams_across_loop_boundary", True):
+                raise ValueError("restarting the streams at each loop is not implemented")
+        elif int(mget("streams", 1)) != 1:
+            raise ValueError("mHC disabled with several streams is not implemented")
         if sget(sub("router"), "context_aware"):
             raise ValueError("the context-aware router path is not implemented")
         if sget(sub("moe"), "shared_experts") != 0:
@@ -78,6 +101,7 @@ class HybridConfig:
             moe_experts=sget(sub("moe"), "routed_experts"), moe_top_k=sget(sub("moe"), "routed_top_k"),
             moe_hidden=sget(sub("moe"), "expert_hidden"),
             conv_kernel=sget(sub("gdn"), "conv_kernel"),
+            mhc_streams=mhc_streams, mhc_iterations=mhc_iters,
         )
 
 

@@ -835,3 +835,37 @@ def moe_selected_fp32(x: torch.Tensor, idx: torch.Tensor, prob: torch.Tensor,
     _native.call("llmyb_moe_selected_fp32", _ptr(x), _ptr(idx), _ptr(prob), _ptr(gate_up),
                  _ptr(down), _ptr(act), _ptr(route), _ptr(out), d, h, e, k, _stream())
     return out
+
+
+# --------------------------------------------------------- hyper-connections
+def mhc_read(streams: torch.Tensor, n_streams: int, mhc, norm_w: torch.Tensor | None, eps: float,
+             iterations: int, maps: torch.Tensor, *, out_bf16: torch.Tensor | None = None,
+             out_f32: torch.Tensor | None = None) -> None:
+    """Sub-layer input from the S residual streams (mhc.py:135-156, :193-206):
+    streams [N, S*D] fp32; mhc a weights.MhcBlock; writes the maps [N, 2S+S*S]
+    and RMSNorm(LayerNorm(sum_s pre_s stream_s)) * norm_w into out_bf16 / out_f32."""
+    _require_cuda(streams, maps, out_bf16, out_f32)
+    n = streams.shape[0]
+    d = streams.shape[1] // n_streams
+    raw = torch.mm(streams, mhc.theta.t())  # theta with the mapping-norm weight folded in
+    _native.call("llmyb_mhc_read", _ptr(streams), n, n_streams, d, _ptr(raw), _ptr(mhc.bias),
+                 _ptr(mhc.scalars), _ptr(mhc.ln_w), _ptr(mhc.ln_b), _ptr(norm_w), float(eps),
+                 int(iterations), _ptr(maps), _ptr(out_bf16), _ptr(out_f32), _stream())
+
+
+def mhc_write(streams: torch.Tensor, n_streams: int, mhc, maps: torch.Tensor,
+              delta: torch.Tensor | None, plan: RoutePlan | None = None) -> None:
+    """streams [N, S*D] += g * scale * (res @ streams + post * update) in place
+    (mhc.py:208-229); update = delta [N, D] bf16, or with `plan` the sum of
+    each token's routed expert rows delta[plan.route_pos[t*k + s]]."""
+    _require_cuda(streams, maps, delta)
+    _inplace(streams, "streams")
+    n = streams.shape[0]
+    d = streams.shape[1] // n_streams
+    route_pos, k = (None, 0)
+    if plan is not None:
+        route_pos, k = plan.route_pos, plan.topk_idx.shape[1]
+    if delta is not None:
+        delta = delta.contiguous()
+    _native.call("llmyb_mhc_write", _ptr(streams), n, n_streams, d, _ptr(delta), _ptr(route_pos),
+                 int(k), _ptr(maps), _ptr(mhc.stream_scale), _ptr(mhc.scalars), _stream())

@@ -121,15 +121,25 @@ class LoopedHybridModel:
         reset = None if reset_mask is None else reset_mask.to(self.device, torch.bool)
         if reset is not None and bool(reset[:, 0].any()):
             state.reset_rows(reset[:, 0])
-        streams = kernels.embed(ids.reshape(-1), self.w.embed, self.w.stream_seed)  # [N, D] fp32
+        streams = self._embed(ids.reshape(-1))  # [N, S*D] fp32
         self._run_core(streams, state, bsz, t, reset, loops)
         state.positions.fill_(t)
-        d = c.d_model
-        hs = streams.view(bsz, t, d)
+        w = c.streams * c.d_model
+        hs = streams.view(bsz, t, w)
         if last_logits_only:
             hs = hs[:, -1:].contiguous()
-        logits = self._head(hs.reshape(-1, d)).view(bsz, -1, c.vocab_size)
+        logits = self._head(hs.reshape(-1, w)).view(bsz, -1, c.vocab_size)
         return HybridOutput(logits, state)
+
+    def _embed(self, ids: torch.Tensor) -> torch.Tensor:
+        """Residual streams of the tokens: embed + stream_seed, [N, S*D] fp32
+        (model/model.py:442-444; S = 1 without hyper-connections)."""
+        c = self.cfg
+        if c.streams == 1:
+            return kernels.embed(ids, self.w.embed, self.w.stream_seed)
+        h = kernels.embed(ids, self.w.embed, None)
+        seed = self.w.stream_seed.view(1, c.streams, c.d_model)
+        return (h.unsqueeze(1) + seed).reshape(h.shape[0], -1)
 
     @torch.no_grad()
     def run_stack(self, hidden: torch.Tensor, *, state: RecurrentState | None = None,
@@ -138,16 +148,21 @@ class LoopedHybridModel:
         workload; model/model.py:618-687 without embedding and head).  Returns
         the fp32 residual stream after the last loop."""
         c = self.cfg
-        bsz, t, d = hidden.shape
+        bsz, t = hidden.shape[:2]
+        w = c.streams * c.d_model
+        if hidden.shape[2:].numel() != w:
+            raise ValueError(f"hidden must be [B, T, D] (or [B, T, S, D] with {c.streams} streams)")
         if state is None:
             state = RecurrentState(c, bsz, self.device)
-        streams = hidden.to(self.device, torch.float32).reshape(bsz * t, d).clone()
+        streams = hidden.to(self.device, torch.float32).reshape(bsz * t, w).clone()
         self._run_core(streams, state, bsz, t, None, c.num_loops if num_loops is None else num_loops)
         state.positions.fill_(t)
-        return streams.view(bsz, t, d)
+        return streams.view(hidden.shape)
 
     def _run_core(self, streams, state, bsz, t, reset, loops) -> None:
         c = self.cfg
+        if c.mhc_streams:
+            return self._run_core_mhc(streams, state, bsz, t, reset, loops)
         n, d = bsz * t, c.d_model
         normed = torch.empty(n, d, dtype=torch.bfloat16, device=self.device)
         m_bf = torch.empty_like(normed)
@@ -165,6 +180,46 @@ class LoopedHybridModel:
                                     out_f32=m_f32)
                 pending = self._moe(blk, m_bf, m_f32)
         self._add_pending(streams, pending, None, normalize=False)
+
+    def _mhc_write(self, streams, blk: Block, maps, pending) -> None:
+        """Close a sub-layer: its output (a bf16 delta, or routed expert rows +
+        plan whose per-token sum is the MoE combine) into the S streams."""
+        if pending is None:
+            return
+        if isinstance(pending, tuple):
+            kernels.mhc_write(streams, self.cfg.mhc_streams, blk.mhc, maps, pending[0], pending[1])
+        else:
+            kernels.mhc_write(streams, self.cfg.mhc_streams, blk.mhc, maps, pending)
+
+    def _run_core_mhc(self, streams, state, bsz, t, reset, loops) -> None:
+        """The recurrent core with hyper-connections (PhysicalBlock.forward,
+        model/model.py:162-264 with self.mhc): per sub-layer a read (maps +
+        LayerNorm'd weighted stream sum + the block's RMSNorm) and, after the
+        sub-layer, a write of its output with the same maps."""
+        c = self.cfg
+        n, d, ns = bsz * t, c.d_model, c.mhc_streams
+        nm = 2 * ns + ns * ns
+        normed = torch.empty(n, d, dtype=torch.bfloat16, device=self.device)
+        m_bf = torch.empty_like(normed)
+        m_f32 = torch.empty(n, d, dtype=torch.float32, device=self.device)
+        maps_mix = torch.empty(n, nm, dtype=torch.float32, device=self.device)
+        maps_ffn = torch.empty_like(maps_mix)
+        pending, prev = None, None
+        for i in range(loops):
+            for j, blk in enumerate(self.w.blocks):
+                key = state_key(i, j)
+                self._mhc_write(streams, prev, maps_ffn, pending)
+                kernels.mhc_read(streams, ns, blk.mhc, blk.mixer_norm, c.rms_eps, c.mhc_iterations,
+                                 maps_mix, out_bf16=normed)
+                if isinstance(blk.mixer, GdnBlock):
+                    mixed = self._gdn_prefill(blk.mixer, normed, state, key, bsz, t, reset)
+                else:
+                    mixed = self._csa_prefill(blk.mixer, normed, state, key, bsz, t)
+                kernels.mhc_write(streams, ns, blk.mhc, maps_mix, mixed)
+                kernels.mhc_read(streams, ns, blk.mhc, blk.ffn_norm, c.rms_eps, c.mhc_iterations,
+                                 maps_ffn, out_bf16=m_bf, out_f32=m_f32)
+                pending, prev = self._moe(blk, m_bf, m_f32), blk
+        self._mhc_write(streams, prev, maps_ffn, pending)
 
     def _gdn_prefill(self, g: GdnBlock, normed, state: RecurrentState, key: str, bsz: int, t: int,
                      reset) -> torch.Tensor:
@@ -225,6 +280,8 @@ class LoopedHybridModel:
         bsz = ids.shape[0]
         loops = c.num_loops if num_loops is None else int(num_loops)
         d = c.d_model
+        if c.mhc_streams:
+            return self._decode_mhc(ids, state, loops)
         if self.decode_fused and kernels.decode_fused_supported(
                 bsz, d, c.moe_experts, c.moe_top_k, c.gdn_heads * c.gdn_value_dim, d):
             return self._decode_fused(ids, state, loops)
@@ -281,6 +338,43 @@ class LoopedHybridModel:
         logits = torch.mm(h, self.w.embed.t())
         state.positions.add_(1)
         return logits
+
+    def _decode_mhc(self, ids: torch.Tensor, state: RecurrentState, loops: int) -> torch.Tensor:
+        """decode_step with hyper-connections (PhysicalBlock.forward_step,
+        model/model.py:266-376 with self.mhc): the read / write pairs of the
+        prefill core around the mixer step kernels and the routed experts."""
+        c = self.cfg
+        bsz, d, ns = ids.shape[0], c.d_model, c.mhc_streams
+        nm = 2 * ns + ns * ns
+        streams = self._embed(ids)
+        normed = torch.empty(bsz, d, dtype=torch.bfloat16, device=self.device)
+        m_bf = torch.empty_like(normed)
+        m_f32 = torch.empty(bsz, d, dtype=torch.float32, device=self.device)
+        maps_mix = torch.empty(bsz, nm, dtype=torch.float32, device=self.device)
+        maps_ffn = torch.empty_like(maps_mix)
+        pending, prev = None, None
+        for i in range(loops):
+            for j, blk in enumerate(self.w.blocks):
+                key = state_key(i, j)
+                self._mhc_write(streams, prev, maps_ffn, pending)
+                kernels.mhc_read(streams, ns, blk.mhc, blk.mixer_norm, c.rms_eps, c.mhc_iterations,
+                                 maps_mix, out_bf16=normed)
+                if isinstance(blk.mixer, GdnBlock):
+                    mixed = self._gdn_step(blk.mixer, normed, state, key, bsz)
+                else:
+                    mixed = self._csa_step(blk.mixer, normed, state, key, bsz)
+                kernels.mhc_write(streams, ns, blk.mhc, maps_mix, mixed)
+                kernels.mhc_read(streams, ns, blk.mhc, blk.ffn_norm, c.rms_eps, c.mhc_iterations,
+                                 maps_ffn, out_bf16=m_bf, out_f32=m_f32)
+                r_in = torch.empty_like(m_f32)
+                kernels.add_rmsnorm(m_f32, None, blk.moe.router_norm, c.rms_eps, out_f32=r_in)
+                plan = kernels.route(torch.mm(r_in, blk.moe.router.t()), c.moe_top_k, tile_m=128)
+                pending, prev = self._experts(blk, m_bf, plan), blk
+        self._mhc_write(streams, prev, maps_ffn, pending)
+        h = kernels.rmsnorm_bf16(torch.mm(streams.to(torch.bfloat16), self.w.collapse.t()),
+                                 self.w.final_norm, c.rms_eps)
+        state.positions.add_(1)
+        return torch.mm(h, self.w.embed.t())
 
     def _decode_fused(self, ids: torch.Tensor, state: RecurrentState, loops: int) -> torch.Tensor:
         """decode_step on the fused small-batch kernels: per block [A] residual

@@ -2,8 +2,12 @@
 
 Parameter names follow the reference state dict (model/model.py:383-423 and
 the layer modules), so a reference checkpoint's tensors load directly:
-  embed_tokens.weight [V,D]; stream_seed [1,D]; mhc_collapse.weight [D,D];
+  embed_tokens.weight [V,D]; stream_seed [S,D]; mhc_collapse.weight [D,S*D];
   final_norm.weight [D]; recurrent_core.{j}.mixer_norm.weight / ffn_norm.weight;
+  mHC  recurrent_core.{j}.mhc.{stream_scale [S,D], stream_norm.{weight,bias} [D],
+       mapping_norm.weight [S*D], theta.weight [2S+S*S, S*D], pre_bias [S],
+       post_bias [S], residual_bias [S,S], alpha_pre, alpha_post, alpha_residual,
+       gating_logit, read_logits, write_logits}        (mhc.py:62-88; S streams)
   GDN  recurrent_core.{j}.mixer.{q,k,v,gate,out}_proj.weight, beta_proj.{weight,bias},
        conv.weight [D,1,4], decay_logit [H]          (gated_deltanet.py:105-113)
   CSA  recurrent_core.{j}.mixer.{query,key,value,local_out,out}.weight  (csa.py:23-28)
@@ -19,7 +23,12 @@ halves its weight traffic per token.
 
 ``synthetic_state_dict`` draws the random-init weights of the benchmark
 workloads: every tensor with two or more dimensions ~ N(0, 0.02), norm
-weights 1, beta bias 0, decay_logit 2 (the reference's own 1-D inits), each
+weights 1, beta bias 0, decay_logit 2 (the reference's own 1-D inits).  The
+hyper-connection parameters get values that exercise every term of the maps
+instead of the reference's near-identity init: theta ~ N(0, 0.02); scales,
+norm weights ~ 1 + N(0, 0.1); biases ~ N(0, 0.1) around the reference's
+(logit(1/S) for pre, 4·I for the residual map, with N(0, 0.5)); alphas 0.3;
+gating factor 0.3.  Each
 tensor from its own generator seeded by (seed, name) so that any subset can
 be regenerated identically on any machine (CPU generation) or quickly on the
 GPU (CUDA generation).
@@ -39,14 +48,25 @@ from .config import HybridConfig
 def parameter_shapes(cfg: HybridConfig) -> dict[str, tuple[int, ...]]:
     """Every reference parameter name the B200 path reads, with its shape."""
     d, e, f = cfg.d_model, cfg.moe_experts, cfg.moe_hidden
+    ns = cfg.streams
     shapes: dict[str, tuple[int, ...]] = {
-        "embed_tokens.weight": (cfg.vocab_size, d), "stream_seed": (1, d),
-        "mhc_collapse.weight": (d, d), "final_norm.weight": (d,),
+        "embed_tokens.weight": (cfg.vocab_size, d), "stream_seed": (ns, d),
+        "mhc_collapse.weight": (d, ns * d), "final_norm.weight": (d,),
     }
     for j in range(cfg.n_blocks):
         p = f"recurrent_core.{j}."
         shapes[p + "mixer_norm.weight"] = (d,)
         shapes[p + "ffn_norm.weight"] = (d,)
+        if cfg.mhc_streams:
+            q = p + "mhc."
+            shapes.update({
+                q + "read_logits": (ns, ns), q + "write_logits": (ns, ns),
+                q + "stream_scale": (ns, d), q + "stream_norm.weight": (d,),
+                q + "stream_norm.bias": (d,), q + "mapping_norm.weight": (ns * d,),
+                q + "theta.weight": (2 * ns + ns * ns, ns * d), q + "pre_bias": (ns,),
+                q + "post_bias": (ns,), q + "residual_bias": (ns, ns), q + "alpha_pre": (),
+                q + "alpha_post": (), q + "alpha_residual": (), q + "gating_logit": (),
+            })
         if cfg.block_kind(j) == "gdn":
             h, kd, vd = cfg.gdn_heads, cfg.gdn_key_dim, cfg.gdn_value_dim
             shapes.update({
@@ -94,7 +114,35 @@ def synthetic_state_dict(cfg: HybridConfig, seed: int = 0, device: str | torch.d
                          std: float = 0.02) -> LazyStateDict:
     device = torch.device(device)
 
+    def noise(name: str, shape: tuple, scale: float) -> torch.Tensor:
+        gen = torch.Generator(device=device)
+        gen.manual_seed((seed * 1_000_003 + zlib.crc32(name.encode())) % (2 ** 62))
+        return torch.randn(shape, generator=gen, device=device, dtype=torch.float32) * scale
+
+    def make_mhc(name: str, shape: tuple) -> torch.Tensor:
+        leaf = name.rsplit("mhc.", 1)[1]
+        ns = cfg.streams
+        if leaf in ("read_logits", "write_logits"):
+            return torch.eye(ns, device=device) * 4.0
+        if leaf == "theta.weight":
+            return noise(name, shape, std)
+        if leaf in ("stream_scale", "stream_norm.weight", "mapping_norm.weight"):
+            return 1.0 + noise(name, shape, 0.1)
+        if leaf == "stream_norm.bias" or leaf == "post_bias":
+            return noise(name, shape, 0.1)
+        if leaf == "pre_bias":
+            return torch.logit(torch.tensor(1.0 / ns)) + noise(name, shape, 0.1)
+        if leaf == "residual_bias":
+            return torch.eye(ns, device=device) * 4.0 + noise(name, shape, 0.5)
+        if leaf.startswith("alpha_"):
+            return torch.tensor(0.3, device=device)
+        if leaf == "gating_logit":
+            return torch.logit(torch.tensor(0.3)).to(device)
+        raise KeyError(name)
+
     def make(name: str, shape: tuple) -> torch.Tensor:
+        if ".mhc." in name:
+            return make_mhc(name, shape)
         if len(shape) >= 2:
             gen = torch.Generator(device=device)
             gen.manual_seed((seed * 1_000_003 + zlib.crc32(name.encode())) % (2 ** 62))
@@ -135,12 +183,24 @@ class MoeBlock:
 
 
 @dataclass
+class MhcBlock:
+    """One block's hyper-connection (mhc.py:52-229) in the kernels' layout."""
+    theta: torch.Tensor         # [2S+S*S, S*D] fp32: theta.weight * mapping_norm.weight (columns)
+    stream_scale: torch.Tensor  # [S, D] fp32
+    ln_w: torch.Tensor          # [D] fp32 stream_norm (LayerNorm) weight
+    ln_b: torch.Tensor          # [D] fp32 stream_norm bias
+    bias: torch.Tensor          # [2S+S*S] fp32: pre_bias | post_bias | residual_bias
+    scalars: torch.Tensor       # [4] fp32: alpha_pre, alpha_post, alpha_residual, sigmoid(gating)
+
+
+@dataclass
 class Block:
     kind: str
     mixer_norm: torch.Tensor
     ffn_norm: torch.Tensor
     mixer: GdnBlock | CsaBlock
     moe: MoeBlock
+    mhc: MhcBlock | None = None
 
 
 def _experts(sd: Mapping[str, torch.Tensor], p: str, name: str, lo: int, hi: int,
@@ -159,8 +219,8 @@ def _experts(sd: Mapping[str, torch.Tensor], p: str, name: str, lo: int, hi: int
 class ModelWeights:
     cfg: HybridConfig
     embed: torch.Tensor       # [V, D] bf16 (tied LM head)
-    stream_seed: torch.Tensor  # [D] fp32
-    collapse: torch.Tensor    # [D, D] bf16
+    stream_seed: torch.Tensor  # [S*D] fp32 (S = cfg.streams)
+    collapse: torch.Tensor    # [D, S*D] bf16
     final_norm: torch.Tensor  # [D] fp32
     blocks: list[Block]
 
@@ -204,12 +264,30 @@ class ModelWeights:
                            router=f32(p + "moe.router.logits.weight"), w13=w13, w2=w2)
             moe.router_folded = kernels.fold_router(moe.router, f32(p + "ffn_norm.weight"),
                                                     moe.router_norm)
+            mhc = None
+            if cfg.mhc_streams:
+                q = p + "mhc."
+                sc = lambda n: float(sd[q + n].reshape(()).float())
+                mhc = MhcBlock(
+                    theta=(f32(q + "theta.weight") * f32(q + "mapping_norm.weight")[None, :]
+                           ).contiguous(),
+                    stream_scale=f32(q + "stream_scale"), ln_w=f32(q + "stream_norm.weight"),
+                    ln_b=f32(q + "stream_norm.bias"),
+                    bias=torch.cat([f32(q + "pre_bias").reshape(-1), f32(q + "post_bias").reshape(-1),
+                                    f32(q + "residual_bias").reshape(-1)]).contiguous(),
+                    scalars=torch.tensor([sc("alpha_pre"), sc("alpha_post"), sc("alpha_residual"),
+                                          float(torch.sigmoid(torch.tensor(sc("gating_logit"))))],
+                                         dtype=torch.float32, device=dev))
             blocks.append(Block(cfg.block_kind(j), f32(p + "mixer_norm.weight"),
-                                f32(p + "ffn_norm.weight"), mixer, moe))
+                                f32(p + "ffn_norm.weight"), mixer, moe, mhc))
+        ns = cfg.streams
+        seed_t = f32("stream_seed")
+        collapse = bf("mhc_collapse.weight")
+        if seed_t.numel() != ns * cfg.d_model or tuple(collapse.shape) != (cfg.d_model, ns * cfg.d_model):
+            raise ValueError(f"stream_seed / mhc_collapse do not match {ns} residual stream(s)")
         return cls(cfg=cfg, embed=bf("embed_tokens.weight"),
-                   stream_seed=f32("stream_seed").reshape(-1).contiguous(),
-                   collapse=bf("mhc_collapse.weight"), final_norm=f32("final_norm.weight"),
-                   blocks=blocks)
+                   stream_seed=seed_t.reshape(-1).contiguous(), collapse=collapse,
+                   final_norm=f32("final_norm.weight"), blocks=blocks)
 
     @classmethod
     def from_llmy(cls, path, device: str | torch.device = "cuda",
@@ -237,4 +315,6 @@ class ModelWeights:
         for b in self.blocks:
             yield from (b.mixer_norm, b.ffn_norm)
             yield from vars(b.mixer).values()
-            yield from vars(b.moe).values()
+            yield from (t for t in vars(b.moe).values() if t is not None)
+            if b.mhc is not None:
+                yield from vars(b.mhc).values()

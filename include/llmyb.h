@@ -484,6 +484,34 @@ int32_t llmyb_moe_selected_fp32(const float* x, const int64_t* idx, const float*
                                 float* route_output, float* out, int32_t D, int32_t H, int32_t E,
                                 int32_t k, void* stream);
 
+/* ------------------------------------------------ hyper-connections (mHC)
+ * Replace MultiStreamHyperConnection.read / write (model/layers/mhc.py:135-156,
+ * :193-229) around each block sub-layer, for S = n_streams in {1, 2, 4} live
+ * fp32 residual streams per token, laid out [N, S*D].  maps [N, 2S+S*S] fp32
+ * hold pre | post | res (row-major) of a read for the write that follows it.
+ *
+ * llmyb_mhc_read: raw [N, 2S+S*S] = streams @ (theta * mapping_norm.weight)^T
+ * (the caller's GEMM); bias = pre_bias | post_bias | residual_bias;
+ * scalars = alpha_pre, alpha_post, alpha_residual, sigmoid(gating_logit).
+ * Computes the maps (mapping RMSNorm with the fp32 epsilon, sigmoids, Sinkhorn
+ * with `iterations` rounds), hidden = LayerNorm(sum_s pre[s] streams[s]) with
+ * ln_w / ln_b (eps 1e-5), then RMSNorm(hidden) * norm_w (norm_w nullable = 1)
+ * into out_bf16 [N, D] and/or out_f32 [N, D].  D % 4 == 0, D <= 4096.
+ *
+ * llmyb_mhc_write: streams[i] += g * stream_scale[i] * (sum_j res[i,j]
+ * streams[j] + post[i] * update), update = delta [N, D] bf16, or with
+ * route_pos the fp32 sum of the top_k routed rows delta[route_pos[n*k + s]]
+ * (the MoE combine), or zero for a null delta. */
+int32_t llmyb_mhc_read(const float* streams, int32_t n_tokens, int32_t n_streams, int32_t d_model,
+                       const float* raw, const float* bias, const float* scalars,
+                       const float* ln_w, const float* ln_b, const float* norm_w, float rms_eps,
+                       int32_t iterations, float* maps, void* out_bf16, float* out_f32,
+                       void* stream);
+int32_t llmyb_mhc_write(float* streams, int32_t n_tokens, int32_t n_streams, int32_t d_model,
+                        const void* delta, const int32_t* route_pos, int32_t top_k,
+                        const float* maps, const float* stream_scale, const float* scalars,
+                        void* stream);
+
 #ifdef __cplusplus
 }
 #endif

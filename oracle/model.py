@@ -2,9 +2,10 @@
 
 Restates LoopedHybridMoEForCausalLM.forward and decode_step
 (model/model.py:530-707, :787-915) and PhysicalBlock.forward / forward_step
-(:162-376) for the configuration subset the B200 path serves (mHC off,
-plain router, no shared experts, CSA remote branch off, no stem/tail), over a
-state dict with the reference's parameter names.
+(:162-376) for the configuration subset the B200 path serves (one plain
+residual stream or multi-stream hyper-connections shared across loops, plain
+router, no shared experts, CSA remote branch off, no stem/tail), over a state
+dict with the reference's parameter names.
 """
 from __future__ import annotations
 
@@ -16,7 +17,7 @@ def _fp(x):
     x = np.asarray(x)
     return x if x.dtype == np.float32 else x.astype(np.float64)
 
-from . import attention, gdn, routing
+from . import attention, gdn, mhc, routing
 
 
 def rmsnorm(x, w, eps=1e-6):
@@ -65,6 +66,22 @@ class OracleModel:
         out = routing.moe_forward(flat, idx, prob, wg, wu, wd, dtype=self.dtype)
         return out.reshape(*lead, -1), logits
 
+    def _read(self, j, x, norm):
+        """Sub-layer input (PhysicalBlock._read + its RMSNorm, model.py:119-123):
+        returns (normed, maps); maps is None on the plain residual stream."""
+        c, w = self.cfg, self.p[f"recurrent_core.{j}.{norm}.weight"]
+        if not c.mhc_streams:
+            return rmsnorm(x, w, c.rms_eps), None
+        maps, hidden = mhc.read(x, self.p, f"recurrent_core.{j}.mhc.", c.mhc_streams,
+                                c.mhc_iterations)
+        return rmsnorm(hidden, w, c.rms_eps), maps
+
+    def _write(self, j, x, update, maps):
+        """PhysicalBlock._write (model.py:125-126)."""
+        if maps is None:
+            return x + update
+        return mhc.write(x, update, maps, self.p, f"recurrent_core.{j}.mhc.")
+
     def new_state(self, batch):
         c = self.cfg
         st = {"gdn": {}, "conv": {}, "hist": {}, "pos": np.zeros(batch, dtype=np.int64)}
@@ -83,8 +100,7 @@ class OracleModel:
         t = x.shape[1]
         for i in range(loops):
             for j in range(c.n_blocks):
-                pre = f"recurrent_core.{j}."
-                normed = rmsnorm(x, self.p[pre + "mixer_norm.weight"], c.rms_eps)
+                normed, maps = self._read(j, x, "mixer_norm")
                 if c.block_kind(j) == "gdn":
                     mixed, s = gdn.gdn_layer(normed, self._gdn_params(j), state["gdn"][(i, j)])
                     state["gdn"][(i, j)] = s
@@ -92,23 +108,29 @@ class OracleModel:
                 else:
                     mixed = attention.csa_layer(normed, self._csa_params(j), c.csa_heads, c.csa_window)
                     state["hist"][(i, j)] = normed[:, -(c.csa_window - 1):]
-                x = x + mixed
-                m = rmsnorm(x, self.p[pre + "ffn_norm.weight"], c.rms_eps)
+                x = self._write(j, x, mixed, maps)
+                m, maps = self._read(j, x, "ffn_norm")
                 y, lg = self._moe(j, m)
                 if router_logits is not None:
                     router_logits.append(lg)
-                x = x + y
+                x = self._write(j, x, y, maps)
         state["pos"][:] = t
         return x
 
     def head(self, x):
         c = self.cfg
-        col = np.asarray(x) @ self.p["mhc_collapse.weight"].T
+        x = np.asarray(x)
+        if c.mhc_streams:
+            x = x.reshape(*x.shape[:-2], -1)
+        col = x @ self.p["mhc_collapse.weight"].T
         h = rmsnorm(col, self.p["final_norm.weight"], c.rms_eps)
         return h @ self.p["embed_tokens.weight"].T
 
     def embed(self, ids):
-        return self.p["embed_tokens.weight"][np.asarray(ids)] + self.p["stream_seed"].reshape(-1)
+        e = self.p["embed_tokens.weight"][np.asarray(ids)]
+        if self.cfg.mhc_streams:
+            return e[..., None, :] + self.p["stream_seed"].reshape(self.cfg.mhc_streams, -1)
+        return e + self.p["stream_seed"].reshape(-1)
 
     def forward(self, ids, state=None):
         ids = np.asarray(ids)
@@ -123,8 +145,7 @@ class OracleModel:
         x = self.embed(ids)[:, None, :]
         for i in range(c.num_loops):
             for j in range(c.n_blocks):
-                pre = f"recurrent_core.{j}."
-                normed = rmsnorm(x, self.p[pre + "mixer_norm.weight"], c.rms_eps)
+                normed, maps = self._read(j, x, "mixer_norm")
                 if c.block_kind(j) == "gdn":
                     hist = state["conv"][(i, j)]
                     if hist.shape[1] < c.conv_kernel - 1:
@@ -145,9 +166,9 @@ class OracleModel:
                     local = attention.csa_local_step(q, k, v)
                     mixed = ((local @ a["local_out"].T) @ a["out"].T)[:, None, :]
                     state["hist"][(i, j)] = win[:, -(c.csa_window - 1):]
-                x = x + mixed
-                m = rmsnorm(x, self.p[pre + "ffn_norm.weight"], c.rms_eps)
+                x = self._write(j, x, mixed, maps)
+                m, maps = self._read(j, x, "ffn_norm")
                 y, _ = self._moe(j, m)
-                x = x + y
+                x = self._write(j, x, y, maps)
         state["pos"] += 1
         return self.head(x[:, 0]), state

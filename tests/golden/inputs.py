@@ -128,6 +128,13 @@ def mini_config():
                         name="mini")
 
 
+def mhc_config():
+    """The mini model with four hyper-connection streams (mhc.py defaults: 10
+    Sinkhorn iterations, shared across loops, streams kept across loops)."""
+    import dataclasses
+    return dataclasses.replace(mini_config(), mhc_streams=4, mhc_iterations=10, name="mini-mhc")
+
+
 def llmy_config():
     """A small looped hybrid model for the .llmy format fixture."""
     from hybrid_llm_b200.config import HybridConfig
@@ -148,13 +155,16 @@ def block_hidden():
 
 
 def v6_mapping(cfg) -> dict:
-    """Reference V6Config fields for a HybridConfig (mHC, context router, shared
-    experts, loop memory, halting and the CSA remote branch switched off)."""
+    """Reference V6Config fields for a HybridConfig (mHC as configured; context
+    router, shared experts, loop memory, halting and the CSA remote branch
+    switched off)."""
     return dict(
         vocab_size=cfg.vocab_size, d_model=cfg.d_model, physical_blocks=cfg.n_blocks,
         stem_blocks=0, recurrent_blocks=cfg.n_blocks, tail_blocks=0, num_loops=cfg.num_loops,
         recurrent_layout=list(cfg.recurrent_layout),
-        mhc=dict(enabled=False, streams=1),
+        mhc=(dict(enabled=True, streams=cfg.mhc_streams, sinkhorn_iterations=cfg.mhc_iterations,
+                  shared_across_loops=True, preserve_streams_across_loop_boundary=True)
+             if cfg.mhc_streams else dict(enabled=False, streams=1)),
         gdn=dict(qk_heads=cfg.gdn_heads, value_heads=cfg.gdn_heads, qk_head_dim=cfg.gdn_key_dim,
                  value_head_dim=cfg.gdn_value_dim, conv_kernel=cfg.conv_kernel),
         moe=dict(routed_experts=cfg.moe_experts, shared_experts=0, routed_top_k=cfg.moe_top_k,

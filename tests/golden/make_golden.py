@@ -303,7 +303,34 @@ def sec_model() -> None:
     save("model", **res)
 
 
-SECTIONS = {"model": sec_model, "sample": sec_sample, "router": sec_router, "moe": sec_moe, "gdn": sec_gdn, "csa": sec_csa, "band": sec_band}
+def sec_mhc() -> None:
+    """The mini model with four hyper-connection streams: prefill logits of the
+    package model, and greedy decode from sample_standalone.py's copy (the
+    loop output carried, as for the mini model above)."""
+    cfg = inputs.mhc_config()
+    ids = torch.from_numpy(inputs.mini_prompt())
+    pkg = _reference_model(cfg)
+    sa = _reference_model(cfg, standalone=True)
+    res = {}
+    with torch.no_grad():
+        o1 = pkg(ids, collect_diagnostics=False)
+        res["mhc_prefill_last"] = o1.logits[:, -1].numpy()
+        out = sa(ids, collect_diagnostics=False)
+        res["mhc_sa_prefill_last"] = out.logits[:, -1].numpy()
+        state, logits = out.state, out.logits[:, -1]
+        toks, step_logits = [], []
+        for _ in range(4):
+            nxt = logits.argmax(-1, keepdim=True)
+            toks.append(nxt[:, 0].numpy())
+            o = sa.decode_step(nxt, state=state)
+            logits = o.logits[:, -1]
+            step_logits.append(logits.numpy())
+    res["mhc_tokens"] = np.stack(toks, 1)
+    res["mhc_step_logits"] = np.stack(step_logits, 1)
+    save("mhc", **res)
+
+
+SECTIONS = {"mhc": sec_mhc, "model": sec_model, "sample": sec_sample, "router": sec_router, "moe": sec_moe, "gdn": sec_gdn, "csa": sec_csa, "band": sec_band}
 
 
 def main(argv: list[str]) -> None:

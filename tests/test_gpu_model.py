@@ -188,3 +188,65 @@ def test_decode_out_router(cuda, gdn):
     ref = routing.dispatch_plan(got, e, tile_m=128)
     for f in ("counts", "offsets", "tile_offsets", "perm_token", "route_pos"):
         np.testing.assert_array_equal(getattr(plan, f).cpu().numpy(), ref[f], err_msg=f)
+
+
+def test_mhc_model_prefill_and_greedy_decode(cuda):
+    """Four hyper-connection streams: prefill and decode against the reference
+    goldens (bf16 storage / fp32 accumulation, LOGIT_REL) and the write/read
+    kernels' fp32 maps against the fp64 oracle on one block."""
+    g = golden("mhc")
+    m = _model(inputs.mhc_config())
+    ids = torch.from_numpy(inputs.mini_prompt()).cuda()
+    out = m.forward(ids, last_logits_only=True)
+    lg = out.logits[:, -1].float().cpu().numpy()
+    assert _rel(lg, g["mhc_prefill_last"]) < LOGIT_REL, _rel(lg, g["mhc_prefill_last"])
+    state = out.state
+    tok = torch.from_numpy(g["mhc_tokens"][:, 0]).cuda()
+    _greedy_ok(lg, g["mhc_prefill_last"], lg.argmax(-1), g["mhc_tokens"][:, 0])
+    for i in range(g["mhc_tokens"].shape[1]):
+        lg = m.decode_step(tok, state).float().cpu().numpy()
+        assert _rel(lg, g["mhc_step_logits"][:, i]) < LOGIT_REL, (i, _rel(lg, g["mhc_step_logits"][:, i]))
+        if i + 1 < g["mhc_tokens"].shape[1]:
+            _greedy_ok(lg, g["mhc_step_logits"][:, i], lg.argmax(-1), g["mhc_tokens"][:, i + 1])
+            tok = torch.from_numpy(g["mhc_tokens"][:, i + 1]).cuda()
+
+
+@pytest.mark.parametrize("ns", [1, 2, 4])
+def test_mhc_read_write_kernels(cuda, ns):
+    """mhc_read / mhc_write on random streams against oracle.mhc (fp64):
+    maps and the written streams to fp32 rounding, the normed read to bf16."""
+    import dataclasses
+
+    from hybrid_llm_b200 import kernels
+    from hybrid_llm_b200.weights import ModelWeights, synthetic_state_dict
+    from oracle import mhc
+    from oracle.model import rmsnorm
+
+    cfg = dataclasses.replace(inputs.mini_config(), mhc_streams=ns, mhc_iterations=7)
+    sd = synthetic_state_dict(cfg, seed=3)
+    w = ModelWeights.from_state_dict(cfg, sd, "cuda")
+    blk = w.blocks[0]
+    n, d = 70, cfg.d_model
+    rng = np.random.default_rng(ns)
+    x = rng.normal(size=(n, ns, d)).astype(np.float32)
+    streams = torch.from_numpy(x.reshape(n, -1)).cuda()
+    nm = 2 * ns + ns * ns
+    maps = torch.empty(n, nm, device="cuda")
+    ob = torch.empty(n, d, dtype=torch.bfloat16, device="cuda")
+    of = torch.empty(n, d, device="cuda")
+    kernels.mhc_read(streams, ns, blk.mhc, blk.mixer_norm, cfg.rms_eps, cfg.mhc_iterations, maps,
+                     out_bf16=ob, out_f32=of)
+    p = {k: sd[k].numpy() for k in sd if k.startswith("recurrent_core.0.")}
+    (pre, post, res), hidden = mhc.read(x, p, "recurrent_core.0.mhc.", ns, cfg.mhc_iterations)
+    ref_maps = np.concatenate([pre, post, res.reshape(n, -1)], axis=1)
+    got_maps = maps.cpu().numpy()
+    assert np.allclose(got_maps, ref_maps, rtol=1e-4, atol=1e-5), np.abs(got_maps - ref_maps).max()
+    normed = rmsnorm(hidden, p["recurrent_core.0.mixer_norm.weight"], cfg.rms_eps)
+    assert _rel(of.cpu().numpy(), normed) < 1e-4
+    assert _rel(ob.float().cpu().numpy(), normed) < 1e-2
+    upd = rng.normal(size=(n, d)).astype(np.float32)
+    upd_bf = torch.from_numpy(upd).cuda().to(torch.bfloat16)
+    kernels.mhc_write(streams, ns, blk.mhc, maps, upd_bf)
+    want = mhc.write(x, upd_bf.float().cpu().numpy(), (pre, post, res), p, "recurrent_core.0.mhc.")
+    got = streams.cpu().numpy().reshape(n, ns, d)
+    assert np.allclose(got, want, rtol=1e-4, atol=1e-4), np.abs(got - want).max()

@@ -44,3 +44,35 @@ def test_package_decode_step_drops_the_loop_output():
     emb_only = m.head(m.embed(tok))
     np.testing.assert_allclose(g["mini_pkg_step0_logits"], emb_only, rtol=1e-3, atol=1e-4)
     assert np.abs(g["mini_step_logits"][:, 0] - emb_only).max() > 1e-2
+
+
+def test_mhc_model_prefill_and_greedy_decode_match_reference():
+    """Four hyper-connection streams (model/layers/mhc.py) around every sub-layer."""
+    g = golden("mhc")
+    np.testing.assert_allclose(g["mhc_prefill_last"], g["mhc_sa_prefill_last"], rtol=1e-5, atol=1e-6)
+    m = _oracle(inputs.mhc_config())
+    logits, state = m.forward(inputs.mini_prompt())
+    np.testing.assert_allclose(logits[:, -1], g["mhc_prefill_last"], rtol=1e-5, atol=1e-5)
+    last = logits[:, -1]
+    for i in range(g["mhc_tokens"].shape[1]):
+        tok = last.argmax(-1)
+        np.testing.assert_array_equal(tok, g["mhc_tokens"][:, i])
+        last, state = m.decode_step(tok, state)
+        np.testing.assert_allclose(last, g["mhc_step_logits"][:, i], rtol=1e-5, atol=1e-5)
+
+
+def test_mhc_config_conversion():
+    import pytest
+    from hybrid_llm_b200.config import HybridConfig
+
+    cfg = inputs.mhc_config()
+    assert HybridConfig.from_v6(inputs.v6_mapping(cfg)) == cfg
+    assert cfg.streams == 4 and inputs.mini_config().streams == 1
+    base = inputs.v6_mapping(cfg)
+    for key, value in (("shared_across_loops", False),
+                       ("preserve_streams_across_loop_boundary", False), ("streams", 3)):
+        bad = dict(base, mhc=dict(base["mhc"], **{key: value}))
+        with pytest.raises(ValueError):
+            HybridConfig.from_v6(bad)
+    off = dict(base, mhc=dict(enabled=False, streams=1))
+    assert HybridConfig.from_v6(off).mhc_streams == 0
