@@ -354,6 +354,74 @@ def secondary_moe(p: dict, reps: int = 10) -> dict:
             "expert_load": counts}
 
 
+def secondary_mhc(p: dict, reps: int = 10) -> dict:
+    """Hyper-connection read / write around one sub-layer: 16384 tokens x D=1024
+    with 4 fp32 streams (256 MB, above L2), L2 flushed before each timed call.
+    Algorithmic bytes: write = streams read + written + bf16 update; read
+    kernel = streams + bf16 and fp32 outputs (+ maps); theta GEMM = streams."""
+    import numpy as np
+    import torch
+
+    from hybrid_llm_b200 import kernels
+    from hybrid_llm_b200.weights import MhcBlock
+
+    n, d, ns = 16384, 1024, 4
+    nm = 2 * ns + ns * ns
+    g = torch.Generator(device="cuda").manual_seed(0)
+    rnd = lambda *shape, s=1.0: torch.randn(*shape, device="cuda", generator=g) * s
+    blk = MhcBlock(theta=rnd(nm, ns * d, s=0.02).contiguous(), stream_scale=1 + rnd(ns, d, s=0.1),
+                   ln_w=1 + rnd(d, s=0.1), ln_b=rnd(d, s=0.1),
+                   bias=torch.cat([rnd(2 * ns, s=0.1), (torch.eye(ns, device="cuda") * 4).reshape(-1)]),
+                   scalars=torch.tensor([0.3, 0.3, 0.3, 0.3], device="cuda"))
+    norm_w = 1 + rnd(d, s=0.1)
+    streams = rnd(n, ns * d)
+    upd = rnd(n, d).bfloat16()
+    maps = torch.empty(n, nm, device="cuda")
+    ob = torch.empty(n, d, dtype=torch.bfloat16, device="cuda")
+    of = torch.empty(n, d, device="cuda")
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    iters = 10
+
+    def read_kernel(raw):
+        kernels._native.call("llmyb_mhc_read", streams.data_ptr(), n, ns, d, raw.data_ptr(),
+                             raw.stride(0), raw.stride(1), blk.bias.data_ptr(), blk.scalars.data_ptr(), blk.ln_w.data_ptr(),
+                             blk.ln_b.data_ptr(), norm_w.data_ptr(), 1e-6, iters, maps.data_ptr(),
+                             ob.data_ptr(), of.data_ptr(), kernels._stream())
+
+    raw = torch.mm(streams, blk.theta.t())
+    parts = {"write": lambda: kernels.mhc_write(streams, ns, blk, maps, upd),
+             "theta_gemm": lambda: torch.mm(streams, blk.theta.t(), out=raw),
+             "read": lambda: read_kernel(raw)}
+    sd4 = n * ns * d * 4
+    alg = {"write": 2 * sd4 + n * d * 2, "theta_gemm": sd4 + n * nm * 4,
+           "read": sd4 + n * nm * 8 + n * d * 6}
+    for f in parts.values():
+        for _ in range(3):
+            f()
+    res = {"workload": f"mHC read/write, {n} tokens x D={d}, {ns} fp32 streams, "
+                       f"{iters} Sinkhorn iterations"}
+    total = 0.0
+    for name, f in parts.items():
+        times = []
+        for _ in range(max(1, reps)):
+            flush.zero_()
+            a, b = _events()
+            a.record()
+            f()
+            b.record()
+            torch.cuda.synchronize()
+            times.append(a.elapsed_time(b))
+        t = float(np.median(times)) * 1e-3
+        total += t
+        gbs = alg[name] / t / 1e9
+        res[f"{name}_us"] = t * 1e6
+        res[f"{name}_gbs"] = gbs
+        res[f"{name}_frac_of_hbm"] = gbs / p["hbm_gbs"]
+    res["sublayer_us"] = total * 1e6
+    res["algorithmic_bytes"] = alg
+    return res
+
+
 def secondary_prefill(p: dict, reps: int = 5, batch: int = 8) -> dict:
     """Long-context prefill kernels: banded attention and the GDN chunked scan
     (batch 8 is the workload; a smaller batch serves kernel profiles)."""
@@ -646,6 +714,7 @@ def run_ours(args) -> None:
         secondary["single_block"] = secondary_block(p)
         secondary["moe_layer"] = secondary_moe(p)
         secondary["long_prefill"] = secondary_prefill(p)
+        secondary["mhc"] = secondary_mhc(p)
     if secondary:
         line["secondary"] = secondary
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -692,7 +761,8 @@ def main() -> None:
                     help="skip the large expert-parallel decode measurement")
     ap.add_argument("--ep-exchange", choices=["p2p", "nccl"], default="p2p",
                     help="expert-parallel exchange of --only ep_decode")
-    ap.add_argument("--only", choices=["single_block", "moe_layer", "long_prefill", "ep_decode"],
+    ap.add_argument("--only", choices=["single_block", "moe_layer", "long_prefill", "ep_decode",
+                                       "mhc"],
                     default=None,
                     help="run one secondary workload alone (used for kernel profiles)")
     ap.add_argument("--prefill-batch", type=int, default=8,
@@ -723,6 +793,8 @@ def main() -> None:
             res = secondary_prefill(peaks(), reps=args.steps, batch=args.prefill_batch)
         elif args.only == "single_block":
             res = secondary_block(peaks(), reps=args.steps)
+        elif args.only == "mhc":
+            res = secondary_mhc(peaks(), reps=args.steps)
         else:
             res = secondary_moe(peaks(), reps=args.steps)
         print(json.dumps({"only": args.only, **res}), flush=True)

@@ -98,7 +98,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "llmyb_mhc_sinkhorn4": (I32, [P, P, I32, I32, P]),
     "llmyb_moe_selected_fp32": (I32, [P, P, P, P, P, P, P, P, I32, I32, I32, I32, P]),
     # hyper-connections
-    "llmyb_mhc_read": (I32, [P, I32, I32, I32, P, P, P, P, P, P, F32, I32, P, P, P, P]),
+    "llmyb_mhc_read": (I32, [P, I32, I32, I32, P, I64, I64, P, P, P, P, P, F32, I32, P, P, P, P]),
     "llmyb_mhc_write": (I32, [P, I32, I32, I32, P, P, I32, P, P, P, P]),
 }
 

@@ -130,10 +130,13 @@ __device__ __forceinline__ float group_lse_cols(float v) {
   return m + logf(e);
 }
 
-template <int S>
+// C = float4 chunks per thread and stream (D <= 1024 C): the streams of the
+// token stay in registers across the reductions.  raw logits of token n, map
+// o at raw[n * raw_tok + o * raw_map] (either GEMM orientation).
+template <int S, int C>
 __global__ void __launch_bounds__(kThreads) mhc_read_kernel(
-    const float* __restrict__ streams, const float* __restrict__ raw,
-    const float* __restrict__ bias, const float* __restrict__ scalars,
+    const float* __restrict__ streams, const float* __restrict__ raw, int64_t raw_tok,
+    int64_t raw_map, const float* __restrict__ bias, const float* __restrict__ scalars,
     const float* __restrict__ ln_w, const float* __restrict__ ln_b,
     const float* __restrict__ norm_w, float rms_eps, int iters, int D,
     float* __restrict__ maps, __nv_bfloat16* __restrict__ out_bf16, float* __restrict__ out_f32) {
@@ -144,10 +147,10 @@ __global__ void __launch_bounds__(kThreads) mhc_read_kernel(
   const int tid = threadIdx.x, lane = tid & 31;
   const float* x = streams + n * S * D;
 
-  float4 st[S][kMaxChunks];
+  float4 st[S][C];
   float ss = 0.f;
 #pragma unroll
-  for (int c = 0; c < kMaxChunks; ++c) {
+  for (int c = 0; c < C; ++c) {
     const int d = (tid + c * kThreads) * 4;
 #pragma unroll
     for (int s = 0; s < S; ++s) {
@@ -160,11 +163,12 @@ __global__ void __launch_bounds__(kThreads) mhc_read_kernel(
   const float r = rsqrtf(block_sum(ss, red) / static_cast<float>(S * D) + FLT_EPSILON);
 
   if (tid < 32) {
-    const float* lg = raw + n * M;
+    const float* lg = raw + n * raw_tok;
     // pre / post: lanes [0, 2S)
     if (lane < 2 * S) {
       const bool is_pre = lane < S;
-      const float z = __ldg(scalars + (is_pre ? 0 : 1)) * (r * __ldg(lg + lane)) + __ldg(bias + lane);
+      const float z = __ldg(scalars + (is_pre ? 0 : 1)) * (r * __ldg(lg + lane * raw_map)) +
+                      __ldg(bias + lane);
       const float v = is_pre ? sigmoidf_(z) : 2.0f * sigmoidf_(z);
       maps[n * M + lane] = v;
       if (is_pre) pre_s[lane] = v;
@@ -173,7 +177,8 @@ __global__ void __launch_bounds__(kThreads) mhc_read_kernel(
     // log domain, rows then columns per iteration (mhc.py:12-17)
     float a = 0.f;
     if (lane < S * S)
-      a = __ldg(scalars + 2) * (r * __ldg(lg + 2 * S + lane)) + __ldg(bias + 2 * S + lane);
+      a = __ldg(scalars + 2) * (r * __ldg(lg + (2 * S + lane) * raw_map)) +
+          __ldg(bias + 2 * S + lane);
     for (int it = 0; it < iters; ++it) {
       a -= group_lse_rows<S>(a);
       a -= group_lse_cols<S>(a);
@@ -186,10 +191,10 @@ __global__ void __launch_bounds__(kThreads) mhc_read_kernel(
   float pre[S];
 #pragma unroll
   for (int s = 0; s < S; ++s) pre[s] = pre_s[s];
-  float4 v[kMaxChunks];
+  float4 v[C];
   float sum = 0.f;
 #pragma unroll
-  for (int c = 0; c < kMaxChunks; ++c) {
+  for (int c = 0; c < C; ++c) {
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
     for (int s = 0; s < S; ++s) {
@@ -204,7 +209,7 @@ __global__ void __launch_bounds__(kThreads) mhc_read_kernel(
   const float mean = block_sum(sum, red) / static_cast<float>(D);
   float var = 0.f;
 #pragma unroll
-  for (int c = 0; c < kMaxChunks; ++c) {
+  for (int c = 0; c < C; ++c) {
     if ((tid + c * kThreads) * 4 < D) {
       const float a0 = v[c].x - mean, a1 = v[c].y - mean, a2 = v[c].z - mean, a3 = v[c].w - mean;
       var += a0 * a0 + a1 * a1 + a2 * a2 + a3 * a3;
@@ -213,7 +218,7 @@ __global__ void __launch_bounds__(kThreads) mhc_read_kernel(
   const float rstd = rsqrtf(block_sum(var, red) / static_cast<float>(D) + 1e-5f);
   float hs = 0.f;
 #pragma unroll
-  for (int c = 0; c < kMaxChunks; ++c) {
+  for (int c = 0; c < C; ++c) {
     const int d = (tid + c * kThreads) * 4;
     if (d < D) {
       const float4 w = __ldg(reinterpret_cast<const float4*>(ln_w + d));
@@ -228,7 +233,7 @@ __global__ void __launch_bounds__(kThreads) mhc_read_kernel(
   // the block's RMSNorm of the read value
   const float rn = rsqrtf(block_sum(hs, red) / static_cast<float>(D) + rms_eps);
 #pragma unroll
-  for (int c = 0; c < kMaxChunks; ++c) {
+  for (int c = 0; c < C; ++c) {
     const int d = (tid + c * kThreads) * 4;
     if (d < D) {
       float4 w = make_float4(1.f, 1.f, 1.f, 1.f);
@@ -282,8 +287,29 @@ LLMYB_API int32_t llmyb_mhc_write(float* streams, int32_t n_tokens, int32_t n_st
   return launch_status();
 }
 
+namespace {
+template <int S>
+void launch_read(int32_t n, int32_t D, const float* streams, const float* raw, int64_t raw_tok,
+                 int64_t raw_map, const float* bias, const float* scalars, const float* ln_w,
+                 const float* ln_b, const float* norm_w, float eps, int32_t iters, float* maps,
+                 __nv_bfloat16* ob, float* of, cudaStream_t s) {
+  const int c = (D + kThreads * 4 - 1) / (kThreads * 4);
+#define LLMYB_MHC_READ(C_)                                                                   \
+  mhc_read_kernel<S, C_><<<n, kThreads, 0, s>>>(streams, raw, raw_tok, raw_map, bias, scalars, \
+                                                ln_w, ln_b, norm_w, eps, iters, D, maps, ob, of)
+  if (c <= 1)
+    LLMYB_MHC_READ(1);
+  else if (c <= 2)
+    LLMYB_MHC_READ(2);
+  else
+    LLMYB_MHC_READ(4);
+#undef LLMYB_MHC_READ
+}
+}  // namespace
+
 LLMYB_API int32_t llmyb_mhc_read(const float* streams, int32_t n_tokens, int32_t n_streams,
-                                 int32_t d_model, const float* raw, const float* bias,
+                                 int32_t d_model, const float* raw, int64_t raw_tok,
+                                 int64_t raw_map, const float* bias,
                                  const float* scalars, const float* ln_w, const float* ln_b,
                                  const float* norm_w, float rms_eps, int32_t iterations,
                                  float* maps, void* out_bf16, float* out_f32, void* stream) {
@@ -299,19 +325,16 @@ LLMYB_API int32_t llmyb_mhc_read(const float* streams, int32_t n_tokens, int32_t
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   switch (n_streams) {
     case 1:
-      mhc_read_kernel<1><<<n_tokens, kThreads, 0, s>>>(streams, raw, bias, scalars, ln_w, ln_b,
-                                                       norm_w, rms_eps, iterations, d_model, maps,
-                                                       ob, out_f32);
+      launch_read<1>(n_tokens, d_model, streams, raw, raw_tok, raw_map, bias, scalars, ln_w, ln_b,
+                     norm_w, rms_eps, iterations, maps, ob, out_f32, s);
       break;
     case 2:
-      mhc_read_kernel<2><<<n_tokens, kThreads, 0, s>>>(streams, raw, bias, scalars, ln_w, ln_b,
-                                                       norm_w, rms_eps, iterations, d_model, maps,
-                                                       ob, out_f32);
+      launch_read<2>(n_tokens, d_model, streams, raw, raw_tok, raw_map, bias, scalars, ln_w, ln_b,
+                     norm_w, rms_eps, iterations, maps, ob, out_f32, s);
       break;
     case 4:
-      mhc_read_kernel<4><<<n_tokens, kThreads, 0, s>>>(streams, raw, bias, scalars, ln_w, ln_b,
-                                                       norm_w, rms_eps, iterations, d_model, maps,
-                                                       ob, out_f32);
+      launch_read<4>(n_tokens, d_model, streams, raw, raw_tok, raw_map, bias, scalars, ln_w, ln_b,
+                     norm_w, rms_eps, iterations, maps, ob, out_f32, s);
       break;
     default:
       return LLMYB_EUNSUPPORTED;

@@ -838,6 +838,16 @@ def moe_selected_fp32(x: torch.Tensor, idx: torch.Tensor, prob: torch.Tensor,
 
 
 # --------------------------------------------------------- hyper-connections
+_ZEROS: dict = {}
+
+
+def _zero_scalar(device: torch.device) -> torch.Tensor:
+    z = _ZEROS.get(device)
+    if z is None:
+        z = _ZEROS[device] = torch.zeros(4, dtype=torch.float32, device=device)
+    return z
+
+
 def mhc_read(streams: torch.Tensor, n_streams: int, mhc, norm_w: torch.Tensor | None, eps: float,
              iterations: int, maps: torch.Tensor, *, out_bf16: torch.Tensor | None = None,
              out_f32: torch.Tensor | None = None) -> None:
@@ -847,8 +857,14 @@ def mhc_read(streams: torch.Tensor, n_streams: int, mhc, norm_w: torch.Tensor | 
     _require_cuda(streams, maps, out_bf16, out_f32)
     n = streams.shape[0]
     d = streams.shape[1] // n_streams
-    raw = torch.mm(streams, mhc.theta.t())  # theta with the mapping-norm weight folded in
-    _native.call("llmyb_mhc_read", _ptr(streams), n, n_streams, d, _ptr(raw), _ptr(mhc.bias),
+    if getattr(mhc, "static", False):
+        # an all-zero theta gives zero logits: one zero read for every map
+        raw, ld_tok, ld_map = _zero_scalar(streams.device), 0, 0
+    else:
+        raw = torch.mm(streams, mhc.theta.t())  # theta with the mapping-norm weight folded in
+        ld_tok, ld_map = raw.stride(0), raw.stride(1)
+    _native.call("llmyb_mhc_read", _ptr(streams), n, n_streams, d, _ptr(raw), ld_tok, ld_map,
+                 _ptr(mhc.bias),
                  _ptr(mhc.scalars), _ptr(mhc.ln_w), _ptr(mhc.ln_b), _ptr(norm_w), float(eps),
                  int(iterations), _ptr(maps), _ptr(out_bf16), _ptr(out_f32), _stream())
 

@@ -191,6 +191,7 @@ class MhcBlock:
     ln_b: torch.Tensor          # [D] fp32 stream_norm bias
     bias: torch.Tensor          # [2S+S*S] fp32: pre_bias | post_bias | residual_bias
     scalars: torch.Tensor       # [4] fp32: alpha_pre, alpha_post, alpha_residual, sigmoid(gating)
+    static: bool = False        # theta is all zero: input-independent maps (mhc.py:114-118)
 
 
 @dataclass
@@ -278,6 +279,7 @@ class ModelWeights:
                     scalars=torch.tensor([sc("alpha_pre"), sc("alpha_post"), sc("alpha_residual"),
                                           float(torch.sigmoid(torch.tensor(sc("gating_logit"))))],
                                          dtype=torch.float32, device=dev))
+                mhc.static = not bool(torch.count_nonzero(mhc.theta))
             blocks.append(Block(cfg.block_kind(j), f32(p + "mixer_norm.weight"),
                                 f32(p + "ffn_norm.weight"), mixer, moe, mhc))
         ns = cfg.streams

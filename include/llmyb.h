@@ -490,8 +490,9 @@ int32_t llmyb_moe_selected_fp32(const float* x, const int64_t* idx, const float*
  * fp32 residual streams per token, laid out [N, S*D].  maps [N, 2S+S*S] fp32
  * hold pre | post | res (row-major) of a read for the write that follows it.
  *
- * llmyb_mhc_read: raw [N, 2S+S*S] = streams @ (theta * mapping_norm.weight)^T
- * (the caller's GEMM); bias = pre_bias | post_bias | residual_bias;
+ * llmyb_mhc_read: raw = the logits streams @ (theta * mapping_norm.weight)^T
+ * (the caller's GEMM), map o of token n at raw[n * raw_tok + o * raw_map]
+ * (either orientation); bias = pre_bias | post_bias | residual_bias;
  * scalars = alpha_pre, alpha_post, alpha_residual, sigmoid(gating_logit).
  * Computes the maps (mapping RMSNorm with the fp32 epsilon, sigmoids, Sinkhorn
  * with `iterations` rounds), hidden = LayerNorm(sum_s pre[s] streams[s]) with
@@ -503,7 +504,8 @@ int32_t llmyb_moe_selected_fp32(const float* x, const int64_t* idx, const float*
  * route_pos the fp32 sum of the top_k routed rows delta[route_pos[n*k + s]]
  * (the MoE combine), or zero for a null delta. */
 int32_t llmyb_mhc_read(const float* streams, int32_t n_tokens, int32_t n_streams, int32_t d_model,
-                       const float* raw, const float* bias, const float* scalars,
+                       const float* raw, int64_t raw_tok, int64_t raw_map, const float* bias,
+                       const float* scalars,
                        const float* ln_w, const float* ln_b, const float* norm_w, float rms_eps,
                        int32_t iterations, float* maps, void* out_bf16, float* out_f32,
                        void* stream);

@@ -250,3 +250,23 @@ def test_mhc_read_write_kernels(cuda, ns):
     want = mhc.write(x, upd_bf.float().cpu().numpy(), (pre, post, res), p, "recurrent_core.0.mhc.")
     got = streams.cpu().numpy().reshape(n, ns, d)
     assert np.allclose(got, want, rtol=1e-4, atol=1e-4), np.abs(got - want).max()
+
+
+def test_mhc_static_maps_skip_the_projection(cuda):
+    """An all-zero theta (the reference's static inference maps, mhc.py:114-118)
+    takes the no-GEMM path and gives the same model output as the dynamic path
+    on the same (zero) weights."""
+    from hybrid_llm_b200.model import LoopedHybridModel
+    from hybrid_llm_b200.weights import ModelWeights, synthetic_state_dict
+
+    cfg = inputs.mhc_config()
+    sd = synthetic_state_dict(cfg, seed=0)
+    zero = {k: (sd[k] * 0 if k.endswith("mhc.theta.weight") else sd[k]) for k in sd}
+    w = ModelWeights.from_state_dict(cfg, zero, "cuda")
+    assert all(b.mhc.static for b in w.blocks)
+    ids = torch.from_numpy(inputs.mini_prompt()).cuda()
+    a = LoopedHybridModel(w).forward(ids, last_logits_only=True).logits
+    for b in w.blocks:
+        b.mhc.static = False
+    b_ = LoopedHybridModel(w).forward(ids, last_logits_only=True).logits
+    assert torch.equal(a, b_)
