@@ -100,6 +100,9 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     # hyper-connections
     "llmyb_mhc_read": (I32, [P, I32, I32, I32, P, I64, I64, P, P, P, P, P, F32, I32, P, P, P, P]),
     "llmyb_mhc_write": (I32, [P, I32, I32, I32, P, P, I32, P, P, P, P]),
+    # router local context
+    "llmyb_router_ctx_prefill": (I32, [P, I32, I32, I32, I32, P, P, P, P, P]),
+    "llmyb_router_ctx_step": (I32, [P, I32, I32, I32, P, P, P, P, P, P]),
 }
 
 _lock = threading.Lock()

@@ -5,8 +5,10 @@ B200 path implements: a recurrent core of ``gdn_moe`` / ``csa_moe`` blocks run
 ``num_loops`` times, with either one plain residual stream (mHC disabled,
 ``mhc_streams == 0``) or multi-stream hyper-connections (``mhc_streams`` = 1, 2
 or 4 live streams, input-dependent maps, shared across loops, streams carried
-across loop boundaries), plain top-k softmax router (no context path), no
-shared experts, CSA with its remote compressed branch disabled
+across loop boundaries), a top-k softmax router with or without its local
+context path (``router_context``: the causal box-filtered MLA latents of the
+last ``router_local_context`` tokens; no HCA global latents), no shared
+experts, CSA with its remote compressed branch disabled
 (temporal_compression beyond any sequence), no stem/tail blocks.  ``from_v6`` converts a reference config (dataclass or mapping) and
 rejects anything outside that subset instead of silently changing the model.
 """
@@ -35,6 +37,9 @@ class HybridConfig:
     rms_eps: float = 1e-6
     mhc_streams: int = 0          # 0: plain residual; S > 0: S-stream hyper-connections
     mhc_iterations: int = 10      # Sinkhorn iterations of the residual map
+    router_context: bool = False  # ContextAwareRouter local-context path (context_router.py)
+    router_latent_dim: int = 256  # mla.latent_dim
+    router_local_context: int = 128  # router.local_context (box-filter window)
     name: str = field(default="custom", compare=False)
 
     def __post_init__(self) -> None:
@@ -51,6 +56,9 @@ class HybridConfig:
             raise ValueError("hyper-connections are implemented for 1, 2 or 4 streams")
         if self.mhc_iterations < 0:
             raise ValueError("mhc_iterations must be >= 0")
+        if self.router_context and (self.router_local_context < 1 or self.router_latent_dim < 1
+                                    or self.router_latent_dim > 1024):
+            raise ValueError("router context needs local_context >= 1 and 1 <= latent_dim <= 1024")
 
     @property
     def streams(self) -> int:
@@ -82,8 +90,14 @@ class HybridConfig:
                 raise ValueError("restarting the streams at each loop is not implemented")
         elif int(mget("streams", 1)) != 1:
             raise ValueError("mHC disabled with several streams is not implemented")
-        if sget(sub("router"), "context_aware"):
-            raise ValueError("the context-aware router path is not implemented")
+        router = sub("router")
+        rget = lambda k, default: (router.get(k, default) if isinstance(router, dict)
+                                   else getattr(router, k, default))
+        router_context = bool(rget("context_aware", True))
+        local_context = int(rget("local_context", 128))
+        mla = sub("mla") if (isinstance(cfg, dict) and "mla" in cfg) or hasattr(cfg, "mla") else {}
+        latent_dim = int(mla.get("latent_dim", 256) if isinstance(mla, dict)
+                         else getattr(mla, "latent_dim", 256))
         if sget(sub("moe"), "shared_experts") != 0:
             raise ValueError("shared experts are not implemented")
         if sub("stem_blocks") or sub("tail_blocks"):
@@ -102,6 +116,8 @@ class HybridConfig:
             moe_hidden=sget(sub("moe"), "expert_hidden"),
             conv_kernel=sget(sub("gdn"), "conv_kernel"),
             mhc_streams=mhc_streams, mhc_iterations=mhc_iters,
+            router_context=router_context, router_latent_dim=latent_dim,
+            router_local_context=local_context,
         )
 
 

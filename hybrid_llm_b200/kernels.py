@@ -885,3 +885,30 @@ def mhc_write(streams: torch.Tensor, n_streams: int, mhc, maps: torch.Tensor,
         delta = delta.contiguous()
     _native.call("llmyb_mhc_write", _ptr(streams), n, n_streams, d, _ptr(delta), _ptr(route_pos),
                  int(k), _ptr(maps), _ptr(mhc.stream_scale), _ptr(mhc.scalars), _stream())
+
+
+# ----------------------------------------------------- router local context
+def router_context_logits(r_in: torch.Tensor, moe, window: int, *, batch: int, seq: int,
+                          ring: torch.Tensor | None = None,
+                          positions: torch.Tensor | None = None) -> torch.Tensor:
+    """Router logits with the ContextAwareRouter's local context
+    (context_router.py:59-74 / :89-133): router (local + g ctx(box)) with box
+    the causal window mean of LayerNorm(down(local)).  r_in [batch*seq, D]
+    fp32 is the router-normed input; moe a weights.MoeBlock with the ctx_*
+    fields.  Prefill (positions None): the window runs over each row's `seq`
+    tokens and the last `window` latents go to `ring` [batch, window, L]; decode
+    (seq 1, positions [batch]): the new latent enters the ring first."""
+    _require_cuda(r_in, ring, positions)
+    lat = torch.mm(r_in, moe.ctx_down.t())
+    box = torch.empty_like(lat)
+    latent = lat.shape[1]
+    if positions is None:
+        _native.call("llmyb_router_ctx_prefill", _ptr(lat), int(batch), int(seq), latent,
+                     int(window), _ptr(moe.ctx_ln_w), _ptr(moe.ctx_ln_b), _ptr(box), _ptr(ring),
+                     _stream())
+    else:
+        _native.call("llmyb_router_ctx_step", _ptr(lat), int(batch), latent, int(window),
+                     _ptr(moe.ctx_ln_w), _ptr(moe.ctx_ln_b), _ptr(ring), _ptr(positions),
+                     _ptr(box), _stream())
+    logits = torch.mm(r_in, moe.router.t())
+    return logits.addmm_(box, moe.ctx_logits.t(), alpha=moe.ctx_gate)

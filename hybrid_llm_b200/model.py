@@ -74,16 +74,28 @@ class LoopedHybridModel:
         beta = proj[..., 2 * hk + 2 * hv:2 * hk + 2 * hv + h]
         return q, k, v, gate, beta
 
-    def _moe(self, blk: Block, m_bf: torch.Tensor, m_f32: torch.Tensor):
+    def _router_logits(self, blk: Block, m_f32: torch.Tensor, state: RecurrentState, key: str,
+                       bsz: int, t: int, step: bool) -> torch.Tensor:
+        """ContextAwareRouter logits (context_router.py:59-74 prefill, :89-133
+        decode step): local = RMSNorm(hidden); logits = W local, plus the local
+        context term when the router has it (the window's latents kept in
+        state.router_latents for the following decode steps)."""
+        c = self.cfg
+        r_in = torch.empty_like(m_f32)
+        kernels.add_rmsnorm(m_f32, None, blk.moe.router_norm, c.rms_eps, out_f32=r_in)
+        if not c.router_context:
+            return torch.mm(r_in, blk.moe.router.t())
+        return kernels.router_context_logits(
+            r_in, blk.moe, c.router_local_context, batch=bsz, seq=t,
+            ring=state.router_latents[key], positions=state.positions if step else None)
+
+    def _moe(self, blk: Block, m_bf: torch.Tensor, m_f32: torch.Tensor, state: RecurrentState,
+             key: str, bsz: int, t: int):
         """SparseMoE.forward without shared experts (moe.py:172-204): the routed
         expert rows and the plan whose per-token sum is the combine (added to
         the residual stream by the next add_rmsnorm_routed)."""
-        c = self.cfg
-        r_in = torch.empty_like(m_f32)
-        # ContextAwareRouter: local = RMSNorm(hidden); logits = W local (context_router.py:62-72)
-        kernels.add_rmsnorm(m_f32, None, blk.moe.router_norm, c.rms_eps, out_f32=r_in)
-        logits = torch.mm(r_in, blk.moe.router.t())
-        plan = kernels.route(logits, c.moe_top_k)
+        logits = self._router_logits(blk, m_f32, state, key, bsz, t, step=False)
+        plan = kernels.route(logits, self.cfg.moe_top_k)
         return self._experts(blk, m_bf, plan)
 
     def _add_pending(self, streams, pending, weight, **out) -> None:
@@ -178,7 +190,7 @@ class LoopedHybridModel:
                     mixed = self._csa_prefill(blk.mixer, normed, state, key, bsz, t)
                 kernels.add_rmsnorm(streams, mixed, blk.ffn_norm, c.rms_eps, out_bf16=m_bf,
                                     out_f32=m_f32)
-                pending = self._moe(blk, m_bf, m_f32)
+                pending = self._moe(blk, m_bf, m_f32, state, key, bsz, t)
         self._add_pending(streams, pending, None, normalize=False)
 
     def _mhc_write(self, streams, blk: Block, maps, pending) -> None:
@@ -218,7 +230,7 @@ class LoopedHybridModel:
                 kernels.mhc_write(streams, ns, blk.mhc, maps_mix, mixed)
                 kernels.mhc_read(streams, ns, blk.mhc, blk.ffn_norm, c.rms_eps, c.mhc_iterations,
                                  maps_ffn, out_bf16=m_bf, out_f32=m_f32)
-                pending, prev = self._moe(blk, m_bf, m_f32), blk
+                pending, prev = self._moe(blk, m_bf, m_f32, state, key, bsz, t), blk
         self._mhc_write(streams, prev, maps_ffn, pending)
 
     def _gdn_prefill(self, g: GdnBlock, normed, state: RecurrentState, key: str, bsz: int, t: int,
@@ -282,10 +294,11 @@ class LoopedHybridModel:
         d = c.d_model
         if c.mhc_streams:
             return self._decode_mhc(ids, state, loops)
-        if self.decode_fused and kernels.decode_fused_supported(
+        if self.decode_fused and not c.router_context and kernels.decode_fused_supported(
                 bsz, d, c.moe_experts, c.moe_top_k, c.gdn_heads * c.gdn_value_dim, d):
             return self._decode_fused(ids, state, loops)
-        fused_router = kernels.route_fused_supported(bsz, c.moe_experts, c.moe_top_k, d)
+        fused_router = (not c.router_context
+                        and kernels.route_fused_supported(bsz, c.moe_experts, c.moe_top_k, d))
         # 128-row tiles for the grouped expert GEMMs at a few rows per expert
         tile_m = 128
         streams = kernels.embed(ids, self.w.embed, self.w.stream_seed)
@@ -312,10 +325,8 @@ class LoopedHybridModel:
                 else:
                     kernels.add_rmsnorm(streams, mixed, blk.ffn_norm, c.rms_eps, out_bf16=m_bf,
                                         out_f32=m_f32)
-                    r_in = torch.empty_like(m_f32)
-                    kernels.add_rmsnorm(m_f32, None, blk.moe.router_norm, c.rms_eps, out_f32=r_in)
-                    plan = kernels.route(torch.mm(r_in, blk.moe.router.t()), c.moe_top_k,
-                                         tile_m=tile_m)
+                    logits = self._router_logits(blk, m_f32, state, key, bsz, 1, step=True)
+                    plan = kernels.route(logits, c.moe_top_k, tile_m=tile_m)
                 y_rows, plan = self._experts(blk, m_bf, plan)
         return self._decode_head(streams, y_rows, plan, state)
 
@@ -366,9 +377,8 @@ class LoopedHybridModel:
                 kernels.mhc_write(streams, ns, blk.mhc, maps_mix, mixed)
                 kernels.mhc_read(streams, ns, blk.mhc, blk.ffn_norm, c.rms_eps, c.mhc_iterations,
                                  maps_ffn, out_bf16=m_bf, out_f32=m_f32)
-                r_in = torch.empty_like(m_f32)
-                kernels.add_rmsnorm(m_f32, None, blk.moe.router_norm, c.rms_eps, out_f32=r_in)
-                plan = kernels.route(torch.mm(r_in, blk.moe.router.t()), c.moe_top_k, tile_m=128)
+                logits = self._router_logits(blk, m_f32, state, key, bsz, 1, step=True)
+                plan = kernels.route(logits, c.moe_top_k, tile_m=128)
                 pending, prev = self._experts(blk, m_bf, plan), blk
         self._mhc_write(streams, prev, maps_ffn, pending)
         h = kernels.rmsnorm_bf16(torch.mm(streams.to(torch.bfloat16), self.w.collapse.t()),

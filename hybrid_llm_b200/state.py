@@ -9,6 +9,9 @@ keys (model/model.py:168-171) —
     of the CSA window (token p at slot p % W).  The reference keeps the
     normed hidden rows and re-projects K/V every step (csa.py:176-178); the
     cache holds the same projections computed once.
+  * ``router_latents[key]``    [B, W, L] fp32 ring of the router's LayerNorm'd
+    MLA latents of the last W positions (router_latent_histories,
+    model/model.py:239-247; only with the router's local context).
   * ``positions`` [B] int32, position of the next token of each row.
 All buffers are allocated once for a batch size so that a captured decode
 graph can update them in place.
@@ -49,6 +52,15 @@ class RecurrentState:
                         dtype=torch.bfloat16, device=self.device)
                     self.local_v[key] = torch.zeros(batch, cfg.csa_window, d,
                                                     dtype=torch.bfloat16, device=self.device)
+        # router local context: the LayerNorm'd latents of the last W positions
+        # (position p at slot p % W) per loop and block
+        self.router_latents: dict[str, torch.Tensor] = {}
+        if cfg.router_context:
+            for i in range(cfg.num_loops):
+                for j in range(cfg.n_blocks):
+                    self.router_latents[state_key(i, j)] = torch.zeros(
+                        batch, cfg.router_local_context, cfg.router_latent_dim,
+                        dtype=torch.float32, device=self.device)
         self.positions = torch.zeros(batch, dtype=torch.int32, device=self.device)
 
     def fill_synthetic(self, position: int, seed: int = 0) -> None:
@@ -68,26 +80,30 @@ class RecurrentState:
     def reset_rows(self, rows: torch.Tensor) -> None:
         """Clear the state of the selected rows (recurrent_state.py:218-244)."""
         mask = rows.to(device=self.device, dtype=torch.bool)
-        for t in (*self.gdn_states.values(), *self.gdn_conv_histories.values()):
+        for t in (*self.gdn_states.values(), *self.gdn_conv_histories.values(),
+                  *self.router_latents.values()):
             t[mask] = 0
         self.positions[mask] = 0
 
     def zero_(self) -> None:
         """Zero every state tensor and position (a fresh conversation)."""
         for t in (*self.gdn_states.values(), *self.gdn_conv_histories.values(),
-                  *self.local_k.values(), *self.local_v.values(), self.positions):
+                  *self.local_k.values(), *self.local_v.values(), *self.router_latents.values(),
+                  self.positions):
             t.zero_()
 
     def nbytes(self) -> int:
         tensors = (*self.gdn_states.values(), *self.gdn_conv_histories.values(),
-                   *self.local_k.values(), *self.local_v.values(), self.positions)
+                   *self.local_k.values(), *self.local_v.values(),
+                   *self.router_latents.values(), self.positions)
         return sum(t.numel() * t.element_size() for t in tensors)
 
     def state_dict(self) -> dict[str, torch.Tensor]:
         out: dict[str, torch.Tensor] = {"positions": self.positions.clone()}
         for name, table in (("gdn_states", self.gdn_states),
                             ("gdn_conv_histories", self.gdn_conv_histories),
-                            ("local_k", self.local_k), ("local_v", self.local_v)):
+                            ("local_k", self.local_k), ("local_v", self.local_v),
+                            ("router_latents", self.router_latents)):
             for key, t in table.items():
                 out[f"{name}.{key}"] = t.clone()
         return out
@@ -96,6 +112,7 @@ class RecurrentState:
         self.positions.copy_(sd["positions"])
         for name, table in (("gdn_states", self.gdn_states),
                             ("gdn_conv_histories", self.gdn_conv_histories),
-                            ("local_k", self.local_k), ("local_v", self.local_v)):
+                            ("local_k", self.local_k), ("local_v", self.local_v),
+                            ("router_latents", self.router_latents)):
             for key, t in table.items():
                 t.copy_(sd[f"{name}.{key}"])

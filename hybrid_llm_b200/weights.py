@@ -8,6 +8,9 @@ the layer modules), so a reference checkpoint's tensors load directly:
        mapping_norm.weight [S*D], theta.weight [2S+S*S, S*D], pre_bias [S],
        post_bias [S], residual_bias [S,S], alpha_pre, alpha_post, alpha_residual,
        gating_logit, read_logits, write_logits}        (mhc.py:62-88; S streams)
+  router context  recurrent_core.{j}.moe.router.{latent_memory.down.weight [L,D],
+       latent_memory.norm.{weight,bias} [L], local_context_out.weight [D,L],
+       context_out.weight [D,D], route_gate}         (context_router.py:14-27)
   GDN  recurrent_core.{j}.mixer.{q,k,v,gate,out}_proj.weight, beta_proj.{weight,bias},
        conv.weight [D,1,4], decay_logit [H]          (gated_deltanet.py:105-113)
   CSA  recurrent_core.{j}.mixer.{query,key,value,local_out,out}.weight  (csa.py:23-28)
@@ -85,6 +88,13 @@ def parameter_shapes(cfg: HybridConfig) -> dict[str, tuple[int, ...]]:
             })
         shapes[p + "moe.router.norm.weight"] = (d,)
         shapes[p + "moe.router.logits.weight"] = (e, d)
+        if cfg.router_context:
+            q, lat = p + "moe.router.", cfg.router_latent_dim
+            shapes.update({
+                q + "latent_memory.down.weight": (lat, d), q + "latent_memory.norm.weight": (lat,),
+                q + "latent_memory.norm.bias": (lat,), q + "local_context_out.weight": (d, lat),
+                q + "context_out.weight": (d, d), q + "route_gate": (),
+            })
         for x in range(e):
             q = f"{p}moe.experts.{x}."
             shapes[q + "gate_proj.weight"] = (f, d)
@@ -147,7 +157,11 @@ def synthetic_state_dict(cfg: HybridConfig, seed: int = 0, device: str | torch.d
             gen = torch.Generator(device=device)
             gen.manual_seed((seed * 1_000_003 + zlib.crc32(name.encode())) % (2 ** 62))
             return torch.randn(shape, generator=gen, device=device, dtype=torch.float32) * std
-        if name.endswith("beta_proj.bias"):
+        if name.endswith("beta_proj.bias") or name.endswith("latent_memory.norm.bias"):
+            return torch.zeros(shape, device=device)
+        if name.endswith("route_gate"):
+            # sigmoid(0) = 0.5 (the reference's init, -4.595, gives 0.01) so that
+            # the local context visibly moves the routing logits
             return torch.zeros(shape, device=device)
         if name.endswith("decay_logit"):
             return torch.full(shape, 2.0, device=device)
@@ -180,6 +194,12 @@ class MoeBlock:
     w13: torch.Tensor          # [E, 2F, D] bf16 (interleaved gate/up)
     w2: torch.Tensor           # [E, D, F] bf16
     router_folded: torch.Tensor | None = None  # [E, D] fp32 = router * ffn_norm * router_norm
+    # local-context path of the ContextAwareRouter (None without it)
+    ctx_down: torch.Tensor | None = None   # [L, D] fp32 latent_memory.down
+    ctx_ln_w: torch.Tensor | None = None   # [L] fp32 latent_memory.norm (LayerNorm)
+    ctx_ln_b: torch.Tensor | None = None   # [L] fp32
+    ctx_logits: torch.Tensor | None = None  # [E, L] fp32 = router @ context_out @ local_context_out
+    ctx_gate: float = 0.0                  # sigmoid(route_gate)
 
 
 @dataclass
@@ -265,6 +285,16 @@ class ModelWeights:
                            router=f32(p + "moe.router.logits.weight"), w13=w13, w2=w2)
             moe.router_folded = kernels.fold_router(moe.router, f32(p + "ffn_norm.weight"),
                                                     moe.router_norm)
+            if cfg.router_context:
+                q = p + "moe.router."
+                moe.ctx_down = f32(q + "latent_memory.down.weight")
+                moe.ctx_ln_w = f32(q + "latent_memory.norm.weight")
+                moe.ctx_ln_b = f32(q + "latent_memory.norm.bias")
+                # logits = router (local + g context_out(local_context_out(box)))
+                #        = router local + g (router context_out local_context_out) box
+                moe.ctx_logits = (moe.router @ f32(q + "context_out.weight")
+                                  @ f32(q + "local_context_out.weight")).contiguous()
+                moe.ctx_gate = float(torch.sigmoid(sd[q + "route_gate"].reshape(()).float()))
             mhc = None
             if cfg.mhc_streams:
                 q = p + "mhc."
@@ -317,6 +347,6 @@ class ModelWeights:
         for b in self.blocks:
             yield from (b.mixer_norm, b.ffn_norm)
             yield from vars(b.mixer).values()
-            yield from (t for t in vars(b.moe).values() if t is not None)
+            yield from (t for t in vars(b.moe).values() if isinstance(t, torch.Tensor))
             if b.mhc is not None:
                 yield from vars(b.mhc).values()

@@ -514,6 +514,28 @@ int32_t llmyb_mhc_write(float* streams, int32_t n_tokens, int32_t n_streams, int
                         const float* maps, const float* stream_scale, const float* scalars,
                         void* stream);
 
+/* ------------------------------------------------- router local context
+ * The ContextAwareRouter's local-context path (model/layers/context_router.py:59-74,
+ * :89-133; mla_memory.py:23-48) without HCA latents: latents = LayerNorm(down(local))
+ * (eps 1e-5) and their causal mean over the last `window` tokens ("box"),
+ * which the caller's GEMMs turn into router logits.  fp32 throughout.
+ *
+ * llmyb_router_ctx_prefill: lat [batch*seq, latent] = down(local) in, the
+ * LayerNorm'd latents out (in place); box [batch*seq, latent]; ring
+ * [batch, window, latent] (nullable) receives the last `window` latents of each
+ * row (position p at slot p % window).  latent <= 1024.
+ *
+ * llmyb_router_ctx_step: one decode token per row at positions[b]: lat
+ * [batch, latent] in (LayerNorm'd in place), stored at ring slot
+ * positions[b] % window; box [batch, latent] = mean of the latents of
+ * positions max(0, p-window+1) .. p. */
+int32_t llmyb_router_ctx_prefill(float* lat, int32_t batch, int32_t seq, int32_t latent,
+                                 int32_t window, const float* ln_w, const float* ln_b, float* box,
+                                 float* ring, void* stream);
+int32_t llmyb_router_ctx_step(float* lat, int32_t batch, int32_t latent, int32_t window,
+                              const float* ln_w, const float* ln_b, float* ring,
+                              const int32_t* positions, float* box, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

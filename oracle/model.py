@@ -49,13 +49,41 @@ class OracleModel:
         p = f"recurrent_core.{j}.mixer."
         return {n: self.p[p + n + ".weight"] for n in ("query", "key", "value", "local_out", "out")}
 
-    def _moe(self, j, m):
+    def _router_logits(self, j, m, state, key, step):
+        """ContextAwareRouter.forward / forward_step (context_router.py:59-74,
+        :89-133) without HCA latents, on m [B, T, D]: local = RMSNorm(m);
+        with the local context, route_input = local + sigmoid(route_gate) *
+        context_out(local_context_out(window mean of LayerNorm(down(local))))
+        (mla_memory.py:23-48), the window being the last W tokens in prefill
+        and the kept latent history plus the new token in a decode step."""
+        c, p = self.cfg, f"recurrent_core.{j}.moe.router."
+        g = lambda n: self.p[p + n]
+        local = rmsnorm(m, g("norm.weight"), c.rms_eps)
+        if not c.router_context:
+            return local @ g("logits.weight").T
+        z = local @ g("latent_memory.down.weight").T
+        mu = z.mean(-1, keepdims=True)
+        var = ((z - mu) ** 2).mean(-1, keepdims=True)
+        lat = (z - mu) / np.sqrt(var + 1e-5) * g("latent_memory.norm.weight") + \
+            g("latent_memory.norm.bias")
+        w = c.router_local_context
+        if step:
+            hist = np.concatenate([state["rlat"][key], lat], axis=1)[:, -w:]
+            state["rlat"][key] = hist
+            box = hist.mean(1, keepdims=True)
+        else:
+            box = np.stack([lat[:, max(0, t - w + 1):t + 1].mean(1) for t in range(lat.shape[1])], 1)
+            state["rlat"][key] = lat[:, -w:]
+        ctx = (box @ g("local_context_out.weight").T) @ g("context_out.weight").T
+        gate = 1.0 / (1.0 + np.exp(-np.asarray(g("route_gate"), dtype=np.float64)))
+        return (local + gate * ctx) @ g("logits.weight").T
+
+    def _moe(self, j, m, state=None, key=None, step=False):
         """SparseMoE.forward (moe.py:172-199) without shared experts."""
         c, p = self.cfg, f"recurrent_core.{j}.moe."
         lead = m.shape[:-1]
         flat = m.reshape(-1, m.shape[-1])
-        r = rmsnorm(flat, self.p[p + "router.norm.weight"], c.rms_eps)
-        logits = r @ self.p[p + "router.logits.weight"].T
+        logits = self._router_logits(j, m, state, key, step).reshape(flat.shape[0], -1)
         idx, prob = routing.router_topk(logits.astype(np.float32), c.moe_top_k)
         if j not in self._experts:
             e = c.moe_experts
@@ -84,7 +112,7 @@ class OracleModel:
 
     def new_state(self, batch):
         c = self.cfg
-        st = {"gdn": {}, "conv": {}, "hist": {}, "pos": np.zeros(batch, dtype=np.int64)}
+        st = {"gdn": {}, "conv": {}, "hist": {}, "rlat": {}, "pos": np.zeros(batch, dtype=np.int64)}
         for i in range(c.num_loops):
             for j in range(c.n_blocks):
                 if c.block_kind(j) == "gdn":
@@ -110,7 +138,7 @@ class OracleModel:
                     state["hist"][(i, j)] = normed[:, -(c.csa_window - 1):]
                 x = self._write(j, x, mixed, maps)
                 m, maps = self._read(j, x, "ffn_norm")
-                y, lg = self._moe(j, m)
+                y, lg = self._moe(j, m, state, (i, j))
                 if router_logits is not None:
                     router_logits.append(lg)
                 x = self._write(j, x, y, maps)
@@ -168,7 +196,7 @@ class OracleModel:
                     state["hist"][(i, j)] = win[:, -(c.csa_window - 1):]
                 x = self._write(j, x, mixed, maps)
                 m, maps = self._read(j, x, "ffn_norm")
-                y, _ = self._moe(j, m)
+                y, _ = self._moe(j, m, state, (i, j), step=True)
                 x = self._write(j, x, y, maps)
         state["pos"] += 1
         return self.head(x[:, 0]), state

@@ -135,6 +135,14 @@ def mhc_config():
     return dataclasses.replace(mini_config(), mhc_streams=4, mhc_iterations=10, name="mini-mhc")
 
 
+def router_ctx_config():
+    """The mini model with the context-aware router: 64-wide latents averaged
+    over the last 8 tokens (the 50-token prompt fills the window)."""
+    import dataclasses
+    return dataclasses.replace(mini_config(), router_context=True, router_latent_dim=64,
+                               router_local_context=8, name="mini-router-ctx")
+
+
 def llmy_config():
     """A small looped hybrid model for the .llmy format fixture."""
     from hybrid_llm_b200.config import HybridConfig
@@ -155,9 +163,9 @@ def block_hidden():
 
 
 def v6_mapping(cfg) -> dict:
-    """Reference V6Config fields for a HybridConfig (mHC as configured; context
-    router, shared experts, loop memory, halting and the CSA remote branch
-    switched off)."""
+    """Reference V6Config fields for a HybridConfig (mHC and the router's local
+    context path as configured; shared experts, loop memory, halting and the
+    CSA remote branch switched off)."""
     return dict(
         vocab_size=cfg.vocab_size, d_model=cfg.d_model, physical_blocks=cfg.n_blocks,
         stem_blocks=0, recurrent_blocks=cfg.n_blocks, tail_blocks=0, num_loops=cfg.num_loops,
@@ -169,7 +177,8 @@ def v6_mapping(cfg) -> dict:
                  value_head_dim=cfg.gdn_value_dim, conv_kernel=cfg.conv_kernel),
         moe=dict(routed_experts=cfg.moe_experts, shared_experts=0, routed_top_k=cfg.moe_top_k,
                  expert_hidden=cfg.moe_hidden),
-        router=dict(context_aware=False),
+        router=dict(context_aware=cfg.router_context, local_context=cfg.router_local_context),
+        mla=dict(latent_dim=cfg.router_latent_dim),
         csa=dict(temporal_compression=10 ** 9, local_window=cfg.csa_window,
                  index_heads=cfg.csa_heads, index_head_dim=cfg.csa_head_dim, index_top_k=4),
         loop_attnres=dict(enabled=False), adaptive_loops=dict(enabled=False),

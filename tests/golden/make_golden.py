@@ -303,6 +303,34 @@ def sec_model() -> None:
     save("model", **res)
 
 
+def _prefill_and_decode(cfg, tag: str, steps: int = 4) -> dict:
+    """Prefill logits of the package model and of sample_standalone.py's copy,
+    then greedy decode from the standalone copy (the loop output carried)."""
+    ids = torch.from_numpy(inputs.mini_prompt())
+    pkg = _reference_model(cfg)
+    sa = _reference_model(cfg, standalone=True)
+    res = {}
+    with torch.no_grad():
+        res[f"{tag}_prefill_last"] = pkg(ids, collect_diagnostics=False).logits[:, -1].numpy()
+        out = sa(ids, collect_diagnostics=False)
+        res[f"{tag}_sa_prefill_last"] = out.logits[:, -1].numpy()
+        state, logits = out.state, out.logits[:, -1]
+        toks, step_logits = [], []
+        for _ in range(steps):
+            nxt = logits.argmax(-1, keepdim=True)
+            toks.append(nxt[:, 0].numpy())
+            logits = sa.decode_step(nxt, state=state).logits[:, -1]
+            step_logits.append(logits.numpy())
+    res[f"{tag}_tokens"] = np.stack(toks, 1)
+    res[f"{tag}_step_logits"] = np.stack(step_logits, 1)
+    return res
+
+
+def sec_router_ctx() -> None:
+    """The mini model with the context-aware router (64-wide latents, window 8)."""
+    save("router_ctx", **_prefill_and_decode(inputs.router_ctx_config(), "rc", steps=10))
+
+
 def sec_mhc() -> None:
     """The mini model with four hyper-connection streams: prefill logits of the
     package model, and greedy decode from sample_standalone.py's copy (the
@@ -330,7 +358,7 @@ def sec_mhc() -> None:
     save("mhc", **res)
 
 
-SECTIONS = {"mhc": sec_mhc, "model": sec_model, "sample": sec_sample, "router": sec_router, "moe": sec_moe, "gdn": sec_gdn, "csa": sec_csa, "band": sec_band}
+SECTIONS = {"router_ctx": sec_router_ctx, "mhc": sec_mhc, "model": sec_model, "sample": sec_sample, "router": sec_router, "moe": sec_moe, "gdn": sec_gdn, "csa": sec_csa, "band": sec_band}
 
 
 def main(argv: list[str]) -> None:

@@ -270,3 +270,76 @@ def test_mhc_static_maps_skip_the_projection(cuda):
         b.mhc.static = False
     b_ = LoopedHybridModel(w).forward(ids, last_logits_only=True).logits
     assert torch.equal(a, b_)
+
+
+# Decode steps of the router-context golden compared at the bf16 logit
+# tolerance.  In the reference trajectory the smallest top-k routing margin is
+# 1.2e-2 .. 7.7e-2 of the logit range at steps 0-6 but 2.8e-3 at step 7 (and
+# 3.4e-3 at step 9), below the bf16 model's router-logit noise, where the bf16
+# path may pick the other expert; the routing itself is checked at fp32
+# tolerance over ten decode steps by test_router_context_logits_vs_fp64.
+ROUTER_CTX_STEPS = 7
+
+
+def test_router_context_model_prefill_and_greedy_decode(cuda):
+    g = golden("router_ctx")
+    m = _model(inputs.router_ctx_config())
+    ids = torch.from_numpy(inputs.mini_prompt()).cuda()
+    out = m.forward(ids, last_logits_only=True)
+    lg = out.logits[:, -1].float().cpu().numpy()
+    assert _rel(lg, g["rc_prefill_last"]) < LOGIT_REL, _rel(lg, g["rc_prefill_last"])
+    state = out.state
+    tok = torch.from_numpy(g["rc_tokens"][:, 0]).cuda()
+    for i in range(ROUTER_CTX_STEPS):
+        lg = m.decode_step(tok, state).float().cpu().numpy()
+        assert _rel(lg, g["rc_step_logits"][:, i]) < LOGIT_REL, (i, _rel(lg, g["rc_step_logits"][:, i]))
+        if i + 1 < g["rc_tokens"].shape[1]:
+            _greedy_ok(lg, g["rc_step_logits"][:, i], lg.argmax(-1), g["rc_tokens"][:, i + 1])
+            tok = torch.from_numpy(g["rc_tokens"][:, i + 1]).cuda()
+
+
+def test_router_context_logits_vs_fp64(cuda):
+    """kernels.router_context_logits (latent LayerNorm, causal window mean, ring
+    kept for decode, folded output projections) against an fp64 restatement of
+    context_router.py:59-133 on random router inputs: prefill of 2 x 20 tokens
+    with window 8, then ten decode steps (the last windows hold only latents
+    written by decode steps); fp32 tolerance rtol 1e-4."""
+    from hybrid_llm_b200 import kernels
+    from hybrid_llm_b200.weights import ModelWeights, synthetic_state_dict
+
+    cfg = inputs.router_ctx_config()
+    sd = synthetic_state_dict(cfg, seed=4)
+    blk = ModelWeights.from_state_dict(cfg, sd, "cuda").blocks[1].moe
+    p = {k.rsplit("moe.router.", 1)[1]: sd[k].double().numpy() for k in sd
+         if k.startswith("recurrent_core.1.moe.router.")}
+    b, t, w, d = 2, 20, cfg.router_local_context, cfg.d_model
+    rng = np.random.default_rng(9)
+    r = rng.normal(size=(b, t + 10, d))
+
+    def latent(x):
+        z = x @ p["latent_memory.down.weight"].T
+        mu, var = z.mean(-1, keepdims=True), z.var(-1, keepdims=True)
+        return (z - mu) / np.sqrt(var + 1e-5) * p["latent_memory.norm.weight"] + \
+            p["latent_memory.norm.bias"]
+
+    def logits(x, box):
+        gate = 1 / (1 + np.exp(-p["route_gate"]))
+        ctx = box @ p["local_context_out.weight"].T @ p["context_out.weight"].T
+        return (x + gate * ctx) @ p["logits.weight"].T
+
+    lat = latent(r)
+    ring = torch.zeros(b, w, cfg.router_latent_dim, device="cuda")
+    got = kernels.router_context_logits(
+        torch.from_numpy(r[:, :t].reshape(b * t, d)).float().cuda(), blk, w, batch=b, seq=t,
+        ring=ring).cpu().numpy().reshape(b, t, -1)
+    box = np.stack([lat[:, max(0, i - w + 1):i + 1].mean(1) for i in range(t)], 1)
+    want = logits(r[:, :t], box)
+    assert _rel(got, want) < 1e-4, _rel(got, want)
+    pos = torch.full((b,), t, dtype=torch.int32, device="cuda")
+    for s in range(10):
+        got = kernels.router_context_logits(
+            torch.from_numpy(r[:, t + s]).float().cuda(), blk, w, batch=b, seq=1, ring=ring,
+            positions=pos).cpu().numpy()
+        want = logits(r[:, t + s], lat[:, t + s - w + 1:t + s + 1].mean(1))
+        assert _rel(got, want) < 1e-4, (s, _rel(got, want))
+        pos += 1

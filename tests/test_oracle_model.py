@@ -76,3 +76,31 @@ def test_mhc_config_conversion():
             HybridConfig.from_v6(bad)
     off = dict(base, mhc=dict(enabled=False, streams=1))
     assert HybridConfig.from_v6(off).mhc_streams == 0
+
+
+def test_router_context_model_matches_reference():
+    """The context-aware router's local-context path (context_router.py:59-133):
+    prefill and ten greedy decode steps (the 8-token window wraps)."""
+    g = golden("router_ctx")
+    np.testing.assert_allclose(g["rc_prefill_last"], g["rc_sa_prefill_last"], rtol=1e-5, atol=1e-6)
+    m = _oracle(inputs.router_ctx_config())
+    logits, state = m.forward(inputs.mini_prompt())
+    np.testing.assert_allclose(logits[:, -1], g["rc_prefill_last"], rtol=1e-5, atol=1e-5)
+    last = logits[:, -1]
+    for i in range(g["rc_tokens"].shape[1]):
+        tok = last.argmax(-1)
+        np.testing.assert_array_equal(tok, g["rc_tokens"][:, i])
+        last, state = m.decode_step(tok, state)
+        np.testing.assert_allclose(last, g["rc_step_logits"][:, i], rtol=1e-5, atol=1e-5)
+
+
+def test_router_context_config_conversion():
+    from hybrid_llm_b200.config import HybridConfig
+
+    cfg = inputs.router_ctx_config()
+    assert HybridConfig.from_v6(inputs.v6_mapping(cfg)) == cfg
+    assert (cfg.router_context, cfg.router_latent_dim, cfg.router_local_context) == (True, 64, 8)
+    # the reference's defaults: context on, latent 256, window 128
+    base = inputs.v6_mapping(inputs.mini_config())
+    dflt = HybridConfig.from_v6(dict(base, router={}, mla={}))
+    assert (dflt.router_context, dflt.router_latent_dim, dflt.router_local_context) == (True, 256, 128)
