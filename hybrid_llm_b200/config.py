@@ -18,6 +18,12 @@ from dataclasses import dataclass, field
 from typing import Any
 
 
+# A CSA temporal_compression at least this large (16M tokens; the reference's
+# own "off" setting is 10**9) completes no block in any sequence the engine
+# holds, so its remote branch contributes exactly zero.
+CSA_COMPRESSION_OFF = 1 << 24
+
+
 @dataclass(frozen=True)
 class HybridConfig:
     vocab_size: int
@@ -40,6 +46,10 @@ class HybridConfig:
     router_context: bool = False  # ContextAwareRouter local-context path (context_router.py)
     router_latent_dim: int = 256  # mla.latent_dim
     router_local_context: int = 128  # router.local_context (box-filter window)
+    # CSA remote compressed branch: block ratio (0 = off: temporal_compression
+    # beyond any sequence) and summaries attended per query and head
+    csa_compression: int = 0
+    csa_top_k: int = 32
     name: str = field(default="custom", compare=False)
 
     def __post_init__(self) -> None:
@@ -56,6 +66,8 @@ class HybridConfig:
             raise ValueError("hyper-connections are implemented for 1, 2 or 4 streams")
         if self.mhc_iterations < 0:
             raise ValueError("mhc_iterations must be >= 0")
+        if self.csa_compression < 0 or self.csa_top_k < 1:
+            raise ValueError("csa_compression must be >= 0 and csa_top_k >= 1")
         if self.router_context and (self.router_local_context < 1 or self.router_latent_dim < 1
                                     or self.router_latent_dim > 1024):
             raise ValueError("router context needs local_context >= 1 and 1 <= latent_dim <= 1024")
@@ -105,6 +117,9 @@ class HybridConfig:
         if sget(sub("loop_attnres"), "enabled") or sget(sub("adaptive_loops"), "enabled"):
             raise ValueError("loop memory and adaptive halting are not implemented")
         csa = sub("csa")
+        ratio = int(sget(csa, "temporal_compression"))
+        csa_compression = 0 if ratio >= CSA_COMPRESSION_OFF else ratio
+        csa_top_k = int(sget(csa, "index_top_k")) if csa_compression else 32
         return cls(
             vocab_size=sub("vocab_size"), d_model=sub("d_model"),
             recurrent_layout=tuple(sub("recurrent_layout")), num_loops=sub("num_loops"),
@@ -118,6 +133,7 @@ class HybridConfig:
             mhc_streams=mhc_streams, mhc_iterations=mhc_iters,
             router_context=router_context, router_latent_dim=latent_dim,
             router_local_context=local_context,
+            csa_compression=csa_compression, csa_top_k=csa_top_k,
         )
 
 

@@ -46,6 +46,10 @@ class LoopedHybridModel:
     every rank of the group then runs the same calls on its own sequences."""
 
     def __init__(self, weights: ModelWeights, ep=None):
+        if weights.cfg.csa_compression:
+            raise NotImplementedError(
+                "the CSA remote compressed branch (csa.temporal_compression) has no B200 kernel "
+                "yet; oracle.model.OracleModel restates it")
         self.w = weights
         self.cfg: HybridConfig = weights.cfg
         self.device = weights.embed.device

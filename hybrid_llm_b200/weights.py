@@ -86,6 +86,12 @@ def parameter_shapes(cfg: HybridConfig) -> dict[str, tuple[int, ...]]:
                 p + "mixer.value.weight": (d, d), p + "mixer.local_out.weight": (d, d),
                 p + "mixer.out.weight": (d, d),
             })
+            if cfg.csa_compression:
+                shapes.update({
+                    p + "mixer.remote_out.weight": (d, d),
+                    p + "mixer.compressor.key.weight": (w, d),
+                    p + "mixer.compressor.value.weight": (d, d),
+                })
         shapes[p + "moe.router.norm.weight"] = (d,)
         shapes[p + "moe.router.logits.weight"] = (e, d)
         if cfg.router_context:

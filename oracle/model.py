@@ -47,7 +47,10 @@ class OracleModel:
 
     def _csa_params(self, j):
         p = f"recurrent_core.{j}.mixer."
-        return {n: self.p[p + n + ".weight"] for n in ("query", "key", "value", "local_out", "out")}
+        names = ("query", "key", "value", "local_out", "out")
+        if self.cfg.csa_compression:
+            names += ("remote_out", "compressor.key", "compressor.value")
+        return {n: self.p[p + n + ".weight"] for n in names}
 
     def _router_logits(self, j, m, state, key, step):
         """ContextAwareRouter.forward / forward_step (context_router.py:59-74,
@@ -112,7 +115,8 @@ class OracleModel:
 
     def new_state(self, batch):
         c = self.cfg
-        st = {"gdn": {}, "conv": {}, "hist": {}, "rlat": {}, "pos": np.zeros(batch, dtype=np.int64)}
+        st = {"gdn": {}, "conv": {}, "hist": {}, "rlat": {}, "cmem": {},
+              "pos": np.zeros(batch, dtype=np.int64)}
         for i in range(c.num_loops):
             for j in range(c.n_blocks):
                 if c.block_kind(j) == "gdn":
@@ -133,6 +137,11 @@ class OracleModel:
                     mixed, s = gdn.gdn_layer(normed, self._gdn_params(j), state["gdn"][(i, j)])
                     state["gdn"][(i, j)] = s
                     state["conv"][(i, j)] = normed[:, -(c.conv_kernel - 1):]
+                elif c.csa_compression:
+                    mixed, state["cmem"][(i, j)] = attention.csa_layer_remote(
+                        normed, self._csa_params(j), c.csa_heads, c.csa_window, c.csa_compression,
+                        c.csa_top_k)
+                    state["hist"][(i, j)] = normed[:, -(c.csa_window - 1):]
                 else:
                     mixed = attention.csa_layer(normed, self._csa_params(j), c.csa_heads, c.csa_window)
                     state["hist"][(i, j)] = normed[:, -(c.csa_window - 1):]
@@ -192,7 +201,16 @@ class OracleModel:
                     k = (win @ a["key"].T).reshape(b_, L, c.csa_heads, -1)
                     v = win @ a["value"].T
                     local = attention.csa_local_step(q, k, v)
-                    mixed = ((local @ a["local_out"].T) @ a["out"].T)[:, None, :]
+                    out = local @ a["local_out"].T
+                    if c.csa_compression:
+                        pos = int(state["pos"][0])
+                        mem = attention.compress_step(state["cmem"][(i, j)], normed[:, 0],
+                                                      a["compressor.key"], a["compressor.value"],
+                                                      c.csa_compression, pos)
+                        remote = attention.remote_attention(q[:, None], mem["keys"], mem["values"],
+                                                            mem["pos"], np.array([pos]), c.csa_top_k)
+                        out = out + remote[:, 0] @ a["remote_out"].T
+                    mixed = (out @ a["out"].T)[:, None, :]
                     state["hist"][(i, j)] = win[:, -(c.csa_window - 1):]
                 x = self._write(j, x, mixed, maps)
                 m, maps = self._read(j, x, "ffn_norm")

@@ -143,6 +143,14 @@ def router_ctx_config():
                                router_local_context=8, name="mini-router-ctx")
 
 
+def csa_remote_config():
+    """The mini model with the CSA remote branch on: 4-token block summaries,
+    top-3 per query and head (the 50-token prompt gives 12 summaries)."""
+    import dataclasses
+    return dataclasses.replace(mini_config(), csa_compression=4, csa_top_k=3,
+                               name="mini-csa-remote")
+
+
 def llmy_config():
     """A small looped hybrid model for the .llmy format fixture."""
     from hybrid_llm_b200.config import HybridConfig
@@ -163,9 +171,9 @@ def block_hidden():
 
 
 def v6_mapping(cfg) -> dict:
-    """Reference V6Config fields for a HybridConfig (mHC and the router's local
-    context path as configured; shared experts, loop memory, halting and the
-    CSA remote branch switched off)."""
+    """Reference V6Config fields for a HybridConfig (mHC, the router's local
+    context path and the CSA remote branch as configured; shared experts, loop
+    memory and halting switched off)."""
     return dict(
         vocab_size=cfg.vocab_size, d_model=cfg.d_model, physical_blocks=cfg.n_blocks,
         stem_blocks=0, recurrent_blocks=cfg.n_blocks, tail_blocks=0, num_loops=cfg.num_loops,
@@ -179,7 +187,8 @@ def v6_mapping(cfg) -> dict:
                  expert_hidden=cfg.moe_hidden),
         router=dict(context_aware=cfg.router_context, local_context=cfg.router_local_context),
         mla=dict(latent_dim=cfg.router_latent_dim),
-        csa=dict(temporal_compression=10 ** 9, local_window=cfg.csa_window,
-                 index_heads=cfg.csa_heads, index_head_dim=cfg.csa_head_dim, index_top_k=4),
+        csa=dict(temporal_compression=cfg.csa_compression or 10 ** 9, local_window=cfg.csa_window,
+                 index_heads=cfg.csa_heads, index_head_dim=cfg.csa_head_dim,
+                 index_top_k=cfg.csa_top_k if cfg.csa_compression else 4),
         loop_attnres=dict(enabled=False), adaptive_loops=dict(enabled=False),
     )

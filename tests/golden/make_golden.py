@@ -326,6 +326,12 @@ def _prefill_and_decode(cfg, tag: str, steps: int = 4) -> dict:
     return res
 
 
+def sec_csa_remote() -> None:
+    """The mini model with the CSA remote compressed branch (4-token summaries,
+    top-3); eight decode steps complete two more summaries."""
+    save("csa_remote", **_prefill_and_decode(inputs.csa_remote_config(), "cr", steps=8))
+
+
 def sec_router_ctx() -> None:
     """The mini model with the context-aware router (64-wide latents, window 8)."""
     save("router_ctx", **_prefill_and_decode(inputs.router_ctx_config(), "rc", steps=10))
@@ -358,7 +364,7 @@ def sec_mhc() -> None:
     save("mhc", **res)
 
 
-SECTIONS = {"router_ctx": sec_router_ctx, "mhc": sec_mhc, "model": sec_model, "sample": sec_sample, "router": sec_router, "moe": sec_moe, "gdn": sec_gdn, "csa": sec_csa, "band": sec_band}
+SECTIONS = {"csa_remote": sec_csa_remote, "router_ctx": sec_router_ctx, "mhc": sec_mhc, "model": sec_model, "sample": sec_sample, "router": sec_router, "moe": sec_moe, "gdn": sec_gdn, "csa": sec_csa, "band": sec_band}
 
 
 def main(argv: list[str]) -> None:

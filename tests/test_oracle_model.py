@@ -104,3 +104,37 @@ def test_router_context_config_conversion():
     base = inputs.v6_mapping(inputs.mini_config())
     dflt = HybridConfig.from_v6(dict(base, router={}, mla={}))
     assert (dflt.router_context, dflt.router_latent_dim, dflt.router_local_context) == (True, 256, 128)
+
+
+def test_csa_remote_branch_matches_reference():
+    """CSA's remote compressed branch (csa.py:77-131, :208-256;
+    compressed_attention.py:85-206): 4-token summaries, top-3 per query and
+    head, prefill and eight decode steps (two more summaries complete)."""
+    g = golden("csa_remote")
+    np.testing.assert_allclose(g["cr_prefill_last"], g["cr_sa_prefill_last"], rtol=1e-5, atol=1e-6)
+    m = _oracle(inputs.csa_remote_config())
+    logits, state = m.forward(inputs.mini_prompt())
+    np.testing.assert_allclose(logits[:, -1], g["cr_prefill_last"], rtol=1e-5, atol=1e-5)
+    last = logits[:, -1]
+    for i in range(g["cr_tokens"].shape[1]):
+        tok = last.argmax(-1)
+        np.testing.assert_array_equal(tok, g["cr_tokens"][:, i])
+        last, state = m.decode_step(tok, state)
+        np.testing.assert_allclose(last, g["cr_step_logits"][:, i], rtol=1e-5, atol=1e-5)
+
+
+def test_csa_remote_config_and_model_guard():
+    import types
+
+    import pytest
+    from hybrid_llm_b200.config import HybridConfig
+    from hybrid_llm_b200.model import LoopedHybridModel
+
+    cfg = inputs.csa_remote_config()
+    assert HybridConfig.from_v6(inputs.v6_mapping(cfg)) == cfg
+    off = inputs.v6_mapping(inputs.mini_config())
+    assert off["csa"]["temporal_compression"] == 10 ** 9
+    assert HybridConfig.from_v6(off).csa_compression == 0
+    # the B200 path refuses the branch instead of silently dropping it
+    with pytest.raises(NotImplementedError):
+        LoopedHybridModel(types.SimpleNamespace(cfg=cfg))
