@@ -244,3 +244,77 @@ def write_llmy(path: str | Path, config: Mapping[str, Any] | str,
         f.seek(index_start)
         for e in entries:
             f.write(e)
+
+
+# ------------------------------------------------------------------- converter
+def convert_checkpoint(src: str | Path, dst: str | Path, *, keep_fp32: bool = False,
+                       strict: bool = False) -> int:
+    """The converter tool (llmy_cuda/tools/convert_checkpoint.py:122-222): a
+    training checkpoint ``{"model": state_dict, "config": mapping}`` (or a bare
+    state dict with a "config" entry) to ``.llmy``.  Non-tensor entries are
+    skipped; keep_fp32 stores every tensor as float32; strict fails on any
+    tensor that is not float32.  Returns the process exit status (0, or 1 with a
+    message on stderr), as the tool does."""
+    import sys
+    src, dst = Path(src), Path(dst)
+    if not src.is_file():
+        print(f"error: {src} is not a file", file=sys.stderr)
+        return 1
+    ckpt = torch.load(src, map_location="cpu", weights_only=False)
+    if not isinstance(ckpt, dict):
+        print("error: checkpoint is not a dict", file=sys.stderr)
+        return 1
+    cfg = ckpt.get("config")
+    if cfg is None:
+        print("error: checkpoint has no embedded config", file=sys.stderr)
+        return 1
+    if not isinstance(cfg, dict):
+        print(f"error: config is {type(cfg).__name__}, expected dict", file=sys.stderr)
+        return 1
+    state = ckpt.get("model", ckpt)
+    if not isinstance(state, dict):
+        print("error: state dict is not a dict", file=sys.stderr)
+        return 1
+    tensors: dict[str, torch.Tensor] = {}
+    for name, t in state.items():
+        if not isinstance(t, torch.Tensor):
+            continue
+        t = t.float() if keep_fp32 else t
+        if strict and t.dtype != torch.float32:
+            print(f"error: tensor {name.replace('_orig_mod.', '')} is {t.dtype}", file=sys.stderr)
+            return 1
+        tensors[name] = t
+    write_llmy(dst, cfg, tensors)
+    return 0
+
+
+def _main(argv: list[str] | None = None) -> int:
+    import argparse
+    ap = argparse.ArgumentParser(prog="python -m hybrid_llm_b200.llmy_format",
+                                 description="Convert a training checkpoint to .llmy, or list one.")
+    sub = ap.add_subparsers(dest="cmd", required=True)
+    cv = sub.add_parser("convert", help="training checkpoint (.pt) -> .llmy")
+    cv.add_argument("input", type=Path)
+    cv.add_argument("output", type=Path)
+    cv.add_argument("--keep-fp32", action="store_true",
+                    help="store all tensors as float32 (default: keep input dtype)")
+    cv.add_argument("--strict", action="store_true",
+                    help="fail if any tensor is not float32 after conversion")
+    ls = sub.add_parser("info", help="print the configuration and tensor index of a .llmy file")
+    ls.add_argument("file", type=Path)
+    args = ap.parse_args(argv)
+    if args.cmd == "convert":
+        return convert_checkpoint(args.input, args.output, keep_fp32=args.keep_fp32,
+                                  strict=args.strict)
+    f = read_llmy(args.file)
+    try:
+        print(f.config_text, end="")
+        for name, t in f.tensors.items():
+            print(f"{name}\t{str(t.dtype).replace('torch.', '')}\t{list(t.shape)}")
+    finally:
+        f.close()
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(_main())

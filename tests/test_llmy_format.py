@@ -116,3 +116,32 @@ def test_model_from_llmy_equals_model_from_state_dict(cuda):
         lb = b.decode_step(nxt[:, None], ob.state)
         assert torch.equal(la, lb)
         nxt = la.float().argmax(-1)
+
+
+def test_converter_tool_reproduces_the_fixture(tmp_path, capsys):
+    """convert_checkpoint on the checkpoint the fixture came from writes the
+    reference converter's bytes; its error exits match the tool's."""
+    f = llmy_format.read_llmy(FIXTURE)
+    try:
+        sd = {k: v.clone() for k, v in f.tensors.items()}  # the full state, experts stacked
+    finally:
+        f.close()
+    ckpt = tmp_path / "tiny.pt"
+    torch.save({"format_version": 1, "model": sd, "config": _mapping()}, ckpt)
+    out = tmp_path / "tiny.llmy"
+    assert llmy_format._main(["convert", str(ckpt), str(out)]) == 0
+    assert out.read_bytes() == FIXTURE.read_bytes()
+    # --keep-fp32 stores float32 copies, --strict rejects the bf16 ones
+    out32 = tmp_path / "tiny32.llmy"
+    assert llmy_format.convert_checkpoint(ckpt, out32, keep_fp32=True) == 0
+    f = llmy_format.read_llmy(out32)
+    try:
+        assert all(t.dtype == torch.float32 for t in f.tensors.values())
+    finally:
+        f.close()
+    assert llmy_format.convert_checkpoint(ckpt, tmp_path / "x.llmy", strict=True) == 1
+    torch.save({"model": dict(sd)}, tmp_path / "nocfg.pt")
+    assert llmy_format.convert_checkpoint(tmp_path / "nocfg.pt", tmp_path / "y.llmy") == 1
+    assert llmy_format.convert_checkpoint(tmp_path / "missing.pt", tmp_path / "z.llmy") == 1
+    err = capsys.readouterr().err
+    assert "no embedded config" in err and "is not a file" in err and "is torch.bfloat16" in err
