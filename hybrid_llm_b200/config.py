@@ -110,6 +110,15 @@ class HybridConfig:
         mla = sub("mla") if (isinstance(cfg, dict) and "mla" in cfg) or hasattr(cfg, "mla") else {}
         latent_dim = int(mla.get("latent_dim", 256) if isinstance(mla, dict)
                          else getattr(mla, "latent_dim", 256))
+        gdn = sub("gdn")
+        gget = lambda k, default: (gdn.get(k, default) if isinstance(gdn, dict)
+                                   else getattr(gdn, k, default))
+        if str(gget("sensitive_state_dtype", "float32")).lower() not in ("float32", "fp32"):
+            # model/model.py:93 keeps the delta-rule state in fp16 then; this
+            # build keeps it in fp32 only
+            raise ValueError("the GDN state is kept in float32 only (gdn.sensitive_state_dtype)")
+        if int(gget("value_heads", gget("qk_heads", 0))) != int(gget("qk_heads", 0)):
+            raise ValueError("GDN needs equal q/k and value head counts (gated_deltanet.py:93)")
         if sget(sub("moe"), "shared_experts") != 0:
             raise ValueError("shared experts are not implemented")
         if sub("stem_blocks") or sub("tail_blocks"):

@@ -138,3 +138,13 @@ def test_csa_remote_config_and_model_guard():
     # the B200 path refuses the branch instead of silently dropping it
     with pytest.raises(NotImplementedError):
         LoopedHybridModel(types.SimpleNamespace(cfg=cfg))
+
+
+def test_from_v6_rejects_a_half_precision_gdn_state():
+    import pytest
+    from hybrid_llm_b200.config import HybridConfig
+
+    base = inputs.v6_mapping(inputs.mini_config())
+    HybridConfig.from_v6(dict(base, gdn=dict(base["gdn"], sensitive_state_dtype="fp32")))
+    with pytest.raises(ValueError):
+        HybridConfig.from_v6(dict(base, gdn=dict(base["gdn"], sensitive_state_dtype="float16")))
