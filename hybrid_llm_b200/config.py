@@ -50,6 +50,7 @@ class HybridConfig:
     # beyond any sequence) and summaries attended per query and head
     csa_compression: int = 0
     csa_top_k: int = 32
+    moe_shared: int = 0  # shared experts (moe.py:185-198): sum of their SwiGLU / sqrt(n)
     name: str = field(default="custom", compare=False)
 
     def __post_init__(self) -> None:
@@ -66,6 +67,8 @@ class HybridConfig:
             raise ValueError("hyper-connections are implemented for 1, 2 or 4 streams")
         if self.mhc_iterations < 0:
             raise ValueError("mhc_iterations must be >= 0")
+        if self.moe_shared < 0:
+            raise ValueError("moe_shared must be >= 0")
         if self.csa_compression < 0 or self.csa_top_k < 1:
             raise ValueError("csa_compression must be >= 0 and csa_top_k >= 1")
         if self.router_context and (self.router_local_context < 1 or self.router_latent_dim < 1
@@ -119,8 +122,6 @@ class HybridConfig:
             raise ValueError("the GDN state is kept in float32 only (gdn.sensitive_state_dtype)")
         if int(gget("value_heads", gget("qk_heads", 0))) != int(gget("qk_heads", 0)):
             raise ValueError("GDN needs equal q/k and value head counts (gated_deltanet.py:93)")
-        if sget(sub("moe"), "shared_experts") != 0:
-            raise ValueError("shared experts are not implemented")
         if sub("stem_blocks") or sub("tail_blocks"):
             raise ValueError("stem/tail dense blocks are not implemented")
         if sget(sub("loop_attnres"), "enabled") or sget(sub("adaptive_loops"), "enabled"):
@@ -143,6 +144,7 @@ class HybridConfig:
             router_context=router_context, router_latent_dim=latent_dim,
             router_local_context=local_context,
             csa_compression=csa_compression, csa_top_k=csa_top_k,
+            moe_shared=int(sget(sub("moe"), "shared_experts")),
         )
 
 

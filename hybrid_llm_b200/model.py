@@ -50,6 +50,10 @@ class LoopedHybridModel:
             raise NotImplementedError(
                 "the CSA remote compressed branch (csa.temporal_compression) has no B200 kernel "
                 "yet; oracle.model.OracleModel restates it")
+        if weights.cfg.moe_shared:
+            raise NotImplementedError(
+                "shared experts (moe.shared_experts) have no B200 path yet; "
+                "oracle.model.OracleModel restates them")
         self.w = weights
         self.cfg: HybridConfig = weights.cfg
         self.device = weights.embed.device

@@ -106,6 +106,11 @@ def parameter_shapes(cfg: HybridConfig) -> dict[str, tuple[int, ...]]:
             shapes[q + "gate_proj.weight"] = (f, d)
             shapes[q + "up_proj.weight"] = (f, d)
             shapes[q + "down_proj.weight"] = (d, f)
+        for x in range(cfg.moe_shared):
+            q = f"{p}moe.shared.{x}."
+            shapes[q + "gate_proj.weight"] = (f, d)
+            shapes[q + "up_proj.weight"] = (f, d)
+            shapes[q + "down_proj.weight"] = (d, f)
     return shapes
 
 

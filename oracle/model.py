@@ -95,6 +95,15 @@ class OracleModel:
                 for n in ("gate", "up", "down"))
         wg, wu, wd = self._experts[j]
         out = routing.moe_forward(flat, idx, prob, wg, wu, wd, dtype=self.dtype)
+        if c.moe_shared:
+            # shared experts (moe.py:185-198): every token, sum / sqrt(n_shared)
+            x = np.asarray(flat, dtype=out.dtype)
+            for s in range(c.moe_shared):
+                q = f"{p}shared.{s}."
+                g_ = x @ self.p[q + "gate_proj.weight"].T
+                u_ = x @ self.p[q + "up_proj.weight"].T
+                out = out + ((routing.silu(g_) * u_) @ self.p[q + "down_proj.weight"].T
+                             ) / np.sqrt(c.moe_shared)
         return out.reshape(*lead, -1), logits
 
     def _read(self, j, x, norm):

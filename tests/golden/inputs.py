@@ -151,6 +151,12 @@ def csa_remote_config():
                                name="mini-csa-remote")
 
 
+def shared_experts_config():
+    """The mini model with two shared experts next to the routed ones."""
+    import dataclasses
+    return dataclasses.replace(mini_config(), moe_shared=2, name="mini-shared")
+
+
 def llmy_config():
     """A small looped hybrid model for the .llmy format fixture."""
     from hybrid_llm_b200.config import HybridConfig
@@ -172,7 +178,7 @@ def block_hidden():
 
 def v6_mapping(cfg) -> dict:
     """Reference V6Config fields for a HybridConfig (mHC, the router's local
-    context path and the CSA remote branch as configured; shared experts, loop
+    context path, the CSA remote branch and shared experts as configured; loop
     memory and halting switched off)."""
     return dict(
         vocab_size=cfg.vocab_size, d_model=cfg.d_model, physical_blocks=cfg.n_blocks,
@@ -183,8 +189,8 @@ def v6_mapping(cfg) -> dict:
              if cfg.mhc_streams else dict(enabled=False, streams=1)),
         gdn=dict(qk_heads=cfg.gdn_heads, value_heads=cfg.gdn_heads, qk_head_dim=cfg.gdn_key_dim,
                  value_head_dim=cfg.gdn_value_dim, conv_kernel=cfg.conv_kernel),
-        moe=dict(routed_experts=cfg.moe_experts, shared_experts=0, routed_top_k=cfg.moe_top_k,
-                 expert_hidden=cfg.moe_hidden),
+        moe=dict(routed_experts=cfg.moe_experts, shared_experts=cfg.moe_shared,
+                 routed_top_k=cfg.moe_top_k, expert_hidden=cfg.moe_hidden),
         router=dict(context_aware=cfg.router_context, local_context=cfg.router_local_context),
         mla=dict(latent_dim=cfg.router_latent_dim),
         csa=dict(temporal_compression=cfg.csa_compression or 10 ** 9, local_window=cfg.csa_window,

@@ -326,6 +326,11 @@ def _prefill_and_decode(cfg, tag: str, steps: int = 4) -> dict:
     return res
 
 
+def sec_shared() -> None:
+    """The mini model with two shared experts next to the routed ones."""
+    save("shared", **_prefill_and_decode(inputs.shared_experts_config(), "sh", steps=4))
+
+
 def sec_csa_remote() -> None:
     """The mini model with the CSA remote compressed branch (4-token summaries,
     top-3); eight decode steps complete two more summaries."""
@@ -364,7 +369,7 @@ def sec_mhc() -> None:
     save("mhc", **res)
 
 
-SECTIONS = {"csa_remote": sec_csa_remote, "router_ctx": sec_router_ctx, "mhc": sec_mhc, "model": sec_model, "sample": sec_sample, "router": sec_router, "moe": sec_moe, "gdn": sec_gdn, "csa": sec_csa, "band": sec_band}
+SECTIONS = {"shared": sec_shared, "csa_remote": sec_csa_remote, "router_ctx": sec_router_ctx, "mhc": sec_mhc, "model": sec_model, "sample": sec_sample, "router": sec_router, "moe": sec_moe, "gdn": sec_gdn, "csa": sec_csa, "band": sec_band}
 
 
 def main(argv: list[str]) -> None:

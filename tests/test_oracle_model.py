@@ -148,3 +148,32 @@ def test_from_v6_rejects_a_half_precision_gdn_state():
     HybridConfig.from_v6(dict(base, gdn=dict(base["gdn"], sensitive_state_dtype="fp32")))
     with pytest.raises(ValueError):
         HybridConfig.from_v6(dict(base, gdn=dict(base["gdn"], sensitive_state_dtype="float16")))
+
+
+def test_shared_experts_match_reference():
+    """Shared experts (moe.py:185-198, decode :221-234): every token through
+    each, sum / sqrt(n), added to the routed output; prefill and decode."""
+    g = golden("shared")
+    np.testing.assert_allclose(g["sh_prefill_last"], g["sh_sa_prefill_last"], rtol=1e-5, atol=1e-6)
+    m = _oracle(inputs.shared_experts_config())
+    logits, state = m.forward(inputs.mini_prompt())
+    np.testing.assert_allclose(logits[:, -1], g["sh_prefill_last"], rtol=1e-5, atol=1e-5)
+    last = logits[:, -1]
+    for i in range(g["sh_tokens"].shape[1]):
+        tok = last.argmax(-1)
+        np.testing.assert_array_equal(tok, g["sh_tokens"][:, i])
+        last, state = m.decode_step(tok, state)
+        np.testing.assert_allclose(last, g["sh_step_logits"][:, i], rtol=1e-5, atol=1e-5)
+
+
+def test_shared_experts_config_and_model_guard():
+    import types
+
+    import pytest
+    from hybrid_llm_b200.config import HybridConfig
+    from hybrid_llm_b200.model import LoopedHybridModel
+
+    cfg = inputs.shared_experts_config()
+    assert HybridConfig.from_v6(inputs.v6_mapping(cfg)) == cfg and cfg.moe_shared == 2
+    with pytest.raises(NotImplementedError):
+        LoopedHybridModel(types.SimpleNamespace(cfg=cfg))
