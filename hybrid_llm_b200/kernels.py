@@ -7,6 +7,7 @@ CPU path: tensors must live on a CUDA device.
 """
 from __future__ import annotations
 
+import math
 from dataclasses import dataclass
 
 import torch
@@ -912,3 +913,37 @@ def router_context_logits(r_in: torch.Tensor, moe, window: int, *, batch: int, s
                      _ptr(box), _stream())
     logits = torch.mm(r_in, moe.router.t())
     return logits.addmm_(box, moe.ctx_logits.t(), alpha=moe.ctx_gate)
+
+
+# ------------------------------------------------------------- shared experts
+def with_shared_experts(plan: RoutePlan, n_shared: int) -> RoutePlan:
+    """The plan extended by n_shared shared experts (moe.py:185-198) as
+    experts E..E+n-1 that every token is routed to with probability
+    1/sqrt(n): their rows follow the routed ones (expert E+i holds tokens
+    0..N-1 at rows N*k + i*N + t), so the grouped GEMMs scale each by the
+    probability in their down-projection epilogue and the combine over the
+    k + n rows of a token gives routed + sum_s SwiGLU_s(x) / sqrt(n).  Expert
+    weights must be stacked routed first, then shared.  Device-side tensor
+    ops only (no synchronisation)."""
+    n = int(n_shared)
+    if n <= 0:
+        return plan
+    tokens, k = plan.topk_idx.shape
+    e = plan.n_experts
+    dev = plan.offsets.device
+    i32 = dict(dtype=torch.int32, device=dev)
+    step = torch.arange(1, n + 1, **i32)
+    p = 1.0 / math.sqrt(n)
+    shared_pos = (tokens * k + torch.arange(n, **i32)[None, :] * tokens
+                  + torch.arange(tokens, **i32)[:, None])
+    tiles = -(-tokens // plan.tile_m)
+    return RoutePlan(
+        topk_idx=torch.cat([plan.topk_idx, (e + torch.arange(n, device=dev)).expand(tokens, n)], 1),
+        topk_prob=torch.cat([plan.topk_prob, torch.full((tokens, n), p, device=dev)], 1),
+        counts=torch.cat([plan.counts, torch.full((n,), tokens, **i32)]),
+        offsets=torch.cat([plan.offsets, plan.offsets[-1:] + tokens * step]),
+        tile_offsets=torch.cat([plan.tile_offsets, plan.tile_offsets[-1:] + tiles * step]),
+        perm_token=torch.cat([plan.perm_token, torch.arange(tokens, **i32).repeat(n)]),
+        perm_prob=torch.cat([plan.perm_prob, torch.full((tokens * n,), p, device=dev)]),
+        route_pos=torch.cat([plan.route_pos.view(tokens, k), shared_pos], 1).reshape(-1).contiguous(),
+        sort_order=None, tile_m=plan.tile_m)
