@@ -595,6 +595,7 @@ def secondary_ep_decode(p: dict, steps: int = 10, warmup: int = 3, global_batch:
                 "peer-memory stores over NVLink (CUDA IPC), flags" if exchange == "p2p"
                 else "NCCL all_to_all_single"),
             "graph": use_graph, "tok_s": global_batch / step_s, "ms_per_step": step_s * 1e3,
+            "scaling": "strong (global batch 64 split over the ranks)",
             "llmyb_launches_per_step": launches,
             "hbm_bytes_per_step_per_rank": touched, "achieved_gbs_per_rank": achieved,
             "frac_of_hbm": achieved / p["hbm_gbs"]}
