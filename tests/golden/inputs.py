@@ -157,6 +157,15 @@ def shared_experts_config():
     return dataclasses.replace(mini_config(), moe_shared=2, name="mini-shared")
 
 
+def combined_config():
+    """mHC (4 streams), the router's local context, the CSA remote branch and
+    shared experts together on the mini model (their interaction)."""
+    import dataclasses
+    return dataclasses.replace(mini_config(), mhc_streams=4, mhc_iterations=10,
+                               router_context=True, router_latent_dim=64, router_local_context=8,
+                               csa_compression=4, csa_top_k=3, moe_shared=2, name="mini-combined")
+
+
 def llmy_config():
     """A small looped hybrid model for the .llmy format fixture."""
     from hybrid_llm_b200.config import HybridConfig

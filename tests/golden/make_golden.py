@@ -326,6 +326,11 @@ def _prefill_and_decode(cfg, tag: str, steps: int = 4) -> dict:
     return res
 
 
+def sec_combined() -> None:
+    """mHC, router context, CSA remote branch and shared experts together."""
+    save("combined", **_prefill_and_decode(inputs.combined_config(), "cb", steps=6))
+
+
 def sec_shared() -> None:
     """The mini model with two shared experts next to the routed ones."""
     save("shared", **_prefill_and_decode(inputs.shared_experts_config(), "sh", steps=4))
@@ -369,7 +374,7 @@ def sec_mhc() -> None:
     save("mhc", **res)
 
 
-SECTIONS = {"shared": sec_shared, "csa_remote": sec_csa_remote, "router_ctx": sec_router_ctx, "mhc": sec_mhc, "model": sec_model, "sample": sec_sample, "router": sec_router, "moe": sec_moe, "gdn": sec_gdn, "csa": sec_csa, "band": sec_band}
+SECTIONS = {"combined": sec_combined, "shared": sec_shared, "csa_remote": sec_csa_remote, "router_ctx": sec_router_ctx, "mhc": sec_mhc, "model": sec_model, "sample": sec_sample, "router": sec_router, "moe": sec_moe, "gdn": sec_gdn, "csa": sec_csa, "band": sec_band}
 
 
 def main(argv: list[str]) -> None:

@@ -177,3 +177,19 @@ def test_shared_experts_config_and_model_guard():
     assert HybridConfig.from_v6(inputs.v6_mapping(cfg)) == cfg and cfg.moe_shared == 2
     with pytest.raises(NotImplementedError):
         LoopedHybridModel(types.SimpleNamespace(cfg=cfg))
+
+
+def test_combined_features_match_reference():
+    """mHC (4 streams) + the router's local context + the CSA remote branch +
+    shared experts on one model: prefill and six decode steps."""
+    g = golden("combined")
+    np.testing.assert_allclose(g["cb_prefill_last"], g["cb_sa_prefill_last"], rtol=1e-5, atol=1e-6)
+    m = _oracle(inputs.combined_config())
+    logits, state = m.forward(inputs.mini_prompt())
+    np.testing.assert_allclose(logits[:, -1], g["cb_prefill_last"], rtol=1e-5, atol=1e-5)
+    last = logits[:, -1]
+    for i in range(g["cb_tokens"].shape[1]):
+        tok = last.argmax(-1)
+        np.testing.assert_array_equal(tok, g["cb_tokens"][:, i])
+        last, state = m.decode_step(tok, state)
+        np.testing.assert_allclose(last, g["cb_step_logits"][:, i], rtol=1e-5, atol=1e-5)
