@@ -42,6 +42,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
                                 P, P]),
     "llmyb_route_decode": (I32, [P, P, I32, I32, P, P, P, F32, I32, I32, I32, P, P, P, P, P, P, P,
                                  P, P, P, P]),
+    "llmyb_plan_append_shared": (I32, [I32, I32, I32, I32, I32, P, P, P, P, P, P, P, P, P, P, P, P,
+                                       P, P, P, P, P]),
     # MoE expert FFN
     "llmyb_moe_pack_w13": (I32, [P, P, I32, I32, I32, P, P]),
     "llmyb_moe_grouped_scratch_bytes": (I64, [I32, I32, I32, I32]),
@@ -63,7 +65,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "llmyb_ep_shared_free": (I32, [P]),
     "llmyb_ep_dispatch_p2p": (I32, [P, I32, P, P, P, P, I32, I32, I32, I32, P, P, P, P, P]),
     "llmyb_ep_return_p2p": (I32, [P, P, I32, I32, I32, I32, P, P, P, P]),
-    "llmyb_ep_wait": (I32, [P, I32, P, P, P]),
+    "llmyb_ep_wait": (I32, [P, I32, P, P, I64, P]),
     # gated delta rule
     "llmyb_gdn_activate": (I32, [P, I64, I32, I32, I32, I32, P, P]),
     "llmyb_gdn_step": (I32, [P, I64, P, I64, P, I64, P, I64, P, I64, P, P, P, I32, I32, I32, I32,
@@ -100,6 +102,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     # hyper-connections
     "llmyb_mhc_read": (I32, [P, I32, I32, I32, P, I64, I64, P, P, P, P, P, F32, I32, P, P, P, P]),
     "llmyb_mhc_write": (I32, [P, I32, I32, I32, P, P, I32, P, P, P, P]),
+    # loop memory
+    "llmyb_loop_mem_norm": (I32, [P, I64, I32, I32, I32, P, P, F32, P, I64, P]),
+    "llmyb_loop_mem_attend": (I32, [P, P, I32, I32, I32, I32, P, P]),
+    "llmyb_loop_mem_add": (I32, [P, I32, I32, I32, P, F32, P]),
     # router local context
     "llmyb_router_ctx_prefill": (I32, [P, I32, I32, I32, I32, P, P, P, P, P]),
     "llmyb_router_ctx_step": (I32, [P, I32, I32, I32, P, P, P, P, P, P]),

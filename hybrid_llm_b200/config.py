@@ -7,10 +7,12 @@ B200 path implements: a recurrent core of ``gdn_moe`` / ``csa_moe`` blocks run
 or 4 live streams, input-dependent maps, shared across loops, streams carried
 across loop boundaries), a top-k softmax router with or without its local
 context path (``router_context``: the causal box-filtered MLA latents of the
-last ``router_local_context`` tokens; no HCA global latents), no shared
-experts, CSA with its remote compressed branch disabled
-(temporal_compression beyond any sequence), no stem/tail blocks.  ``from_v6`` converts a reference config (dataclass or mapping) and
-rejects anything outside that subset instead of silently changing the model.
+last ``router_local_context`` tokens; no HCA global latents), routed and
+shared experts (``moe_shared``), CSA with or without its remote compressed
+branch (``csa_compression``), the loop memory between loops (``loop_memory``),
+no stem/tail blocks and no adaptive halting.  ``from_v6`` converts a
+reference config (dataclass or mapping) and rejects anything outside that
+subset instead of silently changing the model.
 """
 from __future__ import annotations
 
@@ -51,6 +53,13 @@ class HybridConfig:
     csa_compression: int = 0
     csa_top_k: int = 32
     moe_shared: int = 0  # shared experts (moe.py:185-198): sum of their SwiGLU / sqrt(n)
+    # loop memory (loop_memory.py LoopMemoryHook, config loop_attnres): before
+    # every loop after the first, each token attends over LayerNorm'd latent
+    # summaries of its own streams at the end of the earlier loops
+    loop_memory: bool = False
+    loop_memory_latent: int = 128
+    loop_memory_heads: int = 4
+    loop_memory_head_dim: int = 32
     name: str = field(default="custom", compare=False)
 
     def __post_init__(self) -> None:
@@ -74,6 +83,9 @@ class HybridConfig:
         if self.router_context and (self.router_local_context < 1 or self.router_latent_dim < 1
                                     or self.router_latent_dim > 1024):
             raise ValueError("router context needs local_context >= 1 and 1 <= latent_dim <= 1024")
+        if self.loop_memory and (self.loop_memory_latent < 1 or self.loop_memory_heads < 1
+                                 or self.loop_memory_head_dim < 1 or self.num_loops > 16):
+            raise ValueError("loop memory needs positive latent / head sizes and at most 16 loops")
 
     @property
     def streams(self) -> int:
@@ -124,8 +136,11 @@ class HybridConfig:
             raise ValueError("GDN needs equal q/k and value head counts (gated_deltanet.py:93)")
         if sub("stem_blocks") or sub("tail_blocks"):
             raise ValueError("stem/tail dense blocks are not implemented")
-        if sget(sub("loop_attnres"), "enabled") or sget(sub("adaptive_loops"), "enabled"):
-            raise ValueError("loop memory and adaptive halting are not implemented")
+        if sget(sub("adaptive_loops"), "enabled"):
+            raise ValueError("adaptive halting is not implemented")
+        lm = sub("loop_attnres")
+        lmget = lambda k, default: (lm.get(k, default) if isinstance(lm, dict)
+                                    else getattr(lm, k, default))
         csa = sub("csa")
         ratio = int(sget(csa, "temporal_compression"))
         csa_compression = 0 if ratio >= CSA_COMPRESSION_OFF else ratio
@@ -145,6 +160,10 @@ class HybridConfig:
             router_local_context=local_context,
             csa_compression=csa_compression, csa_top_k=csa_top_k,
             moe_shared=int(sget(sub("moe"), "shared_experts")),
+            loop_memory=bool(lmget("enabled", False)),
+            loop_memory_latent=int(lmget("latent_dim", 128)),
+            loop_memory_heads=int(lmget("heads", 4)),
+            loop_memory_head_dim=int(lmget("head_dim", 32)),
         )
 
 

@@ -684,23 +684,15 @@ __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(NT, STAGE
   cluster.sync();  // keep shared memory alive until every peer finished reading
 }
 
-template <typename K>
-int32_t set_smem(K kernel, int bytes) {
-  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-  return e == cudaSuccess ? LLMYB_OK : static_cast<int32_t>(e);
-}
-
 template <int D, bool STATS>
 int32_t launch_band(const __nv_bfloat16* q, int64_t sq, const __nv_bfloat16* k, int64_t sk,
                     const __nv_bfloat16* v, int64_t sv, int v_heads, int B, int T, int H, int W,
                     float scale, __nv_bfloat16* out, int64_t so, float* m_out, float* l_out,
                     cudaStream_t s) {
   constexpr int bytes = sizeof(BandSmem<D, STATS>);
-  static bool attr = false;
-  if (!attr) {
-    int32_t st = set_smem(banded_attn_kernel<D, STATS>, bytes);
+  {
+    int32_t st = ensure_smem(banded_attn_kernel<D, STATS>, bytes);
     if (st) return st;
-    attr = true;
   }
   const int grid = B * H * static_cast<int>(ceil_div(T, BMQ));
   banded_attn_kernel<D, STATS><<<grid, 128, bytes, s>>>(q, sq, k, sk, v, sv, v_heads, B, T, H, W,
@@ -763,7 +755,7 @@ LLMYB_API int32_t llmyb_csa_local_prefill(const void* q, int64_t q_stride, const
   auto run = [&](auto kern, int BM, int base_bytes, int dh) -> int32_t {
     const int bytes = base_bytes + BM * (hd + 8) * 2 + BM * heads * 2 * 4;
     if (bytes > 227 * 1024) return LLMYB_EUNSUPPORTED;
-    int32_t e = set_smem(kern, bytes);
+    int32_t e = ensure_smem(kern, bytes);
     if (e) return e;
     const int grid = batch * static_cast<int>(ceil_div(seq, BM)) * (d_model / DC);
     kern<<<grid, BM * 2, bytes, s>>>(Q, q_stride, K, k_stride, V, v_stride, batch, seq, heads,
@@ -818,11 +810,10 @@ LLMYB_API int32_t llmyb_csa_local_decode(const void* q, int64_t q_stride, const 
   const int kch = hd <= 768 ? 3 : (hd <= 1024 ? 4 : 8);
   const bool seg16 = head_dim == 128;
   if (bytes > 227 * 1024) return LLMYB_EUNSUPPORTED;
-  auto launch = [&](auto kernel, int nt, int& attr_bytes) -> int32_t {
-    if (bytes > attr_bytes) {
-      int32_t st = set_smem(kernel, bytes);
+  auto launch = [&](auto kernel, int nt) -> int32_t {
+    {
+      int32_t st = ensure_smem(kernel, bytes);
       if (st) return st;
-      attr_bytes = bytes;
     }
     return static_cast<int32_t>(launch_pdl(
         kernel, dim3(batch * kClusterCtas), dim3(nt), bytes, static_cast<cudaStream_t>(stream),
@@ -832,16 +823,11 @@ LLMYB_API int32_t llmyb_csa_local_decode(const void* q, int64_t q_stride, const 
         heads, head_dim, d_model, window, kLog2e / sqrtf(static_cast<float>(head_dim)),
         static_cast<__nv_bfloat16*>(out), out_stride, dev_status));
   };
-  static int attr[2][3][2] = {};
-  const int ki = kch == 3 ? 0 : (kch == 4 ? 1 : 2);
   int32_t st;
 #define LLMYB_CSA(ST, NTV, SEGV)                                                         \
-  (kch == 3 ? launch(csa_decode_kernel<ST, NTV, 3, SEGV>, NTV,                          \
-                     attr[ST ? 0 : 1][ki][SEGV == 16])                                   \
-   : kch == 4 ? launch(csa_decode_kernel<ST, NTV, 4, SEGV>, NTV,                        \
-                       attr[ST ? 0 : 1][ki][SEGV == 16])                                 \
-              : launch(csa_decode_kernel<ST, NTV, 8, SEGV>, NTV,                        \
-                       attr[ST ? 0 : 1][ki][SEGV == 16]))
+  (kch == 3 ? launch(csa_decode_kernel<ST, NTV, 3, SEGV>, NTV)                          \
+   : kch == 4 ? launch(csa_decode_kernel<ST, NTV, 4, SEGV>, NTV)                        \
+              : launch(csa_decode_kernel<ST, NTV, 8, SEGV>, NTV))
   if (staged)
     st = seg16 ? LLMYB_CSA(true, 512, 16) : LLMYB_CSA(true, 512, 8);
   else

@@ -410,12 +410,9 @@ int32_t launch_band_tc(const void* q, int64_t sq, const void* k, int64_t sk, con
                        int64_t sv, int v_heads, int B, int T, int H, int W, float scale,
                        void* out, int64_t so, int32_t* dev_status, cudaStream_t stream) {
   using L = BandTcLayout<D>;
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(band_tc_kernel<D>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, L::kSmem);
-    if (e != cudaSuccess) return static_cast<int32_t>(e);
-    attr = true;
+  {
+    int32_t st = ensure_smem(band_tc_kernel<D>, L::kSmem);
+    if (st) return st;
   }
   CUtensorMap mq, mk, mv;
   if (!make_bf16_3d_map(&mq, q, B, T, static_cast<uint64_t>(H) * D, sq, kRows) ||

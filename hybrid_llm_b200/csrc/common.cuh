@@ -29,6 +29,16 @@ __host__ __device__ inline int64_t ceil_div(int64_t a, int64_t b) { return (a + 
 int64_t& launch_counter();
 inline void count_launch(int n = 1) { launch_counter() += n; }
 
+// Raise a kernel's dynamic shared-memory limit to at least `bytes` on the
+// current device.  The attribute belongs to the (device, kernel) pair, so the
+// largest value set is remembered per pair, under a lock: a process that
+// drives several GPUs sets it on each, and concurrent host threads agree.
+int32_t smem_limit_at_least(const void* kernel, int bytes);
+template <typename K>
+inline int32_t ensure_smem(K* kernel, int bytes) {
+  return smem_limit_at_least(reinterpret_cast<const void*>(kernel), bytes);
+}
+
 inline int32_t launch_status() {
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? LLMYB_OK : static_cast<int32_t>(e);

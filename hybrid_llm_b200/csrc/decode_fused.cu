@@ -513,14 +513,6 @@ int bm_for(int B) { return B <= 1 ? 1 : (B <= 4 ? 4 : 8); }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-template <typename Kern>
-int32_t ensure_smem(Kern kernel, int bytes, int& attr) {
-  if (bytes <= attr) return LLMYB_OK;
-  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-  if (e != cudaSuccess) return e;
-  attr = bytes;
-  return LLMYB_OK;
-}
 
 }  // namespace
 }  // namespace llmyb
@@ -549,13 +541,11 @@ LLMYB_API int32_t llmyb_decode_norm_gemv(const float* streams_in, const void* de
   const auto* wb = static_cast<const __nv_bfloat16*>(w);
   auto* ob = static_cast<__nv_bfloat16*>(out);
   auto* nb = static_cast<__nv_bfloat16*>(normed_out);
-  static int attr[3][3] = {};
   const int bm = bm_for(n_tokens);
-  const int bi = bm == 1 ? 0 : (bm == 4 ? 1 : 2), ki = kch == 3 ? 0 : (kch == 4 ? 1 : 2);
   int32_t st = LLMYB_OK;
 #define LLMYB_NG(BMV, KCHV)                                                                     \
   do {                                                                                          \
-    st = ensure_smem(decode_norm_gemv_kernel<BMV, KCHV>, bytes, attr[bi][ki]);                  \
+    st = ensure_smem(decode_norm_gemv_kernel<BMV, KCHV>, bytes);                                \
     if (st) return st;                                                                          \
     st = launch_pdl(decode_norm_gemv_kernel<BMV, KCHV>, dim3(grid), dim3(256), bytes, s,         \
                     streams_in, dl, route_pos, top_k, n_tokens, d_model, norm_w, eps, wb, n_out, \
@@ -603,13 +593,10 @@ LLMYB_API int32_t llmyb_decode_out_router(
       n_tokens * n_experts <= 64) {
     const int rpw = d_model / (kOrCtas * kOrWarps);
     const int cbytes = ((n_tokens * k_in * 2 + 15) & ~15) + n_experts * (kOrWarps * rpw) * 4;
-    static int cattr[3][2][2] = {};
-    const int bi = bm == 1 ? 0 : (bm == 4 ? 1 : 2), ki = kch == 3 ? 0 : 1, ri = rpw == 6 ? 0 : 1;
     int32_t st = LLMYB_OK;
 #define LLMYB_ORC(BMV, KCHV, RPWV)                                                              \
   do {                                                                                          \
-    st = ensure_smem(decode_out_router_cluster_kernel<BMV, KCHV, RPWV>, cbytes,                 \
-                     cattr[bi][ki][ri]);                                                        \
+    st = ensure_smem(decode_out_router_cluster_kernel<BMV, KCHV, RPWV>, cbytes);                \
     if (st) return st;                                                                          \
     st = launch_pdl(decode_out_router_cluster_kernel<BMV, KCHV, RPWV>, dim3(kOrCtas),            \
         dim3(kOrWarps * 32), cbytes, s, static_cast<const __nv_bfloat16*>(in), in_ld, k_in,     \
@@ -635,12 +622,10 @@ LLMYB_API int32_t llmyb_decode_out_router(
   const int bytes =
       std::max(n_tokens * k_in * 2, (n_tokens * nv + n_tokens * n_experts) * 4);
   const int grid = static_cast<int>(ceil_div(d_model, 8));
-  static int attr[3][3] = {};
-  const int bi = bm == 1 ? 0 : (bm == 4 ? 1 : 2), ki = kch == 3 ? 0 : (kch == 4 ? 1 : 2);
   int32_t st = LLMYB_OK;
 #define LLMYB_OR(BMV, KCHV)                                                                     \
   do {                                                                                          \
-    st = ensure_smem(decode_out_router_kernel<BMV, KCHV>, bytes, attr[bi][ki]);                 \
+    st = ensure_smem(decode_out_router_kernel<BMV, KCHV>, bytes);                               \
     if (st) return st;                                                                          \
     st = launch_pdl(decode_out_router_kernel<BMV, KCHV>, dim3(grid), dim3(256), bytes, s,        \
         static_cast<const __nv_bfloat16*>(in), in_ld, k_in,                                     \

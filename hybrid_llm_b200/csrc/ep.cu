@@ -81,10 +81,11 @@ __device__ __forceinline__ void publish_send(const PeerTable& peers, int W, int*
 }
 
 // Wait until flags[0..W) all hold the current epoch (sync[0]), by thread 0;
-// gives up after kWaitLimitNs and records LLMYB_ETIMEOUT.  Returns to all
+// gives up after limit_ns and records LLMYB_ETIMEOUT.  Returns to all
 // threads of the CTA.
 __device__ __forceinline__ bool wait_flags(const int* flags, int W, const int* sync,
-                                           int32_t* dev_status) {
+                                           int32_t* dev_status,
+                                           uint64_t limit_ns = kWaitLimitNs) {
   __shared__ int s_ok;
   if (threadIdx.x == 0) {
     const int e = *reinterpret_cast<const volatile int*>(sync);
@@ -93,7 +94,7 @@ __device__ __forceinline__ bool wait_flags(const int* flags, int W, const int* s
     for (int src = 0; src < W && ok; ++src) {
       uint32_t spins = 0;
       while (ld_acquire_sys(flags + src) != e) {
-        if (((++spins) & 63u) == 0u && globaltimer_ns() - t0 > kWaitLimitNs) {
+        if (((++spins) & 63u) == 0u && globaltimer_ns() - t0 > limit_ns) {
           report_status(dev_status, LLMYB_ETIMEOUT);
           ok = 0;
           break;
@@ -286,8 +287,9 @@ __global__ void ep_return_kernel(const __nv_bfloat16* __restrict__ ret_send,
 }
 
 // Wait for the W return flags of the current exchange round (one CTA).
-__global__ void ep_wait_kernel(const int* flags, int W, const int* sync, int32_t* dev_status) {
-  wait_flags(flags, W, sync, dev_status);
+__global__ void ep_wait_kernel(const int* flags, int W, const int* sync, int32_t* dev_status,
+                               uint64_t limit_ns) {
+  wait_flags(flags, W, sync, dev_status, limit_ns);
 }
 
 }  // namespace
@@ -469,11 +471,16 @@ LLMYB_API int32_t llmyb_ep_return_p2p(const void* ret_send, const void* recv, in
 }
 
 // Wait (bounded, one CTA) until flags[0..W) hold the current round sync[0];
-// dev_status gets LLMYB_ETIMEOUT after one second.
+// dev_status gets LLMYB_ETIMEOUT once limit_ns have passed (0: one second;
+// at most one second).
 LLMYB_API int32_t llmyb_ep_wait(const int32_t* flags, int32_t world, const int32_t* sync,
-                                int32_t* dev_status, void* stream) {
-  if (!flags || !sync || !dev_status || world <= 0 || world > 64) return LLMYB_EINVAL;
-  ep_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(flags, world, sync, dev_status);
+                                int32_t* dev_status, int64_t limit_ns, void* stream) {
+  if (!flags || !sync || !dev_status || world <= 0 || world > 64 || limit_ns < 0)
+    return LLMYB_EINVAL;
+  const uint64_t limit = (limit_ns == 0 || static_cast<uint64_t>(limit_ns) > kWaitLimitNs)
+                             ? kWaitLimitNs : static_cast<uint64_t>(limit_ns);
+  ep_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(flags, world, sync, dev_status,
+                                                                   limit);
   count_launch();
   return launch_status();
 }

@@ -1236,12 +1236,6 @@ __global__ void __launch_bounds__(320, 1) gdn_scan_tc_kernel(
   }
 }
 
-template <typename K>
-int32_t set_smem(K kernel, int bytes) {
-  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-  return e == cudaSuccess ? LLMYB_OK : static_cast<int32_t>(e);
-}
-
 int32_t check_io(const GdnIO& io, int KD, int VD) {
   if (!io.q || !io.k || !io.v || !io.gate || !io.beta) return LLMYB_EINVAL;
   if (!io.decay_logit && !io.log_alpha) return LLMYB_EINVAL;
@@ -1314,22 +1308,18 @@ int32_t launch_prefill(const GdnIO& io, int B, int T, int H, void* scratch, floa
   constexpr int kPrepSmem = sizeof(PrepSmem<KD, VD>);
   constexpr int VC = 32, NG = 2;  // two 32-column groups per CTA
   constexpr int kScanSmem = sizeof(ScanSmem<KD, VC * NG>);
-  static bool attrs = false;
-  if (!attrs) {
-    int32_t st = set_smem(gdn_chunk_prep_kernel<KD, VD>, kPrepSmem);
+  {
+    int32_t st = ensure_smem(gdn_chunk_prep_kernel<KD, VD>, kPrepSmem);
     if (st) return st;
-    st = set_smem(gdn_chunk_scan_kernel<KD, VD, VC, NG>, kScanSmem);
+    st = ensure_smem(gdn_chunk_scan_kernel<KD, VD, VC, NG>, kScanSmem);
     if (st) return st;
-    attrs = true;
   }
   gdn_chunk_prep_kernel<KD, VD><<<B * H * nC, 128, kPrepSmem, s>>>(io, B, T, H, po);
   count_launch();
   if (tc) {
-    static bool tc_attr = false;
-    if (!tc_attr) {
-      int32_t st = set_smem(gdn_scan_tc_kernel, scan_tc::kSmem);
+    {
+      int32_t st = ensure_smem(gdn_scan_tc_kernel, scan_tc::kSmem);
       if (st) return st;
-      tc_attr = true;
     }
     CUtensorMap mkw, mqs, mk, maqk, mu;
     if (!make_bf16_4d_map(&mkw, po.Kw, B, T, H, KD, kC) ||

@@ -236,18 +236,13 @@ int32_t launch_experts(const void* x, int32_t n_tokens, int32_t d_model, int32_t
                        const void* w2, int32_t ffn, __nv_bfloat16* h, __nv_bfloat16* y,
                        const int32_t* out_row, cudaStream_t s) {
   const int up_smem = kTok * d_model * 2, down_smem = kTok * ffn * 2;
-  static int up_attr = 0, down_attr = 0;
-  if (up_smem > 48 * 1024 && up_smem > up_attr) {
-    cudaError_t e = cudaFuncSetAttribute(moe_decode_up_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, up_smem);
-    if (e != cudaSuccess) return e;
-    up_attr = up_smem;
+  if (up_smem > 48 * 1024) {
+    int32_t st = ensure_smem(moe_decode_up_kernel, up_smem);
+    if (st) return st;
   }
-  if (down_smem > 48 * 1024 && down_smem > down_attr) {
-    cudaError_t e = cudaFuncSetAttribute(moe_decode_down_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, down_smem);
-    if (e != cudaSuccess) return e;
-    down_attr = down_smem;
+  if (down_smem > 48 * 1024) {
+    int32_t st = ensure_smem(moe_decode_down_kernel, down_smem);
+    if (st) return st;
   }
   // at most n_rows experts have rows: a grid over those slots only, each
   // finding its expert on the device, when that is smaller than all E

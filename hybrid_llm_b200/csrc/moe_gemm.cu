@@ -583,24 +583,12 @@ int grid_for(int64_t work, int threads) {
   return static_cast<int>(blocks < 8 * 148 ? (blocks > 0 ? blocks : 1) : 8 * 148);
 }
 
-bool gemm_attr_set = false;
-
 int32_t ensure_gemm_attrs() {
-  if (gemm_attr_set) return LLMYB_OK;
-  cudaError_t e1 = cudaFuncSetAttribute(moe_gemm_kernel<kSwiGLU>,
-                                        cudaFuncAttributeMaxDynamicSharedMemorySize, GEMM_SMEM);
-  cudaError_t e2 = cudaFuncSetAttribute(moe_gemm_kernel<kScale>,
-                                        cudaFuncAttributeMaxDynamicSharedMemorySize, GEMM_SMEM);
-  if (e1 != cudaSuccess) return e1;
-  if (e2 != cudaSuccess) return e2;
-  cudaError_t e3 = cudaFuncSetAttribute(moe_gemm_pair_kernel<kSwiGLU>,
-                                        cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM);
-  cudaError_t e4 = cudaFuncSetAttribute(moe_gemm_pair_kernel<kScale>,
-                                        cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM);
-  if (e3 != cudaSuccess) return e3;
-  if (e4 != cudaSuccess) return e4;
-  gemm_attr_set = true;
-  return LLMYB_OK;
+  int32_t st = ensure_smem(moe_gemm_kernel<kSwiGLU>, GEMM_SMEM);
+  if (!st) st = ensure_smem(moe_gemm_kernel<kScale>, GEMM_SMEM);
+  if (!st) st = ensure_smem(moe_gemm_pair_kernel<kSwiGLU>, P_SMEM);
+  if (!st) st = ensure_smem(moe_gemm_pair_kernel<kScale>, P_SMEM);
+  return st;
 }
 
 // gather -> GEMM1 (SwiGLU) -> GEMM2 (probability scale) for a plan of `rows`

@@ -8,6 +8,10 @@
 // :442-444 (embedding + stream_seed).  Under bf16 autocast the residual
 // stream stays fp32 while sub-layer outputs are bf16; the same split is
 // used here: streams fp32, normalised activations bf16 (fp32 on request).
+#include <map>
+#include <mutex>
+#include <utility>
+
 #include "common.cuh"
 
 namespace llmyb {
@@ -220,6 +224,21 @@ namespace llmyb {
 int64_t& launch_counter() {
   static int64_t n = 0;
   return n;
+}
+
+int32_t smem_limit_at_least(const void* kernel, int bytes) {
+  static std::mutex mu;
+  static std::map<std::pair<int, const void*>, int> set;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return static_cast<int32_t>(e);
+  std::lock_guard<std::mutex> lock(mu);
+  int& have = set[{dev, kernel}];
+  if (bytes <= have) return LLMYB_OK;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) return static_cast<int32_t>(e);
+  have = bytes;
+  return LLMYB_OK;
 }
 }  // namespace llmyb
 

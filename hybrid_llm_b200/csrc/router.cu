@@ -21,6 +21,9 @@
 #include "common.cuh"
 #include "router_device.cuh"
 
+#include <algorithm>
+#include <climits>
+#include <cmath>
 #include <mutex>
 
 namespace llmyb {
@@ -488,13 +491,10 @@ LLMYB_API int32_t llmyb_route_fused(float* streams, const void* delta, int32_t n
   const int bytes = (n_tokens * d_model + n_tokens * n_experts) * static_cast<int>(sizeof(float));
   if (bytes > 190 * 1024) return LLMYB_EUNSUPPORTED;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  auto launch = [&](auto kernel, int slot) -> int32_t {
-    static int attr[4] = {0, 0, 0, 0};
-    if (bytes > attr[slot]) {  // static + dynamic shared memory may pass 48 KB
-      cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           bytes);
-      if (e != cudaSuccess) return e;
-      attr[slot] = bytes;
+  auto launch = [&](auto kernel, int) -> int32_t {
+    {  // static + dynamic shared memory may pass 48 KB
+      int32_t st = ensure_smem(kernel, bytes);
+      if (st) return st;
     }
     kernel<<<1, 256, bytes, s>>>(streams, static_cast<const __nv_bfloat16*>(delta), n_tokens,
                                  d_model, ffn_norm, router_norm, w_router, eps, n_experts, top_k,
@@ -510,6 +510,95 @@ LLMYB_API int32_t llmyb_route_fused(float* streams, const void* delta, int32_t n
     default: st = launch(router_fused_kernel<8>, 3); break;
   }
   if (st) return st;
+  count_launch();
+  return launch_status();
+}
+
+// ----------------------------------------------------------------------------
+// Shared experts (model/layers/moe.py:185-198 prefill, :221-234 decode step):
+// every token goes through each of the S shared experts and their sum, scaled
+// by 1/sqrt(S), is added to the routed output.  They become plan experts
+// E..E+S-1 that every token is routed to with probability 1/sqrt(S), placed
+// after the routed rows in plan order (expert E+s holds tokens 0..N-1 at rows
+// N*k + s*N + t).  The expert kernels then run routed and shared experts in
+// one call (weights stacked routed first, then shared), scaling each row by
+// its probability, and the combine over a token's k + S rows gives
+// routed + sum_s SwiGLU_s(x) / sqrt(S).
+namespace llmyb {
+namespace {
+__global__ void plan_append_shared_kernel(
+    int N, int E, int k, int S, int tile_m, float p, const int64_t* __restrict__ idx,
+    const float* __restrict__ prob, const int* __restrict__ counts,
+    const int* __restrict__ offsets, const int* __restrict__ tiles,
+    const int* __restrict__ perm_token, const float* __restrict__ perm_prob,
+    const int* __restrict__ route_pos, int64_t* __restrict__ idx2, float* __restrict__ prob2,
+    int* __restrict__ counts2, int* __restrict__ offsets2, int* __restrict__ tiles2,
+    int* __restrict__ perm_token2, float* __restrict__ perm_prob2,
+    int* __restrict__ route_pos2) {
+  const int64_t n_routes = static_cast<int64_t>(N) * k;
+  const int64_t total = static_cast<int64_t>(N) * (k + S);
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += stride) {
+    // plan rows: the routed rows unchanged, then S groups of N token rows
+    if (i < n_routes) {
+      perm_token2[i] = perm_token[i];
+      perm_prob2[i] = perm_prob[i];
+    } else {
+      perm_token2[i] = static_cast<int>((i - n_routes) % N);
+      perm_prob2[i] = p;
+    }
+    // per-token slots: [t, 0..k) routed, [t, k..k+S) shared
+    const int64_t t = i / (k + S);
+    const int s = static_cast<int>(i - t * (k + S));
+    if (s < k) {
+      idx2[i] = idx[t * k + s];
+      prob2[i] = prob[t * k + s];
+      route_pos2[i] = route_pos[t * k + s];
+    } else {
+      idx2[i] = E + (s - k);
+      prob2[i] = p;
+      route_pos2[i] = static_cast<int>(n_routes + static_cast<int64_t>(s - k) * N + t);
+    }
+  }
+  if (blockIdx.x == 0) {
+    const int tiles_per = (N + tile_m - 1) / tile_m;
+    for (int e = threadIdx.x; e <= E + S; e += blockDim.x) {
+      if (e < E + S) counts2[e] = e < E ? counts[e] : N;
+      offsets2[e] = e <= E ? offsets[e] : static_cast<int>(n_routes + static_cast<int64_t>(e - E) * N);
+      tiles2[e] = e <= E ? tiles[e] : tiles[E] + (e - E) * tiles_per;
+    }
+  }
+}
+}  // namespace
+}  // namespace llmyb
+
+LLMYB_API int32_t llmyb_plan_append_shared(
+    int32_t n_tokens, int32_t n_experts, int32_t top_k, int32_t n_shared, int32_t tile_m,
+    const int64_t* topk_idx, const float* topk_prob, const int32_t* expert_counts,
+    const int32_t* expert_offsets, const int32_t* tile_offsets, const int32_t* perm_token,
+    const float* perm_prob, const int32_t* route_pos, int64_t* out_topk_idx,
+    float* out_topk_prob, int32_t* out_counts, int32_t* out_offsets, int32_t* out_tile_offsets,
+    int32_t* out_perm_token, float* out_perm_prob, int32_t* out_route_pos, void* stream) {
+  if (n_tokens < 0 || n_experts <= 0 || top_k <= 0 || n_shared <= 0 || tile_m <= 0)
+    return LLMYB_EINVAL;
+  if (static_cast<int64_t>(n_tokens) * (top_k + n_shared) > INT32_MAX) return LLMYB_EUNSUPPORTED;
+  if (!expert_counts || !expert_offsets || !tile_offsets || !out_counts || !out_offsets ||
+      !out_tile_offsets)
+    return LLMYB_EINVAL;
+  if (n_tokens > 0 && (!topk_idx || !topk_prob || !perm_token || !perm_prob || !route_pos ||
+                       !out_topk_idx || !out_topk_prob || !out_perm_token || !out_perm_prob ||
+                       !out_route_pos))
+    return LLMYB_EINVAL;
+  const int64_t total = static_cast<int64_t>(n_tokens) * (top_k + n_shared);
+  const int grid = static_cast<int>(std::min<int64_t>(std::max<int64_t>(ceil_div(total, 256), 1),
+                                                      4 * 148));
+  plan_append_shared_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      n_tokens, n_experts, top_k, n_shared, tile_m,
+      static_cast<float>(1.0 / std::sqrt(static_cast<double>(n_shared))),
+      topk_idx, topk_prob, expert_counts, expert_offsets, tile_offsets, perm_token, perm_prob,
+      route_pos, out_topk_idx, out_topk_prob, out_counts, out_offsets, out_tile_offsets,
+      out_perm_token, out_perm_prob, out_route_pos);
   count_launch();
   return launch_status();
 }

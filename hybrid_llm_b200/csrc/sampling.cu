@@ -387,9 +387,8 @@ LLMYB_API int32_t llmyb_sample(const float* logits, int64_t ld, int32_t batch, i
   a.status = dev_status;
   const int dyn = n_blocked > 0 ? ((vocab + 31) / 32) * 4 : 0;
   if (dyn > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         dyn);
-    if (e != cudaSuccess) return e;
+    int32_t st = ensure_smem(sample_kernel, dyn);
+    if (st) return st;
   }
   sample_kernel<<<batch, kThreads, dyn, static_cast<cudaStream_t>(stream)>>>(a);
   count_launch();

@@ -267,6 +267,15 @@ class ExpertParallel:
             self.ops.return_push(self)
         return EpResult(self.ret_recv, rp)
 
+    def check(self) -> None:
+        """Raise if a device step of the exchange recorded an error in the device
+        status word: a flag wait that ran out (a peer that never published,
+        LLMYB_ETIMEOUT) or a malformed segment header (LLMYB_EINVAL).  Waits
+        for the device.  LoopedHybridModel calls it after every eager forward
+        and decode step; a caller replaying a captured step calls it at its
+        own synchronisation points."""
+        kernels.check_device_status(self.device)
+
     def close(self) -> None:
         """Unmap the peers' buffers and free this rank's (peer-memory exchange)."""
         if self.peers is not None:

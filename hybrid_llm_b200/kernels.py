@@ -321,11 +321,12 @@ def ep_return_p2p(ret_send: torch.Tensor, recv: torch.Tensor, world: int, capaci
                  int(capacity), int(experts_per_rank), peer_segs, peer_flags, _ptr(sync), _stream())
 
 
-def ep_wait(flags: torch.Tensor, world: int, sync: torch.Tensor) -> None:
-    """Bounded device-side wait for the current exchange round's flags."""
+def ep_wait(flags: torch.Tensor, world: int, sync: torch.Tensor, limit_ns: int = 0) -> None:
+    """Bounded device-side wait for the current exchange round's flags; after
+    limit_ns (0: one second) the device status word gets LLMYB_ETIMEOUT."""
     _require_cuda(flags, sync)
     _native.call("llmyb_ep_wait", _ptr(flags), int(world), _ptr(sync),
-                 _ptr(device_status(flags.device)), _stream())
+                 _ptr(device_status(flags.device)), int(limit_ns), _stream())
 
 
 def grouped_scratch_bytes(n_rows: int, d_model: int, ffn: int) -> int:
@@ -916,34 +917,78 @@ def router_context_logits(r_in: torch.Tensor, moe, window: int, *, batch: int, s
 
 
 # ------------------------------------------------------------- shared experts
-def with_shared_experts(plan: RoutePlan, n_shared: int) -> RoutePlan:
-    """The plan extended by n_shared shared experts (moe.py:185-198) as
-    experts E..E+n-1 that every token is routed to with probability
-    1/sqrt(n): their rows follow the routed ones (expert E+i holds tokens
-    0..N-1 at rows N*k + i*N + t), so the grouped GEMMs scale each by the
-    probability in their down-projection epilogue and the combine over the
-    k + n rows of a token gives routed + sum_s SwiGLU_s(x) / sqrt(n).  Expert
-    weights must be stacked routed first, then shared.  Device-side tensor
-    ops only (no synchronisation)."""
+def plan_append_shared(plan: RoutePlan, n_shared: int) -> RoutePlan:
+    """The plan extended by n_shared shared experts (moe.py:185-198, :221-234)
+    as plan experts E..E+n-1 that every token is routed to with probability
+    1/sqrt(n), their rows after the routed ones (expert E+s holds tokens
+    0..N-1 at rows N*k + s*N + t): the expert kernels scale each row by that
+    probability and the combine over a token's k + n rows gives routed +
+    sum_s SwiGLU_s(x) / sqrt(n).  Expert weights must be stacked routed first,
+    then shared.  One kernel launch, no synchronisation."""
     n = int(n_shared)
     if n <= 0:
         return plan
+    _require_cuda(plan.offsets)
     tokens, k = plan.topk_idx.shape
     e = plan.n_experts
+    out = _plan_buffers(tokens, e + n, 1, plan.offsets.device, False)
+    rows = tokens * (k + n)
     dev = plan.offsets.device
     i32 = dict(dtype=torch.int32, device=dev)
-    step = torch.arange(1, n + 1, **i32)
-    p = 1.0 / math.sqrt(n)
-    shared_pos = (tokens * k + torch.arange(n, **i32)[None, :] * tokens
-                  + torch.arange(tokens, **i32)[:, None])
-    tiles = -(-tokens // plan.tile_m)
-    return RoutePlan(
-        topk_idx=torch.cat([plan.topk_idx, (e + torch.arange(n, device=dev)).expand(tokens, n)], 1),
-        topk_prob=torch.cat([plan.topk_prob, torch.full((tokens, n), p, device=dev)], 1),
-        counts=torch.cat([plan.counts, torch.full((n,), tokens, **i32)]),
-        offsets=torch.cat([plan.offsets, plan.offsets[-1:] + tokens * step]),
-        tile_offsets=torch.cat([plan.tile_offsets, plan.tile_offsets[-1:] + tiles * step]),
-        perm_token=torch.cat([plan.perm_token, torch.arange(tokens, **i32).repeat(n)]),
-        perm_prob=torch.cat([plan.perm_prob, torch.full((tokens * n,), p, device=dev)]),
-        route_pos=torch.cat([plan.route_pos.view(tokens, k), shared_pos], 1).reshape(-1).contiguous(),
-        sort_order=None, tile_m=plan.tile_m)
+    out.update(perm_token=torch.empty(rows, **i32), route_pos=torch.empty(rows, **i32),
+               perm_prob=torch.empty(rows, dtype=torch.float32, device=dev))
+    idx = torch.empty(tokens, k + n, dtype=torch.int64, device=dev)
+    prob = torch.empty(tokens, k + n, dtype=torch.float32, device=dev)
+    _native.call("llmyb_plan_append_shared", tokens, e, k, n, plan.tile_m, _ptr(plan.topk_idx),
+                 _ptr(plan.topk_prob), _ptr(plan.counts), _ptr(plan.offsets),
+                 _ptr(plan.tile_offsets), _ptr(plan.perm_token), _ptr(plan.perm_prob),
+                 _ptr(plan.route_pos), _ptr(idx), _ptr(prob), _ptr(out["counts"]),
+                 _ptr(out["offsets"]), _ptr(out["tile_offsets"]), _ptr(out["perm_token"]),
+                 _ptr(out["perm_prob"]), _ptr(out["route_pos"]), _stream())
+    return RoutePlan(topk_idx=idx, topk_prob=prob, counts=out["counts"], offsets=out["offsets"],
+                     tile_offsets=out["tile_offsets"], perm_token=out["perm_token"],
+                     perm_prob=out["perm_prob"], route_pos=out["route_pos"], sort_order=None,
+                     tile_m=plan.tile_m)
+
+
+# ------------------------------------------------------------- loop memory
+def loop_mem_norm(x: torch.Tensor, n_streams: int, width: int, ln_w: torch.Tensor | None = None,
+                  ln_b: torch.Tensor | None = None, eps: float = 1e-5,
+                  out: torch.Tensor | None = None) -> torch.Tensor:
+    """Per token: the mean of the n_streams width-wide fp32 streams of x
+    [N, n_streams*width], then LayerNorm(ln_w, ln_b, eps) if ln_w is given."""
+    _require_cuda(x, ln_w, ln_b, out)
+    if x.dtype != torch.float32 or x.dim() != 2 or x.shape[1] < n_streams * width:
+        raise ValueError("loop_mem_norm expects fp32 rows of n_streams * width values")
+    _rows(x, "x")
+    n = x.shape[0]
+    if out is None:
+        out = torch.empty(n, width, dtype=torch.float32, device=x.device)
+    _rows(out, "out")
+    _native.call("llmyb_loop_mem_norm", _ptr(x), x.stride(0), n, int(n_streams), int(width),
+                 _ptr(ln_w), _ptr(ln_b), float(eps), _ptr(out), out.stride(0), _stream())
+    return out
+
+
+def loop_mem_attend(q: torch.Tensor, kv: torch.Tensor, n_mem: int, heads: int, head_dim: int,
+                    out: torch.Tensor | None = None) -> torch.Tensor:
+    """Per (token, head) softmax over the n_mem endpoints of q.k/sqrt(hd), times
+    v: q [N, H*hd], kv [>= n_mem, N, 2*H*hd] fp32 -> [N, H*hd] fp32."""
+    _require_cuda(q, kv, out)
+    q, kv = q.contiguous(), kv.contiguous()
+    n = q.shape[0]
+    if out is None:
+        out = torch.empty(n, heads * head_dim, dtype=torch.float32, device=q.device)
+    _native.call("llmyb_loop_mem_attend", _ptr(q), _ptr(kv), n, int(n_mem), int(heads),
+                 int(head_dim), _ptr(_inplace(out, "out")), _stream())
+    return out
+
+
+def loop_mem_add(streams: torch.Tensor, n_streams: int, delta: torch.Tensor, gate: float) -> None:
+    """streams [N, S*D] += gate * delta [N, D] on every stream (fp32, in place)."""
+    _require_cuda(streams, delta)
+    _inplace(streams, "streams")
+    delta = delta.contiguous()
+    n, d = delta.shape
+    _native.call("llmyb_loop_mem_add", _ptr(streams), n, int(n_streams), d, _ptr(delta),
+                 float(gate), _stream())

@@ -50,10 +50,10 @@ class LoopedHybridModel:
             raise NotImplementedError(
                 "the CSA remote compressed branch (csa.temporal_compression) has no B200 kernel "
                 "yet; oracle.model.OracleModel restates it")
-        if weights.cfg.moe_shared:
+        if weights.cfg.moe_shared and ep is not None:
             raise NotImplementedError(
-                "shared experts (moe.shared_experts) have no B200 path yet; "
-                "oracle.model.OracleModel restates them")
+                "shared experts (moe.shared_experts) are served on one device only, not under "
+                "expert parallelism")
         self.w = weights
         self.cfg: HybridConfig = weights.cfg
         self.device = weights.embed.device
@@ -66,6 +66,10 @@ class LoopedHybridModel:
         # decode_out_router) when the shapes allow; False forces the unfused path
         self.decode_fused = True
         self._counter = torch.zeros(1, dtype=torch.int32, device=self.device)
+        # diagnostics: when a list, every MoE call appends its routed top-k
+        # indices [N, k] (device tensors, in call order; inside a CUDA graph
+        # capture these are the graph's own buffers, rewritten by each replay)
+        self.route_log: list | None = None
         shard = weights.blocks[0].moe.w13.shape[0] if weights.blocks else None
         if ep is not None and shard != ep.experts_per_rank:
             raise ValueError("expert-parallel model needs the weights of this rank's experts only")
@@ -99,9 +103,9 @@ class LoopedHybridModel:
 
     def _moe(self, blk: Block, m_bf: torch.Tensor, m_f32: torch.Tensor, state: RecurrentState,
              key: str, bsz: int, t: int):
-        """SparseMoE.forward without shared experts (moe.py:172-204): the routed
-        expert rows and the plan whose per-token sum is the combine (added to
-        the residual stream by the next add_rmsnorm_routed)."""
+        """SparseMoE.forward (moe.py:172-204): the expert rows and the plan whose
+        per-token sum is the combine (added to the residual stream by the next
+        add_rmsnorm_routed)."""
         logits = self._router_logits(blk, m_f32, state, key, bsz, t, step=False)
         plan = kernels.route(logits, self.cfg.moe_top_k)
         return self._experts(blk, m_bf, plan)
@@ -114,6 +118,35 @@ class LoopedHybridModel:
                                        **out)
         else:
             kernels.add_rmsnorm(streams, pending, weight, self.cfg.rms_eps, **out)
+
+    # --------------------------------------------------------- loop memory
+    def _lm_buffer(self, n: int, loops: int) -> torch.Tensor | None:
+        """k|v projections of the loop endpoints [loops-1, N, 2*H*hd] fp32."""
+        c = self.cfg
+        if not c.loop_memory or loops < 2:
+            return None
+        w = 2 * c.loop_memory_heads * c.loop_memory_head_dim
+        return torch.empty(loops - 1, n, w, dtype=torch.float32, device=self.device)
+
+    def _lm_record(self, streams: torch.Tensor, kv: torch.Tensor, i: int) -> None:
+        """LoopMemoryHook.record / encode (loop_memory.py:36-38, :54-66) after
+        loop i: endpoint = LayerNorm(down(mean over streams)), kept as its k|v
+        projections for the later loops' attention."""
+        c, lm = self.cfg, self.w.loop_memory
+        x = streams if c.streams == 1 else kernels.loop_mem_norm(streams, c.streams, c.d_model)
+        lat = kernels.loop_mem_norm(torch.mm(x, lm.down.t()), 1, c.loop_memory_latent,
+                                    lm.lat_w, lm.lat_b)
+        torch.mm(lat, lm.wkv.t(), out=kv[i])
+
+    def _lm_inject(self, streams: torch.Tensor, kv: torch.Tensor, i: int) -> None:
+        """LoopMemoryHook.inject (loop_memory.py:40-52) before loop i >= 1: every
+        token attends over its endpoints of loops 0..i-1 (LatentAttention,
+        mla_memory.py:66-86, no mask); streams += gate * o(attention)."""
+        c, lm = self.cfg, self.w.loop_memory
+        qn = kernels.loop_mem_norm(streams, c.streams, c.d_model, lm.q_ln_w, lm.q_ln_b)
+        att = kernels.loop_mem_attend(torch.mm(qn, lm.wq.t()), kv, i, c.loop_memory_heads,
+                                      c.loop_memory_head_dim)
+        kernels.loop_mem_add(streams, c.streams, torch.mm(att, lm.wo.t()), lm.gate)
 
     def _head(self, streams: torch.Tensor) -> torch.Tensor:
         """mhc_collapse -> final_norm -> tied LM head (model/model.py:699-707)."""
@@ -149,7 +182,16 @@ class LoopedHybridModel:
         if last_logits_only:
             hs = hs[:, -1:].contiguous()
         logits = self._head(hs.reshape(-1, w)).view(bsz, -1, c.vocab_size)
+        self._check_ep()
         return HybridOutput(logits, state)
+
+    def _check_ep(self) -> None:
+        """Under expert parallelism, surface a failed exchange (a peer that never
+        published its rows, a malformed header) as an error after an eager call
+        instead of serving wrong tokens.  Skipped while a CUDA graph is being
+        captured: whoever replays it checks (ExpertParallel.check)."""
+        if self.ep is not None and not torch.cuda.is_current_stream_capturing():
+            self.ep.check()
 
     def _embed(self, ids: torch.Tensor) -> torch.Tensor:
         """Residual streams of the tokens: embed + stream_seed, [N, S*D] fp32
@@ -188,7 +230,10 @@ class LoopedHybridModel:
         m_bf = torch.empty_like(normed)
         m_f32 = torch.empty_like(streams)
         pending = None  # bf16 update not yet added to the residual stream
+        kv = self._lm_buffer(n, loops)
         for i in range(loops):
+            if kv is not None and i > 0:
+                self._lm_inject(streams, kv, i)
             for j, blk in enumerate(self.w.blocks):
                 key = state_key(i, j)
                 self._add_pending(streams, pending, blk.mixer_norm, out_bf16=normed)
@@ -199,7 +244,12 @@ class LoopedHybridModel:
                 kernels.add_rmsnorm(streams, mixed, blk.ffn_norm, c.rms_eps, out_bf16=m_bf,
                                     out_f32=m_f32)
                 pending = self._moe(blk, m_bf, m_f32, state, key, bsz, t)
-        self._add_pending(streams, pending, None, normalize=False)
+            if kv is not None and i < loops - 1:
+                self._add_pending(streams, pending, None, normalize=False)
+                pending = None
+                self._lm_record(streams, kv, i)
+        if pending is not None:
+            self._add_pending(streams, pending, None, normalize=False)
 
     def _mhc_write(self, streams, blk: Block, maps, pending) -> None:
         """Close a sub-layer: its output (a bf16 delta, or routed expert rows +
@@ -225,7 +275,13 @@ class LoopedHybridModel:
         maps_mix = torch.empty(n, nm, dtype=torch.float32, device=self.device)
         maps_ffn = torch.empty_like(maps_mix)
         pending, prev = None, None
+        kv = self._lm_buffer(n, loops)
         for i in range(loops):
+            if kv is not None and i > 0:
+                self._mhc_write(streams, prev, maps_ffn, pending)
+                pending, prev = None, None
+                self._lm_record(streams, kv, i - 1)
+                self._lm_inject(streams, kv, i)
             for j, blk in enumerate(self.w.blocks):
                 key = state_key(i, j)
                 self._mhc_write(streams, prev, maps_ffn, pending)
@@ -284,6 +340,12 @@ class LoopedHybridModel:
     @torch.no_grad()
     def decode_step(self, input_ids: torch.Tensor, state: RecurrentState,
                     num_loops: int | None = None) -> torch.Tensor:
+        logits = self._decode_step(input_ids, state, num_loops)
+        self._check_ep()
+        return logits
+
+    def _decode_step(self, input_ids: torch.Tensor, state: RecurrentState,
+                     num_loops: int | None = None) -> torch.Tensor:
         """One token per row (LoopedHybridMoEForCausalLM.decode_step, model/model.py:787-915,
         with the loop output carried as in sample_standalone.py's copy).
 
@@ -314,7 +376,13 @@ class LoopedHybridModel:
         m_bf = torch.empty_like(normed)
         m_f32 = torch.empty_like(streams)
         y_rows, plan = None, None
+        kv = self._lm_buffer(bsz, loops)
         for i in range(loops):
+            if kv is not None and i > 0:
+                kernels.add_rmsnorm_routed(streams, y_rows, plan, None, c.rms_eps, normalize=False)
+                y_rows, plan = None, None
+                self._lm_record(streams, kv, i - 1)
+                self._lm_inject(streams, kv, i)
             for j, blk in enumerate(self.w.blocks):
                 key = state_key(i, j)
                 if y_rows is None:
@@ -339,7 +407,14 @@ class LoopedHybridModel:
         return self._decode_head(streams, y_rows, plan, state)
 
     def _experts(self, blk: Block, m_bf: torch.Tensor, plan: kernels.RoutePlan):
-        """Routed expert rows and the plan that combines them (prefill and decode)."""
+        """Routed (and shared) expert rows and the plan that combines them
+        (prefill and decode).  Shared experts (moe.py:185-198, :221-234) are
+        plan experts E..E+S-1 that every token is routed to with probability
+        1/sqrt(S), stacked after the routed experts in w13 / w2."""
+        if self.route_log is not None:
+            self.route_log.append(plan.topk_idx)
+        if self.cfg.moe_shared:
+            plan = kernels.plan_append_shared(plan, self.cfg.moe_shared)
         if self.ep is not None:
             res = self.ep.run(m_bf, plan, blk.moe.w13, blk.moe.w2, path=self.expert_path)
             return res.y_rows, res.plan_for_combine(plan)
@@ -372,7 +447,13 @@ class LoopedHybridModel:
         maps_mix = torch.empty(bsz, nm, dtype=torch.float32, device=self.device)
         maps_ffn = torch.empty_like(maps_mix)
         pending, prev = None, None
+        kv = self._lm_buffer(bsz, loops)
         for i in range(loops):
+            if kv is not None and i > 0:
+                self._mhc_write(streams, prev, maps_ffn, pending)
+                pending, prev = None, None
+                self._lm_record(streams, kv, i - 1)
+                self._lm_inject(streams, kv, i)
             for j, blk in enumerate(self.w.blocks):
                 key = state_key(i, j)
                 self._mhc_write(streams, prev, maps_ffn, pending)
@@ -408,7 +489,13 @@ class LoopedHybridModel:
         m_bf = torch.empty_like(normed)
         hd = c.csa_heads * c.csa_head_dim
         y_rows, plan = None, None
+        kv = self._lm_buffer(bsz, loops)
         for i in range(loops):
+            if kv is not None and i > 0:
+                kernels.add_rmsnorm_routed(cur, y_rows, plan, None, c.rms_eps, normalize=False)
+                y_rows, plan = None, None
+                self._lm_record(cur, kv, i - 1)
+                self._lm_inject(cur, kv, i)
             for j, blk in enumerate(self.w.blocks):
                 key = state_key(i, j)
                 mix = blk.mixer
@@ -479,12 +566,16 @@ class GreedyDecoder:
         self.graph = None
         self.use_graph = use_graph
         self.logprob = None
+        # fp32 logits [B, V] of the last step (in graph mode the graph's own
+        # output buffer, rewritten by every replay)
+        self.logits = None
 
     def _body(self):
         logits = self.model.decode_step(self.tokens, self.state).float()
         tok, lp = kernels.sample(logits, seen=self.seen, uniforms=self.uniforms, update_seen=True,
                                  out=self.tokens, **self.sampling)
         self.logprob = lp
+        self.logits = logits
         return logits
 
     def prime(self, first_tokens: torch.Tensor) -> None:

@@ -111,6 +111,17 @@ def parameter_shapes(cfg: HybridConfig) -> dict[str, tuple[int, ...]]:
             shapes[q + "gate_proj.weight"] = (f, d)
             shapes[q + "up_proj.weight"] = (f, d)
             shapes[q + "down_proj.weight"] = (d, f)
+    if cfg.loop_memory:
+        q, lat = "loop_memory.", cfg.loop_memory_latent
+        w = cfg.loop_memory_heads * cfg.loop_memory_head_dim
+        shapes.update({
+            q + "compressor.down.weight": (lat, d), q + "compressor.up.weight": (d, lat),
+            q + "compressor.norm.weight": (lat,), q + "compressor.norm.bias": (lat,),
+            q + "query_norm.weight": (d,), q + "query_norm.bias": (d,),
+            q + "attention.q.weight": (w, d), q + "attention.k.weight": (w, lat),
+            q + "attention.v.weight": (w, lat), q + "attention.o.weight": (d, w),
+            q + "gating_logit": (),
+        })
     return shapes
 
 
@@ -161,9 +172,20 @@ def synthetic_state_dict(cfg: HybridConfig, seed: int = 0, device: str | torch.d
             return torch.logit(torch.tensor(0.3)).to(device)
         raise KeyError(name)
 
+    def make_loop_memory(name: str, shape: tuple) -> torch.Tensor:
+        if name.endswith("gating_logit"):
+            return torch.zeros(shape, device=device)  # gate sigmoid(0) = 0.5
+        if name.endswith("norm.weight"):
+            return 1.0 + noise(name, shape, 0.1)
+        if name.endswith("norm.bias"):
+            return noise(name, shape, 0.1)
+        return noise(name, shape, 0.1)
+
     def make(name: str, shape: tuple) -> torch.Tensor:
         if ".mhc." in name:
             return make_mhc(name, shape)
+        if name.startswith("loop_memory."):
+            return make_loop_memory(name, shape)
         if len(shape) >= 2:
             gen = torch.Generator(device=device)
             gen.manual_seed((seed * 1_000_003 + zlib.crc32(name.encode())) % (2 ** 62))
@@ -202,8 +224,8 @@ class CsaBlock:
 class MoeBlock:
     router_norm: torch.Tensor  # [D] fp32
     router: torch.Tensor       # [E, D] fp32
-    w13: torch.Tensor          # [E, 2F, D] bf16 (interleaved gate/up)
-    w2: torch.Tensor           # [E, D, F] bf16
+    w13: torch.Tensor          # [E+S, 2F, D] bf16 (interleaved gate/up; routed, then S shared)
+    w2: torch.Tensor           # [E+S, D, F] bf16
     router_folded: torch.Tensor | None = None  # [E, D] fp32 = router * ffn_norm * router_norm
     # local-context path of the ContextAwareRouter (None without it)
     ctx_down: torch.Tensor | None = None   # [L, D] fp32 latent_memory.down
@@ -226,6 +248,21 @@ class MhcBlock:
 
 
 @dataclass
+class LoopMemory:
+    """The loop memory hook (loop_memory.py:11-66) in fp32: latent compressor
+    (down, LayerNorm), query LayerNorm, latent attention and its gate."""
+    down: torch.Tensor      # [L, D]
+    lat_w: torch.Tensor     # [L] compressor LayerNorm
+    lat_b: torch.Tensor     # [L]
+    q_ln_w: torch.Tensor    # [D] query LayerNorm
+    q_ln_b: torch.Tensor    # [D]
+    wq: torch.Tensor        # [H*hd, D]
+    wkv: torch.Tensor       # [2*H*hd, L]: k rows, then v rows
+    wo: torch.Tensor        # [D, H*hd]
+    gate: float             # sigmoid(gating_logit)
+
+
+@dataclass
 class Block:
     kind: str
     mixer_norm: torch.Tensor
@@ -236,15 +273,25 @@ class Block:
 
 
 def _experts(sd: Mapping[str, torch.Tensor], p: str, name: str, lo: int, hi: int,
-             dev: torch.device) -> torch.Tensor:
+             dev: torch.device, group: str = "experts") -> torch.Tensor:
     """Experts lo..hi-1 of one projection as [hi-lo, rows, cols] bf16: from the
-    per-expert parameters (moe.experts.<e>.<name>.weight) or from one stacked
-    tensor (moe.experts.<name>.weight, the .llmy converter's layout)."""
-    stacked = sd.get(f"{p}moe.experts.{name}.weight")
+    per-expert parameters (moe.<group>.<e>.<name>.weight) or from one stacked
+    tensor (moe.<group>.<name>.weight, the .llmy converter's layout); group
+    "experts" (routed) or "shared"."""
+    stacked = sd.get(f"{p}moe.{group}.{name}.weight")
     if stacked is not None:
         return stacked[lo:hi].to(dev, torch.bfloat16)
-    return torch.stack([sd[f"{p}moe.experts.{x}.{name}.weight"].to(dev, torch.bfloat16)
+    return torch.stack([sd[f"{p}moe.{group}.{x}.{name}.weight"].to(dev, torch.bfloat16)
                         for x in range(lo, hi)])
+
+
+def _expert_stack(sd, p: str, name: str, lo: int, hi: int, n_shared: int,
+                  dev: torch.device) -> torch.Tensor:
+    """Routed experts lo..hi-1, then the n_shared shared experts, of one projection."""
+    routed = _experts(sd, p, name, lo, hi, dev)
+    if not n_shared:
+        return routed
+    return torch.cat([routed, _experts(sd, p, name, 0, n_shared, dev, group="shared")])
 
 
 @dataclass
@@ -255,6 +302,7 @@ class ModelWeights:
     collapse: torch.Tensor    # [D, S*D] bf16
     final_norm: torch.Tensor  # [D] fp32
     blocks: list[Block]
+    loop_memory: LoopMemory | None = None
 
     @classmethod
     def from_state_dict(cls, cfg: HybridConfig, sd: Mapping[str, torch.Tensor],
@@ -287,11 +335,12 @@ class ModelWeights:
                                     bf(p + "mixer.value.weight")]).contiguous(),
                     local_out=bf(p + "mixer.local_out.weight"), out=bf(p + "mixer.out.weight"),
                     w_o=w_o.to(torch.bfloat16).contiguous())
-            gate = _experts(sd, p, "gate_proj", lo, hi, dev)
-            up = _experts(sd, p, "up_proj", lo, hi, dev)
+            ns = cfg.moe_shared
+            gate = _expert_stack(sd, p, "gate_proj", lo, hi, ns, dev)
+            up = _expert_stack(sd, p, "up_proj", lo, hi, ns, dev)
             w13 = kernels.pack_w13(gate, up)
             del gate, up
-            w2 = _experts(sd, p, "down_proj", lo, hi, dev).contiguous()
+            w2 = _expert_stack(sd, p, "down_proj", lo, hi, ns, dev).contiguous()
             moe = MoeBlock(router_norm=f32(p + "moe.router.norm.weight"),
                            router=f32(p + "moe.router.logits.weight"), w13=w13, w2=w2)
             moe.router_folded = kernels.fold_router(moe.router, f32(p + "ffn_norm.weight"),
@@ -328,9 +377,20 @@ class ModelWeights:
         collapse = bf("mhc_collapse.weight")
         if seed_t.numel() != ns * cfg.d_model or tuple(collapse.shape) != (cfg.d_model, ns * cfg.d_model):
             raise ValueError(f"stream_seed / mhc_collapse do not match {ns} residual stream(s)")
+        loop_memory = None
+        if cfg.loop_memory:
+            q = "loop_memory."
+            loop_memory = LoopMemory(
+                down=f32(q + "compressor.down.weight"), lat_w=f32(q + "compressor.norm.weight"),
+                lat_b=f32(q + "compressor.norm.bias"), q_ln_w=f32(q + "query_norm.weight"),
+                q_ln_b=f32(q + "query_norm.bias"), wq=f32(q + "attention.q.weight"),
+                wkv=torch.cat([f32(q + "attention.k.weight"), f32(q + "attention.v.weight")]
+                              ).contiguous(),
+                wo=f32(q + "attention.o.weight"),
+                gate=float(torch.sigmoid(sd[q + "gating_logit"].reshape(()).float())))
         return cls(cfg=cfg, embed=bf("embed_tokens.weight"),
                    stream_seed=seed_t.reshape(-1).contiguous(), collapse=collapse,
-                   final_norm=f32("final_norm.weight"), blocks=blocks)
+                   final_norm=f32("final_norm.weight"), blocks=blocks, loop_memory=loop_memory)
 
     @classmethod
     def from_llmy(cls, path, device: str | torch.device = "cuda",
@@ -355,6 +415,8 @@ class ModelWeights:
 
     def _tensors(self):
         yield from (self.embed, self.stream_seed, self.collapse, self.final_norm)
+        if self.loop_memory is not None:
+            yield from (t for t in vars(self.loop_memory).values() if isinstance(t, torch.Tensor))
         for b in self.blocks:
             yield from (b.mixer_norm, b.ffn_norm)
             yield from vars(b.mixer).values()

@@ -111,6 +111,25 @@ int32_t llmyb_route_decode(float* streams, const void* delta, int32_t n_tokens, 
                            int32_t* tile_offsets, int32_t* perm_token, float* perm_prob,
                            int32_t* route_pos, void* stream);
 
+/* Shared experts (model/layers/moe.py:185-198 prefill, :221-234 decode, where
+ * SparseMoE adds sum_s SwiGLU_s(x) / sqrt(S) to the routed output) as plan
+ * experts E..E+S-1: a plan over E routed experts (any llmyb_route* output)
+ * is written extended into the out_* buffers ([N, k+S] slots, E+S counts,
+ * E+S+1 offsets, N*(k+S) rows).  Every token gets a slot per shared expert
+ * with probability 1/sqrt(S); the shared rows follow the routed ones in plan
+ * order (row N*k + s*N + t).  The expert entry points then run routed and
+ * shared experts in one call over weights stacked routed first, then shared,
+ * and the routed combine sums k+S rows per token.  One launch, no host sync. */
+int32_t llmyb_plan_append_shared(int32_t n_tokens, int32_t n_experts, int32_t top_k,
+                                 int32_t n_shared, int32_t tile_m, const int64_t* topk_idx,
+                                 const float* topk_prob, const int32_t* expert_counts,
+                                 const int32_t* expert_offsets, const int32_t* tile_offsets,
+                                 const int32_t* perm_token, const float* perm_prob,
+                                 const int32_t* route_pos, int64_t* out_topk_idx,
+                                 float* out_topk_prob, int32_t* out_counts, int32_t* out_offsets,
+                                 int32_t* out_tile_offsets, int32_t* out_perm_token,
+                                 float* out_perm_prob, int32_t* out_route_pos, void* stream);
+
 /* --------------------------------------------------------------- MoE FFN
  * Replaces _moe_dispatch_fused's expert math (model/layers/moe.py:68-81),
  * triton_moe_dispatch (runpod/kernels/triton_swiglu_moe.py:160-266) and the
@@ -258,9 +277,12 @@ int32_t llmyb_ep_return_p2p(const void* ret_send, const void* recv, int32_t d_mo
                             void* const* peer_segs, int32_t* const* peer_flags, int32_t* sync,
                             void* stream);
 
-/* Bounded wait (one CTA) until flags[0..W) hold the current round. */
+/* Bounded wait (one CTA) until flags[0..W) hold the current round.  After
+ * limit_ns (0: one second; capped at one second) it records LLMYB_ETIMEOUT in
+ * dev_status and returns: a peer that never publishes shows up as an error
+ * the host reads, not as a hung kernel. */
 int32_t llmyb_ep_wait(const int32_t* flags, int32_t world, const int32_t* sync,
-                      int32_t* dev_status, void* stream);
+                      int32_t* dev_status, int64_t limit_ns, void* stream);
 
 /* ------------------------------------------------------ gated delta rule
  * Replaces GatedDeltaNet's recurrence (model/layers/gated_deltanet.py:140-149
@@ -535,6 +557,33 @@ int32_t llmyb_router_ctx_prefill(float* lat, int32_t batch, int32_t seq, int32_t
 int32_t llmyb_router_ctx_step(float* lat, int32_t batch, int32_t latent, int32_t window,
                               const float* ln_w, const float* ln_b, float* ring,
                               const int32_t* positions, float* box, void* stream);
+
+/* ------------------------------------------------------------- loop memory
+ * The loop memory between recurrent loops (model/loop_memory.py:36-66,
+ * LatentAttention mla_memory.py:66-86; called at model/model.py:636, :661-667
+ * and :877, :884-891).  Before every loop after the first, each token attends
+ * over LayerNorm'd latent summaries of its own streams at the end of the
+ * earlier loops; the gated result is added to every stream.  The fp32
+ * projections (down, q, k|v, o) are the caller's GEMMs; these are the
+ * per-token steps between them. */
+
+/* y[t] = mean over the S streams of x[t] (rows of S*width floats at stride
+ * ld; S = 1 copies), then LayerNorm(ln_w, ln_b, eps) if ln_w is non-null
+ * (ln_b nullable).  width <= 24576. */
+int32_t llmyb_loop_mem_norm(const float* x, int64_t ld, int32_t n_tokens, int32_t n_streams,
+                            int32_t width, const float* ln_w, const float* ln_b, float eps,
+                            float* y, int64_t y_ld, void* stream);
+
+/* out [N, H*hd] = per (token, head) softmax_j(q . k_j / sqrt(hd)) v_j over the
+ * n_mem <= 16 endpoints; kv [n_mem, N, 2*H*hd] holds each endpoint's k
+ * projection then its v projection (LatentAttention with causal=False). */
+int32_t llmyb_loop_mem_attend(const float* q, const float* kv, int32_t n_tokens, int32_t n_mem,
+                              int32_t heads, int32_t head_dim, float* out, void* stream);
+
+/* streams [N, S*D] fp32 += gate * delta [N, D] fp32 on every stream
+ * (D % 4 == 0, 16-byte aligned pointers). */
+int32_t llmyb_loop_mem_add(float* streams, int32_t n_tokens, int32_t n_streams, int32_t d_model,
+                           const float* delta, float gate, void* stream);
 
 #ifdef __cplusplus
 }

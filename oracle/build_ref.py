@@ -1,7 +1,7 @@
 """Test infrastructure: build the reference engine's host sampler for parity checks.
 
-Compiles llmy_cuda/src/llmy.cpp of a reference checkout (default
-``/root/reference``, override with ``LLMY_REFERENCE``) with g++ against its own
+Compiles llmy_cuda/src/llmy.cpp of a reference checkout (``LLMY_REFERENCE``;
+by default the directory ``reference`` beside this repository) with g++ against its own
 headers and the CUDA headers, and links ``oracle/_ref/libllmy_ref.so``.  Only
 ``llmy_sample`` (llmy.cpp:132-202, a pure host function) is ever called from it:
 the engine entry points it also contains reference model code that is not
@@ -22,7 +22,8 @@ LIB = OUT / "libllmy_ref.so"
 
 
 def reference_root() -> Path:
-    return Path(os.environ.get("LLMY_REFERENCE", "/root/reference"))
+    return Path(os.environ.get("LLMY_REFERENCE",
+                        Path(__file__).resolve().parents[1].parent / "reference"))
 
 
 def build_ref() -> Path | None:

@@ -27,15 +27,78 @@ def rmsnorm(x, w, eps=1e-6):
     return x * r * (1.0 if w is None else _fp(w))
 
 
+def _layernorm(x, w, b, eps=1e-5):
+    """nn.LayerNorm (default eps 1e-5) over the last dimension."""
+    mu = x.mean(-1, keepdims=True)
+    var = ((x - mu) ** 2).mean(-1, keepdims=True)
+    return (x - mu) / np.sqrt(var + eps) * w + b
+
+
+def _to_numpy(v, dtype):
+    return np.asarray(v.detach().cpu().numpy() if hasattr(v, "detach") else v, dtype=dtype)
+
+
+class _LazyParams:
+    """name -> array converted on first access.  Routed-expert weights are
+    cached only while the cache stays under `expert_cache_bytes` (the
+    large model's experts are 40 GB in fp32): past it they are converted
+    again on every access."""
+
+    def __init__(self, sd, dtype, expert_cache_bytes: int):
+        self._sd, self._dtype = sd, dtype
+        self._cache: dict = {}
+        self._expert_budget = expert_cache_bytes
+
+    def __getitem__(self, name):
+        got = self._cache.get(name)
+        if got is not None:
+            return got
+        a = _to_numpy(self._sd[name], self._dtype)
+        if ".moe.experts." not in name:
+            self._cache[name] = a
+        elif a.nbytes <= self._expert_budget:
+            self._expert_budget -= a.nbytes
+            self._cache[name] = a
+        return a
+
+    def __contains__(self, name):
+        return name in self._sd
+
+
+class _ExpertStack:
+    """w[e] -> expert e's weight of one projection, fetched on use (only the
+    routed experts of a call are read)."""
+
+    def __init__(self, p, prefix: str, name: str):
+        self._p, self._prefix, self._name = p, prefix, name
+
+    def __getitem__(self, e):
+        return self._p[f"{self._prefix}experts.{int(e)}.{self._name}_proj.weight"]
+
+
 class OracleModel:
-    def __init__(self, cfg, sd, dtype=np.float64):
+    def __init__(self, cfg, sd, dtype=np.float64, lazy: bool = False,
+                 expert_cache_bytes: int = 0):
         """cfg: hybrid_llm_b200.config.HybridConfig-like; sd: name -> array-like.
-        dtype float32 is used for the timed CPU baseline, float64 for parity."""
+        dtype float32 is used for the timed CPU baseline, float64 for parity.
+        lazy: convert parameters on first use instead of all up front, and read
+        only the routed experts' weights (for models too large to hold in host
+        memory at `dtype`); expert_cache_bytes bounds the expert weights kept."""
         self.cfg = cfg
         self.dtype = dtype
-        self.p = {k: np.asarray(v.detach().cpu().numpy() if hasattr(v, "detach") else v,
-                                dtype=dtype) for k, v in sd.items()}
+        self.lazy = lazy
+        if lazy:
+            self.p = _LazyParams(sd, dtype, expert_cache_bytes)
+        else:
+            self.p = {k: _to_numpy(v, dtype) for k, v in sd.items()}
         self._experts: dict[int, tuple] = {}
+        # Routing records / overrides, in call order (one entry per MoE call):
+        # route_log collects (own top-k indices, own fp32 router logits);
+        # forced_routes, when set, is a list of top-k index arrays that the
+        # calls take instead of their own top-k (probabilities are still the
+        # softmax of this model's own logits at those experts, context_router.py:73-74).
+        self.route_log: list | None = None
+        self.forced_routes: list | None = None
 
     def _gdn_params(self, j):
         p = f"recurrent_core.{j}.mixer."
@@ -88,11 +151,21 @@ class OracleModel:
         flat = m.reshape(-1, m.shape[-1])
         logits = self._router_logits(j, m, state, key, step).reshape(flat.shape[0], -1)
         idx, prob = routing.router_topk(logits.astype(np.float32), c.moe_top_k)
+        if self.route_log is not None:
+            self.route_log.append((idx, logits.astype(np.float32)))
+        if self.forced_routes is not None:
+            idx = np.asarray(self.forced_routes.pop(0), dtype=np.int64).reshape(idx.shape)
+            top = np.take_along_axis(logits.astype(np.float32).astype(np.float64), idx, -1)
+            prob = np.exp(top - top.max(-1, keepdims=True))
+            prob = prob / prob.sum(-1, keepdims=True)
         if j not in self._experts:
             e = c.moe_experts
-            self._experts[j] = tuple(
-                np.stack([self.p[f"{p}experts.{x}.{n}_proj.weight"] for x in range(e)])
-                for n in ("gate", "up", "down"))
+            if self.lazy:
+                self._experts[j] = tuple(_ExpertStack(self.p, p, n) for n in ("gate", "up", "down"))
+            else:
+                self._experts[j] = tuple(
+                    np.stack([self.p[f"{p}experts.{x}.{n}_proj.weight"] for x in range(e)])
+                    for n in ("gate", "up", "down"))
         wg, wu, wd = self._experts[j]
         out = routing.moe_forward(flat, idx, prob, wg, wu, wd, dtype=self.dtype)
         if c.moe_shared:
@@ -115,6 +188,44 @@ class OracleModel:
         maps, hidden = mhc.read(x, self.p, f"recurrent_core.{j}.mhc.", c.mhc_streams,
                                 c.mhc_iterations)
         return rmsnorm(hidden, w, c.rms_eps), maps
+
+    # -------------------------------------------------------- loop memory
+    def _streams_mean(self, x):
+        """The token's hidden state as the hook sees it: the mean over the
+        streams (loop_memory.py:38, :45); x itself on one plain stream."""
+        return x.mean(-2) if self.cfg.mhc_streams else x
+
+    def _lm_encode(self, x):
+        """LoopMemoryHook.encode / record (loop_memory.py:36-38, :54-66):
+        LayerNorm(down(mean over streams)), the endpoint of one loop."""
+        p = "loop_memory.compressor."
+        h = self._streams_mean(x) @ self.p[p + "down.weight"].T
+        return _layernorm(h, self.p[p + "norm.weight"], self.p[p + "norm.bias"])
+
+    def _lm_inject(self, x, endpoints):
+        """LoopMemoryHook.inject (loop_memory.py:40-52) with LatentAttention
+        (mla_memory.py:66-86, causal=False, no key mask): every token attends
+        over its own endpoints of the earlier loops; the gated output is added
+        to every stream."""
+        if not endpoints:
+            return x
+        c, p = self.cfg, "loop_memory."
+        h, hd = c.loop_memory_heads, c.loop_memory_head_dim
+        qn = _layernorm(self._streams_mean(x), self.p[p + "query_norm.weight"],
+                        self.p[p + "query_norm.bias"])
+        lead = qn.shape[:-1]
+        q = (qn @ self.p[p + "attention.q.weight"].T).reshape(*lead, h, hd)
+        mem = np.stack(endpoints, axis=-2)                      # [..., J, L]
+        k = (mem @ self.p[p + "attention.k.weight"].T).reshape(*lead, len(endpoints), h, hd)
+        v = (mem @ self.p[p + "attention.v.weight"].T).reshape(*lead, len(endpoints), h, hd)
+        s = np.einsum("...hd,...jhd->...hj", q, k) / np.sqrt(hd)
+        s = np.exp(s - s.max(-1, keepdims=True))
+        prob = s / s.sum(-1, keepdims=True)
+        o = np.einsum("...hj,...jhd->...hd", prob, v).reshape(*lead, h * hd)
+        o = o @ self.p[p + "attention.o.weight"].T
+        gate = 1.0 / (1.0 + np.exp(-np.asarray(self.p[p + "gating_logit"], dtype=np.float64)))
+        gate = np.asarray(gate, dtype=o.dtype)
+        return x + gate * (o[..., None, :] if c.mhc_streams else o)
 
     def _write(self, j, x, update, maps):
         """PhysicalBlock._write (model.py:125-126)."""
@@ -139,7 +250,10 @@ class OracleModel:
         loops = c.num_loops if loops is None else loops
         x = _fp(streams)
         t = x.shape[1]
+        endpoints = []  # loop memory (model/model.py:608, :636, :661-667)
         for i in range(loops):
+            if c.loop_memory:
+                x = self._lm_inject(x, endpoints)
             for j in range(c.n_blocks):
                 normed, maps = self._read(j, x, "mixer_norm")
                 if c.block_kind(j) == "gdn":
@@ -160,6 +274,8 @@ class OracleModel:
                 if router_logits is not None:
                     router_logits.append(lg)
                 x = self._write(j, x, y, maps)
+            if c.loop_memory:
+                endpoints.append(self._lm_encode(x))
         state["pos"][:] = t
         return x
 
@@ -189,7 +305,10 @@ class OracleModel:
         c = self.cfg
         ids = np.asarray(ids).reshape(-1)
         x = self.embed(ids)[:, None, :]
+        endpoints = []  # loop memory of this step (model/model.py:840, :877, :884-891)
         for i in range(c.num_loops):
+            if c.loop_memory:
+                x = self._lm_inject(x, endpoints)
             for j in range(c.n_blocks):
                 normed, maps = self._read(j, x, "mixer_norm")
                 if c.block_kind(j) == "gdn":
@@ -225,5 +344,7 @@ class OracleModel:
                 m, maps = self._read(j, x, "ffn_norm")
                 y, _ = self._moe(j, m, state, (i, j), step=True)
                 x = self._write(j, x, y, maps)
+            if c.loop_memory:
+                endpoints.append(self._lm_encode(x))
         state["pos"] += 1
         return self.head(x[:, 0]), state

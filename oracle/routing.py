@@ -51,6 +51,37 @@ def dispatch_plan(idx: np.ndarray, n_experts: int, tile_m: int = 128) -> dict[st
                 perm_token=order // k, route_pos=route_pos)
 
 
+def append_shared(plan: dict, idx: np.ndarray, prob: np.ndarray, n_experts: int, n_shared: int,
+                  tile_m: int = 128) -> dict:
+    """A dispatch plan (dispatch_plan's arrays plus perm_prob, and the routes'
+    idx / prob [N, k]) extended by n_shared shared experts (moe.py:185-198,
+    :221-234: every token through each, the sum scaled by 1/sqrt(n_shared))
+    as experts E..E+S-1 with probability 1/sqrt(S) for every token, their
+    rows after the routed ones: expert E+s holds tokens 0..N-1 at rows
+    N*k + s*N + t.  Summing each token's k + S rows, each row scaled by its
+    probability, gives routed + sum_s SwiGLU_s(x) / sqrt(S)."""
+    idx = np.asarray(idx, dtype=np.int64)
+    n, k = idx.shape
+    s_ = int(n_shared)
+    p = np.float32(1.0 / np.sqrt(float(s_)))
+    rows = n * k
+    shared_pos = rows + np.arange(s_)[None, :] * n + np.arange(n)[:, None]
+    tiles = -(-n // tile_m)
+    step = np.arange(1, s_ + 1)
+    return dict(
+        topk_idx=np.concatenate([idx, np.broadcast_to(n_experts + np.arange(s_), (n, s_))], 1),
+        topk_prob=np.concatenate([np.asarray(prob, np.float32), np.full((n, s_), p, np.float32)], 1),
+        counts=np.concatenate([plan["counts"], np.full(s_, n)]),
+        offsets=np.concatenate([plan["offsets"], plan["offsets"][-1] + n * step]),
+        tile_offsets=np.concatenate([plan["tile_offsets"], plan["tile_offsets"][-1] + tiles * step]),
+        perm_token=np.concatenate([plan["perm_token"], np.tile(np.arange(n), s_)]),
+        perm_prob=np.concatenate([np.asarray(plan["perm_prob"], np.float32),
+                                  np.full(n * s_, p, np.float32)]),
+        route_pos=np.concatenate([np.asarray(plan["route_pos"]).reshape(n, k), shared_pos],
+                                 1).reshape(-1),
+    )
+
+
 def silu(x: np.ndarray) -> np.ndarray:
     return x / (1.0 + np.exp(-x))
 

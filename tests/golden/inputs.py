@@ -157,6 +157,14 @@ def shared_experts_config():
     return dataclasses.replace(mini_config(), moe_shared=2, name="mini-shared")
 
 
+def loop_memory_config():
+    """The mini model with the loop memory between loops, three loops so that
+    the last loop attends over two endpoints (LoopMemoryHook defaults:
+    latent 128, 4 heads x 32)."""
+    import dataclasses
+    return dataclasses.replace(mini_config(), num_loops=3, loop_memory=True, name="mini-loop-mem")
+
+
 def combined_config():
     """mHC (4 streams), the router's local context, the CSA remote branch and
     shared experts together on the mini model (their interaction)."""
@@ -187,8 +195,8 @@ def block_hidden():
 
 def v6_mapping(cfg) -> dict:
     """Reference V6Config fields for a HybridConfig (mHC, the router's local
-    context path, the CSA remote branch and shared experts as configured; loop
-    memory and halting switched off)."""
+    context path, the CSA remote branch, shared experts and the loop memory as
+    configured; adaptive halting switched off)."""
     return dict(
         vocab_size=cfg.vocab_size, d_model=cfg.d_model, physical_blocks=cfg.n_blocks,
         stem_blocks=0, recurrent_blocks=cfg.n_blocks, tail_blocks=0, num_loops=cfg.num_loops,
@@ -205,5 +213,7 @@ def v6_mapping(cfg) -> dict:
         csa=dict(temporal_compression=cfg.csa_compression or 10 ** 9, local_window=cfg.csa_window,
                  index_heads=cfg.csa_heads, index_head_dim=cfg.csa_head_dim,
                  index_top_k=cfg.csa_top_k if cfg.csa_compression else 4),
-        loop_attnres=dict(enabled=False), adaptive_loops=dict(enabled=False),
+        loop_attnres=dict(enabled=cfg.loop_memory, latent_dim=cfg.loop_memory_latent,
+                          heads=cfg.loop_memory_heads, head_dim=cfg.loop_memory_head_dim),
+        adaptive_loops=dict(enabled=False),
     )

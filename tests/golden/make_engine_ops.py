@@ -1,7 +1,7 @@
 """Golden vectors for the engine's device entry points, from the reference's own code.
 
-Run in a container that has the reference checkout (default ``/root/reference``;
-override with ``LLMY_REFERENCE``)::
+Run in a container that has the reference checkout (``LLMY_REFERENCE``;
+by default the directory ``reference`` beside this repository)::
 
     python tests/golden/make_engine_ops.py
 
@@ -21,7 +21,8 @@ from pathlib import Path
 import numpy as np
 
 HERE = Path(__file__).resolve().parent
-REF = Path(os.environ.get("LLMY_REFERENCE", "/root/reference"))
+REF = Path(os.environ.get("LLMY_REFERENCE",
+                        Path(__file__).resolve().parents[2].parent / "reference"))
 
 import torch  # noqa: E402
 

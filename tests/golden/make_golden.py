@@ -1,7 +1,7 @@
 """Generate the golden fixtures by running the reference's own PyTorch code.
 
-Run in a container that has the reference checkout (default
-``/root/reference``; override with ``LLMY_REFERENCE``)::
+Run in a container that has the reference checkout (``LLMY_REFERENCE``;
+by default the directory ``reference`` beside this repository)::
 
     python tests/golden/make_golden.py [section ...]
 
@@ -20,7 +20,8 @@ from pathlib import Path
 import numpy as np
 
 HERE = Path(__file__).resolve().parent
-REF = Path(os.environ.get("LLMY_REFERENCE", "/root/reference"))
+REF = Path(os.environ.get("LLMY_REFERENCE",
+                        Path(__file__).resolve().parents[2].parent / "reference"))
 sys.path.insert(0, str(HERE.parents[1]))  # repo root, for the weight generator
 
 os.environ.setdefault("LLMY_DISABLE_TRITON", "1")
@@ -331,6 +332,11 @@ def sec_combined() -> None:
     save("combined", **_prefill_and_decode(inputs.combined_config(), "cb", steps=6))
 
 
+def sec_loop_mem() -> None:
+    """The mini model with the loop memory (loop_memory.py) between its three loops."""
+    save("loop_mem", **_prefill_and_decode(inputs.loop_memory_config(), "lm", steps=4))
+
+
 def sec_shared() -> None:
     """The mini model with two shared experts next to the routed ones."""
     save("shared", **_prefill_and_decode(inputs.shared_experts_config(), "sh", steps=4))
@@ -374,7 +380,7 @@ def sec_mhc() -> None:
     save("mhc", **res)
 
 
-SECTIONS = {"combined": sec_combined, "shared": sec_shared, "csa_remote": sec_csa_remote, "router_ctx": sec_router_ctx, "mhc": sec_mhc, "model": sec_model, "sample": sec_sample, "router": sec_router, "moe": sec_moe, "gdn": sec_gdn, "csa": sec_csa, "band": sec_band}
+SECTIONS = {"loop_mem": sec_loop_mem, "combined": sec_combined, "shared": sec_shared, "csa_remote": sec_csa_remote, "router_ctx": sec_router_ctx, "mhc": sec_mhc, "model": sec_model, "sample": sec_sample, "router": sec_router, "moe": sec_moe, "gdn": sec_gdn, "csa": sec_csa, "band": sec_band}
 
 
 def main(argv: list[str]) -> None:

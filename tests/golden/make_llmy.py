@@ -1,7 +1,7 @@
 """Generate the ``.llmy`` fixture with the reference's own checkpoint converter.
 
-Run in a container that has the reference checkout (default ``/root/reference``;
-override with ``LLMY_REFERENCE``)::
+Run in a container that has the reference checkout (``LLMY_REFERENCE``;
+by default the directory ``reference`` beside this repository)::
 
     python tests/golden/make_llmy.py
 
@@ -26,7 +26,8 @@ from pathlib import Path
 import numpy as np
 
 HERE = Path(__file__).resolve().parent
-REF = Path(os.environ.get("LLMY_REFERENCE", "/root/reference"))
+REF = Path(os.environ.get("LLMY_REFERENCE",
+                        Path(__file__).resolve().parents[2].parent / "reference"))
 sys.path.insert(0, str(HERE.parents[1]))
 sys.path.insert(0, str(HERE))
 os.environ.setdefault("LLMY_DISABLE_TRITON", "1")

@@ -140,13 +140,15 @@ def test_decode_norm_gemv(cuda, n, d, p):
     assert float((out.float() - ref).abs().max() / ref.abs().max()) < 1e-2
 
 
+@pytest.mark.parametrize("n", [1, 2])
 @pytest.mark.parametrize("gdn", [True, False])
-def test_decode_out_router(cuda, gdn):
+def test_decode_out_router(cuda, gdn, n):
     """[C]: projection (+ conv gate) into the residual stream, then the
-    router: the stream update against torch, routes against fp64 top-k."""
+    router: the stream update against torch, routes against fp64 top-k.
+    n = 1 at D = 768 is the B=1 decode step's one-cluster variant."""
     from hybrid_llm_b200 import kernels
     from oracle import routing
-    n, d, kin, e, k = 2, 768, 768, 16, 2
+    d, kin, e, k = 768, 768, 16, 2
     g = torch.Generator(device="cuda").manual_seed(5 + gdn)
     inp = torch.randn(n, kin, device="cuda", generator=g).bfloat16()
     w = (torch.randn(d, kin, device="cuda", generator=g) * 0.03).bfloat16()

@@ -175,8 +175,9 @@ def test_shared_experts_config_and_model_guard():
 
     cfg = inputs.shared_experts_config()
     assert HybridConfig.from_v6(inputs.v6_mapping(cfg)) == cfg and cfg.moe_shared == 2
+    # served on one device; refused under expert parallelism
     with pytest.raises(NotImplementedError):
-        LoopedHybridModel(types.SimpleNamespace(cfg=cfg))
+        LoopedHybridModel(types.SimpleNamespace(cfg=cfg), ep=object())
 
 
 def test_combined_features_match_reference():
@@ -193,3 +194,58 @@ def test_combined_features_match_reference():
         np.testing.assert_array_equal(tok, g["cb_tokens"][:, i])
         last, state = m.decode_step(tok, state)
         np.testing.assert_allclose(last, g["cb_step_logits"][:, i], rtol=1e-5, atol=1e-5)
+
+
+def test_loop_memory_matches_reference():
+    """The loop memory between loops (loop_memory.py:36-66, model/model.py:608-667
+    prefill, :840-891 decode): three loops, prefill and four decode steps."""
+    g = golden("loop_mem")
+    np.testing.assert_allclose(g["lm_prefill_last"], g["lm_sa_prefill_last"], rtol=1e-5, atol=1e-6)
+    cfg = inputs.loop_memory_config()
+    m = _oracle(cfg)
+    logits, state = m.forward(inputs.mini_prompt())
+    np.testing.assert_allclose(logits[:, -1], g["lm_prefill_last"], rtol=1e-5, atol=1e-5)
+    last = logits[:, -1]
+    for i in range(g["lm_tokens"].shape[1]):
+        tok = last.argmax(-1)
+        np.testing.assert_array_equal(tok, g["lm_tokens"][:, i])
+        last, state = m.decode_step(tok, state)
+        np.testing.assert_allclose(last, g["lm_step_logits"][:, i], rtol=1e-5, atol=1e-5)
+    # the hook matters: without it the same weights give other logits
+    import dataclasses
+    off = dataclasses.replace(cfg, loop_memory=False)
+    sd = synthetic_state_dict(cfg, seed=0)
+    base, _ = OracleModel(off, {k: sd[k] for k in sd}).forward(inputs.mini_prompt())
+    moved = np.abs(base[:, -1] - g["lm_prefill_last"]).max() / np.abs(g["lm_prefill_last"]).max()
+    assert moved > 0.05, moved
+
+
+def test_loop_memory_config_conversion():
+    import pytest
+    from hybrid_llm_b200.config import HybridConfig
+
+    cfg = inputs.loop_memory_config()
+    assert HybridConfig.from_v6(inputs.v6_mapping(cfg)) == cfg
+    base = inputs.v6_mapping(cfg)
+    with pytest.raises(ValueError):
+        HybridConfig.from_v6(dict(base, adaptive_loops=dict(enabled=True)))
+
+
+def test_forced_routes_reproduce_free_routing():
+    """OracleModel.forced_routes (the routing-forced full-size parity tests):
+    forcing a model's own routes changes nothing; forcing other routes does."""
+    cfg = inputs.mini_config()
+    m = _oracle(cfg)
+    m.route_log = []
+    free, st = m.forward(inputs.mini_prompt())
+    own = [idx for idx, _ in m.route_log]
+    assert len(own) == cfg.num_loops * cfg.n_blocks
+    m2 = _oracle(cfg)
+    m2.forced_routes = list(own)
+    forced, _ = m2.forward(inputs.mini_prompt())
+    assert not m2.forced_routes
+    np.testing.assert_array_equal(forced, free)
+    m3 = _oracle(cfg)
+    m3.forced_routes = [np.roll(r, 1, axis=0) for r in own]
+    other, _ = m3.forward(inputs.mini_prompt())
+    assert np.abs(other - free).max() > 1e-3

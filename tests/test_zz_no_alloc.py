@@ -34,7 +34,9 @@ def _args(b):
                                       "perm_prob", "route_pos", "order")]
 
 
-@pytest.mark.parametrize("n,e,k", [(4096, 64, 8), (16384, 32, 4), (37, 16, 2)])
+# (65792, 255, 2) needs ceil(65792/256) * 255 + 1 = 65,536 histogram ints:
+# exactly the array's capacity.
+@pytest.mark.parametrize("n,e,k", [(4096, 64, 8), (16384, 32, 4), (37, 16, 2), (65792, 255, 2)])
 def test_route_noalloc_matches_route(cuda, n, e, k):
     from hybrid_llm_b200 import _native
     lib = _native.lib()
@@ -54,12 +56,18 @@ def test_route_noalloc_matches_route(cuda, n, e, k):
             assert torch.equal(ref[name], got[name]), (call, name)
 
 
-def test_route_noalloc_rejects_oversized_calls(cuda):
+@pytest.mark.parametrize("over", [1, 257])
+def test_route_noalloc_rejects_oversized_calls(cuda, over):
+    """A call needing `over` more histogram ints than the array holds is refused
+    (over = 1: one past the limit; the array's contents are not touched)."""
     from hybrid_llm_b200 import _native
     lib = _native.lib()
     cap = int(lib.llmyb_route_noalloc_max_scratch_ints())
+    assert cap == 65536
     e = 256
-    n = ((cap // e) + 1) * 256  # needs more histogram entries than the array holds
+    # need = ceil(n / 256) * e + 1 = cap + over
+    n = (cap + over - 1) // e * 256
+    assert (n + 255) // 256 * e + 1 == cap + over
     logits = torch.zeros(n, e, device="cuda")
     b = _buffers(n, e, 2)
     status = lib.llmyb_route_noalloc(logits.data_ptr(), None, n, e, 2, TILE_M, *_args(b),
