@@ -992,3 +992,63 @@ def loop_mem_add(streams: torch.Tensor, n_streams: int, delta: torch.Tensor, gat
     n, d = delta.shape
     _native.call("llmyb_loop_mem_add", _ptr(streams), n, int(n_streams), d, _ptr(delta),
                  float(gate), _stream())
+
+
+# ------------------------------------------------------------- CSA remote branch
+def csa_remote_prefill(x: torch.Tensor, q: torch.Tensor, w_comp: torch.Tensor, ratio: int,
+                       top_k: int, heads: int, pend_sum: torch.Tensor, pend_cnt: torch.Tensor):
+    """CSA remote branch over a prompt (csa.py:77-131, compressed_attention.py:85-149).
+
+    x [B, T, D] bf16 (the CSA input), q [B, T, H*Dh] bf16 (a view is fine),
+    w_comp [H*Dh + D, D] bf16 = [compressor.key; compressor.value].  Returns
+    (remote [B, T, D] bf16, summaries [B, n, H*Dh + D] bf16 = key | value of
+    every complete block); pend_sum [B, D] fp32 / pend_cnt [B] int32 receive
+    the pending partial block."""
+    _require_cuda(x, q, w_comp, pend_sum, pend_cnt)
+    bsz, t, d = x.shape
+    hd = q.shape[-1]
+    n = t // ratio
+    _rows(x, "x")
+    _rows(q, "q")
+    dev = x.device
+    means = torch.empty(bsz, max(n, 1), d, dtype=torch.bfloat16, device=dev)
+    _native.call("llmyb_csa_block_means", _ptr(x), x.stride(1), bsz, t, d, int(ratio),
+                 _ptr(means), _ptr(_inplace(pend_sum, "pend_sum")),
+                 _ptr(_inplace(pend_cnt, "pend_cnt")), _stream())
+    remote = torch.zeros(bsz, t, d, dtype=torch.bfloat16, device=dev)
+    if n == 0:
+        return remote, torch.empty(bsz, 0, hd + d, dtype=torch.bfloat16, device=dev)
+    summ = torch.mm(means.view(bsz * n, d), w_comp.t()).view(bsz, n, hd + d)
+    ldp = (n + 7) // 8 * 8
+    p = torch.empty(bsz, t, ldp, dtype=torch.bfloat16, device=dev)
+    _native.call("llmyb_csa_remote_rows", _ptr(q), q.stride(1), _ptr(summ), hd + d, bsz, t,
+                 int(heads), hd // heads, n, int(ratio), int(top_k), _ptr(p), ldp, _stream())
+    torch.bmm(p[..., :n], summ[..., hd:], out=remote)
+    return remote, summ
+
+
+def csa_remote_step(x: torch.Tensor, q: torch.Tensor, w_comp: torch.Tensor, ratio: int,
+                    top_k: int, heads: int, mem_k: torch.Tensor, mem_v: torch.Tensor,
+                    mem_count: torch.Tensor, pend_sum: torch.Tensor, pend_cnt: torch.Tensor,
+                    out: torch.Tensor, scratch: tuple[torch.Tensor, torch.Tensor] | None = None):
+    """One decode token of the CSA remote branch (csa.py:208-256,
+    compressed_attention.py:151-206): x [B, D] bf16 joins the pending block
+    (a completed block's summary is stored at slot mem_count); out [B, D]
+    (a row view is fine) receives the remote attention of q [B, H*Dh] over
+    the row's summaries.  mem_k [B, cap, H*Dh], mem_v [B, cap, D] bf16."""
+    _require_cuda(x, q, w_comp, mem_k, mem_v, mem_count, pend_sum, pend_cnt, out)
+    for t_, nm in ((x, "x"), (q, "q"), (out, "out")):
+        _rows(t_, nm)
+    bsz, d = x.shape
+    hd = q.shape[-1]
+    cap = mem_k.shape[1]
+    if scratch is None:
+        scratch = (torch.empty(bsz * heads * top_k, dtype=torch.int32, device=x.device),
+                   torch.empty(bsz * heads * top_k, dtype=torch.float32, device=x.device))
+    _native.call("llmyb_csa_remote_step", _ptr(x), x.stride(0), _ptr(q), q.stride(0), bsz,
+                 int(heads), hd // heads, d, int(ratio), int(top_k), cap, _ptr(w_comp),
+                 _ptr(_inplace(mem_k, "mem_k")), _ptr(_inplace(mem_v, "mem_v")),
+                 _ptr(_inplace(mem_count, "mem_count")), _ptr(_inplace(pend_sum, "pend_sum")),
+                 _ptr(_inplace(pend_cnt, "pend_cnt")), _ptr(scratch[0]), _ptr(scratch[1]),
+                 _ptr(out), out.stride(0), _ptr(device_status(x.device)), _stream())
+    return out

@@ -46,10 +46,6 @@ class LoopedHybridModel:
     every rank of the group then runs the same calls on its own sequences."""
 
     def __init__(self, weights: ModelWeights, ep=None):
-        if weights.cfg.csa_compression:
-            raise NotImplementedError(
-                "the CSA remote compressed branch (csa.temporal_compression) has no B200 kernel "
-                "yet; oracle.model.OracleModel restates it")
         if weights.cfg.moe_shared and ep is not None:
             raise NotImplementedError(
                 "shared experts (moe.shared_experts) are served on one device only, not under "
@@ -326,7 +322,21 @@ class LoopedHybridModel:
         k = proj[..., hd:2 * hd].unflatten(-1, (c.csa_heads, c.csa_head_dim))
         v = proj[..., 2 * hd:]
         local = kernels.csa_local_prefill(q, k, v, c.csa_window)
-        mixed = torch.mm(torch.mm(local.view(bsz * t, -1), a.local_out.t()), a.out.t())
+        h = torch.mm(local.view(bsz * t, -1), a.local_out.t())
+        if c.csa_compression:
+            # remote branch (csa.py:77-131): out(local_out(local) + remote_out(remote))
+            remote, summ = kernels.csa_remote_prefill(
+                normed.view(bsz, t, -1), proj[..., :hd], a.w_comp, c.csa_compression, c.csa_top_k,
+                c.csa_heads, state.remote_sum[key], state.remote_pending[key])
+            n = summ.shape[1]
+            if n > state.remote_k[key].shape[1]:
+                raise ValueError(f"{t} prompt tokens exceed the state's remote memory "
+                                 f"(RecurrentState max_len {state.max_len})")
+            state.remote_k[key][:, :n] = summ[..., :hd]
+            state.remote_v[key][:, :n] = summ[..., hd:]
+            state.remote_count[key].fill_(n)
+            h.addmm_(remote.view(bsz * t, -1), a.remote_out.t())
+        mixed = torch.mm(h, a.out.t())
         # ring caches for decode: token p at slot p % W (last min(T, W) tokens)
         w = c.csa_window
         lo = max(0, t - w)
@@ -364,8 +374,9 @@ class LoopedHybridModel:
         d = c.d_model
         if c.mhc_streams:
             return self._decode_mhc(ids, state, loops)
+        csa_in = 2 * d if c.csa_compression else d  # input width of the CSA output projection
         if self.decode_fused and not c.router_context and kernels.decode_fused_supported(
-                bsz, d, c.moe_experts, c.moe_top_k, c.gdn_heads * c.gdn_value_dim, d):
+                bsz, d, c.moe_experts, c.moe_top_k, c.gdn_heads * c.gdn_value_dim, csa_in):
             return self._decode_fused(ids, state, loops)
         fused_router = (not c.router_context
                         and kernels.route_fused_supported(bsz, c.moe_experts, c.moe_top_k, d))
@@ -487,7 +498,6 @@ class LoopedHybridModel:
         nxt = torch.empty_like(cur)
         normed = torch.empty(bsz, d, dtype=torch.bfloat16, device=self.device)
         m_bf = torch.empty_like(normed)
-        hd = c.csa_heads * c.csa_head_dim
         y_rows, plan = None, None
         kv = self._lm_buffer(bsz, loops)
         for i in range(loops):
@@ -514,11 +524,8 @@ class LoopedHybridModel:
                         o.view(bsz, -1), mix.w_out, *router, conv_w=mix.conv, normed=normed,
                         history=state.gdn_conv_histories[key], tile_m=128)
                 else:
-                    local = kernels.csa_local_decode(proj[:, :hd], proj[:, hd:2 * hd],
-                                                     proj[:, 2 * hd:], state.local_k[key],
-                                                     state.local_v[key], state.positions,
-                                                     c.csa_heads)
-                    plan = kernels.decode_out_router(local, mix.w_o, *router, tile_m=128)
+                    attn = self._csa_mix_step(mix, proj, normed, state, key, bsz)
+                    plan = kernels.decode_out_router(attn, mix.w_o, *router, tile_m=128)
                 y_rows, plan = self._experts(blk, m_bf, plan)
         return self._decode_head(cur, y_rows, plan, state)
 
@@ -537,10 +544,25 @@ class LoopedHybridModel:
         c = self.cfg
         hd = c.csa_heads * c.csa_head_dim
         proj = torch.mm(normed, a.w_in.t())
-        local = kernels.csa_local_decode(proj[:, :hd], proj[:, hd:2 * hd], proj[:, 2 * hd:],
-                                         state.local_k[key], state.local_v[key], state.positions,
-                                         c.csa_heads)
-        return torch.mm(local, a.w_o.t())
+        return torch.mm(self._csa_mix_step(a, proj, normed, state, key, bsz), a.w_o.t())
+
+    def _csa_mix_step(self, a: CsaBlock, proj, normed, state: RecurrentState, key: str,
+                      bsz: int):
+        """The CSA decode step's attention outputs: local [B, D], or with the
+        remote branch [local | remote] [B, 2D] (the input of w_o; csa.py:172-256)."""
+        c = self.cfg
+        hd, d = c.csa_heads * c.csa_head_dim, c.d_model
+        width = 2 * d if c.csa_compression else d
+        mix = torch.empty(bsz, width, dtype=torch.bfloat16, device=self.device)
+        kernels.csa_local_decode(proj[:, :hd], proj[:, hd:2 * hd], proj[:, 2 * hd:],
+                                 state.local_k[key], state.local_v[key], state.positions,
+                                 c.csa_heads, out=mix[:, :d])
+        if c.csa_compression:
+            kernels.csa_remote_step(normed, proj[:, :hd], a.w_comp, c.csa_compression, c.csa_top_k, c.csa_heads,
+                                    state.remote_k[key], state.remote_v[key],
+                                    state.remote_count[key], state.remote_sum[key],
+                                    state.remote_pending[key], mix[:, d:])
+        return mix
 
 
 class GreedyDecoder:

@@ -12,6 +12,15 @@ keys (model/model.py:168-171) —
   * ``router_latents[key]``    [B, W, L] fp32 ring of the router's LayerNorm'd
     MLA latents of the last W positions (router_latent_histories,
     model/model.py:239-247; only with the router's local context).
+  * CSA remote branch (only with ``csa_compression``): ``remote_k[key]``
+    [B, C, H*Dh] / ``remote_v[key]`` [B, C, D] bf16, the keys and values of
+    the row's completed block summaries (compressed memory keys / values,
+    csa.py:208-256), ``remote_count[key]`` [B] int32 how many there are,
+    ``remote_sum[key]`` [B, D] fp32 / ``remote_pending[key]`` [B] int32 the
+    pending partial block (MemoryState.pending_sum / pending_count).  C =
+    ceil(max_len / ratio) summaries.  The reference also appends an
+    invisible entry for every decode token that completes no block; no query
+    can see those, so they are not kept.
   * ``positions`` [B] int32, position of the next token of each row.
 All buffers are allocated once for a batch size so that a captured decode
 graph can update them in place.
@@ -28,9 +37,13 @@ def state_key(loop: int, block: int) -> str:
 
 
 class RecurrentState:
-    def __init__(self, cfg: HybridConfig, batch: int, device: torch.device | str = "cuda"):
+    def __init__(self, cfg: HybridConfig, batch: int, device: torch.device | str = "cuda",
+                 max_len: int = 8192):
+        """max_len: the longest sequence (prompt + generated tokens) the CSA
+        remote branch's summary memory holds."""
         self.cfg = cfg
         self.batch = int(batch)
+        self.max_len = int(max_len)
         self.device = torch.device(device)
         d = cfg.d_model
         self.gdn_states: dict[str, torch.Tensor] = {}
@@ -61,7 +74,32 @@ class RecurrentState:
                     self.router_latents[state_key(i, j)] = torch.zeros(
                         batch, cfg.router_local_context, cfg.router_latent_dim,
                         dtype=torch.float32, device=self.device)
+        self.remote_k: dict[str, torch.Tensor] = {}
+        self.remote_v: dict[str, torch.Tensor] = {}
+        self.remote_count: dict[str, torch.Tensor] = {}
+        self.remote_sum: dict[str, torch.Tensor] = {}
+        self.remote_pending: dict[str, torch.Tensor] = {}
+        if cfg.csa_compression:
+            cap = -(-self.max_len // cfg.csa_compression)
+            hd = cfg.csa_heads * cfg.csa_head_dim
+            for key in self.local_k:
+                self.remote_k[key] = torch.zeros(batch, cap, hd, dtype=torch.bfloat16,
+                                                 device=self.device)
+                self.remote_v[key] = torch.zeros(batch, cap, d, dtype=torch.bfloat16,
+                                                 device=self.device)
+                self.remote_count[key] = torch.zeros(batch, dtype=torch.int32, device=self.device)
+                self.remote_sum[key] = torch.zeros(batch, d, dtype=torch.float32,
+                                                   device=self.device)
+                self.remote_pending[key] = torch.zeros(batch, dtype=torch.int32,
+                                                       device=self.device)
         self.positions = torch.zeros(batch, dtype=torch.int32, device=self.device)
+
+    def _tables(self):
+        return (("gdn_states", self.gdn_states), ("gdn_conv_histories", self.gdn_conv_histories),
+                ("local_k", self.local_k), ("local_v", self.local_v),
+                ("router_latents", self.router_latents), ("remote_k", self.remote_k),
+                ("remote_v", self.remote_v), ("remote_count", self.remote_count),
+                ("remote_sum", self.remote_sum), ("remote_pending", self.remote_pending))
 
     def fill_synthetic(self, position: int, seed: int = 0) -> None:
         """Stand-in for a prefilled context of `position` tokens (benchmarks
@@ -81,38 +119,31 @@ class RecurrentState:
         """Clear the state of the selected rows (recurrent_state.py:218-244)."""
         mask = rows.to(device=self.device, dtype=torch.bool)
         for t in (*self.gdn_states.values(), *self.gdn_conv_histories.values(),
-                  *self.router_latents.values()):
+                  *self.router_latents.values(), *self.remote_count.values(),
+                  *self.remote_sum.values(), *self.remote_pending.values()):
             t[mask] = 0
         self.positions[mask] = 0
 
     def zero_(self) -> None:
         """Zero every state tensor and position (a fresh conversation)."""
-        for t in (*self.gdn_states.values(), *self.gdn_conv_histories.values(),
-                  *self.local_k.values(), *self.local_v.values(), *self.router_latents.values(),
-                  self.positions):
-            t.zero_()
+        for _, table in self._tables():
+            for t in table.values():
+                t.zero_()
+        self.positions.zero_()
 
     def nbytes(self) -> int:
-        tensors = (*self.gdn_states.values(), *self.gdn_conv_histories.values(),
-                   *self.local_k.values(), *self.local_v.values(),
-                   *self.router_latents.values(), self.positions)
+        tensors = [t for _, table in self._tables() for t in table.values()] + [self.positions]
         return sum(t.numel() * t.element_size() for t in tensors)
 
     def state_dict(self) -> dict[str, torch.Tensor]:
         out: dict[str, torch.Tensor] = {"positions": self.positions.clone()}
-        for name, table in (("gdn_states", self.gdn_states),
-                            ("gdn_conv_histories", self.gdn_conv_histories),
-                            ("local_k", self.local_k), ("local_v", self.local_v),
-                            ("router_latents", self.router_latents)):
+        for name, table in self._tables():
             for key, t in table.items():
                 out[f"{name}.{key}"] = t.clone()
         return out
 
     def load_state_dict(self, sd: dict[str, torch.Tensor]) -> None:
         self.positions.copy_(sd["positions"])
-        for name, table in (("gdn_states", self.gdn_states),
-                            ("gdn_conv_histories", self.gdn_conv_histories),
-                            ("local_k", self.local_k), ("local_v", self.local_v),
-                            ("router_latents", self.router_latents)):
+        for name, table in self._tables():
             for key, t in table.items():
                 t.copy_(sd[f"{name}.{key}"])

@@ -217,7 +217,13 @@ class CsaBlock:
     w_in: torch.Tensor       # [2*H*Dh + D, D] bf16: query | key | value
     local_out: torch.Tensor  # [D, D] bf16
     out: torch.Tensor        # [D, D] bf16
-    w_o: torch.Tensor        # [D, D] bf16 = out @ local_out (computed in fp32), for decode
+    # decode output projection (computed in fp32): out @ local_out [D, D], or
+    # with the remote branch [out @ local_out | out @ remote_out] [D, 2D]
+    w_o: torch.Tensor
+    # remote branch (None without it): remote_out [D, D] and the compressor's
+    # [key; value] [H*Dh + D, D] (compressed_attention.py:80-83), bf16
+    remote_out: torch.Tensor | None = None
+    w_comp: torch.Tensor | None = None
 
 
 @dataclass
@@ -330,11 +336,19 @@ class ModelWeights:
                     conv=f32(p + "mixer.conv.weight").reshape(cfg.d_model, -1).contiguous())
             else:
                 w_o = (f32(p + "mixer.out.weight") @ f32(p + "mixer.local_out.weight"))
+                remote_out = w_comp = None
+                if cfg.csa_compression:
+                    w_o = torch.cat([w_o, f32(p + "mixer.out.weight")
+                                     @ f32(p + "mixer.remote_out.weight")], 1)
+                    remote_out = bf(p + "mixer.remote_out.weight")
+                    w_comp = torch.cat([bf(p + "mixer.compressor.key.weight"),
+                                        bf(p + "mixer.compressor.value.weight")]).contiguous()
                 mixer = CsaBlock(
                     w_in=torch.cat([bf(p + "mixer.query.weight"), bf(p + "mixer.key.weight"),
                                     bf(p + "mixer.value.weight")]).contiguous(),
                     local_out=bf(p + "mixer.local_out.weight"), out=bf(p + "mixer.out.weight"),
-                    w_o=w_o.to(torch.bfloat16).contiguous())
+                    w_o=w_o.to(torch.bfloat16).contiguous(), remote_out=remote_out,
+                    w_comp=w_comp)
             ns = cfg.moe_shared
             gate = _expert_stack(sd, p, "gate_proj", lo, hi, ns, dev)
             up = _expert_stack(sd, p, "up_proj", lo, hi, ns, dev)

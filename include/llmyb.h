@@ -585,6 +585,48 @@ int32_t llmyb_loop_mem_attend(const float* q, const float* kv, int32_t n_tokens,
 int32_t llmyb_loop_mem_add(float* streams, int32_t n_tokens, int32_t n_streams, int32_t d_model,
                            const float* delta, float gate, void* stream);
 
+/* ------------------------------------------------------ CSA remote branch
+ * The CSA remote compressed branch (model/layers/csa.py:77-131 prefill,
+ * :208-256 decode) over the causal temporal compressor
+ * (model/layers/compressed_attention.py:85-206), without segment ids: every
+ * complete `ratio`-token block of the CSA input is summarised by its mean m
+ * (key W_k m [H*Dh], value W_v m [D]), visible from the block's last
+ * position; each query attends per head to its top_k (<= 32) visible
+ * summaries (softmax over the selected scores, ties to the lower index) and
+ * the heads' results are averaged.  Bf16 inputs/outputs, fp32 arithmetic. */
+
+/* Prefill compressor: means [B, n, D] (n = seq / ratio) of the complete
+ * blocks of x [B, seq, D] (rows at stride ldx), and the pending partial
+ * block's sum pend_sum [B, D] fp32 / count pend_cnt [B] for decode. */
+int32_t llmyb_csa_block_means(const void* x, int64_t ldx, int32_t batch, int32_t seq,
+                              int32_t d_model, int32_t ratio, void* means, float* pend_sum,
+                              int32_t* pend_cnt, void* stream);
+
+/* Prefill attention weights: P[b, t, 0:n] (bf16, row stride ldp) = the mean
+ * over heads of each head's top-k softmax weights over the summaries visible
+ * to token t (the first min(n, (t+1)/ratio)); q [B*seq] rows at stride ldq,
+ * keys [B*n] rows of H*Dh at stride ldk.  remote = P V is then one batched
+ * GEMM of the caller. */
+int32_t llmyb_csa_remote_rows(const void* q, int64_t ldq, const void* keys, int64_t ldk,
+                              int32_t batch, int32_t seq, int32_t heads, int32_t head_dim,
+                              int32_t n_summaries, int32_t ratio, int32_t top_k, void* P,
+                              int64_t ldp, void* stream);
+
+/* Decode step (three launches): the token x [B, D] joins each row's pending
+ * block; a completing block's summary [key | value] = w_comp [H*Dh + D, D] .
+ * mean goes to slot mem_count[b] of mem_k [B, capacity, H*Dh] / mem_v
+ * [B, capacity, D]; then out [B, D] (row stride ldo) = the remote attention
+ * of q over the row's summaries, and the compressor state (pend_sum fp32
+ * [B, D], pend_cnt, mem_count) advances.  sel_j / sel_w [B, H, top_k] are
+ * scratch.  A row past `capacity` summaries records LLMYB_EUNSUPPORTED in
+ * dev_status (nullable) and keeps its oldest summaries. */
+int32_t llmyb_csa_remote_step(const void* x, int64_t ldx, const void* q, int64_t ldq,
+                              int32_t batch, int32_t heads, int32_t head_dim, int32_t d_model,
+                              int32_t ratio, int32_t top_k, int32_t capacity, const void* w_comp,
+                              void* mem_k, void* mem_v, int32_t* mem_count, float* pend_sum,
+                              int32_t* pend_cnt, int32_t* sel_j, float* sel_w, void* out,
+                              int64_t ldo, int32_t* dev_status, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
