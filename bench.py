@@ -194,6 +194,9 @@ def run_reference(args) -> None:
 # decode shape, measured with ncu (dram__bytes_read.sum + dram__bytes_write.sum,
 # caches flushed before the launch; two launches: 1,305,344 and 1,323,520 bytes).
 OUT_ROUTER_TRAFFIC = 1_314_432
+# ncu dram__bytes_read.sum + dram__bytes_write.sum of one decode_persistent_kernel
+# launch at the benchmark's decode shape (None until captured)
+PERSISTENT_TRAFFIC = None
 
 
 def out_router_roofline(model, p: dict, reps: int = 50) -> dict:
@@ -250,6 +253,59 @@ def out_router_roofline(model, p: dict, reps: int = 50) -> dict:
                       "combined through distributed shared memory; top-k/plan in CTA 0",
             "algorithmic_bytes_per_launch": alg, "avg_launch_us": dt * 1e6,
             "timing": f"CUDA events over a graph of {reps} launches x 5 replays",
+            "peak_source": p["source"]}
+
+
+def persistent_roofline(model, state, p: dict, reps: int = 20) -> dict:
+    """Roofline of the decode step's kernel when the step is one persistent
+    launch (llmyb_decode_persistent): algorithmic bytes per launch (every
+    weight, cache and state byte the step touches, decode_bytes_per_step with
+    the folded CSA projection) over the average launch time, timed with CUDA
+    events over a CUDA graph of `reps` launches (each a 4-byte barrier reset +
+    the kernel) on the stream they run on.  The launches advance a copy of the
+    decode state."""
+    import ctypes
+
+    import torch
+
+    from hybrid_llm_b200 import _native
+    from hybrid_llm_b200.state import RecurrentState
+
+    st = RecurrentState(model.cfg, state.batch, "cuda")
+    st.load_state_dict(state.state_dict())
+    pd = model._persistent_for(st)
+    pd.prepare()
+    lib = _native.lib()
+    call = lambda: _native.check(lib.llmyb_decode_persistent(
+        ctypes.byref(pd.params), torch.cuda.current_stream().cuda_stream), "persistent")
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        call()
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for _ in range(reps):
+            call()
+    graph.replay()
+    torch.cuda.synchronize()
+    a, b = _events()
+    a.record()
+    for _ in range(3):
+        graph.replay()
+    b.record()
+    torch.cuda.synchronize()
+    dt = a.elapsed_time(b) * 1e-3 / (3 * reps)
+    alg = decode_bytes_per_step(model, model.cfg, folded=True)
+    achieved = alg / dt / 1e9
+    return {"bound": "hbm", "achieved": achieved, "peak": p["hbm_gbs"], "unit": "GB/s",
+            "frac": achieved / p["hbm_gbs"], "traffic": PERSISTENT_TRAFFIC,
+            "kernel": "decode_persistent_kernel<3,4>: the whole batch-1 decode step (24 block "
+                      "applications + collapse + final norm + LM head) as one cooperative "
+                      "launch of one 512-thread CTA per SM, phases separated by grid barriers",
+            "algorithmic_bytes_per_launch": alg, "avg_launch_us": dt * 1e6,
+            "timing": f"CUDA events over a graph of {reps} launches x 3 replays",
             "peak_source": p["source"]}
 
 
@@ -703,7 +759,15 @@ def run_ours(args) -> None:
                      "what": "whole decode step (one CUDA graph); algorithmic bytes = weights "
                              "and state touched per token",
                      "algorithmic_bytes_per_step": touched}
-    roofline = out_router_roofline(model, p)
+    from hybrid_llm_b200 import persistent
+    if model.decode_persistent and persistent.supported(model, bsz):
+        roofline = persistent_roofline(model, dec.state, p)
+        touched = decode_bytes_per_step(model, cfg, folded=True)
+        achieved = touched / (t_ms * 1e-3 / args.steps) / 1e9
+        step_roofline.update(achieved=achieved, frac=achieved / p["hbm_gbs"],
+                             algorithmic_bytes_per_step=touched)
+    else:
+        roofline = out_router_roofline(model, p)
 
     line = {
         "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
@@ -738,10 +802,12 @@ def run_ours(args) -> None:
         dist.destroy_process_group()
 
 
-def decode_bytes_per_step(model, cfg) -> float:
+def decode_bytes_per_step(model, cfg, folded: bool = False) -> float:
     """Algorithmic HBM bytes of one decode token at B=1: every dense weight once,
     the routed experts (top-k of E per block and loop), the KV window and GDN
-    state of every block-loop, the tied LM head."""
+    state of every block-loop, the tied LM head.  folded: the persistent step's
+    CSA input projection carries the output projection in its value rows, so
+    no separate output matrix is read."""
     d = cfg.d_model
     dense = 0
     nb = lambda t: t.numel() * t.element_size()
@@ -750,7 +816,8 @@ def decode_bytes_per_step(model, cfg) -> float:
         if blk.kind == "gdn":
             dense += nb(m.w_in) + nb(m.w_out) + nb(m.conv)
         else:
-            dense += nb(m.w_in) + nb(m.w_o)  # decode uses the pre-multiplied output matrix
+            # decode uses the pre-multiplied output matrix, or (folded) none at all
+            dense += nb(m.w_in) + (0 if folded else nb(m.w_o))
         dense += nb(blk.moe.router)
     dense *= cfg.num_loops
     expert = 3 * cfg.moe_hidden * d * 2 * cfg.moe_top_k * cfg.n_blocks * cfg.num_loops

@@ -102,6 +102,9 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     # hyper-connections
     "llmyb_mhc_read": (I32, [P, I32, I32, I32, P, I64, I64, P, P, P, P, P, F32, I32, P, P, P, P]),
     "llmyb_mhc_write": (I32, [P, I32, I32, I32, P, P, I32, P, P, P, P]),
+    # persistent decode step
+    "llmyb_decode_persistent_grid": (I32, []),
+    "llmyb_decode_persistent": (I32, [P, P]),
     # CSA remote branch
     "llmyb_csa_block_means": (I32, [P, I64, I32, I32, I32, I32, P, P, P, P]),
     "llmyb_csa_remote_rows": (I32, [P, I64, P, I64, I32, I32, I32, I32, I32, I32, I32, P, I64,

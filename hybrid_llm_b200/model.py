@@ -61,6 +61,9 @@ class LoopedHybridModel:
         # small-batch decode on the fused kernels (decode_norm_gemv /
         # decode_out_router) when the shapes allow; False forces the unfused path
         self.decode_fused = True
+        # batch-1 decode as one persistent launch (persistent.py) when the model
+        # is in its served subset; False keeps the per-sub-layer kernels
+        self.decode_persistent = True
         self._counter = torch.zeros(1, dtype=torch.int32, device=self.device)
         # diagnostics: when a list, every MoE call appends its routed top-k
         # indices [N, k] (device tensors, in call order; inside a CUDA graph
@@ -167,6 +170,7 @@ class LoopedHybridModel:
         if state is None:
             state = RecurrentState(c, bsz, self.device)
         ids = input_ids.to(self.device)
+        state.folded_rings = False  # the prefill rewrites the plain CSA value rings
         reset = None if reset_mask is None else reset_mask.to(self.device, torch.bool)
         if reset is not None and bool(reset[:, 0].any()):
             state.reset_rows(reset[:, 0])
@@ -354,6 +358,28 @@ class LoopedHybridModel:
         self._check_ep()
         return logits
 
+    def _persistent_for(self, state: RecurrentState):
+        from .persistent import PersistentDecode
+        pd = getattr(state, "_persistent", None)
+        if pd is None or pd.model is not self:
+            pd = PersistentDecode(self, state)
+            state._persistent = pd
+        return pd
+
+    def prepare_decode(self, state: RecurrentState) -> None:
+        """Work the decode path needs once per state and must not capture in a
+        CUDA graph (the persistent step folds the CSA value rings a prefill left)."""
+        from . import persistent
+        if self.decode_persistent and persistent.supported(self, state.batch):
+            self._persistent_for(state).prepare()
+
+    def _decode_persist(self, ids: torch.Tensor, state: RecurrentState) -> torch.Tensor:
+        pd = self._persistent_for(state)
+        logits = pd.step(ids)
+        if self.route_log is not None:
+            self.route_log.extend(pd.route_idx[r:r + 1] for r in range(pd.route_idx.shape[0]))
+        return logits
+
     def _decode_step(self, input_ids: torch.Tensor, state: RecurrentState,
                      num_loops: int | None = None) -> torch.Tensor:
         """One token per row (LoopedHybridMoEForCausalLM.decode_step, model/model.py:787-915,
@@ -372,6 +398,14 @@ class LoopedHybridModel:
         bsz = ids.shape[0]
         loops = c.num_loops if num_loops is None else int(num_loops)
         d = c.d_model
+        if self.decode_persistent and loops == c.num_loops:
+            from . import persistent
+            if persistent.supported(self, bsz):
+                return self._decode_persist(ids, state)
+        if getattr(state, "folded_rings", False):
+            raise RuntimeError("this state is advanced by the persistent decode step (its CSA "
+                               "value rings are folded); continue with decode_persistent=True "
+                               "or start again with a prefill")
         if c.mhc_streams:
             return self._decode_mhc(ids, state, loops)
         csa_in = 2 * d if c.csa_compression else d  # input width of the CSA output projection
@@ -614,8 +648,10 @@ class GreedyDecoder:
         torch.cuda.current_stream().wait_stream(s)
         torch.cuda.synchronize()
         self.state.load_state_dict(saved)
+        self.model.prepare_decode(self.state)
         self.tokens.copy_(tok0)
         self.seen.zero_()
+        torch.cuda.synchronize()
         self.graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(self.graph):
             self._body()

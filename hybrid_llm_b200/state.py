@@ -21,6 +21,10 @@ keys (model/model.py:168-171) —
     ceil(max_len / ratio) summaries.  The reference also appends an
     invisible entry for every decode token that completes no block; no query
     can see those, so they are not kept.
+  * ``local_vo[key]`` [B, W, D] bf16: the CSA value ring folded with the
+    block's output projection (W_o v), kept by the batch-1 persistent decode
+    step (persistent.py) once ``folded_rings`` is set; the plain ``local_v``
+    then falls behind until the next prefill.
   * ``positions`` [B] int32, position of the next token of each row.
 All buffers are allocated once for a batch size so that a captured decode
 graph can update them in place.
@@ -92,6 +96,8 @@ class RecurrentState:
                                                    device=self.device)
                 self.remote_pending[key] = torch.zeros(batch, dtype=torch.int32,
                                                        device=self.device)
+        self.local_vo: dict[str, torch.Tensor] = {}
+        self.folded_rings = False
         self.positions = torch.zeros(batch, dtype=torch.int32, device=self.device)
 
     def _tables(self):
@@ -99,7 +105,8 @@ class RecurrentState:
                 ("local_k", self.local_k), ("local_v", self.local_v),
                 ("router_latents", self.router_latents), ("remote_k", self.remote_k),
                 ("remote_v", self.remote_v), ("remote_count", self.remote_count),
-                ("remote_sum", self.remote_sum), ("remote_pending", self.remote_pending))
+                ("remote_sum", self.remote_sum), ("remote_pending", self.remote_pending),
+                ("local_vo", self.local_vo))
 
     def fill_synthetic(self, position: int, seed: int = 0) -> None:
         """Stand-in for a prefilled context of `position` tokens (benchmarks
@@ -136,14 +143,20 @@ class RecurrentState:
         return sum(t.numel() * t.element_size() for t in tensors)
 
     def state_dict(self) -> dict[str, torch.Tensor]:
-        out: dict[str, torch.Tensor] = {"positions": self.positions.clone()}
+        out: dict[str, torch.Tensor] = {"positions": self.positions.clone(),
+                                        "folded_rings": torch.tensor(self.folded_rings)}
         for name, table in self._tables():
             for key, t in table.items():
                 out[f"{name}.{key}"] = t.clone()
         return out
 
     def load_state_dict(self, sd: dict[str, torch.Tensor]) -> None:
+        """Tables missing from `sd` (the folded rings of a state saved before
+        the persistent step created them) keep their contents."""
         self.positions.copy_(sd["positions"])
+        self.folded_rings = bool(sd.get("folded_rings", torch.tensor(False)))
         for name, table in self._tables():
             for key, t in table.items():
+                if name == "local_vo" and f"{name}.{key}" not in sd:
+                    continue
                 t.copy_(sd[f"{name}.{key}"])

@@ -627,6 +627,87 @@ int32_t llmyb_csa_remote_step(const void* x, int64_t ldx, const void* q, int64_t
                               int32_t* pend_cnt, int32_t* sel_j, float* sel_w, void* out,
                               int64_t ldo, int32_t* dev_status, void* stream);
 
+/* ------------------------------------------------- persistent decode step
+ * The whole batch-1 decode step of the looped stack (model/model.py:787-915
+ * with PhysicalBlock.forward_step :266-376, as in sample_standalone.py's
+ * decode, and the head :913-915) as ONE cooperative launch: one 512-thread
+ * CTA per SM walks every block of every loop in phases separated by bounded
+ * grid barriers (input projection; CSA attention or the GDN step; the GDN
+ * output projection; router + expert gate/up; expert down), then the collapse,
+ * final norm and LM head.  Each phase loads its weight rows before waiting on
+ * the barrier.  The CSA output projection is folded into the cached values:
+ * ring_v holds W_o W_v x (W_o = out . local_out), and w_in's value rows are
+ * W_o W_v, so the attention output is the block's output.  Served: one plain
+ * residual stream, CSA without the remote branch (head_dim 64), GDN with key =
+ * value dim 64, routed experts only, D <= 1024 (D % 8 == 0), F <= 2048
+ * (F % 128 == 0), E <= 64, top_k <= 8, window <= 1024, CSA heads <= 16.
+ * Before every launch the caller zeroes *bar (4 bytes).  A barrier that does
+ * not complete within one second records LLMYB_ETIMEOUT in *status and every
+ * CTA returns. */
+typedef struct {
+  int32_t kind;                 /* 0: CSA (local branch), 1: GDN */
+  int32_t rows;                 /* rows of w_in */
+  const float* mixer_norm;      /* [D] */
+  const float* ffn_norm;        /* [D] */
+  const float* router_fold;     /* [E, D] = router * ffn_norm * router_norm */
+  const void* w_in;             /* CSA [2*H*Dh + D, D]: q | k | W_o W_v;  GDN [P, D] */
+  const float* beta_bias;       /* GDN [H] */
+  const float* decay_logit;     /* GDN [H] */
+  const void* w_out;            /* GDN [D, H*V] */
+  const float* conv;            /* GDN [D, 4] */
+  const void* w13;              /* [E, 2F, D] interleaved gate/up */
+  const void* w2;               /* [E, D, F] */
+} llmyb_pblock;
+
+typedef struct {
+  void* ring_k;                 /* CSA [W, H*Dh] bf16 */
+  void* ring_v;                 /* CSA [W, D] bf16, folded values W_o W_v x */
+  float* gdn_state;             /* GDN [H, 64, 64] fp32 */
+  void* conv_hist;              /* GDN [3, D] bf16 */
+} llmyb_player;
+
+typedef struct {
+  int32_t d_model, n_blocks, n_loops, vocab;
+  int32_t csa_heads, csa_head_dim, window;
+  int32_t gdn_heads, gdn_dim;
+  int32_t n_experts, top_k, ffn;
+  float eps;
+  int32_t grid;                 /* CTAs (one per SM); sizes stats / partials */
+  const llmyb_pblock* blocks;   /* device array [n_blocks] */
+  const llmyb_player* layers;   /* device array [n_loops * n_blocks] */
+  const void* embed;            /* [vocab, D] bf16 (tied LM head) */
+  const float* stream_seed;     /* [D] */
+  const void* collapse;         /* [D, D] bf16 */
+  const float* final_norm;      /* [D] */
+  const int64_t* token;         /* [1] */
+  int32_t* positions;           /* [1], incremented by the step */
+  float* x;                     /* scratch [2, D] */
+  void* proj;                   /* scratch [max rows] bf16 */
+  void* normed;                 /* scratch [D] bf16 */
+  float* scores;                /* scratch [csa_heads, window] */
+  float* stats;                 /* scratch [grid, csa_heads, 2] */
+  void* mix;                    /* scratch [max(D, gdn_heads*gdn_dim)] bf16 */
+  float* partials;              /* scratch [grid, 2 + E] */
+  void* hbuf;                   /* scratch [top_k, F] bf16 */
+  void* ybuf;                   /* scratch [top_k, D] bf16 */
+  void* collapsed;              /* scratch [D] bf16 */
+  int32_t* route_idx;           /* out [n_loops * n_blocks, top_k] */
+  float* route_prob;            /* out [n_loops * n_blocks, top_k] */
+  float* logits;                /* out [vocab] fp32 (bf16-rounded LM head output) */
+  uint32_t* bar;                /* grid barrier counter, zeroed before each launch */
+  int32_t* status;              /* device status word */
+  uint64_t* trace;              /* nullable: [2, 2, 512] %globaltimer stamps of CTA 0 and the
+                                   last CTA, at every barrier wait's end and arrive */
+} llmyb_pdecode;
+
+/* CTAs per grid that llmyb_decode_persistent will use on the current device
+ * (one per SM, if a 512-thread CTA with its shared memory fits), or a
+ * negative status. */
+int32_t llmyb_decode_persistent_grid(void);
+
+/* One decode step; `p` is a host struct (copied into the launch). */
+int32_t llmyb_decode_persistent(const llmyb_pdecode* p, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
