@@ -66,6 +66,20 @@ __device__ __forceinline__ void stcg_bf(bf16* p, float v) {
   const bf16 b = f2bf(v);
   __stcg(reinterpret_cast<unsigned short*>(p), *reinterpret_cast<const unsigned short*>(&b));
 }
+// 16-byte asynchronous copy global -> shared (L2 only): a prefetch issued
+// before a barrier wait that holds no registers while it is in flight
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+// wait until at most N of this thread's most recent commit groups are pending
+template <int N>
+__device__ __forceinline__ void cp_async_wait_group() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 __device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
   uint32_t v;
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -106,6 +120,18 @@ __device__ __forceinline__ float row_dot(const uint4 (&w)[NC], const bf16* s_vec
     const int c = lane + 32 * i;
     if (c < n8) s += dot8(w[i], reinterpret_cast<const uint4*>(s_vec)[c]);
   }
+  return warp_sum(s);
+}
+
+// A row of n8 16-byte chunks copied into shared memory by the warp (lane c,
+// c + 32, ...), and its dot with a bf16 vector in shared memory.
+__device__ __forceinline__ void warp_copy_row(bf16* srow, const bf16* grow, int n8, int lane) {
+  for (int c = lane; c < n8; c += 32) cp_async16(srow + c * 8, grow + c * 8);
+}
+__device__ __forceinline__ float srow_dot(const bf16* srow, const bf16* s_vec, int n8, int lane) {
+  float s = 0.f;
+  for (int c = lane; c < n8; c += 32)
+    s += dot8(reinterpret_cast<const uint4*>(srow)[c], reinterpret_cast<const uint4*>(s_vec)[c]);
   return warp_sum(s);
 }
 
@@ -192,6 +218,10 @@ struct Smem {
   int idx[kMaxK];
   float scal[4];
   float ptmp[128 * (2 + kMaxE)];     // router partial sums of all producing CTAs
+  uint4 vring[kMaxW];                // CSA: this CTA's 8 columns of every cached value;
+                                     // GDN: the unit's state slice [64][32] fp32
+  bf16 wbuf[kPW][2 * kMaxD];         // per warp: input-projection / expert-down / collapse rows
+  bf16 kbuf[kPW][kMaxD];             // per warp: CSA key row / GDN output-projection row
 };
 
 // DC / FC: 16-byte chunks per lane of a D-long / F-long weight row (D <= 256 DC,
@@ -248,10 +278,41 @@ __global__ void __launch_bounds__(kPT, 1) decode_persistent_kernel(const llmyb_p
       float* xdst = p.x + (xs ^ 1) * D;
       // ================================================================ A
       {
-        uint4 wa[2][DC];
+        // asynchronous copies into shared memory before the wait, in three
+        // commit groups: this phase's rows; the next phase's rows (CSA key row,
+        // GDN output-projection row); the CSA value chunks / the GDN state slice
         const int r0 = gw, r1 = gw + NW;
-        if (r0 < B.rows) load_row<DC>(w_in + static_cast<int64_t>(r0) * D, n8, lane, wa[0]);
-        if (r1 < B.rows) load_row<DC>(w_in + static_cast<int64_t>(r1) * D, n8, lane, wa[1]);
+        bf16* wb = sm.wbuf[warp];
+        if (r0 < B.rows) warp_copy_row(wb, w_in + static_cast<int64_t>(r0) * D, n8, lane);
+        if (r1 < B.rows) warp_copy_row(wb + kMaxD, w_in + static_cast<int64_t>(r1) * D, n8, lane);
+        cp_async_commit();
+        if (B.kind == 0) {
+          const int key = cta * kPW + warp;
+          if (cta < nk1 && key < nk && key != slot)
+            warp_copy_row(sm.kbuf[warp], static_cast<const bf16*>(L.ring_k) + static_cast<int64_t>(key) * HDc,
+                          HDc >> 3, lane);
+          cp_async_commit();
+          if (cta < ncs)
+            for (int jj = tid; jj < nk; jj += kPT)
+              if (jj != slot)
+                cp_async16(&sm.vring[jj], static_cast<const bf16*>(L.ring_v) +
+                                              static_cast<int64_t>(jj) * D + cta * 8);
+          cp_async_commit();
+        } else {
+          const int HVg = Hg * Kg;
+          if (gw < D)
+            warp_copy_row(sm.kbuf[warp], static_cast<const bf16*>(B.w_out) + static_cast<int64_t>(gw) * HVg,
+                          HVg >> 3, lane);
+          cp_async_commit();
+          if (cta < gunits) {  // state rows 0..63, columns v0..v0+31 of the unit (8 chunks a row)
+            const int uh = cta / (Kg / 32), uv0 = (cta % (Kg / 32)) * 32;
+            const float* S0 = L.gdn_state + (static_cast<int64_t>(uh) * Kg) * Kg + uv0;
+            for (int i = tid; i < Kg * 8; i += kPT)
+              cp_async16(reinterpret_cast<float*>(sm.vring) + (i >> 3) * 32 + (i & 7) * 4,
+                         S0 + static_cast<int64_t>(i >> 3) * Kg + (i & 7) * 4);
+          }
+          cp_async_commit();
+        }
         float4 nwa = make_float4(0.f, 0.f, 0.f, 0.f), nwb = nwa;
         if (tid < n8) {
           nwa = __ldg(reinterpret_cast<const float4*>(B.mixer_norm) + 2 * tid);
@@ -306,13 +367,14 @@ __global__ void __launch_bounds__(kPT, 1) decode_persistent_kernel(const llmyb_p
             stcg16(normed_g + tid * 8, o);
           }
         }
+        cp_async_wait_group<2>();  // this phase's rows (later groups may still fly)
         __syncthreads();
         if (r0 < B.rows) {
-          const float acc = row_dot<DC>(wa[0], s_vec, n8, lane);
+          const float acc = srow_dot(wb, s_vec, n8, lane);
           if (lane == 0) stcg_bf(proj + r0, acc);
         }
         if (r1 < B.rows) {
-          const float acc = row_dot<DC>(wa[1], s_vec, n8, lane);
+          const float acc = srow_dot(wb + kMaxD, s_vec, n8, lane);
           if (lane == 0) stcg_bf(proj + r1, acc);
         }
         gb.arrive();
@@ -328,24 +390,21 @@ __global__ void __launch_bounds__(kPT, 1) decode_persistent_kernel(const llmyb_p
         const int key = cta * kPW + warp;
         const bool mine = cta < nk1 && key < nk;
         const int hdc8 = HDc >> 3;
-        uint4 kr[DC];
-        if (mine && key != slot)
-          load_row<DC>(ring_k + static_cast<int64_t>(key) * HDc, hdc8, lane, kr);
+        uint4* krow = reinterpret_cast<uint4*>(sm.kbuf[warp]);  // copied during phase A
         if (!gb.wait()) return;
         if (cta < nk1) {
           for (int i = tid; i < HDc; i += kPT) sm.q[i] = ldcg_bf(proj + i) * qscale;
+          cp_async_wait_group<1>();
           __syncthreads();
           if (mine) {
             if (key == slot) {
               // the new token: key from the projection, stored with its value
-#pragma unroll
-              for (int i = 0; i < DC; ++i) {
-                const int c = lane + 32 * i;
-                if (c < hdc8) {
-                  kr[i] = ldcg16(proj + HDc + c * 8);
-                  stcg16(ring_k + static_cast<int64_t>(slot) * HDc + c * 8, kr[i]);
-                }
+              for (int c = lane; c < hdc8; c += 32) {
+                const uint4 kv = ldcg16(proj + HDc + c * 8);
+                krow[c] = kv;
+                stcg16(ring_k + static_cast<int64_t>(slot) * HDc + c * 8, kv);
               }
+              __syncwarp();
               for (int c = lane; c < n8; c += 32)
                 stcg16(ring_v + static_cast<int64_t>(slot) * D + c * 8,
                        ldcg16(proj + 2 * HDc + c * 8));
@@ -357,7 +416,8 @@ __global__ void __launch_bounds__(kPT, 1) decode_persistent_kernel(const llmyb_p
               const int c = lane + 32 * i;
               float s = 0.f;
               if (c < hdc8) {
-                const uint32_t kw[4] = {kr[i].x, kr[i].y, kr[i].z, kr[i].w};
+                const uint4 k4 = krow[c];
+                const uint32_t kw[4] = {k4.x, k4.y, k4.z, k4.w};
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
                   const float2 f = unpack_bf16x2(kw[e]);
@@ -390,15 +450,10 @@ __global__ void __launch_bounds__(kPT, 1) decode_persistent_kernel(const llmyb_p
         const int col0 = cta * 8;
         constexpr int kKpg = kMaxW / 64;
         const int grp = tid >> 3, cc = tid & 7;
-        bf16 vk[kKpg];
         float fcol = 0.f, ffc = 0.f;
         if (cta < ncs) {
-#pragma unroll
-          for (int i = 0; i < kKpg; ++i) {
-            const int jj = grp + 64 * i;
-            vk[i] = (jj < nk && jj != slot) ? ring_v[static_cast<int64_t>(jj) * D + col0 + cc]
-                                           : f2bf(0.f);
-          }
+          // (the cached values' chunks of these columns were copied into
+          // sm.vring during phase A)
           // router row t / 8 at column t % 8; threads t < 8: the FFN norm weight
           if (tid < 8 * E) fcol = __ldg(B.router_fold + static_cast<int64_t>(tid >> 3) * D + col0 + (tid & 7));
           if (tid < 8) ffc = __ldg(B.ffn_norm + col0 + tid);
@@ -419,7 +474,12 @@ __global__ void __launch_bounds__(kPT, 1) decode_persistent_kernel(const llmyb_p
             }
           }
           const float xold = tid < 8 ? __ldcg(xdst + col0 + tid) : 0.f;
-          if (grp == slot % 64 && slot < nk) vk[slot / 64] = f2bf(ldcg_bf(ring_v + static_cast<int64_t>(slot) * D + col0 + cc));
+          if (tid == 0 && slot < nk) sm.vring[slot] = ldcg16(ring_v + static_cast<int64_t>(slot) * D + col0);
+          // this thread's key's scores, in the same round of loads
+          float sck[kMaxHeads];
+#pragma unroll
+          for (int h = 0; h < kMaxHeads; ++h)
+            sck[h] = (h < Hc && tid < nk) ? __ldcg(p.scores + h * W + tid) : 0.f;
           if (warp < Hc) {
             const float m = warp_max(fmaxf(sm0, sm1));
             float l = 0.f;
@@ -435,7 +495,15 @@ __global__ void __launch_bounds__(kPT, 1) decode_persistent_kernel(const llmyb_p
           gb.point(li * p.n_blocks + j, 1);
           // head-averaged probability of every key, once
           float* pbar = sm.ptmp;  // [nk]
-          for (int jj = tid; jj < nk; jj += kPT) {
+          cp_async_wait_group<0>();
+          if (tid < nk) {
+            float pb = 0.f;
+#pragma unroll
+            for (int h = 0; h < kMaxHeads; ++h)
+              if (h < Hc) pb += exp2f(sck[h] - sm.hM[h]) * sm.hInvL[h];
+            pbar[tid] = pb;
+          }
+          for (int jj = tid + kPT; jj < nk; jj += kPT) {  // windows past 512 keys
             float pb = 0.f;
             for (int h = 0; h < Hc; ++h)
               pb += exp2f(__ldcg(p.scores + h * W + jj) - sm.hM[h]) * sm.hInvL[h];
@@ -443,10 +511,11 @@ __global__ void __launch_bounds__(kPT, 1) decode_persistent_kernel(const llmyb_p
           }
           __syncthreads();
           float acc = 0.f;
+          const bf16* vr = reinterpret_cast<const bf16*>(sm.vring);
 #pragma unroll
           for (int i = 0; i < kKpg; ++i) {
             const int jj = grp + 64 * i;
-            if (jj < nk) acc += pbar[jj] * bf2f(vk[i]);
+            if (jj < nk) acc += pbar[jj] * bf2f(vr[jj * 8 + cc]);
           }
           // the 4 key groups of a warp share the column: lanes c, c+8, c+16, c+24
           acc += __shfl_xor_sync(0xffffffffu, acc, 8);
@@ -497,10 +566,6 @@ __global__ void __launch_bounds__(kPT, 1) decode_persistent_kernel(const llmyb_p
         constexpr int RPW = 16;  // 4 warps x 16 state rows = key dim 64
         float sreg[RPW];
         float* S = state + (static_cast<int64_t>(unit_h) * Kg) * Kg + v0 + lane;
-        if (cta < gunits && warp < 4)
-#pragma unroll
-          for (int r = 0; r < RPW; ++r)
-            sreg[r] = __ldcg(S + static_cast<int64_t>(warp * RPW + r) * Kg);
         const float a_dec = cta < gunits ? sigmoidf_(__ldg(B.decay_logit + unit_h)) : 0.f;
         const float b_bias = cta < gunits ? __ldg(B.beta_bias + unit_h) : 0.f;
         if (!gb.wait()) return;
@@ -516,7 +581,13 @@ __global__ void __launch_bounds__(kPT, 1) decode_persistent_kernel(const llmyb_p
             sm.q[tid] = ldcg_bf(proj + unit_h * Kg + tid);
             sm.kk[tid] = ldcg_bf(proj + HKg + unit_h * Kg + tid);
           }
+          cp_async_wait_group<0>();  // the state slice (copied during phase A)
           __syncthreads();
+          if (warp < 4) {
+            const float* gs = reinterpret_cast<const float*>(sm.vring);
+#pragma unroll
+            for (int r = 0; r < RPW; ++r) sreg[r] = gs[(warp * RPW + r) * 32 + lane];
+          }
           if (warp == 0) {
             // q, k <- x * rsqrt(max(sum x^2, 1e-12)) (gated_deltanet.py:128-129)
             float sq = 0.f, sk = 0.f;
@@ -577,14 +648,12 @@ __global__ void __launch_bounds__(kPT, 1) decode_persistent_kernel(const llmyb_p
           bf16* hist = static_cast<bf16*>(L.conv_hist);
           const int n = gw;  // output column of this warp (D <= warps of the grid)
           const int hv8 = HVg >> 3;
-          uint4 wo[DC];
           float c4[4] = {0.f, 0.f, 0.f, 0.f}, h3[3] = {0.f, 0.f, 0.f}, fw = 0.f;
           // router weights of this column for the values v = lane + 32 u (v >= 2);
           // the residual and normalised input of the column (written by phase A)
           float fv[3] = {0.f, 0.f, 0.f};
           float xpre = 0.f, npre = 0.f;
           if (n < D) {
-            load_row<DC>(w_out + static_cast<int64_t>(n) * HVg, hv8, lane, wo);
 #pragma unroll
             for (int q = 0; q < 4; ++q) c4[q] = __ldg(B.conv + n * 4 + q);
 #pragma unroll
@@ -602,10 +671,11 @@ __global__ void __launch_bounds__(kPT, 1) decode_persistent_kernel(const llmyb_p
           if (!gb.wait()) return;
           for (int c = tid; c < hv8; c += kPT)
             reinterpret_cast<uint4*>(s_vec)[c] = ldcg16(mix + c * 8);
+          cp_async_wait_group<0>();  // this warp's output-projection row (phase A)
           __syncthreads();
           float x = 0.f;
           if (n < D) {
-            const float y = bf2f(f2bf(row_dot<DC>(wo, s_vec, hv8, lane)));
+            const float y = bf2f(f2bf(srow_dot(sm.kbuf[warp], s_vec, hv8, lane)));
             const float xb = npre;
             // conv gate of the decode step over [history, this input]
             const float cacc = c4[0] * h3[0] + c4[1] * h3[1] + c4[2] * h3[2] + c4[3] * xb;
@@ -645,34 +715,27 @@ __global__ void __launch_bounds__(kPT, 1) decode_persistent_kernel(const llmyb_p
           fwb = __ldg(reinterpret_cast<const float4*>(B.ffn_norm) + 2 * tid + 1);
         }
         if (!gb.wait()) return;
-        // the router partial sums of all producing CTAs and the residual row,
-        // loaded together (the row only after the partials are in flight)
-        const int ntot = n_part * NV;
-        for (int i0 = tid; i0 < ntot; i0 += 4 * kPT) {
-          float t4[4];
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const int i = i0 + u * kPT;
-            t4[u] = i < ntot ? __ldcg(p.partials + i) : 0.f;
-          }
-#pragma unroll
-          for (int u = 0; u < 4; ++u)
-            if (i0 + u * kPT < ntot) sm.ptmp[i0 + u * kPT] = t4[u];
-        }
+        // the router partial sums of all producing CTAs and the residual row in
+        // one round of loads: thread t < 8 NV sums slots t % 8, t % 8 + 8, ...
+        // of value t / 8 in registers, then a fixed xor tree (the same order in
+        // every CTA, so all of them route identically)
+        constexpr int kSlots = 128 / 8;
         float4 xa = make_float4(0.f, 0.f, 0.f, 0.f), xb4 = xa;
         if (tid < n8) {
           xa = __ldcg(reinterpret_cast<const float4*>(xdst) + 2 * tid);
           xb4 = __ldcg(reinterpret_cast<const float4*>(xdst) + 2 * tid + 1);
         }
-        __syncthreads();
-        gb.point(li * p.n_blocks + j, 4);
-        // value v = t / 8 summed by 8 threads over slots in a fixed order, then
-        // a fixed xor tree (the same in every CTA, so all route identically)
         if (warp < (8 * NV + 31) / 32) {  // warp-uniform: the shuffles see full warps
           const int v = tid >> 3, part = tid & 7;
+          float t16[kSlots];
+#pragma unroll
+          for (int u = 0; u < kSlots; ++u) {
+            const int s_ = part + 8 * u;
+            t16[u] = (tid < 8 * NV && s_ < n_part) ? __ldcg(p.partials + s_ * NV + v) : 0.f;
+          }
           float a = 0.f;
-          if (tid < 8 * NV)
-            for (int s = part; s < n_part; s += 8) a += sm.ptmp[s * NV + v];
+#pragma unroll
+          for (int u = 0; u < kSlots; ++u) a += t16[u];
           a += __shfl_xor_sync(0xffffffffu, a, 4);
           a += __shfl_xor_sync(0xffffffffu, a, 2);
           a += __shfl_xor_sync(0xffffffffu, a, 1);
@@ -681,10 +744,14 @@ __global__ void __launch_bounds__(kPT, 1) decode_persistent_kernel(const llmyb_p
           }
         }
         __syncthreads();
+        gb.point(li * p.n_blocks + j, 4);
         const float inv1 = rsqrtf(sm.scal[0] / static_cast<float>(D) + eps);
         const float inv2 = rsqrtf(inv1 * inv1 * sm.scal[1] / static_cast<float>(D) + eps);
-        if (warp == 0) {
-          // top-k by value (desc), index (asc); softmax of the k values
+        // every warp takes the top-k itself (value desc, index asc; softmax of
+        // the k values), so it can fetch its expert rows without another barrier
+        int my_e = 0;
+        float my_p = 0.f;
+        {
           float v0 = lane < E ? sm.logit[lane] * inv1 * inv2 : -INFINITY;
           float v1 = lane + 32 < E ? sm.logit[lane + 32] * inv1 * inv2 : -INFINITY;
           float top = 0.f, mine = 0.f;
@@ -706,15 +773,27 @@ __global__ void __launch_bounds__(kPT, 1) decode_persistent_kernel(const llmyb_p
           }
           const float ex = lane < K ? expf(mine - top) : 0.f;
           const float den = warp_sum(ex);
-          mine_i = min(max(mine_i, 0), E - 1);  // a NaN row must not pick a missing expert
-          if (lane < K) {
-            sm.idx[lane] = mine_i;
-            sm.prob[lane] = ex / den;
+          my_e = min(max(mine_i, 0), E - 1);  // a NaN row must not pick a missing expert
+          my_p = ex / den;
+          if (warp == 0 && lane < K) {
+            sm.idx[lane] = my_e;
+            sm.prob[lane] = my_p;
             if (cta == 0) {
-              p.route_idx[(li * p.n_blocks + j) * K + lane] = mine_i;
-              p.route_prob[(li * p.n_blocks + j) * K + lane] = ex / den;
+              p.route_idx[(li * p.n_blocks + j) * K + lane] = my_e;
+              p.route_prob[(li * p.n_blocks + j) * K + lane] = my_p;
             }
           }
+        }
+        // this warp's first feature: fetch its gate / up rows now
+        const bf16* w13 = static_cast<const bf16*>(B.w13);
+        uint4 wg[DC], wu[DC];
+        int g_first = gw;
+        if (g_first < K * F) {
+          const int s0 = g_first / F, f0 = g_first - s0 * F;
+          const int e0 = __shfl_sync(0xffffffffu, my_e, s0);
+          const int64_t grow = static_cast<int64_t>(e0) * 2 * F + (f0 / 128) * 256 + (f0 % 128);
+          load_row<DC>(w13 + grow * D, n8, lane, wg);
+          load_row<DC>(w13 + (grow + 128) * D, n8, lane, wu);
         }
         // the experts' input m = RMSNorm(x) * ffn_norm (bf16)
         if (tid < n8) {
@@ -729,13 +808,14 @@ __global__ void __launch_bounds__(kPT, 1) decode_persistent_kernel(const llmyb_p
         }
         __syncthreads();
         gb.point(li * p.n_blocks + j, 5);
-        const bf16* w13 = static_cast<const bf16*>(B.w13);
-        for (int g = gw; g < K * F; g += NW) {
+        for (int g = g_first; g < K * F; g += NW) {
           const int s = g / F, f = g - s * F;
-          const int64_t grow = static_cast<int64_t>(sm.idx[s]) * 2 * F + (f / 128) * 256 + (f % 128);
-          uint4 wg[DC], wu[DC];
-          load_row<DC>(w13 + grow * D, n8, lane, wg);
-          load_row<DC>(w13 + (grow + 128) * D, n8, lane, wu);
+          if (g != g_first) {
+            const int e = __shfl_sync(0xffffffffu, my_e, s);
+            const int64_t grow = static_cast<int64_t>(e) * 2 * F + (f / 128) * 256 + (f % 128);
+            load_row<DC>(w13 + grow * D, n8, lane, wg);
+            load_row<DC>(w13 + (grow + 128) * D, n8, lane, wu);
+          }
           const float ga = row_dot<DC>(wg, s_vec, n8, lane);
           const float ua = row_dot<DC>(wu, s_vec, n8, lane);
           if (lane == 0) stcg_bf(hbuf + static_cast<int64_t>(s) * F + f, silu_mul(ga, ua));
@@ -749,19 +829,26 @@ __global__ void __launch_bounds__(kPT, 1) decode_persistent_kernel(const llmyb_p
         const int f8 = F >> 3;
         uint4 wd[FC];
         const int r0 = gw;
+        bf16* wb = sm.wbuf[warp];
         if (r0 < K * D) {
           const int s = r0 / D, n = r0 - s * D;
-          load_row<FC>(w2 + (static_cast<int64_t>(sm.idx[s]) * D + n) * F, f8, lane, wd);
+          warp_copy_row(wb, w2 + (static_cast<int64_t>(sm.idx[s]) * D + n) * F, f8, lane);
         }
+        cp_async_commit();
         if (!gb.wait()) return;
         for (int c = tid; c < K * f8; c += kPT)
           reinterpret_cast<uint4*>(s_vec)[c] = ldcg16(hbuf + c * 8);
+        cp_async_wait_group<0>();
         __syncthreads();
         for (int r = r0; r < K * D; r += NW) {
           const int s = r / D, n = r - s * D;
-          if (r != r0)
+          float acc;
+          if (r == r0) {
+            acc = srow_dot(wb, s_vec + s * F, f8, lane);
+          } else {
             load_row<FC>(w2 + (static_cast<int64_t>(sm.idx[s]) * D + n) * F, f8, lane, wd);
-          const float acc = row_dot<FC>(wd, s_vec + s * F, f8, lane);
+            acc = row_dot<FC>(wd, s_vec + s * F, f8, lane);
+          }
           if (lane == 0) stcg_bf(ybuf + static_cast<int64_t>(s) * D + n, acc * sm.prob[s]);
         }
         gb.arrive();
@@ -774,8 +861,8 @@ __global__ void __launch_bounds__(kPT, 1) decode_persistent_kernel(const llmyb_p
     const float* xcur = p.x + xs * D;
     const bf16* collapse = static_cast<const bf16*>(p.collapse);
     bf16* collapsed = static_cast<bf16*>(p.collapsed);
-    uint4 wc[DC];
-    if (gw < D) load_row<DC>(collapse + static_cast<int64_t>(gw) * D, n8, lane, wc);
+    if (gw < D) warp_copy_row(sm.wbuf[warp], collapse + static_cast<int64_t>(gw) * D, n8, lane);
+    cp_async_commit();
     if (!gb.wait()) return;
     if (tid < n8) {
       const float4 a = __ldcg(reinterpret_cast<const float4*>(xcur) + 2 * tid);
@@ -799,9 +886,10 @@ __global__ void __launch_bounds__(kPT, 1) decode_persistent_kernel(const llmyb_p
       o.w = pack_bf16x2(v[6], v[7]);
       reinterpret_cast<uint4*>(s_vec)[tid] = o;
     }
+    cp_async_wait_group<0>();
     __syncthreads();
     if (gw < D) {
-      const float acc = row_dot<DC>(wc, s_vec, n8, lane);
+      const float acc = srow_dot(sm.wbuf[warp], s_vec, n8, lane);
       if (lane == 0) stcg_bf(collapsed + gw, acc);
     }
     gb.arrive();
