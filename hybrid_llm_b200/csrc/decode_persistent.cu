@@ -923,16 +923,92 @@ __global__ void __launch_bounds__(kPT, 1) decode_persistent_kernel(const llmyb_p
       reinterpret_cast<uint4*>(s_vec)[tid] = o;
     }
     __syncthreads();
+    // greedy sampling state of this warp: first maximal logit, and the running
+    // max / exp-sum of its logits (online log-sum-exp)
+    float best = -INFINITY, run_m = -INFINITY, run_s = 0.f;
+    int best_i = 0;
+    auto track = [&](float l, int vi) {
+      if (l > best) { best = l; best_i = vi; }  // rows come in increasing order
+      if (l > run_m) {
+        run_s = (run_m == -INFINITY ? 0.f : run_s * expf(run_m - l)) + 1.f;
+        run_m = l;
+      } else {
+        run_s += expf(l - run_m);
+      }
+    };
     // two rows in flight: the next row streams in while this one is reduced
     for (; v < p.vocab; v += 2 * NW) {
       const int v1 = v + NW, v2 = v + 2 * NW;
       if (v1 < p.vocab) load_row<DC>(embed + static_cast<int64_t>(v1) * D, n8, lane, we[1]);
-      const float a0 = row_dot<DC>(we[0], s_vec, n8, lane);
-      if (lane == 0) __stcg(p.logits + v, bf2f(f2bf(a0)));
+      const float a0 = bf2f(f2bf(row_dot<DC>(we[0], s_vec, n8, lane)));
+      if (lane == 0) __stcg(p.logits + v, a0);
+      track(a0, v);
       if (v2 < p.vocab) load_row<DC>(embed + static_cast<int64_t>(v2) * D, n8, lane, we[0]);
       if (v1 < p.vocab) {
-        const float a1 = row_dot<DC>(we[1], s_vec, n8, lane);
-        if (lane == 0) __stcg(p.logits + v1, bf2f(f2bf(a1)));
+        const float a1 = bf2f(f2bf(row_dot<DC>(we[1], s_vec, n8, lane)));
+        if (lane == 0) __stcg(p.logits + v1, a1);
+        track(a1, v1);
+      }
+    }
+    if (p.out_token != nullptr) {
+      // CTA: combine the warps in order; then the last CTA to finish combines
+      // the CTAs in order (the same result however the CTAs are scheduled)
+      if (lane == 0) {
+        sm.part[warp][0] = best;
+        sm.part[warp][1] = __int_as_float(best_i);
+        sm.part[warp][2] = run_m;
+        sm.part[warp][3] = run_s;
+      }
+      __syncthreads();
+      __shared__ int s_last;
+      if (tid == 0) {
+        float b = -INFINITY, m = -INFINITY, s = 0.f;
+        int bi = 0;
+        for (int w = 0; w < kPW; ++w) {
+          const float wb = sm.part[w][0], wm = sm.part[w][2], ws = sm.part[w][3];
+          const int wi = __float_as_int(sm.part[w][1]);
+          if (wb > b || (wb == b && wi < bi)) { b = wb; bi = wi; }
+          const float nm = fmaxf(m, wm);
+          s = (m == -INFINITY ? 0.f : s * expf(m - nm)) + (wm == -INFINITY ? 0.f : ws * expf(wm - nm));
+          m = nm;
+        }
+        __stcg(p.head_part + cta * 4, b);
+        __stcg(p.head_part + cta * 4 + 1, __int_as_float(bi));
+        __stcg(p.head_part + cta * 4 + 2, m);
+        __stcg(p.head_part + cta * 4 + 3, s);
+        __threadfence();
+        s_last = atomicAdd(p.bar + 1, 1u) == static_cast<uint32_t>(G) - 1;
+      }
+      __syncthreads();
+      if (s_last && warp == 0) {
+        __threadfence();
+        float b = -INFINITY, m = -INFINITY, s = 0.f;
+        int bi = 0;
+        for (int c = lane; c < G; c += 32) {  // lane-ordered, then a fixed xor tree
+          const float cb = __ldcg(p.head_part + c * 4), cm = __ldcg(p.head_part + c * 4 + 2);
+          const float cs = __ldcg(p.head_part + c * 4 + 3);
+          const int ci = __float_as_int(__ldcg(p.head_part + c * 4 + 1));
+          if (cb > b || (cb == b && ci < bi)) { b = cb; bi = ci; }
+          const float nm = fmaxf(m, cm);
+          s = (m == -INFINITY ? 0.f : s * expf(m - nm)) + (cm == -INFINITY ? 0.f : cs * expf(cm - nm));
+          m = nm;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+          const float ob = __shfl_xor_sync(0xffffffffu, b, o);
+          const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+          const float om = __shfl_xor_sync(0xffffffffu, m, o);
+          const float os = __shfl_xor_sync(0xffffffffu, s, o);
+          if (ob > b || (ob == b && oi < bi)) { b = ob; bi = oi; }
+          const float nm = fmaxf(m, om);
+          s = (m == -INFINITY ? 0.f : s * expf(m - nm)) + (om == -INFINITY ? 0.f : os * expf(om - nm));
+          m = nm;
+        }
+        if (lane == 0) {
+          *p.out_token = bi;
+          if (p.out_logprob != nullptr) *p.out_logprob = b - (m + logf(s));  // raw log-softmax
+          if (p.seen != nullptr) atomicOr(p.seen + (bi >> 5), 1 << (bi & 31));
+        }
       }
     }
     if (cta == 0 && tid == 0) *p.positions = pos + 1;  // every CTA read it before a barrier
@@ -997,7 +1073,8 @@ LLMYB_API int32_t llmyb_decode_persistent(const llmyb_pdecode* p, void* stream) 
   int32_t st = ensure_smem(kern, kSmemBytes);
   if (st) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  cudaError_t e = cudaMemsetAsync(p->bar, 0, sizeof(uint32_t), s);
+  if (p->out_token != nullptr && !p->head_part) return LLMYB_EINVAL;
+  cudaError_t e = cudaMemsetAsync(p->bar, 0, 2 * sizeof(uint32_t), s);
   if (e != cudaSuccess) return static_cast<int32_t>(e);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(p->grid));

@@ -373,6 +373,24 @@ class LoopedHybridModel:
         if self.decode_persistent and persistent.supported(self, state.batch):
             self._persistent_for(state).prepare()
 
+    def greedy_fused(self, batch: int) -> bool:
+        """Whether a greedy decode step of this model samples inside the
+        persistent decode launch (the LM head fused with the argmax)."""
+        from . import persistent
+        return self.decode_persistent and persistent.supported(self, batch)
+
+    def decode_step_greedy(self, ids: torch.Tensor, state: RecurrentState, out_token: torch.Tensor,
+                           logprob: torch.Tensor | None = None,
+                           seen: torch.Tensor | None = None) -> torch.Tensor:
+        """decode_step followed by greedy sampling (temperature 0, no repetition
+        penalty) in one persistent launch; out_token [1] int64 receives the
+        token.  Requires greedy_fused(1).  Returns the logits [1, V] fp32."""
+        pd = self._persistent_for(state)
+        logits = pd.step(ids.reshape(-1), out_token=out_token, logprob=logprob, seen=seen)
+        if self.route_log is not None:
+            self.route_log.extend(pd.route_idx[r:r + 1] for r in range(pd.route_idx.shape[0]))
+        return logits
+
     def _decode_persist(self, ids: torch.Tensor, state: RecurrentState) -> torch.Tensor:
         pd = self._persistent_for(state)
         logits = pd.step(ids)
@@ -627,6 +645,16 @@ class GreedyDecoder:
         self.logits = None
 
     def _body(self):
+        s = self.sampling
+        if (s["temperature"] <= 1e-4 and s["repetition_penalty"] == 1.0
+                and self.model.greedy_fused(self.bsz)):
+            # greedy: the LM head and the argmax run inside the decode launch
+            if self.logprob is None:
+                self.logprob = torch.zeros(self.bsz, dtype=torch.float32, device=self.tokens.device)
+            logits = self.model.decode_step_greedy(self.tokens, self.state, self.tokens,
+                                                   self.logprob, self.seen.view(-1))
+            self.logits = logits
+            return logits
         logits = self.model.decode_step(self.tokens, self.state).float()
         tok, lp = kernels.sample(logits, seen=self.seen, uniforms=self.uniforms, update_seen=True,
                                  out=self.tokens, **self.sampling)

@@ -54,7 +54,8 @@ class PDecode(C.Structure):
                 ("mix", C.c_void_p), ("partials", C.c_void_p), ("hbuf", C.c_void_p),
                 ("ybuf", C.c_void_p), ("collapsed", C.c_void_p), ("route_idx", C.c_void_p),
                 ("route_prob", C.c_void_p), ("logits", C.c_void_p), ("bar", C.c_void_p),
-                ("status", C.c_void_p), ("trace", C.c_void_p)]
+                ("status", C.c_void_p), ("trace", C.c_void_p), ("out_token", C.c_void_p),
+                ("out_logprob", C.c_void_p), ("seen", C.c_void_p), ("head_part", C.c_void_p)]
 
 
 def supported(model, batch: int) -> bool:
@@ -166,7 +167,8 @@ class PersistentDecode:
         self.route_idx = torch.zeros(nl * nb, k, dtype=torch.int32, device=dev)
         self.route_prob = torch.zeros(nl * nb, k, **f32)
         self.logits = torch.zeros(1, c.vocab_size, **f32)
-        self.bar = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.bar = torch.zeros(2, dtype=torch.int32, device=dev)
+        self.head_part = torch.zeros(self.grid, 4, **f32)
         del u8
         p = PDecode()
         p.d_model, p.n_blocks, p.n_loops, p.vocab = d, nb, nl, c.vocab_size
@@ -186,6 +188,7 @@ class PersistentDecode:
                      "collapsed", "route_idx", "route_prob", "logits", "bar"):
             setattr(p, name, getattr(self, name).data_ptr())
         p.status = kernels.device_status(dev).data_ptr()
+        p.head_part = self.head_part.data_ptr()
         self.params = p
 
     def prepare(self) -> None:
@@ -207,11 +210,23 @@ class PersistentDecode:
                     torch.matmul(v.view(-1, v.shape[-1]), b.mixer.w_o.t()).view_as(v))
         st.folded_rings = True
 
-    def step(self, ids: torch.Tensor) -> torch.Tensor:
+    def step(self, ids: torch.Tensor, out_token: torch.Tensor | None = None,
+             logprob: torch.Tensor | None = None, seen: torch.Tensor | None = None) -> torch.Tensor:
         """One decode token: ids [1] (device).  Returns the logits [1, V] fp32
-        (this object's buffer, rewritten by the next step)."""
+        (this object's buffer, rewritten by the next step).  With out_token
+        ([1] int64, may be `ids` itself) the step also samples greedily in the
+        same launch: the first maximal logit's index, its raw log-softmax into
+        logprob ([1] fp32) and its bit into seen ([ceil(V/32)] int32)."""
         self.prepare()
         self.token.copy_(ids.reshape(-1)[:1])
-        _native.call("llmyb_decode_persistent", C.byref(self.params),
-                     torch.cuda.current_stream().cuda_stream)
+        p = self.params
+        for name, t in (("out_token", out_token), ("out_logprob", logprob), ("seen", seen)):
+            if t is not None and (not t.is_cuda or not t.is_contiguous()):
+                raise ValueError(f"{name} must be a contiguous CUDA tensor")
+        if out_token is not None and out_token.dtype != torch.int64:
+            raise ValueError("out_token must be int64")
+        p.out_token = 0 if out_token is None else out_token.data_ptr()
+        p.out_logprob = 0 if logprob is None else logprob.data_ptr()
+        p.seen = 0 if seen is None else seen.data_ptr()
+        _native.call("llmyb_decode_persistent", C.byref(p), torch.cuda.current_stream().cuda_stream)
         return self.logits

@@ -694,10 +694,21 @@ typedef struct {
   int32_t* route_idx;           /* out [n_loops * n_blocks, top_k] */
   float* route_prob;            /* out [n_loops * n_blocks, top_k] */
   float* logits;                /* out [vocab] fp32 (bf16-rounded LM head output) */
-  uint32_t* bar;                /* grid barrier counter, zeroed before each launch */
+  uint32_t* bar;                /* [2]: grid barrier counter and the greedy step's arrival
+                                   count, both zeroed before each launch */
   int32_t* status;              /* device status word */
   uint64_t* trace;              /* nullable: [2, 2, 512] %globaltimer stamps of CTA 0 and the
-                                   last CTA, at every barrier wait's end and arrive */
+                                   last CTA, at every barrier wait's end and arrive (and
+                                   [2048, ...] points inside phases) */
+  /* Greedy sampling fused into the LM head (nullable out_token: logits only).
+   * The first maximal logit's index (sample_standalone.py:5383-5423 with
+   * temperature <= 1e-4 and no repetition penalty) goes to out_token, its
+   * raw log-softmax to out_logprob (nullable), its bit into seen (nullable
+   * [ceil(vocab/32)] bitmask); head_part is scratch [grid, 4]. */
+  int64_t* out_token;
+  float* out_logprob;
+  int32_t* seen;
+  float* head_part;
 } llmyb_pdecode;
 
 /* CTAs per grid that llmyb_decode_persistent will use on the current device

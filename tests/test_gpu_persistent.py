@@ -117,3 +117,38 @@ def test_persistent_graph_replay_matches_eager(cuda):
         dec.prime(o.logits[:, -1].float().argmax(-1))
         toks.append(torch.stack([dec.step().clone() for _ in range(10)], 1).cpu())
     assert torch.equal(toks[0], toks[1])
+
+
+def test_fused_greedy_matches_the_sampler(cuda):
+    """The LM head fused with greedy sampling (first maximal logit, its raw
+    log-softmax, its bit in the seen mask) against the same persistent step's
+    logits handed to the sampler kernel (temperature 0): identical tokens and
+    masks, log-probabilities within 1e-5."""
+    from hybrid_llm_b200 import kernels
+    from hybrid_llm_b200.state import RecurrentState
+    from hybrid_llm_b200.config import small_llmy_config
+    for cfg, t in ((inputs.mini_config(), 50), (small_llmy_config(), 64)):
+        m = _model(cfg)
+        assert m.greedy_fused(1)
+        ids = torch.from_numpy(np.random.default_rng(1).integers(0, cfg.vocab_size, (1, t))).cuda()
+        out = m.forward(ids, last_logits_only=True)
+        sts = []
+        for _ in range(2):
+            st = RecurrentState(cfg, 1, "cuda")
+            st.load_state_dict(out.state.state_dict())
+            sts.append(st)
+        words = (cfg.vocab_size + 31) // 32
+        seen = [torch.zeros(1, words, dtype=torch.int32, device="cuda") for _ in range(2)]
+        tok_a = out.logits[:, -1].float().argmax(-1)
+        tok_b = tok_a.clone()
+        lp_b = torch.zeros(1, device="cuda")
+        for _ in range(12):
+            logits = m.decode_step(tok_a, sts[0])
+            tok_a, lp_a = kernels.sample(logits, temperature=0.0, top_k=0, top_p=1.0,
+                                         seen=seen[0], update_seen=True)
+            m.decode_step_greedy(tok_b, sts[1], tok_b, lp_b, seen[1].view(-1))
+            torch.cuda.synchronize()
+            assert torch.equal(tok_a, tok_b)
+            assert abs(float(lp_a) - float(lp_b)) < 1e-5, (float(lp_a), float(lp_b))
+            assert torch.equal(seen[0], seen[1])
+        kernels.check_device_status()
