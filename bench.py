@@ -195,8 +195,9 @@ def run_reference(args) -> None:
 # caches flushed before the launch; two launches: 1,305,344 and 1,323,520 bytes).
 OUT_ROUTER_TRAFFIC = 1_314_432
 # ncu dram__bytes_read.sum + dram__bytes_write.sum of one decode_persistent_kernel
-# launch at the benchmark's decode shape (None until captured)
-PERSISTENT_TRAFFIC = None
+# launch at the benchmark's decode shape (small LLMY, 512-token prompt, sixth
+# decode step): 412,692,992 read + 5,650,944 written
+PERSISTENT_TRAFFIC = 418_343_936
 
 
 def out_router_roofline(model, p: dict, reps: int = 50) -> dict:
