@@ -347,6 +347,9 @@ def secondary_block(p: dict, reps: int = 20) -> dict:
     flops = 4 * 2.0 * 256 * cfg.moe_top_k * 3 * cfg.d_model * cfg.moe_hidden
     return {"workload": "single looped block [1, 256, 512], csa_moe + gdn_moe, 2 loops",
             "ms": t * 1e3, "tok_s": 256 / t, "moe_tflops": flops / t / 1e12,
+            "precision": "bf16 operands, fp32 accumulation and residual: measured against the "
+                         "reference's fp32 configuration at the bf16 tolerance (2e-2 of the "
+                         "residual update), not an fp32 result",
             "note": "latency-bound (256 tokens); timed with CUDA events, median"}
 
 
