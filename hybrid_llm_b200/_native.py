@@ -99,6 +99,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     # engine device entry points
     "llmyb_mhc_sinkhorn4": (I32, [P, P, I32, I32, P]),
     "llmyb_moe_selected_fp32": (I32, [P, P, P, P, P, P, P, P, I32, I32, I32, I32, P]),
+    # native engine (include/llmy.h)
+    "llmyb_engine_routes": (I32, [P, P, P, I32]),
     # hyper-connections
     "llmyb_mhc_read": (I32, [P, I32, I32, I32, P, I64, I64, P, P, P, P, P, F32, I32, P, P, P, P]),
     "llmyb_mhc_write": (I32, [P, I32, I32, I32, P, P, I32, P, P, P, P]),

@@ -857,6 +857,11 @@ __global__ void __launch_bounds__(kPT, 1) decode_persistent_kernel(const llmyb_p
     }
   }
   // ================================================================== head
+  if (p.skip_head) {
+    cp_async_wait_group<0>();
+    if (cta == 0 && tid == 0) *p.positions = pos + 1;  // every CTA read it before a barrier
+    return;
+  }
   {
     const float* xcur = p.x + xs * D;
     const bf16* collapse = static_cast<const bf16*>(p.collapse);

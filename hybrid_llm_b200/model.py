@@ -391,11 +391,13 @@ class LoopedHybridModel:
             self.route_log.extend(pd.route_idx[r:r + 1] for r in range(pd.route_idx.shape[0]))
         return logits
 
-    def _decode_persist(self, ids: torch.Tensor, state: RecurrentState) -> torch.Tensor:
+    def _decode_persist(self, ids: torch.Tensor, state: RecurrentState,
+                        loops: int | None = None) -> torch.Tensor:
         pd = self._persistent_for(state)
-        logits = pd.step(ids)
+        logits = pd.step(ids, n_loops=loops)
         if self.route_log is not None:
-            self.route_log.extend(pd.route_idx[r:r + 1] for r in range(pd.route_idx.shape[0]))
+            rows = (loops or self.cfg.num_loops) * self.cfg.n_blocks
+            self.route_log.extend(pd.route_idx[r:r + 1] for r in range(rows))
         return logits
 
     def _decode_step(self, input_ids: torch.Tensor, state: RecurrentState,
@@ -416,10 +418,10 @@ class LoopedHybridModel:
         bsz = ids.shape[0]
         loops = c.num_loops if num_loops is None else int(num_loops)
         d = c.d_model
-        if self.decode_persistent and loops == c.num_loops:
+        if self.decode_persistent and 1 <= loops <= c.num_loops:
             from . import persistent
             if persistent.supported(self, bsz):
-                return self._decode_persist(ids, state)
+                return self._decode_persist(ids, state, loops)
         if getattr(state, "folded_rings", False):
             raise RuntimeError("this state is advanced by the persistent decode step (its CSA "
                                "value rings are folded); continue with decode_persistent=True "

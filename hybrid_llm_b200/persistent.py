@@ -55,7 +55,8 @@ class PDecode(C.Structure):
                 ("ybuf", C.c_void_p), ("collapsed", C.c_void_p), ("route_idx", C.c_void_p),
                 ("route_prob", C.c_void_p), ("logits", C.c_void_p), ("bar", C.c_void_p),
                 ("status", C.c_void_p), ("trace", C.c_void_p), ("out_token", C.c_void_p),
-                ("out_logprob", C.c_void_p), ("seen", C.c_void_p), ("head_part", C.c_void_p)]
+                ("out_logprob", C.c_void_p), ("seen", C.c_void_p), ("head_part", C.c_void_p),
+                ("skip_head", C.c_int32)]
 
 
 def supported(model, batch: int) -> bool:
@@ -211,15 +212,23 @@ class PersistentDecode:
         st.folded_rings = True
 
     def step(self, ids: torch.Tensor, out_token: torch.Tensor | None = None,
-             logprob: torch.Tensor | None = None, seen: torch.Tensor | None = None) -> torch.Tensor:
+             logprob: torch.Tensor | None = None, seen: torch.Tensor | None = None,
+             n_loops: int | None = None) -> torch.Tensor:
         """One decode token: ids [1] (device).  Returns the logits [1, V] fp32
         (this object's buffer, rewritten by the next step).  With out_token
         ([1] int64, may be `ids` itself) the step also samples greedily in the
         same launch: the first maximal logit's index, its raw log-softmax into
-        logprob ([1] fp32) and its bit into seen ([ceil(V/32)] int32)."""
+        logprob ([1] fp32) and its bit into seen ([ceil(V/32)] int32).
+        n_loops: run the first n loops (default all), as the reference's
+        model_step does for a smaller num_loops (model.cpp:1824-1825)."""
+        nl = self.model.cfg.num_loops
+        n_loops = nl if n_loops is None else int(n_loops)
+        if not 1 <= n_loops <= nl:
+            raise ValueError(f"n_loops must be in [1, {nl}], got {n_loops}")
         self.prepare()
         self.token.copy_(ids.reshape(-1)[:1])
         p = self.params
+        p.n_loops = n_loops
         for name, t in (("out_token", out_token), ("out_logprob", logprob), ("seen", seen)):
             if t is not None and (not t.is_cuda or not t.is_contiguous()):
                 raise ValueError(f"{name} must be a contiguous CUDA tensor")

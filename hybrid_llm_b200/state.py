@@ -155,6 +155,10 @@ class RecurrentState:
         the persistent step created them) keep their contents."""
         self.positions.copy_(sd["positions"])
         self.folded_rings = bool(sd.get("folded_rings", torch.tensor(False)))
+        for name in sd:  # folded rings this state has not created yet
+            key = name[len("local_vo."):]
+            if name.startswith("local_vo.") and key not in self.local_vo:
+                self.local_vo[key] = torch.empty_like(self.local_v[key])
         for name, table in self._tables():
             for key, t in table.items():
                 if name == "local_vo" and f"{name}.{key}" not in sd:

@@ -709,6 +709,9 @@ typedef struct {
   float* out_logprob;
   int32_t* seen;
   float* head_part;
+  /* Non-zero: a prompt token whose logits nobody reads: the step ends after
+   * the last expert phase (no collapse, final norm, LM head or sampling). */
+  int32_t skip_head;
 } llmyb_pdecode;
 
 /* CTAs per grid that llmyb_decode_persistent will use on the current device

@@ -35,7 +35,10 @@ def _layernorm(x, w, b, eps=1e-5):
 
 
 def _to_numpy(v, dtype):
-    return np.asarray(v.detach().cpu().numpy() if hasattr(v, "detach") else v, dtype=dtype)
+    if hasattr(v, "detach"):  # a torch tensor; bf16 widens exactly to fp32 first
+        v = v.detach().cpu()
+        v = (v.float() if v.is_floating_point() else v).numpy()
+    return np.asarray(v, dtype=dtype)
 
 
 class _LazyParams:

@@ -52,3 +52,18 @@ def test_state_dict_round_trip():
         assert ta.keys() == tb.keys() and all(torch.equal(ta[k], tb[k]) for k in ta)
     assert torch.equal(a.positions, b.positions)
     assert b.nbytes() == a.nbytes() > 0
+
+
+def test_state_dict_carries_folded_rings_into_a_fresh_state():
+    """A state the persistent step advanced (folded value rings, local_vo)
+    restores into a new state that has not created those rings yet."""
+    cfg = inputs.router_ctx_config()
+    a = _filled(cfg)
+    for key, v in a.local_v.items():
+        a.local_vo[key] = torch.randn_like(v.float()).to(v.dtype)
+    a.folded_rings = True
+    b = RecurrentState(cfg, 3, "cpu")
+    assert not b.local_vo
+    b.load_state_dict(a.state_dict())
+    assert b.folded_rings and b.local_vo.keys() == a.local_vo.keys()
+    assert all(torch.equal(a.local_vo[k], b.local_vo[k]) for k in a.local_vo)
