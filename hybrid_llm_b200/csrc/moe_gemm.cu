@@ -104,15 +104,16 @@ __device__ __forceinline__ void store_chunk_rows(const uint4 (&pk)[4], bool vali
   }
 }
 
-template <int EPI>
-__device__ __forceinline__ void epilogue_rows(uint32_t t_row, bool valid, float scale,
+// NCH 32-column chunks of the warp's 32 rows starting at output column c0
+// (kSwiGLU: gate columns c0.., up columns 128 + c0..; kScale: columns c0..).
+template <int EPI, int NCH>
+__device__ __forceinline__ void epilogue_part(uint32_t t_row, int c0, bool valid, float scale,
                                               __nv_bfloat16* dst, uint4* scratch, int lane) {
   static_assert(BN == 256, "epilogue assumes 256 accumulator columns");
   if constexpr (EPI == kSwiGLU) {
-    constexpr int NCH = BN / 2 / 32;
     uint32_t g[2][32], u[2][32];
-    sm100::tmem_ld_32x32b_x32(t_row, g[0]);
-    sm100::tmem_ld_32x32b_x32(t_row + BN / 2, u[0]);
+    sm100::tmem_ld_32x32b_x32(t_row + c0, g[0]);
+    sm100::tmem_ld_32x32b_x32(t_row + BN / 2 + c0, u[0]);
 #pragma unroll
     for (int i = 0; i < NCH; ++i) {
       const int b = i & 1;
@@ -120,8 +121,8 @@ __device__ __forceinline__ void epilogue_rows(uint32_t t_row, bool valid, float 
       sm100::tmem_regs_ready(g[b]);
       sm100::tmem_regs_ready(u[b]);
       if (i + 1 < NCH) {
-        sm100::tmem_ld_32x32b_x32(t_row + 32 * (i + 1), g[b ^ 1]);
-        sm100::tmem_ld_32x32b_x32(t_row + BN / 2 + 32 * (i + 1), u[b ^ 1]);
+        sm100::tmem_ld_32x32b_x32(t_row + c0 + 32 * (i + 1), g[b ^ 1]);
+        sm100::tmem_ld_32x32b_x32(t_row + BN / 2 + c0 + 32 * (i + 1), u[b ^ 1]);
       }
       uint4 pk[4];
       uint32_t* pw = reinterpret_cast<uint32_t*>(pk);
@@ -129,27 +130,34 @@ __device__ __forceinline__ void epilogue_rows(uint32_t t_row, bool valid, float 
       for (int j = 0; j < 16; ++j)
         pw[j] = pack_bf16x2(swiglu_fast(g[b][2 * j], u[b][2 * j]),
                             swiglu_fast(g[b][2 * j + 1], u[b][2 * j + 1]));
-      store_chunk_rows(pk, valid, dst + 32 * i, scratch, lane);
+      store_chunk_rows(pk, valid, dst + c0 + 32 * i, scratch, lane);
     }
   } else {
-    constexpr int NCH = BN / 32;
     uint32_t a[2][32];
-    sm100::tmem_ld_32x32b_x32(t_row, a[0]);
+    sm100::tmem_ld_32x32b_x32(t_row + c0, a[0]);
 #pragma unroll
     for (int i = 0; i < NCH; ++i) {
       const int b = i & 1;
       sm100::tmem_ld_wait();
       sm100::tmem_regs_ready(a[b]);
-      if (i + 1 < NCH) sm100::tmem_ld_32x32b_x32(t_row + 32 * (i + 1), a[b ^ 1]);
+      if (i + 1 < NCH) sm100::tmem_ld_32x32b_x32(t_row + c0 + 32 * (i + 1), a[b ^ 1]);
       uint4 pk[4];
       uint32_t* pw = reinterpret_cast<uint32_t*>(pk);
 #pragma unroll
       for (int j = 0; j < 16; ++j)
         pw[j] = pack_bf16x2(__uint_as_float(a[b][2 * j]) * scale,
                             __uint_as_float(a[b][2 * j + 1]) * scale);
-      store_chunk_rows(pk, valid, dst + 32 * i, scratch, lane);
+      store_chunk_rows(pk, valid, dst + c0 + 32 * i, scratch, lane);
     }
   }
+}
+
+// All 256 accumulator columns of the warp's rows (one warp per lane quarter).
+template <int EPI>
+__device__ __forceinline__ void epilogue_rows(uint32_t t_row, bool valid, float scale,
+                                              __nv_bfloat16* dst, uint4* scratch, int lane) {
+  epilogue_part<EPI, EPI == kSwiGLU ? BN / 2 / 32 : BN / 32>(t_row, 0, valid, scale, dst, scratch,
+                                                            lane);
 }
 
 template <int EPI>
@@ -319,11 +327,17 @@ __global__ void __launch_bounds__(256, 1) moe_gemm_kernel(
 // CTA's TMA completions are counted on the even CTA's "full" barrier and its
 // epilogue warps arrive remotely on the even CTA's "tmem empty" barrier.
 // Loads are plain (no multicast): every operand is read from local HBM.
+// Eight epilogue warps (warps 4-11 of 384 threads): two per TMEM lane
+// quarter, each draining half of the accumulator's columns, so a tile's
+// epilogue (TMEM loads, conversion, staged stores) runs on two warps per SM
+// sub-partition and finishes inside the next tile's main loop.
 constexpr int PBM = 128, PBN = 256, PBK = 64, PST = 6;
+constexpr int P_THREADS = 384, P_EPI_WARPS = 8;
 constexpr int P_A_BYTES = PBM * PBK * 2;         // 16 KB
 constexpr int P_B_BYTES = (PBN / 2) * PBK * 2;   // 16 KB
 constexpr int P_STAGE = P_A_BYTES + P_B_BYTES;   // 32 KB
-constexpr int P_SMEM = PST * P_STAGE + 1024 + 256 + EPI_SCRATCH;
+constexpr int P_EPI_SCRATCH = P_EPI_WARPS * 32 * 64;
+constexpr int P_SMEM = PST * P_STAGE + 1024 + 256 + P_EPI_SCRATCH;
 
 __device__ __forceinline__ TileInfo map_tile_pair(int tile, int n_tiles, const int* tile_offsets,
                                                   const int* expert_offsets, int E) {
@@ -344,7 +358,7 @@ __device__ __forceinline__ TileInfo map_tile_pair(int tile, int n_tiles, const i
 }
 
 template <int EPI>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1) moe_gemm_pair_kernel(
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1) moe_gemm_pair_kernel(
     const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
     const int* __restrict__ expert_offsets, const int* __restrict__ tile_offsets, int E, int K,
     int n_weight_rows, __nv_bfloat16* __restrict__ out, int out_ld,
@@ -375,7 +389,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1) moe_gemm_pai
     }
     for (int a = 0; a < 2; ++a) {
       sm100::mbar_init(&tmem_full[a], 1);
-      sm100::mbar_init(&tmem_empty[a], 8);  // 4 epilogue warps x 2 CTAs
+      sm100::mbar_init(&tmem_empty[a], 2 * P_EPI_WARPS);  // epilogue warps of both CTAs
     }
     sm100::mbar_init(mma_done, 1);
     *abort_flag = 0;
@@ -470,9 +484,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1) moe_gemm_pai
     sm100::mbar_wait_warp(mma_done, 0, dev_status, nullptr);
   } else if (warp >= 4) {
     // --------------------------------------------------------- epilogue
-    const int q = warp & 3;
+    const int q = warp & 3;                   // TMEM lane quarter this warp may access
+    const int half = (warp - 4) >> 2;         // which half of the columns it drains
     const int r = q * 32 + lane;
-    uint4* epi_scratch = reinterpret_cast<uint4*>(smem + PST * P_STAGE + 256) + q * 128;
+    uint4* epi_scratch = reinterpret_cast<uint4*>(smem + PST * P_STAGE + 256) + (warp - 4) * 128;
     const uint32_t empty_leader0 = sm100::mapa_shared(sm100::smem_u32(&tmem_empty[0]), 0);
     const uint32_t empty_leader1 = sm100::mapa_shared(sm100::smem_u32(&tmem_empty[1]), 0);
     int acc = 0;
@@ -489,7 +504,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1) moe_gemm_pai
       const float scale = (EPI == kScale && valid) ? __ldg(row_scale + row) : 0.0f;
       const int64_t orow = (out_row != nullptr && valid) ? __ldg(out_row + row) : row;
       __nv_bfloat16* dst = out + orow * out_ld + ti.n_tile * (EPI == kSwiGLU ? PBN / 2 : PBN);
-      epilogue_rows<EPI>(t_row, valid, scale, dst, epi_scratch, lane);
+      if constexpr (EPI == kSwiGLU)
+        epilogue_part<EPI, PBN / 4 / 32>(t_row, half * (PBN / 4), valid, scale, dst, epi_scratch,
+                                         lane);
+      else
+        epilogue_part<EPI, PBN / 2 / 32>(t_row, half * (PBN / 2), valid, scale, dst, epi_scratch,
+                                         lane);
       sm100::tc_fence_before();
       __syncwarp();
       if (lane == 0) sm100::mbar_arrive_cluster(acc == 0 ? empty_leader0 : empty_leader1);
@@ -625,11 +645,11 @@ int32_t run_grouped(const __nv_bfloat16* x, int32_t d_model, int64_t rows,
     const int clusters = sms / 2;
     const int grid1 = 2 * static_cast<int>(std::min<int64_t>(clusters, m_tiles_max * (2 * ffn / PBN)));
     const int grid2 = 2 * static_cast<int>(std::min<int64_t>(clusters, m_tiles_max * (d_model / PBN)));
-    moe_gemm_pair_kernel<kSwiGLU><<<grid1, 256, P_SMEM, s>>>(
+    moe_gemm_pair_kernel<kSwiGLU><<<grid1, P_THREADS, P_SMEM, s>>>(
         ma1, mb1, expert_offsets, tile_offsets, n_experts, d_model, 2 * ffn, h_perm, ffn, nullptr,
         nullptr, dev_status);
     count_launch();
-    moe_gemm_pair_kernel<kScale><<<grid2, 256, P_SMEM, s>>>(
+    moe_gemm_pair_kernel<kScale><<<grid2, P_THREADS, P_SMEM, s>>>(
         ma2, mb2, expert_offsets, tile_offsets, n_experts, ffn, d_model, y, d_model, perm_prob,
         out_row, dev_status);
     count_launch();
