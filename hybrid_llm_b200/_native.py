@@ -77,9 +77,9 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     # banded attention
     "llmyb_banded_attention": (I32, [P, I64, P, I64, P, I64, I32, I32, I32, I32, I32, I32, F32, P,
                                      I64, P, P]),
-    "llmyb_csa_prefill_scratch_bytes": (I64, [I32, I32, I32]),
+    "llmyb_csa_prefill_scratch_bytes": (I64, [I32, I32, I32, I32]),
     "llmyb_csa_local_prefill": (I32, [P, I64, P, I64, P, I64, I32, I32, I32, I32, I32, I32, P, I64,
-                                      P, P]),
+                                      P, P, P]),
     "llmyb_csa_local_decode": (I32, [P, I64, P, I64, P, I64, P, P, P, I32, I32, I32, I32, I32, P,
                                      I64, P, P]),
     # diagnostics

@@ -708,22 +708,40 @@ bool aligned16(const void* p, int64_t stride) {
 }  // namespace
 }  // namespace llmyb
 
+namespace llmyb {
+// csa_tc.cu: the tcgen05 prefill (statistics, head-averaged probabilities, PV)
+void csa_tc_geometry(int T, int W, int* nqt, int* nb);
+bool csa_tc_supported(int head_dim, int d_model, int64_t q_stride, int64_t k_stride,
+                      int64_t v_stride, int64_t out_stride);
+int32_t csa_prefill_tc(const void* q, int64_t sq, const void* k, int64_t sk, const void* v,
+                       int64_t sv, int B, int T, int H, int DH, int D, int W, float scale,
+                       void* out, int64_t so, void* scratch, int32_t* dev_status,
+                       cudaStream_t s);
+}  // namespace llmyb
+
 using namespace llmyb;
 
-LLMYB_API int64_t llmyb_csa_prefill_scratch_bytes(int32_t batch, int32_t seq, int32_t heads) {
-  if (batch < 0 || seq < 0 || heads <= 0) return -1;
-  return static_cast<int64_t>(batch) * seq * heads * 2 * sizeof(float);
+LLMYB_API int64_t llmyb_csa_prefill_scratch_bytes(int32_t batch, int32_t seq, int32_t heads,
+                                                  int32_t window) {
+  if (batch < 0 || seq < 0 || heads <= 0 || window <= 0) return -1;
+  const int64_t stats = static_cast<int64_t>(batch) * seq * heads * 2 * sizeof(float);
+  if (seq == 0) return stats;
+  int nqt = 0, nb = 0;
+  csa_tc_geometry(seq, std::max(1, std::min<int>(window, seq)), &nqt, &nb);
+  return (stats + 255) / 256 * 256 + static_cast<int64_t>(batch) * nqt * nb * 128 * 128 * 2;
 }
 
 // CSA local branch, prefill: q,k [B*T, H*DH] (strides), v [B*T, D] shared
 // value stream (stride sv); out [B*T, D].  scratch holds the per-head row
-// statistics (llmyb_csa_prefill_scratch_bytes).
+// statistics and the head-averaged probability tiles
+// (llmyb_csa_prefill_scratch_bytes).  Head dim 64 / 128 with D % 128 == 0 runs
+// on tcgen05 (csa_tc.cu); other shapes on the mma.sync kernels below.
 LLMYB_API int32_t llmyb_csa_local_prefill(const void* q, int64_t q_stride, const void* k,
                                           int64_t k_stride, const void* v, int64_t v_stride,
                                           int32_t batch, int32_t seq, int32_t heads,
                                           int32_t head_dim, int32_t d_model, int32_t window,
                                           void* out, int64_t out_stride, void* scratch,
-                                          void* stream) {
+                                          int32_t* dev_status, void* stream) {
   if (!q || !k || !v || !out || !scratch || batch < 0 || seq < 0 || heads <= 0 || window <= 0)
     return LLMYB_EINVAL;
   if (batch == 0 || seq == 0) return LLMYB_OK;
@@ -733,6 +751,11 @@ LLMYB_API int32_t llmyb_csa_local_prefill(const void* q, int64_t q_stride, const
   // csa.py:42: the window never exceeds the sequence
   const int w = std::max(1, std::min<int>(window, seq));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (csa_tc_supported(head_dim, d_model, q_stride, k_stride, v_stride, out_stride) &&
+      (reinterpret_cast<uintptr_t>(scratch) & 15u) == 0)
+    return csa_prefill_tc(q, q_stride, k, k_stride, v, v_stride, batch, seq, heads, head_dim,
+                          d_model, w, 1.0f / sqrtf(static_cast<float>(head_dim)), out, out_stride,
+                          scratch, dev_status, s);
   auto Q = static_cast<const __nv_bfloat16*>(q);
   auto K = static_cast<const __nv_bfloat16*>(k);
   auto V = static_cast<const __nv_bfloat16*>(v);

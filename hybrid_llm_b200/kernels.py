@@ -674,10 +674,10 @@ def csa_local_prefill(q, k, v, window: int, out=None):
     vp, vs = _tokens(v, "v")
     if out is None:
         out = torch.empty(bsz, t, dm, dtype=torch.bfloat16, device=q.device)
-    need = int(_native.lib().llmyb_csa_prefill_scratch_bytes(bsz, t, h))
+    need = int(_native.lib().llmyb_csa_prefill_scratch_bytes(bsz, t, h, int(window)))
     scratch = torch.empty(max(need, 16), dtype=torch.uint8, device=q.device)
     _native.call("llmyb_csa_local_prefill", qp, qs, kp, ks, vp, vs, bsz, t, h, dh, dm, int(window),
-                 _ptr(out), out.stride(1), _ptr(scratch), _stream())
+                 _ptr(out), out.stride(1), _ptr(scratch), _ptr(device_status(q.device)), _stream())
     return out
 
 

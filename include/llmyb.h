@@ -358,16 +358,24 @@ int32_t llmyb_banded_attention(const void* q, int64_t q_stride, const void* k, i
                                float scale, void* out, int64_t out_stride, int32_t* dev_status,
                                void* stream);
 
-/* Scratch bytes needed by llmyb_csa_local_prefill (per-head row max / sum). */
-int64_t llmyb_csa_prefill_scratch_bytes(int32_t batch, int32_t seq, int32_t heads);
+/* Scratch bytes needed by llmyb_csa_local_prefill: the per-head row max /
+ * sum [B, T, H] fp32, then B * ceil(T/128) * nb head-averaged probability
+ * tiles of 128 x 128 bf16, nb = min(ceil(T/128), ceil((W-1)/128) + 1) with
+ * W = min(window, T). */
+int64_t llmyb_csa_prefill_scratch_bytes(int32_t batch, int32_t seq, int32_t heads,
+                                        int32_t window);
 
 /* CSA local branch, prefill: head-averaged probabilities times the shared
  * value stream v [B*T, D]; out [B*T, D].  Window = min(window, T) as
- * csa.py:42 does.  Head dim in {64, 128}, D % 64 == 0. */
+ * csa.py:42 does.  Head dim in {64, 128}, D % 64 == 0; with D % 128 == 0 the
+ * score and PV products run on tcgen05 (the probability tiles go through
+ * scratch); dev_status (nullable) gets LLMYB_ETIMEOUT if one of their
+ * bounded waits runs out. */
 int32_t llmyb_csa_local_prefill(const void* q, int64_t q_stride, const void* k, int64_t k_stride,
                                 const void* v, int64_t v_stride, int32_t batch, int32_t seq,
                                 int32_t heads, int32_t head_dim, int32_t d_model, int32_t window,
-                                void* out, int64_t out_stride, void* scratch, void* stream);
+                                void* out, int64_t out_stride, void* scratch,
+                                int32_t* dev_status, void* stream);
 
 /* CSA local branch, decode: q/knew [B, H*DH], vnew [B, D]; ring caches
  * kcache [B, window, H*DH], vcache [B, window, D] hold token p at slot

@@ -104,8 +104,13 @@ def test_banded_attention_long_context_full_size(cuda):
 
 @pytest.mark.parametrize("b,t,h,dh,dm,w", [(1, 256, 8, 64, 512, 128), (1, 512, 12, 64, 768, 512),
                                            (2, 100, 4, 128, 256, 40), (1, 70, 16, 128, 2048, 2048),
-                                           (1, 5, 2, 64, 128, 128)])
+                                           (1, 5, 2, 64, 128, 128), (1, 300, 3, 64, 384, 100),
+                                           (3, 1000, 4, 128, 512, 333), (2, 700, 6, 64, 768, 129),
+                                           (1, 384, 2, 64, 192, 1000)])
 def test_csa_local_prefill_matches_oracle(cuda, b, t, h, dh, dm, w):
+    """Head dim 64 / 128 with D % 128 == 0 on the tcgen05 kernels (ragged last
+    query tiles, windows shorter and longer than the sequence, W - 1 a multiple
+    of 128); D = 192 on the mma.sync kernels."""
     from hybrid_llm_b200 import kernels
     rng = np.random.default_rng(t + h)
     q, k = _bf(rng.normal(size=(b, t, h, dh))), _bf(rng.normal(size=(b, t, h, dh)))
