@@ -784,6 +784,7 @@ def run_ours(args) -> None:
         "e2e": e2e, "gpu_launches": launches_per_step * args.steps, "roofline": roofline,
         "step_roofline": step_roofline,
         "clocks": clocks.summary(), "prefill_tok_s_c2": bsz * prompt_len / prefill_s,
+        "prefill_roofline": prefill_roofline(model, cfg, prompt_len, prefill_s, p),
     }
     del dec, out, model
     torch.cuda.empty_cache()
@@ -804,6 +805,45 @@ def run_ours(args) -> None:
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
+
+
+def prefill_roofline(model, cfg, tokens: int, seconds: float, p: dict) -> dict:
+    """Roofline of a B=1 prefill of `tokens` ids: the algorithmic HBM bytes
+    (every dense weight and every expert once per loop -- at 512 tokens and
+    top-2 each of the 16 experts receives rows --, the LM head row block of
+    the last token) against the algorithmic FLOPs (2 x the weights each token
+    uses, the CSA scores and PV over each token's window, the GDN state
+    update and readout); the bound is whichever takes longer at the measured
+    peaks."""
+    d, nl = cfg.d_model, cfg.num_loops
+    nb = lambda t: t.numel() * t.element_size()
+    dense_bytes = dense_params = 0
+    expert_bytes = 0
+    attn_flops = 0.0
+    keys = sum(min(t + 1, cfg.csa_window) for t in range(tokens))
+    for blk in model.w.blocks:
+        m = blk.mixer
+        if blk.kind == "gdn":
+            mats = (m.w_in, m.w_out)
+            attn_flops += tokens * 4.0 * cfg.gdn_heads * cfg.gdn_key_dim * cfg.gdn_value_dim * 2
+        else:
+            mats = (m.w_in, m.local_out, m.out)
+            hd = cfg.csa_heads * cfg.csa_head_dim
+            attn_flops += 2.0 * keys * (hd + d)
+        for w in mats + (blk.moe.router,):
+            dense_bytes += nb(w)
+            dense_params += w.numel()
+        expert_bytes += nb(blk.moe.w13) + nb(blk.moe.w2)
+    act_expert = 3 * cfg.moe_hidden * d * cfg.moe_top_k * cfg.n_blocks
+    flops = nl * (2.0 * tokens * (dense_params + act_expert) + attn_flops) + 2.0 * cfg.vocab_size * d
+    bytes_ = nl * (dense_bytes + expert_bytes) + cfg.vocab_size * d * 2 + tokens * d * 2
+    t_hbm = bytes_ / (p["hbm_gbs"] * 1e9)
+    t_tc = flops / (p["bf16_tflops"] * 1e12)
+    t_roof = max(t_hbm, t_tc)
+    return {"bound": "hbm" if t_hbm >= t_tc else "tensor", "tokens": tokens,
+            "algorithmic_bytes": bytes_, "algorithmic_flops": flops,
+            "t_roofline_ms": t_roof * 1e3, "t_ms": seconds * 1e3, "frac": t_roof / seconds,
+            "achieved_gbs": bytes_ / seconds / 1e9, "achieved_tflops": flops / seconds / 1e12}
 
 
 def decode_bytes_per_step(model, cfg, folded: bool = False) -> float:

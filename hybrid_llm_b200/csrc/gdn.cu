@@ -880,7 +880,9 @@ __global__ void gdn_conv_roll_kernel(const __nv_bfloat16* __restrict__ x,
 }
 
 // ------------------------------------------------- chunk scan on tcgen05
-// K = 128, value slices of 64 columns; one CTA per (row, head, slice).
+// K = 128 (or K = 64 padded to 128: the key-dimension boxes past K read as
+// zeros, so the state rows K..127 stay zero and only rows < K are loaded and
+// stored), value slices of 64 columns; one CTA per (row, head, slice).
 //   warp 0     TMA: per chunk [Kw; Qs] (Qs = diag(qscale) q, from the prep
 //              kernel), K, [0; Aqk] and the U slice, two stages
 //   warp 1     MMA (one thread), per chunk:
@@ -948,8 +950,8 @@ __global__ void __launch_bounds__(320, 1) gdn_scan_tc_kernel(
     const __grid_constant__ CUtensorMap map_k, const __grid_constant__ CUtensorMap map_aqk,
     const __grid_constant__ CUtensorMap map_u, const float* __restrict__ kscale,
     const float* __restrict__ sdecay, const __nv_bfloat16* __restrict__ gate, int64_t sg,
-    int B, int T, int H, int VD, float* __restrict__ state, __nv_bfloat16* __restrict__ out,
-    int64_t so, int32_t* dev_status) {
+    int B, int T, int H, int KD, int VD, float* __restrict__ state,
+    __nv_bfloat16* __restrict__ out, int64_t so, int32_t* dev_status) {
   using namespace scan_tc;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -1018,7 +1020,7 @@ __global__ void __launch_bounds__(320, 1) gdn_scan_tc_kernel(
         for (int x = 0; x < 2; ++x) {
           sm100::tma_load_4d(&map_kw, &st_full[s], st + kA1 + x * 16384, x * 64, h, t0, b);
           sm100::tma_load_4d(&map_qs, &st_full[s], st + kA1 + x * 16384 + 8192, x * 64, h, t0, b);
-          sm100::tma_load_3d(&map_k, &st_full[s], st + kA2 + x * 8192, h * 128 + x * 64, t0, b);
+          sm100::tma_load_4d(&map_k, &st_full[s], st + kA2 + x * 8192, x * 64, h, t0, b);
         }
         sm100::tma_load_2d(&map_aqk, &st_full[s], st + kA3 + 8192, 0,
                            static_cast<int32_t>((bh * nC + c) * kC));
@@ -1091,11 +1093,12 @@ __global__ void __launch_bounds__(320, 1) gdn_scan_tc_kernel(
     uint8_t* w_lo = w_hi + 8192;
     uint8_t* x_hi = w_hi + 16384;
     uint8_t* x_lo = w_hi + 24576;
-    float* Sg = state + (bh * 128 + row) * VD + v0 + 32 * half;
+    const bool key_row = row < KD;  // rows KD..127 of a padded K = 64 state stay zero
+    float* Sg = state + (bh * KD + (key_row ? row : 0)) * VD + v0 + 32 * half;
     uint32_t S[32];  // fp32 bit patterns of S[row][v0 + 32 half ..]
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      const uint4 v = reinterpret_cast<const uint4*>(Sg)[j];
+      const uint4 v = key_row ? reinterpret_cast<const uint4*>(Sg)[j] : make_uint4(0, 0, 0, 0);
       S[4 * j] = v.x;
       S[4 * j + 1] = v.y;
       S[4 * j + 2] = v.z;
@@ -1223,10 +1226,11 @@ __global__ void __launch_bounds__(320, 1) gdn_scan_tc_kernel(
       ks_cur = ks_next;
       sd_cur = sd_next;
     }
+    if (key_row)
 #pragma unroll
-    for (int j = 0; j < 8; ++j)
-      reinterpret_cast<uint4*>(Sg)[j] = make_uint4(S[4 * j], S[4 * j + 1], S[4 * j + 2],
-                                                   S[4 * j + 3]);
+      for (int j = 0; j < 8; ++j)
+        reinterpret_cast<uint4*>(Sg)[j] = make_uint4(S[4 * j], S[4 * j + 1], S[4 * j + 2],
+                                                     S[4 * j + 3]);
   }
   sm100::tc_fence_before();
   __syncthreads();
@@ -1277,8 +1281,8 @@ ScratchLayout scratch_layout(int B, int T, int H, int KD, int VD) {
   s.ks = s.qs + al(bt * H * 4);
   s.sd = s.ks + al(bt * H * 4);
   s.qsq = s.sd + al(static_cast<int64_t>(B) * H * nC * 4);
-  // the scaled q of the tcgen05 scan (K = 128 only)
-  s.total = s.qsq + (KD == 128 && VD % 64 == 0 ? al(bt * H * KD * 2) : 0);
+  // the scaled q of the tcgen05 scan
+  s.total = s.qsq + ((KD == 64 || KD == 128) && VD % 64 == 0 ? al(bt * H * KD * 2) : 0);
   return s;
 }
 
@@ -1286,7 +1290,8 @@ ScratchLayout scratch_layout(int B, int T, int H, int KD, int VD) {
 bool scan_tc_ok(const GdnIO& io, int KD, int VD, const void* state, const void* out,
                 int64_t so) {
   const auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
-  return KD == 128 && VD % scan_tc::kVS == 0 && io.sg % 8 == 0 && so % 8 == 0 && io.sk % 8 == 0 &&
+  return (KD == 64 || KD == 128) && VD % scan_tc::kVS == 0 && io.sg % 8 == 0 && so % 8 == 0 &&
+         io.sk % 8 == 0 &&
          a16(io.gate) && a16(out) && a16(state) && a16(io.k);
 }
 
@@ -1324,13 +1329,13 @@ int32_t launch_prefill(const GdnIO& io, int B, int T, int H, void* scratch, floa
     CUtensorMap mkw, mqs, mk, maqk, mu;
     if (!make_bf16_4d_map(&mkw, po.Kw, B, T, H, KD, kC) ||
         !make_bf16_4d_map(&mqs, po.Qs, B, T, H, KD, kC) ||
-        !make_bf16_3d_map(&mk, io.k, B, T, static_cast<uint64_t>(H) * KD, io.sk, kC) ||
+        !make_bf16_4d_map_ld(&mk, io.k, B, T, H, KD, io.sk, kC) ||
         !make_bf16_2d_map(&maqk, po.Aqk, static_cast<uint64_t>(B) * H * nC * kC, kC, kC, kC, kC) ||
         !make_bf16_4d_map(&mu, po.U, B, T, H, VD, kC))
       return LLMYB_EUNSUPPORTED;
     gdn_scan_tc_kernel<<<B * H * (VD / scan_tc::kVS), 320, scan_tc::kSmem, s>>>(
-        mkw, mqs, mk, maqk, mu, po.kscale, po.sdecay, io.gate, io.sg, B, T, H, VD, state, out, so,
-        dev_status);
+        mkw, mqs, mk, maqk, mu, po.kscale, po.sdecay, io.gate, io.sg, B, T, H, KD, VD, state, out,
+        so, dev_status);
     count_launch();
     return launch_status();
   }

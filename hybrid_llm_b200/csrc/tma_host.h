@@ -79,14 +79,34 @@ inline bool make_bf16_4d_map(CUtensorMap* map, const void* base, uint64_t batch,
   return r == CUDA_SUCCESS;
 }
 
+// bf16 tensor [batch][rows][heads][cols] with row stride ld elements (a head
+// slice of a wider token-major row), boxes of [1, box_rows, 1, 64 cols] with
+// the 128-byte swizzle; rows past `rows` and columns past `cols` read as zeros.
+inline bool make_bf16_4d_map_ld(CUtensorMap* map, const void* base, uint64_t batch,
+                                uint64_t rows, uint64_t heads, uint64_t cols, uint64_t ld,
+                                uint32_t box_rows) {
+  auto enc = tensor_map_encoder();
+  if (enc == nullptr) return false;
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0 || (cols * 2) % 16 != 0 || (ld * 2) % 16 != 0)
+    return false;
+  cuuint64_t dims[4] = {cols, heads, rows, batch};
+  cuuint64_t strides[3] = {cols * 2, ld * 2, rows * ld * 2};
+  cuuint32_t box[4] = {64, 1, box_rows, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims,
+                   strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// SMs of the current device (queried on every call: the attribute belongs to
+// the device, and the query is cheap).
 inline int num_sms() {
-  static int n = []() {
-    int dev = 0, v = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
-    return v > 0 ? v : 148;
-  }();
-  return n;
+  int dev = 0, v = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+  return v > 0 ? v : 148;
 }
 
 }  // namespace llmyb
