@@ -590,7 +590,7 @@ def secondary_ep_decode(p: dict, steps: int = 10, warmup: int = 3, global_batch:
     from hybrid_llm_b200 import kernels
     from hybrid_llm_b200.config import large_ep_config
     from hybrid_llm_b200.expert_parallel import ExpertParallel
-    from hybrid_llm_b200.model import GreedyDecoder, LoopedHybridModel
+    from hybrid_llm_b200.model import GreedyDecoder, LoopedHybridModel, PrefillGraph
     from hybrid_llm_b200.state import RecurrentState
     from hybrid_llm_b200.weights import ModelWeights, synthetic_state_dict
 
@@ -668,7 +668,7 @@ def run_ours(args) -> None:
 
     from hybrid_llm_b200 import kernels
     from hybrid_llm_b200.config import small_llmy_config
-    from hybrid_llm_b200.model import GreedyDecoder, LoopedHybridModel
+    from hybrid_llm_b200.model import GreedyDecoder, LoopedHybridModel, PrefillGraph
     from hybrid_llm_b200.weights import ModelWeights, synthetic_state_dict
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -685,7 +685,7 @@ def run_ours(args) -> None:
         cfg, synthetic_state_dict(cfg, seed=0, device="cuda"), "cuda"))
     prompt = torch.from_numpy(np.random.default_rng(0).integers(0, cfg.vocab_size, (bsz, prompt_len))).cuda()
 
-    # prefill (timed separately: prompt tokens/s)
+    # prefill (timed separately: prompt tokens/s), eager and as one graph replay
     model.forward(prompt, last_logits_only=True)
     torch.cuda.synchronize()
     a, b = _events()
@@ -693,7 +693,17 @@ def run_ours(args) -> None:
     out = model.forward(prompt, last_logits_only=True)
     b.record()
     torch.cuda.synchronize()
-    prefill_s = a.elapsed_time(b) * 1e-3
+    prefill_eager_s = a.elapsed_time(b) * 1e-3
+    pgraph = PrefillGraph(model, bsz, prompt_len)
+    ptimes = []
+    for _ in range(5):
+        a, b = _events()
+        a.record()
+        out = pgraph.run(prompt)
+        b.record()
+        torch.cuda.synchronize()
+        ptimes.append(a.elapsed_time(b))
+    prefill_s = float(np.median(ptimes)) * 1e-3
 
     dec = GreedyDecoder(model, out.state, use_graph=True)
     dec.prime(out.logits[:, -1].float().argmax(-1))
@@ -784,9 +794,12 @@ def run_ours(args) -> None:
         "e2e": e2e, "gpu_launches": launches_per_step * args.steps, "roofline": roofline,
         "step_roofline": step_roofline,
         "clocks": clocks.summary(), "prefill_tok_s_c2": bsz * prompt_len / prefill_s,
+        "prefill_c2_note": "one CUDA graph replay of the 512-token forward (median of 5); "
+                           "eager forward (host launch cost included) in prefill_eager_ms",
+        "prefill_eager_ms": prefill_eager_s * 1e3,
         "prefill_roofline": prefill_roofline(model, cfg, prompt_len, prefill_s, p),
     }
-    del dec, out, model
+    del dec, out, model, pgraph
     torch.cuda.empty_cache()
     secondary = {}
     if not args.no_ep:  # every rank: expert parallel over the whole group when N > 1

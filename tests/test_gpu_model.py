@@ -345,3 +345,23 @@ def test_router_context_logits_vs_fp64(cuda):
         want = logits(r[:, t + s], lat[:, t + s - w + 1:t + s + 1].mean(1))
         assert _rel(got, want) < 1e-4, (s, _rel(got, want))
         pos += 1
+
+
+def test_prefill_graph_equals_eager_forward(cuda):
+    """PrefillGraph: each replay starts from a zeroed state and gives the eager
+    forward's logits and state bit for bit, for two different prompts in turn."""
+    from hybrid_llm_b200.model import LoopedHybridModel, PrefillGraph
+    from hybrid_llm_b200.weights import ModelWeights, synthetic_state_dict
+    cfg = inputs.mini_config()
+    m = LoopedHybridModel(ModelWeights.from_state_dict(cfg, synthetic_state_dict(cfg, seed=0), cuda))
+    pg = PrefillGraph(m, 2, 50)
+    rng = np.random.default_rng(4)
+    for _ in range(2):
+        ids = torch.from_numpy(rng.integers(0, cfg.vocab_size, (2, 50))).to(cuda)
+        ref = m.forward(ids, last_logits_only=True)
+        got = pg.run(ids)
+        torch.cuda.synchronize()
+        assert torch.equal(got.logits, ref.logits)
+        a, b = got.state.state_dict(), ref.state.state_dict()
+        assert a.keys() == b.keys()
+        assert all(torch.equal(a[k], b[k]) for k in a)
