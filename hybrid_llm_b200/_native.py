@@ -35,6 +35,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "llmyb_router_topk": (I32, [P, P, I32, I32, I32, P, P, P]),
     "llmyb_moe_plan_scratch_bytes": (I64, [I32, I32]),
     "llmyb_moe_plan": (I32, [P, P, I32, I32, I32, I32, P, P, P, P, P, P, P, P, P, P]),
+    "llmyb_route_norm": (I32, [P, I32, I32, P, P, F32, P, I32, I32, I32, P, P, P, P, P, P, P, P,
+                               P, P, P, P]),
     "llmyb_route": (I32, [P, P, I32, I32, I32, I32, P, P, P, P, P, P, P, P, P, P, P]),
     "llmyb_route_noalloc": (I32, [P, P, I32, I32, I32, I32, P, P, P, P, P, P, P, P, P, P]),
     "llmyb_route_noalloc_max_scratch_ints": (I64, []),

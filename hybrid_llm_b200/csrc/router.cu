@@ -50,6 +50,102 @@ __global__ void __launch_bounds__(256) router_topk_kernel(
   }
 }
 
+// Prefill router from the FFN-normalised rows m [N, D] fp32, eight tokens per
+// 512-thread CTA: warp w < 8 normalises token w into shared memory,
+// r = m * rsqrt(mean(m^2) + eps) * router_norm (ContextAwareRouter's RMSNorm,
+// context_router.py:62-63), while every warp already holds the row of its
+// first expert (w, then w + 16, ...); after the barrier each warp forms the
+// fp32 logits W_r r (F.linear, :65) of all eight tokens from its expert rows
+// (lane-strided float4 products, a fixed xor tree per token); finally warp
+// w < 8 runs the top-k + softmax of router_topk_kernel on token w's logits.
+// VPL: float4 chunks per lane (D <= 128 VPL).
+template <int VPL>
+__global__ void __launch_bounds__(512) router_norm_topk_kernel(
+    const float* __restrict__ m, int N, int D, const float* __restrict__ rn_w, float eps,
+    const float* __restrict__ Wr, const float* __restrict__ bias, int E, int k,
+    float* __restrict__ logits_out, int64_t* __restrict__ topk_idx, float* __restrict__ topk_prob) {
+  constexpr int kTok = 8, kWarps = 16;
+  extern __shared__ float4 s_r4[];             // [8][D / 4] normalised rows
+  __shared__ float s_logit[kTok][kMaxExperts];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int t0 = blockIdx.x * kTok;
+  const int nc = D >> 2;
+  float4 wrow[VPL];  // the first expert row of this warp, loaded before the barrier
+  if (warp < E) {
+    const float4* wr = reinterpret_cast<const float4*>(Wr + static_cast<int64_t>(warp) * D);
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      const int c = lane + 32 * i;
+      wrow[i] = c < nc ? __ldg(wr + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  }
+  if (warp < kTok) {
+    const int t = t0 + warp;
+    float4 r[VPL];
+    float ss = 0.f;
+    const float4* mr = reinterpret_cast<const float4*>(m + static_cast<int64_t>(min(t, N - 1)) * D);
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      const int c = lane + 32 * i;
+      r[i] = (c < nc && t < N) ? __ldg(mr + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+      ss += r[i].x * r[i].x + r[i].y * r[i].y + r[i].z * r[i].z + r[i].w * r[i].w;
+    }
+    const float inv = rsqrtf(warp_sum(ss) / static_cast<float>(D) + eps);
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      const int c = lane + 32 * i;
+      if (c < nc) {
+        const float4 w = __ldg(reinterpret_cast<const float4*>(rn_w) + c);
+        s_r4[warp * nc + c] = make_float4(r[i].x * inv * w.x, r[i].y * inv * w.y,
+                                          r[i].z * inv * w.z, r[i].w * inv * w.w);
+      }
+    }
+  }
+  __syncthreads();
+  for (int e = warp; e < E; e += kWarps) {
+    if (e != warp) {
+      const float4* wr = reinterpret_cast<const float4*>(Wr + static_cast<int64_t>(e) * D);
+#pragma unroll
+      for (int i = 0; i < VPL; ++i) {
+        const int c = lane + 32 * i;
+        wrow[i] = c < nc ? __ldg(wr + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+    float acc[kTok] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      const int c = lane + 32 * i;
+      if (c < nc) {
+        const float4 a = wrow[i];
+#pragma unroll
+        for (int tt = 0; tt < kTok; ++tt) {
+          const float4 b = s_r4[tt * nc + c];
+          acc[tt] += a.x * b.x + a.y * b.y + a.z * b.z + a.w * b.w;
+        }
+      }
+    }
+#pragma unroll
+    for (int tt = 0; tt < kTok; ++tt) {
+      const float v = warp_sum(acc[tt]);
+      if (lane == 0) {
+        s_logit[tt][e] = v;
+        if (logits_out != nullptr && t0 + tt < N) logits_out[static_cast<int64_t>(t0 + tt) * E + e] = v;
+      }
+    }
+  }
+  __syncthreads();
+  const int t = t0 + warp;
+  if (warp >= kTok || t >= N) return;  // whole warps leave together
+  int idx;
+  float val;
+  warp_topk_row(s_logit[warp], bias, E, k, lane, idx, val);
+  const float p = warp_topk_softmax(val, k, lane);
+  if (lane < k) {
+    topk_idx[static_cast<int64_t>(t) * k + lane] = idx;
+    topk_prob[static_cast<int64_t>(t) * k + lane] = p;
+  }
+}
+
 // Histogram only (top-k supplied by the caller, e.g. the reference router).
 __global__ void __launch_bounds__(256) plan_hist_kernel(const int64_t* __restrict__ topk_idx, int N,
                                                         int E, int k, int* __restrict__ hist,
@@ -422,7 +518,7 @@ int32_t route_impl(const float* logits, const float* bias, int32_t n_tokens, int
     count_launch();
     return launch_status();
   }
-  if (n_tokens <= 256 && n_tokens * top_k <= 256 * kMaxTopK / 4) {
+  if (n_tokens * top_k <= 256 * kMaxTopK / 4) {
     // top-k spread over CTAs (one token per warp), then the plan in one CTA
     router_topk_kernel<<<static_cast<int>(ceil_div(n_tokens, 8)), 256, 0, s>>>(
         logits, bias, n_tokens, n_experts, top_k, topk_idx, topk_prob);
@@ -460,6 +556,58 @@ LLMYB_API int32_t llmyb_route(const float* logits, const float* bias, int32_t n_
   return route_impl(logits, bias, n_tokens, n_experts, top_k, tile_m, topk_idx, topk_prob,
                     expert_counts, expert_offsets, tile_offsets, perm_token, perm_prob, route_pos,
                     sort_order, scratch, static_cast<cudaStream_t>(stream));
+}
+
+// Router from the FFN-normalised rows (router RMSNorm + fp32 logits + top-k
+// in one warp-per-token kernel), then the dispatch plan: one CTA for up to
+// 2048 routes, else the chunked multi-CTA plan.
+LLMYB_API int32_t llmyb_route_norm(const float* m, int32_t n_tokens, int32_t d_model,
+                                   const float* router_norm, const float* w_router, float eps,
+                                   const float* bias, int32_t n_experts, int32_t top_k,
+                                   int32_t tile_m, float* logits_out, int64_t* topk_idx,
+                                   float* topk_prob, int32_t* expert_counts,
+                                   int32_t* expert_offsets, int32_t* tile_offsets,
+                                   int32_t* perm_token, float* perm_prob, int32_t* route_pos,
+                                   int64_t* sort_order, void* scratch, void* stream) {
+  int32_t st = check_route_args(n_tokens, n_experts, top_k, tile_m);
+  if (st) return st;
+  if (!expert_counts || !expert_offsets || !tile_offsets) return LLMYB_EINVAL;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (n_tokens == 0) return empty_plan(n_experts, expert_counts, expert_offsets, tile_offsets, s);
+  if (!m || !router_norm || !w_router || !topk_idx || !topk_prob || !perm_token || !perm_prob ||
+      !route_pos)
+    return LLMYB_EINVAL;
+  if (d_model <= 0 || d_model % 4 != 0 || d_model > 1024 ||
+      ((reinterpret_cast<uintptr_t>(m) | reinterpret_cast<uintptr_t>(router_norm) |
+        reinterpret_cast<uintptr_t>(w_router)) & 15u))
+    return LLMYB_EUNSUPPORTED;
+  const int vpl = static_cast<int>(ceil_div(d_model / 4, 32));
+  const int grid = static_cast<int>(ceil_div(n_tokens, 8));
+  const int smem = 8 * d_model * static_cast<int>(sizeof(float));  // <= 32 KB
+  auto go = [&](auto kern) {
+    kern<<<grid, 512, smem, s>>>(m, n_tokens, d_model, router_norm, eps, w_router, bias,
+                                 n_experts, top_k, logits_out, topk_idx, topk_prob);
+  };
+  if (vpl <= 2) go(router_norm_topk_kernel<2>);
+  else if (vpl <= 4) go(router_norm_topk_kernel<4>);
+  else go(router_norm_topk_kernel<8>);
+  count_launch();
+  if (n_tokens * top_k <= 256 * kMaxTopK / 4) {
+    plan_small_kernel<<<1, 1024, 0, s>>>(topk_idx, topk_prob, n_tokens, n_experts, top_k, tile_m,
+                                         expert_counts, expert_offsets, tile_offsets, perm_token,
+                                         perm_prob, route_pos, sort_order);
+    count_launch();
+    return launch_status();
+  }
+  if (!scratch) return LLMYB_EINVAL;
+  const int nchunks = static_cast<int>(ceil_div(n_tokens, kChunk));
+  int* hist = static_cast<int*>(scratch);
+  plan_hist_kernel<<<nchunks, 256, n_experts * sizeof(int), s>>>(topk_idx, n_tokens, n_experts,
+                                                                 top_k, hist, nullptr);
+  count_launch();
+  return plan_tail(topk_idx, topk_prob, n_tokens, n_experts, top_k, tile_m, expert_counts,
+                   expert_offsets, tile_offsets, perm_token, perm_prob, route_pos, sort_order,
+                   hist, s);
 }
 
 // Decode-step router fused with the residual add and the two RMSNorms that

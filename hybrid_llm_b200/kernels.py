@@ -128,6 +128,48 @@ def route(logits: torch.Tensor, k: int, bias: torch.Tensor | None = None, *,
     return RoutePlan(idx, prob, **b, tile_m=tile_m)
 
 
+def route_norm(m: torch.Tensor, router_norm: torch.Tensor, w_router: torch.Tensor, k: int,
+               eps: float, bias: torch.Tensor | None = None, *, tile_m: int = TILE_M,
+               logits_out: torch.Tensor | None = None,
+               with_sort_order: bool = False) -> RoutePlan:
+    """Prefill router (context_router.py:62-65 without the local context) from
+    the FFN-normalised rows m [N, D] fp32: RMSNorm(m) * router_norm, fp32
+    logits w_router [E, D] . r (into logits_out [N, E] if given), top-k +
+    softmax and the dispatch plan."""
+    _require_cuda(m, router_norm, w_router, bias, logits_out)
+    if m.dtype != torch.float32 or w_router.dtype != torch.float32:
+        raise ValueError("route_norm takes fp32 rows and router weights")
+    m = m.contiguous()
+    n, d = m.shape
+    e = w_router.shape[0]
+    if bias is not None:
+        bias = bias.to(torch.float32).contiguous()
+    if logits_out is not None:
+        _inplace(logits_out, "logits_out")
+    dev = m.device
+    idx = torch.empty(n, k, dtype=torch.int64, device=dev)
+    prob = torch.empty(n, k, dtype=torch.float32, device=dev)
+    b = _plan_buffers(n, e, k, dev, with_sort_order)
+    scratch = _plan_scratch(n, e, dev) if n * k > 2048 else None
+    _native.call("llmyb_route_norm", _ptr(m), n, d, _ptr(router_norm.contiguous()),
+                 _ptr(w_router.contiguous()), float(eps), _ptr(bias), e, k, tile_m,
+                 _ptr(logits_out), _ptr(idx), _ptr(prob), _ptr(b["counts"]), _ptr(b["offsets"]),
+                 _ptr(b["tile_offsets"]), _ptr(b["perm_token"]), _ptr(b["perm_prob"]),
+                 _ptr(b["route_pos"]), _ptr(b["sort_order"]), _ptr(scratch), _stream())
+    return RoutePlan(idx, prob, **b, tile_m=tile_m)
+
+
+def route_norm_supported(d_model: int, n_experts: int) -> bool:
+    return d_model % 4 == 0 and d_model <= 1024 and n_experts <= 256
+
+
+def grouped_tile_m(n_rows: int, n_experts: int) -> int:
+    """Rows per grouped-GEMM tile for a plan of n_rows routes: CTA-pair 256-row
+    tiles once the average expert fills one, else single-CTA 128-row tiles
+    (half the padding rows at a few dozen rows per expert)."""
+    return TILE_M if n_rows >= TILE_M * n_experts else 128
+
+
 def router_topk(logits: torch.Tensor, k: int, bias: torch.Tensor | None = None):
     """(indices int64, probabilities fp32) — context_router.py:73-74 semantics."""
     _require_cuda(logits, bias)

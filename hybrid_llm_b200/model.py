@@ -105,8 +105,14 @@ class LoopedHybridModel:
         """SparseMoE.forward (moe.py:172-204): the expert rows and the plan whose
         per-token sum is the combine (added to the residual stream by the next
         add_rmsnorm_routed)."""
-        logits = self._router_logits(blk, m_f32, state, key, bsz, t, step=False)
-        plan = kernels.route(logits, self.cfg.moe_top_k)
+        c = self.cfg
+        tile_m = kernels.grouped_tile_m(bsz * t * c.moe_top_k, c.moe_experts + c.moe_shared)
+        if not c.router_context and kernels.route_norm_supported(c.d_model, c.moe_experts):
+            plan = kernels.route_norm(m_f32, blk.moe.router_norm, blk.moe.router, c.moe_top_k,
+                                      c.rms_eps, tile_m=tile_m)
+        else:
+            logits = self._router_logits(blk, m_f32, state, key, bsz, t, step=False)
+            plan = kernels.route(logits, c.moe_top_k, tile_m=tile_m)
         return self._experts(blk, m_bf, plan)
 
     def _add_pending(self, streams, pending, weight, **out) -> None:

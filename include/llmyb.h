@@ -63,6 +63,21 @@ int32_t llmyb_route(const float* logits, const float* bias, int32_t n_tokens, in
                     int32_t* perm_token, float* perm_prob, int32_t* route_pos,
                     int64_t* sort_order, void* scratch, void* stream);
 
+/* The prefill router of ContextAwareRouter without the local context
+ * (model/layers/context_router.py:62-65) from the FFN-normalised rows
+ * m [N, D] fp32: r = RMSNorm(m) * router_norm, logits = w_router [E, D] . r
+ * (fp32; written to logits_out [N, E] when it is not null), then top-k +
+ * softmax (+ bias before selection, nullable) and the dispatch plan of
+ * llmyb_moe_plan.  D % 4 == 0, D <= 1024, 16-byte aligned m / norm / router;
+ * scratch (llmyb_moe_plan_scratch_bytes) is only read when N*k > 2048. */
+int32_t llmyb_route_norm(const float* m, int32_t n_tokens, int32_t d_model,
+                         const float* router_norm, const float* w_router, float eps,
+                         const float* bias, int32_t n_experts, int32_t top_k, int32_t tile_m,
+                         float* logits_out, int64_t* topk_idx, float* topk_prob,
+                         int32_t* expert_counts, int32_t* expert_offsets, int32_t* tile_offsets,
+                         int32_t* perm_token, float* perm_prob, int32_t* route_pos,
+                         int64_t* sort_order, void* scratch, void* stream);
+
 /* llmyb_route for callers that cannot allocate device memory (a host that
  * hands the library only its input/output buffers, a server whose memory is
  * reserved up front, code running while another allocator owns the heap).

@@ -156,3 +156,28 @@ def test_route_decode_matches_oracle(cuda, n, d, e, k):
         np.testing.assert_array_equal(getattr(plan, f).cpu().numpy(), ref[f], err_msg=f)
     np.testing.assert_array_equal(plan.perm_prob.cpu().numpy(),
                                   plan.topk_prob.cpu().numpy().reshape(-1)[ref["sort_order"]])
+
+
+@pytest.mark.parametrize("n,d,e,k", [(512, 768, 16, 2), (3000, 1024, 64, 8), (7, 256, 8, 2),
+                                     (1, 128, 4, 1), (1100, 512, 32, 2)])
+def test_route_norm_matches_norm_then_route(cuda, n, d, e, k):
+    """llmyb_route_norm (router RMSNorm + fp32 logits + top-k in one kernel, then
+    the plan): logits within fp32 rounding of an fp64 RMSNorm + F.linear, and
+    the routing and plan bit-identical to llmyb_route on those logits (one CTA
+    plan up to 2048 routes, the chunked plan above)."""
+    from hybrid_llm_b200 import kernels
+    g = torch.Generator(device=cuda).manual_seed(n + d)
+    m = torch.randn(n, d, device=cuda, generator=g)
+    rn = 1 + 0.1 * torch.randn(d, device=cuda, generator=g)
+    w = 0.02 * torch.randn(e, d, device=cuda, generator=g)
+    lg = torch.empty(n, e, device=cuda)
+    plan = kernels.route_norm(m, rn, w, k, 1e-6, tile_m=128, logits_out=lg)
+    md = m.double()
+    r = md * torch.rsqrt(md.pow(2).mean(-1, keepdim=True) + 1e-6) * rn.double()
+    ref = r @ w.double().t()
+    err = float((lg.double() - ref).abs().max() / ref.abs().max())
+    assert err < 1e-5, err
+    want = kernels.route(lg, k, tile_m=128)
+    for name in ("topk_idx", "topk_prob", "counts", "offsets", "tile_offsets", "perm_token",
+                 "perm_prob", "route_pos"):
+        assert torch.equal(getattr(plan, name), getattr(want, name)), name
