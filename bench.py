@@ -426,6 +426,65 @@ def secondary_moe(p: dict, reps: int = 10) -> dict:
             "expert_load": counts}
 
 
+def secondary_sampling_router(p: dict, reps: int = 20) -> dict:
+    """The device sampler on a [64, 32000] fp32 logits block (temperature 0.8,
+    top-k 50, top-p 0.9, repetition penalty 1.1 over a seen mask: the
+    sample_standalone.py:5383-5423 path) and the router top-k + dispatch plan
+    of the isolated MoE layer's shape (16,384 tokens x 32 experts, top-4,
+    Zipf(1.1) bias), each timed alone with CUDA events (median), L2 flushed
+    before every call; algorithmic bytes are the logits read plus what the
+    kernels must write."""
+    import numpy as np
+    import torch
+
+    from hybrid_llm_b200 import kernels
+    from oracle.routing import zipf_expert_bias
+
+    g = torch.Generator(device="cuda").manual_seed(0)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+
+    def timed(fn):
+        for _ in range(3):
+            fn()
+        ts = []
+        for _ in range(max(1, reps)):
+            flush.zero_()
+            a, b = _events()
+            a.record()
+            fn()
+            b.record()
+            torch.cuda.synchronize()
+            ts.append(a.elapsed_time(b))
+        return float(np.median(ts)) * 1e-3
+
+    bsz, vocab = 64, 32000
+    logits = torch.randn(bsz, vocab, device="cuda", generator=g) * 3
+    seen = torch.zeros(bsz, (vocab + 31) // 32, dtype=torch.int32, device="cuda")
+    seen[:, :40].random_(generator=g)
+    uni = torch.rand(bsz, device="cuda", generator=g)
+    tok = torch.empty(bsz, dtype=torch.int64, device="cuda")
+    lp = torch.empty(bsz, dtype=torch.float32, device="cuda")
+    t_s = timed(lambda: kernels.sample(logits, temperature=0.8, top_k=50, top_p=0.9,
+                                       repetition_penalty=1.1, seen=seen, uniforms=uni, out=tok,
+                                       logprob=lp))
+    s_bytes = bsz * vocab * 4 + seen.numel() * 4 + bsz * 12
+
+    n, e, k = 16384, 32, 4
+    rl = torch.randn(n, e, device="cuda", generator=g) * 0.5
+    bias = torch.from_numpy(zipf_expert_bias(e)).cuda()
+    t_r = timed(lambda: kernels.route(rl, k, bias))
+    # logits read; top-k ids (8 B) + probs, the permutation's token, prob and
+    # route position (4 B each) written per route; counts / offsets negligible
+    r_bytes = n * e * 4 + n * k * (8 + 4) + n * k * (4 + 4 + 4)
+    return {"workload": "sampler [64, 32000] fp32 (T 0.8, top-k 50, top-p 0.9, rep 1.1); "
+                        "router top-k + plan 16384 x 32 top-4 (Zipf bias)",
+            "sample_us": t_s * 1e6, "sample_gbs": s_bytes / t_s / 1e9,
+            "sample_frac_of_hbm": s_bytes / t_s / 1e9 / p["hbm_gbs"],
+            "route_us": t_r * 1e6, "route_gbs": r_bytes / t_r / 1e9,
+            "route_frac_of_hbm": r_bytes / t_r / 1e9 / p["hbm_gbs"],
+            "algorithmic_bytes": {"sample": s_bytes, "route": r_bytes}}
+
+
 def secondary_mhc(p: dict, reps: int = 10) -> dict:
     """Hyper-connection read / write around one sub-layer: 16384 tokens x D=1024
     with 4 fp32 streams (256 MB, above L2), L2 flushed before each timed call.
@@ -810,6 +869,7 @@ def run_ours(args) -> None:
         secondary["moe_layer"] = secondary_moe(p)
         secondary["long_prefill"] = secondary_prefill(p)
         secondary["mhc"] = secondary_mhc(p)
+        secondary["sampling_router"] = secondary_sampling_router(p)
     if secondary:
         line["secondary"] = secondary
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -899,7 +959,7 @@ def main() -> None:
     ap.add_argument("--ep-exchange", choices=["p2p", "nccl"], default="p2p",
                     help="expert-parallel exchange of --only ep_decode")
     ap.add_argument("--only", choices=["single_block", "moe_layer", "long_prefill", "ep_decode",
-                                       "mhc"],
+                                       "mhc", "sampling_router"],
                     default=None,
                     help="run one secondary workload alone (used for kernel profiles)")
     ap.add_argument("--prefill-batch", type=int, default=8,
@@ -930,6 +990,8 @@ def main() -> None:
             res = secondary_prefill(peaks(), reps=args.steps, batch=args.prefill_batch)
         elif args.only == "single_block":
             res = secondary_block(peaks(), reps=args.steps)
+        elif args.only == "sampling_router":
+            res = secondary_sampling_router(peaks())
         elif args.only == "mhc":
             res = secondary_mhc(peaks(), reps=args.steps)
         else:

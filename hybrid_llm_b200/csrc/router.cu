@@ -34,6 +34,7 @@ using namespace rdev;
 
 
 
+template <int P>
 __global__ void __launch_bounds__(256) router_topk_kernel(
     const float* __restrict__ logits, const float* __restrict__ bias, int N, int E, int k,
     int64_t* __restrict__ topk_idx, float* __restrict__ topk_prob) {
@@ -42,7 +43,7 @@ __global__ void __launch_bounds__(256) router_topk_kernel(
   if (t >= N) return;
   int idx;
   float val;
-  warp_topk_row(logits + static_cast<int64_t>(t) * E, bias, E, k, lane, idx, val);
+  warp_topk_row<P>(logits + static_cast<int64_t>(t) * E, bias, E, k, lane, idx, val);
   const float p = warp_topk_softmax(val, k, lane);
   if (lane < k) {
     topk_idx[static_cast<int64_t>(t) * k + lane] = idx;
@@ -418,6 +419,22 @@ bool router_aligned(const void* streams, const void* delta, const void* ffn_norm
          ((reinterpret_cast<uintptr_t>(delta) | reinterpret_cast<uintptr_t>(m_bf)) & 7u) == 0;
 }
 
+// router_topk_kernel with the fewest expert slots per lane that hold E
+void launch_router_topk(const float* logits, const float* bias, int N, int E, int k,
+                        int64_t* topk_idx, float* topk_prob, cudaStream_t s) {
+  const dim3 grid(static_cast<unsigned>(ceil_div(N, 8)));
+  if (E <= 32)
+    router_topk_kernel<1><<<grid, 256, 0, s>>>(logits, bias, N, E, k, topk_idx, topk_prob);
+  else if (E <= 64)
+    router_topk_kernel<2><<<grid, 256, 0, s>>>(logits, bias, N, E, k, topk_idx, topk_prob);
+  else if (E <= 128)
+    router_topk_kernel<4><<<grid, 256, 0, s>>>(logits, bias, N, E, k, topk_idx, topk_prob);
+  else
+    router_topk_kernel<kMaxPerLane><<<grid, 256, 0, s>>>(logits, bias, N, E, k, topk_idx,
+                                                         topk_prob);
+  count_launch();
+}
+
 int32_t check_route_args(int N, int E, int k, int tile_m) {
   if (N < 0 || E <= 0 || k <= 0 || k > E || tile_m <= 0) return LLMYB_EINVAL;
   if (k > kMaxTopK || E > kMaxExperts) return LLMYB_EUNSUPPORTED;
@@ -436,10 +453,7 @@ LLMYB_API int32_t llmyb_router_topk(const float* logits, const float* bias, int3
   if (st) return st;
   if (n_tokens == 0) return LLMYB_OK;
   if (!logits || !topk_idx || !topk_prob) return LLMYB_EINVAL;
-  router_topk_kernel<<<static_cast<int>(ceil_div(n_tokens, 8)), 256, 0,
-                       static_cast<cudaStream_t>(stream)>>>(logits, bias, n_tokens, n_experts,
-                                                            top_k, topk_idx, topk_prob);
-  count_launch();
+  launch_router_topk(logits, bias, n_tokens, n_experts, top_k, topk_idx, topk_prob, static_cast<cudaStream_t>(stream));
   return launch_status();
 }
 
@@ -520,9 +534,7 @@ int32_t route_impl(const float* logits, const float* bias, int32_t n_tokens, int
   }
   if (n_tokens * top_k <= 256 * kMaxTopK / 4) {
     // top-k spread over CTAs (one token per warp), then the plan in one CTA
-    router_topk_kernel<<<static_cast<int>(ceil_div(n_tokens, 8)), 256, 0, s>>>(
-        logits, bias, n_tokens, n_experts, top_k, topk_idx, topk_prob);
-    count_launch();
+    launch_router_topk(logits, bias, n_tokens, n_experts, top_k, topk_idx, topk_prob, s);
     plan_small_kernel<<<1, 1024, 0, s>>>(topk_idx, topk_prob, n_tokens, n_experts, top_k, tile_m,
                                          expert_counts, expert_offsets, tile_offsets, perm_token,
                                          perm_prob, route_pos, sort_order);
@@ -532,9 +544,7 @@ int32_t route_impl(const float* logits, const float* bias, int32_t n_tokens, int
   if (!scratch) return LLMYB_EINVAL;
   const int nchunks = static_cast<int>(ceil_div(n_tokens, kChunk));
   int* hist = static_cast<int*>(scratch);
-  router_topk_kernel<<<static_cast<int>(ceil_div(n_tokens, 8)), 256, 0, s>>>(
-      logits, bias, n_tokens, n_experts, top_k, topk_idx, topk_prob);
-  count_launch();
+  launch_router_topk(logits, bias, n_tokens, n_experts, top_k, topk_idx, topk_prob, s);
   plan_hist_kernel<<<nchunks, 256, n_experts * sizeof(int), s>>>(topk_idx, n_tokens, n_experts,
                                                                  top_k, hist, nullptr);
   count_launch();
@@ -866,9 +876,7 @@ LLMYB_API int32_t llmyb_route_decode(float* streams, const void* delta, int32_t 
   router_pair_logits_kernel<<<static_cast<int>(ceil_div(n_tokens * n_experts, 8)), 256, 0, s>>>(
       r, w_router, n_tokens, d_model, n_experts, logits);
   count_launch();
-  router_topk_kernel<<<static_cast<int>(ceil_div(n_tokens, 8)), 256, 0, s>>>(
-      logits, nullptr, n_tokens, n_experts, top_k, topk_idx, topk_prob);
-  count_launch();
+  launch_router_topk(logits, nullptr, n_tokens, n_experts, top_k, topk_idx, topk_prob, s);
   plan_small_kernel<<<1, 1024, 0, s>>>(topk_idx, topk_prob, n_tokens, n_experts, top_k, tile_m,
                                        expert_counts, expert_offsets, tile_offsets, perm_token,
                                        perm_prob, route_pos, nullptr);

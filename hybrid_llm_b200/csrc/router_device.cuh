@@ -18,13 +18,15 @@ constexpr int kMaxPerLane = 8;     // experts per lane -> E <= 256
 constexpr int kMaxExperts = 32 * kMaxPerLane;
 
 // Warp-cooperative top-k over one row of E logits.  Returns, in lane s < k,
-// the index and value of the s-th selected expert.
+// the index and value of the s-th selected expert.  P: expert slots per lane
+// (E <= 32 P); fewer slots only skip slots that hold no expert.
+template <int P = kMaxPerLane>
 __device__ __forceinline__ void warp_topk_row(const float* __restrict__ row,
                                               const float* __restrict__ bias, int E, int k,
                                               int lane, int& out_idx, float& out_val) {
-  float v[kMaxPerLane];
+  float v[P];
 #pragma unroll
-  for (int j = 0; j < kMaxPerLane; ++j) {
+  for (int j = 0; j < P; ++j) {
     const int e = j * 32 + lane;
     float x = -INFINITY;
     if (e < E) {
@@ -41,7 +43,7 @@ __device__ __forceinline__ void warp_topk_row(const float* __restrict__ row,
     float best = -INFINITY;
     int best_e = 0x7fffffff;  // sentinel: no candidate in this lane
 #pragma unroll
-    for (int j = 0; j < kMaxPerLane; ++j) {
+    for (int j = 0; j < P; ++j) {
       const int e = j * 32 + lane;
       // e grows with j, so the first candidate wins ties inside a lane
       if (e < E && !((taken >> j) & 1u) && (best_e == 0x7fffffff || v[j] > best)) {
