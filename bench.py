@@ -485,6 +485,40 @@ def secondary_sampling_router(p: dict, reps: int = 20) -> dict:
             "algorithmic_bytes": {"sample": s_bytes, "route": r_bytes}}
 
 
+def secondary_prefill_c2(p: dict, reps: int = 10) -> dict:
+    """The c2 prompt alone: the small LLMY model's 512-token prefill captured as
+    one CUDA graph (PrefillGraph), replayed `reps` times inside the NVTX range
+    "prefill_graph_timed" (for launch lists), CUDA events, median."""
+    import numpy as np
+    import torch
+
+    from hybrid_llm_b200.config import small_llmy_config
+    from hybrid_llm_b200.model import LoopedHybridModel, PrefillGraph
+    from hybrid_llm_b200.weights import ModelWeights, synthetic_state_dict
+
+    cfg = small_llmy_config()
+    model = LoopedHybridModel(ModelWeights.from_state_dict(
+        cfg, synthetic_state_dict(cfg, seed=0, device="cuda"), "cuda"))
+    prompt = torch.from_numpy(np.random.default_rng(0).integers(0, cfg.vocab_size, (1, 512))).cuda()
+    pg = PrefillGraph(model, 1, 512)
+    for _ in range(3):
+        pg.run(prompt)
+    torch.cuda.synchronize()
+    ts = []
+    torch.cuda.nvtx.range_push("prefill_graph_timed")
+    for _ in range(max(1, reps)):
+        a, b = _events()
+        a.record()
+        pg.run(prompt)
+        b.record()
+        torch.cuda.synchronize()
+        ts.append(a.elapsed_time(b))
+    torch.cuda.nvtx.range_pop()
+    t = float(np.median(ts)) * 1e-3
+    return {"workload": "small-llmy prefill, 512-token prompt, B=1, one CUDA graph replay",
+            "ms": t * 1e3, "tok_s": 512 / t, "roofline": prefill_roofline(model, cfg, 512, t, p)}
+
+
 def secondary_mhc(p: dict, reps: int = 10) -> dict:
     """Hyper-connection read / write around one sub-layer: 16384 tokens x D=1024
     with 4 fp32 streams (256 MB, above L2), L2 flushed before each timed call.
@@ -959,7 +993,7 @@ def main() -> None:
     ap.add_argument("--ep-exchange", choices=["p2p", "nccl"], default="p2p",
                     help="expert-parallel exchange of --only ep_decode")
     ap.add_argument("--only", choices=["single_block", "moe_layer", "long_prefill", "ep_decode",
-                                       "mhc", "sampling_router"],
+                                       "mhc", "sampling_router", "prefill_c2"],
                     default=None,
                     help="run one secondary workload alone (used for kernel profiles)")
     ap.add_argument("--prefill-batch", type=int, default=8,
@@ -990,6 +1024,8 @@ def main() -> None:
             res = secondary_prefill(peaks(), reps=args.steps, batch=args.prefill_batch)
         elif args.only == "single_block":
             res = secondary_block(peaks(), reps=args.steps)
+        elif args.only == "prefill_c2":
+            res = secondary_prefill_c2(peaks())
         elif args.only == "sampling_router":
             res = secondary_sampling_router(peaks())
         elif args.only == "mhc":
