@@ -16,13 +16,17 @@
 //              score buffers, then O += P_{g-1} V_{g-1}: the products are
 //              issued one block apart, so the softmax of block g overlaps the
 //              PV product of block g-1 and the score product of block g+1.
-//   warps 2-5  softmax, one query row per thread (= TMEM lane): scores from
-//              TMEM, the band mask on the edge blocks, base-2 online softmax
-//              with a lazily raised running max (O is rescaled in TMEM only
-//              when a block max exceeds the running max by more than 2^8, so
-//              P <= 256 and rescales are rare), P as bf16 into shared memory in
-//              the 128-byte-swizzled K-major layout of an MMA A operand; at the
-//              end of the unit O / l goes to global memory.
+//   warps 2-9  softmax, two warps per TMEM lane quarter (query rows = TMEM
+//              lanes): each owns 64 of the block's 128 key columns and half of
+//              O's columns.  Scores from TMEM, the band mask on the edge
+//              blocks, base-2 online softmax with a lazily raised running max
+//              shared by the pair (each exchanges its partial block max,
+//              rounded up to bf16, through shared memory and a 64-thread named
+//              barrier; O is rescaled in TMEM only when a block max exceeds the
+//              running max by more than 2^8, so P <= 256 and rescales are
+//              rare), P as bf16 into shared memory in the 128-byte-swizzled
+//              K-major layout of an MMA A operand; at the end of the unit the
+//              pair adds its two row sums and writes O / l to global memory.
 // The PV product reads V in its natural [key][dh] layout as an MN-major B
 // operand.  TMEM: O in columns [0, D), score buffers at [128, 256), [256, 384).
 // Every wait is bounded (1 s): a timeout records LLMYB_ETIMEOUT in the status
@@ -47,7 +51,8 @@ struct BandTcLayout {
   static constexpr int kV = 4 * kTile;         // 2 V stages
   static constexpr int kP = 6 * kTile;         // P (one buffer)
   static constexpr int kBar = kP + kPBytes;
-  static constexpr int kSmem = kBar + 256 + 1024;  // + barriers + alignment slack
+  static constexpr int kX = kBar + 256;        // softmax pair exchange: 1 KB
+  static constexpr int kSmem = kX + 1024 + 1024;  // + alignment slack
 };
 
 struct BandUnit {
@@ -66,7 +71,7 @@ __device__ __forceinline__ BandUnit band_unit(int u, int nqt, int H, int W) {
 }
 
 template <int D>
-__global__ void __launch_bounds__(192, 1) band_tc_kernel(
+__global__ void __launch_bounds__(320, 1) band_tc_kernel(
     const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
     const __grid_constant__ CUtensorMap map_v, int v_heads, int B, int T, int H, int W,
     float scale_log2, __nv_bfloat16* __restrict__ out, int64_t so, int32_t* dev_status) {
@@ -87,7 +92,8 @@ __global__ void __launch_bounds__(192, 1) band_tc_kernel(
   uint64_t* pv_done = bars + 17;
   uint64_t* o_empty = bars + 18;
   uint64_t* mma_done = bars + 19;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 20);
+  uint64_t* pair_bar = bars + 20;  // [4]: the two softmax warps of a TMEM lane quarter
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 24);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -103,12 +109,13 @@ __global__ void __launch_bounds__(192, 1) band_tc_kernel(
       sm100::mbar_init(&v_full[i], 1);
       sm100::mbar_init(&v_empty[i], 1);
       sm100::mbar_init(&s_full[i], 1);
-      sm100::mbar_init(&s_empty[i], 4);  // one arrival per softmax warp
+      sm100::mbar_init(&s_empty[i], 8);  // one arrival per softmax warp
     }
-    sm100::mbar_init(p_full, 4);
+    sm100::mbar_init(p_full, 8);
     sm100::mbar_init(pv_done, 1);
-    sm100::mbar_init(o_empty, 4);
+    sm100::mbar_init(o_empty, 8);
     sm100::mbar_init(mma_done, 1);
+    for (int i = 0; i < 4; ++i) sm100::mbar_init(&pair_bar[i], 2);
     *abort_flag = 0;
     sm100::fence_mbar_init();
     sm100::tma_prefetch_desc(&map_q);
@@ -266,9 +273,24 @@ __global__ void __launch_bounds__(192, 1) band_tc_kernel(
     sm100::mbar_wait_warp(mma_done, 0, dev_status, nullptr);
   } else {
     // --------------------------------------------------------- softmax
-    const int qw = warp & 3;  // TMEM lane quarter of this warp
+    const int qw = warp & 3;            // TMEM lane quarter of this warp
+    const int half = (warp - 2) >> 2;   // key columns [64 half, +64), O columns [D/2 half, +D/2)
     const int row = qw * 32 + lane;
     const uint32_t t_lane = tmem_base + (static_cast<uint32_t>(qw * 32) << 16);
+    // the pair (warps qw + 2 and qw + 6) meets on pair_bar[qw]: both warps
+    // arrive once per meeting and wait (bounded) for the meeting's phase
+    uint32_t meets = 0;
+    auto pair_meet = [&]() -> bool {
+      __syncwarp();
+      if (lane == 0) sm100::mbar_arrive(&pair_bar[qw]);
+      const bool r = sm100::mbar_wait_warp(&pair_bar[qw], meets & 1u, dev_status, abort_flag);
+      __syncwarp();  // every lane's later reads follow lane 0's acquire
+      ++meets;
+      return r;
+    };
+    // exchange: [parity][half][row] bf16 block maxima; at a unit's end [half][row] fp32 sums
+    uint16_t* xmax = reinterpret_cast<uint16_t*>(smem + L::kX);
+    float* xsum = reinterpret_cast<float*>(smem + L::kX);
     uint8_t* prow = smem + L::kP + row * 128;
     const int pswz = row & 7;
     int g = 0;
@@ -284,37 +306,49 @@ __global__ void __launch_bounds__(192, 1) band_tc_kernel(
           break;
         }
         sm100::tc_fence_after();
-        uint32_t sr[4][32];
+        uint32_t sr[2][32];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) sm100::tmem_ld_32x32b_x32(t_lane + 128 + sb * 128 + 32 * c, sr[c]);
+        for (int c = 0; c < 2; ++c)
+          sm100::tmem_ld_32x32b_x32(t_lane + 128 + sb * 128 + half * 64 + 32 * c, sr[c]);
         sm100::tmem_ld_wait();
 #pragma unroll
-        for (int c = 0; c < 4; ++c) sm100::tmem_regs_ready(sr[c]);
+        for (int c = 0; c < 2; ++c) sm100::tmem_regs_ready(sr[c]);
         sm100::tc_fence_before();
         __syncwarp();
         if (lane == 0) sm100::mbar_arrive(&s_empty[sb]);
 
-        const int j0 = (x.kb0 + i) * kRows;
-        if ((j0 + kRows - 1 > q0) || (q0 + kRows - 1 - j0 >= W)) {
-          // band edge: key column c is visible iff lo <= c <= hi
+        const int j0 = (x.kb0 + i) * kRows + half * 64;
+        if ((x.kb0 + i) * kRows + kRows - 1 > q0 || q0 + kRows - 1 - (x.kb0 + i) * kRows >= W) {
+          // band edge: key column c of this half is visible iff lo <= c <= hi
           const int lo = t - W + 1 - j0, hi = t - j0;
 #pragma unroll
-          for (int c = 0; c < 4; ++c)
+          for (int c = 0; c < 2; ++c)
 #pragma unroll
             for (int e = 0; e < 32; ++e)
               if (32 * c + e < lo || 32 * c + e > hi) sr[c][e] = __float_as_uint(-INFINITY);
         }
-        // row max of the raw scores (the scale is positive), 8 independent chains
+        // partial row max of the raw scores (the scale is positive)
         float mx[8];
 #pragma unroll
         for (int a = 0; a < 8; ++a) mx[a] = -INFINITY;
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
+        for (int c = 0; c < 2; ++c)
 #pragma unroll
           for (int e = 0; e < 32; ++e) mx[e & 7] = fmaxf(mx[e & 7], __uint_as_float(sr[c][e]));
-        const float bm = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+        const float pm = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
                                fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))) *
                          scale_log2;
+        // both warps of the pair form the block max from the same two bf16
+        // values (rounded up, so m stays an upper bound of the row's scores)
+        const __nv_bfloat16 pmb = __float2bfloat16_ru(pm);
+        xmax[((g & 1) * 2 + half) * 128 + row] = *reinterpret_cast<const uint16_t*>(&pmb);
+        if (!pair_meet()) {
+          ok = false;
+          break;
+        }
+        const uint16_t o0 = xmax[((g & 1) * 2) * 128 + row], o1 = xmax[((g & 1) * 2 + 1) * 128 + row];
+        const float bm = fmaxf(__uint_as_float(static_cast<uint32_t>(o0) << 16),
+                               __uint_as_float(static_cast<uint32_t>(o1) << 16));
         const bool need = bm > m + 8.f;
         float alpha = 1.f;
         if (need) {
@@ -325,7 +359,7 @@ __global__ void __launch_bounds__(192, 1) band_tc_kernel(
         const float nbase = m == -INFINITY ? 0.f : -m;
         float rs[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
+        for (int c = 0; c < 2; ++c)
 #pragma unroll
           for (int e = 0; e < 32; ++e) {
             const float p = fast_exp2(fmaf(__uint_as_float(sr[c][e]), scale_log2, nbase));
@@ -339,28 +373,30 @@ __global__ void __launch_bounds__(192, 1) band_tc_kernel(
           break;
         }
 #pragma unroll
-        for (int kc = 0; kc < 16; ++kc) {
+        for (int kc = 0; kc < 8; ++kc) {
           const int c = kc >> 2, e = (kc & 3) * 8;
           uint4 w;
           w.x = pack_bf16x2(__uint_as_float(sr[c][e + 0]), __uint_as_float(sr[c][e + 1]));
           w.y = pack_bf16x2(__uint_as_float(sr[c][e + 2]), __uint_as_float(sr[c][e + 3]));
           w.z = pack_bf16x2(__uint_as_float(sr[c][e + 4]), __uint_as_float(sr[c][e + 5]));
           w.w = pack_bf16x2(__uint_as_float(sr[c][e + 6]), __uint_as_float(sr[c][e + 7]));
-          *reinterpret_cast<uint4*>(prow + (kc >> 3) * kBox + (((kc & 7) ^ pswz) << 4)) = w;
+          *reinterpret_cast<uint4*>(prow + half * kBox + ((kc ^ pswz) << 4)) = w;
         }
         sm100::fence_proxy_async_smem();
         if (__any_sync(0xffffffffu, need && i > 0)) {
-          // O holds the products of blocks < i (block g-1 is complete)
+          // O holds the products of blocks < i (block g-1 is complete); this
+          // warp rescales its half of O's columns
           sm100::tc_fence_after();
 #pragma unroll 1
-          for (int c = 0; c < D / 32; ++c) {
+          for (int c = 0; c < D / 64; ++c) {
             uint32_t o[32];
-            sm100::tmem_ld_32x32b_x32(t_lane + 32 * c, o);
+            const uint32_t col = static_cast<uint32_t>(half * (D / 2) + 32 * c);
+            sm100::tmem_ld_32x32b_x32(t_lane + col, o);
             sm100::tmem_ld_wait();
             sm100::tmem_regs_ready(o);
 #pragma unroll
             for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-            sm100::tmem_st_32x32b_x32(t_lane + 32 * c, o);
+            sm100::tmem_st_32x32b_x32(t_lane + col, o);
           }
           sm100::tmem_st_wait();
         }
@@ -370,14 +406,21 @@ __global__ void __launch_bounds__(192, 1) band_tc_kernel(
       }
       if (!ok) break;
       // ---------------------------------------------------- epilogue
+      // the pair's two partial row sums, in the exchange area once both warps
+      // have read this unit's last block maxima
+      if (!pair_meet()) break;
+      xsum[half * 128 + row] = l;
+      if (!pair_meet()) break;
+      const float inv = 1.f / (xsum[row] + xsum[128 + row]);
+      if (!pair_meet()) break;  // read before the next unit's first exchange overwrites
       if (!sm100::mbar_wait_warp(pv_done, (g - 1) & 1, dev_status, abort_flag)) break;
       sm100::tc_fence_after();
-      const float inv = 1.f / l;
       __nv_bfloat16* dst = out + (static_cast<int64_t>(x.b) * T + t) * so + x.h * D;
 #pragma unroll 1
-      for (int c = 0; c < D / 32; ++c) {
+      for (int c = 0; c < D / 64; ++c) {
         uint32_t o[32];
-        sm100::tmem_ld_32x32b_x32(t_lane + 32 * c, o);
+        const int col = half * (D / 2) + 32 * c;
+        sm100::tmem_ld_32x32b_x32(t_lane + col, o);
         sm100::tmem_ld_wait();
         sm100::tmem_regs_ready(o);
         if (t < T) {
@@ -388,7 +431,7 @@ __global__ void __launch_bounds__(192, 1) band_tc_kernel(
             w.y = pack_bf16x2(__uint_as_float(o[8 * v + 2]) * inv, __uint_as_float(o[8 * v + 3]) * inv);
             w.z = pack_bf16x2(__uint_as_float(o[8 * v + 4]) * inv, __uint_as_float(o[8 * v + 5]) * inv);
             w.w = pack_bf16x2(__uint_as_float(o[8 * v + 6]) * inv, __uint_as_float(o[8 * v + 7]) * inv);
-            reinterpret_cast<uint4*>(dst + 32 * c)[v] = w;
+            reinterpret_cast<uint4*>(dst + col)[v] = w;
           }
         }
       }
@@ -422,7 +465,7 @@ int32_t launch_band_tc(const void* q, int64_t sq, const void* k, int64_t sk, con
   const int64_t units = static_cast<int64_t>(B) * H * ((T + kRows - 1) / kRows);
   const int grid = static_cast<int>(std::min<int64_t>(units, num_sms()));
   constexpr float kLog2e = 1.4426950408889634f;
-  band_tc_kernel<D><<<grid, 192, L::kSmem, stream>>>(mq, mk, mv, v_heads, B, T, H, W,
+  band_tc_kernel<D><<<grid, 320, L::kSmem, stream>>>(mq, mk, mv, v_heads, B, T, H, W,
                                                      scale * kLog2e,
                                                      static_cast<__nv_bfloat16*>(out), so,
                                                      dev_status);
