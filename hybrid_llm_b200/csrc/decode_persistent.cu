@@ -438,8 +438,8 @@ __global__ void __launch_bounds__(kPT, 1) decode_persistent_kernel(const llmyb_p
             const float l = warp_sum(lane < nkl ? exp2f(s - m) : 0.f);
             if (lane < nkl) __stcg(p.scores + warp * W + cta * kPW + lane, s);
             if (lane == 0) {
-              __stcg(p.stats + (cta * Hc + warp) * 2, m);
-              __stcg(p.stats + (cta * Hc + warp) * 2 + 1, l);
+              // [head][key chunk][max, sum]: a head's chunks are contiguous for M2
+              __stcg(reinterpret_cast<float2*>(p.stats) + warp * G + cta, make_float2(m, l));
             }
           }
         }
@@ -465,12 +465,15 @@ __global__ void __launch_bounds__(kPT, 1) decode_persistent_kernel(const llmyb_p
           float sm0 = -INFINITY, sl0 = 0.f, sm1 = -INFINITY, sl1 = 0.f;
           if (warp < Hc) {
             if (lane < nk1) {
-              sm0 = __ldcg(p.stats + (lane * Hc + warp) * 2);
-              sl0 = __ldcg(p.stats + (lane * Hc + warp) * 2 + 1);
+              const float2 st0 = __ldcg(reinterpret_cast<const float2*>(p.stats) + warp * G + lane);
+              sm0 = st0.x;
+              sl0 = st0.y;
             }
             if (lane + 32 < nk1) {
-              sm1 = __ldcg(p.stats + ((lane + 32) * Hc + warp) * 2);
-              sl1 = __ldcg(p.stats + ((lane + 32) * Hc + warp) * 2 + 1);
+              const float2 st1 =
+                  __ldcg(reinterpret_cast<const float2*>(p.stats) + warp * G + lane + 32);
+              sm1 = st1.x;
+              sl1 = st1.y;
             }
           }
           const float xold = tid < 8 ? __ldcg(xdst + col0 + tid) : 0.f;
@@ -539,7 +542,7 @@ __global__ void __launch_bounds__(kPT, 1) decode_persistent_kernel(const llmyb_p
             a += __shfl_xor_sync(0xffffffffu, a, 4);
             a += __shfl_xor_sync(0xffffffffu, a, 2);
             a += __shfl_xor_sync(0xffffffffu, a, 1);
-            if ((tid & 7) == 0 && tid < 8 * E) __stcg(p.partials + cta * NV + 2 + (tid >> 3), a);
+            if ((tid & 7) == 0 && tid < 8 * E) __stcg(p.partials + (2 + (tid >> 3)) * G + cta, a);
           }
           if (warp == 0) {
             const float x = tid < 8 ? sm.xrow[tid] : 0.f;
@@ -551,8 +554,8 @@ __global__ void __launch_bounds__(kPT, 1) decode_persistent_kernel(const llmyb_p
             b += __shfl_xor_sync(0xffffffffu, b, 2);
             b += __shfl_xor_sync(0xffffffffu, b, 1);
             if (lane == 0) {
-              __stcg(p.partials + cta * NV, a);
-              __stcg(p.partials + cta * NV + 1, b);
+              __stcg(p.partials + cta, a);
+              __stcg(p.partials + G + cta, b);
             }
           }
         }
@@ -702,7 +705,7 @@ __global__ void __launch_bounds__(kPT, 1) decode_persistent_kernel(const llmyb_p
           if (cta < n_part && tid < NV) {
             float a = 0.f;
             for (int w = 0; w < kPW; ++w) a += sm.part[w][tid];
-            __stcg(p.partials + cta * NV + tid, a);
+            __stcg(p.partials + tid * G + cta, a);
           }
           gb.arrive();
         }
@@ -715,31 +718,26 @@ __global__ void __launch_bounds__(kPT, 1) decode_persistent_kernel(const llmyb_p
           fwb = __ldg(reinterpret_cast<const float4*>(B.ffn_norm) + 2 * tid + 1);
         }
         if (!gb.wait()) return;
-        // the router partial sums of all producing CTAs and the residual row in
-        // one round of loads: thread t < 8 NV sums slots t % 8, t % 8 + 8, ...
-        // of value t / 8 in registers, then a fixed xor tree (the same order in
-        // every CTA, so all of them route identically)
-        constexpr int kSlots = 128 / 8;
+        // the router partial sums of all producing CTAs ([value][slot], slot =
+        // producing CTA) and the residual row in one round of loads: warp w sums
+        // values w, w + 16, ... over the slots lane, lane + 32, ... (each load
+        // one contiguous line), then a fixed xor tree (the same order in every
+        // CTA, so all of them route identically)
         float4 xa = make_float4(0.f, 0.f, 0.f, 0.f), xb4 = xa;
         if (tid < n8) {
           xa = __ldcg(reinterpret_cast<const float4*>(xdst) + 2 * tid);
           xb4 = __ldcg(reinterpret_cast<const float4*>(xdst) + 2 * tid + 1);
         }
-        if (warp < (8 * NV + 31) / 32) {  // warp-uniform: the shuffles see full warps
-          const int v = tid >> 3, part = tid & 7;
-          float t16[kSlots];
+        for (int v = warp; v < NV; v += kPW) {  // warp-uniform
+          const float* pv = p.partials + v * G;
+          float t4[4];
 #pragma unroll
-          for (int u = 0; u < kSlots; ++u) {
-            const int s_ = part + 8 * u;
-            t16[u] = (tid < 8 * NV && s_ < n_part) ? __ldcg(p.partials + s_ * NV + v) : 0.f;
+          for (int u = 0; u < 4; ++u) {  // n_part <= 128 slots
+            const int s_ = lane + 32 * u;
+            t4[u] = s_ < n_part ? __ldcg(pv + s_) : 0.f;
           }
-          float a = 0.f;
-#pragma unroll
-          for (int u = 0; u < kSlots; ++u) a += t16[u];
-          a += __shfl_xor_sync(0xffffffffu, a, 4);
-          a += __shfl_xor_sync(0xffffffffu, a, 2);
-          a += __shfl_xor_sync(0xffffffffu, a, 1);
-          if (part == 0 && tid < 8 * NV) {
+          const float a = warp_sum((t4[0] + t4[1]) + (t4[2] + t4[3]));
+          if (lane == 0) {
             if (v < 2) sm.scal[v] = a; else sm.logit[v - 2] = a;
           }
         }

@@ -159,9 +159,9 @@ class PersistentDecode:
         self.proj = torch.zeros(rows, **bf)
         self.normed = torch.zeros(d, **bf)
         self.scores = torch.zeros(max(hc, 1), max(c.csa_window, 1), **f32)
-        self.stats = torch.zeros(self.grid, max(hc, 1), 2, **f32)
+        self.stats = torch.zeros(max(hc, 1), self.grid, 2, **f32)
         self.mix = torch.zeros(max(d, c.gdn_heads * c.gdn_value_dim), **bf)
-        self.partials = torch.zeros(self.grid, 2 + e, **f32)
+        self.partials = torch.zeros(2 + e, self.grid, **f32)
         self.hbuf = torch.zeros(k, f, **bf)
         self.ybuf = torch.zeros(k, d, **bf)
         self.collapsed = torch.zeros(d, **bf)

@@ -708,9 +708,9 @@ typedef struct {
   void* proj;                   /* scratch [max rows] bf16 */
   void* normed;                 /* scratch [D] bf16 */
   float* scores;                /* scratch [csa_heads, window] */
-  float* stats;                 /* scratch [grid, csa_heads, 2] */
+  float* stats;                 /* scratch [csa_heads, grid, 2] (8-byte aligned) */
   void* mix;                    /* scratch [max(D, gdn_heads*gdn_dim)] bf16 */
-  float* partials;              /* scratch [grid, 2 + E] */
+  float* partials;               /* scratch [2 + E, grid] */
   void* hbuf;                   /* scratch [top_k, F] bf16 */
   void* ybuf;                   /* scratch [top_k, D] bf16 */
   void* collapsed;              /* scratch [D] bf16 */
