@@ -313,6 +313,62 @@ __global__ void __launch_bounds__(1024) route_small_kernel(
 
 // Dispatch plan of N*k <= 2048 routes whose top-k (from router_topk_kernel)
 // is already in topk_idx / topk_prob: one CTA of 1024 threads.
+// The stable permutation of R routes by every warp of the CTA (E <= 64):
+// warp w takes routes [w L, (w + 1) L) in 32-route chunks; it counts them per
+// expert, a per-expert prefix over the warps turns the counts into the
+// segments' first positions (from s_base = the experts' offsets), and each
+// warp then places its segment in order: the same permutation as
+// warp_stable_scatter, without one warp walking all R routes.
+constexpr int kSegExperts = 64;
+__device__ __forceinline__ void cta_stable_scatter(const int* s_idx, const float* s_prob, int R,
+                                                   int k, int E, const int* s_base,
+                                                   int (*s_seg)[kSegExperts],
+                                                   int* __restrict__ perm_token,
+                                                   float* __restrict__ perm_prob,
+                                                   int* __restrict__ route_pos,
+                                                   int64_t* __restrict__ sort_order) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  const int L = static_cast<int>(ceil_div(ceil_div(R, 32), nw)) * 32;
+  const int r_lo = min(R, warp * L), r_hi = min(R, r_lo + L);
+  for (int e = lane; e < E; e += 32) s_seg[warp][e] = 0;
+  __syncwarp();
+  for (int r0 = r_lo; r0 < r_hi; r0 += 32) {
+    const int r = r0 + lane;
+    const bool active = r < r_hi;
+    const int e = active ? s_idx[r] : -1 - lane;
+    const unsigned peers = __match_any_sync(0xffffffffu, e);
+    if (active && lane == 31 - __clz(peers)) s_seg[warp][e] += __popc(peers);
+    __syncwarp();
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    int run = s_base[e];
+    for (int w = 0; w < nw; ++w) {
+      const int c = s_seg[w][e];
+      s_seg[w][e] = run;
+      run += c;
+    }
+  }
+  __syncthreads();
+  for (int r0 = r_lo; r0 < r_hi; r0 += 32) {
+    const int r = r0 + lane;
+    const bool active = r < r_hi;
+    const int e = active ? s_idx[r] : -1 - lane;
+    const unsigned peers = __match_any_sync(0xffffffffu, e);
+    const int rank = __popc(peers & ((1u << lane) - 1u));
+    const int pos = active ? s_seg[warp][e] + rank : 0;
+    __syncwarp();
+    if (active && rank == __popc(peers) - 1) s_seg[warp][e] = pos + 1;
+    __syncwarp();
+    if (active) {
+      perm_token[pos] = r / k;
+      perm_prob[pos] = s_prob[r];
+      route_pos[r] = pos;
+      if (sort_order != nullptr) sort_order[pos] = r;
+    }
+  }
+}
+
 __global__ void __launch_bounds__(1024) plan_small_kernel(
     const int64_t* __restrict__ topk_idx, const float* __restrict__ topk_prob, int N, int E,
     int k, int tile_m, int* __restrict__ counts, int* __restrict__ offsets,
@@ -322,6 +378,7 @@ __global__ void __launch_bounds__(1024) plan_small_kernel(
   __shared__ float s_prob[256 * kMaxTopK / 4];
   __shared__ int s_cnt[kMaxExperts];
   __shared__ int s_warp[32];
+  __shared__ int s_seg[32][kSegExperts];
   for (int e = threadIdx.x; e < E; e += blockDim.x) s_cnt[e] = 0;
   __syncthreads();
   for (int r = threadIdx.x; r < N * k; r += blockDim.x) {
@@ -331,8 +388,32 @@ __global__ void __launch_bounds__(1024) plan_small_kernel(
     atomicAdd(&s_cnt[e], 1);
   }
   __syncthreads();
-  cta_plan_tail(N, E, k, tile_m, s_idx, s_prob, s_cnt, s_warp, counts, offsets, tile_offsets,
-                perm_token, perm_prob, route_pos, sort_order);
+  if (E > kSegExperts || N * k <= 64) {
+    cta_plan_tail(N, E, k, tile_m, s_idx, s_prob, s_cnt, s_warp, counts, offsets, tile_offsets,
+                  perm_token, perm_prob, route_pos, sort_order);
+    return;
+  }
+  // counts, offsets and tile offsets as cta_plan_tail forms them; the
+  // permutation by all warps
+  const int c = threadIdx.x < E ? s_cnt[threadIdx.x] : 0;
+  int total = 0;
+  const int off = block_exclusive_scan(c, s_warp, total);
+  const int tiles = threadIdx.x < E ? static_cast<int>(ceil_div(c, tile_m)) : 0;
+  int total_tiles = 0;
+  const int toff = block_exclusive_scan(tiles, s_warp, total_tiles);
+  if (threadIdx.x < E) {
+    counts[threadIdx.x] = c;
+    offsets[threadIdx.x] = off;
+    tile_offsets[threadIdx.x] = toff;
+    s_cnt[threadIdx.x] = off;
+  }
+  if (threadIdx.x == 0) {
+    offsets[E] = total;
+    tile_offsets[E] = total_tiles;
+  }
+  __syncthreads();
+  cta_stable_scatter(s_idx, s_prob, N * k, k, E, s_cnt, s_seg, perm_token, perm_prob, route_pos,
+                     sort_order);
 }
 
 

@@ -181,3 +181,21 @@ def test_route_norm_matches_norm_then_route(cuda, n, d, e, k):
     for name in ("topk_idx", "topk_prob", "counts", "offsets", "tile_offsets", "perm_token",
                  "perm_prob", "route_pos"):
         assert torch.equal(getattr(plan, name), getattr(want, name)), name
+
+
+@pytest.mark.parametrize("n,e,k", [(512, 16, 2), (1000, 64, 2), (300, 7, 3), (33, 64, 2),
+                                   (256, 8, 8), (1024, 32, 2)])
+def test_single_cta_plan_equals_chunked_plan(cuda, n, e, k):
+    """The one-CTA plan of llmyb_route (up to 2048 routes; the permutation
+    spread over all warps for E <= 64) gives the chunked multi-CTA plan of
+    llmyb_moe_plan on the same routes, field by field."""
+    from hybrid_llm_b200 import kernels
+    g = torch.Generator(device=cuda).manual_seed(n * e + k)
+    logits = torch.randn(n, e, device=cuda, generator=g)
+    logits[: n // 3] = logits[: n // 3].round()  # ties between experts
+    small = kernels.route(logits, k, tile_m=128, with_sort_order=True)
+    chunked = kernels.moe_plan(small.topk_idx, small.topk_prob, e, tile_m=128,
+                               with_sort_order=True)
+    for name in ("counts", "offsets", "tile_offsets", "perm_token", "perm_prob", "route_pos",
+                 "sort_order"):
+        assert torch.equal(getattr(small, name), getattr(chunked, name)), name
