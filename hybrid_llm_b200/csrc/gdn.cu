@@ -1240,6 +1240,416 @@ __global__ void __launch_bounds__(320, 1) gdn_scan_tc_kernel(
   }
 }
 
+// ------------------------------------------------- value-lane tcgen05 scan
+// One CTA per (row, head) for value width 128: the chunk step in transposed
+// form, with the value columns as the MMA's M dimension (TMEM lanes).  Every
+// operand the threads produce (S^T, W^T, X^T as bf16 hi/lo pairs) is then an
+// A operand written straight into tensor memory with tcgen05.st, and shared
+// memory holds only the TMA-loaded chunk operands.  Per chunk:
+//   D1   = S^T [Kw; Qs]^T  (one N = 128 product: columns 0-63 Kw, 64-127 Qs)
+//   D1[:, 0:64] -= U^T     (as U^T (-I): an exact bf16 product)
+//                          -> W = -D1[:, 0:64]^T and X = diag(ks) W
+//   D2   = X^T K           (K [token][key] read MN-major) -> S <- sd S + D2^T
+//   D1[:, 64:128] += W^T Aqk^T  -> O = D1[:, 64:128]^T times the gate
+// A hi part and a lo part are two MMAs accumulating into one fp32 tile.
+// Warps: 0 TMA (stages of [Kw; Qs], K, Aqk, U), 1 MMA, 2-17 lane warps: lane
+// quarter q = warp & 3 (value columns 32q .. 32q+31) and part r = (warp-2)/4
+// (tokens 16r .. 16r+15 of W and O, keys r*KD/4 .. of S).  The gate is copied
+// by each lane warp (cp.async) into its own shared tile one chunk ahead and
+// read transposed; the gated output replaces it there and leaves as 16-byte
+// row pieces.  TMEM (512 columns): D1 [0,128) (W part, O part) D2 [128,128+KD)
+// S hi|lo [256,256+KD) W hi|lo [384,448) X hi|lo [448,512).
+namespace scan_vl {
+constexpr int kVD = 128;
+constexpr int kLaneWarps = 16;
+constexpr int kThreads = 32 * (2 + kLaneWarps);
+template <int KD>
+struct Geo {
+  static constexpr int kNS = KD == 128 ? 2 : 3;     // stages
+  static constexpr int kKQ = 0;                     // KD/64 x [Kw 64 rows; Qs 64 rows], 16 KB each
+  static constexpr int kK = KD / 64 * 16384;        // KD/64 x K [64 tokens][64 keys], 8 KB each
+  static constexpr int kA = kK + KD / 64 * 8192;    // Aqk [64][64]
+  static constexpr int kU = kA + 8192;              // 2 x U [64 tokens][64 columns]
+  static constexpr int kStage = kU + 16384;
+  static constexpr uint32_t kTx = KD / 64 * (16384 + 8192) + 8192 + 16384;
+  static constexpr int kNegI = kNS * kStage;        // -I [64][64], the B operand that adds -U
+  static constexpr int kGate = kNegI + 8192;        // 16 warps x [16 tokens][32 columns]
+  static constexpr int kBar = kGate + kLaneWarps * 1024;
+  static constexpr int kSmem = kBar + 256 + 1024;
+};
+constexpr uint32_t kD1W = 0, kDO = 64, kD2 = 128, kSA = 256, kWA = 384, kXA = 448;
+
+// bf16 hi part of (a, b) and the bf16 rounding of what it leaves
+__device__ __forceinline__ void split_pair(float a, float b, uint32_t& hi, uint32_t& lo) {
+  const __nv_bfloat162 hh = __floats2bfloat162_rn(a, b);
+  const float2 hf = __bfloat1622float2(hh);
+  hi = *reinterpret_cast<const uint32_t*>(&hh);
+  lo = pack_bf16x2(a - hf.x, b - hf.y);
+}
+}  // namespace scan_vl
+
+// Compile-time timeline of CTA 0 (clock64 per chunk and point), off unless
+// LLMYB_GDN_SCAN_TRACE is defined by a diagnostic build.
+#ifdef LLMYB_GDN_SCAN_TRACE
+__device__ long long g_vl_trace[16 * 16];
+#define VL_MARK(c, slot)                                                              \
+  do {                                                                                \
+    if (blockIdx.x == 0 && (c) < 16 && lane == 0) g_vl_trace[(c) * 16 + (slot)] = clock64(); \
+  } while (0)
+#define VL_MARK_MAX(c, slot)                                                          \
+  do {                                                                                \
+    if (blockIdx.x == 0 && (c) < 16 && lane == 0)                                     \
+      atomicMax(reinterpret_cast<unsigned long long*>(&g_vl_trace[(c) * 16 + (slot)]), \
+                static_cast<unsigned long long>(clock64()));                          \
+  } while (0)
+#else
+#define VL_MARK(c, slot) \
+  do {                   \
+  } while (0)
+#define VL_MARK_MAX(c, slot) \
+  do {                       \
+  } while (0)
+#endif
+
+template <int KD>
+__global__ void __launch_bounds__(scan_vl::kThreads, 1) gdn_scan_vl_kernel(
+    const __grid_constant__ CUtensorMap map_kw, const __grid_constant__ CUtensorMap map_qs,
+    const __grid_constant__ CUtensorMap map_k, const __grid_constant__ CUtensorMap map_aqk,
+    const __grid_constant__ CUtensorMap map_u, const float* __restrict__ kscale,
+    const float* __restrict__ sdecay, const __nv_bfloat16* __restrict__ gate, int64_t sg, int B,
+    int T, int H, float* __restrict__ state, __nv_bfloat16* __restrict__ out, int64_t so,
+    int32_t* dev_status) {
+  using namespace scan_vl;
+  using G = Geo<KD>;
+  constexpr int VD = kVD, NS = G::kNS;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + G::kBar);
+  uint64_t* st_full = bars;         // [NS]
+  uint64_t* st_empty = bars + NS;   // [NS]
+  uint64_t* s_ready = bars + 2 * NS;
+  uint64_t* d1w_full = s_ready + 1;
+  uint64_t* w_ready = s_ready + 2;
+  uint64_t* d2_full = s_ready + 3;
+  uint64_t* o_full = s_ready + 4;
+  uint64_t* o_free = s_ready + 5;
+  uint64_t* mma_done = s_ready + 6;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(s_ready + 7);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int h = blockIdx.x % H;
+  const int b = blockIdx.x / H;
+  const int nC = (T + kC - 1) / kC;
+  const int64_t bh = static_cast<int64_t>(b) * H + h;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < NS; ++i) {
+      sm100::mbar_init(&st_full[i], 1);
+      sm100::mbar_init(&st_empty[i], 1);
+    }
+    sm100::mbar_init(s_ready, kLaneWarps);
+    sm100::mbar_init(d1w_full, 1);
+    sm100::mbar_init(w_ready, kLaneWarps);
+    sm100::mbar_init(d2_full, 1);
+    sm100::mbar_init(o_full, 1);
+    sm100::mbar_init(o_free, kLaneWarps);
+    sm100::mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    sm100::fence_mbar_init();
+    sm100::tma_prefetch_desc(&map_kw);
+    sm100::tma_prefetch_desc(&map_qs);
+    sm100::tma_prefetch_desc(&map_k);
+    sm100::tma_prefetch_desc(&map_aqk);
+    sm100::tma_prefetch_desc(&map_u);
+  }
+  // -I as a 128-byte-swizzled K-major [64][64] bf16 tile (row r: 16-byte piece
+  // (c/8) ^ (r%8) holds columns c .. c+7)
+  for (int i = threadIdx.x; i < 8192 / 16; i += blockDim.x) {
+    const int r = i >> 3, piece = i & 7;
+    uint4 z = make_uint4(0, 0, 0, 0);
+    if ((piece ^ (r & 7)) == (r >> 3)) {
+      uint32_t* zw = reinterpret_cast<uint32_t*>(&z);
+      zw[(r & 7) >> 1] = (r & 1) ? 0xBF800000u : 0x0000BF80u;
+    }
+    *reinterpret_cast<uint4*>(smem + G::kNegI + i * 16) = z;
+  }
+  sm100::fence_proxy_async_smem();
+  if (warp == 1) sm100::tmem_alloc(tmem_slot, 512);
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------- TMA
+    uint32_t issued = 0;
+    for (int c = 0; c < nC; ++c) {
+      const int s = c % NS;
+      if (!sm100::mbar_wait_warp(&st_empty[s], ((c / NS) & 1) ^ 1u, dev_status, abort_flag))
+        break;
+      VL_MARK(c, 15);
+      if (lane == 0) {
+        uint8_t* st = smem + s * G::kStage;
+        const int t0 = c * kC;
+        sm100::mbar_arrive_expect_tx(&st_full[s], G::kTx);
+#pragma unroll
+        for (int x = 0; x < KD / 64; ++x) {
+          sm100::tma_load_4d(&map_kw, &st_full[s], st + G::kKQ + x * 16384, x * 64, h, t0, b);
+          sm100::tma_load_4d(&map_qs, &st_full[s], st + G::kKQ + x * 16384 + 8192, x * 64, h, t0,
+                             b);
+          sm100::tma_load_4d(&map_k, &st_full[s], st + G::kK + x * 8192, x * 64, h, t0, b);
+        }
+        sm100::tma_load_2d(&map_aqk, &st_full[s], st + G::kA, 0,
+                           static_cast<int32_t>((bh * nC + c) * kC));
+        sm100::tma_load_4d(&map_u, &st_full[s], st + G::kU, 0, h, t0, b);
+        sm100::tma_load_4d(&map_u, &st_full[s], st + G::kU + 8192, 64, h, t0, b);
+      }
+      ++issued;
+    }
+    // no copy may still be in flight when the CTA exits
+    for (uint32_t i = 1; i <= static_cast<uint32_t>(NS); ++i)
+      if (issued >= i) {
+        const uint32_t c = issued - i;
+        sm100::mbar_wait_warp(&st_full[c % NS], (c / NS) & 1, dev_status, nullptr);
+      }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------- MMA
+    constexpr uint32_t id64 = sm100::make_idesc_bf16_f32(128, 64);
+    constexpr uint32_t id64_amn = id64 | (1u << 15);  // A (U) MN-major
+    constexpr uint32_t idd2 = sm100::make_idesc_bf16_f32(128, KD) | sm100::kIdescBMajorMN;
+    const uint32_t tD1W = tmem_base + kD1W, tDO = tmem_base + kDO, tD2 = tmem_base + kD2;
+    const uint32_t tSh = tmem_base + kSA, tSl = tSh + KD / 2;
+    const uint32_t tWh = tmem_base + kWA, tWl = tWh + 32;
+    const uint32_t tXh = tmem_base + kXA, tXl = tXh + 32;
+    const uint32_t negi = sm100::smem_u32(smem + G::kNegI);
+    constexpr uint32_t id128 = sm100::make_idesc_bf16_f32(128, 128);
+    for (int c = 0; c < nC; ++c) {
+      const int s = c % NS;
+      const uint32_t st = sm100::smem_u32(smem + s * G::kStage);
+      // D1 is free once the lane warps have read the previous chunk's O
+      if (!sm100::mbar_wait_warp(&st_full[s], (c / NS) & 1, dev_status, abort_flag) ||
+          !sm100::mbar_wait_warp(s_ready, c & 1, dev_status, abort_flag) ||
+          (c > 0 && !sm100::mbar_wait_warp(o_free, (c - 1) & 1, dev_status, abort_flag)))
+        break;
+      VL_MARK(c, 0);
+      sm100::tc_fence_after();
+      if (lane == 0) {
+        // D1 = S^T [Kw; Qs]^T (K steps of 16 keys: 8 packed columns of S), then
+        // columns 0-63 -= U^T
+#pragma unroll
+        for (int kk = 0; kk < KD / 16; ++kk) {
+          const uint64_t bkq =
+              sm100::make_sw128_kmajor_desc(st + G::kKQ + (kk >> 2) * 16384 + (kk & 3) * 32);
+          sm100::umma_bf16_ts(tD1W, tSh + kk * 8, bkq, id128, kk != 0 ? 1u : 0u);
+          sm100::umma_bf16_ts(tD1W, tSl + kk * 8, bkq, id128, 1u);
+        }
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          sm100::umma_bf16_ss(tD1W, sm100::make_sw128_desc(st + G::kU + kk * 2048, 8192, 1024),
+                              sm100::make_sw128_kmajor_desc(negi + kk * 32), id64_amn, 1u);
+        sm100::umma_commit(d1w_full);
+      }
+      __syncwarp();
+      VL_MARK(c, 1);
+      if (!sm100::mbar_wait_warp(w_ready, c & 1, dev_status, abort_flag)) break;
+      VL_MARK(c, 4);
+      sm100::tc_fence_after();
+      if (lane == 0) {
+        // D2 = X^T K: K steps of 16 tokens; B = K read MN-major (64-key blocks 8 KB apart)
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          const uint64_t bk = sm100::make_sw128_desc(st + G::kK + kk * 2048, 8192, 1024);
+          sm100::umma_bf16_ts(tD2, tXh + kk * 8, bk, idd2, kk != 0 ? 1u : 0u);
+          sm100::umma_bf16_ts(tD2, tXl + kk * 8, bk, idd2, 1u);
+        }
+        sm100::umma_commit(d2_full);
+        // O part += W^T Aqk^T
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          const uint64_t ba = sm100::make_sw128_kmajor_desc(st + G::kA + kk * 32);
+          sm100::umma_bf16_ts(tDO, tWh + kk * 8, ba, id64, 1u);
+          sm100::umma_bf16_ts(tDO, tWl + kk * 8, ba, id64, 1u);
+        }
+        sm100::umma_commit(o_full);
+        sm100::umma_commit(&st_empty[s]);
+      }
+      __syncwarp();
+      VL_MARK(c, 5);
+    }
+    if (lane == 0) sm100::umma_commit(mma_done);
+    __syncwarp();
+    sm100::mbar_wait_warp(mma_done, 0, dev_status, nullptr);
+  } else {
+    // ------------------------------------------------------- lane warps
+    constexpr int KH = KD / 4;  // keys of S held per thread
+    const int q = warp & 3;
+    const int r = (warp - 2) >> 2;
+    const int v = 32 * q + lane;
+    const int key0 = KH * r;
+    const uint32_t tl = tmem_base + (static_cast<uint32_t>(32 * q) << 16);
+    uint8_t* gtile = smem + G::kGate + (warp - 2) * 1024;  // gate, then the output [16][32]
+    const int pr = lane >> 2, pc = lane & 3;                 // 16-byte piece: token pr + 8u
+    float S[KH];
+    float* Sg = state + (bh * KD + key0) * VD + v;
+#pragma unroll
+    for (int i = 0; i < KH; ++i) S[i] = Sg[static_cast<int64_t>(i) * VD];
+
+    auto store_s = [&]() {
+#pragma unroll
+      for (int part = 0; part < KH / 16; ++part) {
+        uint32_t hi[8], lo[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          split_pair(S[16 * part + 2 * j], S[16 * part + 2 * j + 1], hi[j], lo[j]);
+        sm100::tmem_st_32x32b_x8(tl + kSA + KH / 2 * r + 8 * part, hi);
+        sm100::tmem_st_32x32b_x8(tl + kSA + KD / 2 + KH / 2 * r + 8 * part, lo);
+      }
+    };
+    store_s();
+    sm100::tmem_st_wait();
+    sm100::tc_fence_before();
+    __syncwarp();
+    if (lane == 0) sm100::mbar_arrive(s_ready);
+
+    // the lane's two 16-byte pieces of a chunk's gate tile, copied by
+    // cp.async one chunk ahead (zero past T)
+    auto load_gate = [&](int c) {
+      const int tw = c * kC + 16 * r;
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int t = tw + pr + 8 * u;
+        const bool ok = c < nC && t < T;
+        const int64_t row = static_cast<int64_t>(b) * T + (ok ? t : 0);
+        mma::cp_async16(gtile + (pr + 8 * u) * 64 + pc * 16,
+                        gate + row * sg + h * VD + 32 * q + 8 * pc, ok);
+      }
+      mma::cp_async_commit();
+    };
+    load_gate(0);
+    // kscale of the warp's 16 tokens (lane j < 16: token 16r + j) and the
+    // chunk decay, one chunk ahead
+    auto ks_at = [&](int c) {
+      const int t = c * kC + 16 * r + (lane & 15);
+      return (c < nC && t < T) ? __ldg(kscale + bh * T + t) : 0.f;
+    };
+    float ks_pre = ks_at(0), sd_pre = __ldg(sdecay + bh * nC);
+    for (int c = 0; c < nC; ++c) {
+      const int t0 = c * kC;
+      const int n = min(kC, T - t0);
+      const float ks_c = ks_pre, sd_c = sd_pre;
+      ks_pre = ks_at(c + 1);
+      sd_pre = c + 1 < nC ? __ldg(sdecay + bh * nC + c + 1) : 0.f;
+
+      // ---- W = -D1W and X = ks W for tokens 16r .. 16r+15
+      if (!sm100::mbar_wait_warp(d1w_full, c & 1, dev_status, abort_flag)) break;
+      if (warp == 2) VL_MARK(c, 6);
+      sm100::tc_fence_after();
+      {
+        uint32_t p[16];
+        sm100::tmem_ld_32x32b_x16(tl + kD1W + 16 * r, p);
+        sm100::tmem_ld_wait();
+        if (warp == 2) VL_MARK(c, 7);
+        sm100::tmem_regs_ready(p);
+        uint32_t hi[8], lo[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          split_pair(-__uint_as_float(p[2 * j]), -__uint_as_float(p[2 * j + 1]), hi[j], lo[j]);
+        sm100::tmem_st_32x32b_x8(tl + kWA + 8 * r, hi);
+        sm100::tmem_st_32x32b_x8(tl + kWA + 32 + 8 * r, lo);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float k0 = __shfl_sync(0xffffffffu, ks_c, 2 * j);
+          const float k1 = __shfl_sync(0xffffffffu, ks_c, 2 * j + 1);
+          split_pair(-k0 * __uint_as_float(p[2 * j]), -k1 * __uint_as_float(p[2 * j + 1]), hi[j],
+                     lo[j]);
+        }
+        sm100::tmem_st_32x32b_x8(tl + kXA + 8 * r, hi);
+        sm100::tmem_st_32x32b_x8(tl + kXA + 32 + 8 * r, lo);
+      }
+      sm100::tmem_st_wait();
+      sm100::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) sm100::mbar_arrive(w_ready);
+      if (warp == 2) VL_MARK(c, 8);
+      if (warp == 17) VL_MARK(c, 13);
+
+      // ---- S <- sd S + D2 for keys key0 .. key0+KH-1
+      if (!sm100::mbar_wait_warp(d2_full, c & 1, dev_status, abort_flag)) break;
+      if (warp == 2) VL_MARK(c, 9);
+      sm100::tc_fence_after();
+#pragma unroll
+      for (int part = 0; part < KH / 16; ++part) {
+        uint32_t d[16];
+        sm100::tmem_ld_32x32b_x16(tl + kD2 + key0 + 16 * part, d);
+        sm100::tmem_ld_wait();
+        sm100::tmem_regs_ready(d);
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          S[16 * part + j] = sd_c * S[16 * part + j] + __uint_as_float(d[j]);
+      }
+      if (c + 1 < nC) store_s();
+      sm100::tmem_st_wait();
+      sm100::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) sm100::mbar_arrive(s_ready);
+      if (warp == 2) VL_MARK(c, 10);
+      VL_MARK_MAX(c, 2);
+      if (warp == 17) VL_MARK(c, 14);
+
+      // ---- O = DO^T for tokens 16r .. 16r+15, times the gate; the product
+      // replaces the gate in its tile and leaves as 16-byte row pieces
+      if (!sm100::mbar_wait_warp(o_full, c & 1, dev_status, abort_flag)) break;
+      if (warp == 2) VL_MARK(c, 11);
+      sm100::tc_fence_after();
+      uint32_t o[16];
+      sm100::tmem_ld_32x32b_x16(tl + kDO + 16 * r, o);
+      sm100::tmem_ld_wait();
+      sm100::tmem_regs_ready(o);
+      sm100::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) sm100::mbar_arrive(o_free);
+      VL_MARK_MAX(c, 3);
+      mma::cp_async_wait<0>();  // this chunk's gate
+      __syncwarp();
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        __nv_bfloat16* g0 = reinterpret_cast<__nv_bfloat16*>(gtile + (2 * j) * 64 + lane * 2);
+        __nv_bfloat16* g1 = g0 + 32;
+        // reference order: out.to(hidden dtype) * gate, one rounding each
+        const __nv_bfloat162 ob =
+            __floats2bfloat162_rn(__uint_as_float(o[2 * j]), __uint_as_float(o[2 * j + 1]));
+        const __nv_bfloat162 pg = __hmul2(ob, __halves2bfloat162(*g0, *g1));
+        *g0 = __low2bfloat16(pg);
+        *g1 = __high2bfloat16(pg);
+      }
+      __syncwarp();
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int t = 16 * r + pr + 8 * u;
+        if (t < n) {
+          const int64_t row = static_cast<int64_t>(b) * T + t0 + t;
+          *reinterpret_cast<uint4*>(out + row * so + h * VD + 32 * q + 8 * pc) =
+              *reinterpret_cast<const uint4*>(gtile + (pr + 8 * u) * 64 + pc * 16);
+        }
+      }
+      __syncwarp();
+      load_gate(c + 1);
+      if (warp == 2) VL_MARK(c, 12);
+    }
+    mma::cp_async_wait<0>();  // nothing in flight into shared memory at exit
+#pragma unroll
+    for (int i = 0; i < KH; ++i) Sg[static_cast<int64_t>(i) * VD] = S[i];
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    sm100::tc_fence_after();
+    sm100::tmem_dealloc(tmem_base, 512);
+  }
+}
+
 int32_t check_io(const GdnIO& io, int KD, int VD) {
   if (!io.q || !io.k || !io.v || !io.gate || !io.beta) return LLMYB_EINVAL;
   if (!io.decay_logit && !io.log_alpha) return LLMYB_EINVAL;
@@ -1333,9 +1743,20 @@ int32_t launch_prefill(const GdnIO& io, int B, int T, int H, void* scratch, floa
         !make_bf16_2d_map(&maqk, po.Aqk, static_cast<uint64_t>(B) * H * nC * kC, kC, kC, kC, kC) ||
         !make_bf16_4d_map(&mu, po.U, B, T, H, VD, kC))
       return LLMYB_EUNSUPPORTED;
-    gdn_scan_tc_kernel<<<B * H * (VD / scan_tc::kVS), 320, scan_tc::kSmem, s>>>(
-        mkw, mqs, mk, maqk, mu, po.kscale, po.sdecay, io.gate, io.sg, B, T, H, KD, VD, state, out,
-        so, dev_status);
+    // the value-lane kernel (one CTA per row and head) once the 64-column
+    // kernel (two CTAs per row and head) would need more than one wave
+    if (VD == scan_vl::kVD && 2 * B * H > num_sms()) {
+      constexpr int kVlSmem = scan_vl::Geo<KD>::kSmem;
+      int32_t st = ensure_smem(gdn_scan_vl_kernel<KD>, kVlSmem);
+      if (st) return st;
+      gdn_scan_vl_kernel<KD><<<B * H, scan_vl::kThreads, kVlSmem, s>>>(
+          mkw, mqs, mk, maqk, mu, po.kscale, po.sdecay, io.gate, io.sg, B, T, H, state, out, so,
+          dev_status);
+    } else {
+      gdn_scan_tc_kernel<<<B * H * (VD / scan_tc::kVS), 320, scan_tc::kSmem, s>>>(
+          mkw, mqs, mk, maqk, mu, po.kscale, po.sdecay, io.gate, io.sg, B, T, H, KD, VD, state,
+          out, so, dev_status);
+    }
     count_launch();
     return launch_status();
   }
