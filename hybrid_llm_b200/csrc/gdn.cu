@@ -188,16 +188,20 @@ constexpr int round16(int x) { return (x + 15) / 16 * 16; }
 // Shared memory of the prep kernel, with the phases' buffers aliased so that
 // three CTAs fit on an SM:
 //   qrv : Q (for KK^T / QK^T), then R (blocked inverse), then V (U = T1 V)
-//   at  : A (the (I + A) factor), then T1 | T2 (scaled bf16 copies of T)
+//   at  : A (the (I + A) factor), then the staged U / Kw output tiles
+// Row strides (in 4-byte words) by access: A is read as tf32 A fragments
+// (row g, column t: stride = 4 mod 32 is conflict-free); R and T are written
+// as 8-byte fragment pairs and read as B fragments (row t, column g) or as
+// 8-byte pairs of the U / Kw A fragments (stride = 8 mod 32).
 template <int KD, int VD>
 struct PrepSmem {
-  static constexpr int LK = KD + 8, LV = VD + 8, LT = kC + 8, LF = kC + 1;
-  static constexpr int QRV = round16(cmax(cmax(kC * LK * 2, kC * LF * 4), kC * LV * 2));
-  static constexpr int AT = round16(cmax(kC * LF * 4, 2 * kC * LT * 2));
+  static constexpr int LK = KD + 8, LV = VD + 8, LA = kC + 4, LR = kC + 8, LF = kC + 8;
+  static constexpr int QRV = round16(cmax(cmax(kC * LK * 2, kC * LR * 4), kC * LV * 2));
+  static constexpr int AT = round16(cmax(kC * LA * 4, kC * cmax(KD, VD) * 2));
   __nv_bfloat16 K[kC * LK];
   alignas(16) uint8_t qrv[QRV];
   alignas(16) uint8_t at[AT];
-  float Tm[kC * LF];  // T = (I + A)^-1
+  alignas(16) float Tm[kC * LF];  // T = (I + A)^-1
   // per token: inclusive / exclusive cumulative log2-decay, beta, segment, and
   // the T2 column scale beta * Gamma_{t-1} (0 past a reset)
   float g[kC], gprev[kC], beta[kC], s2[kC];
@@ -237,8 +241,6 @@ __global__ void __launch_bounds__(128) gdn_chunk_prep_kernel(GdnIO io, int B, in
   float* sR = reinterpret_cast<float*>(sm.qrv);
   __nv_bfloat16* sV = reinterpret_cast<__nv_bfloat16*>(sm.qrv);
   float* sA = reinterpret_cast<float*>(sm.at);
-  __nv_bfloat16* sT1 = reinterpret_cast<__nv_bfloat16*>(sm.at);
-  __nv_bfloat16* sT2 = sT1 + kC * SM::LT;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int nC = static_cast<int>(ceil_div(T, kC));
   const int c = blockIdx.x % nC;
@@ -365,19 +367,19 @@ __global__ void __launch_bounds__(128) gdn_chunk_prep_kernel(GdnIO io, int B, in
       for (int half = 0; half < 2; ++half) {
         const int t = r0 + half * 8;
         const int i = nb * 8 + (lane & 3) * 2;
-        float mv[2];
+        float av[2], mv[2];
 #pragma unroll
         for (int u = 0; u < 2; ++u) {
           const int ii = i + u;
           const bool same = sm.seg[t] == sm.seg[ii];
-          sA[t * SM::LF + ii] =
-              (ii < t && same)
-                  ? sm.beta[t] * fast_exp2(sm.gprev[t] - sm.g[ii]) * kk[nb][half * 2 + u]
-                  : 0.f;
+          av[u] = (ii < t && same)
+                      ? sm.beta[t] * fast_exp2(sm.gprev[t] - sm.g[ii]) * kk[nb][half * 2 + u]
+                      : 0.f;
           mv[u] = (ii <= t && same && t < n)
                       ? fast_exp2(sm.g[t] - sm.g[ii]) * qk[nb][half * 2 + u]
                       : 0.f;
         }
+        *reinterpret_cast<float2*>(&sA[t * SM::LA + i]) = make_float2(av[0], av[1]);
         *reinterpret_cast<uint32_t*>(aqk_out + t * kC + i) = pack_bf16x2(mv[0], mv[1]);
       }
     }
@@ -395,15 +397,20 @@ __global__ void __launch_bounds__(128) gdn_chunk_prep_kernel(GdnIO io, int B, in
     for (int t = 0; t < 16; ++t) {
       float acc = (t == j) ? 1.f : 0.f;
 #pragma unroll
-      for (int i = 0; i < t; ++i) acc -= sA[(base + t) * SM::LF + base + i] * col[i];
+      for (int i = 0; i < t; ++i) acc -= sA[(base + t) * SM::LA + base + i] * col[i];
       col[t] = acc;
     }
 #pragma unroll
     for (int t = 0; t < 16; ++t) sm.Tm[(base + t) * SM::LF + base + j] = col[t];
-  }
-  for (int i = tid; i < kC * kC; i += 128) {
-    const int r = i / kC, cc = i % kC;
-    if ((cc >> 4) > (r >> 4)) sm.Tm[r * SM::LF + cc] = 0.f;
+  } else {
+    // meanwhile warps 2-3 zero the six blocks above the diagonal (16-byte stores)
+    for (int i = tid - 64; i < 6 * 16 * 4; i += 64) {
+      const int blk = i >> 6, row = (i >> 2) & 15, piece = i & 3;
+      const int br = blk < 3 ? 0 : (blk < 5 ? 1 : 2);
+      const int bc = blk < 3 ? blk + 1 : (blk < 5 ? blk - 1 : 3);
+      *reinterpret_cast<float4*>(&sm.Tm[(br * 16 + row) * SM::LF + bc * 16 + piece * 4]) =
+          make_float4(0.f, 0.f, 0.f, 0.f);
+    }
   }
   __syncthreads();
   // off-diagonal blocks, block row by block row, on the tensor cores in tf32
@@ -418,18 +425,18 @@ __global__ void __launch_bounds__(128) gdn_chunk_prep_kernel(GdnIO io, int B, in
         float acc[4] = {0.f, 0.f, 0.f, 0.f};
         for (int ks = 0; ks < 2 * bi; ++ks) {  // T is zero above its diagonal blocks
           const uint32_t a[4] = {
-              mma::to_tf32(sA[(r0 + g) * SM::LF + 8 * ks + tq]),
-              mma::to_tf32(sA[(r0 + g + 8) * SM::LF + 8 * ks + tq]),
-              mma::to_tf32(sA[(r0 + g) * SM::LF + 8 * ks + tq + 4]),
-              mma::to_tf32(sA[(r0 + g + 8) * SM::LF + 8 * ks + tq + 4])};
+              mma::to_tf32(sA[(r0 + g) * SM::LA + 8 * ks + tq]),
+              mma::to_tf32(sA[(r0 + g + 8) * SM::LA + 8 * ks + tq]),
+              mma::to_tf32(sA[(r0 + g) * SM::LA + 8 * ks + tq + 4]),
+              mma::to_tf32(sA[(r0 + g + 8) * SM::LA + 8 * ks + tq + 4])};
           const uint32_t bb[2] = {mma::to_tf32(sm.Tm[(8 * ks + tq) * SM::LF + 8 * nt + g]),
                                   mma::to_tf32(sm.Tm[(8 * ks + tq + 4) * SM::LF + 8 * nt + g])};
           mma::mma_tf32(acc, a, bb);
         }
-        sR[(r0 + g) * SM::LF + 8 * nt + 2 * tq] = acc[0];
-        sR[(r0 + g) * SM::LF + 8 * nt + 2 * tq + 1] = acc[1];
-        sR[(r0 + g + 8) * SM::LF + 8 * nt + 2 * tq] = acc[2];
-        sR[(r0 + g + 8) * SM::LF + 8 * nt + 2 * tq + 1] = acc[3];
+        *reinterpret_cast<float2*>(&sR[(r0 + g) * SM::LR + 8 * nt + 2 * tq]) =
+            make_float2(acc[0], acc[1]);
+        *reinterpret_cast<float2*>(&sR[(r0 + g + 8) * SM::LR + 8 * nt + 2 * tq]) =
+            make_float2(acc[2], acc[3]);
       }
       __syncthreads();
       for (int nt = warp; nt < 2 * bi; nt += 4) {
@@ -441,31 +448,25 @@ __global__ void __launch_bounds__(128) gdn_chunk_prep_kernel(GdnIO io, int B, in
               mma::to_tf32(sm.Tm[(r0 + g + 8) * SM::LF + r0 + 8 * ks + tq]),
               mma::to_tf32(sm.Tm[(r0 + g) * SM::LF + r0 + 8 * ks + tq + 4]),
               mma::to_tf32(sm.Tm[(r0 + g + 8) * SM::LF + r0 + 8 * ks + tq + 4])};
-          const uint32_t bb[2] = {mma::to_tf32(sR[(r0 + 8 * ks + tq) * SM::LF + 8 * nt + g]),
-                                  mma::to_tf32(sR[(r0 + 8 * ks + tq + 4) * SM::LF + 8 * nt + g])};
+          const uint32_t bb[2] = {mma::to_tf32(sR[(r0 + 8 * ks + tq) * SM::LR + 8 * nt + g]),
+                                  mma::to_tf32(sR[(r0 + 8 * ks + tq + 4) * SM::LR + 8 * nt + g])};
           mma::mma_tf32(acc, a, bb);
         }
-        sm.Tm[(r0 + g) * SM::LF + 8 * nt + 2 * tq] = -acc[0];
-        sm.Tm[(r0 + g) * SM::LF + 8 * nt + 2 * tq + 1] = -acc[1];
-        sm.Tm[(r0 + g + 8) * SM::LF + 8 * nt + 2 * tq] = -acc[2];
-        sm.Tm[(r0 + g + 8) * SM::LF + 8 * nt + 2 * tq + 1] = -acc[3];
+        *reinterpret_cast<float2*>(&sm.Tm[(r0 + g) * SM::LF + 8 * nt + 2 * tq]) =
+            make_float2(-acc[0], -acc[1]);
+        *reinterpret_cast<float2*>(&sm.Tm[(r0 + g + 8) * SM::LF + 8 * nt + 2 * tq]) =
+            make_float2(-acc[2], -acc[3]);
       }
       __syncthreads();
     }
   }
 
-  // ---- V into the R space (R is dead); T1/T2 into the A space (A is dead)
+  // ---- V into the R space (R is dead)
 #pragma unroll
   for (int u = 0; u < kVPer; ++u) {
     const int i = tid + 128 * u;
     const int r = i / (VD / 8), cc = (i % (VD / 8)) * 8;
     *reinterpret_cast<uint4*>(&sV[r * SM::LV + cc]) = vreg[u];
-  }
-  for (int i = tid; i < kC * kC; i += 128) {
-    const int r = i / kC, cc = i % kC;
-    const float tv = sm.Tm[r * SM::LF + cc];
-    sT1[r * SM::LT + cc] = f2bf(tv * sm.beta[cc]);
-    sT2[r * SM::LT + cc] = f2bf(tv * sm.s2[cc]);
   }
   if (tid < kC) {
     const int t = tid;
@@ -480,15 +481,35 @@ __global__ void __launch_bounds__(128) gdn_chunk_prep_kernel(GdnIO io, int B, in
   mma::cp_async_wait<0>();
   __syncthreads();
 
-  // ---- U = T1 V  (64 x VD), Kw = T2 K (64 x KD): rows 16*warp.., staged in
-  // the (dead) T space and written as whole 16-byte row pieces
+  // ---- U = T1 V  (64 x VD), Kw = T2 K (64 x KD) with T1 = T diag(beta) and
+  // T2 = T diag(s2) rounded to bf16 straight into the A fragments; rows
+  // 16*warp.., staged in the (dead) A space and written as whole 16-byte row
+  // pieces
   {
-    uint8_t* s_out = reinterpret_cast<uint8_t*>(sm.Tm);
+    uint8_t* s_out = sm.at;
     uint32_t a1[4][4], a2[4][4];
+    {
+      const int g = lane >> 2, tq = lane & 3;
+      const float* t0 = sm.Tm + (warp * 16 + g) * SM::LF;
+      const float* t8 = t0 + 8 * SM::LF;
 #pragma unroll
-    for (int ks = 0; ks < 4; ++ks) {
-      mma::load_a(a1[ks], sT1, SM::LT, warp * 16, ks * 16);
-      mma::load_a(a2[ks], sT2, SM::LT, warp * 16, ks * 16);
+      for (int ks = 0; ks < 4; ++ks) {
+        const int c0 = ks * 16 + 2 * tq;
+        const float2 x[4] = {*reinterpret_cast<const float2*>(t0 + c0),
+                             *reinterpret_cast<const float2*>(t8 + c0),
+                             *reinterpret_cast<const float2*>(t0 + c0 + 8),
+                             *reinterpret_cast<const float2*>(t8 + c0 + 8)};
+        const float2 b0 = *reinterpret_cast<const float2*>(&sm.beta[c0]);
+        const float2 b8 = *reinterpret_cast<const float2*>(&sm.beta[c0 + 8]);
+        const float2 s0 = *reinterpret_cast<const float2*>(&sm.s2[c0]);
+        const float2 s8 = *reinterpret_cast<const float2*>(&sm.s2[c0 + 8]);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 bs = e < 2 ? b0 : b8, ss = e < 2 ? s0 : s8;
+          a1[ks][e] = pack_bf16x2(x[e].x * bs.x, x[e].y * bs.y);
+          a2[ks][e] = pack_bf16x2(x[e].x * ss.x, x[e].y * ss.y);
+        }
+      }
     }
     const int r = warp * 16 + (lane >> 2);
 #pragma unroll
