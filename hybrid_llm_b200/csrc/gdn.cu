@@ -186,9 +186,11 @@ constexpr int cmax(int a, int b) { return a > b ? a : b; }
 constexpr int round16(int x) { return (x + 15) / 16 * 16; }
 
 // Shared memory of the prep kernel, with the phases' buffers aliased so that
-// three CTAs fit on an SM:
+// four CTAs fit on an SM:
+//   ka  : K (for KK^T / QK^T), then A (the (I + A) factor), then K again
+//         (reloaded from L2 for Kw = T2 K)
 //   qrv : Q (for KK^T / QK^T), then R (blocked inverse), then V (U = T1 V)
-//   at  : A (the (I + A) factor), then the staged U / Kw output tiles
+//   Tm  : T = (I + A)^-1, then the staged U / Kw output tiles
 // Row strides (in 4-byte words) by access: A is read as tf32 A fragments
 // (row g, column t: stride = 4 mod 32 is conflict-free); R and T are written
 // as 8-byte fragment pairs and read as B fragments (row t, column g) or as
@@ -196,12 +198,12 @@ constexpr int round16(int x) { return (x + 15) / 16 * 16; }
 template <int KD, int VD>
 struct PrepSmem {
   static constexpr int LK = KD + 8, LV = VD + 8, LA = kC + 4, LR = kC + 8, LF = kC + 8;
+  static constexpr int KA = round16(cmax(kC * LK * 2, kC * LA * 4));
   static constexpr int QRV = round16(cmax(cmax(kC * LK * 2, kC * LR * 4), kC * LV * 2));
-  static constexpr int AT = round16(cmax(kC * LA * 4, kC * cmax(KD, VD) * 2));
-  __nv_bfloat16 K[kC * LK];
+  static constexpr int TS = round16(cmax(kC * LF * 4, kC * cmax(KD, VD) * 2));
+  alignas(16) uint8_t ka[KA];
   alignas(16) uint8_t qrv[QRV];
-  alignas(16) uint8_t at[AT];
-  alignas(16) float Tm[kC * LF];  // T = (I + A)^-1
+  alignas(16) float Tm[TS / 4];
   // per token: inclusive / exclusive cumulative log2-decay, beta, segment, and
   // the T2 column scale beta * Gamma_{t-1} (0 past a reset)
   float g[kC], gprev[kC], beta[kC], s2[kC];
@@ -240,7 +242,8 @@ __global__ void __launch_bounds__(128) gdn_chunk_prep_kernel(GdnIO io, int B, in
   __nv_bfloat16* sQ = reinterpret_cast<__nv_bfloat16*>(sm.qrv);
   float* sR = reinterpret_cast<float*>(sm.qrv);
   __nv_bfloat16* sV = reinterpret_cast<__nv_bfloat16*>(sm.qrv);
-  float* sA = reinterpret_cast<float*>(sm.at);
+  __nv_bfloat16* sK = reinterpret_cast<__nv_bfloat16*>(sm.ka);
+  float* sA = reinterpret_cast<float*>(sm.ka);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int nC = static_cast<int>(ceil_div(T, kC));
   const int c = blockIdx.x % nC;
@@ -256,7 +259,7 @@ __global__ void __launch_bounds__(128) gdn_chunk_prep_kernel(GdnIO io, int B, in
     const int r = i / (KD / 8), cc = (i % (KD / 8)) * 8;
     const bool ok = r < n;
     const int64_t tok = tok0 + (ok ? r : 0);
-    mma::cp_async16(&sm.K[r * SM::LK + cc], io.k + tok * io.sk + h * KD + cc, ok);
+    mma::cp_async16(&sK[r * SM::LK + cc], io.k + tok * io.sk + h * KD + cc, ok);
     mma::cp_async16(&sQ[r * SM::LK + cc], io.q + tok * io.sq + h * KD + cc, ok);
   }
   mma::cp_async_commit();
@@ -344,19 +347,19 @@ __global__ void __launch_bounds__(128) gdn_chunk_prep_kernel(GdnIO io, int B, in
 #pragma unroll
   for (int ks = 0; ks < KD; ks += 16) {
     uint32_t ak[4], aq[4];
-    mma::load_a(ak, sm.K, SM::LK, warp * 16, ks);
+    mma::load_a(ak, sK, SM::LK, warp * 16, ks);
     mma::load_a(aq, sQ, SM::LK, warp * 16, ks);
 #pragma unroll
     for (int nb = 0; nb < 8; nb += 2) {
       uint32_t bb[4];
-      mma::load_b_nk(bb, sm.K, SM::LK, nb * 8, ks);
+      mma::load_b_nk(bb, sK, SM::LK, nb * 8, ks);
       mma::mma_bf16(kk[nb], ak, bb[0], bb[1]);
       mma::mma_bf16(kk[nb + 1], ak, bb[2], bb[3]);
       mma::mma_bf16(qk[nb], aq, bb[0], bb[1]);
       mma::mma_bf16(qk[nb + 1], aq, bb[2], bb[3]);
     }
   }
-  __syncthreads();  // Q is dead from here on (its space becomes R)
+  __syncthreads();  // Q and K are dead from here on (their spaces become R and A)
   // ---- masks and scales; A to shared memory (fp32), Aqk to global (bf16)
   __nv_bfloat16* aqk_out = po.Aqk + (bh * nC + c) * kC * kC;
   {
@@ -461,7 +464,14 @@ __global__ void __launch_bounds__(128) gdn_chunk_prep_kernel(GdnIO io, int B, in
     }
   }
 
-  // ---- V into the R space (R is dead)
+  // ---- K back into the A space (A is dead) for Kw; V into the R space (R is dead)
+  for (int i = tid; i < kC * (KD / 8); i += 128) {
+    const int r = i / (KD / 8), cc = (i % (KD / 8)) * 8;
+    const bool ok = r < n;
+    const int64_t tok = tok0 + (ok ? r : 0);
+    mma::cp_async16(&sK[r * SM::LK + cc], io.k + tok * io.sk + h * KD + cc, ok);
+  }
+  mma::cp_async_commit();
 #pragma unroll
   for (int u = 0; u < kVPer; ++u) {
     const int i = tid + 128 * u;
@@ -483,10 +493,10 @@ __global__ void __launch_bounds__(128) gdn_chunk_prep_kernel(GdnIO io, int B, in
 
   // ---- U = T1 V  (64 x VD), Kw = T2 K (64 x KD) with T1 = T diag(beta) and
   // T2 = T diag(s2) rounded to bf16 straight into the A fragments; rows
-  // 16*warp.., staged in the (dead) A space and written as whole 16-byte row
-  // pieces
+  // 16*warp.., staged in the T space once every warp holds its fragments, and
+  // written as whole 16-byte row pieces
   {
-    uint8_t* s_out = sm.at;
+    uint8_t* s_out = reinterpret_cast<uint8_t*>(sm.Tm);
     uint32_t a1[4][4], a2[4][4];
     {
       const int g = lane >> 2, tq = lane & 3;
@@ -511,6 +521,7 @@ __global__ void __launch_bounds__(128) gdn_chunk_prep_kernel(GdnIO io, int B, in
         }
       }
     }
+    __syncthreads();  // T is dead: its space stages the outputs
     const int r = warp * 16 + (lane >> 2);
 #pragma unroll
     for (int nb = 0; nb < VD / 8; nb += 2) {
@@ -539,7 +550,7 @@ __global__ void __launch_bounds__(128) gdn_chunk_prep_kernel(GdnIO io, int B, in
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks) {
         uint32_t bb[4];
-        mma::load_b_kn(bb, sm.K, SM::LK, ks * 16, nb * 8);
+        mma::load_b_kn(bb, sK, SM::LK, ks * 16, nb * 8);
         mma::mma_bf16(acc0, a2[ks], bb[0], bb[1]);
         mma::mma_bf16(acc1, a2[ks], bb[2], bb[3]);
       }

@@ -59,23 +59,38 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with a suspend-time hint: the thread sleeps until the phase
+// completes or about hint_ns pass, instead of spinning on issue slots.
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint64_t* bar, uint32_t parity,
+                                                      uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
+constexpr uint32_t kSuspendHintNs = 20000;
+
 // Wait for the phase with the given parity to complete.  Gives up after
 // kWaitLimitNs, records LLMYB_ETIMEOUT and returns false so that the caller
-// can unwind instead of spinning forever.
+// can unwind instead of spinning forever; another waiter's timeout (the
+// abort flag) is seen within one suspend period.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int32_t* dev_status,
                                           volatile int* abort_flag) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
-  uint32_t spins = 0;
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if (((++spins) & 63u) == 0u) {
-      if (abort_flag != nullptr && *abort_flag) return false;
-      if (globaltimer_ns() - t0 > kWaitLimitNs) {
-        report_status(dev_status, LLMYB_ETIMEOUT);
-        if (abort_flag != nullptr) *abort_flag = 1;
-        return false;
-      }
+    if (mbar_try_wait_suspend(bar, parity, kSuspendHintNs)) return true;
+    if (abort_flag != nullptr && *abort_flag) return false;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      report_status(dev_status, LLMYB_ETIMEOUT);
+      if (abort_flag != nullptr) *abort_flag = 1;
+      return false;
     }
   }
 }
