@@ -76,6 +76,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "llmyb_gdn_prefill": (I32, [P, I64, P, I64, P, I64, P, I64, P, I64, P, P, P, I32, I32, I32,
                                 I32, I32, P, P, I64, P, P, P]),
     "llmyb_gdn_conv_gate": (I32, [P, P, P, P, P, I32, I32, I32, P, P, I32, P]),
+    "llmyb_gdn_history_set": (I32, [P, P, I32, I32, I32, P]),
     # banded attention
     "llmyb_banded_attention": (I32, [P, I64, P, I64, P, I64, I32, I32, I32, I32, I32, I32, F32, P,
                                      I64, P, P]),
@@ -84,8 +85,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
                                       P, P, P]),
     "llmyb_csa_local_decode": (I32, [P, I64, P, I64, P, I64, P, P, P, I32, I32, I32, I32, I32, P,
                                      I64, P, P]),
+    "llmyb_csa_ring_write": (I32, [P, I64, P, I64, I32, I32, I32, I32, P, P, I32, P]),
     # diagnostics
     "llmyb_launch_count": (I64, []),
+    "llmyb_zero_regions": (I32, [P, I32, I64, P]),
     # residual stream
     "llmyb_embed": (I32, [P, I64, P, I64, I32, P, P, P, P]),
     "llmyb_add_rmsnorm": (I32, [P, P, I64, I32, P, F32, I32, P, P, P]),

@@ -705,6 +705,35 @@ bool aligned16(const void* p, int64_t stride) {
   return (reinterpret_cast<uintptr_t>(p) & 15u) == 0 && stride % 8 == 0;
 }
 
+// One token's row of width w: src -> dst, 16-byte vectors when both sides
+// allow (VEC), else bf16 elements.
+template <bool VEC>
+__device__ __forceinline__ void copy_row(const __nv_bfloat16* __restrict__ src,
+                                         __nv_bfloat16* __restrict__ dst, int w) {
+  if constexpr (VEC) {
+    for (int i = threadIdx.x; i < w / 8; i += blockDim.x)
+      reinterpret_cast<uint4*>(dst)[i] = __ldg(reinterpret_cast<const uint4*>(src) + i);
+  } else {
+    for (int i = threadIdx.x; i < w; i += blockDim.x) dst[i] = src[i];
+  }
+}
+
+// The decode ring after a prompt: token p of the last min(T, W) lands in slot
+// p % W of kcache [B, W, kw] and vcache [B, W, vw] (blockIdx.x: the token's
+// index among them, blockIdx.y: the batch row).
+template <bool VEC>
+__global__ void csa_ring_write_kernel(const __nv_bfloat16* __restrict__ k, int64_t sk,
+                                      const __nv_bfloat16* __restrict__ v, int64_t sv, int T,
+                                      int kw, int vw, __nv_bfloat16* __restrict__ kcache,
+                                      __nv_bfloat16* __restrict__ vcache, int W) {
+  const int b = blockIdx.y;
+  const int p = max(0, T - W) + static_cast<int>(blockIdx.x);
+  const int64_t row = static_cast<int64_t>(b) * T + p;
+  const int64_t slot = static_cast<int64_t>(b) * W + p % W;
+  copy_row<VEC>(k + row * sk, kcache + slot * kw, kw);
+  copy_row<VEC>(v + row * sv, vcache + slot * vw, vw);
+}
+
 }  // namespace
 }  // namespace llmyb
 
@@ -800,6 +829,38 @@ LLMYB_API int32_t llmyb_csa_local_prefill(const void* q, int64_t q_stride, const
 // vcache [B, Wc, D] hold token p at slot p % Wc; positions[b] is the new
 // token's position (its K/V are written to slot positions[b] % Wc).  The
 // window is the last min(positions[b] + 1, Wc) tokens (csa.py:185-187).
+// Ring caches after a prompt (csa.py:208-258 cache layout): kcache [B, W, kw],
+// vcache [B, W, vw] get token p of the last min(T, W) tokens of k [B*T, kw]
+// (token stride k_stride) and v [B*T, vw] at slot p % W; other slots keep
+// their contents.
+LLMYB_API int32_t llmyb_csa_ring_write(const void* k, int64_t k_stride, const void* v,
+                                       int64_t v_stride, int32_t batch, int32_t seq,
+                                       int32_t k_width, int32_t v_width, void* kcache,
+                                       void* vcache, int32_t window, void* stream) {
+  if (!k || !v || !kcache || !vcache || batch < 0 || seq < 0 || k_width <= 0 || v_width <= 0 ||
+      window <= 0 || k_stride < k_width || v_stride < v_width)
+    return LLMYB_EINVAL;
+  if (batch == 0 || seq == 0) return LLMYB_OK;
+  if (batch > 65535) return LLMYB_EUNSUPPORTED;
+  const int n = std::min(seq, window);
+  const bool vec = aligned16(k, k_stride) && aligned16(v, v_stride) && aligned16(kcache, k_width) &&
+                   aligned16(vcache, v_width) && k_width % 8 == 0 && v_width % 8 == 0;
+  const auto* kp = static_cast<const __nv_bfloat16*>(k);
+  const auto* vp = static_cast<const __nv_bfloat16*>(v);
+  auto* kc = static_cast<__nv_bfloat16*>(kcache);
+  auto* vc = static_cast<__nv_bfloat16*>(vcache);
+  const dim3 grid(static_cast<unsigned>(n), static_cast<unsigned>(batch));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (vec)
+    csa_ring_write_kernel<true><<<grid, 128, 0, s>>>(kp, k_stride, vp, v_stride, seq, k_width,
+                                                     v_width, kc, vc, window);
+  else
+    csa_ring_write_kernel<false><<<grid, 128, 0, s>>>(kp, k_stride, vp, v_stride, seq, k_width,
+                                                      v_width, kc, vc, window);
+  count_launch();
+  return launch_status();
+}
+
 LLMYB_API int32_t llmyb_csa_local_decode(const void* q, int64_t q_stride, const void* knew,
                                          int64_t knew_stride, const void* vnew,
                                          int64_t vnew_stride, void* kcache, void* vcache,

@@ -911,6 +911,32 @@ __global__ void gdn_conv_roll_kernel(const __nv_bfloat16* __restrict__ x,
     history[static_cast<int64_t>(b) * 3 * D + i] = s_roll[i];
 }
 
+// history[b] = the last three inputs x[b, T-3 .. T-1] of a prompt, zero where
+// T - 3 + j < 0 (the decode conv history a prefill leaves; 16-byte vectors
+// when D % 8 == 0 and both tensors are 16-byte aligned).
+template <bool VEC>
+__global__ void gdn_history_set_kernel(const __nv_bfloat16* __restrict__ x,
+                                       __nv_bfloat16* __restrict__ history, int T, int D) {
+  const int b = blockIdx.x;
+  __nv_bfloat16* h = history + static_cast<int64_t>(b) * 3 * D;
+  if constexpr (VEC) {
+    const int dv = D / 8;
+    for (int i = threadIdx.x; i < 3 * dv; i += blockDim.x) {
+      const int j = i / dv, c = i - j * dv;
+      const int src = T - 3 + j;
+      reinterpret_cast<uint4*>(h)[i] =
+          src >= 0 ? __ldg(reinterpret_cast<const uint4*>(x + (static_cast<int64_t>(b) * T + src) * D) + c)
+                   : make_uint4(0, 0, 0, 0);
+    }
+  } else {
+    for (int i = threadIdx.x; i < 3 * D; i += blockDim.x) {
+      const int j = i / D, d = i - j * D;
+      const int src = T - 3 + j;
+      h[i] = src >= 0 ? x[(static_cast<int64_t>(b) * T + src) * D + d] : __float2bfloat16_rn(0.f);
+    }
+  }
+}
+
 // ------------------------------------------------- chunk scan on tcgen05
 // K = 128 (or K = 64 padded to 128: the key-dimension boxes past K read as
 // zeros, so the state rows K..127 stay zero and only rows < K are loaded and
@@ -1886,6 +1912,25 @@ LLMYB_API int32_t llmyb_gdn_prefill(const void* q, int64_t q_stride, const void*
   if (key_dim == 64 && value_dim == 128)
     return launch_prefill<64, 128>(io, batch, seq, heads, scratch, state, o, out_stride, dev_status, s);
   return launch_prefill<128, 64>(io, batch, seq, heads, scratch, state, o, out_stride, dev_status, s);
+}
+
+// history [B, 3, D] = the last three rows of x [B, T, D] per batch row, zero
+// rows where the prompt is shorter (model/model.py:180-182).
+LLMYB_API int32_t llmyb_gdn_history_set(const void* x, void* history, int32_t batch, int32_t seq,
+                                        int32_t d_model, void* stream) {
+  if (!x || !history || batch < 0 || seq < 0 || d_model <= 0) return LLMYB_EINVAL;
+  if (batch == 0) return LLMYB_OK;
+  const bool vec = d_model % 8 == 0 && (reinterpret_cast<uintptr_t>(x) & 15u) == 0 &&
+                   (reinterpret_cast<uintptr_t>(history) & 15u) == 0;
+  const auto* xp = static_cast<const __nv_bfloat16*>(x);
+  auto* hp = static_cast<__nv_bfloat16*>(history);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (vec)
+    gdn_history_set_kernel<true><<<batch, 128, 0, s>>>(xp, hp, seq, d_model);
+  else
+    gdn_history_set_kernel<false><<<batch, 128, 0, s>>>(xp, hp, seq, d_model);
+  count_launch();
+  return launch_status();
 }
 
 // Conv gate + (optional) residual add + (optional) history roll; see

@@ -8,6 +8,7 @@
 // :442-444 (embedding + stream_seed).  Under bf16 autocast the residual
 // stream stays fp32 while sub-layer outputs are bf16; the same split is
 // used here: streams fp32, normalised activations bf16 (fp32 on request).
+#include <algorithm>
 #include <map>
 #include <mutex>
 #include <utility>
@@ -240,12 +241,44 @@ int32_t smem_limit_at_least(const void* kernel, int bytes) {
   have = bytes;
   return LLMYB_OK;
 }
+// Zeroes n regions, regions[2r] = device address, regions[2r+1] = bytes:
+// blockIdx.y picks the region; 16-byte stores over its aligned body, byte
+// stores over the unaligned head and tail.
+__global__ void zero_regions_kernel(const int64_t* __restrict__ regions) {
+  const int r = blockIdx.y;
+  uint8_t* p = reinterpret_cast<uint8_t*>(static_cast<uintptr_t>(regions[2 * r]));
+  const int64_t bytes = regions[2 * r + 1];
+  const int64_t head =
+      min(bytes, static_cast<int64_t>((16u - (reinterpret_cast<uintptr_t>(p) & 15u)) & 15u));
+  const int64_t body = (bytes - head) / 16;
+  const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t nthreads = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  if (tid < head) p[tid] = 0;
+  uint4* b4 = reinterpret_cast<uint4*>(p + head);
+  for (int64_t i = tid; i < body; i += nthreads) b4[i] = make_uint4(0, 0, 0, 0);
+  const int64_t tail0 = head + body * 16;
+  if (tid < bytes - tail0) p[tail0 + tid] = 0;
+}
+
 }  // namespace llmyb
 
 using namespace llmyb;
 
 // Number of kernel launches this library has issued since it was loaded.
 LLMYB_API int64_t llmyb_launch_count(void) { return launch_counter(); }
+
+LLMYB_API int32_t llmyb_zero_regions(const int64_t* regions, int32_t n_regions, int64_t max_bytes,
+                                     void* stream) {
+  if (n_regions < 0 || max_bytes < 0 || (n_regions > 0 && !regions)) return LLMYB_EINVAL;
+  if (n_regions > 65535) return LLMYB_EUNSUPPORTED;
+  if (n_regions == 0 || max_bytes == 0) return LLMYB_OK;
+  const int64_t blocks = std::min<int64_t>(ceil_div(max_bytes, 16 * 256), 64);
+  zero_regions_kernel<<<dim3(static_cast<unsigned>(std::max<int64_t>(blocks, 1)),
+                             static_cast<unsigned>(n_regions)),
+                        256, 0, static_cast<cudaStream_t>(stream)>>>(regions);
+  count_launch();
+  return launch_status();
+}
 
 LLMYB_API int32_t llmyb_embed(const int64_t* ids, int64_t n_tokens, const void* table,
                               int64_t vocab, int32_t d_model, const float* stream_seed,

@@ -654,6 +654,41 @@ def gdn_prefill(q, k, v, gate, beta, state, *, decay_logit=None, log_alpha=None,
     return out
 
 
+def gdn_history_set(x, history) -> None:
+    """history [B,3,D] = the last three rows of x [B,T,D] (zero rows when T < 3):
+    the decode conv history a prompt leaves (model/model.py:180-182)."""
+    _require_cuda(x, history)
+    _inplace(history, "history")
+    x = x.contiguous()
+    bsz, t, d = x.shape
+    if tuple(history.shape) != (bsz, 3, d) or history.dtype != torch.bfloat16 or x.dtype != torch.bfloat16:
+        raise ValueError("history must be bf16 [B, 3, D] for bf16 x [B, T, D]")
+    _native.call("llmyb_gdn_history_set", _ptr(x), _ptr(history), bsz, t, d, _stream())
+
+
+def zero_regions(regions: torch.Tensor, max_bytes: int) -> None:
+    """Zero every (address, bytes) region of the int64 device table regions
+    [n, 2] in one launch (see region_table)."""
+    _require_cuda(regions)
+    if regions.dtype != torch.int64 or regions.dim() != 2 or regions.shape[1] != 2:
+        raise ValueError("regions must be an int64 [n, 2] table of (address, bytes)")
+    _native.call("llmyb_zero_regions", _ptr(regions.contiguous()), regions.shape[0],
+                 int(max_bytes), _stream())
+
+
+def region_table(tensors, device) -> tuple[torch.Tensor, int]:
+    """(int64 device table [n, 2] of (address, bytes), largest size) for the
+    contiguous tensors, to zero them all with zero_regions."""
+    rows = []
+    for t in tensors:
+        if not t.is_contiguous():
+            raise ValueError("region_table takes contiguous tensors")
+        if t.numel():
+            rows.append((t.data_ptr(), t.numel() * t.element_size()))
+    table = torch.tensor(rows if rows else [(0, 0)], dtype=torch.int64).to(device)
+    return table[: len(rows)], max((r[1] for r in rows), default=0)
+
+
 def gdn_conv_gate(x, y_proj, conv_w, *, history=None, reset=None, out=None, residual=None,
                   roll_history=False):
     """y = y_proj * sigmoid(causal_conv4(x)); into `out` or added into `residual`."""
@@ -721,6 +756,27 @@ def csa_local_prefill(q, k, v, window: int, out=None):
     _native.call("llmyb_csa_local_prefill", qp, qs, kp, ks, vp, vs, bsz, t, h, dh, dm, int(window),
                  _ptr(out), out.stride(1), _ptr(scratch), _ptr(device_status(q.device)), _stream())
     return out
+
+
+def csa_ring_write(k, v, kcache, vcache) -> None:
+    """Decode ring caches after a prompt (csa.py:208-258 layout): token p of the
+    last min(T, W) tokens of k [B,T,kw] and v [B,T,vw] (evenly strided token
+    rows, e.g. column slices of the fused projection) into slot p % W of
+    kcache [B,W,kw] and vcache [B,W,vw]; the other slots keep their rows."""
+    _require_cuda(k, v, kcache, vcache)
+    _inplace(kcache, "kcache")
+    _inplace(vcache, "vcache")
+    bsz, t, kw = k.shape
+    vw = v.shape[-1]
+    w = kcache.shape[1]
+    if tuple(kcache.shape) != (bsz, w, kw) or tuple(vcache.shape) != (bsz, w, vw):
+        raise ValueError("kcache / vcache must be [B, W, width] for the k / v widths")
+    if kcache.dtype != torch.bfloat16 or vcache.dtype != torch.bfloat16:
+        raise ValueError("ring caches must be bf16")
+    kp, ks = _tokens(k, "k")
+    vp, vs = _tokens(v, "v")
+    _native.call("llmyb_csa_ring_write", kp, ks, vp, vs, bsz, t, kw, vw, _ptr(kcache),
+                 _ptr(vcache), w, _stream())
 
 
 def csa_local_decode(q, knew, vnew, kcache, vcache, positions, heads: int, out=None):

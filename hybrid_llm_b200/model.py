@@ -316,10 +316,7 @@ class LoopedHybridModel:
         x3 = normed.view(bsz, t, -1)
         mixed = kernels.gdn_conv_gate(x3, y.view(bsz, t, -1), g.conv, reset=reset)
         # conv history for decode: the last three inputs (model/model.py:180-182)
-        hist = state.gdn_conv_histories[key]
-        keep = min(t, hist.shape[1])
-        hist.zero_()
-        hist[:, hist.shape[1] - keep:] = x3[:, t - keep:]
+        kernels.gdn_history_set(x3, state.gdn_conv_histories[key])
         return mixed.view(bsz * t, -1)
 
     def _csa_prefill(self, a: CsaBlock, normed, state: RecurrentState, key: str, bsz: int,
@@ -348,12 +345,8 @@ class LoopedHybridModel:
             h.addmm_(remote.view(bsz * t, -1), a.remote_out.t())
         mixed = torch.mm(h, a.out.t())
         # ring caches for decode: token p at slot p % W (last min(T, W) tokens)
-        w = c.csa_window
-        lo = max(0, t - w)
-        src = torch.arange(lo, t, device=self.device)
-        slots = src % w
-        state.local_k[key][:, slots] = proj[:, lo:t, hd:2 * hd]
-        state.local_v[key][:, slots] = proj[:, lo:t, 2 * hd:]
+        kernels.csa_ring_write(proj[..., hd:2 * hd], proj[..., 2 * hd:], state.local_k[key],
+                               state.local_v[key])
         return mixed
 
     # -------------------------------------------------------------- decode

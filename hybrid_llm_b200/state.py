@@ -132,11 +132,21 @@ class RecurrentState:
         self.positions[mask] = 0
 
     def zero_(self) -> None:
-        """Zero every state tensor and position (a fresh conversation)."""
-        for _, table in self._tables():
-            for t in table.values():
+        """Zero every state tensor and position (a fresh conversation); on a
+        CUDA device one native launch over a table of the tensors' regions,
+        built on the first call (make that call before capturing it in a CUDA
+        graph) and rebuilt when a table's tensors change."""
+        tensors = [t for _, table in self._tables() for t in table.values()] + [self.positions]
+        if self.device.type != "cuda":
+            for t in tensors:
                 t.zero_()
-        self.positions.zero_()
+            return
+        from . import kernels
+        key = tuple((t.data_ptr(), t.numel() * t.element_size()) for t in tensors)
+        if getattr(self, "_zero_key", None) != key:
+            self._zero_table, self._zero_max = kernels.region_table(tensors, self.device)
+            self._zero_key = key
+        kernels.zero_regions(self._zero_table, self._zero_max)
 
     def nbytes(self) -> int:
         tensors = [t for _, table in self._tables() for t in table.values()] + [self.positions]

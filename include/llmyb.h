@@ -355,6 +355,12 @@ int32_t llmyb_gdn_conv_gate(const void* x, const void* y_proj, const float* conv
                             int32_t d_model, void* out, void* residual, int32_t roll_history,
                             void* stream);
 
+/* The decode conv history a prompt leaves (model/model.py:180-182): history
+ * [B,3,D] = the last three rows of x [B,T,D] per batch row, zero rows where
+ * T < 3.  Replaces the reference's slice assignment of the history buffer. */
+int32_t llmyb_gdn_history_set(const void* x, void* history, int32_t batch, int32_t seq,
+                              int32_t d_model, void* stream);
+
 /* ------------------------------------------------------ banded attention
  * Replaces fused_banded_local_attention / triton_banded_local_attention
  * (sample_standalone.py:70-85, :253-409), the CSA local branch
@@ -405,11 +411,29 @@ int32_t llmyb_csa_local_decode(const void* q, int64_t q_stride, const void* knew
                                int32_t window, void* out, int64_t out_stride,
                                int32_t* dev_status, void* stream);
 
+/* The ring caches a prompt leaves for decode (the cache layout of
+ * csa.py:208-258): kcache [B, window, k_width] and vcache [B, window, v_width]
+ * receive token p of the last min(seq, window) tokens of k [B*seq, k_width]
+ * and v [B*seq, v_width] (token strides k_stride, v_stride) at slot
+ * p % window; the other slots keep their contents.  Replaces the
+ * reference's indexed assignment of the cache rows. */
+int32_t llmyb_csa_ring_write(const void* k, int64_t k_stride, const void* v, int64_t v_stride,
+                             int32_t batch, int32_t seq, int32_t k_width, int32_t v_width,
+                             void* kcache, void* vcache, int32_t window, void* stream);
+
 /* ------------------------------------------------------------- diagnostics
  * Number of kernel launches this library has issued since it was loaded
  * (host-side count; a captured CUDA graph replays the launches counted while
  * it was captured).  No counterpart in the reference. */
 int64_t llmyb_launch_count(void);
+
+/* Zero n_regions device regions in one launch: regions is a device array of
+ * n_regions (address, bytes) int64 pairs, max_bytes the largest size (it
+ * sizes the grid).  Used to clear a whole recurrent state (every GDN state,
+ * conv history, ring cache and position counter) as a fresh conversation
+ * (recurrent_state.py:218-244 clears row by row); no reference counterpart. */
+int32_t llmyb_zero_regions(const int64_t* regions, int32_t n_regions, int64_t max_bytes,
+                           void* stream);
 
 /* --------------------------------------------------------- residual stream
  * PhysicalBlock's residual glue with mHC disabled (model/model.py:119-126,
