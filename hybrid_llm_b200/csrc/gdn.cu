@@ -1052,10 +1052,16 @@ __global__ void __launch_bounds__(320, 1) gdn_scan_tc_kernel(
     sm100::tma_prefetch_desc(&map_aqk);
     sm100::tma_prefetch_desc(&map_u);
   }
-  // the zero rows of [0; Aqk] (TMA writes only rows 64-127)
+  // the zero rows of [0; Aqk] (TMA writes only rows 64-127); with K = 64 also
+  // the second 64-key block of K, which is never loaded (so the rows K..127
+  // of D2 stay zero) -- only the first key block of Kw, Qs and K is fetched
+  // and D1 runs over the K / 16 key steps that carry data
+  const int kblk = KD / 64;
   for (int i = threadIdx.x; i < 2 * 8192 / 16; i += blockDim.x) {
     const int st = i / 512, o = (i % 512) * 16;
     *reinterpret_cast<uint4*>(smem + st * kStage + kA3 + o) = make_uint4(0, 0, 0, 0);
+    if (kblk == 1)
+      *reinterpret_cast<uint4*>(smem + st * kStage + kA2 + 8192 + o) = make_uint4(0, 0, 0, 0);
   }
   sm100::fence_proxy_async_smem();
   if (warp == 1) sm100::tmem_alloc(tmem_slot, kTmemCols);
@@ -1073,9 +1079,8 @@ __global__ void __launch_bounds__(320, 1) gdn_scan_tc_kernel(
       if (lane == 0) {
         uint8_t* st = smem + s * kStage;
         const int t0 = c * kC;
-        sm100::mbar_arrive_expect_tx(&st_full[s], kTx);
-#pragma unroll
-        for (int x = 0; x < 2; ++x) {
+        sm100::mbar_arrive_expect_tx(&st_full[s], kTx - (2 - kblk) * 3 * 8192);
+        for (int x = 0; x < kblk; ++x) {
           sm100::tma_load_4d(&map_kw, &st_full[s], st + kA1 + x * 16384, x * 64, h, t0, b);
           sm100::tma_load_4d(&map_qs, &st_full[s], st + kA1 + x * 16384 + 8192, x * 64, h, t0, b);
           sm100::tma_load_4d(&map_k, &st_full[s], st + kA2 + x * 8192, x * 64, h, t0, b);
@@ -1108,7 +1113,7 @@ __global__ void __launch_bounds__(320, 1) gdn_scan_tc_kernel(
       sm100::tc_fence_after();
       if (lane == 0) {
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
+        for (int kk = 0; kk < 4 * kblk; ++kk) {
           const uint64_t ad =
               sm100::make_sw128_kmajor_desc(st + kA1 + (kk >> 2) * 16384 + (kk & 3) * 32);
           const uint64_t bd = sm100::make_sw128_desc(s_hi + kk * 2048, s_lo - s_hi, 1024);
