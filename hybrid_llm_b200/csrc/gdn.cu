@@ -1351,29 +1351,6 @@ __device__ __forceinline__ void split_pair(float a, float b, uint32_t& hi, uint3
 }
 }  // namespace scan_vl
 
-// Compile-time timeline of CTA 0 (clock64 per chunk and point), off unless
-// LLMYB_GDN_SCAN_TRACE is defined by a diagnostic build.
-#ifdef LLMYB_GDN_SCAN_TRACE
-__device__ long long g_vl_trace[16 * 16];
-#define VL_MARK(c, slot)                                                              \
-  do {                                                                                \
-    if (blockIdx.x == 0 && (c) < 16 && lane == 0) g_vl_trace[(c) * 16 + (slot)] = clock64(); \
-  } while (0)
-#define VL_MARK_MAX(c, slot)                                                          \
-  do {                                                                                \
-    if (blockIdx.x == 0 && (c) < 16 && lane == 0)                                     \
-      atomicMax(reinterpret_cast<unsigned long long*>(&g_vl_trace[(c) * 16 + (slot)]), \
-                static_cast<unsigned long long>(clock64()));                          \
-  } while (0)
-#else
-#define VL_MARK(c, slot) \
-  do {                   \
-  } while (0)
-#define VL_MARK_MAX(c, slot) \
-  do {                       \
-  } while (0)
-#endif
-
 template <int KD>
 __global__ void __launch_bounds__(scan_vl::kThreads, 1) gdn_scan_vl_kernel(
     const __grid_constant__ CUtensorMap map_kw, const __grid_constant__ CUtensorMap map_qs,
@@ -1452,7 +1429,6 @@ __global__ void __launch_bounds__(scan_vl::kThreads, 1) gdn_scan_vl_kernel(
       const int s = c % NS;
       if (!sm100::mbar_wait_warp(&st_empty[s], ((c / NS) & 1) ^ 1u, dev_status, abort_flag))
         break;
-      VL_MARK(c, 15);
       if (lane == 0) {
         uint8_t* st = smem + s * G::kStage;
         const int t0 = c * kC;
@@ -1496,7 +1472,6 @@ __global__ void __launch_bounds__(scan_vl::kThreads, 1) gdn_scan_vl_kernel(
           !sm100::mbar_wait_warp(s_ready, c & 1, dev_status, abort_flag) ||
           (c > 0 && !sm100::mbar_wait_warp(o_free, (c - 1) & 1, dev_status, abort_flag)))
         break;
-      VL_MARK(c, 0);
       sm100::tc_fence_after();
       if (lane == 0) {
         // D1 = S^T [Kw; Qs]^T (K steps of 16 keys: 8 packed columns of S), then
@@ -1515,9 +1490,7 @@ __global__ void __launch_bounds__(scan_vl::kThreads, 1) gdn_scan_vl_kernel(
         sm100::umma_commit(d1w_full);
       }
       __syncwarp();
-      VL_MARK(c, 1);
       if (!sm100::mbar_wait_warp(w_ready, c & 1, dev_status, abort_flag)) break;
-      VL_MARK(c, 4);
       sm100::tc_fence_after();
       if (lane == 0) {
         // D2 = X^T K: K steps of 16 tokens; B = K read MN-major (64-key blocks 8 KB apart)
@@ -1539,7 +1512,6 @@ __global__ void __launch_bounds__(scan_vl::kThreads, 1) gdn_scan_vl_kernel(
         sm100::umma_commit(&st_empty[s]);
       }
       __syncwarp();
-      VL_MARK(c, 5);
     }
     if (lane == 0) sm100::umma_commit(mma_done);
     __syncwarp();
@@ -1607,13 +1579,11 @@ __global__ void __launch_bounds__(scan_vl::kThreads, 1) gdn_scan_vl_kernel(
 
       // ---- W = -D1W and X = ks W for tokens 16r .. 16r+15
       if (!sm100::mbar_wait_warp(d1w_full, c & 1, dev_status, abort_flag)) break;
-      if (warp == 2) VL_MARK(c, 6);
       sm100::tc_fence_after();
       {
         uint32_t p[16];
         sm100::tmem_ld_32x32b_x16(tl + kD1W + 16 * r, p);
         sm100::tmem_ld_wait();
-        if (warp == 2) VL_MARK(c, 7);
         sm100::tmem_regs_ready(p);
         uint32_t hi[8], lo[8];
 #pragma unroll
@@ -1635,12 +1605,9 @@ __global__ void __launch_bounds__(scan_vl::kThreads, 1) gdn_scan_vl_kernel(
       sm100::tc_fence_before();
       __syncwarp();
       if (lane == 0) sm100::mbar_arrive(w_ready);
-      if (warp == 2) VL_MARK(c, 8);
-      if (warp == 17) VL_MARK(c, 13);
 
       // ---- S <- sd S + D2 for keys key0 .. key0+KH-1
       if (!sm100::mbar_wait_warp(d2_full, c & 1, dev_status, abort_flag)) break;
-      if (warp == 2) VL_MARK(c, 9);
       sm100::tc_fence_after();
 #pragma unroll
       for (int part = 0; part < KH / 16; ++part) {
@@ -1657,14 +1624,10 @@ __global__ void __launch_bounds__(scan_vl::kThreads, 1) gdn_scan_vl_kernel(
       sm100::tc_fence_before();
       __syncwarp();
       if (lane == 0) sm100::mbar_arrive(s_ready);
-      if (warp == 2) VL_MARK(c, 10);
-      VL_MARK_MAX(c, 2);
-      if (warp == 17) VL_MARK(c, 14);
 
       // ---- O = DO^T for tokens 16r .. 16r+15, times the gate; the product
       // replaces the gate in its tile and leaves as 16-byte row pieces
       if (!sm100::mbar_wait_warp(o_full, c & 1, dev_status, abort_flag)) break;
-      if (warp == 2) VL_MARK(c, 11);
       sm100::tc_fence_after();
       uint32_t o[16];
       sm100::tmem_ld_32x32b_x16(tl + kDO + 16 * r, o);
@@ -1673,7 +1636,6 @@ __global__ void __launch_bounds__(scan_vl::kThreads, 1) gdn_scan_vl_kernel(
       sm100::tc_fence_before();
       __syncwarp();
       if (lane == 0) sm100::mbar_arrive(o_free);
-      VL_MARK_MAX(c, 3);
       mma::cp_async_wait<0>();  // this chunk's gate
       __syncwarp();
 #pragma unroll
@@ -1699,7 +1661,6 @@ __global__ void __launch_bounds__(scan_vl::kThreads, 1) gdn_scan_vl_kernel(
       }
       __syncwarp();
       load_gate(c + 1);
-      if (warp == 2) VL_MARK(c, 12);
     }
     mma::cp_async_wait<0>();  // nothing in flight into shared memory at exit
 #pragma unroll

@@ -254,26 +254,28 @@ def convert_checkpoint(src: str | Path, dst: str | Path, *, keep_fp32: bool = Fa
     state dict with a "config" entry) to ``.llmy``.  Non-tensor entries are
     skipped; keep_fp32 stores every tensor as float32; strict fails on any
     tensor that is not float32.  Returns the process exit status (0, or 1 with a
-    message on stderr), as the tool does."""
+    message on stderr) at the same points as the tool; the messages are this
+    project's own."""
     import sys
     src, dst = Path(src), Path(dst)
     if not src.is_file():
-        print(f"error: {src} is not a file", file=sys.stderr)
+        print(f"llmy convert: cannot read {src}: no such file", file=sys.stderr)
         return 1
     ckpt = torch.load(src, map_location="cpu", weights_only=False)
     if not isinstance(ckpt, dict):
-        print("error: checkpoint is not a dict", file=sys.stderr)
+        print(f"llmy convert: {src} holds a {type(ckpt).__name__}, not a mapping", file=sys.stderr)
         return 1
     cfg = ckpt.get("config")
     if cfg is None:
-        print("error: checkpoint has no embedded config", file=sys.stderr)
+        print(f"llmy convert: {src} carries no 'config' entry", file=sys.stderr)
         return 1
     if not isinstance(cfg, dict):
-        print(f"error: config is {type(cfg).__name__}, expected dict", file=sys.stderr)
+        print(f"llmy convert: the 'config' entry is a {type(cfg).__name__}; a mapping is required",
+              file=sys.stderr)
         return 1
     state = ckpt.get("model", ckpt)
     if not isinstance(state, dict):
-        print("error: state dict is not a dict", file=sys.stderr)
+        print("llmy convert: the weights ('model' entry) are not a mapping", file=sys.stderr)
         return 1
     tensors: dict[str, torch.Tensor] = {}
     for name, t in state.items():
@@ -281,7 +283,8 @@ def convert_checkpoint(src: str | Path, dst: str | Path, *, keep_fp32: bool = Fa
             continue
         t = t.float() if keep_fp32 else t
         if strict and t.dtype != torch.float32:
-            print(f"error: tensor {name.replace('_orig_mod.', '')} is {t.dtype}", file=sys.stderr)
+            print(f"llmy convert: --strict: {name.replace('_orig_mod.', '')} has dtype {t.dtype}, "
+                  "not float32", file=sys.stderr)
             return 1
         tensors[name] = t
     write_llmy(dst, cfg, tensors)
@@ -291,16 +294,19 @@ def convert_checkpoint(src: str | Path, dst: str | Path, *, keep_fp32: bool = Fa
 def _main(argv: list[str] | None = None) -> int:
     import argparse
     ap = argparse.ArgumentParser(prog="python -m hybrid_llm_b200.llmy_format",
-                                 description="Convert a training checkpoint to .llmy, or list one.")
+                                 description="Write a .llmy file from a training checkpoint, or print a "
+                                             ".llmy file's configuration and tensor table.")
     sub = ap.add_subparsers(dest="cmd", required=True)
-    cv = sub.add_parser("convert", help="training checkpoint (.pt) -> .llmy")
+    cv = sub.add_parser("convert", help="pack a .pt training checkpoint into a .llmy file")
     cv.add_argument("input", type=Path)
     cv.add_argument("output", type=Path)
     cv.add_argument("--keep-fp32", action="store_true",
-                    help="store all tensors as float32 (default: keep input dtype)")
+                    help="widen every tensor to float32 (otherwise each keeps its dtype)")
     cv.add_argument("--strict", action="store_true",
-                    help="fail if any tensor is not float32 after conversion")
-    ls = sub.add_parser("info", help="print the configuration and tensor index of a .llmy file")
+                    help="exit with status 1 if a tensor would be stored in a dtype other "
+                         "than float32")
+    ls = sub.add_parser("info", help="show a .llmy file's configuration text and its tensors "
+                         "(name, dtype, shape)")
     ls.add_argument("file", type=Path)
     args = ap.parse_args(argv)
     if args.cmd == "convert":

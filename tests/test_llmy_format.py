@@ -144,4 +144,4 @@ def test_converter_tool_reproduces_the_fixture(tmp_path, capsys):
     assert llmy_format.convert_checkpoint(tmp_path / "nocfg.pt", tmp_path / "y.llmy") == 1
     assert llmy_format.convert_checkpoint(tmp_path / "missing.pt", tmp_path / "z.llmy") == 1
     err = capsys.readouterr().err
-    assert "no embedded config" in err and "is not a file" in err and "is torch.bfloat16" in err
+    assert "no 'config' entry" in err and "no such file" in err and "dtype torch.bfloat16" in err
