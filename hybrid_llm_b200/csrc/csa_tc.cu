@@ -15,6 +15,11 @@
 //                 block, Pbar = sum_h exp2(c s - m_h) / (H l_h), masked to the
 //                 band; written as a bf16 [128 x 128] tile.  Eight softmax
 //                 warps, two per TMEM lane quarter, each summing 64 columns.
+//                 With few units (short prompts) a cluster of G CTAs shares
+//                 a unit: each sums H/G heads into an fp32 partial tile in its
+//                 shared memory, and after a bounded cluster-wide handoff
+//                 (remote mbarrier arrivals) each CTA adds one slice of the G
+//                 partials through distributed shared memory, in rank order.
 //   csa_pv_tc     (b, query tile, NSW-column slice of D): O = sum over the
 //                 band's key blocks of Pbar_blk V_blk, V read in its natural
 //                 [key][d] layout as an MN-major B operand; two TMEM
@@ -254,7 +259,9 @@ struct PbarLayout {
   static constexpr int kTile = kR * DH * 2;
   static constexpr int kStages = DH == 64 ? 4 : 2;
   static constexpr int kStage = 2 * kTile;  // Q_h | K_h
-  static constexpr int kBar = kStages * kStage;
+  static constexpr int kPartLd = kR + 4;    // partial-tile row stride (fp32): float4 rows conflict-free
+  static constexpr int kPart = kStages * kStage;  // this CTA's sum over its heads [128][kPartLd]
+  static constexpr int kBar = kPart + kR * kPartLd * 4;
   static constexpr int kSmem = kBar + 256 + 1024;
 };
 
@@ -274,11 +281,20 @@ __global__ void __launch_bounds__(320, 1) csa_pbar_tc_kernel(
   uint64_t* s_full = bars + 2 * ST;  // [2]
   uint64_t* s_empty = s_full + 2;    // [2]
   uint64_t* mma_done = s_empty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  uint64_t* cl_ready = mma_done + 1;  // every CTA of the cluster wrote its partial
+  uint64_t* cl_done = cl_ready + 1;   // every CTA of the cluster read the partials
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(cl_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* part = reinterpret_cast<float*>(smem + L::kPart);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int units = g.B * g.nqt * g.nb;
   const int H = g.H;
+  // a cluster of G CTAs shares each unit, CTA `rank` taking heads
+  // [rank H/G, (rank+1) H/G) (G divides H)
+  const int G = static_cast<int>(sm100::cluster_nctarank());
+  const int rank = static_cast<int>(sm100::cluster_ctarank());
+  const int cid = blockIdx.x / G, ncl = gridDim.x / G;
+  const int hs = H / G, h0 = rank * hs;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < ST; ++i) {
@@ -290,6 +306,8 @@ __global__ void __launch_bounds__(320, 1) csa_pbar_tc_kernel(
       sm100::mbar_init(&s_empty[i], 8);
     }
     sm100::mbar_init(mma_done, 1);
+    sm100::mbar_init(cl_ready, 8 * G);
+    sm100::mbar_init(cl_done, 8 * G);
     *abort_flag = 0;
     sm100::fence_mbar_init();
     sm100::tma_prefetch_desc(&map_q);
@@ -298,6 +316,7 @@ __global__ void __launch_bounds__(320, 1) csa_pbar_tc_kernel(
   if (warp == 1) sm100::tmem_alloc(tmem_slot, 256);
   sm100::tc_fence_before();
   __syncthreads();
+  sm100::cluster_sync();  // peers' barriers are initialised before anyone arrives on them
   sm100::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -308,11 +327,11 @@ __global__ void __launch_bounds__(320, 1) csa_pbar_tc_kernel(
     for (int i = 0; i < ST; ++i) issued[i] = 0;
     bool ok = true;
     int n = 0;  // stage loads issued
-    for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+    for (int u = cid; u < units && ok; u += ncl) {
       const int i = u % g.nb, qt = (u / g.nb) % g.nqt, b = u / (g.nb * g.nqt);
       if (i >= g.nblk(qt)) continue;
       const int kb = g.kb0(qt) + i;
-      for (int h = 0; h < H; ++h, ++n) {
+      for (int h = h0; h < h0 + hs; ++h, ++n) {
         const int s = n % ST;
         if (!sm100::mbar_wait_warp(&empty[s], ((n / ST) & 1) ^ 1u, dev_status, abort_flag)) {
           ok = false;
@@ -339,10 +358,10 @@ __global__ void __launch_bounds__(320, 1) csa_pbar_tc_kernel(
     const uint32_t s0 = sm100::smem_u32(smem);
     bool ok = true;
     int n = 0;
-    for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+    for (int u = cid; u < units && ok; u += ncl) {
       const int i = u % g.nb, qt = (u / g.nb) % g.nqt;
       if (i >= g.nblk(qt)) continue;
-      for (int h = 0; h < H; ++h, ++n) {
+      for (int h = h0; h < h0 + hs; ++h, ++n) {
         const int s = n % ST, sb = n & 1;
         if (!sm100::mbar_wait_warp(&full[s], (n / ST) & 1, dev_status, abort_flag) ||
             !sm100::mbar_wait_warp(&s_empty[sb], ((n >> 1) & 1) ^ 1u, dev_status, abort_flag)) {
@@ -374,8 +393,9 @@ __global__ void __launch_bounds__(320, 1) csa_pbar_tc_kernel(
     const uint32_t t_lane = tmem_base + (static_cast<uint32_t>(qw * 32) << 16) + half * 64;
     const float invh = 1.0f / static_cast<float>(H);
     int n = 0;
+    int uc = 0;  // units this cluster has finished (phase of cl_ready / cl_done)
     bool ok = true;
-    for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+    for (int u = cid; u < units && ok; u += ncl) {
       const int i = u % g.nb, qt = (u / g.nb) % g.nqt, b = u / (g.nb * g.nqt);
       if (i >= g.nblk(qt)) continue;
       const int kb = g.kb0(qt) + i, t = qt * kR + row;
@@ -385,7 +405,7 @@ __global__ void __launch_bounds__(320, 1) csa_pbar_tc_kernel(
       float acc[64];
 #pragma unroll
       for (int e = 0; e < 64; ++e) acc[e] = 0.f;
-      for (int h = 0; h < H; ++h, ++n) {
+      for (int h = h0; h < h0 + hs; ++h, ++n) {
         const int sb = n & 1;
         // this row's statistics for head h (a row past T contributes zero)
         const float mh = t < g.T ? __ldg(m_in + so + h) : 0.f;
@@ -417,21 +437,49 @@ __global__ void __launch_bounds__(320, 1) csa_pbar_tc_kernel(
         }
       }
       if (!ok) break;
-      __nv_bfloat16* dst = pbar + ((static_cast<int64_t>(b) * g.nqt + qt) * g.nb + i) * (kR * kR) +
-                           row * kR + half * 64;
+      // this CTA's sum over its heads into its partial tile (once every peer
+      // has read the previous unit's), then each CTA sums one slice of the
+      // tile over the cluster, in rank order, and writes it as bf16
+      if (uc > 0 && !sm100::mbar_wait_warp(cl_done, (uc - 1) & 1, dev_status, abort_flag)) break;
+      float* prow = part + row * L::kPartLd + half * 64;
 #pragma unroll
-      for (int v = 0; v < 8; ++v) {
+      for (int v = 0; v < 16; ++v)
+        reinterpret_cast<float4*>(prow)[v] =
+            make_float4(acc[4 * v], acc[4 * v + 1], acc[4 * v + 2], acc[4 * v + 3]);
+      sm100::fence_acq_rel_cluster();
+      __syncwarp();
+      if (lane < G) sm100::mbar_arrive_cluster(sm100::mapa_shared(sm100::smem_u32(cl_ready), lane));
+      if (!sm100::mbar_wait_warp(cl_ready, uc & 1, dev_status, abort_flag)) break;
+      sm100::fence_acq_rel_cluster();
+      __nv_bfloat16* tile = pbar + ((static_cast<int64_t>(b) * g.nqt + qt) * g.nb + i) * (kR * kR);
+      constexpr int kChunks = kR * kR / 8;  // 8-column pieces of the tile
+      const int per = (kChunks + G - 1) / G;
+      const int c_end = min(kChunks, (rank + 1) * per);
+      for (int ch = rank * per + (threadIdx.x - 64); ch < c_end; ch += 256) {
+        const int r = ch >> 4, col = (ch & 15) * 8;
+        const uint32_t la = sm100::smem_u32(part + r * L::kPartLd + col);
+        float sum[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        for (int q = 0; q < G; ++q) {
+          const uint32_t ra = sm100::mapa_shared(la, static_cast<uint32_t>(q));
+          const float4 x0 = sm100::ld_dsmem_f4(ra), x1 = sm100::ld_dsmem_f4(ra + 16);
+          sum[0] += x0.x; sum[1] += x0.y; sum[2] += x0.z; sum[3] += x0.w;
+          sum[4] += x1.x; sum[5] += x1.y; sum[6] += x1.z; sum[7] += x1.w;
+        }
         uint4 w;
-        w.x = pack_bf16x2(acc[8 * v + 0], acc[8 * v + 1]);
-        w.y = pack_bf16x2(acc[8 * v + 2], acc[8 * v + 3]);
-        w.z = pack_bf16x2(acc[8 * v + 4], acc[8 * v + 5]);
-        w.w = pack_bf16x2(acc[8 * v + 6], acc[8 * v + 7]);
-        reinterpret_cast<uint4*>(dst)[v] = w;
+        w.x = pack_bf16x2(sum[0], sum[1]);
+        w.y = pack_bf16x2(sum[2], sum[3]);
+        w.z = pack_bf16x2(sum[4], sum[5]);
+        w.w = pack_bf16x2(sum[6], sum[7]);
+        *reinterpret_cast<uint4*>(tile + r * kR + col) = w;
       }
+      __syncwarp();
+      if (lane < G) sm100::mbar_arrive_cluster(sm100::mapa_shared(sm100::smem_u32(cl_done), lane));
+      ++uc;
     }
   }
   sm100::tc_fence_before();
   __syncthreads();
+  sm100::cluster_sync();  // no CTA leaves while a peer may still read its partial tile
   if (warp == 1) {
     sm100::tc_fence_after();
     sm100::tmem_dealloc(tmem_base, 256);
@@ -617,9 +665,34 @@ int32_t launch_csa_tc(const void* q, int64_t sq, const void* k, int64_t sk, cons
   csa_stats_tc_kernel<DH><<<grid(static_cast<int64_t>(g.B) * g.H * g.nqt), 192,
                             StatsLayout<DH>::kSmem, s>>>(mq, mk, g, c, m, l, dev_status);
   count_launch();
-  csa_pbar_tc_kernel<DH><<<grid(static_cast<int64_t>(g.B) * g.nqt * g.nb), 320,
-                           PbarLayout<DH>::kSmem, s>>>(mq, mk, g, c, m, l, pbar, dev_status);
-  count_launch();
+  {
+    // few units (short prompts): a cluster of G CTAs per unit splits its heads
+    const int64_t units = static_cast<int64_t>(g.B) * g.nqt * g.nb;
+    int G = 1;
+    for (int d = 8; d >= 2; --d)
+      if (g.H % d == 0 && units * d <= sms) {
+        G = d;
+        break;
+      }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(
+        G * std::max<int64_t>(1, std::min<int64_t>(units, sms / G))));
+    cfg.blockDim = dim3(320);
+    cfg.dynamicSmemBytes = PbarLayout<DH>::kSmem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = static_cast<unsigned>(G);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e =
+        cudaLaunchKernelEx(&cfg, csa_pbar_tc_kernel<DH>, mq, mk, g, c, static_cast<const float*>(m),
+                           static_cast<const float*>(l), pbar, dev_status);
+    if (e != cudaSuccess) return static_cast<int32_t>(e);
+    count_launch();
+  }
   auto* o = static_cast<__nv_bfloat16*>(out);
   if (D % 256 == 0)
     csa_pv_tc_kernel<256><<<grid(static_cast<int64_t>(g.B) * g.nqt * (D / 256)), 192,

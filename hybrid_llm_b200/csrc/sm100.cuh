@@ -360,6 +360,30 @@ __device__ __forceinline__ uint32_t cluster_ctarank() {
 }
 
 // shared::cluster address of the same shared variable in CTA `rank`.
+// Number of CTAs in this CTA's cluster.
+__device__ __forceinline__ uint32_t cluster_nctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
+  return r;
+}
+
+// Cluster-scope fence: orders this thread's shared-memory writes before a later
+// release to peer CTAs, or peer writes seen through an acquire before later
+// distributed shared memory reads.
+__device__ __forceinline__ void fence_acq_rel_cluster() {
+  asm volatile("fence.acq_rel.cluster;" ::: "memory");
+}
+
+// 16 bytes of a (possibly peer) CTA's shared memory by shared::cluster address.
+__device__ __forceinline__ float4 ld_dsmem_f4(uint32_t cluster_addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(cluster_addr)
+               : "memory");
+  return v;
+}
+
 __device__ __forceinline__ uint32_t mapa_shared(uint32_t smem_addr, uint32_t rank) {
   uint32_t r;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr), "r"(rank));
