@@ -329,12 +329,9 @@ class LoopedHybridModel:
         k = proj[..., hd:2 * hd].unflatten(-1, (c.csa_heads, c.csa_head_dim))
         v = proj[..., 2 * hd:]
         local = kernels.csa_local_prefill(q, k, v, c.csa_window)
-        # out(local_out(local) [+ remote_out(remote)]) (csa.py:132) as one product with the
-        # pre-multiplied w_o = [out local_out | out remote_out] that decode uses too
-        d = c.d_model
-        mixed = torch.mm(local.view(bsz * t, -1), a.w_o[:, :d].t())
+        h = torch.mm(local.view(bsz * t, -1), a.local_out.t())
         if c.csa_compression:
-            # remote branch (csa.py:77-131)
+            # remote branch (csa.py:77-131): out(local_out(local) + remote_out(remote))
             remote, summ = kernels.csa_remote_prefill(
                 normed.view(bsz, t, -1), proj[..., :hd], a.w_comp, c.csa_compression, c.csa_top_k,
                 c.csa_heads, state.remote_sum[key], state.remote_pending[key])
@@ -345,7 +342,8 @@ class LoopedHybridModel:
             state.remote_k[key][:, :n] = summ[..., :hd]
             state.remote_v[key][:, :n] = summ[..., hd:]
             state.remote_count[key].fill_(n)
-            mixed.addmm_(remote.view(bsz * t, -1), a.w_o[:, d:].t())
+            h.addmm_(remote.view(bsz * t, -1), a.remote_out.t())
+        mixed = torch.mm(h, a.out.t())
         # ring caches for decode: token p at slot p % W (last min(T, W) tokens)
         kernels.csa_ring_write(proj[..., hd:2 * hd], proj[..., 2 * hd:], state.local_k[key],
                                state.local_v[key])
