@@ -831,19 +831,17 @@ def run_ours(args) -> None:
         t_ms = float(tt.item())
     value = bsz * args.steps * world / (t_ms * 1e-3)
 
-    # e2e: public decode API with a pinned-host token round trip per step
-    host_in = torch.empty(bsz, dtype=torch.int64).pin_memory()
-    host_out = torch.empty(bsz, dtype=torch.int64).pin_memory()
-    host_lp = torch.empty(bsz, dtype=torch.float32).pin_memory()
-    host_in.copy_(dec.tokens.cpu())
+    # e2e: public decode API with a pinned-host token round trip per step: the
+    # token in, the step and the token + log-probability out are one graph
+    # replay (GreedyDecoder.step_host), then the host waits and feeds the token back
+    dec.step_host()  # captures the host-I/O graph (one untimed step)
+    host_in, host_out, host_lp = dec.host_in, dec.host_out, dec.host_lp
     torch.cuda.synchronize()
+    host_in.copy_(host_out)
     a, b = _events()
     a.record()
     for _ in range(args.steps):
-        dec.tokens.copy_(host_in, non_blocking=True)
-        tok = dec.step()
-        host_out.copy_(tok, non_blocking=True)
-        host_lp.copy_(dec.logprob, non_blocking=True)
+        dec.step_host()
         torch.cuda.current_stream().synchronize()
         host_in.copy_(host_out)
     b.record()

@@ -639,8 +639,11 @@ class GreedyDecoder:
         self.sampling = dict(temperature=temperature, top_k=top_k, top_p=top_p,
                              repetition_penalty=repetition_penalty)
         self.graph = None
+        self.io_graph = None
         self.use_graph = use_graph
         self.logprob = None
+        # pinned host buffers of step_host (allocated on its first call)
+        self.host_in = self.host_out = self.host_lp = None
         # fp32 logits [B, V] of the last step (in graph mode the graph's own
         # output buffer, rewritten by every replay)
         self.logits = None
@@ -694,6 +697,31 @@ class GreedyDecoder:
         else:
             self._body()
         return self.tokens
+
+    def step_host(self) -> tuple[torch.Tensor, torch.Tensor]:
+        """One step with the host round trip inside the graph: the tokens in
+        self.host_in (pinned, [B] int64) go to the device, the step runs, and the
+        sampled tokens and their log-probabilities come back into self.host_out
+        and self.host_lp (pinned) -- one graph submission per step; the caller
+        synchronizes the stream before reading them.  Call step() once first (it
+        captures the step); the first step_host() call captures this graph."""
+        if self.graph is None:
+            raise RuntimeError("call step() once before step_host()")
+        if self.io_graph is None:
+            self.host_in = torch.empty(self.bsz, dtype=torch.int64).pin_memory()
+            self.host_out = torch.empty(self.bsz, dtype=torch.int64).pin_memory()
+            self.host_lp = torch.empty(self.bsz, dtype=torch.float32).pin_memory()
+            self.host_in.copy_(self.tokens.cpu())
+            torch.cuda.synchronize()
+            self.io_graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(self.io_graph):
+                self.tokens.copy_(self.host_in, non_blocking=True)
+                self._body()
+                self.host_out.copy_(self.tokens, non_blocking=True)
+                self.host_lp.copy_(self.logprob, non_blocking=True)
+            torch.cuda.synchronize()
+        self.io_graph.replay()
+        return self.host_out, self.host_lp
 
 
 class PrefillGraph:

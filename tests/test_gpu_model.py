@@ -79,6 +79,33 @@ def test_graph_decoder_matches_eager_decode(cuda):
     assert torch.equal(outs[0], outs[1])
 
 
+def test_host_io_graph_step_matches_graph_step(cuda):
+    """GreedyDecoder.step_host (token copies inside the graph) yields the tokens
+    and log-probabilities of step() on the same state."""
+    from hybrid_llm_b200.model import GreedyDecoder
+    m = _model(inputs.mini_config())
+    ids = torch.from_numpy(inputs.mini_prompt()).cuda()
+    runs = []
+    for host in (False, True):
+        o = m.forward(ids, last_logits_only=True)
+        dec = GreedyDecoder(m, o.state, use_graph=True)
+        dec.prime(o.logits[:, -1].float().argmax(-1))
+        toks, lps = [dec.step().clone()], [dec.logprob.clone()]
+        for _ in range(6):
+            if host:
+                t, lp = dec.step_host()
+                torch.cuda.current_stream().synchronize()
+                toks.append(t.clone().cuda())
+                lps.append(lp.clone().cuda())
+                dec.host_in.copy_(t)
+            else:
+                toks.append(dec.step().clone())
+                lps.append(dec.logprob.clone())
+        runs.append((torch.stack(toks, 1).cpu(), torch.stack(lps, 1).cpu()))
+    assert torch.equal(runs[0][0], runs[1][0])
+    assert torch.equal(runs[0][1], runs[1][1])
+
+
 def test_decode_equals_prefill_of_extended_sequence(cuda):
     """The reference's own parity check (sample_standalone.py:5474-5527): logits of a
     decode step equal the last-position logits of a prefill over the longer prompt."""
