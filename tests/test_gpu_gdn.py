@@ -61,7 +61,9 @@ def test_gdn_step_matches_oracle(cuda, b, h, kd, vd):
 
 @pytest.mark.parametrize("b,t,h,kd,vd,per_token", [
     (2, 150, 3, 64, 64, False), (1, 300, 2, 128, 128, True), (3, 64, 2, 64, 128, False),
-    (1, 1, 2, 128, 64, False), (2, 513, 4, 128, 128, False), (1, 200, 1, 64, 64, True)])
+    (1, 1, 2, 128, 64, False), (2, 513, 4, 128, 128, False), (1, 200, 1, 64, 64, True),
+    # 2*B*H > SMs: the value-lane scan (one CTA per row and head), K = 64 and 128
+    (5, 200, 16, 64, 128, False), (5, 130, 16, 128, 128, True)])
 def test_gdn_prefill_matches_oracle(cuda, b, t, h, kd, vd, per_token):
     from hybrid_llm_b200 import kernels
     q, k, v, beta, gate, dl, la, reset, state = _inputs(b, t, h, kd, vd, seed=t + kd, per_token=per_token)
