@@ -745,11 +745,9 @@ __global__ void __launch_bounds__(kPT, 1) decode_persistent_kernel(const llmyb_p
         gb.point(li * p.n_blocks + j, 4);
         const float inv1 = rsqrtf(sm.scal[0] / static_cast<float>(D) + eps);
         const float inv2 = rsqrtf(inv1 * inv1 * sm.scal[1] / static_cast<float>(D) + eps);
-        // every warp takes the top-k itself (value desc, index asc; softmax of
-        // the k values), so it can fetch its expert rows without another barrier
-        int my_e = 0;
-        float my_p = 0.f;
-        {
+        // warp 0 takes the top-k (value desc, index asc; softmax of the k values)
+        // while the others form the experts' input; one CTA barrier hands it on
+        if (warp == 0) {
           float v0 = lane < E ? sm.logit[lane] * inv1 * inv2 : -INFINITY;
           float v1 = lane + 32 < E ? sm.logit[lane + 32] * inv1 * inv2 : -INFINITY;
           float top = 0.f, mine = 0.f;
@@ -771,9 +769,9 @@ __global__ void __launch_bounds__(kPT, 1) decode_persistent_kernel(const llmyb_p
           }
           const float ex = lane < K ? expf(mine - top) : 0.f;
           const float den = warp_sum(ex);
-          my_e = min(max(mine_i, 0), E - 1);  // a NaN row must not pick a missing expert
-          my_p = ex / den;
-          if (warp == 0 && lane < K) {
+          if (lane < K) {
+            const int my_e = min(max(mine_i, 0), E - 1);  // a NaN row must not pick a missing expert
+            const float my_p = ex / den;
             sm.idx[lane] = my_e;
             sm.prob[lane] = my_p;
             if (cta == 0) {
@@ -781,17 +779,6 @@ __global__ void __launch_bounds__(kPT, 1) decode_persistent_kernel(const llmyb_p
               p.route_prob[(li * p.n_blocks + j) * K + lane] = my_p;
             }
           }
-        }
-        // this warp's first feature: fetch its gate / up rows now
-        const bf16* w13 = static_cast<const bf16*>(B.w13);
-        uint4 wg[DC], wu[DC];
-        int g_first = gw;
-        if (g_first < K * F) {
-          const int s0 = g_first / F, f0 = g_first - s0 * F;
-          const int e0 = __shfl_sync(0xffffffffu, my_e, s0);
-          const int64_t grow = static_cast<int64_t>(e0) * 2 * F + (f0 / 128) * 256 + (f0 % 128);
-          load_row<DC>(w13 + grow * D, n8, lane, wg);
-          load_row<DC>(w13 + (grow + 128) * D, n8, lane, wu);
         }
         // the experts' input m = RMSNorm(x) * ffn_norm (bf16)
         if (tid < n8) {
@@ -806,14 +793,13 @@ __global__ void __launch_bounds__(kPT, 1) decode_persistent_kernel(const llmyb_p
         }
         __syncthreads();
         gb.point(li * p.n_blocks + j, 5);
-        for (int g = g_first; g < K * F; g += NW) {
+        const bf16* w13 = static_cast<const bf16*>(B.w13);
+        uint4 wg[DC], wu[DC];
+        for (int g = gw; g < K * F; g += NW) {
           const int s = g / F, f = g - s * F;
-          if (g != g_first) {
-            const int e = __shfl_sync(0xffffffffu, my_e, s);
-            const int64_t grow = static_cast<int64_t>(e) * 2 * F + (f / 128) * 256 + (f % 128);
-            load_row<DC>(w13 + grow * D, n8, lane, wg);
-            load_row<DC>(w13 + (grow + 128) * D, n8, lane, wu);
-          }
+          const int64_t grow = static_cast<int64_t>(sm.idx[s]) * 2 * F + (f / 128) * 256 + (f % 128);
+          load_row<DC>(w13 + grow * D, n8, lane, wg);
+          load_row<DC>(w13 + (grow + 128) * D, n8, lane, wu);
           const float ga = row_dot<DC>(wg, s_vec, n8, lane);
           const float ua = row_dot<DC>(wu, s_vec, n8, lane);
           if (lane == 0) stcg_bf(hbuf + static_cast<int64_t>(s) * F + f, silu_mul(ga, ua));
