@@ -398,16 +398,14 @@ __global__ void __launch_bounds__(kPT, 1) decode_persistent_kernel(const llmyb_p
           __syncthreads();
           if (mine) {
             if (key == slot) {
-              // the new token: key from the projection, stored with its value
+              // the new token's key from the projection, into the ring (its
+              // value goes into the ring column by column in M2)
               for (int c = lane; c < hdc8; c += 32) {
                 const uint4 kv = ldcg16(proj + HDc + c * 8);
                 krow[c] = kv;
                 stcg16(ring_k + static_cast<int64_t>(slot) * HDc + c * 8, kv);
               }
               __syncwarp();
-              for (int c = lane; c < n8; c += 32)
-                stcg16(ring_v + static_cast<int64_t>(slot) * D + c * 8,
-                       ldcg16(proj + 2 * HDc + c * 8));
             }
             // per-head dots: chunk c covers dims [8c, 8c + 8) of head 8c / Dh;
             // the Dh / 8 lanes of a head reduce by xor shuffles
@@ -477,7 +475,13 @@ __global__ void __launch_bounds__(kPT, 1) decode_persistent_kernel(const llmyb_p
             }
           }
           const float xold = tid < 8 ? __ldcg(xdst + col0 + tid) : 0.f;
-          if (tid == 0 && slot < nk) sm.vring[slot] = ldcg16(ring_v + static_cast<int64_t>(slot) * D + col0);
+          if (tid == 0 && slot < nk) {
+            // the new token's value chunk of these columns, from the projection,
+            // also stored into the ring for the following steps
+            const uint4 vnew = ldcg16(proj + 2 * HDc + col0);
+            sm.vring[slot] = vnew;
+            stcg16(ring_v + static_cast<int64_t>(slot) * D + col0, vnew);
+          }
           // this thread's key's scores, in the same round of loads
           float sck[kMaxHeads];
 #pragma unroll
