@@ -799,7 +799,9 @@ __global__ void __launch_bounds__(kPT, 1) decode_persistent_kernel(const llmyb_p
         gb.point(li * p.n_blocks + j, 5);
         const bf16* w13 = static_cast<const bf16*>(B.w13);
         uint4 wg[DC], wu[DC];
-        for (int g = gw; g < K * F; g += NW) {
+        // features round-robin over the CTAs (warp w of CTA c: w * G + c, ...), so
+        // every SM streams about the same number of expert rows
+        for (int g = warp * G + cta; g < K * F; g += NW) {
           const int s = g / F, f = g - s * F;
           const int64_t grow = static_cast<int64_t>(sm.idx[s]) * 2 * F + (f / 128) * 256 + (f % 128);
           load_row<DC>(w13 + grow * D, n8, lane, wg);
@@ -816,7 +818,7 @@ __global__ void __launch_bounds__(kPT, 1) decode_persistent_kernel(const llmyb_p
         const bf16* w2 = static_cast<const bf16*>(B.w2);
         const int f8 = F >> 3;
         uint4 wd[FC];
-        const int r0 = gw;
+        const int r0 = warp * G + cta;  // rows round-robin over the CTAs
         bf16* wb = sm.wbuf[warp];
         if (r0 < K * D) {
           const int s = r0 / D, n = r0 - s * D;
