@@ -288,9 +288,19 @@ __global__ void __launch_bounds__(320, 1) band_tc_kernel(
       ++meets;
       return r;
     };
-    // exchange: [parity][half][row] bf16 block maxima; at a unit's end [half][row] fp32 sums
+    // exchange: [parity][half][row] bf16 block maxima; at a unit's end the
+    // pair's two fp32 row sums.  The four pairs meet only within themselves,
+    // so the sums must land in bytes that hold this pair's own rows of the
+    // maxima (slot s = parity * 2 + half covers bytes [256 s + 64 qw, +64) for
+    // pair qw): sum k = half * 32 + lane goes to float 64 (k / 16) + 16 qw +
+    // k % 16.  A layout that spilled into another pair's rows would overwrite
+    // maxima that pair is still exchanging.
     uint16_t* xmax = reinterpret_cast<uint16_t*>(smem + L::kX);
     float* xsum = reinterpret_cast<float*>(smem + L::kX);
+    auto xsum_at = [&](int h) -> int {
+      const int k = h * 32 + lane;
+      return 64 * (k >> 4) + 16 * qw + (k & 15);
+    };
     uint8_t* prow = smem + L::kP + row * 128;
     const int pswz = row & 7;
     int g = 0;
@@ -409,9 +419,9 @@ __global__ void __launch_bounds__(320, 1) band_tc_kernel(
       // the pair's two partial row sums, in the exchange area once both warps
       // have read this unit's last block maxima
       if (!pair_meet()) break;
-      xsum[half * 128 + row] = l;
+      xsum[xsum_at(half)] = l;
       if (!pair_meet()) break;
-      const float inv = 1.f / (xsum[row] + xsum[128 + row]);
+      const float inv = 1.f / (xsum[xsum_at(0)] + xsum[xsum_at(1)]);
       if (!pair_meet()) break;  // read before the next unit's first exchange overwrites
       if (!sm100::mbar_wait_warp(pv_done, (g - 1) & 1, dev_status, abort_flag)) break;
       sm100::tc_fence_after();
