@@ -519,6 +519,55 @@ def secondary_prefill_c2(p: dict, reps: int = 10) -> dict:
             "ms": t * 1e3, "tok_s": 512 / t, "roofline": prefill_roofline(model, cfg, 512, t, p)}
 
 
+def secondary_large_prefill(p: dict, reps: int = 2, chunk: int = 8, context: int = 4096,
+                            global_batch: int = 64) -> dict:
+    """Prompt forward of the large expert-parallel config on one GPU (d 2048,
+    24 blocks, 64 experts top-8, 3 loops, vocab 64000): the 64 x 4096-token
+    context as row chunks of `chunk` rows (prompt rows are independent, so a
+    chunk of 8 does 1/8 of the work; at 8 rows every tensor stays below 2^31
+    elements: 262,144 routed rows x 2048).  Eager forward (kernel-bound at
+    32,768 tokens per call), last-position logits only, each call from a
+    zeroed state; median over `reps` calls after one warm-up call."""
+    import numpy as np
+    import torch
+
+    from hybrid_llm_b200 import kernels
+    from hybrid_llm_b200.config import large_ep_config
+    from hybrid_llm_b200.model import LoopedHybridModel
+    from hybrid_llm_b200.state import RecurrentState
+    from hybrid_llm_b200.weights import ModelWeights, synthetic_state_dict
+
+    cfg = large_ep_config()
+    model = LoopedHybridModel(ModelWeights.from_state_dict(
+        cfg, synthetic_state_dict(cfg, seed=0, device="cuda"), "cuda"))
+    g = torch.Generator(device="cpu").manual_seed(0)
+    ids = torch.randint(0, cfg.vocab_size, (chunk, context), generator=g).cuda()
+    state = RecurrentState(cfg, chunk, "cuda")
+    out = model.forward(ids, state=state, last_logits_only=True)
+    torch.cuda.synchronize()
+    kernels.check_device_status()
+    ts = []
+    torch.cuda.nvtx.range_push("large_prefill_timed")
+    for _ in range(max(1, reps)):
+        state.zero_()
+        a, b = _events()
+        a.record()
+        out = model.forward(ids, state=state, last_logits_only=True)
+        b.record()
+        torch.cuda.synchronize()
+        ts.append(a.elapsed_time(b))
+    torch.cuda.nvtx.range_pop()
+    kernels.check_device_status()
+    finite = bool(torch.isfinite(out.logits).all())
+    t = float(np.median(ts)) * 1e-3
+    tokens = chunk * context
+    return {"workload": f"large-config prompt prefill, {context} tokens x {global_batch} rows as "
+                        f"{global_batch // chunk} chunks of {chunk} rows, one GPU, eager forward",
+            "chunk_rows": chunk, "ms_per_chunk": t * 1e3, "tok_s": tokens / t,
+            "ms_for_global_batch": t * 1e3 * global_batch / chunk, "logits_finite": finite,
+            "roofline": prefill_roofline(model, cfg, context, t, p, batch=chunk)}
+
+
 def secondary_mhc(p: dict, reps: int = 10) -> dict:
     """Hyper-connection read / write around one sub-layer: 16384 tokens x D=1024
     with 4 fp32 streams (256 MB, above L2), L2 flushed before each timed call.
@@ -900,6 +949,8 @@ def run_ours(args) -> None:
         secondary["single_block"] = secondary_block(p)
         secondary["moe_layer"] = secondary_moe(p)
         secondary["long_prefill"] = secondary_prefill(p)
+        secondary["large_prefill"] = secondary_large_prefill(p)
+        torch.cuda.empty_cache()
         secondary["mhc"] = secondary_mhc(p)
         secondary["sampling_router"] = secondary_sampling_router(p)
     if secondary:
@@ -912,8 +963,8 @@ def run_ours(args) -> None:
         dist.destroy_process_group()
 
 
-def prefill_roofline(model, cfg, tokens: int, seconds: float, p: dict) -> dict:
-    """Roofline of a B=1 prefill of `tokens` ids: the algorithmic HBM bytes
+def prefill_roofline(model, cfg, tokens: int, seconds: float, p: dict, batch: int = 1) -> dict:
+    """Roofline of a prefill of `batch` rows of `tokens` ids: the algorithmic HBM bytes
     (every dense weight and every expert once per loop -- at 512 tokens and
     top-2 each of the 16 experts receives rows --, the LM head row block of
     the last token) against the algorithmic FLOPs (2 x the weights each token
@@ -940,12 +991,13 @@ def prefill_roofline(model, cfg, tokens: int, seconds: float, p: dict) -> dict:
             dense_params += w.numel()
         expert_bytes += nb(blk.moe.w13) + nb(blk.moe.w2)
     act_expert = 3 * cfg.moe_hidden * d * cfg.moe_top_k * cfg.n_blocks
-    flops = nl * (2.0 * tokens * (dense_params + act_expert) + attn_flops) + 2.0 * cfg.vocab_size * d
-    bytes_ = nl * (dense_bytes + expert_bytes) + cfg.vocab_size * d * 2 + tokens * d * 2
+    flops = batch * (nl * (2.0 * tokens * (dense_params + act_expert) + attn_flops) +
+                     2.0 * cfg.vocab_size * d)
+    bytes_ = nl * (dense_bytes + expert_bytes) + cfg.vocab_size * d * 2 + batch * tokens * d * 2
     t_hbm = bytes_ / (p["hbm_gbs"] * 1e9)
     t_tc = flops / (p["bf16_tflops"] * 1e12)
     t_roof = max(t_hbm, t_tc)
-    return {"bound": "hbm" if t_hbm >= t_tc else "tensor", "tokens": tokens,
+    return {"bound": "hbm" if t_hbm >= t_tc else "tensor", "tokens": tokens, "batch": batch,
             "algorithmic_bytes": bytes_, "algorithmic_flops": flops,
             "t_roofline_ms": t_roof * 1e3, "t_ms": seconds * 1e3, "frac": t_roof / seconds,
             "achieved_gbs": bytes_ / seconds / 1e9, "achieved_tflops": flops / seconds / 1e12}
@@ -991,7 +1043,7 @@ def main() -> None:
     ap.add_argument("--ep-exchange", choices=["p2p", "nccl"], default="p2p",
                     help="expert-parallel exchange of --only ep_decode")
     ap.add_argument("--only", choices=["single_block", "moe_layer", "long_prefill", "ep_decode",
-                                       "mhc", "sampling_router", "prefill_c2"],
+                                       "mhc", "sampling_router", "prefill_c2", "large_prefill"],
                     default=None,
                     help="run one secondary workload alone (used for kernel profiles)")
     ap.add_argument("--prefill-batch", type=int, default=8,
@@ -1024,6 +1076,8 @@ def main() -> None:
             res = secondary_block(peaks(), reps=args.steps)
         elif args.only == "prefill_c2":
             res = secondary_prefill_c2(peaks())
+        elif args.only == "large_prefill":
+            res = secondary_large_prefill(peaks(), reps=args.steps, chunk=args.prefill_batch)
         elif args.only == "sampling_router":
             res = secondary_sampling_router(peaks())
         elif args.only == "mhc":
