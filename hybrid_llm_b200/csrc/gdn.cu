@@ -70,6 +70,69 @@ __global__ void gdn_activate_kernel(__nv_bfloat16* __restrict__ proj, int64_t N,
   }
 }
 
+// The same activation on 16-byte pieces (8 bf16) for rows whose width is a
+// multiple of 8 elements (the model pads its fused projection to that).
+// Threads [0, n_norm) take one piece of a q or k head each, KD / 8
+// consecutive lanes per head, and form the head's sum of squares with xor
+// shuffles inside that lane group; threads [n_norm, n_norm + n_gate) take one
+// piece of a gate head, and the first piece of each head also its beta.  Each
+// element is read once and written once (the per-head warp kernel above reads
+// q and k twice, two bytes per lane).
+__global__ void gdn_activate_vec_kernel(__nv_bfloat16* __restrict__ proj, uint32_t n_norm,
+                                        uint32_t n_gate, int width, int H, int KD, int VD,
+                                        const float* __restrict__ beta_bias) {
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n_norm) {
+    const uint32_t kp = static_cast<uint32_t>(KD) >> 3;  // pieces per head: 2..32, power of 2
+    const uint32_t per_tok = 2u * static_cast<uint32_t>(H) * kp;
+    const uint32_t tok = i / per_tok;
+    uint4* p = reinterpret_cast<uint4*>(proj + static_cast<int64_t>(tok) * width +
+                                        static_cast<int64_t>(i - tok * per_tok) * 8);
+    uint4 u = *p;
+    uint32_t w[4] = {u.x, u.y, u.z, u.w};
+    float v[8];
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = unpack_bf16x2(w[j]);
+      v[2 * j] = f.x;
+      v[2 * j + 1] = f.y;
+      ss += f.x * f.x + f.y * f.y;
+    }
+    // n_norm is a multiple of kp and groups start at multiples of kp, so a
+    // group never straddles a warp or the end of the q/k range
+    const int lane = threadIdx.x & 31;
+    const uint32_t gmask = (kp >= 32 ? 0xffffffffu : ((1u << kp) - 1u)) << (lane & ~(kp - 1u));
+    for (uint32_t o = kp >> 1; o > 0; o >>= 1) ss += __shfl_xor_sync(gmask, ss, o);
+    const float sc = rsqrtf(fmaxf(ss, 1e-12f));
+    u.x = pack_bf16x2(v[0] * sc, v[1] * sc);
+    u.y = pack_bf16x2(v[2] * sc, v[3] * sc);
+    u.z = pack_bf16x2(v[4] * sc, v[5] * sc);
+    u.w = pack_bf16x2(v[6] * sc, v[7] * sc);
+    *p = u;
+  } else if (i - n_norm < n_gate) {
+    const uint32_t j = i - n_norm;
+    const uint32_t per_tok = static_cast<uint32_t>(H * VD) >> 3;
+    const uint32_t tok = j / per_tok;
+    const uint32_t off = (j - tok * per_tok) * 8;  // element offset inside the gate block
+    __nv_bfloat16* row = proj + static_cast<int64_t>(tok) * width;
+    uint4* p = reinterpret_cast<uint4*>(row + 2 * H * KD + H * VD + off);
+    uint4 u = *p;
+    uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float2 f = unpack_bf16x2(w[k]);
+      w[k] = pack_bf16x2(sigmoidf_(f.x), sigmoidf_(f.y));
+    }
+    *p = make_uint4(w[0], w[1], w[2], w[3]);
+    if (off % VD == 0) {
+      const int h = static_cast<int>(off / VD);
+      __nv_bfloat16* b = row + 2 * H * KD + 2 * H * VD + h;
+      *b = f2bf(sigmoidf_(bf2f(*b) + (beta_bias ? beta_bias[h] : 0.f)));
+    }
+  }
+}
+
 // --------------------------------------------------------------- decode
 struct GdnIO {
   const __nv_bfloat16 *q, *k, *v, *gate, *beta;  // token-major with strides below
@@ -889,6 +952,95 @@ __global__ void gdn_conv_gate_kernel(const __nv_bfloat16* __restrict__ x,
       residual[i] = f2bf(bf2f(residual[i]) + bf2f(f2bf(yv)));
     } else {
       out[i] = f2bf(yv);
+    }
+  }
+}
+
+// The prompt form of the conv gate (no history, so taps before the row's
+// first token are zero) on 16-byte pieces: a thread owns 8 channels of one
+// row over a run of `run` tokens and slides the 4-tap window along it in
+// registers, so each input row is read once per run (plus three warm-up rows)
+// instead of once per tap, and the 8 x 4 filter taps are loaded once.  A reset
+// at token t clears the three older taps before x[t] enters the window, which
+// keeps exactly the taps at or after the latest reset in [t - 3, t] (the
+// same-segment rule of the kernel above).  Consecutive threads take
+// consecutive channel pieces of the same run, so a warp reads 512 contiguous
+// bytes per token.  Result into out, or added into residual.
+__global__ void __launch_bounds__(256) gdn_conv_gate_run_kernel(
+    const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ y_proj,
+    const float* __restrict__ conv_w, const uint8_t* __restrict__ reset, int B, int T, int D,
+    int run, __nv_bfloat16* __restrict__ dst, int add) {
+  const uint32_t nc = static_cast<uint32_t>(D) >> 3;
+  const uint32_t runs = (static_cast<uint32_t>(T) + run - 1) / run;
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= static_cast<uint32_t>(B) * runs * nc) return;
+  const uint32_t c = i % nc, rr = i / nc;
+  const int r = static_cast<int>(rr % runs), b = static_cast<int>(rr / runs);
+  float w[8][4];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const float4 f = __ldg(reinterpret_cast<const float4*>(conv_w) + c * 8 + k);
+    w[k][0] = f.x;
+    w[k][1] = f.y;
+    w[k][2] = f.z;
+    w[k][3] = f.w;
+  }
+  const int64_t row0 = static_cast<int64_t>(b) * T;
+  // the window holds the inputs as they are stored (bf16 pairs): x[t-3],
+  // x[t-2], x[t-1] of the next token t
+  uint32_t win[3][4];
+#pragma unroll
+  for (int j = 0; j < 3; ++j)
+#pragma unroll
+    for (int k = 0; k < 4; ++k) win[j][k] = 0u;
+  const int t0 = r * run, t1 = min(T, t0 + run);
+  for (int t = max(0, t0 - 3); t < t1; ++t) {
+    if (reset != nullptr && reset[row0 + t]) {
+#pragma unroll
+      for (int j = 0; j < 3; ++j)
+#pragma unroll
+        for (int k = 0; k < 4; ++k) win[j][k] = 0u;
+    }
+    const int64_t off = (row0 + t) * D + static_cast<int64_t>(c) * 8;
+    const uint4 xu = __ldg(reinterpret_cast<const uint4*>(x + off));
+    const uint32_t xw[4] = {xu.x, xu.y, xu.z, xu.w};
+    if (t >= t0) {
+      const uint4 yu = __ldg(reinterpret_cast<const uint4*>(y_proj + off));
+      const uint32_t yw[4] = {yu.x, yu.y, yu.z, yu.w};
+      uint4 ru = make_uint4(0u, 0u, 0u, 0u);
+      if (add) ru = *reinterpret_cast<const uint4*>(dst + off);
+      const uint32_t rw[4] = {ru.x, ru.y, ru.z, ru.w};
+      uint32_t ow[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 a0 = unpack_bf16x2(win[0][k]), a1 = unpack_bf16x2(win[1][k]);
+        const float2 a2 = unpack_bf16x2(win[2][k]), a3 = unpack_bf16x2(xw[k]);
+        float acc0 = 0.f, acc1 = 0.f;
+        acc0 += w[2 * k][0] * a0.x;
+        acc0 += w[2 * k][1] * a1.x;
+        acc0 += w[2 * k][2] * a2.x;
+        acc0 += w[2 * k][3] * a3.x;
+        acc1 += w[2 * k + 1][0] * a0.y;
+        acc1 += w[2 * k + 1][1] * a1.y;
+        acc1 += w[2 * k + 1][2] * a2.y;
+        acc1 += w[2 * k + 1][3] * a3.y;
+        const float2 yf = unpack_bf16x2(yw[k]);
+        const float o0 = yf.x * sigmoidf_(acc0), o1 = yf.y * sigmoidf_(acc1);
+        if (add) {
+          const float2 rf = unpack_bf16x2(rw[k]);
+          const float2 of = unpack_bf16x2(pack_bf16x2(o0, o1));
+          ow[k] = pack_bf16x2(rf.x + of.x, rf.y + of.y);
+        } else {
+          ow[k] = pack_bf16x2(o0, o1);
+        }
+      }
+      *reinterpret_cast<uint4*>(dst + off) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      win[0][k] = win[1][k];
+      win[1][k] = win[2][k];
+      win[2][k] = xw[k];
     }
   }
 }
@@ -1801,6 +1953,19 @@ LLMYB_API int32_t llmyb_gdn_activate(void* proj, int64_t n_tokens, int32_t width
   if (!proj || n_tokens < 0 || heads <= 0 || key_dim <= 0 || value_dim <= 0) return LLMYB_EINVAL;
   if (width < 2 * heads * (key_dim + value_dim) + heads) return LLMYB_EINVAL;
   if (n_tokens == 0) return LLMYB_OK;
+  const int kp = key_dim / 8;
+  const int64_t n_norm = n_tokens * 2 * heads * static_cast<int64_t>(kp);
+  const int64_t n_gate = n_tokens * heads * static_cast<int64_t>(value_dim) / 8;
+  if (width % 8 == 0 && key_dim % 8 == 0 && value_dim % 8 == 0 && kp <= 32 &&
+      (kp & (kp - 1)) == 0 && (reinterpret_cast<uintptr_t>(proj) & 15u) == 0 &&
+      n_norm + n_gate < (int64_t{1} << 31)) {
+    gdn_activate_vec_kernel<<<static_cast<int>(ceil_div(n_norm + n_gate, 256)), 256, 0,
+                              static_cast<cudaStream_t>(stream)>>>(
+        static_cast<__nv_bfloat16*>(proj), static_cast<uint32_t>(n_norm),
+        static_cast<uint32_t>(n_gate), width, heads, key_dim, value_dim, beta_bias);
+    count_launch();
+    return launch_status();
+  }
   const int64_t warps = n_tokens * heads;
   gdn_activate_kernel<<<static_cast<int>(ceil_div(warps * 32, 256)), 256, 0,
                         static_cast<cudaStream_t>(stream)>>>(
@@ -1912,6 +2077,23 @@ LLMYB_API int32_t llmyb_gdn_conv_gate(const void* x, const void* y_proj, const f
   if (batch == 0 || seq == 0) return LLMYB_OK;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int64_t total = static_cast<int64_t>(batch) * seq * d_model;
+  void* dst = residual ? residual : out;
+  if (!history && d_model % 8 == 0 &&
+      ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y_proj) |
+        reinterpret_cast<uintptr_t>(conv_w) | reinterpret_cast<uintptr_t>(dst)) & 15u) == 0 &&
+      total / 8 < (int64_t{1} << 30)) {
+    // runs long enough to amortise the three warm-up rows, short enough to
+    // leave a few thousand threads per SM
+    const int64_t pieces = total / 8;
+    int run = 1;
+    while (run < 16 && pieces / (2 * run) >= static_cast<int64_t>(num_sms()) * 2048) run *= 2;
+    const int64_t threads = static_cast<int64_t>(batch) * ceil_div(seq, run) * (d_model / 8);
+    gdn_conv_gate_run_kernel<<<static_cast<int>(ceil_div(threads, 256)), 256, 0, s>>>(
+        static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(y_proj), conv_w,
+        reset, batch, seq, d_model, run, static_cast<__nv_bfloat16*>(dst), residual ? 1 : 0);
+    count_launch();
+    return launch_status();
+  }
   const int grid = static_cast<int>(std::min<int64_t>(ceil_div(total, 256), 148 * 16));
   gdn_conv_gate_kernel<<<grid, 256, 0, s>>>(
       static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(y_proj), conv_w,

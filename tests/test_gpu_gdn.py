@@ -196,3 +196,70 @@ def test_gdn_step_raw_inputs_equal_activated_inputs(cuda):
     torch.cuda.synchronize()
     assert _rel(_f(o_raw), _f(o_act)) < 2e-2
     assert _rel(s_raw.cpu().numpy(), s_act.cpu().numpy()) < 1e-2
+
+
+def _torch_conv_gate(x, y, w, reset, residual=None):
+    """fp32 torch restatement of the prompt conv gate: tap x[t - s] (s = 3..0)
+    is kept when it exists and no reset lies in (t - s, t]."""
+    xf, yf = x.float(), y.float()
+    b, t, d = xf.shape
+    seg = torch.cumsum(reset.int(), dim=1)
+    acc = torch.zeros_like(xf)
+    for j in range(4):
+        s = 3 - j
+        xs = torch.zeros_like(xf)
+        ok = torch.zeros(b, t, dtype=torch.bool, device=x.device)
+        if s < t:
+            xs[:, s:] = xf[:, :t - s]
+            ok[:, s:] = seg[:, :t - s] == seg[:, s:]
+        acc += w[:, j].float() * xs * ok[..., None]
+    out = (yf * torch.sigmoid(acc)).bfloat16().float()
+    return out if residual is None else residual.float() + out
+
+
+@pytest.mark.parametrize("b,t,d", [(3, 100, 256), (4, 4096, 512), (8, 4096, 2048)])
+@pytest.mark.parametrize("add", [False, True])
+def test_conv_gate_prompt_runs_match_torch(cuda, b, t, d, add):
+    """The run kernel of the prompt conv gate (each thread slides the taps over
+    1 to 16 tokens; the three sizes select runs of 1, 2 and 8) with resets at
+    run boundaries, inside runs and at token 0."""
+    from hybrid_llm_b200 import kernels
+    g = torch.Generator(device="cuda").manual_seed(b * t + d)
+    x = torch.randn(b, t, d, device="cuda", generator=g).bfloat16()
+    y = torch.randn(b, t, d, device="cuda", generator=g).bfloat16()
+    w = torch.randn(d, 4, device="cuda", generator=g) * 0.3
+    reset = torch.zeros(b, t, dtype=torch.bool, device="cuda")
+    for p in (0, 1, 15, 16, 17, 31, 33, 34, t - 1):
+        reset[p % b, min(p, t - 1)] = True
+    reset[:, :: 97] |= torch.rand(b, (t + 96) // 97, device="cuda", generator=g) < 0.5
+    res = torch.randn(b, t, d, device="cuda", generator=g).bfloat16() if add else None
+    got = kernels.gdn_conv_gate(x, y, w, reset=reset,
+                                residual=None if res is None else res.clone())
+    kernels.check_device_status()
+    ref = _torch_conv_gate(x, y, w, reset, res)
+    err = (got.float() - ref).abs().max().item() / ref.abs().max().item()
+    assert err < 1e-2, err
+
+
+@pytest.mark.parametrize("h,kd,vd", [(12, 64, 64), (16, 128, 128), (4, 128, 64)])
+def test_gdn_activate_vector_path_matches_reference(cuda, h, kd, vd):
+    """16-byte rows (the model's padded projection) take the piece-per-thread
+    kernel, other widths the per-head warp kernel; both against fp64."""
+    from hybrid_llm_b200 import kernels
+    n = 300
+    base = 2 * h * (kd + vd) + h
+    g = torch.Generator(device="cuda").manual_seed(h + kd)
+    bias = torch.randn(h, device="cuda", generator=g)
+    for width in (base + (-base) % 8, base + (1 if (base + 1) % 8 else 2)):
+        proj = (torch.randn(n, width, device="cuda", generator=g) * 2).bfloat16()
+        ref = proj.double().clone()
+        kernels.gdn_activate(proj, h, kd, vd, bias)
+        kernels.check_device_status()
+        hk, hv = h * kd, h * vd
+        qk = ref[:, :2 * hk].view(n, 2 * h, kd)
+        ref[:, :2 * hk] = (qk / qk.square().sum(-1, keepdim=True).clamp_min(1e-12).sqrt()).view(n, -1)
+        ref[:, 2 * hk + hv:2 * hk + 2 * hv] = torch.sigmoid(ref[:, 2 * hk + hv:2 * hk + 2 * hv])
+        ref[:, 2 * hk + 2 * hv:2 * hk + 2 * hv + h] = torch.sigmoid(
+            ref[:, 2 * hk + 2 * hv:2 * hk + 2 * hv + h] + bias.double())
+        err = (proj.double() - ref).abs().max().item()
+        assert err < 8e-3, (width, err)
