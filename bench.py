@@ -1000,6 +1000,8 @@ def prefill_roofline(model, cfg, tokens: int, seconds: float, p: dict, batch: in
     return {"bound": "hbm" if t_hbm >= t_tc else "tensor", "tokens": tokens, "batch": batch,
             "algorithmic_bytes": bytes_, "algorithmic_flops": flops,
             "t_roofline_ms": t_roof * 1e3, "t_ms": seconds * 1e3, "frac": t_roof / seconds,
+            "frac_of_sustained_peaks": max(
+                t_hbm, flops / (p.get("bf16_tflops_sustained", p["bf16_tflops"]) * 1e12)) / seconds,
             "achieved_gbs": bytes_ / seconds / 1e9, "achieved_tflops": flops / seconds / 1e12}
 
 

@@ -534,16 +534,31 @@ __global__ void gather_rows_kernel(const __nv_bfloat16* __restrict__ x,
                                    const int* __restrict__ perm_token, int64_t rows, int D,
                                    __nv_bfloat16* __restrict__ x_perm,
                                    const int* __restrict__ valid_rows) {
+  // one warp per row: the row's source index is loaded once, and each lane
+  // has up to eight 16-byte copies in flight (no per-vector division)
+  constexpr int kUnroll = 8;
   const int vec = D / 8;
   if (valid_rows != nullptr) rows = min(rows, static_cast<int64_t>(__ldg(valid_rows)));
-  const int64_t total = rows * vec;
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t pos = i / vec;
-    const int c = static_cast<int>(i - pos * vec);
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t pos = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
+       pos < rows; pos += warps) {
     const int t = __ldg(perm_token + pos);
-    reinterpret_cast<uint4*>(x_perm + pos * D)[c] =
-        __ldg(reinterpret_cast<const uint4*>(x + static_cast<int64_t>(t) * D) + c);
+    const uint4* src = reinterpret_cast<const uint4*>(x + static_cast<int64_t>(t) * D);
+    uint4* dst = reinterpret_cast<uint4*>(x_perm + pos * D);
+    for (int c0 = 0; c0 < vec; c0 += 32 * kUnroll) {
+      uint4 v[kUnroll];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const int c = c0 + u * 32 + lane;
+        if (c < vec) v[u] = __ldg(src + c);
+      }
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const int c = c0 + u * 32 + lane;
+        if (c < vec) dst[c] = v[u];
+      }
+    }
   }
 }
 
@@ -623,7 +638,7 @@ int32_t run_grouped(const __nv_bfloat16* x, int32_t d_model, int64_t rows,
                     cudaStream_t s) {
   int32_t st = ensure_gemm_attrs();
   if (st) return st;
-  gather_rows_kernel<<<grid_for(rows * (d_model / 8), 256), 256, 0, s>>>(
+  gather_rows_kernel<<<grid_for(rows * 32, 256), 256, 0, s>>>(
       x, perm_token, rows, d_model, x_perm, valid_count ? expert_offsets + n_experts : nullptr);
   count_launch();
 

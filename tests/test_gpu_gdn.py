@@ -221,7 +221,7 @@ def _torch_conv_gate(x, y, w, reset, residual=None):
 @pytest.mark.parametrize("add", [False, True])
 def test_conv_gate_prompt_runs_match_torch(cuda, b, t, d, add):
     """The run kernel of the prompt conv gate (each thread slides the taps over
-    1 to 16 tokens; the three sizes select runs of 1, 2 and 8) with resets at
+    1 to 16 tokens; the three sizes select runs of 1, 2 and 16) with resets at
     run boundaries, inside runs and at token 0."""
     from hybrid_llm_b200 import kernels
     g = torch.Generator(device="cuda").manual_seed(b * t + d)
