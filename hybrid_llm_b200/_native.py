@@ -93,6 +93,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "llmyb_embed": (I32, [P, I64, P, I64, I32, P, P, P, P]),
     "llmyb_add_rmsnorm": (I32, [P, P, I64, I32, P, F32, I32, P, P, P]),
     "llmyb_add_rmsnorm_routed": (I32, [P, P, P, I32, I64, I32, P, F32, I32, P, P, P]),
+    "llmyb_add_rmsnorm_router": (I32, [P, P, I64, I32, P, P, F32, P, P, P]),
     "llmyb_decode_norm_gemv": (I32, [P, P, P, I32, I32, I32, P, F32, P, I32, P, I64, P, P, P]),
     "llmyb_decode_out_router": (I32, [P, I64, I32, P, I32, I32, P, P, P, P, P, P, P, P, F32, I32,
                                       I32, I32, P, P, P, P, P, P, P, P, P, P]),

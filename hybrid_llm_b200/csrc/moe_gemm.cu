@@ -573,15 +573,29 @@ __global__ void combine_rows_kernel(const __nv_bfloat16* __restrict__ y_perm,
     const int64_t t = i / vec;
     const int c = static_cast<int>(i - t * vec);
     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    for (int s = 0; s < k; ++s) {
-      const int pos = __ldg(route_pos + t * k + s);
-      const uint4 v = __ldg(reinterpret_cast<const uint4*>(y_perm + static_cast<int64_t>(pos) * D) + c);
-      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    // up to eight slots at a time: their positions, then their row pieces, are
+    // loaded together (one dependent round each instead of one per slot);
+    // the sum stays in slot order
+    for (int s0 = 0; s0 < k; s0 += 8) {
+      int pos[8];
+      uint4 v[8];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float2 f = unpack_bf16x2(w[j]);
-        acc[2 * j] += f.x;
-        acc[2 * j + 1] += f.y;
+      for (int u = 0; u < 8; ++u)
+        if (s0 + u < k) pos[u] = __ldg(route_pos + t * k + s0 + u);
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        if (s0 + u < k)
+          v[u] = __ldg(reinterpret_cast<const uint4*>(y_perm + static_cast<int64_t>(pos[u]) * D) + c);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        if (s0 + u >= k) break;
+        const uint32_t w[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = unpack_bf16x2(w[j]);
+          acc[2 * j] += f.x;
+          acc[2 * j + 1] += f.y;
+        }
       }
     }
     uint4 o;

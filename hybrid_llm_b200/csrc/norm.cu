@@ -77,12 +77,18 @@ __global__ void __launch_bounds__(256) add_rmsnorm_kernel(
 // between the sum of squares and the scaled write); the routed delta rows of
 // a vector are loaded together.  The per-element sum order (stream value,
 // then the k routed rows in slot order) is that of add_rmsnorm_kernel.
-template <int VMAX>
+// kRouter: out_f32 receives the router's input RMSNorm(y) * weight2 instead of
+// y (context_router.py:62, local = norm(hidden) on the FFN-normalised row),
+// with the second sum of squares formed exactly as a separate add_rmsnorm
+// pass over y would (same per-thread order, same block reduction).
+template <int VMAX, bool kRouter = false>
 __global__ void __launch_bounds__(256) add_rmsnorm_vec_kernel(
     float* __restrict__ streams, const __nv_bfloat16* __restrict__ delta,
     const int* __restrict__ route_pos, int k, int D, const float* __restrict__ weight, float eps,
-    int normalize, __nv_bfloat16* __restrict__ out_bf16, float* __restrict__ out_f32) {
+    int normalize, __nv_bfloat16* __restrict__ out_bf16, float* __restrict__ out_f32,
+    const float* __restrict__ weight2 = nullptr) {
   __shared__ float red[8];
+  __shared__ float red2[8];
   const int64_t n = blockIdx.x;
   const int nv = D >> 3;
   float4* x4 = reinterpret_cast<float4*>(streams + n * D);
@@ -159,10 +165,41 @@ __global__ void __launch_bounds__(256) add_rmsnorm_vec_kernel(
       o.w = pack_bf16x2(y[6], y[7]);
       reinterpret_cast<uint4*>(out_bf16 + n * D)[c] = o;
     }
-    if (out_f32 != nullptr) {
+    if constexpr (kRouter) {
+#pragma unroll
+      for (int q = 0; q < 8; ++q) v[j][q] = y[q];
+    } else if (out_f32 != nullptr) {
       float4* o4 = reinterpret_cast<float4*>(out_f32 + n * D);
       o4[2 * c] = make_float4(y[0], y[1], y[2], y[3]);
       o4[2 * c + 1] = make_float4(y[4], y[5], y[6], y[7]);
+    }
+  }
+  if constexpr (kRouter) {
+    float ss2 = 0.f;
+#pragma unroll
+    for (int j = 0; j < VMAX; ++j) {
+      if (threadIdx.x + j * 256 >= nv) continue;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) ss2 += v[j][q] * v[j][q];
+    }
+    ss2 = warp_sum(ss2);
+    if ((threadIdx.x & 31) == 0) red2[threadIdx.x >> 5] = ss2;
+    __syncthreads();
+    float tot2 = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) tot2 += red2[i];
+    const float r2 = rsqrtf(tot2 / static_cast<float>(D) + eps);
+#pragma unroll
+    for (int j = 0; j < VMAX; ++j) {
+      const int c = threadIdx.x + j * 256;
+      if (c >= nv) continue;
+      const float4 wa = __ldg(reinterpret_cast<const float4*>(weight2) + 2 * c);
+      const float4 wb = __ldg(reinterpret_cast<const float4*>(weight2) + 2 * c + 1);
+      float4* o4 = reinterpret_cast<float4*>(out_f32 + n * D);
+      o4[2 * c] = make_float4(v[j][0] * r2 * wa.x, v[j][1] * r2 * wa.y, v[j][2] * r2 * wa.z,
+                              v[j][3] * r2 * wa.w);
+      o4[2 * c + 1] = make_float4(v[j][4] * r2 * wb.x, v[j][5] * r2 * wb.y, v[j][6] * r2 * wb.z,
+                                  v[j][7] * r2 * wb.w);
     }
   }
 }
@@ -318,6 +355,42 @@ LLMYB_API int32_t llmyb_add_rmsnorm_routed(float* streams, const void* y_rows,
                             n_tokens, d_model, weight, eps, normalize,
                             static_cast<__nv_bfloat16*>(out_bf16), out_f32,
                             static_cast<cudaStream_t>(stream));
+}
+
+// streams += delta; m = RMSNorm(streams) * ffn_weight (bf16 into out_bf16);
+// router_in = RMSNorm(m) * router_weight (fp32), in one pass over the row.
+LLMYB_API int32_t llmyb_add_rmsnorm_router(float* streams, const void* delta, int64_t n_tokens,
+                                           int32_t d_model, const float* ffn_weight,
+                                           const float* router_weight, float eps,
+                                           void* out_bf16, float* router_in, void* stream) {
+  if (!streams || !ffn_weight || !router_weight || !router_in || n_tokens < 0 || d_model <= 0)
+    return LLMYB_EINVAL;
+  if (n_tokens == 0) return LLMYB_OK;
+  const uintptr_t align = reinterpret_cast<uintptr_t>(streams) |
+                          reinterpret_cast<uintptr_t>(delta) |
+                          reinterpret_cast<uintptr_t>(ffn_weight) |
+                          reinterpret_cast<uintptr_t>(router_weight) |
+                          reinterpret_cast<uintptr_t>(out_bf16) |
+                          reinterpret_cast<uintptr_t>(router_in);
+  if (d_model % 8 != 0 || (align & 15u) != 0 || d_model > 8 * 256 * 4) return LLMYB_EUNSUPPORTED;
+  const unsigned grid = static_cast<unsigned>(n_tokens);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const auto* dl = static_cast<const __nv_bfloat16*>(delta);
+  auto* ob = static_cast<__nv_bfloat16*>(out_bf16);
+  if (d_model <= 8 * 256)
+    add_rmsnorm_vec_kernel<1, true><<<grid, 256, 0, s>>>(streams, dl, nullptr, 0, d_model,
+                                                         ffn_weight, eps, 1, ob, router_in,
+                                                         router_weight);
+  else if (d_model <= 8 * 256 * 2)
+    add_rmsnorm_vec_kernel<2, true><<<grid, 256, 0, s>>>(streams, dl, nullptr, 0, d_model,
+                                                         ffn_weight, eps, 1, ob, router_in,
+                                                         router_weight);
+  else
+    add_rmsnorm_vec_kernel<4, true><<<grid, 256, 0, s>>>(streams, dl, nullptr, 0, d_model,
+                                                         ffn_weight, eps, 1, ob, router_in,
+                                                         router_weight);
+  count_launch();
+  return launch_status();
 }
 
 LLMYB_API int32_t llmyb_rmsnorm_bf16(const void* x, int64_t n_tokens, int32_t d_model,

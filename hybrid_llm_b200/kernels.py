@@ -880,6 +880,28 @@ def add_rmsnorm(streams: torch.Tensor, delta: torch.Tensor | None, weight: torch
                  int(normalize), _ptr(out_bf16), _ptr(out_f32), _stream())
 
 
+def add_rmsnorm_router(streams: torch.Tensor, delta: torch.Tensor | None,
+                       ffn_weight: torch.Tensor, router_weight: torch.Tensor, eps: float, *,
+                       out_bf16: torch.Tensor | None, router_in: torch.Tensor) -> None:
+    """streams += delta; m = RMSNorm(streams) * ffn_weight (bf16 into out_bf16);
+    router_in = RMSNorm(m) * router_weight (fp32), in one pass: the same bits as
+    add_rmsnorm(..., out_f32=m) followed by add_rmsnorm(m, None, router_weight)."""
+    _require_cuda(streams, delta, ffn_weight, router_weight)
+    _inplace(streams, "streams")
+    _inplace(router_in, "router_in")
+    if out_bf16 is not None:
+        _inplace(out_bf16, "out_bf16")
+    delta = None if delta is None else delta.contiguous()
+    d = streams.shape[-1]
+    n = streams.numel() // d
+    _native.call("llmyb_add_rmsnorm_router", _ptr(streams), _ptr(delta), n, d, _ptr(ffn_weight),
+                 _ptr(router_weight), float(eps), _ptr(out_bf16), _ptr(router_in), _stream())
+
+
+def add_rmsnorm_router_supported(d_model: int) -> bool:
+    return d_model % 8 == 0 and d_model <= 8192
+
+
 def rmsnorm_bf16(x: torch.Tensor, weight: torch.Tensor | None, eps: float,
                  out: torch.Tensor | None = None) -> torch.Tensor:
     _require_cuda(x, weight)

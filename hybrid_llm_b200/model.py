@@ -86,32 +86,46 @@ class LoopedHybridModel:
         return q, k, v, gate, beta
 
     def _router_logits(self, blk: Block, m_f32: torch.Tensor, state: RecurrentState, key: str,
-                       bsz: int, t: int, step: bool) -> torch.Tensor:
+                       bsz: int, t: int, step: bool, normed: bool = False) -> torch.Tensor:
         """ContextAwareRouter logits (context_router.py:59-74 prefill, :89-133
         decode step): local = RMSNorm(hidden); logits = W local, plus the local
         context term when the router has it (the window's latents kept in
-        state.router_latents for the following decode steps)."""
+        state.router_latents for the following decode steps).  normed: m_f32
+        already holds local (add_rmsnorm_router formed it with the FFN norm)."""
         c = self.cfg
-        r_in = torch.empty_like(m_f32)
-        kernels.add_rmsnorm(m_f32, None, blk.moe.router_norm, c.rms_eps, out_f32=r_in)
+        if normed:
+            r_in = m_f32
+        else:
+            r_in = torch.empty_like(m_f32)
+            kernels.add_rmsnorm(m_f32, None, blk.moe.router_norm, c.rms_eps, out_f32=r_in)
         if not c.router_context:
             return torch.mm(r_in, blk.moe.router.t())
         return kernels.router_context_logits(
             r_in, blk.moe, c.router_local_context, batch=bsz, seq=t,
             ring=state.router_latents[key], positions=state.positions if step else None)
 
+    def _router_in_fused(self) -> bool:
+        """Prompt MoE sub-layers whose router input is formed together with the
+        FFN norm (add_rmsnorm_router): where the one-kernel router
+        (route_norm) does not take the shape."""
+        c = self.cfg
+        return ((c.router_context or not kernels.route_norm_supported(c.d_model, c.moe_experts))
+                and kernels.add_rmsnorm_router_supported(c.d_model))
+
     def _moe(self, blk: Block, m_bf: torch.Tensor, m_f32: torch.Tensor, state: RecurrentState,
-             key: str, bsz: int, t: int):
+             key: str, bsz: int, t: int, normed: bool = False):
         """SparseMoE.forward (moe.py:172-204): the expert rows and the plan whose
         per-token sum is the combine (added to the residual stream by the next
-        add_rmsnorm_routed)."""
+        add_rmsnorm_routed).  normed: m_f32 is the router's input already."""
         c = self.cfg
         tile_m = kernels.grouped_tile_m(bsz * t * c.moe_top_k, c.moe_experts + c.moe_shared)
-        if not c.router_context and kernels.route_norm_supported(c.d_model, c.moe_experts):
+        if (not normed and not c.router_context
+                and kernels.route_norm_supported(c.d_model, c.moe_experts)):
             plan = kernels.route_norm(m_f32, blk.moe.router_norm, blk.moe.router, c.moe_top_k,
                                       c.rms_eps, tile_m=tile_m)
         else:
-            logits = self._router_logits(blk, m_f32, state, key, bsz, t, step=False)
+            logits = self._router_logits(blk, m_f32, state, key, bsz, t, step=False,
+                                         normed=normed)
             plan = kernels.route(logits, c.moe_top_k, tile_m=tile_m)
         return self._experts(blk, m_bf, plan)
 
@@ -237,6 +251,7 @@ class LoopedHybridModel:
         m_f32 = torch.empty_like(streams)
         pending = None  # bf16 update not yet added to the residual stream
         kv = self._lm_buffer(n, loops)
+        fused_router_in = self._router_in_fused()
         for i in range(loops):
             if kv is not None and i > 0:
                 self._lm_inject(streams, kv, i)
@@ -247,9 +262,13 @@ class LoopedHybridModel:
                     mixed = self._gdn_prefill(blk.mixer, normed, state, key, bsz, t, reset)
                 else:
                     mixed = self._csa_prefill(blk.mixer, normed, state, key, bsz, t)
-                kernels.add_rmsnorm(streams, mixed, blk.ffn_norm, c.rms_eps, out_bf16=m_bf,
-                                    out_f32=m_f32)
-                pending = self._moe(blk, m_bf, m_f32, state, key, bsz, t)
+                if fused_router_in:
+                    kernels.add_rmsnorm_router(streams, mixed, blk.ffn_norm, blk.moe.router_norm,
+                                               c.rms_eps, out_bf16=m_bf, router_in=m_f32)
+                else:
+                    kernels.add_rmsnorm(streams, mixed, blk.ffn_norm, c.rms_eps, out_bf16=m_bf,
+                                        out_f32=m_f32)
+                pending = self._moe(blk, m_bf, m_f32, state, key, bsz, t, normed=fused_router_in)
             if kv is not None and i < loops - 1:
                 self._add_pending(streams, pending, None, normalize=False)
                 pending = None

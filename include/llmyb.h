@@ -461,6 +461,19 @@ int32_t llmyb_add_rmsnorm_routed(float* streams, const void* y_rows, const int32
                                  const float* weight, float eps, int32_t normalize,
                                  void* out_bf16, float* out_f32, void* stream);
 
+/* The FFN norm and the router's input norm of a prompt's MoE sub-layer in one
+ * pass (SparseMoE input m = norms.py:13-16 RMSNorm of the residual;
+ * ContextAwareRouter local = RMSNorm(m), context_router.py:62):
+ * streams (fp32) += delta (bf16, nullable); m = RMSNorm(streams) * ffn_weight
+ * into out_bf16 (bf16, nullable); router_in = RMSNorm(m) * router_weight (fp32),
+ * bit-identical to llmyb_add_rmsnorm with out_f32 followed by llmyb_add_rmsnorm
+ * of that fp32 row.  D % 8 == 0, D <= 8192, 16-byte aligned rows, else
+ * LLMYB_EUNSUPPORTED. */
+int32_t llmyb_add_rmsnorm_router(float* streams, const void* delta, int64_t n_tokens,
+                                 int32_t d_model, const float* ffn_weight,
+                                 const float* router_weight, float eps, void* out_bf16,
+                                 float* router_in, void* stream);
+
 /* ------------------------------------------------ fused small-batch decode
  * Two kernels that shorten the launch chain of a decode step at 1..8 tokens
  * (PhysicalBlock.forward_step, model/model.py:214-241).  No counterpart in

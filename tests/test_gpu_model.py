@@ -392,3 +392,25 @@ def test_prefill_graph_equals_eager_forward(cuda):
         a, b = got.state.state_dict(), ref.state.state_dict()
         assert a.keys() == b.keys()
         assert all(torch.equal(a[k], b[k]) for k in a)
+
+
+@pytest.mark.parametrize("n,d,with_delta", [(37, 2048, True), (300, 768, True), (5, 4096, False),
+                                            (64, 6144, True)])
+def test_add_rmsnorm_router_equals_two_passes(cuda, n, d, with_delta):
+    """The fused FFN norm + router-input norm gives the bits of the two
+    separate passes (residual add + FFN norm with an fp32 copy, then the
+    router's RMSNorm of that copy), for one to three 8-element pieces per thread."""
+    from hybrid_llm_b200 import kernels
+    g = torch.Generator(device="cuda").manual_seed(n + d)
+    s0 = torch.randn(n, d, device="cuda", generator=g) * 3
+    delta = torch.randn(n, d, device="cuda", generator=g).bfloat16() if with_delta else None
+    w_ffn = 1 + 0.1 * torch.randn(d, device="cuda", generator=g)
+    w_rt = 1 + 0.1 * torch.randn(d, device="cuda", generator=g)
+    s_ref, m_bf_ref, m_ref, r_ref = s0.clone(), torch.empty(n, d, device="cuda").bfloat16(), \
+        torch.empty(n, d, device="cuda"), torch.empty(n, d, device="cuda")
+    kernels.add_rmsnorm(s_ref, delta, w_ffn, 1e-6, out_bf16=m_bf_ref, out_f32=m_ref)
+    kernels.add_rmsnorm(m_ref, None, w_rt, 1e-6, out_f32=r_ref)
+    s, m_bf, r = s0.clone(), torch.empty_like(m_bf_ref), torch.empty_like(r_ref)
+    kernels.add_rmsnorm_router(s, delta, w_ffn, w_rt, 1e-6, out_bf16=m_bf, router_in=r)
+    torch.cuda.synchronize()
+    assert torch.equal(s, s_ref) and torch.equal(m_bf, m_bf_ref) and torch.equal(r, r_ref)
