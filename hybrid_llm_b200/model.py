@@ -743,6 +743,47 @@ class GreedyDecoder:
         return self.host_out, self.host_lp
 
 
+class StackGraph:
+    """The looped recurrent core on hidden states of a fixed shape [batch, seq,
+    D] (run_stack: model/model.py:618-687 without embedding and head) captured
+    in one CUDA graph.  At a few hundred tokens the eager core is bound by the
+    host cost of its launches; a replay issues them at once.  Each replay
+    starts from a zeroed RecurrentState (zeroed inside the graph) and returns
+    the graph's own fp32 output stream, which the next replay overwrites."""
+
+    def __init__(self, model: LoopedHybridModel, batch: int, seq: int,
+                 num_loops: int | None = None):
+        dev = model.device
+        self.model, self.num_loops = model, num_loops
+        w = model.cfg.streams * model.cfg.d_model
+        self.hidden = torch.zeros(batch, seq, w, dtype=torch.float32, device=dev)
+        self.state = RecurrentState(model.cfg, batch, dev)
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):  # warm-up: workspaces and one-time attributes
+            self._body()
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.out = self._body()
+        torch.cuda.synchronize()
+
+    def _body(self) -> torch.Tensor:
+        self.state.zero_()
+        return self.model.run_stack(self.hidden, state=self.state, num_loops=self.num_loops)
+
+    def run(self, hidden: torch.Tensor) -> torch.Tensor:
+        """The core on `hidden` [batch, seq, D] (device or host): copies it into
+        the graph's input buffer and replays."""
+        if tuple(hidden.shape) != tuple(self.hidden.shape):
+            raise ValueError(f"this graph was captured for hidden states of shape "
+                             f"{tuple(self.hidden.shape)}")
+        self.hidden.copy_(hidden, non_blocking=True)
+        self.graph.replay()
+        return self.out
+
+
 class PrefillGraph:
     """A prompt forward of fixed shape [batch, seq] captured in one CUDA graph.
 

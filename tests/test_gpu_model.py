@@ -414,3 +414,20 @@ def test_add_rmsnorm_router_equals_two_passes(cuda, n, d, with_delta):
     kernels.add_rmsnorm_router(s, delta, w_ffn, w_rt, 1e-6, out_bf16=m_bf, router_in=r)
     torch.cuda.synchronize()
     assert torch.equal(s, s_ref) and torch.equal(m_bf, m_bf_ref) and torch.equal(r, r_ref)
+
+
+def test_stack_graph_replay_equals_eager(cuda):
+    """The single looped block core captured in one CUDA graph (StackGraph):
+    every replay starts from a zeroed state and gives the eager run_stack bits."""
+    from hybrid_llm_b200.config import single_block_config
+    from hybrid_llm_b200.model import StackGraph
+    cfg = single_block_config()
+    model = _model(cfg)
+    g = torch.Generator(device="cuda").manual_seed(4)
+    x = torch.randn(1, 256, cfg.d_model, device="cuda", generator=g)
+    x2 = torch.randn(1, 256, cfg.d_model, device="cuda", generator=g)
+    sg = StackGraph(model, 1, 256)
+    for inp in (x, x2, x):
+        got = sg.run(inp).clone()
+        torch.cuda.synchronize()
+        assert torch.equal(got, model.run_stack(inp))
