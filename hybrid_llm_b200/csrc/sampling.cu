@@ -50,6 +50,7 @@ struct SampleArgs {
   float* out_logprob;
   int update_seen;
   int32_t* status;
+  int cache_keys;  // 1: the top-k order keys of the row are kept in shared memory
 };
 
 __device__ float block_sum(float v, float* red) {
@@ -98,7 +99,7 @@ __global__ void __launch_bounds__(kThreads) sample_kernel(SampleArgs a) {
   __shared__ int s_count, s_tok;
   __shared__ uint32_t s_prefix;
   __shared__ int s_need;
-  extern __shared__ uint32_t s_block[];  // blocked-id bitmask [ceil(V/32)]
+  extern __shared__ uint32_t s_block[];  // blocked-id bitmask [ceil(V/32)], then the key cache [V]
 
   const int row = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int V = a.V;
@@ -235,13 +236,23 @@ __global__ void __launch_bounds__(kThreads) sample_kernel(SampleArgs a) {
         s_prefix = 0u;
         s_need = K;
       }
+      // order key of element i: formed once (first pass) into the row's key
+      // cache when the launch gave one, read back by the later passes and the
+      // candidate collection (the same bits as forming it again)
+      uint32_t* s_kc = s_block + (a.n_blocked > 0 ? nwords : 0);
+      auto key_of = [&](int i, bool first) -> uint32_t {
+        if (a.cache_keys && !first) return s_kc[i];
+        const uint32_t kk = order_key(adjusted(i) / a.temp);
+        if (a.cache_keys) s_kc[i] = kk;
+        return kk;
+      };
       uint32_t mask = 0u;
       for (int shift = 24; shift >= 0; shift -= 8) {
         for (int i = tid; i < 256; i += kThreads) s_hist[i] = 0;
         __syncthreads();
         const uint32_t prefix = s_prefix;
         for (int i = tid; i < V; i += kThreads) {
-          const uint32_t kk = order_key(adjusted(i) / a.temp);
+          const uint32_t kk = key_of(i, shift == 24);
           if ((kk & mask) == prefix) atomicAdd(&s_hist[(kk >> shift) & 255u], 1);
         }
         __syncthreads();
@@ -261,7 +272,7 @@ __global__ void __launch_bounds__(kThreads) sample_kernel(SampleArgs a) {
       if (tid == 0) s_count = 0;
       __syncthreads();
       for (int i = tid; i < V; i += kThreads) {
-        const uint32_t kk = order_key(adjusted(i) / a.temp);
+        const uint32_t kk = key_of(i, false);
         if (kk >= tau) {
           const int slot = atomicAdd(&s_count, 1);
           if (slot < kBuf) {
@@ -385,7 +396,13 @@ LLMYB_API int32_t llmyb_sample(const float* logits, int64_t ld, int32_t batch, i
   a.out_logprob = out_logprob;
   a.update_seen = update_seen;
   a.status = dev_status;
-  const int dyn = n_blocked > 0 ? ((vocab + 31) / 32) * 4 : 0;
+  int dyn = n_blocked > 0 ? ((vocab + 31) / 32) * 4 : 0;
+  // the key cache for the top-k passes when the row fits next to the static
+  // buffers (vocabularies up to ~49K ids)
+  constexpr int kDynLimit = 227 * 1024 - 20 * 1024;
+  const bool topk_path = temperature > 1e-4f && (top_k > 0 || (top_p > 0.f && top_p < 1.f));
+  a.cache_keys = topk_path && dyn + static_cast<int64_t>(vocab) * 4 <= kDynLimit ? 1 : 0;
+  if (a.cache_keys) dyn += vocab * 4;
   if (dyn > 48 * 1024) {
     int32_t st = ensure_smem(sample_kernel, dyn);
     if (st) return st;
