@@ -115,29 +115,45 @@ __global__ void __launch_bounds__(kThreads) sample_kernel(SampleArgs a) {
     }
     __syncthreads();
   }
-  auto adjusted = [&](int i) -> float {
-    float x = lg[i];
+  // the penalised / blocked value of element i whose raw logit is x
+  auto adjusted_x = [&](float x, int i) -> float {
     if (a.n_blocked > 0 && ((s_block[i >> 5] >> (i & 31)) & 1u)) return -INFINITY;
     if (seen != nullptr && a.rep != 1.0f && ((seen[i >> 5] >> (i & 31)) & 1u))
       x = x > 0.f ? x / a.rep : x * a.rep;
     return x;
   };
+  auto adjusted = [&](int i) -> float { return adjusted_x(lg[i], i); };
+  // A thread walks its elements i = tid, tid + kThreads, ... in batches of
+  // kBatch whose logits are all loaded before any is used, so the loads of a
+  // batch are in flight together; the arithmetic keeps the element order.
+  constexpr int kBatch = 8;
 
   // ---- pass 1: raw log-sum-exp, adjusted argmax (value desc, index asc)
   float rm = -INFINITY, rs = 0.f, bm = -INFINITY;
   int bi = 0x7fffffff;
-  for (int i = tid; i < V; i += kThreads) {
-    const float x = lg[i];
-    if (x > rm) {
-      rs = rs * expf(rm - x) + 1.f;
-      rm = x;
-    } else {
-      rs += expf(x - rm);
+  for (int i0 = tid; i0 < V; i0 += kBatch * kThreads) {
+    float xs[kBatch];
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      const int i = i0 + u * kThreads;
+      xs[u] = i < V ? lg[i] : 0.f;
     }
-    const float w = adjusted(i);
-    if (bi == 0x7fffffff || w > bm) {  // i grows per thread: first maximal index wins
-      bm = w;
-      bi = i;
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      const int i = i0 + u * kThreads;
+      if (i >= V) break;
+      const float x = xs[u];
+      if (x > rm) {
+        rs = rs * expf(rm - x) + 1.f;
+        rm = x;
+      } else {
+        rs += expf(x - rm);
+      }
+      const float w = adjusted_x(x, i);
+      if (bi == 0x7fffffff || w > bm) {  // i grows per thread: first maximal index wins
+        bm = w;
+        bi = i;
+      }
     }
   }
 #pragma unroll
@@ -236,24 +252,48 @@ __global__ void __launch_bounds__(kThreads) sample_kernel(SampleArgs a) {
         s_prefix = 0u;
         s_need = K;
       }
-      // order key of element i: formed once (first pass) into the row's key
-      // cache when the launch gave one, read back by the later passes and the
-      // candidate collection (the same bits as forming it again)
+      // order keys of one batch of a thread's elements (see kBatch): formed
+      // in the first pass into the row's key cache when the launch gave one,
+      // read back by the later passes and the candidate collection (the same
+      // bits as forming them again)
       uint32_t* s_kc = s_block + (a.n_blocked > 0 ? nwords : 0);
-      auto key_of = [&](int i, bool first) -> uint32_t {
-        if (a.cache_keys && !first) return s_kc[i];
-        const uint32_t kk = order_key(adjusted(i) / a.temp);
-        if (a.cache_keys) s_kc[i] = kk;
-        return kk;
+      auto batch_keys = [&](int i0, bool first, uint32_t (&kk)[kBatch]) {
+        if (a.cache_keys && !first) {
+#pragma unroll
+          for (int u = 0; u < kBatch; ++u) {
+            const int i = i0 + u * kThreads;
+            kk[u] = i < V ? s_kc[i] : 0u;
+          }
+          return;
+        }
+        float xs[kBatch];
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) {
+          const int i = i0 + u * kThreads;
+          xs[u] = i < V ? lg[i] : 0.f;
+        }
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) {
+          const int i = i0 + u * kThreads;
+          kk[u] = 0u;
+          if (i < V) {
+            kk[u] = order_key(adjusted_x(xs[u], i) / a.temp);
+            if (a.cache_keys) s_kc[i] = kk[u];
+          }
+        }
       };
       uint32_t mask = 0u;
       for (int shift = 24; shift >= 0; shift -= 8) {
         for (int i = tid; i < 256; i += kThreads) s_hist[i] = 0;
         __syncthreads();
         const uint32_t prefix = s_prefix;
-        for (int i = tid; i < V; i += kThreads) {
-          const uint32_t kk = key_of(i, shift == 24);
-          if ((kk & mask) == prefix) atomicAdd(&s_hist[(kk >> shift) & 255u], 1);
+        for (int i0 = tid; i0 < V; i0 += kBatch * kThreads) {
+          uint32_t kk[kBatch];
+          batch_keys(i0, shift == 24, kk);
+#pragma unroll
+          for (int u = 0; u < kBatch; ++u)
+            if (i0 + u * kThreads < V && (kk[u] & mask) == prefix)
+              atomicAdd(&s_hist[(kk[u] >> shift) & 255u], 1);
         }
         __syncthreads();
         if (tid == 0) {
@@ -271,13 +311,18 @@ __global__ void __launch_bounds__(kThreads) sample_kernel(SampleArgs a) {
       const uint32_t tau = s_prefix;  // key of the K-th largest value
       if (tid == 0) s_count = 0;
       __syncthreads();
-      for (int i = tid; i < V; i += kThreads) {
-        const uint32_t kk = key_of(i, false);
-        if (kk >= tau) {
-          const int slot = atomicAdd(&s_count, 1);
-          if (slot < kBuf) {
-            s_keys[slot] = kk;
-            s_idx[slot] = i;
+      for (int i0 = tid; i0 < V; i0 += kBatch * kThreads) {
+        uint32_t kk[kBatch];
+        batch_keys(i0, false, kk);
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) {
+          const int i = i0 + u * kThreads;
+          if (i < V && kk[u] >= tau) {
+            const int slot = atomicAdd(&s_count, 1);
+            if (slot < kBuf) {
+              s_keys[slot] = kk[u];
+              s_idx[slot] = i;
+            }
           }
         }
       }
